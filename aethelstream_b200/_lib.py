@@ -1,0 +1,137 @@
+"""ctypes binding of libaeth_galore.so (include/aeth_galore.h).
+
+The shared library is the product; this module only declares its C ABI for
+Python callers.  Importing fails loudly when the library is missing -- there
+is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("AETH_GALORE_LIB", os.path.join(HERE, "libaeth_galore.so"))
+
+AETH_OK = 0
+AETH_ERR_ARG = -1
+AETH_ERR_SHAPE = -2
+AETH_ERR_CONFIG = -3
+AETH_ERR_UNSUPPORTED = -4
+AETH_ERR_NOT_FOUND = -5
+AETH_ERR_TIMEOUT = -6
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+MODE_REF, MODE_B200 = 0, 1
+CODEC_PER_TENSOR, CODEC_BLOCK_LINEAR, CODEC_BLOCK_DYNAMIC = 0, 1, 2
+WEIGHT_NONE, WEIGHT_F32, WEIGHT_NF4 = 0, 1, 2
+
+
+class GaloreConfig(C.Structure):
+    _fields_ = [
+        ("mode", C.c_int), ("default_rank", C.c_int), ("attn_rank", C.c_int), ("mlp_rank", C.c_int),
+        ("vector_rank", C.c_int), ("switch_interval", C.c_uint64), ("oversampling", C.c_int),
+        ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float), ("lr", C.c_float),
+        ("weight_decay", C.c_float), ("scale_lr_by_rank", C.c_int), ("max_grad_norm", C.c_float),
+        ("state_codec", C.c_int), ("state_block", C.c_int), ("init_projectors", C.c_int),
+    ]
+
+
+class ParamSpec(C.Structure):
+    _fields_ = [("layer_idx", C.c_uint32), ("name", C.c_char_p), ("m", C.c_int), ("n", C.c_int), ("rank", C.c_int)]
+
+
+class ParamInfo(C.Structure):
+    _fields_ = [("m", C.c_int), ("n", C.c_int), ("rank", C.c_int), ("side", C.c_int),
+                ("state_elems", C.c_int64), ("state_blocks", C.c_int64), ("layer_idx", C.c_uint32)]
+
+
+class WeightRef(C.Structure):
+    _fields_ = [("kind", C.c_int), ("data", C.c_void_p), ("absmax", C.c_void_p), ("delta_out", C.c_void_p),
+                ("prequant_out", C.c_void_p)]
+
+
+SQ_HOOK = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p)
+
+_vp, _i, _i64, _f, _u32, _u64, _d = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_uint32, C.c_uint64, C.c_double
+
+# name -> (restype, argtypes); every function declared in include/aeth_galore.h
+SIGNATURES = {
+    "galore_project_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "galore_project_backward": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "galore_quantize_absmax_f32_to_i8": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "galore_dequantize_i8_to_f32": (_i, [_vp, _vp, _f, _i, _vp]),
+    "doublepass_galore_apply": (None, [_vp, _vp, _vp, _vp, _f, _f, _f, _f, _f, _i, _i]),
+    "aeth_galore_config_default": (None, [C.POINTER(GaloreConfig)]),
+    "aeth_galore_create": (_i, [C.POINTER(GaloreConfig), C.POINTER(ParamSpec), _i, _i, C.POINTER(_vp)]),
+    "aeth_galore_destroy": (_i, [_vp]),
+    "aeth_galore_find": (_i, [_vp, _u32, C.c_char_p]),
+    "aeth_galore_param_info": (_i, [_vp, _i, C.POINTER(ParamInfo)]),
+    "aeth_galore_num_params": (_i, [_vp]),
+    "aeth_galore_project_accumulate": (_i, [_vp, _i, _vp, _i, _vp]),
+    "aeth_galore_sqnorm_device": (_i, [_vp, _i, _vp, _vp]),
+    "aeth_galore_sqnorm": (_i, [_vp, _i, C.POINTER(_d), _vp]),
+    "aeth_clip_coeff_device": (_i, [_vp, _i, _f, _vp, _vp, _vp]),
+    "aeth_galore_apply_update": (_i, [_vp, _i, _f, _vp, C.POINTER(WeightRef), _vp]),
+    "aeth_galore_zero_accum": (_i, [_vp, _i, _vp]),
+    "aeth_galore_notify_step": (_i, [_vp, _u64]),
+    "aeth_galore_step_count": (_u64, [_vp]),
+    "aeth_galore_step": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(_vp), _i, C.POINTER(WeightRef), SQ_HOOK, _vp, _vp,
+                              _vp]),
+    "aeth_galore_set_projector": (_i, [_vp, _i, _vp, _vp, _vp]),
+    "aeth_galore_get_projector": (_i, [_vp, _i, _vp, _vp, _vp]),
+    "aeth_galore_get_state": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp]),
+    "aeth_galore_set_state": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp]),
+    "aeth_galore_get_accum": (_i, [_vp, _i, _vp, _vp]),
+    "aeth_nf4_dequant": (_i, [_vp, _vp, _i64, _i, _vp, _i, _vp]),
+    "aeth_nf4_quant": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),
+    "aeth_int8_quantize": (_i, [_vp, _i64, _i, _i, _i, _vp, _vp, _vp]),
+    "aeth_int8_dequantize": (_i, [_vp, _vp, _i64, _i, _i, _i, _vp, _vp]),
+    "aeth_dynamic_map": (_i, [_i, C.POINTER(_f)]),
+    "aeth_lomo_sqnorm": (_i, [_vp, _i64, _vp, _vp]),
+    "aeth_lomo_update": (_i, [_vp, _i64, _vp, _f, _f, _f, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "aeth_status_string": (C.c_char_p, [_i]),
+    "aeth_last_error": (_i, []),
+    "aeth_device_error": (_i, [_i]),
+    "aeth_version": (C.c_char_p, []),
+}
+
+_lib = None
+
+
+class AethError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        super().__init__(f"{what}: status {status} ({status_string(status)})")
+
+
+def load(path: str | None = None):
+    """Load the library (once).  Raises ImportError if it is absent."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise ImportError(
+            f"libaeth_galore.so not found at {p}; build it with `python -m aethelstream_b200.build` "
+            "(this package has no CPU fallback)")
+    L = C.CDLL(p)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = L
+    return L
+
+
+def status_string(st: int) -> str:
+    try:
+        return load().aeth_status_string(st).decode()
+    except Exception:  # noqa: BLE001 - used while formatting another error
+        return "?"
+
+
+def check(st: int, what: str = "aeth call"):
+    if st != AETH_OK:
+        raise AethError(st, what)
+    return st

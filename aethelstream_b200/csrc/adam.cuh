@@ -1,0 +1,220 @@
+// adam.cuh -- low-rank Adam (K5), squared norms, the global clip and the
+// full-rank fused Adam of doublepass_galore_apply.
+#pragma once
+#include "codec.cuh"
+#include "common.cuh"
+
+namespace aeth {
+
+// ---------------------------------------------------------------------------
+// REF mode: one parameter's r x r Adam step with per-tensor absmax INT8 state,
+// bit-exact with galore/src/optimizer.rs:314-351 + adamw.rs:79-88,116-135 +
+// quantize.rs:4-26.  One CTA; two passes separated by the absmax reduction.
+//   mom/var: fp32 working buffers (the Rust struct's momentum/variance Vecs).
+//   scales[0] = scale_m, scales[1] = scale_v (device, in/out).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) ref_adam_kernel(const float* __restrict__ accum, int8_t* __restrict__ m8,
+                                                        int8_t* __restrict__ v8, float* __restrict__ scales,
+                                                        float* __restrict__ mom, float* __restrict__ var,
+                                                        float* __restrict__ normalized, int64_t n, float clip_host,
+                                                        const float* __restrict__ clip_dev, float b1, float b2,
+                                                        float eps) {
+    __shared__ float red_m[32], red_v[32];
+    __shared__ float s_scales[2];
+    const float clip = clip_dev ? *clip_dev : clip_host;
+    const float sm = scales[0], sv = scales[1];
+    const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
+    float am = 0.0f, av = 0.0f;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        float mo = __fmul_rn((float)m8[i], sm);
+        float va = __fmul_rn((float)v8[i], sv);
+        float g = accum[i];
+        if (clip != 1.0f) g = __fmul_rn(g, clip);
+        mo = __fadd_rn(__fmul_rn(b1, mo), __fmul_rn(omb1, g));
+        va = __fadd_rn(__fmul_rn(b2, va), __fmul_rn(__fmul_rn(omb2, g), g));
+        normalized[i] = __fdiv_rn(mo, __fadd_rn(__fsqrt_rn(va), eps));
+        mom[i] = mo;
+        var[i] = va;
+        am = fmaxf(am, fabsf(mo));
+        av = fmaxf(av, fabsf(va));
+    }
+    am = warp_max(am);
+    av = warp_max(av);
+    if ((threadIdx.x & 31) == 0) { red_m[threadIdx.x >> 5] = am; red_v[threadIdx.x >> 5] = av; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.0f, b = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { a = fmaxf(a, red_m[w]); b = fmaxf(b, red_v[w]); }
+        s_scales[0] = lin_scale_from_absmax(a);
+        s_scales[1] = lin_scale_from_absmax(b);
+    }
+    __syncthreads();
+    const float nsm = s_scales[0], nsv = s_scales[1];
+    const float im = lin_inv(nsm), iv = lin_inv(nsv);
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        m8[i] = lin_encode(mom[i], im);
+        v8[i] = lin_encode(var[i], iv);
+    }
+    if (threadIdx.x == 0) { scales[0] = nsm; scales[1] = nsv; }
+}
+
+// ---------------------------------------------------------------------------
+// B200 mode: Adam over the l x r state with blockwise INT8 m/v.  One CTA per
+// state block (grid-stride over blocks).  Pass 1 updates and tracks the block
+// absmax and writes N (bf16); pass 2 recomputes the same values (bit-identical)
+// and encodes them with the new block scales.  Optionally zeroes the
+// accumulator (the fused zero_accum of a whole-layer step).
+// ---------------------------------------------------------------------------
+struct AdamB2Args {
+    const float* accum;
+    int8_t* m8;
+    int8_t* v8;
+    float* m_scales;
+    float* v_scales;
+    uint16_t* n_out;  // bf16 N, same l x r layout
+    int64_t count;
+    int block;
+    int codec;        // AETH_CODEC_BLOCK_LINEAR / AETH_CODEC_BLOCK_DYNAMIC
+    float clip_host;
+    const float* clip_dev;
+    float b1, b2, eps;
+    int zero_accum;
+};
+
+__device__ __forceinline__ void b2_adam_elem(float g_raw, float clip, int8_t qm, int8_t qv, float sm, float sv,
+                                             int codec, const float* dm, const float* du, float b1, float omb1,
+                                             float b2, float omb2, float& mo, float& va) {
+    float g = clip != 1.0f ? __fmul_rn(g_raw, clip) : g_raw;
+    float m0, v0;
+    if (codec == AETH_CODEC_BLOCK_LINEAR) {
+        m0 = __fmul_rn((float)qm, sm);
+        v0 = __fmul_rn((float)qv, sv);
+    } else {
+        m0 = __fmul_rn(dm[(uint8_t)qm], sm);
+        v0 = __fmul_rn(du[(uint8_t)qv], sv);
+    }
+    mo = __fadd_rn(__fmul_rn(b1, m0), __fmul_rn(omb1, g));
+    va = __fadd_rn(__fmul_rn(b2, v0), __fmul_rn(__fmul_rn(omb2, g), g));
+}
+
+__global__ void __launch_bounds__(256) b2_adam_kernel(AdamB2Args a) {
+    __shared__ float dm[256], du[256];
+    __shared__ float red_m[8], red_v[8];
+    if (a.codec == AETH_CODEC_BLOCK_DYNAMIC) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) { dm[i] = c_dmap_signed[i]; du[i] = c_dmap_unsigned[i]; }
+    }
+    const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
+    const float omb1 = __fsub_rn(1.0f, a.b1), omb2 = __fsub_rn(1.0f, a.b2);
+    const int64_t n_blocks = (a.count + a.block - 1) / a.block;
+    __syncthreads();
+    for (int64_t b = blockIdx.x; b < n_blocks; b += gridDim.x) {
+        const int64_t s = b * a.block, e = s + a.block < a.count ? s + a.block : a.count;
+        const float sm = a.m_scales[b], sv = a.v_scales[b];
+        float am = 0.0f, av = 0.0f;
+        for (int64_t i = s + threadIdx.x; i < e; i += blockDim.x) {
+            float mo, va;
+            b2_adam_elem(a.accum[i], clip, a.m8[i], a.v8[i], sm, sv, a.codec, dm, du, a.b1, omb1, a.b2, omb2, mo, va);
+            float nv = __fdiv_rn(mo, __fadd_rn(__fsqrt_rn(va), a.eps));
+            a.n_out[i] = f32_to_bf16_bits(nv);
+            am = fmaxf(am, fabsf(mo));
+            av = fmaxf(av, fabsf(va));
+        }
+        am = warp_max(am);
+        av = warp_max(av);
+        if ((threadIdx.x & 31) == 0) { red_m[threadIdx.x >> 5] = am; red_v[threadIdx.x >> 5] = av; }
+        __syncthreads();
+        float bm = 0.0f, bv = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { bm = fmaxf(bm, red_m[w]); bv = fmaxf(bv, red_v[w]); }
+        float nsm, nsv, im = 0.0f, iv = 0.0f;
+        if (a.codec == AETH_CODEC_BLOCK_LINEAR) {
+            nsm = lin_scale_from_absmax(bm); nsv = lin_scale_from_absmax(bv);
+            im = lin_inv(nsm); iv = lin_inv(nsv);
+        } else {
+            nsm = bm; nsv = bv;
+        }
+        // Every thread has read the old scales and the block's old codes for
+        // its own elements; pass 2 touches only the same elements.
+        for (int64_t i = s + threadIdx.x; i < e; i += blockDim.x) {
+            float mo, va;
+            b2_adam_elem(a.accum[i], clip, a.m8[i], a.v8[i], sm, sv, a.codec, dm, du, a.b1, omb1, a.b2, omb2, mo, va);
+            if (a.codec == AETH_CODEC_BLOCK_LINEAR) {
+                a.m8[i] = lin_encode(mo, im);
+                a.v8[i] = lin_encode(va, iv);
+            } else {
+                a.m8[i] = (int8_t)(uint8_t)dmap_encode(dm, dyn_xn(mo, nsm));
+                a.v8[i] = (int8_t)(uint8_t)dmap_encode(du, dyn_xn(va, nsv));
+            }
+            if (a.zero_accum) const_cast<float*>(a.accum)[i] = 0.0f;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) { a.m_scales[b] = nsm; a.v_scales[b] = nsv; }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Squared Frobenius norm in f64 (adamw.rs:99-104).  Deterministic: fixed grid
+// of partial sums, then an ordered final sum.
+// ---------------------------------------------------------------------------
+constexpr int kSqPartials = 256;
+
+__global__ void __launch_bounds__(256) sqnorm_partial_kernel(const float* __restrict__ x, int64_t n,
+                                                             double* __restrict__ partials) {
+    __shared__ double red[8];
+    double s = 0.0;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        double v = (double)x[i];
+        s += v * v;
+    }
+    s = warp_sum_d(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+        partials[blockIdx.x] = t;
+    }
+}
+
+__global__ void sqnorm_final_kernel(const double* __restrict__ partials, int np, double* __restrict__ out) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < np; ++i) t += partials[i];
+        *out = t;
+    }
+}
+
+// hook.rs:184-187: clip = min(1, (max_norm / (sqrt(sum) + 1e-6)) as f32).
+__global__ void clip_coeff_kernel(const double* __restrict__ sq, int n, float max_norm, float* __restrict__ clip_out,
+                                  double* __restrict__ gnorm_out) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < n; ++i) t += sq[i];
+        double gnorm = sqrt(t);
+        float c = (float)((double)max_norm / (gnorm + 1e-6));
+        *clip_out = c < 1.0f ? c : 1.0f;
+        if (gnorm_out) *gnorm_out = gnorm;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Full-rank fused Adam (doublepass_galore_apply; StandardAdamW arithmetic of
+// standard_adamw.rs:84-114 with optional bias correction).
+// ---------------------------------------------------------------------------
+__global__ void full_adam_kernel(float* __restrict__ param, const float* __restrict__ grad, float* __restrict__ m,
+                                 float* __restrict__ v, int64_t n, float clip, float b1, float b2, float eps, float lr,
+                                 int bias_correct, float bc1, float bc2) {
+    const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float gs = __fmul_rn(grad[i], clip);
+        float mo = __fadd_rn(__fmul_rn(b1, m[i]), __fmul_rn(omb1, gs));
+        float va = __fadd_rn(__fmul_rn(b2, v[i]), __fmul_rn(__fmul_rn(omb2, gs), gs));
+        m[i] = mo;
+        v[i] = va;
+        float mh = mo, vh = va;
+        if (bias_correct) { mh = __fdiv_rn(mh, bc1); vh = __fdiv_rn(vh, bc2); }
+        float d = __fdiv_rn(__fmul_rn(lr, mh), __fadd_rn(__fsqrt_rn(vh), eps));
+        param[i] = __fsub_rn(param[i], d);
+    }
+}
+
+}  // namespace aeth

@@ -1,0 +1,975 @@
+// aeth_galore.cu -- libaeth_galore: the C ABI of include/aeth_galore.h.
+//
+// One translation unit (the kernels live in the included .cuh files) so the
+// __constant__ tables exist once per library.  Reference paths are relative
+// to the reference project's aethelStream/ directory.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "adam.cuh"
+#include "codec.cuh"
+#include "common.cuh"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+#include "lomo.cuh"
+#include "nf4.cuh"
+
+using namespace aeth;
+
+// ===========================================================================
+// Host helpers
+// ===========================================================================
+namespace aeth {
+
+// Dynamic 8-bit map (Dettmers et al. 2021 dynamic tree quantisation): after
+// the optional sign bit, E = 0..6 leading zero bits select the decade 10^-E,
+// an indicator bit follows, and the remaining F bits (6-E signed, 7-E
+// unsigned) index the centres of 2^F equal bins over [0.1, 1].  Plus 0 and 1.
+// Sorted ascending; a code is an index into the table.
+int build_dynamic_map(int is_signed, float out[256]) {
+    static const double decade[7] = {1.0, 1e-1, 1e-2, 1e-3, 1e-4, 1e-5, 1e-6};
+    std::vector<float> v;
+    v.reserve(256);
+    for (int e = 0; e < 7; ++e) {
+        int fbits = (is_signed ? 6 : 7) - e;
+        int levels = 1 << fbits;
+        for (int j = 0; j < levels; ++j) {
+            double f = 0.1 + 0.9 * ((double)j + 0.5) / (double)levels;
+            v.push_back((float)(decade[e] * f));
+            if (is_signed) v.push_back((float)(-decade[e] * f));
+        }
+    }
+    v.push_back(0.0f);
+    v.push_back(1.0f);
+    if (v.size() != 256) return AETH_ERR_CONFIG;
+    std::sort(v.begin(), v.end());
+    memcpy(out, v.data(), sizeof(float) * 256);
+    return AETH_OK;
+}
+
+// init_random_projection (galore/src/optimizer.rs:419-448): xorshift64
+// uniforms in [-0.5, 0.5) then modified Gram-Schmidt in f32.  One-time
+// initialisation at create(); the step path never calls it.
+static void init_random_projection_host(int rows, int cols, uint32_t seed, float* data) {
+    uint64_t s = (uint64_t)seed + 1;
+    for (int64_t i = 0; i < (int64_t)rows * cols; ++i) {
+        s ^= s << 13;
+        s ^= s >> 7;
+        s ^= s << 17;
+        data[i] = ((float)(s >> 40) / (float)(1u << 24)) - 0.5f;
+    }
+    for (int j = 0; j < cols; ++j) {
+        for (int i = 0; i < j; ++i) {
+            float dot = 0.0f;
+            for (int r = 0; r < rows; ++r) {
+                volatile float prod = data[(int64_t)r * cols + i] * data[(int64_t)r * cols + j];
+                dot = dot + prod;
+            }
+            for (int r = 0; r < rows; ++r) {
+                volatile float prod = dot * data[(int64_t)r * cols + i];
+                data[(int64_t)r * cols + j] = data[(int64_t)r * cols + j] - prod;
+            }
+        }
+        float norm = 0.0f;
+        for (int r = 0; r < rows; ++r) {
+            volatile float prod = data[(int64_t)r * cols + j] * data[(int64_t)r * cols + j];
+            norm = norm + prod;
+        }
+        norm = sqrtf(fmaxf(norm, 1e-12f));
+        for (int r = 0; r < rows; ++r) data[(int64_t)r * cols + j] /= norm;
+    }
+}
+
+// LayerRankConfig::rank_for_param (galore/src/layer_rank.rs:32-40).
+static int rank_for_param(const aeth_galore_config& c, const char* name, int m, int n) {
+    int base = c.default_rank;
+    std::string s = name ? name : "";
+    if (s == "d_wq" || s == "d_wk" || s == "d_wv" || s == "d_wo") base = c.attn_rank;
+    else if (s == "d_wg" || s == "d_wu" || s == "d_wd") base = c.mlp_rank;
+    else if (s == "d_rms1_w" || s == "d_rms2_w") base = c.vector_rank;
+    int mm = m < 1 ? 1 : m, nn = n < 1 ? 1 : n;
+    int v = base < mm ? base : mm;
+    v = v < nn ? v : nn;
+    return v < 1 ? 1 : v;
+}
+
+static uint16_t host_f32_to_bf16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    if ((x & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((x >> 16) | 0x40u);
+    x += 0x7fffu + ((x >> 16) & 1u);
+    return (uint16_t)(x >> 16);
+}
+
+// Projector conversion: fp32 s x r -> bf16 proj (s x r) and projT (r x s).
+__global__ void proj_to_bf16_kernel(const float* __restrict__ p, int s, int r, uint16_t* __restrict__ proj,
+                                    uint16_t* __restrict__ projT) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)s * r; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t row = i / r, col = i % r;
+        uint16_t b = f32_to_bf16_bits(p[i]);
+        proj[i] = b;
+        projT[col * s + row] = b;
+    }
+}
+
+__global__ void bf16_to_f32_kernel(const uint16_t* __restrict__ x, int64_t n, float* __restrict__ y) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = bf16_bits_to_f32(x[i]);
+}
+
+__global__ void to_bf16_kernel(const void* __restrict__ x, int dtype, int64_t n, uint16_t* __restrict__ y) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = f32_to_bf16_bits(load_as_f32(x, i, dtype));
+}
+
+__global__ void fill_f32_kernel(float* __restrict__ x, int64_t n, float v) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) x[i] = v;
+}
+
+// Dense delta applied to an NF4 weight (REF mode with an NF4 weight):
+// w = dequant(w) - delta, requantised.  One thread per 64-element block.
+__global__ void nf4_apply_delta_kernel(uint8_t* __restrict__ wp, float* __restrict__ wa, const float* __restrict__ delta,
+                                       int64_t n_blocks, float* __restrict__ prequant) {
+    __shared__ Nf4Tables tab;
+    nf4_tables_init(&tab, threadIdx.x, blockDim.x);
+    __syncthreads();
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < n_blocks; b += (int64_t)gridDim.x * blockDim.x) {
+        uint8_t* p = wp + b * 32;
+        uint32_t q[8];
+        for (int k = 0; k < 8; ++k) q[k] = reinterpret_cast<uint32_t*>(p)[k];
+        float w[64];
+        float am0 = wa[b];
+        for (int k = 0; k < 8; ++k) nf4_dequant_word(q[k], am0, tab.byte_lut, w + 8 * k);
+        float amax = 0.0f;
+        for (int i = 0; i < 64; ++i) {
+            w[i] = __fsub_rn(w[i], delta[b * 64 + i]);
+            amax = fmaxf(amax, fabsf(w[i]));
+            if (prequant) prequant[b * 64 + i] = w[i];
+        }
+        uint32_t pk[8];
+        nf4_quant_regs<64>(w, amax, tab.bucket, pk);
+        for (int k = 0; k < 8; ++k) reinterpret_cast<uint32_t*>(p)[k] = pk[k];
+        wa[b] = amax;
+    }
+}
+
+// Generic f16/bf16/f32 GEMM for shapes TMA cannot describe (unaligned row
+// pitch): one thread per output, fp32 accumulation in increasing k.
+__global__ void simt_gemm_any_kernel(const void* A, int adt, int64_t sai, int64_t sak, const void* B, int bdt,
+                                     int64_t sbk, int64_t sbj, void* C, int cdt, int64_t ldc, int M, int N, int K) {
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < (int64_t)M * N; t += (int64_t)gridDim.x * blockDim.x) {
+        int i = (int)(t / N), j = (int)(t % N);
+        float s = 0.0f;
+        for (int k = 0; k < K; ++k)
+            s = __fadd_rn(s, __fmul_rn(load_as_f32(A, i * sai + k * sak, adt), load_as_f32(B, k * sbk + j * sbj, bdt)));
+        int64_t o = (int64_t)i * ldc + j;
+        if (cdt == AETH_DTYPE_F32) static_cast<float*>(C)[o] = s;
+        else if (cdt == AETH_DTYPE_F16) static_cast<__half*>(C)[o] = __float2half_rn(s);
+        else static_cast<__nv_bfloat16*>(C)[o] = __float2bfloat16_rn(s);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 GEMM dispatch on (A major, B major, N width).
+// ---------------------------------------------------------------------------
+template <bool A_MN, bool B_MN, class Epi>
+static int tc_gemm(TcOperand A, TcOperand B, int M, int N, int K, bool bf16, const Epi& epi, cudaStream_t st) {
+    if (N <= 64) return tc_gemm_launch<64, 4, A_MN, B_MN>(A, B, M, N, K, bf16, epi, st);
+    if (N <= 128) return tc_gemm_launch<128, 4, A_MN, B_MN>(A, B, M, N, K, bf16, epi, st);
+    return tc_gemm_launch<256, 4, A_MN, B_MN>(A, B, M, N, K, bf16, epi, st);
+}
+
+}  // namespace aeth
+
+// ===========================================================================
+// Context
+// ===========================================================================
+struct Param {
+    uint32_t layer = 0;
+    std::string name;
+    int m = 0, n = 0, r = 0;
+    int side = 0;  // 0 two-sided (REF), 1 left, 2 right
+    int64_t state_elems = 0, state_blocks = 0;
+    // REF
+    float* P = nullptr;
+    float* Q = nullptr;
+    float* mom = nullptr;
+    float* var = nullptr;
+    float* normalized = nullptr;
+    float* temp = nullptr;
+    float* gtmp = nullptr;
+    float* dtmp = nullptr;
+    // shared
+    float* accum = nullptr;
+    int8_t* m8 = nullptr;
+    int8_t* v8 = nullptr;
+    float* mscale = nullptr;
+    float* vscale = nullptr;
+    // B200
+    uint16_t* proj = nullptr;
+    uint16_t* projT = nullptr;
+    uint16_t* nbuf = nullptr;
+    uint16_t* gbf = nullptr;  // bf16 copy of a non-bf16 gradient (lazy)
+};
+
+struct aeth_galore_ctx {
+    aeth_galore_config cfg;
+    int device = 0;
+    uint64_t step = 0;
+    std::vector<Param> params;
+    double* sq_slots = nullptr;  // one per parameter
+    double* sq_step = nullptr;   // contiguous slots for aeth_galore_step
+    double* partials = nullptr;  // kSqPartials
+    float* clip_dev = nullptr;
+    double* gnorm_dev = nullptr;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+template <class T>
+int ctx_alloc(aeth_galore_ctx* c, T** p, int64_t count) {
+    void* v = nullptr;
+    if (count <= 0) count = 1;
+    AETH_CUDA(cudaMalloc(&v, (size_t)count * sizeof(T)));
+    c->allocs.push_back(v);
+    *p = static_cast<T*>(v);
+    return AETH_OK;
+}
+
+int reset_state(aeth_galore_ctx* c, Param& p, cudaStream_t st) {
+    AETH_CUDA(cudaMemsetAsync(p.m8, 0, p.state_elems, st));
+    AETH_CUDA(cudaMemsetAsync(p.v8, 0, p.state_elems, st));
+    AETH_CUDA(cudaMemsetAsync(p.accum, 0, p.state_elems * sizeof(float), st));
+    // LowRankAdamState::new + quantize_to_ram (adamw.rs:65-76): scale 1.0.
+    float init = c->cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC ? 0.0f : 1.0f;
+    fill_f32_kernel<<<grid_for(p.state_blocks, 256), 256, 0, st>>>(p.mscale, p.state_blocks, init);
+    fill_f32_kernel<<<grid_for(p.state_blocks, 256), 256, 0, st>>>(p.vscale, p.state_blocks, init);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int check_idx(const aeth_galore_ctx* c, int idx) {
+    if (!c) return AETH_ERR_ARG;
+    if (idx < 0 || idx >= (int)c->params.size()) return AETH_ERR_NOT_FOUND;
+    return AETH_OK;
+}
+
+int sqnorm_into(aeth_galore_ctx* c, Param& p, double* out_dev, cudaStream_t st) {
+    sqnorm_partial_kernel<<<kSqPartials, 256, 0, st>>>(p.accum, p.state_elems, c->partials);
+    sqnorm_final_kernel<<<1, 32, 0, st>>>(c->partials, kSqPartials, out_dev);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+// ---- REF mode -------------------------------------------------------------
+int ref_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t st) {
+    const float* g = static_cast<const float*>(grad);
+    if (dtype != AETH_DTYPE_F32) {
+        to_f32_kernel<<<grid_for((int64_t)p.m * p.n, 256), 256, 0, st>>>(grad, dtype, (int64_t)p.m * p.n, p.gtmp);
+        AETH_LAUNCH_CHECK();
+        g = p.gtmp;
+    }
+    const int m = p.m, n = p.n, r = p.r;
+    // project.rs:36-46: Temp(r x n) = P^T G, sum over k of p[k*r+i] * g[k*n+j].
+    AETH_TRY(simt_gemm_exact(p.P, 1, r, g, n, 1, p.temp, n, r, n, m, SIMT_STORE, 1.0f, nullptr, st));
+    // project.rs:46 + adamw.rs:91-96: accum += Temp Q.
+    AETH_TRY(simt_gemm_exact(p.temp, n, 1, p.Q, r, 1, p.accum, r, r, r, n, SIMT_ACCUM, 1.0f, nullptr, st));
+    return AETH_OK;
+}
+
+int ref_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, const aeth_weight_ref* w,
+              cudaStream_t st) {
+    const aeth_galore_config& cfg = c->cfg;
+    const int m = p.m, n = p.n, r = p.r;
+    ref_adam_kernel<<<1, 1024, 0, st>>>(p.accum, p.m8, p.v8, p.mscale, p.mom, p.var, p.normalized,
+                                        (int64_t)r * r, clip, clip_dev, cfg.beta1, cfg.beta2, cfg.eps);
+    AETH_LAUNCH_CHECK();
+    const float lr = cfg.scale_lr_by_rank ? cfg.lr / (float)(r < 1 ? 1 : r) : cfg.lr;  // adamw.rs:37-43
+    // project.rs:50-58: Temp(m x r) = P N; dW = Temp Q^T; dW *= lr.
+    AETH_TRY(simt_gemm_exact(p.P, r, 1, p.normalized, r, 1, p.temp, r, m, r, r, SIMT_STORE, 1.0f, nullptr, st));
+    const int kind = w ? w->kind : AETH_WEIGHT_NONE;
+    if (kind == AETH_WEIGHT_F32) {
+        AETH_TRY(simt_gemm_exact(p.temp, r, 1, p.Q, 1, r, static_cast<float*>(w->data), n, m, n, r, SIMT_SUB_SCALED,
+                                 lr, w->delta_out, st));
+    } else {
+        float* dst = (kind == AETH_WEIGHT_NF4) ? p.dtmp : (w ? w->delta_out : nullptr);
+        if (kind == AETH_WEIGHT_NF4 && w->delta_out) dst = w->delta_out;
+        if (dst) AETH_TRY(simt_gemm_exact(p.temp, r, 1, p.Q, 1, r, dst, n, m, n, r, SIMT_SCALE, lr, nullptr, st));
+        if (kind == AETH_WEIGHT_NF4) {
+            if (((int64_t)m * n) % 64 != 0) return AETH_ERR_SHAPE;
+            int64_t nb = (int64_t)m * n / 64;
+            nf4_apply_delta_kernel<<<grid_for(nb, 128), 128, 0, st>>>(static_cast<uint8_t*>(w->data), w->absmax, dst,
+                                                                    nb, w->prequant_out);
+            AETH_LAUNCH_CHECK();
+        }
+    }
+    return AETH_OK;
+}
+
+// ---- B200 mode ------------------------------------------------------------
+int b2_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t st) {
+    const int m = p.m, n = p.n, r = p.r;
+    if (dtype != AETH_DTYPE_BF16) {
+        // f32 / f16 gradients are rounded to bf16 (RNE) first; the buffer is
+        // allocated on the first such call.
+        if (!p.gbf) AETH_CUDA(cudaMalloc(&p.gbf, (size_t)m * n * sizeof(uint16_t)));
+        to_bf16_kernel<<<grid_for((int64_t)m * n, 256), 256, 0, st>>>(grad, dtype, (int64_t)m * n, p.gbf);
+        AETH_LAUNCH_CHECK();
+        grad = p.gbf;
+    }
+    EpiAccum epi{p.accum, r};
+    if (p.side == 2) {
+        // R(m x r) += G Q : A = G (K-major, ld n), B(k,j) = Q[k][j] = projT[j*n + k] (K-major, ld n)
+        return tc_gemm<false, false>(TcOperand{grad, n}, TcOperand{p.projT, n}, m, r, n, true, epi, st);
+    }
+    // R^T(n x r) += G^T P : A(i,k) = G[k*n + i] (MN-major, ld n), B(k,j) = P[k][j] = projT[j*m + k] (K-major, ld m)
+    return tc_gemm<true, false>(TcOperand{grad, n}, TcOperand{p.projT, m}, n, r, m, true, epi, st);
+}
+
+int b2_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, const aeth_weight_ref* w,
+             int zero_accum, cudaStream_t st) {
+    const aeth_galore_config& cfg = c->cfg;
+    AETH_TRY(codec_maps_ensure());
+    AdamB2Args a;
+    a.accum = p.accum;
+    a.m8 = p.m8;
+    a.v8 = p.v8;
+    a.m_scales = p.mscale;
+    a.v_scales = p.vscale;
+    a.n_out = p.nbuf;
+    a.count = p.state_elems;
+    a.block = cfg.state_block;
+    a.codec = cfg.state_codec;
+    a.clip_host = clip;
+    a.clip_dev = clip_dev;
+    a.b1 = cfg.beta1;
+    a.b2 = cfg.beta2;
+    a.eps = cfg.eps;
+    a.zero_accum = zero_accum;
+    b2_adam_kernel<<<grid_for(p.state_blocks, 1, 148 * 8), 256, 0, st>>>(a);
+    AETH_LAUNCH_CHECK();
+    const int m = p.m, n = p.n, r = p.r;
+    const float lr = cfg.scale_lr_by_rank ? cfg.lr / (float)(r < 1 ? 1 : r) : cfg.lr;
+    const int has_decay = cfg.weight_decay > 0.0f;
+    const float decay_mul = 1.0f - lr * cfg.weight_decay;
+    // dW = X Y^T with X (m x r), Y (n x r), both K-major.
+    TcOperand X = p.side == 2 ? TcOperand{p.nbuf, r} : TcOperand{p.proj, r};
+    TcOperand Y = p.side == 2 ? TcOperand{p.proj, r} : TcOperand{p.nbuf, r};
+    const int kind = w ? w->kind : AETH_WEIGHT_NONE;
+    if (kind == AETH_WEIGHT_NF4) {
+        if (n % 64 != 0) return AETH_ERR_UNSUPPORTED;
+        EpiNf4Update e{static_cast<uint8_t*>(w->data), w->absmax, n, lr, decay_mul, has_decay, w->delta_out,
+                       w->prequant_out};
+        return tc_gemm_launch<256, 2, false, false>(X, Y, m, n, r, true, e, st);
+    }
+    if (kind == AETH_WEIGHT_F32) {
+        EpiF32Update e{static_cast<float*>(w->data), n, lr, decay_mul, has_decay, w->delta_out};
+        return tc_gemm_launch<256, 2, false, false>(X, Y, m, n, r, true, e, st);
+    }
+    if (w && w->delta_out) {
+        // take_weight_delta semantics: delta = lr * dW (fp32).
+        EpiStore s{w->delta_out, n, AETH_DTYPE_F32, lr};
+        return tc_gemm_launch<256, 2, false, false>(X, Y, m, n, r, true, s, st);
+    }
+    return AETH_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* aeth_version(void) { return "aeth_galore 0.1 (sm_100a)"; }
+
+const char* aeth_status_string(int st) {
+    switch (st) {
+        case AETH_OK: return "ok";
+        case AETH_ERR_ARG: return "invalid argument";
+        case AETH_ERR_SHAPE: return "shape mismatch";
+        case AETH_ERR_CONFIG: return "configuration error";
+        case AETH_ERR_UNSUPPORTED: return "unsupported shape or alignment";
+        case AETH_ERR_NOT_FOUND: return "unknown parameter";
+        case AETH_ERR_TIMEOUT: return "device wait timed out";
+        default: return st > 0 ? cudaGetErrorString((cudaError_t)st) : "unknown error";
+    }
+}
+
+int aeth_last_error(void) { return tl_last_error; }
+
+int aeth_device_error(int device) {
+    DeviceGuard g(device);
+    DeviceRuntime* rt = nullptr;
+    AETH_TRY(runtime_for_current(&rt));
+    AETH_CUDA(cudaDeviceSynchronize());
+    uint32_t v = 0;
+    AETH_CUDA(cudaMemcpy(&v, rt->err_word, sizeof(v), cudaMemcpyDeviceToHost));
+    AETH_CUDA(cudaMemset(rt->err_word, 0, sizeof(uint32_t)));
+    return v ? AETH_ERR_TIMEOUT : AETH_OK;
+}
+
+int aeth_dynamic_map(int is_signed, float out[256]) {
+    if (!out) return AETH_ERR_ARG;
+    return build_dynamic_map(is_signed, out);
+}
+
+// ---------------------------------------------------------------------------
+// Reference-compatible symbols
+// ---------------------------------------------------------------------------
+int galore_project_forward(const void* G, const void* P, const void* Q, void* R, void* temp, int m, int n, int r,
+                           aeth_stream_t stream) {
+    if (m <= 0 || n <= 0 || r <= 0) return set_err(AETH_ERR_ARG);
+    if (!G || !P || !Q || !R || !temp) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    // Temp(r x n) = P^T G: A(i,k) = P[k*r + i] (MN-major), B(k,j) = G[k*n + j] (MN-major)
+    EpiStore e1{temp, n, AETH_DTYPE_F16, 1.0f};
+    int s1 = tc_gemm<true, true>(TcOperand{P, r}, TcOperand{G, n}, r, n, m, false, e1, st);
+    if (s1 == AETH_ERR_UNSUPPORTED) {
+        simt_gemm_any_kernel<<<grid_for((int64_t)r * n, 256), 256, 0, st>>>(P, AETH_DTYPE_F16, 1, r, G, AETH_DTYPE_F16,
+                                                                          n, 1, temp, AETH_DTYPE_F16, n, r, n, m);
+        AETH_LAUNCH_CHECK();
+    } else if (s1 != AETH_OK) {
+        return set_err(s1);
+    }
+    // R(r x r) = Temp Q: A = Temp (K-major, ld n), B(k,j) = Q[k*r + j] (MN-major, ld r)
+    EpiStore e2{R, r, AETH_DTYPE_F16, 1.0f};
+    int s2 = tc_gemm<false, true>(TcOperand{temp, n}, TcOperand{Q, r}, r, r, n, false, e2, st);
+    if (s2 == AETH_ERR_UNSUPPORTED) {
+        simt_gemm_any_kernel<<<grid_for((int64_t)r * r, 256), 256, 0, st>>>(temp, AETH_DTYPE_F16, n, 1, Q,
+                                                                          AETH_DTYPE_F16, r, 1, R, AETH_DTYPE_F16, r, r,
+                                                                          r, n);
+        AETH_LAUNCH_CHECK();
+    } else if (s2 != AETH_OK) {
+        return set_err(s2);
+    }
+    return AETH_OK;
+}
+
+int galore_project_backward(const void* N, const void* P, const void* Q, void* G_tilde, void* temp, int m, int n,
+                            int r, aeth_stream_t stream) {
+    if (m <= 0 || n <= 0 || r <= 0) return set_err(AETH_ERR_ARG);
+    if (!N || !P || !Q || !G_tilde || !temp) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    // Temp(m x r) = P N: A = P (K-major, ld r), B(k,j) = N[k*r + j] (MN-major, ld r)
+    EpiStore e1{temp, r, AETH_DTYPE_F16, 1.0f};
+    int s1 = tc_gemm<false, true>(TcOperand{P, r}, TcOperand{N, r}, m, r, r, false, e1, st);
+    if (s1 == AETH_ERR_UNSUPPORTED) {
+        simt_gemm_any_kernel<<<grid_for((int64_t)m * r, 256), 256, 0, st>>>(P, AETH_DTYPE_F16, r, 1, N, AETH_DTYPE_F16,
+                                                                          r, 1, temp, AETH_DTYPE_F16, r, m, r, r);
+        AETH_LAUNCH_CHECK();
+    } else if (s1 != AETH_OK) {
+        return set_err(s1);
+    }
+    // G~(m x n) = Temp Q^T: A = Temp (K-major, ld r), B(k,j) = Q[j*r + k] (K-major, ld r)
+    EpiStore e2{G_tilde, n, AETH_DTYPE_F16, 1.0f};
+    int s2 = tc_gemm<false, false>(TcOperand{temp, r}, TcOperand{Q, r}, m, n, r, false, e2, st);
+    if (s2 == AETH_ERR_UNSUPPORTED) {
+        simt_gemm_any_kernel<<<grid_for((int64_t)m * n, 256), 256, 0, st>>>(temp, AETH_DTYPE_F16, r, 1, Q,
+                                                                          AETH_DTYPE_F16, 1, r, G_tilde, AETH_DTYPE_F16,
+                                                                          n, m, n, r);
+        AETH_LAUNCH_CHECK();
+    } else if (s2 != AETH_OK) {
+        return set_err(s2);
+    }
+    return AETH_OK;
+}
+
+int galore_quantize_absmax_f32_to_i8(const float* src, int8_t* dst, float* scale_out, int n_elements,
+                                     aeth_stream_t stream) {
+    if (n_elements <= 0 || !src || !dst || !scale_out) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    AETH_CUDA(cudaMemsetAsync(scale_out, 0, sizeof(float), st));
+    absmax_reduce_kernel<<<grid_for(n_elements, 256, 148 * 4), 256, 0, st>>>(src, n_elements, scale_out);
+    per_tensor_encode_kernel<<<grid_for(n_elements, 256), 256, 0, st>>>(src, n_elements, scale_out, dst);
+    per_tensor_finalize_kernel<<<1, 1, 0, st>>>(scale_out);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int galore_dequantize_i8_to_f32(const int8_t* src, float* dst, float scale, int n_elements, aeth_stream_t stream) {
+    if (n_elements <= 0 || !src || !dst) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    dequant_linear_kernel<<<grid_for(n_elements, 256), 256, 0, st>>>(src, nullptr, scale, n_elements, 0, dst);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+void doublepass_galore_apply(float* param, const float* grad_lr, float* m, float* v, float clip_scale, float beta1,
+                             float beta2, float eps, float lr, int n_elements, int step) {
+    tl_last_error = AETH_OK;
+    if (n_elements <= 0 || !param || !grad_lr || !m || !v) {
+        set_err(AETH_ERR_ARG);
+        return;
+    }
+    float bc1 = 1.0f, bc2 = 1.0f;
+    if (step >= 1) {
+        bc1 = (float)(1.0 - pow((double)beta1, (double)step));
+        bc2 = (float)(1.0 - pow((double)beta2, (double)step));
+    }
+    full_adam_kernel<<<grid_for(n_elements, 256), 256, 0, 0>>>(param, grad_lr, m, v, n_elements, clip_scale, beta1,
+                                                               beta2, eps, lr, step >= 1 ? 1 : 0, bc1, bc2);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) set_err((int)e);
+}
+
+// ---------------------------------------------------------------------------
+// Optimizer handle
+// ---------------------------------------------------------------------------
+void aeth_galore_config_default(aeth_galore_config* c) {
+    if (!c) return;
+    memset(c, 0, sizeof(*c));
+    c->mode = AETH_MODE_REF;
+    c->default_rank = 16;   // GaLoreConfig::default rank (optimizer.rs:49-60)
+    c->attn_rank = 32;      // LayerRankConfig::default (layer_rank.rs:19-27)
+    c->mlp_rank = 16;
+    c->vector_rank = 8;
+    c->switch_interval = 200;
+    c->oversampling = 10;
+    c->beta1 = 0.9f;        // AdamWConfig::default (adamw.rs:23-33)
+    c->beta2 = 0.999f;
+    c->eps = 1e-8f;
+    c->lr = 1e-3f;
+    c->weight_decay = 0.0f;
+    c->scale_lr_by_rank = 0;
+    c->max_grad_norm = 1.0f;  // TrainingPlan (doublepass/src/plan.rs)
+    c->state_codec = AETH_CODEC_PER_TENSOR;
+    c->state_block = 2048;
+    c->init_projectors = 1;
+}
+
+int aeth_galore_destroy(aeth_galore_ctx* ctx) {
+    if (!ctx) return AETH_ERR_ARG;
+    DeviceGuard g(ctx->device);
+    cudaDeviceSynchronize();
+    for (void* p : ctx->allocs) cudaFree(p);
+    for (Param& p : ctx->params)
+        if (p.gbf) cudaFree(p.gbf);
+    delete ctx;
+    return AETH_OK;
+}
+
+int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* specs, int n_specs, int device,
+                       aeth_galore_ctx** out) {
+    if (!cfg || !out || n_specs < 0 || (n_specs > 0 && !specs)) return set_err(AETH_ERR_ARG);
+    *out = nullptr;
+    if (cfg->mode != AETH_MODE_REF && cfg->mode != AETH_MODE_B200) return set_err(AETH_ERR_CONFIG);
+    if (cfg->mode == AETH_MODE_REF && cfg->state_codec != AETH_CODEC_PER_TENSOR) return set_err(AETH_ERR_CONFIG);
+    if (cfg->mode == AETH_MODE_B200 &&
+        (cfg->state_codec == AETH_CODEC_PER_TENSOR || cfg->state_block <= 0))
+        return set_err(AETH_ERR_CONFIG);
+    DeviceGuard g(device);
+    aeth_galore_ctx* c = new aeth_galore_ctx();
+    c->cfg = *cfg;
+    c->device = device;
+    auto fail = [&](int st) {
+        aeth_galore_destroy(c);
+        return set_err(st);
+    };
+    int st = AETH_OK;
+    if ((st = codec_maps_ensure()) != AETH_OK) return fail(st);
+    c->params.resize(n_specs);
+    for (int i = 0; i < n_specs; ++i) {
+        const aeth_param_spec& s = specs[i];
+        if (s.m <= 0 || s.n <= 0) return fail(AETH_ERR_SHAPE);
+        for (int j = 0; j < i; ++j)
+            if (specs[j].layer_idx == s.layer_idx && std::string(specs[j].name ? specs[j].name : "") == (s.name ? s.name : ""))
+                return fail(AETH_ERR_CONFIG);
+        Param& p = c->params[i];
+        p.layer = s.layer_idx;
+        p.name = s.name ? s.name : "";
+        p.m = s.m;
+        p.n = s.n;
+        p.r = s.rank > 0 ? s.rank : rank_for_param(*cfg, s.name, s.m, s.n);
+        if (p.r > (s.m < s.n ? s.m : s.n)) return fail(AETH_ERR_CONFIG);
+        const int m = p.m, n = p.n, r = p.r;
+        if (cfg->mode == AETH_MODE_REF) {
+            p.side = 0;
+            p.state_elems = (int64_t)r * r;
+            p.state_blocks = 1;
+            if ((st = ctx_alloc(c, &p.P, (int64_t)m * r)) || (st = ctx_alloc(c, &p.Q, (int64_t)n * r)) ||
+                (st = ctx_alloc(c, &p.mom, (int64_t)r * r)) || (st = ctx_alloc(c, &p.var, (int64_t)r * r)) ||
+                (st = ctx_alloc(c, &p.normalized, (int64_t)r * r)) ||
+                (st = ctx_alloc(c, &p.temp, std::max((int64_t)r * n, (int64_t)m * r))) ||
+                (st = ctx_alloc(c, &p.gtmp, (int64_t)m * n)) || (st = ctx_alloc(c, &p.dtmp, (int64_t)m * n)))
+                return fail(st);
+        } else {
+            p.side = m >= n ? 2 : 1;
+            const int64_t l = m >= n ? m : n;
+            const int s_dim = m >= n ? n : m;
+            p.state_elems = l * r;
+            p.state_blocks = (p.state_elems + cfg->state_block - 1) / cfg->state_block;
+            if ((st = ctx_alloc(c, &p.proj, (int64_t)s_dim * r)) || (st = ctx_alloc(c, &p.projT, (int64_t)s_dim * r)) ||
+                (st = ctx_alloc(c, &p.nbuf, p.state_elems)))
+                return fail(st);
+        }
+        if ((st = ctx_alloc(c, &p.accum, p.state_elems)) || (st = ctx_alloc(c, &p.m8, p.state_elems)) ||
+            (st = ctx_alloc(c, &p.v8, p.state_elems)) || (st = ctx_alloc(c, &p.mscale, p.state_blocks)) ||
+            (st = ctx_alloc(c, &p.vscale, p.state_blocks)))
+            return fail(st);
+        if ((st = reset_state(c, p, 0)) != AETH_OK) return fail(st);
+        // Projector initialisation (optimizer.rs:98-100): P from seed layer*17, Q from layer*31.
+        const bool want_p = cfg->mode == AETH_MODE_REF || p.side == 1;
+        const bool want_q = cfg->mode == AETH_MODE_REF || p.side == 2;
+        std::vector<float> hp, hq;
+        if (cfg->init_projectors) {
+            if (want_p) { hp.resize((size_t)m * r); init_random_projection_host(m, r, p.layer * 17u, hp.data()); }
+            if (want_q) { hq.resize((size_t)n * r); init_random_projection_host(n, r, p.layer * 31u, hq.data()); }
+        } else {
+            if (want_p) hp.assign((size_t)m * r, 0.0f);
+            if (want_q) hq.assign((size_t)n * r, 0.0f);
+        }
+        if (cfg->mode == AETH_MODE_REF) {
+            if (cudaMemcpy(p.P, hp.data(), hp.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(p.Q, hq.data(), hq.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                return fail(AETH_ERR_CONFIG);
+        } else {
+            const std::vector<float>& src = p.side == 1 ? hp : hq;
+            const int s_dim = p.side == 1 ? m : n;
+            std::vector<uint16_t> b(src.size()), bt(src.size());
+            for (int row = 0; row < s_dim; ++row)
+                for (int col = 0; col < r; ++col) {
+                    uint16_t v = host_f32_to_bf16(src[(size_t)row * r + col]);
+                    b[(size_t)row * r + col] = v;
+                    bt[(size_t)col * s_dim + row] = v;
+                }
+            if (cudaMemcpy(p.proj, b.data(), b.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(p.projT, bt.data(), bt.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+                return fail(AETH_ERR_CONFIG);
+        }
+    }
+    if ((st = ctx_alloc(c, &c->sq_slots, n_specs)) || (st = ctx_alloc(c, &c->sq_step, n_specs)) ||
+        (st = ctx_alloc(c, &c->partials, kSqPartials)) || (st = ctx_alloc(c, &c->clip_dev, 1)) ||
+        (st = ctx_alloc(c, &c->gnorm_dev, 1)))
+        return fail(st);
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail(AETH_ERR_CONFIG);
+    *out = c;
+    return AETH_OK;
+}
+
+int aeth_galore_num_params(const aeth_galore_ctx* ctx) { return ctx ? (int)ctx->params.size() : AETH_ERR_ARG; }
+
+int aeth_galore_find(const aeth_galore_ctx* ctx, uint32_t layer_idx, const char* name) {
+    if (!ctx || !name) return AETH_ERR_ARG;
+    for (size_t i = 0; i < ctx->params.size(); ++i)
+        if (ctx->params[i].layer == layer_idx && ctx->params[i].name == name) return (int)i;
+    return AETH_ERR_NOT_FOUND;
+}
+
+int aeth_galore_param_info(const aeth_galore_ctx* ctx, int idx, aeth_param_info* out) {
+    AETH_TRY(check_idx(ctx, idx));
+    if (!out) return AETH_ERR_ARG;
+    const Param& p = ctx->params[idx];
+    out->m = p.m;
+    out->n = p.n;
+    out->rank = p.r;
+    out->side = p.side;
+    out->state_elems = p.state_elems;
+    out->state_blocks = p.state_blocks;
+    out->layer_idx = p.layer;
+    return AETH_OK;
+}
+
+int aeth_galore_project_accumulate(aeth_galore_ctx* ctx, int idx, const void* grad, int grad_dtype,
+                                   aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    if (!grad) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    cudaStream_t st = to_stream(stream);
+    if (ctx->cfg.mode == AETH_MODE_REF) return set_err(ref_project_accumulate(p, grad, grad_dtype, st));
+    return set_err(b2_project_accumulate(p, grad, grad_dtype, st));
+}
+
+int aeth_galore_sqnorm_device(aeth_galore_ctx* ctx, int idx, double* out_dev, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    return set_err(sqnorm_into(ctx, p, out_dev ? out_dev : ctx->sq_slots + idx, to_stream(stream)));
+}
+
+int aeth_galore_sqnorm(aeth_galore_ctx* ctx, int idx, double* out_host, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    if (!out_host) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    AETH_TRY(sqnorm_into(ctx, ctx->params[idx], ctx->sq_slots + idx, st));
+    AETH_CUDA(cudaMemcpyAsync(out_host, ctx->sq_slots + idx, sizeof(double), cudaMemcpyDeviceToHost, st));
+    AETH_CUDA(cudaStreamSynchronize(st));
+    return AETH_OK;
+}
+
+int aeth_clip_coeff_device(const double* sq_dev, int n, float max_norm, float* clip_dev, double* gnorm_dev,
+                           aeth_stream_t stream) {
+    if (!sq_dev || n <= 0 || !clip_dev) return set_err(AETH_ERR_ARG);
+    clip_coeff_kernel<<<1, 32, 0, to_stream(stream)>>>(sq_dev, n, max_norm, clip_dev, gnorm_dev);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_galore_apply_update(aeth_galore_ctx* ctx, int idx, float clip, const float* clip_dev,
+                             const aeth_weight_ref* w, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    cudaStream_t st = to_stream(stream);
+    if (w && w->kind != AETH_WEIGHT_NONE && !w->data) return set_err(AETH_ERR_ARG);
+    if (w && w->kind == AETH_WEIGHT_NF4 && !w->absmax) return set_err(AETH_ERR_ARG);
+    if (ctx->cfg.mode == AETH_MODE_REF) return set_err(ref_apply(ctx, p, clip, clip_dev, w, st));
+    return set_err(b2_apply(ctx, p, clip, clip_dev, w, 0, st));
+}
+
+int aeth_galore_zero_accum(aeth_galore_ctx* ctx, int idx, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    AETH_CUDA(cudaMemsetAsync(p.accum, 0, p.state_elems * sizeof(float), to_stream(stream)));
+    return AETH_OK;
+}
+
+int aeth_galore_notify_step(aeth_galore_ctx* ctx, uint64_t step) {
+    if (!ctx) return AETH_ERR_ARG;
+    ctx->step = step;
+    return AETH_OK;
+}
+
+uint64_t aeth_galore_step_count(const aeth_galore_ctx* ctx) { return ctx ? ctx->step : 0; }
+
+int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
+                     const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out,
+                     aeth_stream_t stream) {
+    if (!ctx || n <= 0 || !idx || !grads) return set_err(AETH_ERR_ARG);
+    if (n > (int)ctx->params.size()) return set_err(AETH_ERR_ARG);
+    for (int i = 0; i < n; ++i) AETH_TRY(check_idx(ctx, idx[i]));
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    const bool ref = ctx->cfg.mode == AETH_MODE_REF;
+    // A3 hook: project_and_accumulate for every parameter (backward.rs:510-521).
+    for (int i = 0; i < n; ++i) {
+        Param& p = ctx->params[idx[i]];
+        AETH_TRY(ref ? ref_project_accumulate(p, grads[i], grad_dtype, st)
+                     : b2_project_accumulate(p, grads[i], grad_dtype, st));
+    }
+    // A6 pass 1: squared norms (hook.rs:149-182).
+    for (int i = 0; i < n; ++i) AETH_TRY(sqnorm_into(ctx, ctx->params[idx[i]], ctx->sq_step + i, st));
+    if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
+    float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
+    clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
+    AETH_LAUNCH_CHECK();
+    // A6 pass 2: apply_update + zero_accum (hook.rs:190-194).
+    for (int i = 0; i < n; ++i) {
+        Param& p = ctx->params[idx[i]];
+        const aeth_weight_ref* w = weights ? &weights[i] : nullptr;
+        if (ref) {
+            AETH_TRY(ref_apply(ctx, p, 1.0f, clip, w, st));
+            AETH_CUDA(cudaMemsetAsync(p.accum, 0, p.state_elems * sizeof(float), st));
+        } else {
+            AETH_TRY(b2_apply(ctx, p, 1.0f, clip, w, 1, st));
+        }
+    }
+    return AETH_OK;
+}
+
+int aeth_galore_set_projector(aeth_galore_ctx* ctx, int idx, const float* P, const float* Q, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    cudaStream_t st = to_stream(stream);
+    if (ctx->cfg.mode == AETH_MODE_REF) {
+        if (!P || !Q) return set_err(AETH_ERR_ARG);
+        AETH_CUDA(cudaMemcpyAsync(p.P, P, (size_t)p.m * p.r * 4, cudaMemcpyDeviceToDevice, st));
+        AETH_CUDA(cudaMemcpyAsync(p.Q, Q, (size_t)p.n * p.r * 4, cudaMemcpyDeviceToDevice, st));
+    } else {
+        const float* src = p.side == 1 ? P : Q;
+        if (!src) return set_err(AETH_ERR_ARG);
+        const int s_dim = p.side == 1 ? p.m : p.n;
+        proj_to_bf16_kernel<<<grid_for((int64_t)s_dim * p.r, 256), 256, 0, st>>>(src, s_dim, p.r, p.proj, p.projT);
+        AETH_LAUNCH_CHECK();
+    }
+    // Subspace switch resets the Adam state (optimizer.rs:236-238).
+    return set_err(reset_state(ctx, p, st));
+}
+
+int aeth_galore_get_projector(aeth_galore_ctx* ctx, int idx, float* P, float* Q, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    cudaStream_t st = to_stream(stream);
+    if (ctx->cfg.mode == AETH_MODE_REF) {
+        if (P) AETH_CUDA(cudaMemcpyAsync(P, p.P, (size_t)p.m * p.r * 4, cudaMemcpyDeviceToDevice, st));
+        if (Q) AETH_CUDA(cudaMemcpyAsync(Q, p.Q, (size_t)p.n * p.r * 4, cudaMemcpyDeviceToDevice, st));
+    } else {
+        float* dst = p.side == 1 ? P : Q;
+        const int s_dim = p.side == 1 ? p.m : p.n;
+        if (dst) {
+            bf16_to_f32_kernel<<<grid_for((int64_t)s_dim * p.r, 256), 256, 0, st>>>(p.proj, (int64_t)s_dim * p.r, dst);
+            AETH_LAUNCH_CHECK();
+        }
+    }
+    return AETH_OK;
+}
+
+int aeth_galore_get_state(aeth_galore_ctx* ctx, int idx, int8_t* m8, int8_t* v8, float* m_scales, float* v_scales,
+                          aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    cudaStream_t st = to_stream(stream);
+    if (m8) AETH_CUDA(cudaMemcpyAsync(m8, p.m8, p.state_elems, cudaMemcpyDeviceToDevice, st));
+    if (v8) AETH_CUDA(cudaMemcpyAsync(v8, p.v8, p.state_elems, cudaMemcpyDeviceToDevice, st));
+    if (m_scales) AETH_CUDA(cudaMemcpyAsync(m_scales, p.mscale, p.state_blocks * 4, cudaMemcpyDeviceToDevice, st));
+    if (v_scales) AETH_CUDA(cudaMemcpyAsync(v_scales, p.vscale, p.state_blocks * 4, cudaMemcpyDeviceToDevice, st));
+    return AETH_OK;
+}
+
+int aeth_galore_set_state(aeth_galore_ctx* ctx, int idx, const int8_t* m8, const int8_t* v8, const float* m_scales,
+                          const float* v_scales, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    cudaStream_t st = to_stream(stream);
+    if (m8) AETH_CUDA(cudaMemcpyAsync(p.m8, m8, p.state_elems, cudaMemcpyDeviceToDevice, st));
+    if (v8) AETH_CUDA(cudaMemcpyAsync(p.v8, v8, p.state_elems, cudaMemcpyDeviceToDevice, st));
+    if (m_scales) AETH_CUDA(cudaMemcpyAsync(p.mscale, m_scales, p.state_blocks * 4, cudaMemcpyDeviceToDevice, st));
+    if (v_scales) AETH_CUDA(cudaMemcpyAsync(p.vscale, v_scales, p.state_blocks * 4, cudaMemcpyDeviceToDevice, st));
+    return AETH_OK;
+}
+
+int aeth_galore_get_accum(aeth_galore_ctx* ctx, int idx, float* accum, aeth_stream_t stream) {
+    AETH_TRY(check_idx(ctx, idx));
+    if (!accum) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    Param& p = ctx->params[idx];
+    AETH_CUDA(cudaMemcpyAsync(accum, p.accum, p.state_elems * 4, cudaMemcpyDeviceToDevice, to_stream(stream)));
+    return AETH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Stand-alone kernels
+// ---------------------------------------------------------------------------
+int aeth_nf4_dequant(const uint8_t* packed, const float* absmax, int64_t n, int block, void* out, int out_dtype,
+                     aeth_stream_t stream) {
+    if (!packed || !absmax || !out || n <= 0 || block <= 0) return set_err(AETH_ERR_ARG);
+    if (out_dtype < AETH_DTYPE_F32 || out_dtype > AETH_DTYPE_BF16) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    const bool aligned = (reinterpret_cast<uintptr_t>(packed) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    if (block == 64 && n % 32 == 0 && aligned) {
+        int64_t chunks = n / 32;
+        int grid = grid_for(chunks, 256, 148 * 8);
+        if (out_dtype == AETH_DTYPE_F32)
+            nf4_dequant64_kernel<float><<<grid, 256, 0, st>>>(packed, absmax, chunks, static_cast<float*>(out));
+        else if (out_dtype == AETH_DTYPE_F16)
+            nf4_dequant64_kernel<__half><<<grid, 256, 0, st>>>(packed, absmax, chunks, static_cast<__half*>(out));
+        else
+            nf4_dequant64_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(packed, absmax, chunks,
+                                                                      static_cast<__nv_bfloat16*>(out));
+    } else {
+        nf4_dequant_generic_kernel<<<grid_for(n, 256), 256, 0, st>>>(packed, absmax, n, block, out, out_dtype);
+    }
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_nf4_quant(const void* x, int x_dtype, int64_t n, int block, uint8_t* packed, float* absmax,
+                   aeth_stream_t stream) {
+    if (!x || !packed || !absmax || n <= 0 || block <= 0) return set_err(AETH_ERR_ARG);
+    if (x_dtype < AETH_DTYPE_F32 || x_dtype > AETH_DTYPE_BF16) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(packed) & 7) == 0;
+    if (block == 64 && n % 64 == 0 && aligned) {
+        int64_t nb = n / 64;
+        nf4_quant64_kernel<<<grid_for(nb * 4, 256, 148 * 8), 256, 0, st>>>(x, x_dtype, nb, packed, absmax);
+    } else {
+        int64_t nb = (n + block - 1) / block;
+        nf4_absmax_generic_kernel<<<grid_for(nb * 32, 256), 256, 0, st>>>(x, x_dtype, n, block, nb, absmax);
+        nf4_pack_generic_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, st>>>(x, x_dtype, n, block, absmax, packed);
+    }
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_int8_quantize(const float* x, int64_t n, int codec, int block, int is_signed, int8_t* q, float* scales,
+                       aeth_stream_t stream) {
+    if (!x || !q || !scales || n <= 0) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    AETH_TRY(codec_maps_ensure());
+    if (codec == AETH_CODEC_PER_TENSOR) {
+        AETH_CUDA(cudaMemsetAsync(scales, 0, sizeof(float), st));
+        absmax_reduce_kernel<<<grid_for(n, 256, 148 * 4), 256, 0, st>>>(x, n, scales);
+        per_tensor_encode_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, n, scales, q);
+        per_tensor_finalize_kernel<<<1, 1, 0, st>>>(scales);
+    } else if (codec == AETH_CODEC_BLOCK_LINEAR || codec == AETH_CODEC_BLOCK_DYNAMIC) {
+        if (block <= 0) return set_err(AETH_ERR_ARG);
+        int64_t nb = (n + block - 1) / block;
+        block_encode_kernel<<<grid_for(nb, 1, 148 * 8), 256, 0, st>>>(x, n, block, codec, is_signed, q, scales);
+    } else {
+        return set_err(AETH_ERR_ARG);
+    }
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_int8_dequantize(const int8_t* q, const float* scales, int64_t n, int codec, int block, int is_signed,
+                         float* out, aeth_stream_t stream) {
+    if (!q || !scales || !out || n <= 0) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    AETH_TRY(codec_maps_ensure());
+    if (codec == AETH_CODEC_PER_TENSOR) {
+        dequant_linear_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, scales, 0.0f, n, 0, out);
+    } else if (codec == AETH_CODEC_BLOCK_LINEAR) {
+        if (block <= 0) return set_err(AETH_ERR_ARG);
+        dequant_linear_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, scales, 0.0f, n, block, out);
+    } else if (codec == AETH_CODEC_BLOCK_DYNAMIC) {
+        if (block <= 0) return set_err(AETH_ERR_ARG);
+        dequant_dynamic_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, scales, n, block, is_signed, out);
+    } else {
+        return set_err(AETH_ERR_ARG);
+    }
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_lomo_sqnorm(const void* grad_bf16, int64_t n, double* sq_dev, aeth_stream_t stream) {
+    if (!grad_bf16 || !sq_dev || n <= 0) return set_err(AETH_ERR_ARG);
+    if ((reinterpret_cast<uintptr_t>(grad_bf16) & 15) != 0) return set_err(AETH_ERR_UNSUPPORTED);
+    lomo_sqnorm_kernel<<<grid_for(n / 8 + 1, 256, 148 * 4), 256, 0, to_stream(stream)>>>(
+        static_cast<const uint16_t*>(grad_bf16), n, sq_dev);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_lomo_update(const void* grad_bf16, int64_t n, const double* sq_dev, float max_norm, float lr, float beta,
+                     int codec, int block, int8_t* mom8, float* mom_scales, uint8_t* w_packed, float* w_absmax,
+                     float* prequant_out, aeth_stream_t stream) {
+    if (!grad_bf16 || !sq_dev || !mom8 || !mom_scales || !w_packed || !w_absmax || n <= 0) return set_err(AETH_ERR_ARG);
+    if (block != 2048 || n % 2048 != 0) return set_err(AETH_ERR_UNSUPPORTED);
+    if (codec != AETH_CODEC_BLOCK_LINEAR && codec != AETH_CODEC_BLOCK_DYNAMIC) return set_err(AETH_ERR_ARG);
+    if ((reinterpret_cast<uintptr_t>(grad_bf16) & 15) || (reinterpret_cast<uintptr_t>(mom8) & 7) ||
+        (reinterpret_cast<uintptr_t>(w_packed) & 3))
+        return set_err(AETH_ERR_UNSUPPORTED);
+    AETH_TRY(codec_maps_ensure());
+    int64_t nb = n / 2048;
+    lomo_update_kernel<<<grid_for(nb, 1, 148 * 8), 256, 0, to_stream(stream)>>>(
+        static_cast<const uint16_t*>(grad_bf16), n, sq_dev, max_norm, lr, beta, codec, mom8, mom_scales, w_packed,
+        w_absmax, prequant_out);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+}  // extern "C"

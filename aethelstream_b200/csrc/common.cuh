@@ -1,0 +1,130 @@
+// common.cuh -- status codes, per-thread last error, bounded device waits and
+// small numeric helpers shared by every kernel of libaeth_galore.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/aeth_galore.h"
+
+namespace aeth {
+
+// Last status recorded on the calling host thread (read by aeth_last_error()).
+inline thread_local int tl_last_error = AETH_OK;
+
+inline int set_err(int st) {
+    if (st != AETH_OK) tl_last_error = st;
+    return st;
+}
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? AETH_OK : set_err((int)e); }
+
+#define AETH_TRY(expr)                                 \
+    do {                                               \
+        int _st = (expr);                              \
+        if (_st != AETH_OK) return ::aeth::set_err(_st); \
+    } while (0)
+
+#define AETH_CUDA(expr)                                         \
+    do {                                                        \
+        cudaError_t _e = (expr);                                \
+        if (_e != cudaSuccess) return ::aeth::set_err((int)_e); \
+    } while (0)
+
+// Kernel-launch check: configuration errors surface here, asynchronous
+// errors on the next synchronising call.
+#define AETH_LAUNCH_CHECK() AETH_CUDA(cudaGetLastError())
+
+inline cudaStream_t to_stream(aeth_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---------------------------------------------------------------------------
+// Device-side error word.  Kernels with spin waits give up after a time limit
+// and OR a code into this word instead of hanging; the host reads it with
+// aeth_device_error().  One word per device, allocated on first use.
+// ---------------------------------------------------------------------------
+enum : uint32_t { DEVERR_TIMEOUT_TMA = 1u, DEVERR_TIMEOUT_MMA = 2u, DEVERR_TIMEOUT_EPI = 4u, DEVERR_BAD_ARG = 8u };
+
+struct DeviceRuntime {
+    uint32_t* err_word = nullptr;  // device
+    bool init = false;
+};
+
+constexpr int kMaxDevices = 64;
+inline DeviceRuntime g_rt[kMaxDevices];
+
+inline int current_device(int* dev) { return cuda_status(cudaGetDevice(dev)); }
+
+inline int runtime_for_current(DeviceRuntime** out) {
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return set_err(AETH_ERR_UNSUPPORTED);
+    DeviceRuntime& rt = g_rt[dev];
+    if (!rt.init) {
+        AETH_CUDA(cudaMalloc(&rt.err_word, sizeof(uint32_t)));
+        AETH_CUDA(cudaMemset(rt.err_word, 0, sizeof(uint32_t)));
+        rt.init = true;
+    }
+    *out = &rt;
+    return AETH_OK;
+}
+
+// Nanosecond global timer (PTX %globaltimer).
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bound for every device-side wait: long enough for any legitimate stall of
+// these kernels (they never wait on another rank), short enough that a bug
+// ends the kernel within seconds.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ void report_dev_error(uint32_t* err, uint32_t code) {
+    if (err) atomicOr(err, code);
+}
+
+// ---------------------------------------------------------------------------
+// Numeric helpers.  IEEE-rounded intrinsics are used wherever the CPU oracle
+// must be reproduced bit for bit (no FMA contraction, correctly rounded
+// division and square root).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float load_as_f32(const void* p, int64_t i, int dtype) {
+    if (dtype == AETH_DTYPE_F32) return static_cast<const float*>(p)[i];
+    if (dtype == AETH_DTYPE_BF16) return bf16_bits_to_f32(static_cast<const uint16_t*>(p)[i]);
+    return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// atomicMax on a non-negative float stored as its bit pattern.
+__device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
+    atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+inline int grid_for(int64_t work, int threads, int cap = 148 * 16) {
+    int64_t g = (work + threads - 1) / threads;
+    if (g < 1) g = 1;
+    if (g > cap) g = cap;
+    return (int)g;
+}
+
+}  // namespace aeth

@@ -1,0 +1,294 @@
+// nf4.cuh -- NF4 (4-bit NormalFloat, 64-element blocks, fp32 absmax)
+// dequantisation and bit-exact requantisation.
+//
+// Format (shard_engine/src/nf4.rs:6-83, shard_engine/python/pipeline/quantizer.py:21-75):
+//   w[i] = CODES[nib(i)] * absmax[i / 64], nib(i) = high nibble of byte i/2 for even i.
+// Quantisation: absmax = max|x| per block (stored raw); xn = x / max(absmax, 1e-8);
+// code = argmin_c |xn - CODES[c]| with the first index winning ties (torch.argmin).
+//
+// The quantiser here is bit-exact with that definition while avoiding a
+// division and a 16-way search per element: xn is approximated as x * (1/absmax)
+// and classified with a 33-bucket table (bucket width 1/16 is narrower than the
+// smallest gap between decision midpoints, 0.080, so a bucket holds at most one
+// midpoint).  Any element whose approximation lies within 1e-6 of a midpoint --
+// far wider than the few-ulp band in which the approximation or the fp32
+// distance rounding could change the answer -- sends its block through the
+// exact path (IEEE division and the full 16-code argmin).
+#pragma once
+#include "common.cuh"
+
+namespace aeth {
+
+__constant__ float c_nf4_codes[16] = {
+    -1.0f,        -0.6961928f, -0.52507305f, -0.3949175f, -0.28444138f, -0.18477343f,
+    -0.09105004f, 0.0f,        0.0795803f,   0.1609302f,  0.2461123f,   0.33791524f,
+    0.44070983f,  0.562617f,   0.72295684f,  1.0f,
+};
+
+constexpr float kNf4NearWindow = 1e-6f;
+
+struct Nf4Tables {
+    float2 byte_lut[256];  // (CODES[byte >> 4], CODES[byte & 15])
+    float2 bucket[33];     // {midpoint threshold or +inf, lower code index as int bits}
+};
+
+// Fill the shared tables; call with all threads of the CTA, then __syncthreads().
+__device__ __forceinline__ void nf4_tables_init(Nf4Tables* t, int tid, int nthreads) {
+    for (int i = tid; i < 256; i += nthreads)
+        t->byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
+    for (int b = tid; b < 33; b += nthreads) {
+        // bucket b holds xn with rint(16 xn) + 16 == b, i.e. [(b-16.5)/16, (b-15.5)/16)
+        float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
+        int below = 0;
+        float thr = __int_as_float(0x7f800000);  // +inf: no midpoint in this bucket
+        int code = 0;
+        for (int k = 0; k < 15; ++k) {
+            float mid = (c_nf4_codes[k] + c_nf4_codes[k + 1]) * 0.5f;
+            if (mid < lo) below = k + 1;
+            else if (mid < hi) { thr = mid; code = k; }
+        }
+        if (thr == __int_as_float(0x7f800000)) code = below;
+        t->bucket[b] = make_float2(thr, __int_as_float(code));
+    }
+}
+
+// Exact reference decision for one element (quantizer.py:29-35).  Not
+// inlined: it runs only for elements next to a decision boundary, and
+// keeping it out of line keeps the unrolled fast path small.
+__device__ __noinline__ uint32_t nf4_code_exact(float x, float safe) {
+    float xn = __fdiv_rn(x, safe);
+    uint32_t best = 0;
+    float bd = fabsf(__fsub_rn(xn, c_nf4_codes[0]));
+#pragma unroll
+    for (int c = 1; c < 16; ++c) {
+        float d = fabsf(__fsub_rn(xn, c_nf4_codes[c]));
+        if (d < bd) { bd = d; best = (uint32_t)c; }
+    }
+    return best;
+}
+
+// Quantise N values (N a multiple of 8, all in one NF4 block with absmax
+// `amax`) held in registers.  Output: N/8 words, each packing 8 codes in
+// memory byte order (byte k = code[2k] << 4 | code[2k+1]).
+template <int N>
+__device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, const float2* __restrict__ bucket,
+                                               uint32_t (&packed)[N / 8]) {
+    const float safe = fmaxf(amax, 1e-8f);
+    const float inv = __frcp_rn(safe);
+    uint32_t near[N / 8];
+#pragma unroll
+    for (int w = 0; w < N / 8; ++w) {
+        uint32_t word = 0, nb = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float xn = __fmul_rn(v[w * 8 + j], inv);
+            float t = __fmaf_rn(xn, 16.0f, 12582928.0f);  // 1.5*2^23 + 16: low bits = rint(16 xn) + 16
+            float2 e = bucket[__float_as_int(t) & 63];
+            float d = __fsub_rn(xn, e.x);
+            uint32_t code = (uint32_t)__float_as_int(e.y) + (d > 0.0f ? 1u : 0u);
+            nb |= (fabsf(d) < kNf4NearWindow ? 1u : 0u) << j;
+            word |= code << (8 * (j >> 1) + ((j & 1) ? 0 : 4));
+        }
+        packed[w] = word;
+        near[w] = nb;
+    }
+    // Rare: redo the elements next to a boundary with the exact definition.
+#pragma unroll
+    for (int w = 0; w < N / 8; ++w) {
+        if (near[w]) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (near[w] & (1u << j)) {
+                    const uint32_t sh = 8 * (j >> 1) + ((j & 1) ? 0 : 4);
+                    packed[w] = (packed[w] & ~(0xfu << sh)) | (nf4_code_exact(v[w * 8 + j], safe) << sh);
+                }
+            }
+        }
+    }
+}
+
+// Dequantise 8 codes packed in one little-endian word into fp32 products.
+__device__ __forceinline__ void nf4_dequant_word(uint32_t word, float amax, const float2* __restrict__ lut,
+                                                 float* out8) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float2 c = lut[(word >> (8 * k)) & 0xffu];
+        out8[2 * k] = __fmul_rn(c.x, amax);
+        out8[2 * k + 1] = __fmul_rn(c.y, amax);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Stand-alone dequantisation (K1).  Fast kernel: block == 64, n % 32 == 0,
+// 16-byte aligned packed; each thread expands 16 bytes (32 elements).
+// ---------------------------------------------------------------------------
+template <typename OutT>
+__device__ __forceinline__ void store_vals(OutT* out, int64_t base, const float* v, int cnt);
+
+template <>
+__device__ __forceinline__ void store_vals<float>(float* out, int64_t base, const float* v, int cnt) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(out + base + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    (void)cnt;
+}
+
+template <>
+__device__ __forceinline__ void store_vals<__half>(__half* out, int64_t base, const float* v, int cnt) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        uint4 u;
+        __half2 h0 = __floats2half2_rn(v[i], v[i + 1]), h1 = __floats2half2_rn(v[i + 2], v[i + 3]);
+        __half2 h2 = __floats2half2_rn(v[i + 4], v[i + 5]), h3 = __floats2half2_rn(v[i + 6], v[i + 7]);
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        u.z = *reinterpret_cast<uint32_t*>(&h2);
+        u.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(out + base + i) = u;
+    }
+    (void)cnt;
+}
+
+template <>
+__device__ __forceinline__ void store_vals<__nv_bfloat16>(__nv_bfloat16* out, int64_t base, const float* v, int cnt) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        uint4 u;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[i], v[i + 1]), h1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]), h3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        u.z = *reinterpret_cast<uint32_t*>(&h2);
+        u.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(out + base + i) = u;
+    }
+    (void)cnt;
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(256) nf4_dequant64_kernel(const uint8_t* __restrict__ packed,
+                                                            const float* __restrict__ absmax, int64_t n_chunks,
+                                                            OutT* __restrict__ out) {
+    __shared__ float2 lut[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
+    __syncthreads();
+    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < n_chunks; c += (int64_t)gridDim.x * blockDim.x) {
+        uint4 w = __ldg(reinterpret_cast<const uint4*>(packed) + c);
+        float amax = __ldg(absmax + (c >> 1));  // 32 elements per chunk, 64 per block
+        float v[32];
+        nf4_dequant_word(w.x, amax, lut, v);
+        nf4_dequant_word(w.y, amax, lut, v + 8);
+        nf4_dequant_word(w.z, amax, lut, v + 16);
+        nf4_dequant_word(w.w, amax, lut, v + 24);
+        store_vals<OutT>(out, c * 32, v, 32);
+    }
+}
+
+// Generic dequantisation: any block size, any n, any alignment.
+__global__ void nf4_dequant_generic_kernel(const uint8_t* __restrict__ packed, const float* __restrict__ absmax,
+                                           int64_t n, int block, void* __restrict__ out, int out_dtype) {
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        uint8_t byte = packed[e >> 1];
+        int nib = (e & 1) == 0 ? (byte >> 4) & 15 : byte & 15;
+        float v = __fmul_rn(c_nf4_codes[nib], absmax[e / block]);
+        if (out_dtype == AETH_DTYPE_F32) static_cast<float*>(out)[e] = v;
+        else if (out_dtype == AETH_DTYPE_F16) static_cast<__half*>(out)[e] = __float2half_rn(v);
+        else static_cast<__nv_bfloat16*>(out)[e] = __float2bfloat16_rn(v);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Stand-alone quantisation (K2).  Fast kernel: block == 64, n % 64 == 0;
+// 4 threads per block, 16 elements each, absmax by two xor-shuffles.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) nf4_quant64_kernel(const void* __restrict__ x, int x_dtype, int64_t n_blocks,
+                                                          uint8_t* __restrict__ packed, float* __restrict__ absmax) {
+    __shared__ Nf4Tables tab;
+    nf4_tables_init(&tab, threadIdx.x, blockDim.x);
+    __syncthreads();
+    const int64_t n_quads = n_blocks * 4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    // The loop trip count is identical for the 4 lanes of a block (n_quads is a
+    // multiple of 4 and the stride a multiple of 32), so the shuffles below see
+    // all their partners.
+    for (int64_t qd0 = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); qd0 < n_quads; qd0 += stride) {
+        int64_t qd = qd0 + (threadIdx.x & 31);
+        bool active = qd < n_quads;
+        float v[16];
+        int64_t e0 = qd * 16;
+        if (active) {
+            if (x_dtype == AETH_DTYPE_F32) {
+                const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + e0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float4 f = __ldg(p + i);
+                    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+                }
+            } else {
+                const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + e0);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    uint4 u = __ldg(p + i);
+                    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        uint16_t lo = (uint16_t)(w[k] & 0xffffu), hi = (uint16_t)(w[k] >> 16);
+                        if (x_dtype == AETH_DTYPE_BF16) {
+                            v[8 * i + 2 * k] = bf16_bits_to_f32(lo);
+                            v[8 * i + 2 * k + 1] = bf16_bits_to_f32(hi);
+                        } else {
+                            v[8 * i + 2 * k] = __half2float(__ushort_as_half(lo));
+                            v[8 * i + 2 * k + 1] = __half2float(__ushort_as_half(hi));
+                        }
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+        }
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) a = fmaxf(a, fabsf(v[i]));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+        if (active) {
+            uint32_t pk[2];
+            nf4_quant_regs<16>(v, a, tab.bucket, pk);
+            *reinterpret_cast<uint2*>(packed + e0 / 2) = make_uint2(pk[0], pk[1]);
+            if ((qd & 3) == 0) absmax[qd >> 2] = a;
+        }
+    }
+}
+
+// Generic quantisation, pass 1: absmax per block (one warp per block).
+__global__ void nf4_absmax_generic_kernel(const void* __restrict__ x, int x_dtype, int64_t n, int block,
+                                          int64_t n_blocks, float* __restrict__ absmax) {
+    int lane = threadIdx.x & 31;
+    int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t b = warp; b < n_blocks; b += nwarps) {
+        float a = 0.0f;
+        for (int64_t i = lane; i < block; i += 32) {
+            int64_t e = b * block + i;
+            if (e < n) a = fmaxf(a, fabsf(load_as_f32(x, e, x_dtype)));
+        }
+        a = warp_max(a);
+        if (lane == 0) absmax[b] = a;
+    }
+}
+
+// Generic quantisation, pass 2: one thread per packed byte.
+__global__ void nf4_pack_generic_kernel(const void* __restrict__ x, int x_dtype, int64_t n, int block,
+                                        const float* __restrict__ absmax, uint8_t* __restrict__ packed) {
+    int64_t nbytes = (n + 1) / 2;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += (int64_t)gridDim.x * blockDim.x) {
+        int64_t e0 = 2 * k, e1 = 2 * k + 1;
+        uint32_t c0 = nf4_code_exact(load_as_f32(x, e0, x_dtype), fmaxf(absmax[e0 / block], 1e-8f));
+        // quantizer.py:37-39: an odd element count is padded with code 0.
+        uint32_t c1 = e1 < n ? nf4_code_exact(load_as_f32(x, e1, x_dtype), fmaxf(absmax[e1 / block], 1e-8f)) : 0u;
+        packed[k] = (uint8_t)((c0 << 4) | c1);
+    }
+}
+
+}  // namespace aeth

@@ -1,0 +1,419 @@
+"""Host-side mirror of the reference `galore` crate's operator surface.
+
+``GaLoreOptimizer`` implements the methods of ``doublepass::OptimizerBackend``
+(doublepass/src/lib.rs:62-107) as ``galore::GaLoreOptimizer`` does
+(galore/src/optimizer.rs:81-403), with the same names, argument meaning and
+error behaviour (unknown keys and wrong-sized gradients are ignored, as the
+reference does), on top of libaeth_galore's C ABI.  Device memory and streams
+come from torch; all arithmetic runs in the library's CUDA kernels.
+
+``deferred_apply_with_clip`` mirrors doublepass/src/hook.rs:115-259.
+Reference paths are relative to the reference project's aethelStream/.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib as L
+
+
+class ProjectorKind(enum.Enum):
+    """doublepass/src/hook.rs:44-68"""
+    ORTHONORMAL = 0
+    RANDOM = 1
+    NONE = 2
+
+
+@dataclass
+class AdamWConfig:
+    """galore/src/adamw.rs:8-34"""
+    beta1: float = 0.9
+    beta2: float = 0.999
+    eps: float = 1e-8
+    lr: float = 1e-3
+    weight_decay: float = 0.0
+    scale_lr_by_rank: bool = False
+
+
+@dataclass
+class LayerRankConfig:
+    """galore/src/layer_rank.rs:8-40"""
+    default_rank: int = 16
+    attn_rank: int = 32
+    mlp_rank: int = 16
+    vector_rank: int = 8
+
+    def rank_for_param(self, param_name: str, m: int, n: int) -> int:
+        if param_name in ("d_wq", "d_wk", "d_wv", "d_wo"):
+            base = self.attn_rank
+        elif param_name in ("d_wg", "d_wu", "d_wd"):
+            base = self.mlp_rank
+        elif param_name in ("d_rms1_w", "d_rms2_w"):
+            base = self.vector_rank
+        else:
+            base = self.default_rank
+        return max(min(base, max(m, 1), max(n, 1)), 1)
+
+
+@dataclass
+class GaLoreConfig:
+    """galore/src/optimizer.rs:35-61 plus the B200-mode options.
+
+    mode "ref": two-sided projection, fp32, per-tensor INT8 (the reference).
+    mode "b200": one-sided projection on the smaller dimension, bf16 tensor
+    cores, blockwise INT8 state ("linear" or "dynamic"), fused NF4 weight write.
+    """
+    rank: int = 16
+    layer_ranks: LayerRankConfig = field(default_factory=LayerRankConfig)
+    switch_interval: int = 200
+    oversampling: int = 10
+    adam: AdamWConfig = field(default_factory=AdamWConfig)
+    mode: str = "ref"
+    state_codec: str = "per_tensor"
+    state_block: int = 2048
+    max_grad_norm: float = 1.0
+    init_projectors: bool = True
+
+    def to_c(self) -> L.GaloreConfig:
+        c = L.GaloreConfig()
+        L.load().aeth_galore_config_default(C.byref(c))
+        c.mode = {"ref": L.MODE_REF, "b200": L.MODE_B200}[self.mode]
+        c.default_rank = self.layer_ranks.default_rank
+        c.attn_rank = self.layer_ranks.attn_rank
+        c.mlp_rank = self.layer_ranks.mlp_rank
+        c.vector_rank = self.layer_ranks.vector_rank
+        c.switch_interval = self.switch_interval
+        c.oversampling = self.oversampling
+        c.beta1, c.beta2, c.eps, c.lr = self.adam.beta1, self.adam.beta2, self.adam.eps, self.adam.lr
+        c.weight_decay = self.adam.weight_decay
+        c.scale_lr_by_rank = int(self.adam.scale_lr_by_rank)
+        c.max_grad_norm = self.max_grad_norm
+        # REF mode is per-tensor INT8 (quantize.rs); B200 mode is blockwise.
+        codec = "per_tensor" if self.mode == "ref" else ("dynamic" if self.state_codec == "dynamic" else "linear")
+        c.state_codec = {"per_tensor": L.CODEC_PER_TENSOR, "linear": L.CODEC_BLOCK_LINEAR,
+                         "dynamic": L.CODEC_BLOCK_DYNAMIC}[codec]
+        c.state_block = self.state_block
+        c.init_projectors = int(self.init_projectors)
+        return c
+
+
+_DTYPES = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16, torch.bfloat16: L.DTYPE_BF16}
+
+
+def _stream_handle() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+@dataclass
+class NF4Tensor:
+    """NF4 weight: 64-element blocks, fp32 absmax, high nibble = even element
+    (shard_engine/src/nf4.rs:25-83)."""
+    packed: torch.Tensor   # uint8, numel/2
+    absmax: torch.Tensor   # float32, numel/64
+    shape: tuple
+
+    @property
+    def numel(self) -> int:
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+
+def nf4_quantize(x: torch.Tensor, block: int = 64) -> NF4Tensor:
+    """quantize_nf4 (shard_engine/python/pipeline/quantizer.py:21-53) on the GPU, bit-exact."""
+    x = x.contiguous()
+    n = x.numel()
+    packed = torch.empty((n + 1) // 2, dtype=torch.uint8, device=x.device)
+    absmax = torch.empty((n + block - 1) // block, dtype=torch.float32, device=x.device)
+    L.check(L.load().aeth_nf4_quant(_ptr(x), _DTYPES[x.dtype], n, block, _ptr(packed), _ptr(absmax),
+                                    C.c_void_p(_stream_handle())), "aeth_nf4_quant")
+    return NF4Tensor(packed, absmax, tuple(x.shape))
+
+
+def nf4_dequantize(t: NF4Tensor, dtype: torch.dtype = torch.float16, block: int = 64) -> torch.Tensor:
+    """dequant_nf4_into (shard_engine/src/nf4.rs:37-83) / dequantize_nf4 (quantizer.py:55-75)."""
+    out = torch.empty(t.shape, dtype=dtype, device=t.packed.device)
+    L.check(L.load().aeth_nf4_dequant(_ptr(t.packed), _ptr(t.absmax), t.numel, block, _ptr(out), _DTYPES[dtype],
+                                      C.c_void_p(_stream_handle())), "aeth_nf4_dequant")
+    return out
+
+
+class GaLoreOptimizer:
+    """galore::GaLoreOptimizer on the B200 library (one device per instance)."""
+
+    def __init__(self, config: GaLoreConfig, param_specs, device: int | None = None):
+        self.config = config
+        self.device = torch.cuda.current_device() if device is None else device
+        self._lib = L.load()
+        specs = (L.ParamSpec * max(len(param_specs), 1))()
+        self._names = []
+        for i, spec in enumerate(param_specs):
+            li, name, m, n = spec[:4]
+            rank = spec[4] if len(spec) > 4 else 0
+            bname = name.encode()
+            self._names.append(bname)  # keep alive for the call
+            specs[i] = L.ParamSpec(li, bname, m, n, rank)
+        self._cfg = config.to_c()
+        ctx = C.c_void_p()
+        L.check(self._lib.aeth_galore_create(C.byref(self._cfg), specs, len(param_specs), self.device, C.byref(ctx)),
+                "aeth_galore_create")
+        self._ctx = ctx
+        self._pending_deltas: dict = {}
+        self._info: dict = {}
+        for i, spec in enumerate(param_specs):
+            info = L.ParamInfo()
+            L.check(self._lib.aeth_galore_param_info(self._ctx, i, C.byref(info)))
+            self._info[(spec[0], spec[1])] = (i, info)
+
+    def close(self):
+        if getattr(self, "_ctx", None):
+            self._lib.aeth_galore_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+    # ---- helpers ----
+    def _key(self, layer_idx, param_name):
+        return self._info.get((layer_idx, param_name))
+
+    def param_info(self, layer_idx, param_name) -> L.ParamInfo | None:
+        k = self._key(layer_idx, param_name)
+        return None if k is None else k[1]
+
+    def index(self, layer_idx, param_name) -> int:
+        k = self._key(layer_idx, param_name)
+        return -1 if k is None else k[0]
+
+    # ---- OptimizerBackend (doublepass/src/lib.rs:62-107) ----
+    def project_and_accumulate(self, grad: torch.Tensor, layer_idx: int, param_name: str) -> None:
+        """optimizer.rs:264-292; wrong-sized gradients and unknown keys are ignored."""
+        k = self._key(layer_idx, param_name)
+        if k is None:
+            return
+        idx, info = k
+        if grad.numel() != info.m * info.n:
+            return
+        g = grad.contiguous()
+        L.check(self._lib.aeth_galore_project_accumulate(self._ctx, idx, _ptr(g), _DTYPES[g.dtype],
+                                                         C.c_void_p(_stream_handle())), "project_and_accumulate")
+
+    def lowrank_grad_sqnorm(self, layer_idx: int, param_name: str) -> float:
+        """optimizer.rs:294-301 (0.0 for unknown keys)."""
+        k = self._key(layer_idx, param_name)
+        if k is None:
+            return 0.0
+        out = C.c_double()
+        L.check(self._lib.aeth_galore_sqnorm(self._ctx, k[0], C.byref(out), C.c_void_p(_stream_handle())),
+                "lowrank_grad_sqnorm")
+        return out.value
+
+    def apply_update(self, layer_idx: int, param_name: str, clip_scale: float, weight=None,
+                     prequant_out: torch.Tensor | None = None) -> None:
+        """optimizer.rs:303-362.  Without `weight` the delta (lr applied) is
+        kept for take_weight_delta, as the reference does.  With `weight` (an
+        fp32 tensor or an NF4Tensor) the update is applied in place."""
+        k = self._key(layer_idx, param_name)
+        if k is None:
+            return
+        idx, info = k
+        w = L.WeightRef()
+        delta = None
+        if weight is None:
+            delta = torch.empty(info.m, info.n, dtype=torch.float32, device=f"cuda:{self.device}")
+            w.kind, w.delta_out = L.WEIGHT_NONE, delta.data_ptr()
+        elif isinstance(weight, NF4Tensor):
+            w.kind, w.data, w.absmax = L.WEIGHT_NF4, weight.packed.data_ptr(), weight.absmax.data_ptr()
+        else:
+            w.kind, w.data = L.WEIGHT_F32, weight.data_ptr()
+        if prequant_out is not None:
+            w.prequant_out = prequant_out.data_ptr()
+        L.check(self._lib.aeth_galore_apply_update(self._ctx, idx, float(clip_scale), None, C.byref(w),
+                                                   C.c_void_p(_stream_handle())), "apply_update")
+        if delta is not None:
+            self._pending_deltas[(layer_idx, param_name)] = delta
+
+    def zero_accum(self, layer_idx: int, param_name: str) -> None:
+        k = self._key(layer_idx, param_name)
+        if k is not None:
+            L.check(self._lib.aeth_galore_zero_accum(self._ctx, k[0], C.c_void_p(_stream_handle())), "zero_accum")
+
+    def notify_step(self, step: int) -> None:
+        L.check(self._lib.aeth_galore_notify_step(self._ctx, step), "notify_step")
+
+    def projector_kind(self, layer_idx: int, param_name: str) -> ProjectorKind:
+        return ProjectorKind.ORTHONORMAL
+
+    def true_frobenius_sqnorm(self, layer_idx: int, param_name: str):
+        return None
+
+    # ---- GaLoreOptimizer inherent methods ----
+    def take_weight_delta(self, layer_idx: int, param_name: str):
+        """optimizer.rs:195-200"""
+        return self._pending_deltas.pop((layer_idx, param_name), None)
+
+    def step_count(self) -> int:
+        return int(self._lib.aeth_galore_step_count(self._ctx))
+
+    # ---- state access (tests, checkpointing) ----
+    def get_projector(self, layer_idx, param_name):
+        idx, info = self._key(layer_idx, param_name)
+        dev = f"cuda:{self.device}"
+        if info.side == 0:
+            P = torch.empty(info.m, info.rank, device=dev)
+            Q = torch.empty(info.n, info.rank, device=dev)
+        else:
+            s = info.m if info.side == 1 else info.n
+            P = torch.empty(s, info.rank, device=dev) if info.side == 1 else None
+            Q = torch.empty(s, info.rank, device=dev) if info.side == 2 else None
+        L.check(self._lib.aeth_galore_get_projector(self._ctx, idx, _ptr(P), _ptr(Q), C.c_void_p(_stream_handle())))
+        return P, Q
+
+    def set_projector(self, layer_idx, param_name, P=None, Q=None):
+        idx, _ = self._key(layer_idx, param_name)
+        P = None if P is None else P.contiguous().float()
+        Q = None if Q is None else Q.contiguous().float()
+        L.check(self._lib.aeth_galore_set_projector(self._ctx, idx, _ptr(P), _ptr(Q), C.c_void_p(_stream_handle())),
+                "set_projector")
+
+    def get_state(self, layer_idx, param_name):
+        idx, info = self._key(layer_idx, param_name)
+        dev = f"cuda:{self.device}"
+        m8 = torch.empty(info.state_elems, dtype=torch.int8, device=dev)
+        v8 = torch.empty_like(m8)
+        ms = torch.empty(info.state_blocks, dtype=torch.float32, device=dev)
+        vs = torch.empty_like(ms)
+        L.check(self._lib.aeth_galore_get_state(self._ctx, idx, _ptr(m8), _ptr(v8), _ptr(ms), _ptr(vs),
+                                                C.c_void_p(_stream_handle())))
+        return m8, v8, ms, vs
+
+    def set_state(self, layer_idx, param_name, m8, v8, ms, vs):
+        idx, _ = self._key(layer_idx, param_name)
+        L.check(self._lib.aeth_galore_set_state(self._ctx, idx, _ptr(m8), _ptr(v8), _ptr(ms), _ptr(vs),
+                                                C.c_void_p(_stream_handle())))
+
+    def get_accum(self, layer_idx, param_name):
+        idx, info = self._key(layer_idx, param_name)
+        out = torch.empty(info.state_elems, dtype=torch.float32, device=f"cuda:{self.device}")
+        L.check(self._lib.aeth_galore_get_accum(self._ctx, idx, _ptr(out), C.c_void_p(_stream_handle())))
+        return out
+
+    # ---- fused whole-layer step (device-side deferred_apply_with_clip) ----
+    def step_layer(self, keys, grads, weights=None, sq_hook=None):
+        """project_and_accumulate for every (layer, name) in `keys`, the exact
+        global-norm clip on the device, then apply_update + zero_accum
+        (hook.rs:139-203) -- no host synchronisation.  `sq_hook(sq_tensor)`
+        may all-reduce the per-parameter squared norms (multi-GPU).  Returns
+        the device clip coefficient (a 1-element tensor)."""
+        n = len(keys)
+        idx = (C.c_int * n)(*[self._key(*k)[0] for k in keys])
+        gp = (C.c_void_p * n)(*[g.data_ptr() for g in grads])
+        dtype = _DTYPES[grads[0].dtype]
+        wrefs = None
+        if weights is not None:
+            wrefs = (L.WeightRef * n)()
+            for i, w in enumerate(weights):
+                if isinstance(w, NF4Tensor):
+                    wrefs[i].kind, wrefs[i].data, wrefs[i].absmax = L.WEIGHT_NF4, w.packed.data_ptr(), w.absmax.data_ptr()
+                elif w is None:
+                    wrefs[i].kind = L.WEIGHT_NONE
+                else:
+                    wrefs[i].kind, wrefs[i].data = L.WEIGHT_F32, w.data_ptr()
+        clip = torch.empty(1, dtype=torch.float32, device=f"cuda:{self.device}")
+        hook = L.SQ_HOOK(0)
+        if sq_hook is not None:
+            def _cb(sq_ptr, count, stream, user):  # noqa: ARG001 - C callback signature
+                try:
+                    sq_hook(_wrap_device_doubles(sq_ptr, count, self.device))
+                    return 0
+                except Exception:  # noqa: BLE001 - reported as a status to C
+                    return L.AETH_ERR_CONFIG
+            hook = L.SQ_HOOK(_cb)
+        L.check(self._lib.aeth_galore_step(self._ctx, n, idx, gp, dtype, wrefs, hook, None, _ptr(clip),
+                                           C.c_void_p(_stream_handle())), "aeth_galore_step")
+        return clip
+
+
+def _wrap_device_doubles(ptr: int, count: int, device: int) -> torch.Tensor:
+    """A torch view of `count` device doubles owned by the library (no copy)."""
+    class _Holder:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<f8", "data": (ptr, False),
+                                             "version": 2, "strides": None}
+    with torch.cuda.device(device):
+        return torch.as_tensor(_Holder(), device=f"cuda:{device}")
+
+
+@dataclass
+class ClipResult:
+    """doublepass/src/hook.rs:70-94"""
+    global_grad_norm: float
+    clip_coeff: float
+    clipped: bool
+    used_grouped_fallback: bool
+    frobenius_exact_layers: int
+
+
+def _f32(x: float) -> float:
+    import numpy as np
+    return float(np.float32(x))
+
+
+def deferred_apply_with_clip(optimizer, max_grad_norm: float, trainable_layers) -> ClipResult:
+    """doublepass/src/hook.rs:115-136 (global clip, grouped fallback for ProjectorKind.NONE)."""
+    if not trainable_layers:
+        raise ValueError("deferred_apply_with_clip: trainable_layers must not be empty")
+    if any(optimizer.projector_kind(li, pn) == ProjectorKind.NONE for li, pn in trainable_layers):
+        return _grouped_clip_fallback(optimizer, max_grad_norm, trainable_layers)
+    gsq = 0.0
+    exact = 0
+    for li, pn in trainable_layers:
+        kind = optimizer.projector_kind(li, pn)
+        if kind == ProjectorKind.RANDOM:
+            fsq = optimizer.true_frobenius_sqnorm(li, pn)
+            if fsq is not None:
+                exact += 1
+                gsq += fsq
+                continue
+        gsq += optimizer.lowrank_grad_sqnorm(li, pn)
+    gnorm = gsq ** 0.5
+    clip = min(_f32(max_norm_f64(max_grad_norm) / (gnorm + 1e-6)), 1.0)
+    for li, pn in trainable_layers:
+        optimizer.apply_update(li, pn, clip)
+        optimizer.zero_accum(li, pn)
+    return ClipResult(gnorm, clip, clip < 1.0, False, exact)
+
+
+def max_norm_f64(x: float) -> float:
+    """TrainingPlan::max_grad_norm is an f32 widened to f64 (hook.rs:144)."""
+    return _f32(x)
+
+
+def _grouped_clip_fallback(optimizer, max_grad_norm, trainable_layers) -> ClipResult:
+    """doublepass/src/hook.rs:214-259"""
+    layers: dict = {}
+    for li, pn in trainable_layers:
+        layers.setdefault(li, []).append(pn)
+    total = 0.0
+    min_clip = 1.0
+    for li in sorted(layers):
+        sq = sum(optimizer.lowrank_grad_sqnorm(li, pn) for pn in layers[li])
+        clip = min(_f32(max_norm_f64(max_grad_norm) / (sq ** 0.5 + 1e-6)), 1.0)
+        for pn in layers[li]:
+            optimizer.apply_update(li, pn, clip)
+            optimizer.zero_accum(li, pn)
+        total += sq
+        min_clip = min(min_clip, clip)
+    return ClipResult(total ** 0.5, min_clip, min_clip < 1.0, True, 0)

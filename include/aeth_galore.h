@@ -1,0 +1,267 @@
+/*
+ * aeth_galore.h -- C ABI of the B200 (sm_100a) per-layer optimizer step.
+ *
+ * Every entry point takes plain device pointers and sizes and returns an int
+ * status (except doublepass_galore_apply, whose reference signature is void):
+ *     0                  success
+ *    -1  AETH_ERR_ARG    bad dimensions / null pointer (the reference's -1)
+ *    -2  AETH_ERR_SHAPE  shape mismatch (GaLoreError::Shape, galore/src/error.rs:10-29)
+ *    -3  AETH_ERR_CONFIG configuration error (GaLoreError::Config)
+ *    -4  AETH_ERR_UNSUPPORTED  shape/alignment this build does not handle
+ *    -5  AETH_ERR_NOT_FOUND    unknown parameter key
+ *    -6  AETH_ERR_TIMEOUT      a bounded device-side wait gave up (kernel returned early)
+ *    >0  a cudaError_t value
+ * No entry point aborts the process.  All work is enqueued on the caller's
+ * stream; only functions documented as synchronous wait on it.
+ *
+ * Streams are passed as `aeth_stream_t` (void*), ABI-identical to the
+ * reference's cudaStream_t / Rust `*mut c_void` (galore/src/kernels/mod.rs:10-50).
+ * Reference paths below are relative to the reference project's aethelStream/.
+ */
+#ifndef AETH_GALORE_H
+#define AETH_GALORE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* aeth_stream_t;
+
+enum {
+    AETH_OK = 0,
+    AETH_ERR_ARG = -1,
+    AETH_ERR_SHAPE = -2,
+    AETH_ERR_CONFIG = -3,
+    AETH_ERR_UNSUPPORTED = -4,
+    AETH_ERR_NOT_FOUND = -5,
+    AETH_ERR_TIMEOUT = -6,
+};
+
+typedef enum { AETH_DTYPE_F32 = 0, AETH_DTYPE_F16 = 1, AETH_DTYPE_BF16 = 2 } aeth_dtype;
+
+/* ======================================================================
+ * 1. Reference-compatible symbols (same names, signatures and status codes).
+ * ====================================================================== */
+
+/* Replaces galore/kernels/galore_project.cuh:19-29 (galore_project.cu:63-110).
+ * R(r x r) = P^T G Q, all fp16 row-major device buffers; temp is the caller's
+ * r x n fp16 scratch holding P^T G.  tcgen05 tensor cores, fp32 accumulation.
+ * Returns 0, or -1 when m, n or r <= 0. */
+int galore_project_forward(const void* G, const void* P, const void* Q, void* R, void* temp, int m, int n, int r,
+                           aeth_stream_t stream);
+
+/* Replaces galore/kernels/galore_project.cuh:40-50 (galore_project.cu:112-159).
+ * G~(m x n) = P N Q^T; temp is the caller's m x r fp16 scratch holding P N. */
+int galore_project_backward(const void* N, const void* P, const void* Q, void* G_tilde, void* temp, int m, int n,
+                            int r, aeth_stream_t stream);
+
+/* Replaces galore/kernels/quantize_state.cuh:12-18 (quantize_state.cu:61-86).
+ * scale = max|x| / 127 (1.0 when max|x| == 0), q = clamp(round(x / scale), +-127)
+ * with round half away from zero as in the live CPU path (galore/src/quantize.rs:17-26).
+ * scale_out is a device float; no host synchronisation.  Returns -1 when n <= 0. */
+int galore_quantize_absmax_f32_to_i8(const float* src, int8_t* dst, float* scale_out, int n_elements,
+                                     aeth_stream_t stream);
+
+/* Replaces galore/kernels/quantize_state.cuh:20-26 (quantize_state.cu:88-98): dst = q * scale. */
+int galore_dequantize_i8_to_f32(const int8_t* src, float* dst, float scale, int n_elements, aeth_stream_t stream);
+
+/* Replaces the stub doublepass/kernels/galore_apply.cuh:22-34 (galore_apply.cu:16-24).
+ * Full-rank fused Adam on device buffers, legacy default stream:
+ *   g = grad_lr * clip; m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2;
+ *   param -= lr * m_hat / (sqrt(v_hat) + eps)
+ * with m_hat = m / (1 - b1^step), v_hat = v / (1 - b2^step) for step >= 1 and
+ * m_hat = m, v_hat = v for step <= 0 (galore/src/standard_adamw.rs:84-114).
+ * void as in the reference; errors are readable with aeth_last_error(). */
+void doublepass_galore_apply(float* param, const float* grad_lr, float* m, float* v, float clip_scale, float beta1,
+                             float beta2, float eps, float lr, int n_elements, int step);
+
+/* ======================================================================
+ * 2. Optimizer handle: mirrors doublepass::OptimizerBackend
+ *    (doublepass/src/lib.rs:62-107) as implemented by GaLoreOptimizer
+ *    (galore/src/optimizer.rs:81-403), with device pointers and a stream.
+ * ====================================================================== */
+
+typedef enum {
+    /* Reference semantics: two-sided R = P^T G Q (r x r), fp32 throughout,
+     * per-tensor absmax INT8 m/v (galore/src/optimizer.rs:264-362). */
+    AETH_MODE_REF = 0,
+    /* B200 semantics: one-sided projection on the smaller dimension,
+     * bf16 tensor-core GEMMs, blockwise INT8 m/v, fused NF4 weight write. */
+    AETH_MODE_B200 = 1,
+} aeth_mode;
+
+typedef enum {
+    AETH_CODEC_PER_TENSOR = 0,   /* galore/src/quantize.rs:4-34 */
+    AETH_CODEC_BLOCK_LINEAR = 1, /* same formula per block of state_block elements */
+    AETH_CODEC_BLOCK_DYNAMIC = 2 /* 8-bit dynamic map per block (Dettmers et al. 2021) */
+} aeth_state_codec;
+
+/* GaLoreConfig (galore/src/optimizer.rs:35-61) + AdamWConfig (adamw.rs:8-34)
+ * + LayerRankConfig (layer_rank.rs:8-28) + TrainingPlan::max_grad_norm
+ * (doublepass/src/plan.rs:197-243) + the B200-mode options. */
+typedef struct {
+    int mode;                 /* aeth_mode */
+    int default_rank;         /* 16 */
+    int attn_rank;            /* 32 */
+    int mlp_rank;             /* 16 */
+    int vector_rank;          /* 8 */
+    uint64_t switch_interval; /* 200; 0 holds the projection constant */
+    int oversampling;         /* 10 */
+    float beta1, beta2, eps;  /* 0.9, 0.999, 1e-8 */
+    float lr;                 /* 1e-3 */
+    float weight_decay;       /* 0 */
+    int scale_lr_by_rank;     /* 0 */
+    float max_grad_norm;      /* 1.0 */
+    int state_codec;          /* aeth_state_codec; REF mode requires PER_TENSOR */
+    int state_block;          /* 2048 */
+    int init_projectors;      /* 1: init_random_projection at create; 0: zero, set with aeth_galore_set_projector */
+} aeth_galore_config;
+
+typedef struct {
+    uint32_t layer_idx;
+    const char* name; /* d_wq, d_wk, d_wv, d_wo, d_wg, d_wu, d_wd, d_rms1_w, ... */
+    int m, n;         /* weight is m x n row-major (out x in) */
+    int rank;         /* 0: LayerRankConfig::rank_for_param (layer_rank.rs:32-40) */
+} aeth_param_spec;
+
+typedef struct {
+    int m, n, rank;
+    int side;               /* 0 two-sided (REF), 1 left P (m<n), 2 right Q (m>=n) */
+    int64_t state_elems;    /* r*r (REF) or r*max(m,n) (B200) */
+    int64_t state_blocks;   /* number of INT8 scales per moment */
+    uint32_t layer_idx;
+} aeth_param_info;
+
+typedef enum {
+    AETH_WEIGHT_NONE = 0, /* no in-place update: only delta_out (take_weight_delta) */
+    AETH_WEIGHT_F32 = 1,  /* dense fp32 m x n, updated in place: w -= delta */
+    AETH_WEIGHT_NF4 = 2,  /* NF4 (64-element blocks, fp32 absmax), dequant -> update -> requant in place */
+} aeth_weight_kind;
+
+typedef struct {
+    int kind;         /* aeth_weight_kind */
+    void* data;       /* F32: m*n floats; NF4: m*n/2 packed bytes (high nibble = even element) */
+    float* absmax;    /* NF4: m*n/64 floats */
+    float* delta_out; /* optional m*n fp32 delta (lr applied) = GaLoreOptimizer::take_weight_delta */
+    float* prequant_out; /* optional m*n fp32 updated weight before NF4 requantisation (testing) */
+} aeth_weight_ref;
+
+typedef struct aeth_galore_ctx aeth_galore_ctx;
+
+void aeth_galore_config_default(aeth_galore_config* cfg);
+
+/* GaLoreOptimizer::new (optimizer.rs:81-133): registers the parameters,
+ * allocates all per-parameter device state on `device`, initialises P/Q with
+ * init_random_projection (seeds layer*17 and layer*31, optimizer.rs:419-448).
+ * Synchronous. */
+int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* specs, int n_specs, int device,
+                       aeth_galore_ctx** out);
+int aeth_galore_destroy(aeth_galore_ctx* ctx);
+/* Index of (layer_idx, name), or AETH_ERR_NOT_FOUND. */
+int aeth_galore_find(const aeth_galore_ctx* ctx, uint32_t layer_idx, const char* name);
+int aeth_galore_param_info(const aeth_galore_ctx* ctx, int idx, aeth_param_info* out);
+int aeth_galore_num_params(const aeth_galore_ctx* ctx);
+
+/* OptimizerBackend::project_and_accumulate (optimizer.rs:264-292):
+ * accum += projection(grad).  grad is m*n device values of `grad_dtype`
+ * (REF: F32 or BF16/F16 upcast; B200: BF16). */
+int aeth_galore_project_accumulate(aeth_galore_ctx* ctx, int idx, const void* grad, int grad_dtype,
+                                   aeth_stream_t stream);
+/* OptimizerBackend::lowrank_grad_sqnorm (optimizer.rs:294-301): sum of squares
+ * of the accumulator in f64.  The _device form writes it to a device double
+ * without synchronising; the host form synchronises the stream. */
+int aeth_galore_sqnorm_device(aeth_galore_ctx* ctx, int idx, double* out_dev, aeth_stream_t stream);
+int aeth_galore_sqnorm(aeth_galore_ctx* ctx, int idx, double* out_host, aeth_stream_t stream);
+/* Global clip of doublepass/src/hook.rs:139-203 on the device:
+ * *clip_dev = min(1, max_norm / (sqrt(sum_i sq[i]) + 1e-6)) over n device doubles. */
+int aeth_clip_coeff_device(const double* sq_dev, int n, float max_norm, float* clip_dev, double* gnorm_dev,
+                           aeth_stream_t stream);
+/* OptimizerBackend::apply_update (optimizer.rs:303-362) with the clip taken
+ * from the host (clip) or from device memory (clip_dev, if not NULL). */
+int aeth_galore_apply_update(aeth_galore_ctx* ctx, int idx, float clip, const float* clip_dev,
+                             const aeth_weight_ref* w, aeth_stream_t stream);
+/* OptimizerBackend::zero_accum (adamw.rs:107-109). */
+int aeth_galore_zero_accum(aeth_galore_ctx* ctx, int idx, aeth_stream_t stream);
+/* OptimizerBackend::notify_step (optimizer.rs:373-398): records the step.
+ * Subspace refresh is driven by aeth_galore_set_projector in this build. */
+int aeth_galore_notify_step(aeth_galore_ctx* ctx, uint64_t step);
+uint64_t aeth_galore_step_count(const aeth_galore_ctx* ctx);
+
+/* Whole-layer step of deferred_apply_with_clip (hook.rs:115-203) for a
+ * single micro-batch: for each listed parameter project_and_accumulate, then
+ * the exact global-norm clip on the device, then apply_update + zero_accum.
+ * When `sq_hook` is set it is called between the sqnorm and apply phases with
+ * the device array of per-parameter sqnorms (length n) so a multi-GPU caller
+ * can all-reduce it in place on `stream`. */
+typedef int (*aeth_sqnorm_hook)(double* sq_dev, int n, aeth_stream_t stream, void* user);
+int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
+                     const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out,
+                     aeth_stream_t stream);
+
+/* Projector access.  REF: P (m x r) and Q (n x r).  B200: only the projector
+ * of the chosen side (P for m < n, Q for m >= n; the other pointer is ignored).
+ * fp32 device buffers.  set_projector resets the Adam state, as the subspace
+ * switch does (optimizer.rs:236-238). */
+int aeth_galore_set_projector(aeth_galore_ctx* ctx, int idx, const float* P, const float* Q, aeth_stream_t stream);
+int aeth_galore_get_projector(aeth_galore_ctx* ctx, int idx, float* P, float* Q, aeth_stream_t stream);
+/* State access (device buffers): m8, v8 (state_elems), scales (state_blocks). */
+int aeth_galore_get_state(aeth_galore_ctx* ctx, int idx, int8_t* m8, int8_t* v8, float* m_scales, float* v_scales,
+                          aeth_stream_t stream);
+int aeth_galore_set_state(aeth_galore_ctx* ctx, int idx, const int8_t* m8, const int8_t* v8, const float* m_scales,
+                          const float* v_scales, aeth_stream_t stream);
+int aeth_galore_get_accum(aeth_galore_ctx* ctx, int idx, float* accum, aeth_stream_t stream);
+
+/* ======================================================================
+ * 3. Stand-alone kernels of the path.
+ * ====================================================================== */
+
+/* NF4 dequantise (shard_engine/src/nf4.rs:37-83, quantizer.py:55-75): out[i] =
+ * CODES[nib(i)] * absmax[i / block]; out_dtype F32 (the exact product), F16
+ * (RNE, as nf4.rs:78) or BF16 (RNE). */
+int aeth_nf4_dequant(const uint8_t* packed, const float* absmax, int64_t n, int block, void* out, int out_dtype,
+                     aeth_stream_t stream);
+/* NF4 quantise (quantizer.py:21-53), bit-exact: absmax per block (raw),
+ * argmin over the 16 codes of x / max(absmax, 1e-8), first index on ties.
+ * x is F32, F16 or BF16.  Trailing elements of the last block are treated as 0. */
+int aeth_nf4_quant(const void* x, int x_dtype, int64_t n, int block, uint8_t* packed, float* absmax,
+                   aeth_stream_t stream);
+
+/* INT8 state codecs.  PER_TENSOR: scales[0]; BLOCK_*: one scale per block.
+ * is_signed selects the signed or unsigned dynamic map. */
+int aeth_int8_quantize(const float* x, int64_t n, int codec, int block, int is_signed, int8_t* q, float* scales,
+                       aeth_stream_t stream);
+int aeth_int8_dequantize(const int8_t* q, const float* scales, int64_t n, int codec, int block, int is_signed,
+                         float* out, aeth_stream_t stream);
+/* The 256-entry dynamic map used by AETH_CODEC_BLOCK_DYNAMIC (host copy). */
+int aeth_dynamic_map(int is_signed, float out[256]);
+
+/* LOMO fused full-rank update over a flat NF4 tensor (Lv et al. 2023):
+ * aeth_lomo_sqnorm adds sum(g^2) (f64) into *sq_dev; aeth_lomo_update reads
+ * the global sum from sq_dev (after any cross-tensor / cross-rank reduction),
+ * clips with min(1, max_norm / (sqrt(sq) + 1e-6)), updates the blockwise INT8
+ * momentum m = beta m + g*clip, writes w = w - lr m and requantises w to NF4.
+ * grad is bf16; n must be a multiple of 64 and of `block` / 64. */
+int aeth_lomo_sqnorm(const void* grad_bf16, int64_t n, double* sq_dev, aeth_stream_t stream);
+int aeth_lomo_update(const void* grad_bf16, int64_t n, const double* sq_dev, float max_norm, float lr, float beta,
+                     int codec, int block, int8_t* mom8, float* mom_scales, uint8_t* w_packed, float* w_absmax,
+                     float* prequant_out, aeth_stream_t stream);
+
+/* ======================================================================
+ * 4. Errors and build information.
+ * ====================================================================== */
+const char* aeth_status_string(int status);
+/* Last error recorded on the calling thread (for void entry points). */
+int aeth_last_error(void);
+/* Reads and clears the device-side error word set by bounded waits on
+ * `device` (synchronises the device).  Returns AETH_OK or AETH_ERR_TIMEOUT. */
+int aeth_device_error(int device);
+/* Library version string. */
+const char* aeth_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AETH_GALORE_H */
