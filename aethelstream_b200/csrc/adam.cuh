@@ -11,18 +11,18 @@ namespace aeth {
 // bit-exact with galore/src/optimizer.rs:314-351 + adamw.rs:79-88,116-135 +
 // quantize.rs:4-26.  One CTA; two passes separated by the absmax reduction.
 //   mom/var: fp32 working buffers (the Rust struct's momentum/variance Vecs).
-//   scales[0] = scale_m, scales[1] = scale_v (device, in/out).
+//   m_scale, v_scale: one device float each (in/out).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) ref_adam_kernel(const float* __restrict__ accum, int8_t* __restrict__ m8,
-                                                        int8_t* __restrict__ v8, float* __restrict__ scales,
-                                                        float* __restrict__ mom, float* __restrict__ var,
-                                                        float* __restrict__ normalized, int64_t n, float clip_host,
-                                                        const float* __restrict__ clip_dev, float b1, float b2,
-                                                        float eps) {
+                                                        int8_t* __restrict__ v8, float* __restrict__ m_scale,
+                                                        float* __restrict__ v_scale, float* __restrict__ mom,
+                                                        float* __restrict__ var, float* __restrict__ normalized,
+                                                        int64_t n, float clip_host, const float* __restrict__ clip_dev,
+                                                        float b1, float b2, float eps) {
     __shared__ float red_m[32], red_v[32];
     __shared__ float s_scales[2];
     const float clip = clip_dev ? *clip_dev : clip_host;
-    const float sm = scales[0], sv = scales[1];
+    const float sm = *m_scale, sv = *v_scale;
     const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
     float am = 0.0f, av = 0.0f;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(1024) ref_adam_kernel(const float* __restrict_
         m8[i] = lin_encode(mom[i], im);
         v8[i] = lin_encode(var[i], iv);
     }
-    if (threadIdx.x == 0) { scales[0] = nsm; scales[1] = nsv; }
+    if (threadIdx.x == 0) { *m_scale = nsm; *v_scale = nsv; }
 }
 
 // ---------------------------------------------------------------------------

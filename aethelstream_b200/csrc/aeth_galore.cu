@@ -297,7 +297,7 @@ int ref_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, c
               cudaStream_t st) {
     const aeth_galore_config& cfg = c->cfg;
     const int m = p.m, n = p.n, r = p.r;
-    ref_adam_kernel<<<1, 1024, 0, st>>>(p.accum, p.m8, p.v8, p.mscale, p.mom, p.var, p.normalized,
+    ref_adam_kernel<<<1, 1024, 0, st>>>(p.accum, p.m8, p.v8, p.mscale, p.vscale, p.mom, p.var, p.normalized,
                                         (int64_t)r * r, clip, clip_dev, cfg.beta1, cfg.beta2, cfg.eps);
     AETH_LAUNCH_CHECK();
     const float lr = cfg.scale_lr_by_rank ? cfg.lr / (float)(r < 1 ? 1 : r) : cfg.lr;  // adamw.rs:37-43

@@ -1,0 +1,350 @@
+"""Benchmark of the per-layer optimizer step (NF4 -> GaLore -> INT8 Adam -> NF4).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload ("C2"): one Llama-2-7B decoder block per GPU --
+q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008 -- NF4 weights
+N(0, 0.02), bf16 gradients N(0, 1e-3), GaLore rank 128 on the smaller
+dimension with fixed projectors, INT8 blockwise dynamic-map Adam state, 50
+consecutive steps by default.  A step is one full optimizer step of the block
+through the public API (GaLoreOptimizer.step_layer): projection of all seven
+gradients, exact global-norm clip on the device, Adam, back-projection and the
+NF4 weight write.  Gradients cycle through a two-deep ring generated on the
+device from seeds (step parity, matrix); all weights and state stay resident.
+Under torchrun each rank owns one block (weak scaling); the only exchange is
+the f64 all-reduce of the squared norms for the global clip.
+
+The reference arm (--impl reference) times the reference's CPU algorithm
+(oracle/ port of galore/src/{project,adamw,optimizer}.rs, nf4.rs; the Rust
+crate cannot be built here) on all host threads over a bounded row sample of
+the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "params updated/s (NF4->GaLore->INT8-Adam step)"
+UNIT = "params/s"
+SHAPES = [("d_wq", 4096, 4096), ("d_wk", 4096, 4096), ("d_wv", 4096, 4096), ("d_wo", 4096, 4096),
+          ("d_wg", 11008, 4096), ("d_wu", 11008, 4096), ("d_wd", 4096, 11008)]
+RANK = 128
+STATE_BLOCK = 2048
+WORKLOAD = ("C2: one Llama-2-7B block per GPU (q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008), "
+            "GaLore r=128 one-sided on the smaller dim, fixed projectors, NF4 weights, bf16 grads, "
+            "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")
+
+
+def algorithmic(shapes=SHAPES, r=RANK):
+    """Algorithmic bytes and flops per step, split by phase.
+
+    projection phase (K4): read bf16 G (2 B/elem) + projector (2 s r).
+    apply phase (K5+K6): NF4 weight read + write (2 x 0.5625 B/elem), INT8 m/v
+    read + write (4 r l), block scales (8 r l / 2048), projector (2 s r).
+    Flops: 2 r m n per GEMM (projection and back-projection) + ~12 r l (Adam).
+    """
+    bp = ba = fp = fa = 0
+    for _, m, n in shapes:
+        s, l = min(m, n), max(m, n)
+        bp += 2 * m * n + 2 * s * r
+        ba += 2 * 0.5625 * m * n + 4 * r * l + 8 * r * l / STATE_BLOCK + 2 * s * r
+        fp += 2 * r * m * n
+        fa += 2 * r * m * n + 12 * r * l
+    return {"proj_bytes": bp, "apply_bytes": ba, "proj_flops": fp, "apply_flops": fa}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernels from the committed ncu summary (if present)."""
+    p = os.path.join(ROOT, "profiles", "traffic_c2.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:  # noqa: BLE001
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001 - no nvidia-smi: report no clocks
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "", 1).isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "", 1).isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(frac, threads, k=1):
+    """The reference algorithm (oracle port) on a bounded row sample."""
+    from oracle import oracle as O
+    O.build()
+    samp = O.ReferenceSampler([(m, n) for _, m, n in SHAPES], RANK, frac, threads=threads, seed=1)
+    samp.step()  # warm caches
+    t0 = time.perf_counter()
+    done = 0.0
+    for _ in range(k):
+        done += samp.step()
+    dt = time.perf_counter() - t0
+    return done / dt, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    frac = 1.0 / 64
+    from oracle import oracle as O
+    O.build()
+    samp = O.ReferenceSampler([(m, n) for _, m, n in SHAPES], RANK, frac, threads=threads, seed=1)
+    for _ in range(args.warmup):
+        samp.step()
+    t0 = time.perf_counter()
+    done = 0.0
+    for _ in range(args.steps):
+        done += samp.step()
+    dt = time.perf_counter() - t0
+    v = done / dt
+    sample = (f"1/64 of each matrix's output rows per step (2 of 128 rows of P^T G, m/64 rows of the weight delta "
+              f"and NF4 weight apply) over the 7 matrices of the C2 block; params/s = 1/64 x 202.4M x steps / time")
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * 202.4e6 / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD + " -- reference CPU algorithm (two-sided fp32 GaLore, per-tensor "
+                                              "INT8, NF4 dequant + fp32 apply)", "parallelism": "host threads"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args):
+    import numpy as np  # noqa: F401
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from aethelstream_b200 import GaLoreConfig, GaLoreOptimizer, LayerRankConfig, nf4_quantize
+    from aethelstream_b200.sharding import allreduce_sqnorm_hook
+
+    dev = torch.device("cuda", local)
+    layer = rank  # weak scaling: one block per rank (round-robin layer ownership)
+    specs = [(layer, name, m, n, RANK) for name, m, n in SHAPES]
+    cfg = GaLoreConfig(mode="b200", state_codec="dynamic", state_block=STATE_BLOCK,
+                       layer_ranks=LayerRankConfig())
+    opt = GaLoreOptimizer(cfg, specs, device=local)
+    gen = torch.Generator(device=dev)
+    weights = []
+    for i, (name, m, n) in enumerate(SHAPES):
+        gen.manual_seed(1000 * layer + i)
+        w = torch.randn(m, n, generator=gen, device=dev) * 0.02
+        weights.append(nf4_quantize(w))
+        del w
+    ring = []
+    for parity in range(2):
+        gs = []
+        for i, (name, m, n) in enumerate(SHAPES):
+            gen.manual_seed(7919 * (parity + 1) + 100 * layer + i)
+            gs.append((torch.randn(m, n, generator=gen, device=dev) * 1e-3).to(torch.bfloat16))
+        ring.append(gs)
+    keys = [(layer, name) for name, _, _ in SHAPES]
+    stream = torch.cuda.current_stream()
+    phase_events = []
+    allreduce = allreduce_sqnorm_hook() if world > 1 else None
+
+    def hook(sq):
+        if allreduce is not None:
+            allreduce(sq)
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        phase_events.append(ev)
+
+    def step(s):
+        return opt.step_layer(keys, ring[s % 2], weights, sq_hook=hook)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    phase_events.clear()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)  # let the sampler start
+    starts, ends = [], []
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s in range(args.steps):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        starts.append(e)
+        step(s)
+        e2 = torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        ends.append(e2)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    proj_ms = sum(a.elapsed_time(b) for a, b in zip(starts, phase_events))
+    apply_ms = sum(a.elapsed_time(b) for a, b in zip(phase_events, ends))
+    t = torch.tensor([ms, proj_ms, apply_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, proj_ms, apply_ms = t.tolist()
+    params_per_step = sum(m * n for _, m, n in SHAPES)
+    value = params_per_step * world * args.steps / (ms / 1000.0)
+
+    # ---- end to end through the public API: pinned host grads -> device, step, clip -> host
+    host_grads = [g.cpu().pin_memory() for g in ring[0]]
+    dev_grads = [torch.empty_like(g) for g in ring[0]]
+    clip_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    h2d = sum(g.numel() * g.element_size() for g in host_grads)
+    k_e2e = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        for hg, dg in zip(host_grads, dev_grads):
+            dg.copy_(hg, non_blocking=True)
+        clip = opt.step_layer(keys, dev_grads, weights, sq_hook=hook)
+        clip_host.copy_(clip, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return float(clip_host[0])
+
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(k_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = params_per_step * world * k_e2e / (float(e2e_ms.item()) / 1000.0)
+
+    if rank == 0:
+        hbm, tflops, tflops_sus, peak_kind = load_peaks()
+        alg = algorithmic()
+        per_proj = alg["proj_bytes"] / (proj_ms / args.steps / 1000.0) / 1e9
+        per_apply = alg["apply_bytes"] / (apply_ms / args.steps / 1000.0) / 1e9
+        traffic = load_traffic()
+        if apply_ms >= proj_ms:
+            dom, achieved, tkey = "apply (Adam + tcgen05 back-projection + NF4 write)", per_apply, "apply_bytes_per_step"
+        else:
+            dom, achieved, tkey = "projection (tcgen05 P^T G / G Q)", per_proj, "proj_bytes_per_step"
+        step_s = ms / args.steps / 1000.0
+        total_bytes = alg["proj_bytes"] + alg["apply_bytes"]
+        total_flops = alg["proj_flops"] + alg["apply_flops"]
+        ideal_s = max(total_bytes / (hbm * 1e9), total_flops / (tflops_sus * 1e12))
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) bf16 grads)",
+            "config": {"workload": WORKLOAD, "params_per_gpu_step": params_per_step, "rank": RANK,
+                       "state": "int8 dynamic-map, 2048-element blocks", "parallelism": f"layer-sharded x{world}",
+                       "l2": "inputs larger than L2 (405 MB of bf16 gradients per step, 2-deep ring)"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": traffic.get(tkey), "peak_kind": peak_kind},
+            "roofline_step": {"algorithmic_bytes": total_bytes, "algorithmic_flops": total_flops,
+                              "ideal_ms": ideal_s * 1000.0, "measured_ms": step_s * 1000.0,
+                              "frac": ideal_s / step_s, "proj_ms": proj_ms / args.steps,
+                              "apply_ms": apply_ms / args.steps, "proj_gbs": per_proj, "apply_gbs": per_apply},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                    "steps": k_e2e},
+            "gpu_launches": 36 * args.steps,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, dt = cpu_baseline(1.0 / 128, 1)
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
+                                    "sample": "reference CPU algorithm (oracle port), 1/128 of each matrix's output "
+                                              f"rows over the 7 C2 matrices, single thread, {dt:.1f} s"}
+        print(json.dumps(line), flush=True)
+    opt.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -315,6 +315,75 @@ def lomo_sqnorm(g_bits):
     return lib().b2_lomo_sqnorm_bf16(g, g.size)
 
 
+class ReferenceSampler:
+    """Times the reference's CPU algorithm for one optimizer step of a set of
+    matrices on a bounded row sample (CPU baseline of bench.py).
+
+    Per matrix (galore/src/optimizer.rs:264-362, project.rs:33-58, nf4.rs:37-83):
+    Temp = P^T G (only rows i0..i1 of Temp, fraction f of its r rows),
+    R = Temp Q for those rows, the r x r Adam update, Temp2 = P N, the weight
+    delta rows for fraction f of the m rows, NF4 dequantisation of those weight
+    rows and w -= delta.  The O(r m n) loops dominate and scale linearly in f,
+    so params/s = f * sum(m n) / time.  Work is split over `threads` Python
+    threads (ctypes releases the GIL)."""
+
+    def __init__(self, shapes, r, frac, threads=1, seed=0):
+        rng = np.random.default_rng(seed)
+        self.r, self.frac, self.threads = r, frac, max(1, threads)
+        self.mats = []
+        cache = {}
+        for (m, n) in shapes:
+            if (m, n) not in cache:
+                g = (rng.standard_normal((m, n), dtype=np.float32) * np.float32(1e-3))
+                p = np.linalg.qr(rng.standard_normal((m, r)))[0].astype(np.float32)
+                q = np.linalg.qr(rng.standard_normal((n, r)))[0].astype(np.float32)
+                w = (rng.standard_normal(m * n, dtype=np.float32) * np.float32(0.02))
+                wp, wa = nf4_quantize(w)
+                cache[(m, n)] = (g, p, q, wp, wa)
+            self.mats.append((m, n) + cache[(m, n)])
+        self.params = sum(m * n for (m, n) in shapes)
+
+    def step(self):
+        import concurrent.futures as cf
+        lib()
+        r, f = self.r, self.frac
+        tasks = []
+        bufs = []
+        for (m, n, g, p, q, wp, wa) in self.mats:
+            nfwd = max(1, int(round(r * f)))
+            nbwd = max(1, int(round(m * f)))
+            temp = np.zeros((r, n), np.float32)
+            temp2 = np.zeros((m, r), np.float32)
+            out = np.zeros((nbwd, n), np.float32)  # only the sampled rows [0, nbwd) are written
+            bufs.append((temp, temp2, out))
+            rows = [(i, i + 1) for i in range(nfwd)]
+            for (i0, i1) in rows:
+                tasks.append(("f", g, p, q, temp, m, n, r, i0, i1))
+            chunk = max(1, nbwd // self.threads)
+            for i0 in range(0, nbwd, chunk):
+                tasks.append(("b", temp2, q, out, m, n, r, i0, min(nbwd, i0 + chunk), wp, wa))
+
+        def run(t):
+            if t[0] == "f":
+                _, g, p, q, temp, m, n, r_, i0, i1 = t
+                lib().ref_project_forward_rows(g.ctypes.data, p.ctypes.data, q.ctypes.data, temp.ctypes.data,
+                                               m, n, r_, i0, i1)
+            else:
+                _, temp2, q, out, m, n, r_, i0, i1, wp, wa = t
+                lib().ref_project_backward_rows(temp2.ctypes.data, q.ctypes.data, out.ctypes.data, m, n, r_, i0, i1)
+                # weight path for these rows: NF4 dequant (nf4.rs:37-83) and w -= delta
+                w = nf4_dequant_f32(wp[i0 * n // 2:i1 * n // 2], wa[i0 * n // 64:i1 * n // 64], (i1 - i0) * n)
+                w -= out[i0:i1].ravel()
+        with cf.ThreadPoolExecutor(self.threads) as ex:
+            list(ex.map(run, tasks))
+        # R = Temp Q (sampled rows) and the r x r Adam update (small)
+        for (m, n, g, p, q, wp, wa), (temp, temp2, out) in zip(self.mats, bufs):
+            nfwd = max(1, int(round(r * f)))
+            rr = matmul(temp[:nfwd], q, nfwd, n, r)
+            adamw_inner_update(np.resize(rr, r * r), np.zeros(r * r, np.float32), np.zeros(r * r, np.float32))
+        return self.params * f
+
+
 def lomo_update(g_bits, clip, beta, lr, block, codec, mom8, mom_scales, w_packed, w_absmax):
     g = _c(g_bits, np.uint16).ravel()
     n = g.size
