@@ -141,13 +141,152 @@ __global__ void __launch_bounds__(256) b2_adam_kernel(AdamB2Args a) {
                 a.m8[i] = lin_encode(mo, im);
                 a.v8[i] = lin_encode(va, iv);
             } else {
-                a.m8[i] = (int8_t)(uint8_t)dmap_encode(dm, dyn_xn(mo, nsm));
-                a.v8[i] = (int8_t)(uint8_t)dmap_encode(du, dyn_xn(va, nsv));
+                a.m8[i] = (int8_t)(uint8_t)dmap_encode(dm, dyn_xn(mo, dyn_inv(nsm)));
+                a.v8[i] = (int8_t)(uint8_t)dmap_encode(du, dyn_xn(va, dyn_inv(nsv)));
             }
             if (a.zero_accum) const_cast<float*>(a.accum)[i] = 0.0f;
         }
         __syncthreads();
         if (threadIdx.x == 0) { a.m_scales[b] = nsm; a.v_scales[b] = nsv; }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// B200 mode, grouped: the Adam step of every parameter of a layer in one
+// persistent launch.  State blocks of 2048 elements, one per 256-thread CTA
+// iteration; thread t owns elements [8t, 8t+8) of the block, so the update,
+// the block absmax and the encode run from registers in a single HBM pass:
+// read R (4 B) + m, v codes (2 B), write m, v codes (2 B) + N bf16 (2 B)
+// [+ zero R (4 B)] per element.  The dynamic-map encode is a binary search
+// over a lane-replicated copy of the map (entry i for lane L at word
+// 32 i + L, i.e. always bank L), so it never has bank conflicts.
+// ---------------------------------------------------------------------------
+constexpr int kAdamGroupMax = 16;
+
+struct AdamGroupArgs {
+    const float* accum[kAdamGroupMax];
+    int8_t* m8[kAdamGroupMax];
+    int8_t* v8[kAdamGroupMax];
+    float* ms[kAdamGroupMax];
+    float* vs[kAdamGroupMax];
+    uint16_t* nout[kAdamGroupMax];
+    int64_t count[kAdamGroupMax];
+    int block_begin[kAdamGroupMax + 1];
+    int np;
+    int codec;
+    float clip_host;
+    const float* clip_dev;
+    float b1, b2, eps;
+    int zero_accum;
+};
+
+__device__ __forceinline__ uint32_t dmap_encode_rep(const float* __restrict__ rep, int lane, float xn) {
+    int lo = 0;
+#pragma unroll
+    for (int step = 128; step > 0; step >>= 1)
+        if (rep[(lo + step - 1) * 32 + lane] < xn) lo += step;
+    if (lo == 0) return 0u;
+    if (lo == 256) return 255u;
+    const float dl = fabsf(__fsub_rn(xn, rep[(lo - 1) * 32 + lane]));
+    const float dh = fabsf(__fsub_rn(xn, rep[lo * 32 + lane]));
+    return dh < dl ? (uint32_t)lo : (uint32_t)(lo - 1);
+}
+
+__global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
+    extern __shared__ float dyn_smem[];  // DYNAMIC codec: 2 x 256 x 32 floats (signed, unsigned map)
+    __shared__ float red_m[8], red_v[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float* rep_s = dyn_smem;
+    float* rep_u = dyn_smem + 256 * 32;
+    if (a.codec == AETH_CODEC_BLOCK_DYNAMIC) {
+        for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+            rep_s[i] = c_dmap_signed[i >> 5];
+            rep_u[i] = c_dmap_unsigned[i >> 5];
+        }
+    }
+    __syncthreads();
+    const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
+    const float omb1 = __fsub_rn(1.0f, a.b1), omb2 = __fsub_rn(1.0f, a.b2);
+    const int total = a.block_begin[a.np];
+    for (int gb = blockIdx.x; gb < total; gb += gridDim.x) {
+        int p = 0;
+#pragma unroll 1
+        while (p + 1 < a.np && gb >= a.block_begin[p + 1]) ++p;
+        const int b = gb - a.block_begin[p];
+        const int64_t e0 = (int64_t)b * 2048 + threadIdx.x * 8;
+        const bool valid = e0 < a.count[p];  // counts are multiples of 8
+        const float sm = a.ms[p][b], sv = a.vs[p][b];
+        float mo[8], va[8];
+        float am = 0.0f, av = 0.0f;
+        if (valid) {
+            const float4 g0 = *reinterpret_cast<const float4*>(a.accum[p] + e0);
+            const float4 g1 = *reinterpret_cast<const float4*>(a.accum[p] + e0 + 4);
+            const uint2 qm = *reinterpret_cast<const uint2*>(a.m8[p] + e0);
+            const uint2 qv = *reinterpret_cast<const uint2*>(a.v8[p] + e0);
+            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            uint32_t nb[4];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t cm = ((k < 4 ? qm.x : qm.y) >> (8 * (k & 3))) & 0xffu;
+                const uint32_t cv = ((k < 4 ? qv.x : qv.y) >> (8 * (k & 3))) & 0xffu;
+                float m0, v0;
+                if (a.codec == AETH_CODEC_BLOCK_LINEAR) {
+                    m0 = __fmul_rn((float)(int8_t)cm, sm);
+                    v0 = __fmul_rn((float)(int8_t)cv, sv);
+                } else {
+                    m0 = __fmul_rn(rep_s[cm * 32 + lane], sm);
+                    v0 = __fmul_rn(rep_u[cv * 32 + lane], sv);
+                }
+                const float gg = clip != 1.0f ? __fmul_rn(g[k], clip) : g[k];
+                mo[k] = __fadd_rn(__fmul_rn(a.b1, m0), __fmul_rn(omb1, gg));
+                va[k] = __fadd_rn(__fmul_rn(a.b2, v0), __fmul_rn(__fmul_rn(omb2, gg), gg));
+                const float nv = __fdiv_rn(mo[k], __fadd_rn(__fsqrt_rn(va[k]), a.eps));
+                const uint32_t bits = f32_to_bf16_bits(nv);
+                if (k & 1) nb[k >> 1] |= bits << 16; else nb[k >> 1] = bits;
+                am = fmaxf(am, fabsf(mo[k]));
+                av = fmaxf(av, fabsf(va[k]));
+            }
+            *reinterpret_cast<uint4*>(a.nout[p] + e0) = make_uint4(nb[0], nb[1], nb[2], nb[3]);
+        }
+        am = warp_max(am);
+        av = warp_max(av);
+        if (lane == 0) { red_m[warp] = am; red_v[warp] = av; }
+        __syncthreads();
+        float bm = 0.0f, bv = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) { bm = fmaxf(bm, red_m[w]); bv = fmaxf(bv, red_v[w]); }
+        __syncthreads();  // red_* are rewritten by the next block
+        float nsm, nsv;
+        if (valid) {
+            uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
+            if (a.codec == AETH_CODEC_BLOCK_LINEAR) {
+                nsm = lin_scale_from_absmax(bm);
+                nsv = lin_scale_from_absmax(bv);
+                const float im = lin_inv(nsm), iv = lin_inv(nsv);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    om[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(mo[k], im)) << (8 * (k & 3));
+                    ov[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(va[k], iv)) << (8 * (k & 3));
+                }
+            } else {
+                nsm = bm;
+                nsv = bv;
+                const float im = dyn_inv(bm), iv = dyn_inv(bv);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    om[k >> 2] |= dmap_encode_rep(rep_s, lane, dyn_xn(mo[k], im)) << (8 * (k & 3));
+                    ov[k >> 2] |= dmap_encode_rep(rep_u, lane, dyn_xn(va[k], iv)) << (8 * (k & 3));
+                }
+            }
+            *reinterpret_cast<uint2*>(a.m8[p] + e0) = make_uint2(om[0], om[1]);
+            *reinterpret_cast<uint2*>(a.v8[p] + e0) = make_uint2(ov[0], ov[1]);
+            if (a.zero_accum) {
+                float* z = const_cast<float*>(a.accum[p]) + e0;
+                *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4*>(z + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (threadIdx.x == 0) { a.ms[p][b] = nsm; a.vs[p][b] = nsv; }
+        }
     }
 }
 

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "layer_launch.cuh"
 #include "lomo.cuh"
 #include "nf4.cuh"
 
@@ -323,16 +324,22 @@ int ref_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, c
 }
 
 // ---- B200 mode ------------------------------------------------------------
-int b2_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t st) {
+// bf16 view of a gradient: f32 / f16 gradients are rounded to bf16 (RNE) into
+// the parameter's buffer, allocated on the first such call.
+int b2_grad_bf16(Param& p, const void* grad, int dtype, cudaStream_t st, const void** out) {
+    *out = grad;
+    if (dtype == AETH_DTYPE_BF16) return AETH_OK;
+    const int64_t mn = (int64_t)p.m * p.n;
+    if (!p.gbf) AETH_CUDA(cudaMalloc(&p.gbf, (size_t)mn * sizeof(uint16_t)));
+    to_bf16_kernel<<<grid_for(mn, 256), 256, 0, st>>>(grad, dtype, mn, p.gbf);
+    AETH_LAUNCH_CHECK();
+    *out = p.gbf;
+    return AETH_OK;
+}
+
+// One-CTA-per-tile tcgen05 projection, for shapes the grouped kernel does not take.
+int b2_project_tile(Param& p, const void* grad, cudaStream_t st) {
     const int m = p.m, n = p.n, r = p.r;
-    if (dtype != AETH_DTYPE_BF16) {
-        // f32 / f16 gradients are rounded to bf16 (RNE) first; the buffer is
-        // allocated on the first such call.
-        if (!p.gbf) AETH_CUDA(cudaMalloc(&p.gbf, (size_t)m * n * sizeof(uint16_t)));
-        to_bf16_kernel<<<grid_for((int64_t)m * n, 256), 256, 0, st>>>(grad, dtype, (int64_t)m * n, p.gbf);
-        AETH_LAUNCH_CHECK();
-        grad = p.gbf;
-    }
     EpiAccum epi{p.accum, r};
     if (p.side == 2) {
         // R(m x r) += G Q : A = G (K-major, ld n), B(k,j) = Q[k][j] = projT[j*n + k] (K-major, ld n)
@@ -342,8 +349,19 @@ int b2_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t st
     return tc_gemm<true, false>(TcOperand{grad, n}, TcOperand{p.projT, m}, n, r, m, true, epi, st);
 }
 
-int b2_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, const aeth_weight_ref* w,
-             int zero_accum, cudaStream_t st) {
+int b2_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t st) {
+    AETH_TRY(b2_grad_bf16(p, grad, dtype, st, &grad));
+    ProjJob j{grad, p.projT, p.accum, p.m, p.n};
+    int s = proj_grouped_launch(&j, 1, p.r, st);
+    return s == AETH_ERR_UNSUPPORTED ? b2_project_tile(p, grad, st) : s;
+}
+
+float b2_lr(const aeth_galore_config& cfg, int r) {
+    return cfg.scale_lr_by_rank ? cfg.lr / (float)(r < 1 ? 1 : r) : cfg.lr;  // adamw.rs:37-43
+}
+
+// K5: Adam on the state, N (bf16) out, optionally zeroing the accumulator.
+int b2_adam(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, int zero_accum, cudaStream_t st) {
     const aeth_galore_config& cfg = c->cfg;
     AETH_TRY(codec_maps_ensure());
     AdamB2Args a;
@@ -364,8 +382,102 @@ int b2_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, co
     a.zero_accum = zero_accum;
     b2_adam_kernel<<<grid_for(p.state_blocks, 1, 148 * 8), 256, 0, st>>>(a);
     AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+// K5 for several parameters in one persistent launch (2048-element blocks).
+int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, const float* clip_dev, int zero_accum,
+                  cudaStream_t st) {
+    const aeth_galore_config& cfg = c->cfg;
+    if (cfg.state_block != 2048) {
+        for (int i = 0; i < np; ++i) AETH_TRY(b2_adam(c, *ps[i], clip, clip_dev, zero_accum, st));
+        return AETH_OK;
+    }
+    AETH_TRY(codec_maps_ensure());
+    const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
+    const int smem = dyn ? 2 * 256 * 32 * (int)sizeof(float) : 0;
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    if (!attr_set[dev]) {
+        AETH_CUDA(cudaFuncSetAttribute(b2_adam_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       2 * 256 * 32 * (int)sizeof(float)));
+        attr_set[dev] = true;
+    }
+    for (int off = 0; off < np; off += kAdamGroupMax) {
+        const int cnt = std::min(kAdamGroupMax, np - off);
+        AdamGroupArgs a;
+        memset(&a, 0, sizeof(a));
+        int blocks = 0;
+        for (int i = 0; i < cnt; ++i) {
+            Param& p = *ps[off + i];
+            if (p.state_elems % 8 != 0) return AETH_ERR_UNSUPPORTED;
+            a.accum[i] = p.accum;
+            a.m8[i] = p.m8;
+            a.v8[i] = p.v8;
+            a.ms[i] = p.mscale;
+            a.vs[i] = p.vscale;
+            a.nout[i] = p.nbuf;
+            a.count[i] = p.state_elems;
+            a.block_begin[i] = blocks;
+            blocks += (int)p.state_blocks;
+        }
+        a.block_begin[cnt] = blocks;
+        a.np = cnt;
+        a.codec = cfg.state_codec;
+        a.clip_host = clip;
+        a.clip_dev = clip_dev;
+        a.b1 = cfg.beta1;
+        a.b2 = cfg.beta2;
+        a.eps = cfg.eps;
+        a.zero_accum = zero_accum;
+        const int grid = std::min(blocks, num_sms() * (dyn ? 3 : 8));
+        b2_adam_group_kernel<<<grid, 256, smem, st>>>(a);
+        AETH_LAUNCH_CHECK();
+    }
+    return AETH_OK;
+}
+
+// K6 job for an NF4 weight, when the grouped kernel takes the shape.
+bool b2_apply_job(const aeth_galore_config& cfg, const Param& p, const aeth_weight_ref* w, ApplyJob* j) {
+    if (!w || w->kind != AETH_WEIGHT_NF4 || !apply_grouped_supported(p.m, p.n, p.r)) return false;
+    const float lr = b2_lr(cfg, p.r);
+    j->X = p.side == 2 ? p.nbuf : p.proj;
+    j->Y = p.side == 2 ? p.proj : p.nbuf;
+    j->wp = static_cast<uint8_t*>(w->data);
+    j->wa = w->absmax;
+    j->m = p.m;
+    j->n = p.n;
+    j->lr = lr;
+    j->decay_mul = 1.0f - lr * cfg.weight_decay;
+    j->has_decay = cfg.weight_decay > 0.0f;
+    j->prequant = w->prequant_out;
+    j->delta = w->delta_out;
+    return (reinterpret_cast<uintptr_t>(w->data) & 15) == 0 && (reinterpret_cast<uintptr_t>(w->absmax) & 15) == 0;
+}
+
+int b2_weight_tile(aeth_galore_ctx* c, Param& p, const aeth_weight_ref* w, cudaStream_t st);
+
+// K6: back-projection and weight write for one parameter.
+int b2_weight(aeth_galore_ctx* c, Param& p, const aeth_weight_ref* w, cudaStream_t st) {
+    ApplyJob job;
+    if (b2_apply_job(c->cfg, p, w, &job)) return apply_grouped_launch(&job, 1, p.r, st);
+    return b2_weight_tile(c, p, w, st);
+}
+
+int b2_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, const aeth_weight_ref* w,
+             int zero_accum, cudaStream_t st) {
+    Param* pp = &p;
+    AETH_TRY(b2_adam_group(c, &pp, 1, clip, clip_dev, zero_accum, st));
+    return b2_weight(c, p, w, st);
+}
+
+// One-CTA-per-tile back-projection with the generic epilogues (NF4 shapes the
+// grouped kernel does not take, dense fp32 weights, delta-only output).
+int b2_weight_tile(aeth_galore_ctx* c, Param& p, const aeth_weight_ref* w, cudaStream_t st) {
+    const aeth_galore_config& cfg = c->cfg;
     const int m = p.m, n = p.n, r = p.r;
-    const float lr = cfg.scale_lr_by_rank ? cfg.lr / (float)(r < 1 ? 1 : r) : cfg.lr;
+    const float lr = b2_lr(cfg, r);
     const int has_decay = cfg.weight_decay > 0.0f;
     const float decay_mul = 1.0f - lr * cfg.weight_decay;
     // dW = X Y^T with X (m x r), Y (n x r), both K-major.
@@ -655,7 +767,8 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
         }
     }
     if ((st = ctx_alloc(c, &c->sq_slots, n_specs)) || (st = ctx_alloc(c, &c->sq_step, n_specs)) ||
-        (st = ctx_alloc(c, &c->partials, kSqPartials)) || (st = ctx_alloc(c, &c->clip_dev, 1)) ||
+        (st = ctx_alloc(c, &c->partials, std::max(kSqPartials, kSqGroupMax * kSqChunks))) ||
+        (st = ctx_alloc(c, &c->clip_dev, 1)) ||
         (st = ctx_alloc(c, &c->gnorm_dev, 1)))
         return fail(st);
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(AETH_ERR_CONFIG);
@@ -760,28 +873,68 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     DeviceGuard g(ctx->device);
     cudaStream_t st = to_stream(stream);
     const bool ref = ctx->cfg.mode == AETH_MODE_REF;
-    // A3 hook: project_and_accumulate for every parameter (backward.rs:510-521).
+    float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
+    if (ref) {
+        // A3 hook: project_and_accumulate for every parameter (backward.rs:510-521).
+        for (int i = 0; i < n; ++i) AETH_TRY(ref_project_accumulate(ctx->params[idx[i]], grads[i], grad_dtype, st));
+        // A6 pass 1: squared norms (hook.rs:149-182).
+        for (int i = 0; i < n; ++i) AETH_TRY(sqnorm_into(ctx, ctx->params[idx[i]], ctx->sq_step + i, st));
+        if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
+        clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
+        AETH_LAUNCH_CHECK();
+        // A6 pass 2: apply_update + zero_accum (hook.rs:190-194).
+        for (int i = 0; i < n; ++i) {
+            Param& p = ctx->params[idx[i]];
+            AETH_TRY(ref_apply(ctx, p, 1.0f, clip, weights ? &weights[i] : nullptr, st));
+            AETH_CUDA(cudaMemsetAsync(p.accum, 0, p.state_elems * sizeof(float), st));
+        }
+        return AETH_OK;
+    }
+    // B200: the layer's projections in grouped launches (one per rank value).
+    std::vector<ProjJob> jobs;
+    std::vector<int> ranks;
     for (int i = 0; i < n; ++i) {
         Param& p = ctx->params[idx[i]];
-        AETH_TRY(ref ? ref_project_accumulate(p, grads[i], grad_dtype, st)
-                     : b2_project_accumulate(p, grads[i], grad_dtype, st));
+        const void* g = nullptr;
+        AETH_TRY(b2_grad_bf16(p, grads[i], grad_dtype, st, &g));
+        if (std::find(ranks.begin(), ranks.end(), p.r) == ranks.end()) ranks.push_back(p.r);
+        jobs.push_back(ProjJob{g, p.projT, p.accum, p.m, p.n});
     }
-    // A6 pass 1: squared norms (hook.rs:149-182).
-    for (int i = 0; i < n; ++i) AETH_TRY(sqnorm_into(ctx, ctx->params[idx[i]], ctx->sq_step + i, st));
+    for (int r : ranks) {
+        std::vector<ProjJob> grp;
+        std::vector<int> members;
+        for (int i = 0; i < n; ++i)
+            if (ctx->params[idx[i]].r == r) { grp.push_back(jobs[i]); members.push_back(i); }
+        int s = proj_grouped_launch(grp.data(), (int)grp.size(), r, st);
+        if (s == AETH_ERR_UNSUPPORTED) {
+            for (int i : members) AETH_TRY(b2_project_tile(ctx->params[idx[i]], jobs[i].grad, st));
+        } else if (s != AETH_OK) {
+            return set_err(s);
+        }
+    }
+    std::vector<const float*> xs(n);
+    std::vector<int64_t> ns(n);
+    for (int i = 0; i < n; ++i) { xs[i] = ctx->params[idx[i]].accum; ns[i] = ctx->params[idx[i]].state_elems; }
+    AETH_TRY(sqnorm_group(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, st));
     if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
-    float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
     clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
     AETH_LAUNCH_CHECK();
-    // A6 pass 2: apply_update + zero_accum (hook.rs:190-194).
-    for (int i = 0; i < n; ++i) {
-        Param& p = ctx->params[idx[i]];
-        const aeth_weight_ref* w = weights ? &weights[i] : nullptr;
-        if (ref) {
-            AETH_TRY(ref_apply(ctx, p, 1.0f, clip, w, st));
-            AETH_CUDA(cudaMemsetAsync(p.accum, 0, p.state_elems * sizeof(float), st));
-        } else {
-            AETH_TRY(b2_apply(ctx, p, 1.0f, clip, w, 1, st));
+    {
+        std::vector<Param*> ps(n);
+        for (int i = 0; i < n; ++i) ps[i] = &ctx->params[idx[i]];
+        AETH_TRY(b2_adam_group(ctx, ps.data(), n, 1.0f, clip, 1, st));
+    }
+    for (int r : ranks) {
+        std::vector<ApplyJob> grp;
+        for (int i = 0; i < n; ++i) {
+            Param& p = ctx->params[idx[i]];
+            if (p.r != r) continue;
+            const aeth_weight_ref* w = weights ? &weights[i] : nullptr;
+            ApplyJob job;
+            if (b2_apply_job(ctx->cfg, p, w, &job)) grp.push_back(job);
+            else AETH_TRY(b2_weight_tile(ctx, p, w, st));
         }
+        if (!grp.empty()) AETH_TRY(apply_grouped_launch(grp.data(), (int)grp.size(), r, st));
     }
     return AETH_OK;
 }

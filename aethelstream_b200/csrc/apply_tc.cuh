@@ -1,0 +1,320 @@
+// apply_tc.cuh -- K6: back-projection with the fused NF4 weight write, for a
+// whole layer in one persistent launch.
+//
+// For every matrix p: dW = X Y^T (X: m x r, Y: n x r, bf16, K-major; right
+// side X = N, Y = Q; left side X = P, Y = N), then for each 64-element NF4
+// block of the weight: w = CODES[code] * absmax; w -= fl(lr * dW); optional
+// decoupled decay; requantise bit-exactly; store.
+//
+// Unit = (matrix, 128-row tile, 256-column tile).  Warps: 0 = TMEM allocation
+// + TMA producer, 1 = UMMA issuer, 2..17 = epilogue.  Epilogue warp e reads
+// TMEM lane quarter q = warp % 4 and owns the 64-column NF4 block e / 4 of the
+// tile: one row of one block per thread per unit, in two passes over 16-column
+// chunks -- pass 1 dequantises the old block, applies the update, writes the
+// updated values back over the accumulator columns in TMEM and reduces the new
+// absmax; pass 2 reloads them and requantises.  The NF4 tile (128 rows x 128
+// bytes, 128-byte swizzle) and its absmax tile (128 x 4 floats) are TMA-loaded
+// into one of kApplyWSlots weight slots, rewritten in place, and written back
+// with one TMA store per 32-row lane quarter as soon as that quarter's four
+// warps are done; a slot returns to the producer one unit later.  Operand
+// k-blocks (64 columns of r of X and Y) flow through a separate STAGES-deep
+// ring.  TMEM holds two 256-column accumulators so the epilogue of one tile
+// overlaps the MMAs of the next.
+#pragma once
+#include "nf4.cuh"
+#include "umma.cuh"
+
+namespace aeth {
+
+constexpr int kApplyMaxProblems = 8;
+constexpr int kApplyBN = 256;
+constexpr int kApplyEpiWarps = 16;
+constexpr int kApplyWSlots = 3;
+constexpr int kApplyThreads = 64 + 32 * kApplyEpiWarps;
+
+struct ApplyProblem {
+    CUtensorMap tmX;   // X, box 64 x 128
+    CUtensorMap tmY;   // Y, box 64 x 256
+    CUtensorMap tmW;   // packed NF4, box 128 B x 128 rows (load)
+    CUtensorMap tmS;   // absmax, box 4 x 128 (load)
+    CUtensorMap tmWq;  // packed NF4, box 128 B x 32 rows (per-quarter store)
+    CUtensorMap tmSq;  // absmax, box 4 x 32 (per-quarter store)
+    float* prequant_out;
+    float* delta_out;
+    int m, n;
+    int n_tiles;
+    int unit_begin;
+    float lr, decay_mul;
+    int has_decay;
+    int pad;
+};
+
+struct ApplyArgs {
+    ApplyProblem p[kApplyMaxProblems];
+    int nprob;
+    int total_units;
+    int kb;  // k-blocks per unit = ceil(r / 64)
+    uint32_t idesc;
+};
+
+template <int STAGES>
+struct ApplyLayout {
+    static constexpr int kA = 128 * 64 * 2;        // 16 KB
+    static constexpr int kB = kApplyBN * 64 * 2;   // 32 KB
+    static constexpr int kStage = kA + kB;
+    static constexpr int kWPacked = 128 * 128;     // 128 rows x 128 bytes
+    static constexpr int kWScale = 128 * 16;       // 128 rows x 4 floats
+    static constexpr int kWSlot = (kWPacked + kWScale + 1023) / 1024 * 1024;  // slots stay 1 KB aligned
+    static constexpr int kBar = 256;
+    static constexpr int kTotal = STAGES * kStage + kApplyWSlots * kWSlot + kBar + (int)sizeof(Nf4Tables32);
+};
+
+__device__ __forceinline__ int apply_find(const ApplyArgs& a, int u) {
+    int p = 0;
+#pragma unroll 1
+    while (p + 1 < a.nprob && u >= a.p[p + 1].unit_begin) ++p;
+    return p;
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns into v[OFF .. OFF+15].
+template <int OFF, int N>
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[N]) {
+    static_assert(OFF + 16 <= N, "tmem_ld16 destination too small");
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[OFF + i] = __uint_as_float(r[i]);
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kApplyThreads, 1)
+    apply_grouped_kernel(const __grid_constant__ ApplyArgs args, uint32_t* err) {
+    using L = ApplyLayout<STAGES>;
+    constexpr int kEpiThreads = 32 * kApplyEpiWarps;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = base;
+    uint8_t* sB = base + STAGES * L::kA;
+    uint8_t* wslot = base + STAGES * L::kStage;  // kApplyWSlots x (packed tile, scale tile)
+    uint64_t* full = reinterpret_cast<uint64_t*>(wslot + kApplyWSlots * L::kWSlot);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* w_full = acc_empty + 2;
+    uint64_t* w_empty = w_full + kApplyWSlots;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_empty + kApplyWSlots);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    Nf4Tables32* tab = reinterpret_cast<Nf4Tables32*>(reinterpret_cast<uint8_t*>(full) + L::kBar);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiThreads); }
+        for (int b = 0; b < kApplyWSlots; ++b) { mbar_init(&w_full[b], 1); mbar_init(&w_empty[b], 4); }
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) { tmem_alloc(tmem_slot, 2 * kApplyBN); tmem_relinquish(); }
+    nf4_tables32_init(tab, threadIdx.x, blockDim.x);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int total = args.total_units;
+    const int kb_n = args.kb;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0, j = 0;
+            for (int u = blockIdx.x; u < total && !*abort; u += gridDim.x, ++j) {
+                const int p = apply_find(args, u);
+                const ApplyProblem& pr = args.p[p];
+                const int local = u - pr.unit_begin;
+                const int m0 = (local / pr.n_tiles) * 128;
+                const int n0 = (local % pr.n_tiles) * kApplyBN;
+                const int wb = j % kApplyWSlots;
+                if (!mbar_wait(&w_empty[wb], ((uint32_t)(j / kApplyWSlots) & 1u) ^ 1u, abort, err, DEVERR_TIMEOUT_TMA))
+                    break;
+                mbar_arrive_expect_tx(&w_full[wb], L::kWPacked + L::kWScale);
+                uint8_t* ws = wslot + wb * L::kWSlot;
+                tma_load_2d(ws, &pr.tmW, &w_full[wb], n0 / 2, m0);
+                tma_load_2d(ws + L::kWPacked, &pr.tmS, &w_full[wb], n0 / 64, m0);
+                for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort, err, DEVERR_TIMEOUT_TMA)) break;
+                    mbar_arrive_expect_tx(&full[s], L::kStage);
+                    tma_load_2d(sA + s * L::kA, &pr.tmX, &full[s], kb * 64, m0);
+                    tma_load_2d(sB + s * L::kB, &pr.tmY, &full[s], kb * 64, n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int it = 0, j = 0;
+            for (int u = blockIdx.x; u < total && !*abort; u += gridDim.x, ++j) {
+                const int b = j & 1;
+                if (!mbar_wait(&acc_empty[b], ((uint32_t)(j >> 1) & 1u) ^ 1u, abort, err, DEVERR_TIMEOUT_MMA)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(b * kApplyBN);
+                for (int kb = 0; kb < kb_n; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!mbar_wait(&full[s], ph, abort, err, DEVERR_TIMEOUT_MMA)) break;
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + s * L::kA);
+                    const uint32_t b_addr = smem_u32(sB + s * L::kB);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_f16_ss(d, sdesc_sw128(a_addr + kk * 32, 16, 1024), sdesc_sw128(b_addr + kk * 32, 16, 1024),
+                                    args.idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&acc_full[b]);
+            }
+        }
+    } else {
+        const int ew = warp - 2;     // 0..15
+        const int q = warp & 3;      // TMEM lane quarter this warp may access = its 32-row group
+        const int blk = ew >> 2;     // 64-column NF4 block of the 256-wide tile
+        const int cl = blk * 64;     // first column of the block within the tile
+        const int row = q * 32 + lane;
+        const bool qleader = ew < 4 && lane == 0;  // one thread per row group issues its stores
+        const uint32_t tcol0 = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cl;
+        const uint32_t lut_s = smem_u32(tab->byte_lut);
+        const uint32_t bucket_bias = nf4_bucket_bias(tab);
+        int j = 0;
+        int pending = -1;  // slot of this row group's previous store, released one unit later
+        for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
+            const int p = apply_find(args, u);
+            const ApplyProblem& pr = args.p[p];
+            const int local = u - pr.unit_begin;
+            const int m0 = (local / pr.n_tiles) * 128;
+            const int n0 = (local % pr.n_tiles) * kApplyBN;
+            const int b = j & 1;
+            const int wb = j % kApplyWSlots;
+            if (!mbar_wait(&w_full[wb], (uint32_t)(j / kApplyWSlots) & 1u, abort, err, DEVERR_TIMEOUT_EPI)) break;
+            if (!mbar_wait(&acc_full[b], (uint32_t)(j >> 1) & 1u, abort, err, DEVERR_TIMEOUT_EPI) || *abort) break;
+            tc_fence_after();
+            uint8_t* wp = wslot + wb * L::kWSlot;
+            if (n0 + cl < pr.n) {  // warp-uniform
+                const float lr = pr.lr;
+                const int ck = cl / 32;  // first 16-byte chunk of this block's 32 packed bytes
+                uint8_t* rowp = wp + row * 128;
+                float* sp = reinterpret_cast<float*>(wp + L::kWPacked) + row * 4 + blk;
+                const float amax_old = *sp;
+                const uint32_t tcol = tcol0 + (uint32_t)(b * kApplyBN);
+                const int64_t grow = (int64_t)(m0 + row);
+                float* dout = (pr.delta_out && grow < pr.m) ? pr.delta_out + grow * pr.n + n0 + cl : nullptr;
+                float* pout = (pr.prequant_out && grow < pr.m) ? pr.prequant_out + grow * pr.n + n0 + cl : nullptr;
+                // pass 1: w = CODES * absmax_old - fl(lr * dW) [* decay] -> TMEM; block absmax
+                float amax = 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    float v[16], w[16];
+                    tmem_ld16<0>(tcol + (uint32_t)(c * 16), v);
+                    // words 2c, 2c+1 of the block: 8 adjacent bytes of chunk ck + c/2
+                    const uint2 qq =
+                        *reinterpret_cast<const uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
+                    nf4_dequant_word_s(qq.x, amax_old, lut_s, w);
+                    nf4_dequant_word_s(qq.y, amax_old, lut_s, w + 8);
+                    tmem_wait_ld();
+                    if (pr.has_decay) {
+                        const float dmul = pr.decay_mul;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float dl = __fmul_rn(v[i], lr);
+                            w[i] = __fmul_rn(__fsub_rn(w[i], dl), dmul);
+                            v[i] = dl;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float dl = __fmul_rn(v[i], lr);
+                            w[i] = __fsub_rn(w[i], dl);
+                            v[i] = dl;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(w[i]));
+                    tmem_st16(tcol + (uint32_t)(c * 16), w);
+                    if (dout) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4)
+                            *reinterpret_cast<float4*>(dout + c * 16 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    }
+                    if (pout) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4)
+                            *reinterpret_cast<float4*>(pout + c * 16 + i) = make_float4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+                    }
+                }
+                tmem_wait_st();
+                // pass 2: requantise from TMEM (fast classifier; exact fix-up next to boundaries)
+                const float safe = fmaxf(amax, 1e-8f), inv = __frcp_rn(safe);
+                float mind = 1.0f;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    float w[16];
+                    tmem_ld16<0>(tcol + (uint32_t)(c * 16), w);
+                    tmem_wait_ld();
+                    const uint32_t lo = nf4_fast_word8_s(w, inv, bucket_bias, mind);
+                    const uint32_t hi = nf4_fast_word8_s(w + 8, inv, bucket_bias, mind);
+                    *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
+                        make_uint2(lo, hi);
+                }
+                if (__any_sync(0xffffffffu, mind < kNf4NearWindow32)) {
+                    // Rare: redo words holding a near-boundary element with the
+                    // exact definition.  Warp-uniform loop (TMEM loads are
+                    // warp-collective).
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        float w[16];
+                        tmem_ld16<0>(tcol + (uint32_t)(c * 16), w);
+                        tmem_wait_ld();
+                        float m0v = 1.0f, m1v = 1.0f;
+                        nf4_fast_word8_s(w, inv, bucket_bias, m0v);
+                        nf4_fast_word8_s(w + 8, inv, bucket_bias, m1v);
+                        uint32_t* wa = reinterpret_cast<uint32_t*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
+                        if (m0v < kNf4NearWindow32)
+                            wa[0] = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe);
+                        if (m1v < kNf4NearWindow32)
+                            wa[1] = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe);
+                    }
+                }
+                *sp = amax;
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[b]);
+            fence_proxy_async();
+            named_bar(1 + q, 128);  // the four warps of this row group
+            if (qleader) {
+                tma_store_2d(&pr.tmWq, wp + q * 32 * 128, n0 / 2, m0 + q * 32);
+                tma_store_2d(&pr.tmSq, wp + L::kWPacked + q * 32 * 16, n0 / 64, m0 + q * 32);
+                bulk_commit();
+                if (pending >= 0) {
+                    bulk_wait_read<1>();  // this group's previous stores have read their slot
+                    mbar_arrive(&w_empty[pending]);
+                }
+                pending = wb;
+            }
+        }
+        if (qleader) {
+            bulk_wait<0>();
+            if (pending >= 0) mbar_arrive(&w_empty[pending]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * kApplyBN);
+    }
+}
+
+}  // namespace aeth

@@ -5,7 +5,8 @@
 //             from zero; dequant x = q * scale.
 // BLOCK_LINEAR  the same formula per contiguous block of `block` elements.
 // BLOCK_DYNAMIC per-block raw absmax; code = index of the nearest entry of a
-//             sorted 256-entry dynamic map to x / absmax (lower index on ties).
+//             sorted 256-entry dynamic map to x * (1 / absmax) (one reciprocal
+//             per block; lower index on ties).
 #pragma once
 #include "common.cuh"
 
@@ -63,7 +64,9 @@ __device__ __forceinline__ uint32_t dmap_encode(const float* __restrict__ map, f
     return dh < dl ? (uint32_t)lo : (uint32_t)(lo - 1);
 }
 
-__device__ __forceinline__ float dyn_xn(float x, float amax) { return amax > 0.0f ? __fdiv_rn(x, amax) : 0.0f; }
+// Dynamic codec normalisation: xn = x * (1 / absmax), one reciprocal per block.
+__device__ __forceinline__ float dyn_inv(float amax) { return amax > 0.0f ? __frcp_rn(amax) : 0.0f; }
+__device__ __forceinline__ float dyn_xn(float x, float inv) { return __fmul_rn(x, inv); }
 
 // ---------------------------------------------------------------------------
 // Per-tensor codec: absmax reduction into a device float (atomicMax on the
@@ -139,8 +142,9 @@ __global__ void block_encode_kernel(const float* __restrict__ x, int64_t n, int 
             for (int64_t i = s + threadIdx.x; i < e; i += blockDim.x) q[i] = lin_encode(x[i], inv);
             if (threadIdx.x == 0) scales[b] = scale;
         } else {
+            const float inv = dyn_inv(amax);
             for (int64_t i = s + threadIdx.x; i < e; i += blockDim.x)
-                q[i] = (int8_t)(uint8_t)dmap_encode(map, dyn_xn(x[i], amax));
+                q[i] = (int8_t)(uint8_t)dmap_encode(map, dyn_xn(x[i], inv));
             if (threadIdx.x == 0) scales[b] = amax;
         }
     }

@@ -322,21 +322,38 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     return fn;
 }
 
-// 2-D tensor map over a row-major matrix of 16-bit elements: `inner`
-// contiguous elements per row, `outer` rows, row pitch `ld` elements.
-inline int make_tmap_16b(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, int64_t ld,
-                         uint32_t box_inner, uint32_t box_outer, bool bf16) {
+// 2-D tensor map over a row-major matrix: `inner` contiguous elements per row,
+// `outer` rows, row pitch `ld` elements of `esize` bytes.  Returns
+// AETH_ERR_UNSUPPORTED when TMA cannot describe it (base not 16-byte aligned,
+// pitch not a multiple of 16 bytes).
+inline int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int esize, uint64_t inner,
+                        uint64_t outer, int64_t ld, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
     auto enc = tmap_encoder();
     if (!enc) return AETH_ERR_UNSUPPORTED;
-    if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || ((ld * 2) % 16) != 0) return AETH_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || ((ld * esize) % 16) != 0) return AETH_ERR_UNSUPPORTED;
     cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                     const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? AETH_OK : AETH_ERR_UNSUPPORTED;
+}
+
+// Tensor map over 16-bit (f16 / bf16) operands with the 128-byte swizzle the
+// UMMA descriptors expect.
+inline int make_tmap_16b(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, int64_t ld,
+                         uint32_t box_inner, uint32_t box_outer, bool bf16) {
+    return make_tmap_2d(map, ptr, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, inner,
+                        outer, ld, box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+inline int num_sms() {
+    static int n[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+    if (!n[dev] && cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n[dev] = 148;
+    return n[dev];
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>

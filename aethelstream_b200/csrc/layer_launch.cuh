@@ -1,0 +1,228 @@
+// layer_launch.cuh -- host launchers for the grouped (whole-layer) kernels:
+// projection (K4), squared norms, back-projection + NF4 write (K6).
+#pragma once
+#include "adam.cuh"
+#include "apply_tc.cuh"
+#include "gemm_tc.cuh"
+#include "proj_tc.cuh"
+
+namespace aeth {
+
+// ---------------------------------------------------------------------------
+// K4
+// ---------------------------------------------------------------------------
+struct ProjJob {
+    const void* grad;       // bf16 m x n
+    const uint16_t* projT;  // bf16 r x s (s = min(m, n))
+    float* racc;            // fp32 l x r
+    int m, n;
+};
+
+template <int BN>
+int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) {
+    constexpr int STAGES = 4;
+    using L = ProjLayout<BN, STAGES>;
+    DeviceRuntime* rt = nullptr;
+    AETH_TRY(runtime_for_current(&rt));
+    ProjArgs a;
+    memset(&a, 0, sizeof(a));
+    a.nprob = nj;
+    a.r = r;
+    a.idesc_k = idesc_f16(128, BN, true, false, false);
+    a.idesc_mn = idesc_f16(128, BN, true, true, false);
+    int64_t total_kb_tiles = 0;
+    for (int i = 0; i < nj; ++i) {
+        const int l = std::max(jobs[i].m, jobs[i].n), s = std::min(jobs[i].m, jobs[i].n);
+        total_kb_tiles += (int64_t)((l + 127) / 128) * ((s + 63) / 64);
+    }
+    const int64_t target_units = (int64_t)num_sms() * 8;
+    const int kb_target = (int)std::max<int64_t>(8, (total_kb_tiles + target_units - 1) / target_units);
+    int units = 0;
+    for (int i = 0; i < nj; ++i) {
+        const ProjJob& j = jobs[i];
+        ProjProblem& p = a.p[i];
+        const bool right = j.m >= j.n;
+        const int l = right ? j.m : j.n, s = right ? j.n : j.m;
+        if (right) AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)j.m, j.n, 64, 128, true));
+        else AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)j.m, j.n, 64, 64, true));
+        AETH_TRY(make_tmap_16b(&p.tmB, j.projT, (uint64_t)s, (uint64_t)r, s, 64, BN, true));
+        AETH_TRY(make_tmap_2d(&p.tmC, j.racc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)r, (uint64_t)l, r, 32, 128,
+                              CU_TENSOR_MAP_SWIZZLE_128B));
+        p.a_mn = right ? 0 : 1;
+        p.kb_total = (s + 63) / 64;
+        p.splits = (p.kb_total + kb_target - 1) / kb_target;
+        p.kb_per_unit = (p.kb_total + p.splits - 1) / p.splits;
+        p.splits = (p.kb_total + p.kb_per_unit - 1) / p.kb_per_unit;
+        p.unit_begin = units;
+        units += ((l + 127) / 128) * p.splits;
+    }
+    a.total_units = units;
+    const int smem = 1024 + L::kTotal;
+    auto kern = proj_grouped_kernel<BN, STAGES>;
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    if (!attr_set[dev]) {
+        AETH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr_set[dev] = true;
+    }
+    const int grid = std::min(num_sms(), units);
+    kern<<<grid, 192, smem, st>>>(a, rt->err_word);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+// Projects and accumulates every job; jobs must share the rank r.
+inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t st) {
+    if (r <= 0 || r > 256 || r % 8 != 0) return AETH_ERR_UNSUPPORTED;
+    for (int off = 0; off < nj; off += kProjMaxProblems) {
+        const int cnt = std::min(kProjMaxProblems, nj - off);
+        if (r <= 64) AETH_TRY(proj_grouped_launch_bn<64>(jobs + off, cnt, r, st));
+        else if (r <= 128) AETH_TRY(proj_grouped_launch_bn<128>(jobs + off, cnt, r, st));
+        else AETH_TRY(proj_grouped_launch_bn<256>(jobs + off, cnt, r, st));
+    }
+    return AETH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Squared norms of several accumulators, deterministic (fixed partial slots,
+// ordered final sums): grid (kSqChunks, n), then one CTA.
+// ---------------------------------------------------------------------------
+constexpr int kSqGroupMax = 16;
+constexpr int kSqChunks = 32;
+
+struct SqGroupArgs {
+    const float* x[kSqGroupMax];
+    int64_t n[kSqGroupMax];
+};
+
+__global__ void __launch_bounds__(256) sqnorm_group_partial_kernel(SqGroupArgs a, double* __restrict__ partials) {
+    __shared__ double red[8];
+    const int p = blockIdx.y;
+    const float* x = a.x[p];
+    const int64_t n = a.n[p];
+    double s = 0.0;
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+        s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+    for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        double v = (double)x[i];
+        s += v * v;
+    }
+    s = warp_sum_d(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+        partials[p * kSqChunks + blockIdx.x] = t;
+    }
+}
+
+__global__ void sqnorm_group_final_kernel(const double* __restrict__ partials, int np, double* __restrict__ out) {
+    const int p = threadIdx.x;
+    if (p < np) {
+        double t = 0.0;
+        for (int c = 0; c < kSqChunks; ++c) t += partials[p * kSqChunks + c];
+        out[p] = t;
+    }
+}
+
+// out[i] = sum of squares of xs[i] (f64); `partials` holds kSqGroupMax * kSqChunks doubles.
+inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, double* out, double* partials,
+                        cudaStream_t st) {
+    for (int off = 0; off < np; off += kSqGroupMax) {
+        const int cnt = std::min(kSqGroupMax, np - off);
+        SqGroupArgs a;
+        memset(&a, 0, sizeof(a));
+        for (int i = 0; i < cnt; ++i) {
+            a.x[i] = xs[off + i];
+            a.n[i] = ns[off + i];
+            if ((reinterpret_cast<uintptr_t>(a.x[i]) & 15) != 0) return AETH_ERR_UNSUPPORTED;
+        }
+        sqnorm_group_partial_kernel<<<dim3(kSqChunks, cnt), 256, 0, st>>>(a, partials);
+        sqnorm_group_final_kernel<<<1, 32, 0, st>>>(partials, cnt, out + off);
+        AETH_LAUNCH_CHECK();
+    }
+    return AETH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// K6
+// ---------------------------------------------------------------------------
+struct ApplyJob {
+    const uint16_t* X;  // m x r bf16
+    const uint16_t* Y;  // n x r bf16
+    uint8_t* wp;        // m x n/2
+    float* wa;          // m x n/64
+    int m, n;
+    float lr, decay_mul;
+    int has_decay;
+    float* prequant;
+    float* delta;
+};
+
+// The grouped kernel needs n % 256 == 0 (absmax rows a multiple of 16 bytes)
+// and r % 8 == 0, r <= 256.
+inline bool apply_grouped_supported(int m, int n, int r) {
+    return m > 0 && n > 0 && n % 256 == 0 && r > 0 && r % 8 == 0 && r <= 256;
+}
+
+inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
+    constexpr int STAGES = 3;
+    using L = ApplyLayout<STAGES>;
+    DeviceRuntime* rt = nullptr;
+    AETH_TRY(runtime_for_current(&rt));
+    for (int off = 0; off < nj; off += kApplyMaxProblems) {
+        const int cnt = std::min(kApplyMaxProblems, nj - off);
+        ApplyArgs a;
+        memset(&a, 0, sizeof(a));
+        a.nprob = cnt;
+        a.kb = (r + 63) / 64;
+        a.idesc = idesc_f16(128, kApplyBN, true, false, false);
+        int units = 0;
+        for (int i = 0; i < cnt; ++i) {
+            const ApplyJob& j = jobs[off + i];
+            if (!apply_grouped_supported(j.m, j.n, r)) return AETH_ERR_UNSUPPORTED;
+            ApplyProblem& p = a.p[i];
+            AETH_TRY(make_tmap_16b(&p.tmX, j.X, (uint64_t)r, (uint64_t)j.m, r, 64, 128, true));
+            AETH_TRY(make_tmap_16b(&p.tmY, j.Y, (uint64_t)r, (uint64_t)j.n, r, 64, kApplyBN, true));
+            AETH_TRY(make_tmap_2d(&p.tmW, j.wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(j.n / 2), (uint64_t)j.m,
+                                  j.n / 2, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+            AETH_TRY(make_tmap_2d(&p.tmS, j.wa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(j.n / 64), (uint64_t)j.m,
+                                  j.n / 64, 4, 128, CU_TENSOR_MAP_SWIZZLE_NONE));
+            AETH_TRY(make_tmap_2d(&p.tmWq, j.wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(j.n / 2), (uint64_t)j.m,
+                                  j.n / 2, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B));
+            AETH_TRY(make_tmap_2d(&p.tmSq, j.wa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(j.n / 64), (uint64_t)j.m,
+                                  j.n / 64, 4, 32, CU_TENSOR_MAP_SWIZZLE_NONE));
+            p.prequant_out = j.prequant;
+            p.delta_out = j.delta;
+            p.m = j.m;
+            p.n = j.n;
+            p.n_tiles = (j.n + kApplyBN - 1) / kApplyBN;
+            p.unit_begin = units;
+            p.lr = j.lr;
+            p.decay_mul = j.decay_mul;
+            p.has_decay = j.has_decay;
+            units += ((j.m + 127) / 128) * p.n_tiles;
+        }
+        a.total_units = units;
+        const int smem = 1024 + L::kTotal;
+        auto kern = apply_grouped_kernel<STAGES>;
+        static bool attr_set[kMaxDevices] = {};
+        int dev = 0;
+        AETH_TRY(current_device(&dev));
+        if (!attr_set[dev]) {
+            AETH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            attr_set[dev] = true;
+        }
+        const int grid = std::min(num_sms(), units);
+        kern<<<grid, kApplyThreads, smem, st>>>(a, rt->err_word);
+        AETH_LAUNCH_CHECK();
+    }
+    return AETH_OK;
+}
+
+}  // namespace aeth

@@ -19,7 +19,6 @@ __global__ void __launch_bounds__(256) lomo_sqnorm_kernel(const uint16_t* __rest
     for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < n8; c += (int64_t)gridDim.x * blockDim.x) {
         uint4 u = __ldg(reinterpret_cast<const uint4*>(g) + c);
         uint32_t w[4] = {u.x, u.y, u.z, u.w};
-        float part = 0.0f;
         double dpart = 0.0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -27,7 +26,6 @@ __global__ void __launch_bounds__(256) lomo_sqnorm_kernel(const uint16_t* __rest
             double hi = (double)bf16_bits_to_f32((uint16_t)(w[k] >> 16));
             dpart += lo * lo + hi * hi;
         }
-        (void)part;
         s += dpart;
     }
     for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -112,7 +110,9 @@ __global__ void __launch_bounds__(256) lomo_update_kernel(const uint16_t* __rest
             if (threadIdx.x == 0) mom_scales[b] = nsm;
         } else {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) out[k >> 2] |= dmap_encode(dm, dyn_xn(mo[k], bm)) << (8 * (k & 3));
+            const float inv = dyn_inv(bm);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) out[k >> 2] |= dmap_encode(dm, dyn_xn(mo[k], inv)) << (8 * (k & 3));
             if (threadIdx.x == 0) mom_scales[b] = bm;
         }
         *reinterpret_cast<uint2*>(mom8 + e0) = make_uint2(out[0], out[1]);

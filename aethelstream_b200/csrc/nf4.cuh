@@ -27,6 +27,8 @@ __constant__ float c_nf4_codes[16] = {
 
 constexpr float kNf4NearWindow = 1e-6f;
 
+__device__ __forceinline__ uint32_t smem_u32_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
 struct Nf4Tables {
     float2 byte_lut[256];  // (CODES[byte >> 4], CODES[byte & 15])
     float2 bucket[33];     // {midpoint threshold or +inf, lower code index as int bits}
@@ -104,6 +106,160 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
                 }
             }
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Compact tables for the fused epilogues: every lookup is a conflict-free
+// 32-bit LDS.  code16[c] = CODES[c].  bucket32[b] = the midpoint threshold of
+// bucket b (or 2.0 when the bucket holds none) with (lower code + 1) stored in
+// its low 4 mantissa bits; the perturbation (< 16 ulp, < 1e-6 absolute) is
+// covered by the wider near-window kNf4NearWindow32.
+// ---------------------------------------------------------------------------
+constexpr float kNf4NearWindow32 = 2.5e-6f;
+
+struct Nf4Tables32 {
+    float2 byte_lut[256];  // (CODES[byte >> 4], CODES[byte & 15])
+    float code16[16];
+    uint32_t bucket32[33];
+};
+
+__device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
+    for (int i = tid; i < 256; i += nthreads) t->byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
+    for (int i = tid; i < 16; i += nthreads) t->code16[i] = c_nf4_codes[i];
+    for (int b = tid; b < 33; b += nthreads) {
+        float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
+        int below = 0, code = -1;
+        float thr = 2.0f;
+        for (int k = 0; k < 15; ++k) {
+            float mid = (c_nf4_codes[k] + c_nf4_codes[k + 1]) * 0.5f;
+            if (mid < lo) below = k + 1;
+            else if (mid < hi) { thr = mid; code = k; }
+        }
+        if (code < 0) code = below;
+        t->bucket32[b] = (__float_as_uint(thr) & ~15u) | (uint32_t)(code + 1);
+    }
+}
+
+// Exact decisions for 8 elements (rare path; kept out of line).
+__device__ __noinline__ uint32_t nf4_exact_word8(float a0, float a1, float a2, float a3, float a4, float a5, float a6,
+                                                 float a7, float safe) {
+    const float a[8] = {a0, a1, a2, a3, a4, a5, a6, a7};
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) word |= nf4_code_exact(a[j], safe) << (8 * (j >> 1) + ((j & 1) ? 0 : 4));
+    return word;
+}
+
+// Fast classification of 8 values (one packed word) with the compact bucket
+// table; `mind` collects the smallest distance to a decision threshold so the
+// caller can send near-boundary words through nf4_exact_word8.
+__device__ __forceinline__ uint32_t nf4_fast_word8(const float* w, float inv, const uint32_t* __restrict__ bucket,
+                                                   float& mind) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float xn = __fmul_rn(w[j], inv);
+        const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);  // low bits: rint(16 xn) + 16
+        const uint32_t e = bucket[__float_as_uint(t) & 63u];
+        const float d = __fsub_rn(xn, __uint_as_float(e));
+        const uint32_t code = e + (uint32_t)(__float_as_int(d) >> 31);  // (lower + 1) - [d < 0]
+        mind = fminf(mind, fabsf(d));
+        word |= (code & 15u) << (8 * (j >> 1) + ((j & 1) ? 0 : 4));
+    }
+    return word;
+}
+
+// Shared-address variants for the fused apply epilogue.
+// bucket_bias: shared address of bucket32[0] minus (0x4B400000 << 2) modulo
+// 2^32, so the entry of value t = fma(xn, 16, 1.5*2^23 + 16) sits at
+// bucket_bias + (bits(t) << 2) -- one add instead of mask, shift and add.
+__device__ __forceinline__ uint32_t nf4_bucket_bias(const Nf4Tables32* t) {
+    return smem_u32_addr(t->bucket32) - (0x4B400000u << 2);
+}
+
+// 8 values -> one packed word; nibbles are shifted in from the top in memory
+// order (code[6], code[7], code[4], code[5], code[2], code[3], code[0], code[1]).
+__device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t bucket_bias, float& mind) {
+    constexpr int kOrder[8] = {6, 7, 4, 5, 2, 3, 0, 1};
+    uint32_t word = 0;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const float xn = __fmul_rn(w[kOrder[s]], inv);
+        const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);
+        uint32_t e;
+        asm("ld.shared.u32 %0, [%1];" : "=r"(e) : "r"(bucket_bias + (__float_as_uint(t) << 2)));
+        const float d = __fsub_rn(xn, __uint_as_float(e));
+        const uint32_t code = e + (uint32_t)(__float_as_int(d) >> 31);  // (lower + 1) - [d < 0]
+        mind = fminf(mind, fabsf(d));
+        word = (word << 4) | (code & 15u);
+    }
+    return word;
+}
+
+// Dequantise one packed word (8 elements) with the 256-entry byte table at
+// shared address lut_s.
+__device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, uint32_t lut_s, float* out8) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float2 c;
+        asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(c.x), "=f"(c.y) : "r"(lut_s + (__byte_perm(word, 0, 0x4440 + k) << 3)));
+        out8[2 * k] = __fmul_rn(c.x, amax);
+        out8[2 * k + 1] = __fmul_rn(c.y, amax);
+    }
+}
+
+// Quantise N values of one NF4 block (absmax `amax`) held in registers into
+// N/8 packed words, using the compact tables.  Bit-exact with quantizer.py.
+template <int N>
+__device__ __forceinline__ void nf4_quant_regs32(const float (&v)[N], float amax, const uint32_t* __restrict__ bucket,
+                                                 uint32_t (&packed)[N / 8]) {
+    const float safe = fmaxf(amax, 1e-8f);
+    const float inv = __frcp_rn(safe);
+    float mind = 1.0f;
+#pragma unroll
+    for (int w = 0; w < N / 8; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float xn = __fmul_rn(v[w * 8 + j], inv);
+            const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);  // low bits: rint(16 xn) + 16
+            const uint32_t e = bucket[__float_as_uint(t) & 63u];
+            const float d = __fsub_rn(xn, __uint_as_float(e));
+            // code = (lower code + 1) - [d < 0]; d == 0 lies in the near band
+            const uint32_t code = e + (uint32_t)(__float_as_int(d) >> 31);
+            mind = fminf(mind, fabsf(d));
+            word |= (code & 15u) << (8 * (j >> 1) + ((j & 1) ? 0 : 4));
+        }
+        packed[w] = word;
+    }
+    if (mind < kNf4NearWindow32) {
+        // Rare: some element is next to a decision boundary; redo the words
+        // that hold one with the exact definition.
+#pragma unroll
+        for (int w = 0; w < N / 8; ++w) {
+            float m8 = 1.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float xn = __fmul_rn(v[w * 8 + j], inv);
+                const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);
+                m8 = fminf(m8, fabsf(__fsub_rn(xn, __uint_as_float(bucket[__float_as_uint(t) & 63u]))));
+            }
+            if (m8 < kNf4NearWindow32)
+                packed[w] = nf4_exact_word8(v[w * 8], v[w * 8 + 1], v[w * 8 + 2], v[w * 8 + 3], v[w * 8 + 4],
+                                            v[w * 8 + 5], v[w * 8 + 6], v[w * 8 + 7], safe);
+        }
+    }
+}
+
+// Dequantise 8 codes packed in one little-endian word (byte k = code[2k] << 4
+// | code[2k+1]) into fp32 products with the 16-entry table.
+__device__ __forceinline__ void nf4_dequant_word16(uint32_t word, float amax, const float* __restrict__ code16,
+                                                   float* out8) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        out8[2 * k] = __fmul_rn(code16[(word >> (8 * k + 4)) & 15u], amax);
+        out8[2 * k + 1] = __fmul_rn(code16[(word >> (8 * k)) & 15u], amax);
     }
 }
 

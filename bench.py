@@ -34,16 +34,25 @@ sys.path.insert(0, ROOT)
 
 METRIC = "params updated/s (NF4->GaLore->INT8-Adam step)"
 UNIT = "params/s"
-SHAPES = [("d_wq", 4096, 4096), ("d_wk", 4096, 4096), ("d_wv", 4096, 4096), ("d_wo", 4096, 4096),
-          ("d_wg", 11008, 4096), ("d_wu", 11008, 4096), ("d_wd", 4096, 11008)]
+CONFIGS = {
+    # the bench workload
+    "c2": dict(shapes=[("d_wq", 4096, 4096), ("d_wk", 4096, 4096), ("d_wv", 4096, 4096), ("d_wo", 4096, 4096),
+                       ("d_wg", 11008, 4096), ("d_wu", 11008, 4096), ("d_wd", 4096, 11008)],
+               workload=("C2: one Llama-2-7B block per GPU (q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008), "
+                         "GaLore r=128 one-sided on the smaller dim, fixed projectors, NF4 weights, bf16 grads, "
+                         "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
+    # one 4096x4096 weight (used for small profiling captures)
+    "c1": dict(shapes=[("d_wq", 4096, 4096)],
+               workload=("C1: one 4096x4096 weight, GaLore r=128, NF4 weight, bf16 grad, "
+                         "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
+}
+SHAPES = CONFIGS["c2"]["shapes"]
 RANK = 128
 STATE_BLOCK = 2048
-WORKLOAD = ("C2: one Llama-2-7B block per GPU (q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008), "
-            "GaLore r=128 one-sided on the smaller dim, fixed projectors, NF4 weights, bf16 grads, "
-            "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")
+WORKLOAD = CONFIGS["c2"]["workload"]
 
 
-def algorithmic(shapes=SHAPES, r=RANK):
+def algorithmic(shapes=None, r=RANK):
     """Algorithmic bytes and flops per step, split by phase.
 
     projection phase (K4): read bf16 G (2 B/elem) + projector (2 s r).
@@ -52,7 +61,7 @@ def algorithmic(shapes=SHAPES, r=RANK):
     Flops: 2 r m n per GEMM (projection and back-projection) + ~12 r l (Adam).
     """
     bp = ba = fp = fa = 0
-    for _, m, n in shapes:
+    for _, m, n in (shapes or SHAPES):
         s, l = min(m, n), max(m, n)
         bp += 2 * m * n + 2 * s * r
         ba += 2 * 0.5625 * m * n + 4 * r * l + 8 * r * l / STATE_BLOCK + 2 * s * r
@@ -81,48 +90,63 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clocks and clock-event (throttle) reasons sampled during the timed
+    region: NVML in a thread every 10 ms (read-only queries), else
+    nvidia-smi -lms 200."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
+        self.samples = []
+        self.max_mhz = None
+        self._stop = False
+        self.thread = None
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+
+    def _nvml_loop(self, nv, h):
+        while not self._stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.samples.append((sm, get(h)))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.01)
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:  # noqa: BLE001 - no nvidia-smi: report no clocks
-            self.proc = None
+            import threading
+
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self._physical_index())
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001 - no NVML: report no clocks
+            self.thread = None
+
+    def _physical_index(self):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            try:
+                return int(vis.split(",")[self.idx])
+            except (ValueError, IndexError):
+                return self.idx
+        return self.idx
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:  # noqa: BLE001
-            self.proc.kill()
-        self.f.close()
-        rows = []
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "", 1).isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].replace(".", "", 1).isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+        self._stop = True
+        self.thread.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        sm = [s for s, _ in self.samples]
+        reasons = sorted({name for _, rs in self.samples for bit, name in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
 
 
 def cpu_baseline(frac, threads, k=1):
@@ -307,7 +331,9 @@ def run_b200(args):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) bf16 grads)",
             "config": {"workload": WORKLOAD, "params_per_gpu_step": params_per_step, "rank": RANK,
                        "state": "int8 dynamic-map, 2048-element blocks", "parallelism": f"layer-sharded x{world}",
-                       "l2": "inputs larger than L2 (405 MB of bf16 gradients per step, 2-deep ring)"},
+                       "l2": (f"inputs larger than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients per "
+                              "step, 2-deep ring)") if 2 * params_per_step > 126e6 else
+                             f"inputs smaller than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients)"},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic.get(tkey), "peak_kind": peak_kind},
             "roofline_step": {"algorithmic_bytes": total_bytes, "algorithmic_flops": total_flops,
@@ -316,7 +342,8 @@ def run_b200(args):
                               "apply_ms": apply_ms / args.steps, "proj_gbs": per_proj, "apply_gbs": per_apply},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                     "steps": k_e2e},
-            "gpu_launches": 36 * args.steps,
+            # per step: grouped projection, 2 sqnorm, clip, one Adam per matrix, grouped apply
+            "gpu_launches": (5 + len(SHAPES)) * args.steps,
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -338,9 +365,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    global SHAPES, WORKLOAD
+    SHAPES = CONFIGS[args.config]["shapes"]
+    WORKLOAD = CONFIGS[args.config]["workload"]
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -379,7 +379,7 @@ static int dmap_nearest(const float* map, float xn) {
  * block may be partial).  LINEAR: per-block copy of quantize.rs:4-26, so with
  * block >= n it is bit-identical to ref_quantize_absmax.  DYNAMIC: the block's
  * raw absmax is the scale; codes index b2_dynamic_map; nearest entry of
- * x / absmax, lower index on ties. */
+ * x * (1 / absmax) (one fp32 reciprocal per block), lower index on ties. */
 void b2_block_quantize(const float* x, int64_t n, int block, int codec, int is_signed, int8_t* q, float* scales) {
     float map[256];
     if (codec == B2_CODEC_DYNAMIC) b2_dynamic_map(is_signed, map);
@@ -392,8 +392,9 @@ void b2_block_quantize(const float* x, int64_t n, int block, int codec, int is_s
             float amax = 0.0f;
             for (int64_t i = s; i < e; ++i) amax = fmaxf(amax, fabsf(x[i]));
             scales[b] = amax;
+            const float inv = amax > 0.0f ? 1.0f / amax : 0.0f;  /* one reciprocal per block */
             for (int64_t i = s; i < e; ++i) {
-                float xn = amax > 0.0f ? x[i] / amax : 0.0f;
+                float xn = x[i] * inv;
                 q[i] = (int8_t)(uint8_t)dmap_nearest(map, xn);
             }
         }

@@ -134,6 +134,27 @@ def test_b200_step_matches_oracle(oracle, m, n, r, codec):
     opt.close()
 
 
+@pytest.mark.parametrize("m,n", [(4096, 1024), (1024, 4096)])
+def test_b200_projection_split_k_accumulates(oracle, m, n):
+    """Shapes with few row tiles make the grouped projection split K across
+    CTAs (partials added with TMA reduce-add); two calls accumulate."""
+    r = 128
+    opt = _opt("b200", [(0, "d_wq", m, n, r)])
+    rng = np.random.default_rng(m)
+    right = m >= n
+    s, l = (n, m) if right else (m, n)
+    P, Q = opt.get_projector(0, "d_wq")
+    proj = host(Q if right else P)
+    assert np.array_equal(proj, oracle.bf16_round(oracle.init_random_projection(s, r, 0)))  # layer 0: seed 0
+    acc_ref = np.zeros(l * r, np.float32)
+    for _ in range(2):
+        g = oracle.bf16_round((rng.standard_normal((m, n)) * 1e-3).astype(np.float32))
+        opt.project_and_accumulate(dev(g).to(torch.bfloat16), 0, "d_wq")
+        acc_ref = oracle.b2_project_accumulate(g, proj, acc_ref, m, n, r)
+    assert rel_fro(host(opt.get_accum(0, "d_wq")), acc_ref) < 1e-5
+    opt.close()
+
+
 def test_b200_fused_layer_step_equals_sequential(oracle):
     from aethelstream_b200 import nf4_quantize
     specs = [(0, "d_wq", 256, 256, 64), (0, "d_wg", 512, 256, 64), (0, "d_wd", 256, 512, 64)]

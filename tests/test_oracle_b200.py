@@ -37,7 +37,7 @@ def test_dynamic_codec_roundtrip(oracle, signed):
         blk = slice(b * 2048, (b + 1) * 2048)
         assert np.abs(x[blk] - rec[blk]).max() <= bound * s[b] * (1 + 1e-5)
     # nearest-entry property
-    xn = x[:2048] / s[0]
+    xn = x[:2048] * (np.float32(1.0) / s[0])
     d = np.abs(xn[:, None] - m[None, :])
     assert np.array_equal(q[:2048].view(np.uint8), d.argmin(axis=1).astype(np.uint8))
 
