@@ -112,7 +112,7 @@ def load(path: str | None = None):
     p = path or LIB_PATH
     if not os.path.exists(p):
         raise ImportError(
-            f"libaeth_galore.so not found at {p}; build it with `python -m aethelstream_b200.build` "
+            f"libaeth_galore.so not found at {p}; build it with `python aethelstream_b200/build.py` "
             "(this package has no CPU fallback)")
     L = C.CDLL(p)
     for name, (res, args) in SIGNATURES.items():

@@ -1,6 +1,9 @@
 """Build libaeth_galore.so (sm_100a) in-tree with nvcc.
 
-    python -m aethelstream_b200.build [--force] [--verbose]
+    python aethelstream_b200/build.py [--force] [--verbose]
+
+Run it as a script (or load it by file path): importing the package itself
+requires the built library.
 
 The library is a single translation unit (csrc/aeth_galore.cu) linked against
 the static CUDA runtime, so it only needs the driver on the machine that loads

@@ -21,9 +21,9 @@ def header_functions():
 
 @pytest.fixture(scope="module")
 def lib():
+    import __graft_entry__
+    __graft_entry__.build()  # loads aethelstream_b200/build.py by path, then the package
     from aethelstream_b200 import _lib as L
-    from aethelstream_b200 import build
-    build.build()
     return L
 
 
