@@ -58,6 +58,7 @@ _vp, _i, _i64, _f, _u32, _u64, _d = C.c_void_p, C.c_int, C.c_int64, C.c_float, C
 SIGNATURES = {
     "galore_project_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "galore_project_backward": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "galore_project_forward_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "galore_quantize_absmax_f32_to_i8": (_i, [_vp, _vp, _vp, _i, _vp]),
     "galore_dequantize_i8_to_f32": (_i, [_vp, _vp, _f, _i, _vp]),
     "doublepass_galore_apply": (None, [_vp, _vp, _vp, _vp, _f, _f, _f, _f, _f, _i, _i]),

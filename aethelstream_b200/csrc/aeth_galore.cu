@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -572,6 +573,82 @@ int galore_project_forward(const void* G, const void* P, const void* Q, void* R,
         return set_err(s2);
     }
     return AETH_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of galore_project_forward.
+//
+// For callers that cannot allocate device memory at the point of the call:
+// for example code running inside another framework's step whose device
+// memory is all reserved by that framework's caching allocator (a raw
+// cudaMalloc there fails or fragments the pool), or code that must not
+// allocate once a run has started.  The r x n fp16 intermediate P^T G lives
+// in g_noalloc_temp below, a fixed array every device that loads this library
+// holds until the process exits.  Device code may name the array; host code
+// must use the address from cudaGetSymbolAddress (the host-side symbol is a
+// stand-in, not a device address).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocTempElems = 8 * 1024 * 1024;  // 16 MiB of fp16: r * n <= 8,388,608
+
+static __device__ __align__(256) __half g_noalloc_temp[kNoAllocTempElems];
+// Error word for the bounded waits of the tcgen05 kernels, so the first call
+// on a device needs no cudaMalloc either.
+static __device__ __align__(16) uint32_t g_noalloc_err_word;
+
+struct NoAllocDevice {
+    void* temp = nullptr;
+    bool ready = false;
+};
+NoAllocDevice g_noalloc[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: device addresses of the static
+// arrays.  If the library's per-device runtime is not set up yet, its error
+// word becomes g_noalloc_err_word (zero-initialised at module load), so no
+// later step on this path allocates.
+int noalloc_setup(void** temp) {
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return AETH_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc[dev];
+    if (!d.ready) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_temp);
+        if (e != cudaSuccess) return (int)e;
+        if (!g_rt[dev].init) {
+            void* w = nullptr;
+            e = cudaGetSymbolAddress(&w, g_noalloc_err_word);
+            if (e != cudaSuccess) return (int)e;
+            g_rt[dev].err_word = static_cast<uint32_t*>(w);
+            g_rt[dev].init = true;
+        }
+        d.temp = p;
+        d.ready = true;
+    }
+    *temp = d.temp;
+    return AETH_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int galore_project_forward_noalloc(const void* G, const void* P, const void* Q, void* R, int m, int n, int r,
+                                   aeth_stream_t stream) {
+    if (m <= 0 || n <= 0 || r <= 0) return set_err(AETH_ERR_ARG);
+    if (!G || !P || !Q || !R) return set_err(AETH_ERR_ARG);
+    if ((int64_t)r * n > kNoAllocTempElems) return set_err(AETH_ERR_UNSUPPORTED);  // r * n above the fixed scratch
+    void* temp = nullptr;
+    int st = noalloc_setup(&temp);
+    if (st != AETH_OK) return set_err(st);
+    // Every element of the r x n intermediate is written before it is read,
+    // so the array's previous contents never matter.
+    return galore_project_forward(G, P, Q, R, temp, m, n, r, stream);
 }
 
 int galore_project_backward(const void* N, const void* P, const void* Q, void* G_tilde, void* temp, int m, int n,

@@ -58,6 +58,25 @@ int galore_project_forward(const void* G, const void* P, const void* Q, void* R,
 int galore_project_backward(const void* N, const void* P, const void* Q, void* G_tilde, void* temp, int m, int n,
                             int r, aeth_stream_t stream);
 
+/* No counterpart in the reference.  galore_project_forward without the temp
+ * argument, for callers that cannot allocate device memory where they call
+ * this: code inside another framework's step whose device memory is all held
+ * by that framework's caching allocator (a raw cudaMalloc there fails or
+ * fragments the pool), or code that must not allocate once a run has started.
+ * The r x n fp16 intermediate P^T G lives in a fixed 16 MiB array inside the
+ * library (r * n <= 8,388,608), which every GPU that loads the library holds
+ * until the process exits; no call allocates or frees anything.
+ * Larger r * n returns AETH_ERR_UNSUPPORTED (-4) without touching the GPU.
+ * The first call on a device looks up the array's device address (and sets up
+ * the library's per-device error word there); make that first call before any
+ * stream capture.  All calls on a device share the one array: calls whose
+ * work overlaps on the GPU (different streams, or different host threads)
+ * race on it and must be serialised by the caller.  The array's previous
+ * contents never matter, since the intermediate is fully written before it is
+ * read.  Otherwise identical to galore_project_forward (same status codes). */
+int galore_project_forward_noalloc(const void* G, const void* P, const void* Q, void* R, int m, int n, int r,
+                                   aeth_stream_t stream);
+
 /* Replaces galore/kernels/quantize_state.cuh:12-18 (quantize_state.cu:61-86).
  * scale = max|x| / 127 (1.0 when max|x| == 0), q = clamp(round(x / scale), +-127)
  * with round half away from zero as in the live CPU path (galore/src/quantize.rs:17-26).
