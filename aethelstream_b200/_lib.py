@@ -78,6 +78,8 @@ SIGNATURES = {
     "aeth_galore_step_count": (_u64, [_vp]),
     "aeth_galore_step": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(_vp), _i, C.POINTER(WeightRef), SQ_HOOK, _vp, _vp,
                               _vp]),
+    "aeth_galore_set_phase_timing": (_i, [_vp, _i]),
+    "aeth_galore_phase_times": (_i, [_vp, C.POINTER(_d), C.POINTER(_i)]),
     "aeth_galore_set_projector": (_i, [_vp, _i, _vp, _vp, _vp]),
     "aeth_galore_get_projector": (_i, [_vp, _i, _vp, _vp, _vp]),
     "aeth_galore_get_state": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp]),
@@ -88,6 +90,7 @@ SIGNATURES = {
     "aeth_int8_quantize": (_i, [_vp, _i64, _i, _i, _i, _vp, _vp, _vp]),
     "aeth_int8_dequantize": (_i, [_vp, _vp, _i64, _i, _i, _i, _vp, _vp]),
     "aeth_dynamic_map": (_i, [_i, C.POINTER(_f)]),
+    "aeth_selfcheck": (_i, [_i, C.POINTER(C.c_ulonglong)]),
     "aeth_lomo_sqnorm": (_i, [_vp, _i64, _vp, _vp]),
     "aeth_lomo_update": (_i, [_vp, _i64, _vp, _f, _f, _f, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "aeth_status_string": (C.c_char_p, [_i]),

@@ -157,9 +157,11 @@ __global__ void __launch_bounds__(256) b2_adam_kernel(AdamB2Args a) {
 // iteration; thread t owns elements [8t, 8t+8) of the block, so the update,
 // the block absmax and the encode run from registers in a single HBM pass:
 // read R (4 B) + m, v codes (2 B), write m, v codes (2 B) + N bf16 (2 B)
-// [+ zero R (4 B)] per element.  The dynamic-map encode is a binary search
-// over a lane-replicated copy of the map (entry i for lane L at word
-// 32 i + L, i.e. always bank L), so it never has bank conflicts.
+// [+ zero R (4 B)] per element.  Dynamic-map decode reads a copy of the map
+// replicated over 16 banks (entry i for lane L at word 16 i + L % 16); the
+// encode is one bucket-table lookup (dmap_encode_lut).  Element pairs go
+// through the packed f32x2 helpers (mul2_rn, add2_rn), which round every lane like the
+// scalar __fmul_rn / __fadd_rn.
 // ---------------------------------------------------------------------------
 constexpr int kAdamGroupMax = 16;
 
@@ -180,33 +182,88 @@ struct AdamGroupArgs {
     int zero_accum;
 };
 
-__device__ __forceinline__ uint32_t dmap_encode_rep(const float* __restrict__ rep, int lane, float xn) {
-    int lo = 0;
-#pragma unroll
-    for (int step = 128; step > 0; step >>= 1)
-        if (rep[(lo + step - 1) * 32 + lane] < xn) lo += step;
-    if (lo == 0) return 0u;
-    if (lo == 256) return 255u;
-    const float dl = fabsf(__fsub_rn(xn, rep[(lo - 1) * 32 + lane]));
-    const float dh = fabsf(__fsub_rn(xn, rep[lo * 32 + lane]));
-    return dh < dl ? (uint32_t)lo : (uint32_t)(lo - 1);
+// ---------------------------------------------------------------------------
+// Adam direction in bf16: bf16(fl(mo / fl(fl(sqrt(va)) + eps))) (adamw.rs:
+// 129-131 followed by the bf16 store of N).  Fast path: hardware sqrt and
+// reciprocal approximations, q' = fl(mo * rcp(fl(sqrt'(va) + eps))), within
+// about ten ulp of the correctly rounded quotient q (a few ulp for each
+// approximation, half an ulp per rounding).  bf16 rounding of q' and of q
+// agree unless the low 16 bits of q' lie within kAdamDirGuard of the tie
+// 0x8000, so those -- and tiny, infinite or NaN values -- are recomputed
+// with IEEE sqrt and division.  aeth_selfcheck(AETH_SELFCHECK_ADAM_DIR)
+// compares the two paths over every float bit pattern of va.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kAdamDirGuard = 128;  // ulp
+
+__device__ __forceinline__ float adam_dir_exact(float mo, float va, float eps) {
+    return __fdiv_rn(mo, __fadd_rn(__fsqrt_rn(va), eps));
 }
 
+__device__ __forceinline__ float adam_dir_fast(float mo, float va, float eps) {
+    float s, r;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(s) : "f"(va));
+    const float d = __fadd_rn(s, eps);
+    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+    const float q = __fmul_rn(mo, r);
+    const uint32_t qb = __float_as_uint(q), mag = qb & 0x7fffffffu;
+    const bool near_tie = ((qb & 0xffffu) + kAdamDirGuard - 0x8000u) < 2u * kAdamDirGuard;
+    const bool odd = (mag != 0u && mag < 0x0d800000u) || mag >= 0x7f800000u || !(d >= 1e-30f);  // tiny, inf/NaN
+    return (near_tie || odd) ? adam_dir_exact(mo, va, eps) : q;
+}
+
+// Every float bit pattern as va, with mo drawn from [-0.5, 0.5) by a hash of
+// the pattern and eps = 1e-8: counts bf16 disagreements of the two paths.
+__global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ mismatches) {
+    unsigned long long bad = 0;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < (1ull << 32); i += stride) {
+        const float va = __uint_as_float((uint32_t)i);
+        const float mo = (float)(((uint32_t)i * 2654435761u) >> 8) * 0x1p-24f - 0.5f;
+        const uint16_t f = f32_to_bf16_bits(adam_dir_fast(mo, va, 1e-8f));
+        const uint16_t e = f32_to_bf16_bits(adam_dir_exact(mo, va, 1e-8f));
+        // NaN results may differ in payload only
+        bad += f != e && !((f & 0x7fffu) > 0x7f80u && (e & 0x7fffu) > 0x7f80u);
+    }
+    bad = warp_sum_u64(bad);
+    if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
+}
+
+// Dynamic-codec shared memory of b2_adam_group_kernel: two 16-bank replicated
+// maps, the two sorted maps and the two bucket tables.
+constexpr int kAdamDynSmem = (2 * 256 * 16 + 2 * 256 + 2 * kDmapLutN) * 4;
+
+template <bool DYN>
 __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
-    extern __shared__ float dyn_smem[];  // DYNAMIC codec: 2 x 256 x 32 floats (signed, unsigned map)
+    extern __shared__ __align__(16) float dyn_smem[];
     __shared__ float red_m[8], red_v[8];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, l16 = lane & 15;
     float* rep_s = dyn_smem;
-    float* rep_u = dyn_smem + 256 * 32;
-    if (a.codec == AETH_CODEC_BLOCK_DYNAMIC) {
-        for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-            rep_s[i] = c_dmap_signed[i >> 5];
-            rep_u[i] = c_dmap_unsigned[i >> 5];
+    float* rep_u = rep_s + 256 * 16;
+    float* map_s = rep_u + 256 * 16;
+    float* map_u = map_s + 256;
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(map_u + 256);
+    uint32_t* lut_u = lut_s + kDmapLutN;
+    if (DYN) {
+        for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
+            rep_s[i] = c_dmap_signed[i >> 4];
+            rep_u[i] = c_dmap_unsigned[i >> 4];
+        }
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+            map_s[i] = c_dmap_signed[i];
+            map_u[i] = c_dmap_unsigned[i];
+        }
+        for (int i = threadIdx.x; i < kDmapLutN; i += blockDim.x) {
+            lut_s[i] = g_dmap_lut[0][i];
+            lut_u[i] = g_dmap_lut[1][i];
         }
     }
     __syncthreads();
     const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
     const float omb1 = __fsub_rn(1.0f, a.b1), omb2 = __fsub_rn(1.0f, a.b2);
+    const float2 b1x2 = make_float2(a.b1, a.b1), b2x2 = make_float2(a.b2, a.b2);
+    const float2 omb1x2 = make_float2(omb1, omb1), omb2x2 = make_float2(omb2, omb2);
+    const float2 clipx2 = make_float2(clip, clip);
+    const bool fast_dir = a.eps >= 0.0f;
     const int total = a.block_begin[a.np];
     for (int gb = blockIdx.x; gb < total; gb += gridDim.x) {
         int p = 0;
@@ -224,27 +281,40 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
             const uint2 qm = *reinterpret_cast<const uint2*>(a.m8[p] + e0);
             const uint2 qv = *reinterpret_cast<const uint2*>(a.v8[p] + e0);
             const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            const float2 smx2 = make_float2(sm, sm), svx2 = make_float2(sv, sv);
             uint32_t nb[4];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t cm = ((k < 4 ? qm.x : qm.y) >> (8 * (k & 3))) & 0xffu;
-                const uint32_t cv = ((k < 4 ? qv.x : qv.y) >> (8 * (k & 3))) & 0xffu;
-                float m0, v0;
-                if (a.codec == AETH_CODEC_BLOCK_LINEAR) {
-                    m0 = __fmul_rn((float)(int8_t)cm, sm);
-                    v0 = __fmul_rn((float)(int8_t)cv, sv);
+            for (int k = 0; k < 8; k += 2) {
+                const uint32_t wm = k < 4 ? qm.x : qm.y, wv = k < 4 ? qv.x : qv.y;
+                const uint32_t cm0 = (wm >> (8 * (k & 3))) & 0xffu, cm1 = (wm >> (8 * (k & 3) + 8)) & 0xffu;
+                const uint32_t cv0 = (wv >> (8 * (k & 3))) & 0xffu, cv1 = (wv >> (8 * (k & 3) + 8)) & 0xffu;
+                float2 m0, v0;
+                if (DYN) {
+                    m0 = make_float2(rep_s[cm0 * 16 + l16], rep_s[cm1 * 16 + l16]);
+                    v0 = make_float2(rep_u[cv0 * 16 + l16], rep_u[cv1 * 16 + l16]);
                 } else {
-                    m0 = __fmul_rn(rep_s[cm * 32 + lane], sm);
-                    v0 = __fmul_rn(rep_u[cv * 32 + lane], sv);
+                    m0 = make_float2((float)(int8_t)cm0, (float)(int8_t)cm1);
+                    v0 = make_float2((float)(int8_t)cv0, (float)(int8_t)cv1);
                 }
-                const float gg = clip != 1.0f ? __fmul_rn(g[k], clip) : g[k];
-                mo[k] = __fadd_rn(__fmul_rn(a.b1, m0), __fmul_rn(omb1, gg));
-                va[k] = __fadd_rn(__fmul_rn(a.b2, v0), __fmul_rn(__fmul_rn(omb2, gg), gg));
-                const float nv = __fdiv_rn(mo[k], __fadd_rn(__fsqrt_rn(va[k]), a.eps));
-                const uint32_t bits = f32_to_bf16_bits(nv);
-                if (k & 1) nb[k >> 1] |= bits << 16; else nb[k >> 1] = bits;
-                am = fmaxf(am, fabsf(mo[k]));
-                av = fmaxf(av, fabsf(va[k]));
+                m0 = mul2_rn(m0, smx2);
+                v0 = mul2_rn(v0, svx2);
+                float2 gg = make_float2(g[k], g[k + 1]);
+                if (clip != 1.0f) gg = mul2_rn(gg, clipx2);
+                // products paired, sums scalar (a packed add of fresh products would be fused)
+                const float2 mo2 = add2_sep(mul2_rn(b1x2, m0), mul2_rn(omb1x2, gg));
+                const float2 va2 = add2_sep(mul2_rn(b2x2, v0), mul2_rn(mul2_rn(omb2x2, gg), gg));
+                mo[k] = mo2.x;
+                mo[k + 1] = mo2.y;
+                va[k] = va2.x;
+                va[k + 1] = va2.y;
+                // N is stored in bf16, so the approximate quotient serves where its
+                // bf16 rounding provably matches (eps >= 0 keeps the error bound).
+                const float n0 = fast_dir ? adam_dir_fast(mo2.x, va2.x, a.eps) : adam_dir_exact(mo2.x, va2.x, a.eps);
+                const float n1 = fast_dir ? adam_dir_fast(mo2.y, va2.y, a.eps) : adam_dir_exact(mo2.y, va2.y, a.eps);
+                const __nv_bfloat162 nn = __floats2bfloat162_rn(n0, n1);  // .x = n0 in the low half
+                nb[k >> 1] = *reinterpret_cast<const uint32_t*>(&nn);
+                am = fmaxf(am, fmaxf(fabsf(mo2.x), fabsf(mo2.y)));
+                av = fmaxf(av, fmaxf(fabsf(va2.x), fabsf(va2.y)));
             }
             *reinterpret_cast<uint4*>(a.nout[p] + e0) = make_uint4(nb[0], nb[1], nb[2], nb[3]);
         }
@@ -259,7 +329,7 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
         float nsm, nsv;
         if (valid) {
             uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
-            if (a.codec == AETH_CODEC_BLOCK_LINEAR) {
+            if (!DYN) {
                 nsm = lin_scale_from_absmax(bm);
                 nsv = lin_scale_from_absmax(bv);
                 const float im = lin_inv(nsm), iv = lin_inv(nsv);
@@ -272,10 +342,16 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
                 nsm = bm;
                 nsv = bv;
                 const float im = dyn_inv(bm), iv = dyn_inv(bv);
+                const float2 imx2 = make_float2(im, im), ivx2 = make_float2(iv, iv);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    om[k >> 2] |= dmap_encode_rep(rep_s, lane, dyn_xn(mo[k], im)) << (8 * (k & 3));
-                    ov[k >> 2] |= dmap_encode_rep(rep_u, lane, dyn_xn(va[k], iv)) << (8 * (k & 3));
+                for (int k = 0; k < 8; k += 2) {
+                    const float2 xm = mul2_rn(make_float2(mo[k], mo[k + 1]), imx2);  // dyn_xn, paired
+                    const float2 xv = mul2_rn(make_float2(va[k], va[k + 1]), ivx2);
+                    const int sh = 8 * (k & 3);
+                    om[k >> 2] |= (dmap_encode_lut<true>(lut_s, map_s, xm.x) |
+                                   (dmap_encode_lut<true>(lut_s, map_s, xm.y) << 8)) << sh;
+                    ov[k >> 2] |= (dmap_encode_lut<false>(lut_u, map_u, xv.x) |
+                                   (dmap_encode_lut<false>(lut_u, map_u, xv.y) << 8)) << sh;
                 }
             }
             *reinterpret_cast<uint2*>(a.m8[p] + e0) = make_uint2(om[0], om[1]);

@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <array>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -228,10 +229,45 @@ struct aeth_galore_ctx {
     double* partials = nullptr;  // kSqPartials
     float* clip_dev = nullptr;
     double* gnorm_dev = nullptr;
+    unsigned int* sq_ticket = nullptr;  // sqnorm_group's completion counter, zero between launches
     std::vector<void*> allocs;
+    // aeth_galore_set_phase_timing: five events per step (phase boundaries)
+    bool phase_timing = false;
+    std::vector<std::array<cudaEvent_t, 5>> phase_pending, phase_pool;
 };
 
 namespace {
+
+// Phase-boundary events of one aeth_galore_step; the set goes back to the
+// pool unless the step finished and committed it.
+struct PhaseMarks {
+    aeth_galore_ctx* c = nullptr;
+    std::array<cudaEvent_t, 5> ev{};
+    bool committed = false;
+    int begin(aeth_galore_ctx* ctx) {
+        if (!ctx->phase_timing) return AETH_OK;
+        if (ctx->phase_pool.empty()) {
+            std::array<cudaEvent_t, 5> e{};
+            for (cudaEvent_t& x : e) AETH_CUDA(cudaEventCreate(&x));
+            ctx->phase_pool.push_back(e);
+        }
+        ev = ctx->phase_pool.back();
+        ctx->phase_pool.pop_back();
+        c = ctx;
+        return AETH_OK;
+    }
+    int mark(int k, cudaStream_t st) {
+        if (c) AETH_CUDA(cudaEventRecord(ev[k], st));
+        return AETH_OK;
+    }
+    void commit() {
+        if (c) c->phase_pending.push_back(ev);
+        committed = true;
+    }
+    ~PhaseMarks() {
+        if (c && !committed) c->phase_pool.push_back(ev);
+    }
+};
 
 struct DeviceGuard {
     int prev = -1;
@@ -396,15 +432,7 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
     }
     AETH_TRY(codec_maps_ensure());
     const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
-    const int smem = dyn ? 2 * 256 * 32 * (int)sizeof(float) : 0;
-    static bool attr_set[kMaxDevices] = {};
-    int dev = 0;
-    AETH_TRY(current_device(&dev));
-    if (!attr_set[dev]) {
-        AETH_CUDA(cudaFuncSetAttribute(b2_adam_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       2 * 256 * 32 * (int)sizeof(float)));
-        attr_set[dev] = true;
-    }
+    static_assert(kAdamDynSmem <= 48 * 1024, "dynamic-codec tables exceed the default shared-memory limit");
     for (int off = 0; off < np; off += kAdamGroupMax) {
         const int cnt = std::min(kAdamGroupMax, np - off);
         AdamGroupArgs a;
@@ -432,8 +460,11 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         a.b2 = cfg.beta2;
         a.eps = cfg.eps;
         a.zero_accum = zero_accum;
-        const int grid = std::min(blocks, num_sms() * (dyn ? 3 : 8));
-        b2_adam_group_kernel<<<grid, 256, smem, st>>>(a);
+        const int grid = std::min(blocks, num_sms() * (dyn ? 4 : 8));
+        if (dyn)
+            b2_adam_group_kernel<true><<<grid, 256, kAdamDynSmem, st>>>(a);
+        else
+            b2_adam_group_kernel<false><<<grid, 256, 0, st>>>(a);
         AETH_LAUNCH_CHECK();
     }
     return AETH_OK;
@@ -541,6 +572,26 @@ int aeth_device_error(int device) {
 int aeth_dynamic_map(int is_signed, float out[256]) {
     if (!out) return AETH_ERR_ARG;
     return build_dynamic_map(is_signed, out);
+}
+
+int aeth_selfcheck(int which, unsigned long long* mismatches) {
+    if (!mismatches || which < AETH_SELFCHECK_DMAP_SIGNED || which > AETH_SELFCHECK_ADAM_DIR)
+        return set_err(AETH_ERR_ARG);
+    AETH_TRY(codec_maps_ensure());
+    unsigned long long* d = nullptr;
+    AETH_CUDA(cudaMalloc(&d, sizeof(*d)));
+    cudaError_t e = cudaMemset(d, 0, sizeof(*d));
+    if (e == cudaSuccess) {
+        if (which == AETH_SELFCHECK_ADAM_DIR)
+            adam_dir_selfcheck_kernel<<<num_sms() * 8, 256>>>(d);
+        else
+            dmap_selfcheck_kernel<<<num_sms() * 8, 256>>>(which == AETH_SELFCHECK_DMAP_SIGNED ? 1 : 0, d);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(mismatches, d, sizeof(*d), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    AETH_CUDA(e);
+    return AETH_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -747,6 +798,9 @@ int aeth_galore_destroy(aeth_galore_ctx* ctx) {
     if (!ctx) return AETH_ERR_ARG;
     DeviceGuard g(ctx->device);
     cudaDeviceSynchronize();
+    for (auto* v : {&ctx->phase_pending, &ctx->phase_pool})
+        for (auto& evs : *v)
+            for (cudaEvent_t e : evs) cudaEventDestroy(e);
     for (void* p : ctx->allocs) cudaFree(p);
     for (Param& p : ctx->params)
         if (p.gbf) cudaFree(p.gbf);
@@ -846,8 +900,9 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
     if ((st = ctx_alloc(c, &c->sq_slots, n_specs)) || (st = ctx_alloc(c, &c->sq_step, n_specs)) ||
         (st = ctx_alloc(c, &c->partials, std::max(kSqPartials, kSqGroupMax * kSqChunks))) ||
         (st = ctx_alloc(c, &c->clip_dev, 1)) ||
-        (st = ctx_alloc(c, &c->gnorm_dev, 1)))
+        (st = ctx_alloc(c, &c->gnorm_dev, 1)) || (st = ctx_alloc(c, &c->sq_ticket, 1)))
         return fail(st);
+    if (cudaMemset(c->sq_ticket, 0, sizeof(unsigned int)) != cudaSuccess) return fail(AETH_ERR_CONFIG);
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(AETH_ERR_CONFIG);
     *out = c;
     return AETH_OK;
@@ -968,6 +1023,9 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
         return AETH_OK;
     }
     // B200: the layer's projections in grouped launches (one per rank value).
+    PhaseMarks pm;
+    AETH_TRY(pm.begin(ctx));
+    AETH_TRY(pm.mark(0, st));
     std::vector<ProjJob> jobs;
     std::vector<int> ranks;
     for (int i = 0; i < n; ++i) {
@@ -992,15 +1050,24 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     std::vector<const float*> xs(n);
     std::vector<int64_t> ns(n);
     for (int i = 0; i < n; ++i) { xs[i] = ctx->params[idx[i]].accum; ns[i] = ctx->params[idx[i]].state_elems; }
-    AETH_TRY(sqnorm_group(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, st));
-    if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
-    clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
-    AETH_LAUNCH_CHECK();
+    AETH_TRY(pm.mark(1, st));
+    // Without a hook the norms and the clip coefficient come from one launch.
+    const bool fuse_clip = !sq_hook && n <= kSqGroupMax;
+    AETH_TRY(sqnorm_group(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, ctx->sq_ticket,
+                          ctx->cfg.max_grad_norm, fuse_clip ? clip : nullptr, fuse_clip ? ctx->gnorm_dev : nullptr,
+                          st));
+    if (!fuse_clip) {
+        if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
+        clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
+        AETH_LAUNCH_CHECK();
+    }
+    AETH_TRY(pm.mark(2, st));
     {
         std::vector<Param*> ps(n);
         for (int i = 0; i < n; ++i) ps[i] = &ctx->params[idx[i]];
         AETH_TRY(b2_adam_group(ctx, ps.data(), n, 1.0f, clip, 1, st));
     }
+    AETH_TRY(pm.mark(3, st));
     for (int r : ranks) {
         std::vector<ApplyJob> grp;
         for (int i = 0; i < n; ++i) {
@@ -1013,7 +1080,39 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
         }
         if (!grp.empty()) AETH_TRY(apply_grouped_launch(grp.data(), (int)grp.size(), r, st));
     }
+    AETH_TRY(pm.mark(4, st));
+    pm.commit();
     return AETH_OK;
+}
+
+int aeth_galore_set_phase_timing(aeth_galore_ctx* ctx, int enable) {
+    if (!ctx) return set_err(AETH_ERR_ARG);
+    ctx->phase_timing = enable != 0;
+    return AETH_OK;
+}
+
+int aeth_galore_phase_times(aeth_galore_ctx* ctx, double ms_out[4], int* steps) {
+    if (!ctx || !ms_out) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    for (int k = 0; k < 4; ++k) ms_out[k] = 0.0;
+    int done = 0;
+    int status = AETH_OK;
+    for (auto& ev : ctx->phase_pending) {
+        if (status == AETH_OK) {
+            cudaError_t e = cudaEventSynchronize(ev[4]);
+            for (int k = 0; k < 4 && e == cudaSuccess; ++k) {
+                float ms = 0.0f;
+                e = cudaEventElapsedTime(&ms, ev[k], ev[k + 1]);
+                ms_out[k] += ms;
+            }
+            if (e != cudaSuccess) status = set_err((int)e);
+            else ++done;
+        }
+        ctx->phase_pool.push_back(ev);
+    }
+    ctx->phase_pending.clear();
+    if (steps) *steps = done;
+    return status;
 }
 
 int aeth_galore_set_projector(aeth_galore_ctx* ctx, int idx, const float* P, const float* Q, aeth_stream_t stream) {

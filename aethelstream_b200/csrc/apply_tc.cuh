@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
         const int row = q * 32 + lane;
         const bool qleader = ew < 4 && lane == 0;  // one thread per row group issues its stores
         const uint32_t tcol0 = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cl;
-        const uint32_t lut_s = smem_u32(tab->byte_lut);
+        const uint32_t lut_s = nf4_byte_rep_base(tab, lane);
         const uint32_t bucket_bias = nf4_bucket_bias(tab);
         int j = 0;
         int pending = -1;  // slot of this row group's previous store, released one unit later
@@ -203,7 +203,8 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
             tc_fence_after();
             uint8_t* wp = wslot + wb * L::kWSlot;
             if (n0 + cl < pr.n) {  // warp-uniform
-                const float lr = pr.lr;
+                const float2 nlr2 = make_float2(-pr.lr, -pr.lr);
+                const float2 dmul2 = make_float2(pr.decay_mul, pr.decay_mul);
                 const int ck = cl / 32;  // first 16-byte chunk of this block's 32 packed bytes
                 uint8_t* rowp = wp + row * 128;
                 float* sp = reinterpret_cast<float*>(wp + L::kWPacked) + row * 4 + blk;
@@ -224,29 +225,25 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     nf4_dequant_word_s(qq.x, amax_old, lut_s, w);
                     nf4_dequant_word_s(qq.y, amax_old, lut_s, w + 8);
                     tmem_wait_ld();
-                    if (pr.has_decay) {
-                        const float dmul = pr.decay_mul;
+                    // Products paired: v <- fl(v * -lr) = -fl(lr * dW) (round-to-nearest is
+                    // sign-symmetric); sums scalar: w <- fl(w + v) = fl(w - fl(lr * dW)); decay.
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float dl = __fmul_rn(v[i], lr);
-                            w[i] = __fmul_rn(__fsub_rn(w[i], dl), dmul);
-                            v[i] = dl;
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float dl = __fmul_rn(v[i], lr);
-                            w[i] = __fsub_rn(w[i], dl);
-                            v[i] = dl;
-                        }
+                    for (int i = 0; i < 16; i += 2) {
+                        const float2 dl = mul2_rn(make_float2(v[i], v[i + 1]), nlr2);
+                        float2 ww = add2_sep(make_float2(w[i], w[i + 1]), dl);
+                        if (pr.has_decay) ww = mul2_rn(ww, dmul2);
+                        w[i] = ww.x;
+                        w[i + 1] = ww.y;
+                        v[i] = dl.x;
+                        v[i + 1] = dl.y;
+                        amax = fmax3(amax, fabsf(ww.x), fabsf(ww.y));
                     }
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(w[i]));
                     tmem_st16(tcol + (uint32_t)(c * 16), w);
                     if (dout) {
 #pragma unroll
                         for (int i = 0; i < 16; i += 4)
-                            *reinterpret_cast<float4*>(dout + c * 16 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                            *reinterpret_cast<float4*>(dout + c * 16 + i) =
+                                make_float4(-v[i], -v[i + 1], -v[i + 2], -v[i + 3]);
                     }
                     if (pout) {
 #pragma unroll

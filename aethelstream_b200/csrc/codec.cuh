@@ -20,6 +20,68 @@ __constant__ float c_dmap_unsigned[256];
 // Same construction as the oracle's b2_dynamic_map (see aeth_dynamic_map).
 int build_dynamic_map(int is_signed, float out[256]);
 
+// ---------------------------------------------------------------------------
+// Bucket tables for a fast dynamic-map encode that always returns what the
+// binary search (dmap_encode) returns.
+//
+// The encode is a step function of the magnitude a = |xn|: the code changes
+// only at the decision points between neighbouring map entries, each within a
+// couple of ulp of the real midpoint of the two entries.  A magnitude selects
+// bucket b = (bits(a) >> 17) - (103 << 6): 64 buckets per octave over
+// [2^-24, 2), bucket 0 also taking everything below 2^-24.  An entry packs
+// the bucket's single decision threshold t (float bits, low 8 bits cleared) and
+// the code below it (low 8 bits): code = low + [bits(a) >= t].  A bucket with
+// no threshold stores t = bits(3.4e38).  Magnitudes within kDmapGuard ulp of t,
+// buckets with two thresholds (entry 0), a >= 2, infinities and NaN take the
+// binary search.  Midpoints up to kDmapGuard ulp outside a bucket count as
+// inside it, so a decision point never hides next to a bucket edge.
+//
+// Table 0 covers the signed map's non-negative half (indices 127..255); the
+// map is symmetric about index 127 except for the extra entry 1.0 at 255, so a
+// negative xn encodes as 254 - code(|xn|) (0 for codes 254 and 255).  Table 1
+// covers the unsigned map, whose entry 0 is 0.0 and nearest to every negative
+// xn.  Exact ties (xn on a real midpoint) always lie in the guard band, where
+// the binary search applies its own tie rule.
+// ---------------------------------------------------------------------------
+constexpr int kDmapLutExpLo = 103;                     // 2^-24
+constexpr int kDmapLutN = (128 - kDmapLutExpLo) << 6;  // 1600 buckets
+constexpr uint32_t kDmapGuard = 1024;                  // ulp
+constexpr uint32_t kDmapNoThreshold = 0x7f7fff00u;
+__device__ uint32_t g_dmap_lut[2][kDmapLutN];
+
+inline void build_dmap_lut(const float map[256], int is_signed, uint32_t* out) {
+    std::vector<std::pair<double, int>> M;  // entries ascending by magnitude, with their codes
+    for (int i = is_signed ? 127 : 0; i < 256; ++i) M.push_back({(double)map[i], i});
+    for (int b = 0; b < kDmapLutN; ++b) {
+        const uint32_t lo_bits = (uint32_t)(b + (kDmapLutExpLo << 6)) << 17;
+        const uint32_t hi_bits = lo_bits + (1u << 17);
+        float lof, hif, ulp;
+        memcpy(&lof, &lo_bits, 4);
+        memcpy(&hif, &hi_bits, 4);
+        const uint32_t ulp_bits = lo_bits & 0x7f800000u;  // 2^E; one ulp is 2^(E-23)
+        memcpy(&ulp, &ulp_bits, 4);
+        const double u = (double)ulp * 0x1p-23;
+        const double lo = b == 0 ? 0.0 : (double)lof - kDmapGuard * u, hi = (double)hif + kDmapGuard * u;
+        int nmid = 0, kmid = -1;
+        for (size_t k = 0; k + 1 < M.size(); ++k) {
+            const double mid = 0.5 * (M[k].first + M[k + 1].first);
+            if (mid >= lo && mid < hi) { ++nmid; kmid = (int)k; }
+        }
+        if (nmid == 0) {
+            size_t k = 0;  // the nearest entry is the same over the whole bucket
+            while (k + 1 < M.size() && 0.5 * (M[k].first + M[k + 1].first) < lo) ++k;
+            out[b] = kDmapNoThreshold | (uint32_t)M[k].second;
+        } else if (nmid == 1) {
+            const float thr = (float)(0.5 * (M[kmid].first + M[kmid + 1].first));
+            uint32_t tb;
+            memcpy(&tb, &thr, 4);
+            out[b] = (tb & ~0xffu) | (uint32_t)M[kmid].second;
+        } else {
+            out[b] = 0u;
+        }
+    }
+}
+
 inline bool g_maps_uploaded[kMaxDevices] = {};
 
 inline int codec_maps_ensure() {
@@ -32,6 +94,10 @@ inline int codec_maps_ensure() {
         build_dynamic_map(0, u);
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_signed, s, sizeof(s)));
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_unsigned, u, sizeof(u)));
+        static uint32_t lut[2][kDmapLutN];
+        build_dmap_lut(s, 1, lut[0]);
+        build_dmap_lut(u, 0, lut[1]);
+        AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut, lut, sizeof(lut)));
         g_maps_uploaded[dev] = true;
     }
     return AETH_OK;
@@ -62,6 +128,44 @@ __device__ __forceinline__ uint32_t dmap_encode(const float* __restrict__ map, f
     float dl = fabsf(__fsub_rn(xn, map[lo - 1]));
     float dh = fabsf(__fsub_rn(xn, map[lo]));
     return dh < dl ? (uint32_t)lo : (uint32_t)(lo - 1);
+}
+
+// Bucket-table encode (tables built by build_dmap_lut); `lut` is table 0 for
+// the signed map and table 1 for the unsigned one, `map` the sorted map for
+// the rare binary-search cases.  Returns dmap_encode(map, xn) for every xn.
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t dmap_encode_lut(const uint32_t* __restrict__ lut, const float* __restrict__ map,
+                                                    float xn) {
+    const uint32_t ab = __float_as_uint(xn) & 0x7fffffffu;
+    const int b = max((int)(ab >> 17) - (kDmapLutExpLo << 6), 0);
+    const bool in = b < kDmapLutN;
+    const uint32_t e = lut[in ? b : 0];
+    const uint32_t t = e & ~0xffu;
+    uint32_t code = (e & 0xffu) + (ab >= t ? 1u : 0u);
+    // signed: mirror image; unsigned: every negative value is nearest to entry 0 (= 0)
+    if (xn < 0.0f) code = SIGNED ? (code >= 254u ? 0u : 254u - code) : 0u;
+    if (!in || e == 0u || ab - t + kDmapGuard < 2u * kDmapGuard) code = dmap_encode(map, xn);
+    return code;
+}
+
+// Every float bit pattern through dmap_encode_lut and dmap_encode; counts
+// disagreements (a self-check of the bucket tables, run by the test suite).
+__global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restrict__ mismatches) {
+    __shared__ float map[256];
+    __shared__ uint32_t lut[kDmapLutN];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) map[i] = is_signed ? c_dmap_signed[i] : c_dmap_unsigned[i];
+    for (int i = threadIdx.x; i < kDmapLutN; i += blockDim.x) lut[i] = g_dmap_lut[is_signed ? 0 : 1][i];
+    __syncthreads();
+    unsigned long long bad = 0;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < (1ull << 32); i += stride) {
+        const float x = __uint_as_float((uint32_t)i);
+        const uint32_t want = dmap_encode(map, x);
+        const uint32_t got = is_signed ? dmap_encode_lut<true>(lut, map, x) : dmap_encode_lut<false>(lut, map, x);
+        bad += got != want;
+    }
+    bad = warp_sum_u64(bad);
+    if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
 // Dynamic codec normalisation: xn = x * (1 / absmax), one reciprocal per block.

@@ -85,65 +85,116 @@ inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t 
 }
 
 // ---------------------------------------------------------------------------
-// Squared norms of several accumulators, deterministic (fixed partial slots,
-// ordered final sums): grid (kSqChunks, n), then one CTA.
+// Squared norms of several accumulators in one launch, deterministic: CTA
+// (c, p) writes the f64 partial sum of chunk c of accumulator p into a fixed
+// slot; the CTA that takes the last ticket sums each accumulator's slots in
+// chunk order into out[p] and, when asked, also computes the global clip
+// coefficient of clip_coeff_kernel (hook.rs:184-187) from out[0..np), then
+// resets the ticket for the next launch.
 // ---------------------------------------------------------------------------
 constexpr int kSqGroupMax = 16;
-constexpr int kSqChunks = 32;
+constexpr int kSqChunks = 128;
 
 struct SqGroupArgs {
     const float* x[kSqGroupMax];
     int64_t n[kSqGroupMax];
+    int np;
+    float max_norm;
+    float* clip_out;       // null: norms only
+    double* gnorm_out;     // optional, with clip_out
+    double* out;           // np sums
+    double* partials;      // kSqGroupMax * kSqChunks
+    unsigned int* ticket;  // zero between launches
 };
 
-__global__ void __launch_bounds__(256) sqnorm_group_partial_kernel(SqGroupArgs a, double* __restrict__ partials) {
+__global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant__ SqGroupArgs a) {
     __shared__ double red[8];
+    __shared__ unsigned int taken;
     const int p = blockIdx.y;
-    const float* x = a.x[p];
-    const int64_t n = a.n[p];
-    double s = 0.0;
-    const int64_t n4 = n / 4;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-        float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-        s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x[p]);
+    const int64_t n = a.n[p], n4 = n / 4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    double s[4] = {0.0, 0.0, 0.0, 0.0};
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n4; i += 4 * stride) {  // four independent 16-byte loads in flight
+        float4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = __ldcg(x4 + i + k * stride);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            s[k] += (double)u[k].x * u[k].x + (double)u[k].y * u[k].y + (double)u[k].z * u[k].z +
+                    (double)u[k].w * u[k].w;
     }
-    for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        double v = (double)x[i];
-        s += v * v;
+    for (; i < n4; i += stride) {
+        const float4 u = __ldcg(x4 + i);
+        s[0] += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
     }
-    s = warp_sum_d(s);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    for (int64_t k = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += stride) {
+        const double v = (double)a.x[p][k];
+        s[0] += v * v;
+    }
+    const double sum = warp_sum_d((s[0] + s[1]) + (s[2] + s[3]));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
     __syncthreads();
     if (threadIdx.x == 0) {
         double t = 0.0;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-        partials[p * kSqChunks + blockIdx.x] = t;
+        a.partials[p * kSqChunks + blockIdx.x] = t;
+        __threadfence();
+        taken = atomicAdd(a.ticket, 1u);
     }
-}
-
-__global__ void sqnorm_group_final_kernel(const double* __restrict__ partials, int np, double* __restrict__ out) {
-    const int p = threadIdx.x;
-    if (p < np) {
+    __syncthreads();
+    if (taken != gridDim.x * gridDim.y - 1) return;
+    __threadfence();
+    // Last CTA: warp w reduces accumulators w, w + 8, ... in a fixed order
+    // (lane L: chunks L, L + 32, ...; then a fixed shuffle tree).
+    const int lane = threadIdx.x & 31;
+    for (int q = threadIdx.x >> 5; q < a.np; q += (int)(blockDim.x >> 5)) {
         double t = 0.0;
-        for (int c = 0; c < kSqChunks; ++c) t += partials[p * kSqChunks + c];
-        out[p] = t;
+        for (int c = lane; c < (int)gridDim.x; c += 32) t += __ldcg(a.partials + q * kSqChunks + c);
+        t = warp_sum_d(t);
+        if (lane == 0) a.out[q] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (a.clip_out) {
+            double t = 0.0;
+            for (int k = 0; k < a.np; ++k) t += a.out[k];
+            const double gnorm = sqrt(t);
+            const float c = (float)((double)a.max_norm / (gnorm + 1e-6));
+            *a.clip_out = c < 1.0f ? c : 1.0f;
+            if (a.gnorm_out) *a.gnorm_out = gnorm;
+        }
+        *a.ticket = 0u;
     }
 }
 
-// out[i] = sum of squares of xs[i] (f64); `partials` holds kSqGroupMax * kSqChunks doubles.
+// out[i] = sum of squares of xs[i] (f64).  With clip_out (np <= kSqGroupMax)
+// the same launch also writes the global clip coefficient for max_norm.
 inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, double* out, double* partials,
-                        cudaStream_t st) {
+                        unsigned int* ticket, float max_norm, float* clip_out, double* gnorm_out, cudaStream_t st) {
+    if (clip_out && np > kSqGroupMax) return AETH_ERR_UNSUPPORTED;
     for (int off = 0; off < np; off += kSqGroupMax) {
         const int cnt = std::min(kSqGroupMax, np - off);
         SqGroupArgs a;
         memset(&a, 0, sizeof(a));
+        int64_t largest = 0;
         for (int i = 0; i < cnt; ++i) {
             a.x[i] = xs[off + i];
             a.n[i] = ns[off + i];
+            largest = std::max(largest, a.n[i]);
             if ((reinterpret_cast<uintptr_t>(a.x[i]) & 15) != 0) return AETH_ERR_UNSUPPORTED;
         }
-        sqnorm_group_partial_kernel<<<dim3(kSqChunks, cnt), 256, 0, st>>>(a, partials);
-        sqnorm_group_final_kernel<<<1, 32, 0, st>>>(partials, cnt, out + off);
+        a.np = cnt;
+        a.max_norm = max_norm;
+        a.clip_out = clip_out;
+        a.gnorm_out = gnorm_out;
+        a.out = out + off;
+        a.partials = partials;
+        a.ticket = ticket;
+        // about 8K elements per CTA, at most kSqChunks chunks per accumulator
+        const int chunks = (int)std::min<int64_t>(kSqChunks, std::max<int64_t>(1, (largest + 8191) / 8192));
+        sqnorm_group_kernel<<<dim3(chunks, cnt), 256, 0, st>>>(a);
         AETH_LAUNCH_CHECK();
     }
     return AETH_OK;
@@ -171,8 +222,11 @@ inline bool apply_grouped_supported(int m, int n, int r) {
 }
 
 inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
-    constexpr int STAGES = 3;
+    // Two operand stages suffice: a unit's MMAs (K = r <= 256) take a fraction
+    // of its epilogue, and the freed 48 KB hold the replicated byte table.
+    constexpr int STAGES = 2;
     using L = ApplyLayout<STAGES>;
+    static_assert(1024 + L::kTotal <= 227 * 1024, "apply kernel shared memory above the per-CTA limit");
     DeviceRuntime* rt = nullptr;
     AETH_TRY(runtime_for_current(&rt));
     for (int off = 0; off < nj; off += kApplyMaxProblems) {

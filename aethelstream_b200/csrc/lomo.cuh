@@ -51,10 +51,13 @@ __global__ void __launch_bounds__(256) lomo_update_kernel(const uint16_t* __rest
                                                           float* __restrict__ wa, float* __restrict__ prequant) {
     __shared__ Nf4Tables tab;
     __shared__ float dm[256];
+    __shared__ uint32_t dlut[kDmapLutN];
     __shared__ float red[8];
     nf4_tables_init(&tab, threadIdx.x, blockDim.x);
-    if (codec == AETH_CODEC_BLOCK_DYNAMIC)
+    if (codec == AETH_CODEC_BLOCK_DYNAMIC) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) dm[i] = c_dmap_signed[i];
+        for (int i = threadIdx.x; i < kDmapLutN; i += blockDim.x) dlut[i] = g_dmap_lut[0][i];
+    }
     __syncthreads();
     double gnorm = sqrt(*sq);
     float clip = (float)((double)max_norm / (gnorm + 1e-6));
@@ -109,10 +112,10 @@ __global__ void __launch_bounds__(256) lomo_update_kernel(const uint16_t* __rest
             for (int k = 0; k < 8; ++k) out[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(mo[k], inv)) << (8 * (k & 3));
             if (threadIdx.x == 0) mom_scales[b] = nsm;
         } else {
-#pragma unroll
             const float inv = dyn_inv(bm);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) out[k >> 2] |= dmap_encode(dm, dyn_xn(mo[k], inv)) << (8 * (k & 3));
+            for (int k = 0; k < 8; ++k)
+                out[k >> 2] |= dmap_encode_lut<true>(dlut, dm, dyn_xn(mo[k], inv)) << (8 * (k & 3));
             if (threadIdx.x == 0) mom_scales[b] = bm;
         }
         *reinterpret_cast<uint2*>(mom8 + e0) = make_uint2(out[0], out[1]);

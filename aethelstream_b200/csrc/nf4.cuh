@@ -110,23 +110,26 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 }
 
 // ---------------------------------------------------------------------------
-// Compact tables for the fused epilogues: every lookup is a conflict-free
-// 32-bit LDS.  code16[c] = CODES[c].  bucket32[b] = the midpoint threshold of
-// bucket b (or 2.0 when the bucket holds none) with (lower code + 1) stored in
-// its low 4 mantissa bits; the perturbation (< 16 ulp, < 1e-6 absolute) is
-// covered by the wider near-window kNf4NearWindow32.
+// Tables for the fused epilogues.  byte_rep: the 256-entry byte table
+// (CODES[byte >> 4], CODES[byte & 15]) in 16 copies, entry b of copy c at
+// float2 index 16 b + c, so the 16 lanes of a half-warp (copy = lane % 16)
+// read 16 different bank pairs whatever their bytes: one 8-byte lookup costs
+// the minimum two wavefronts per warp.  bucket32[b] = the NEGATED midpoint
+// threshold of bucket b (-2.0 when the bucket holds none) with (lower code + 1)
+// stored in its low 4 mantissa bits, so the signed distance to the threshold
+// is one addition, xn + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
+// is covered by the wider near-window kNf4NearWindow32.
 // ---------------------------------------------------------------------------
 constexpr float kNf4NearWindow32 = 2.5e-6f;
 
 struct Nf4Tables32 {
-    float2 byte_lut[256];  // (CODES[byte >> 4], CODES[byte & 15])
-    float code16[16];
+    float2 byte_rep[256 * 16];
     uint32_t bucket32[33];
 };
 
 __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
-    for (int i = tid; i < 256; i += nthreads) t->byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
-    for (int i = tid; i < 16; i += nthreads) t->code16[i] = c_nf4_codes[i];
+    for (int i = tid; i < 256 * 16; i += nthreads)
+        t->byte_rep[i] = make_float2(c_nf4_codes[i >> 8], c_nf4_codes[(i >> 4) & 15]);
     for (int b = tid; b < 33; b += nthreads) {
         float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
         int below = 0, code = -1;
@@ -137,8 +140,20 @@ __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int n
             else if (mid < hi) { thr = mid; code = k; }
         }
         if (code < 0) code = below;
-        t->bucket32[b] = (__float_as_uint(thr) & ~15u) | (uint32_t)(code + 1);
+        t->bucket32[b] = (__float_as_uint(-thr) & ~15u) | (uint32_t)(code + 1);
     }
+}
+
+// Three-input min / max of sm_100 (one instruction each).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
 }
 
 // Exact decisions for 8 elements (rare path; kept out of line).
@@ -151,24 +166,6 @@ __device__ __noinline__ uint32_t nf4_exact_word8(float a0, float a1, float a2, f
     return word;
 }
 
-// Fast classification of 8 values (one packed word) with the compact bucket
-// table; `mind` collects the smallest distance to a decision threshold so the
-// caller can send near-boundary words through nf4_exact_word8.
-__device__ __forceinline__ uint32_t nf4_fast_word8(const float* w, float inv, const uint32_t* __restrict__ bucket,
-                                                   float& mind) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float xn = __fmul_rn(w[j], inv);
-        const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);  // low bits: rint(16 xn) + 16
-        const uint32_t e = bucket[__float_as_uint(t) & 63u];
-        const float d = __fsub_rn(xn, __uint_as_float(e));
-        const uint32_t code = e + (uint32_t)(__float_as_int(d) >> 31);  // (lower + 1) - [d < 0]
-        mind = fminf(mind, fabsf(d));
-        word |= (code & 15u) << (8 * (j >> 1) + ((j & 1) ? 0 : 4));
-    }
-    return word;
-}
 
 // Shared-address variants for the fused apply epilogue.
 // bucket_bias: shared address of bucket32[0] minus (0x4B400000 << 2) modulo
@@ -178,88 +175,49 @@ __device__ __forceinline__ uint32_t nf4_bucket_bias(const Nf4Tables32* t) {
     return smem_u32_addr(t->bucket32) - (0x4B400000u << 2);
 }
 
-// 8 values -> one packed word; nibbles are shifted in from the top in memory
-// order (code[6], code[7], code[4], code[5], code[2], code[3], code[0], code[1]).
+// 8 values -> one packed word, two elements per step through the packed
+// f32x2 instructions.  Byte k of the word = code[2k] << 4 | code[2k+1]; pairs
+// enter from the bottom, (6,7) first.  The signed distance d = xn +
+// (-threshold) gives code = (lower + 1) - [d < 0]; d == 0 lies in the near
+// band.  ptxas may fuse the xn product into the distance add; that moves d by
+// under an ulp of xn, far inside kNf4NearWindow32, whose elements are decided
+// again exactly from the unscaled value.
 __device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t bucket_bias, float& mind) {
-    constexpr int kOrder[8] = {6, 7, 4, 5, 2, 3, 0, 1};
+    const float2 inv2 = make_float2(inv, inv);
+    const float2 k16 = make_float2(16.0f, 16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
     uint32_t word = 0;
 #pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        const float xn = __fmul_rn(w[kOrder[s]], inv);
-        const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);
-        uint32_t e;
-        asm("ld.shared.u32 %0, [%1];" : "=r"(e) : "r"(bucket_bias + (__float_as_uint(t) << 2)));
-        const float d = __fsub_rn(xn, __uint_as_float(e));
-        const uint32_t code = e + (uint32_t)(__float_as_int(d) >> 31);  // (lower + 1) - [d < 0]
-        mind = fminf(mind, fabsf(d));
-        word = (word << 4) | (code & 15u);
+    for (int s = 3; s >= 0; --s) {
+        const float2 xn = mul2_rn(make_float2(w[2 * s], w[2 * s + 1]), inv2);
+        const float2 t = fma2_rn(xn, k16, kbias);  // low bits: rint(16 xn) + 16
+        uint32_t e0, e1;
+        asm("ld.shared.u32 %0, [%1];" : "=r"(e0) : "r"(bucket_bias + (__float_as_uint(t.x) << 2)));
+        asm("ld.shared.u32 %0, [%1];" : "=r"(e1) : "r"(bucket_bias + (__float_as_uint(t.y) << 2)));
+        const float2 d = add2_rn(xn, make_float2(__uint_as_float(e0), __uint_as_float(e1)));
+        const uint32_t c0 = e0 + (uint32_t)(__float_as_int(d.x) >> 31);
+        const uint32_t c1 = e1 + (uint32_t)(__float_as_int(d.y) >> 31);
+        mind = fmin3(mind, fabsf(d.x), fabsf(d.y));
+        word = (word << 8) | ((c0 & 15u) << 4) | (c1 & 15u);
     }
     return word;
 }
 
-// Dequantise one packed word (8 elements) with the 256-entry byte table at
-// shared address lut_s.
-__device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, uint32_t lut_s, float* out8) {
+// Shared address of this lane's copy of the replicated byte table.
+__device__ __forceinline__ uint32_t nf4_byte_rep_base(const Nf4Tables32* t, int lane) {
+    return smem_u32_addr(t->byte_rep) + (uint32_t)(lane & 15) * 8u;
+}
+
+// Dequantise one packed word (8 elements) with this lane's copy of the byte
+// table (rep_s = nf4_byte_rep_base); one packed multiply per byte.
+__device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, uint32_t rep_s, float* out8) {
+    const float2 a2 = make_float2(amax, amax);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         float2 c;
-        asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(c.x), "=f"(c.y) : "r"(lut_s + (__byte_perm(word, 0, 0x4440 + k) << 3)));
-        out8[2 * k] = __fmul_rn(c.x, amax);
-        out8[2 * k + 1] = __fmul_rn(c.y, amax);
-    }
-}
-
-// Quantise N values of one NF4 block (absmax `amax`) held in registers into
-// N/8 packed words, using the compact tables.  Bit-exact with quantizer.py.
-template <int N>
-__device__ __forceinline__ void nf4_quant_regs32(const float (&v)[N], float amax, const uint32_t* __restrict__ bucket,
-                                                 uint32_t (&packed)[N / 8]) {
-    const float safe = fmaxf(amax, 1e-8f);
-    const float inv = __frcp_rn(safe);
-    float mind = 1.0f;
-#pragma unroll
-    for (int w = 0; w < N / 8; ++w) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float xn = __fmul_rn(v[w * 8 + j], inv);
-            const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);  // low bits: rint(16 xn) + 16
-            const uint32_t e = bucket[__float_as_uint(t) & 63u];
-            const float d = __fsub_rn(xn, __uint_as_float(e));
-            // code = (lower code + 1) - [d < 0]; d == 0 lies in the near band
-            const uint32_t code = e + (uint32_t)(__float_as_int(d) >> 31);
-            mind = fminf(mind, fabsf(d));
-            word |= (code & 15u) << (8 * (j >> 1) + ((j & 1) ? 0 : 4));
-        }
-        packed[w] = word;
-    }
-    if (mind < kNf4NearWindow32) {
-        // Rare: some element is next to a decision boundary; redo the words
-        // that hold one with the exact definition.
-#pragma unroll
-        for (int w = 0; w < N / 8; ++w) {
-            float m8 = 1.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float xn = __fmul_rn(v[w * 8 + j], inv);
-                const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);
-                m8 = fminf(m8, fabsf(__fsub_rn(xn, __uint_as_float(bucket[__float_as_uint(t) & 63u]))));
-            }
-            if (m8 < kNf4NearWindow32)
-                packed[w] = nf4_exact_word8(v[w * 8], v[w * 8 + 1], v[w * 8 + 2], v[w * 8 + 3], v[w * 8 + 4],
-                                            v[w * 8 + 5], v[w * 8 + 6], v[w * 8 + 7], safe);
-        }
-    }
-}
-
-// Dequantise 8 codes packed in one little-endian word (byte k = code[2k] << 4
-// | code[2k+1]) into fp32 products with the 16-entry table.
-__device__ __forceinline__ void nf4_dequant_word16(uint32_t word, float amax, const float* __restrict__ code16,
-                                                   float* out8) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        out8[2 * k] = __fmul_rn(code16[(word >> (8 * k + 4)) & 15u], amax);
-        out8[2 * k + 1] = __fmul_rn(code16[(word >> (8 * k)) & 15u], amax);
+        asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(c.x), "=f"(c.y) : "r"(rep_s + (__byte_perm(word, 0, 0x4440 + k) << 7)));
+        const float2 p = mul2_rn(c, a2);
+        out8[2 * k] = p.x;
+        out8[2 * k + 1] = p.y;
     }
 }
 

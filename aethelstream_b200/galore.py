@@ -345,6 +345,19 @@ class GaLoreOptimizer:
                                            C.c_void_p(_stream_handle())), "aeth_galore_step")
         return clip
 
+    # ---- per-phase device timing of step_layer ----
+    PHASES = ("projection", "sqnorm_clip", "adam", "apply")
+
+    def set_phase_timing(self, enable: bool) -> None:
+        L.check(self._lib.aeth_galore_set_phase_timing(self._ctx, 1 if enable else 0), "set_phase_timing")
+
+    def phase_times(self):
+        """(steps, {phase: total device ms}) over the step_layer calls since the last call."""
+        out = (C.c_double * 4)()
+        steps = C.c_int(0)
+        L.check(self._lib.aeth_galore_phase_times(self._ctx, out, C.byref(steps)), "phase_times")
+        return steps.value, dict(zip(self.PHASES, list(out)))
+
 
 def _wrap_device_doubles(ptr: int, count: int, device: int) -> torch.Tensor:
     """A torch view of `count` device doubles owned by the library (no copy)."""

@@ -70,6 +70,33 @@ def algorithmic(shapes=None, r=RANK):
     return {"proj_bytes": bp, "apply_bytes": ba, "proj_flops": fp, "apply_flops": fa}
 
 
+KERNEL_NAMES = {
+    "projection": "proj_grouped_kernel (tcgen05 one-sided projection, TMA reduce-add into R)",
+    "sqnorm_clip": "sqnorm_group_kernel (f64 squared norms + global clip)",
+    "adam": "b2_adam_group_kernel (INT8 dynamic-map Adam, N in bf16)",
+    "apply": "apply_grouped_kernel (tcgen05 back-projection + fused NF4 dequant/update/requant)",
+}
+
+
+def kernel_bytes(shapes=None, r=RANK):
+    """Compulsory HBM bytes per launch of each step kernel (one launch each per step).
+
+    projection: read G bf16 (2 B/elem) + projector (2 s r), write R f32 (4 r l).
+    sqnorm_clip: read R (4 r l).
+    adam: read R + zero R (8 r l), m/v codes read + write (4 r l), N bf16 write (2 r l),
+          block scales read + write (16 r l / 2048).
+    apply: NF4 weight read + write (2 x 0.5625 B/elem), N bf16 read (2 r l), projector (2 s r).
+    """
+    out = dict.fromkeys(("projection", "sqnorm_clip", "adam", "apply"), 0.0)
+    for _, m, n in (shapes or SHAPES):
+        s, l = min(m, n), max(m, n)
+        out["projection"] += 2 * m * n + 2 * s * r + 4 * r * l
+        out["sqnorm_clip"] += 4 * r * l
+        out["adam"] += 14 * r * l + 16 * r * l / STATE_BLOCK
+        out["apply"] += 2 * 0.5625 * m * n + 2 * r * l + 2 * s * r
+    return out
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -230,15 +257,9 @@ def run_b200(args):
         ring.append(gs)
     keys = [(layer, name) for name, _, _ in SHAPES]
     stream = torch.cuda.current_stream()
-    phase_events = []
-    allreduce = allreduce_sqnorm_hook() if world > 1 else None
-
-    def hook(sq):
-        if allreduce is not None:
-            allreduce(sq)
-        ev = torch.cuda.Event(enable_timing=True)
-        ev.record(stream)
-        phase_events.append(ev)
+    # One GPU: no hook, so the squared norms and the clip come from one launch.
+    # Several GPUs: the hook all-reduces the per-matrix squared norms (8 B each).
+    hook = allreduce_sqnorm_hook() if world > 1 else None
 
     def step(s):
         return opt.step_layer(keys, ring[s % 2], weights, sq_hook=hook)
@@ -246,37 +267,32 @@ def run_b200(args):
     for s in range(args.warmup):
         step(s)
     torch.cuda.synchronize()
-    phase_events.clear()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)  # let the sampler start
-    starts, ends = [], []
+    opt.set_phase_timing(True)  # CUDA events at the phase boundaries, on this stream
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for s in range(args.steps):
-        e = torch.cuda.Event(enable_timing=True)
-        e.record(stream)
-        starts.append(e)
         step(s)
-        e2 = torch.cuda.Event(enable_timing=True)
-        e2.record(stream)
-        ends.append(e2)
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
+    opt.set_phase_timing(False)
+    n_timed, phase_ms = opt.phase_times()
+    assert n_timed == args.steps, (n_timed, args.steps)
     if world > 1:
         dist.barrier()
     ms = t0.elapsed_time(t1)
-    proj_ms = sum(a.elapsed_time(b) for a, b in zip(starts, phase_events))
-    apply_ms = sum(a.elapsed_time(b) for a, b in zip(phase_events, ends))
-    t = torch.tensor([ms, proj_ms, apply_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms] + [phase_ms[k] for k in opt.PHASES], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, proj_ms, apply_ms = t.tolist()
+    ms = t[0].item()
+    phase_ms = dict(zip(opt.PHASES, t[1:].tolist()))
     params_per_step = sum(m * n for _, m, n in SHAPES)
     value = params_per_step * world * args.steps / (ms / 1000.0)
 
@@ -314,13 +330,12 @@ def run_b200(args):
     if rank == 0:
         hbm, tflops, tflops_sus, peak_kind = load_peaks()
         alg = algorithmic()
-        per_proj = alg["proj_bytes"] / (proj_ms / args.steps / 1000.0) / 1e9
-        per_apply = alg["apply_bytes"] / (apply_ms / args.steps / 1000.0) / 1e9
+        kb = kernel_bytes()
+        per_ms = {k: v / args.steps for k, v in phase_ms.items()}
+        gbs = {k: kb[k] / (per_ms[k] / 1000.0) / 1e9 for k in opt.PHASES}
         traffic = load_traffic()
-        if apply_ms >= proj_ms:
-            dom, achieved, tkey = "apply (Adam + tcgen05 back-projection + NF4 write)", per_apply, "apply_bytes_per_step"
-        else:
-            dom, achieved, tkey = "projection (tcgen05 P^T G / G Q)", per_proj, "proj_bytes_per_step"
+        dom = max(opt.PHASES, key=lambda k: per_ms[k])
+        achieved = gbs[dom]
         step_s = ms / args.steps / 1000.0
         total_bytes = alg["proj_bytes"] + alg["apply_bytes"]
         total_flops = alg["proj_flops"] + alg["apply_flops"]
@@ -334,16 +349,19 @@ def run_b200(args):
                        "l2": (f"inputs larger than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients per "
                               "step, 2-deep ring)") if 2 * params_per_step > 126e6 else
                              f"inputs smaller than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients)"},
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": traffic.get(tkey), "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dom], "achieved": achieved, "peak": hbm,
+                         "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": traffic.get(f"{dom}_bytes_per_launch"),
+                         "algorithmic_bytes_per_launch": kb[dom], "launch_ms": per_ms[dom],
+                         "peak_kind": peak_kind},
             "roofline_step": {"algorithmic_bytes": total_bytes, "algorithmic_flops": total_flops,
                               "ideal_ms": ideal_s * 1000.0, "measured_ms": step_s * 1000.0,
-                              "frac": ideal_s / step_s, "proj_ms": proj_ms / args.steps,
-                              "apply_ms": apply_ms / args.steps, "proj_gbs": per_proj, "apply_gbs": per_apply},
+                              "frac": ideal_s / step_s,
+                              "phase_ms": per_ms, "phase_gbs": gbs, "phase_bytes": kb},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                     "steps": k_e2e},
-            # per step: grouped projection, 2 sqnorm, clip, one Adam per matrix, grouped apply
-            "gpu_launches": (5 + len(SHAPES)) * args.steps,
+            # per step: grouped projection, sqnorm (+ clip with the multi-GPU hook), grouped Adam, grouped apply
+            "gpu_launches": (4 if world == 1 else 5) * args.steps,
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -220,6 +220,15 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
                      const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out,
                      aeth_stream_t stream);
 
+/* Per-phase device timing of aeth_galore_step (no reference counterpart).
+ * While enabled, every B200-mode step records CUDA events on its stream at
+ * the phase boundaries: projection | squared norms and clip | Adam |
+ * back-projection with the weight write.  aeth_galore_phase_times waits for
+ * the recorded steps, adds their elapsed milliseconds per phase into
+ * ms_out[0..3], stores the number of steps in *steps and forgets them. */
+int aeth_galore_set_phase_timing(aeth_galore_ctx* ctx, int enable);
+int aeth_galore_phase_times(aeth_galore_ctx* ctx, double ms_out[4], int* steps);
+
 /* Projector access.  REF: P (m x r) and Q (n x r).  B200: only the projector
  * of the chosen side (P for m < n, Q for m >= n; the other pointer is ignored).
  * fp32 device buffers.  set_projector resets the Adam state, as the subspace
@@ -256,6 +265,16 @@ int aeth_int8_dequantize(const int8_t* q, const float* scales, int64_t n, int co
                          float* out, aeth_stream_t stream);
 /* The 256-entry dynamic map used by AETH_CODEC_BLOCK_DYNAMIC (host copy). */
 int aeth_dynamic_map(int is_signed, float out[256]);
+/* Self-checks with no reference counterpart.  Each runs every one of the 2^32
+ * float bit patterns through a fast device path and the plain definition it
+ * replaces, on the current device, and stores the number of disagreements in
+ * *mismatches (synchronous):
+ *   DMAP_SIGNED / DMAP_UNSIGNED: the bucket-table dynamic-map encoder of the
+ *     Adam and LOMO kernels against the binary search over the map;
+ *   ADAM_DIR: the bf16 Adam direction from approximate sqrt and reciprocal
+ *     against IEEE sqrt and division (the pattern is v; m is hashed from it). */
+enum { AETH_SELFCHECK_DMAP_SIGNED = 0, AETH_SELFCHECK_DMAP_UNSIGNED = 1, AETH_SELFCHECK_ADAM_DIR = 2 };
+int aeth_selfcheck(int which, unsigned long long* mismatches);
 
 /* LOMO fused full-rank update over a flat NF4 tensor (Lv et al. 2023):
  * aeth_lomo_sqnorm adds sum(g^2) (f64) into *sq_dev; aeth_lomo_update reads

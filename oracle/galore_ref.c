@@ -308,6 +308,138 @@ int ref_should_switch(uint64_t step, uint64_t interval) {
     return interval > 0 && step > 0 && (step % interval) == 0;
 }
 
+/* ---------------------------------------------------------------------------
+ * Randomized SVD subspace refresh (galore/src/randomized_svd.rs:38-271).
+ * ------------------------------------------------------------------------- */
+
+/* Rng (randomized_svd.rs:38-66): xorshift64 from max(seed, 1); a uniform is
+ * (x >> 40) / 2^24; a Gaussian is Box-Muller over two uniforms with the
+ * first clamped to 1e-7. */
+static uint64_t rsvd_next_u64(uint64_t* s) {
+    uint64_t x = *s;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *s = x;
+    return x;
+}
+static float rsvd_next_f32(uint64_t* s) { return (float)(rsvd_next_u64(s) >> 40) / (float)(1u << 24); }
+float ref_rsvd_gaussian(uint64_t* state) {
+    float u1 = fmaxf(rsvd_next_f32(state), 1e-7f);
+    float u2 = rsvd_next_f32(state);
+    const float two_pi = 2.0f * 3.14159265358979323846f;
+    return sqrtf(-2.0f * logf(u1)) * cosf(two_pi * u2);
+}
+
+void ref_rsvd_omega(uint64_t seed, int64_t count, float* out) {
+    uint64_t s = seed > 1 ? seed : 1;
+    for (int64_t i = 0; i < count; ++i) out[i] = ref_rsvd_gaussian(&s);
+}
+
+/* qr_columns (randomized_svd.rs:160-185): modified Gram-Schmidt on the
+ * columns of a row-major m x k matrix; -1 on a column norm below 1e-12. */
+static int rsvd_mgs(float* q, int m, int k, int fail_on_small) {
+    for (int j = 0; j < k; ++j) {
+        for (int i = 0; i < j; ++i) {
+            float dot = 0.0f;
+            for (int row = 0; row < m; ++row) dot += q[(int64_t)row * k + i] * q[(int64_t)row * k + j];
+            for (int row = 0; row < m; ++row) q[(int64_t)row * k + j] -= dot * q[(int64_t)row * k + i];
+        }
+        float norm = 0.0f;
+        for (int row = 0; row < m; ++row) norm += q[(int64_t)row * k + j] * q[(int64_t)row * k + j];
+        if (fail_on_small) {
+            norm = sqrtf(norm);
+            if (norm < 1e-12f) return -1;
+        } else {
+            /* orthonormalize_columns (randomized_svd.rs:187-207) */
+            norm = sqrtf(fmaxf(norm, 1e-12f));
+        }
+        for (int row = 0; row < m; ++row) q[(int64_t)row * k + j] /= norm;
+    }
+    return 0;
+}
+
+/* jacobi_eigenvectors (randomized_svd.rs:210-271): at most 50 single
+ * rotations, each on the largest off-diagonal |a_pq| (first in row-major
+ * order), stopping below 1e-10.  The rotation loop runs in place over k, so
+ * for k = p and k = q it reads values written earlier in the same loop. */
+void ref_rsvd_jacobi(float* mat, int n, float* u) {
+    for (int i = 0; i < n * n; ++i) u[i] = 0.0f;
+    for (int i = 0; i < n; ++i) u[i * n + i] = 1.0f;
+    for (int it = 0; it < 50; ++it) {
+        float max_off = 0.0f;
+        int p = 0, q = 1;
+        for (int i = 0; i < n; ++i)
+            for (int j = i + 1; j < n; ++j) {
+                float v = fabsf(mat[i * n + j]);
+                if (v > max_off) { max_off = v; p = i; q = j; }
+            }
+        if (max_off < 1e-10f) break;
+        float app = mat[p * n + p], aqq = mat[q * n + q], apq = mat[p * n + q];
+        float tau = (aqq - app) / (2.0f * apq);
+        float t = tau >= 0.0f ? 1.0f / (tau + sqrtf(1.0f + tau * tau)) : -1.0f / (-tau + sqrtf(1.0f + tau * tau));
+        float c = 1.0f / sqrtf(1.0f + t * t);
+        float s = t * c;
+        for (int k = 0; k < n; ++k) {
+            float mkp = mat[k * n + p], mkq = mat[k * n + q];
+            mat[k * n + p] = c * mkp - s * mkq;
+            mat[p * n + k] = mat[k * n + p];
+            mat[k * n + q] = s * mkp + c * mkq;
+            mat[q * n + k] = mat[k * n + q];
+        }
+        mat[p * n + q] = 0.0f;
+        mat[q * n + p] = 0.0f;
+        for (int k = 0; k < n; ++k) {
+            float ukp = u[k * n + p], ukq = u[k * n + q];
+            u[k * n + p] = c * ukp - s * ukq;
+            u[k * n + q] = s * ukp + c * ukq;
+        }
+    }
+}
+
+/* randomized_svd_projections (randomized_svd.rs:76-149).  Returns 0, -2 for
+ * an invalid rank / oversampling (GaLoreError::Config) or -3 for a rank
+ * deficient sketch (GaLoreError::Linalg).  p_out: m x r, q_out: n x r. */
+int ref_randomized_svd(const float* g, int m, int n, int r, int oversampling, uint64_t seed, float* p_out,
+                       float* q_out) {
+    const int l = r + oversampling;
+    if (r == 0 || l > (n < m ? n : m)) return -2;
+    float* omega = (float*)malloc(sizeof(float) * (size_t)n * l);
+    float* y = (float*)malloc(sizeof(float) * (size_t)m * l);
+    float* qt = (float*)malloc(sizeof(float) * (size_t)l * m);
+    float* b = (float*)malloc(sizeof(float) * (size_t)l * n);
+    float* bt = (float*)malloc(sizeof(float) * (size_t)n * l);
+    float* bbt = (float*)malloc(sizeof(float) * (size_t)l * l);
+    float* u = (float*)malloc(sizeof(float) * (size_t)l * l);
+    int st = 0;
+    ref_rsvd_omega(seed, (int64_t)n * l, omega);
+    ref_matmul_f32(g, omega, y, m, n, l);
+    if (rsvd_mgs(y, m, l, 1) != 0) { st = -3; goto done; }
+    for (int i = 0; i < m; ++i)
+        for (int j = 0; j < l; ++j) qt[(int64_t)j * m + i] = y[(int64_t)i * l + j];
+    ref_matmul_f32(qt, g, b, l, m, n);
+    for (int i = 0; i < l; ++i)
+        for (int j = 0; j < n; ++j) bt[(int64_t)j * l + i] = b[(int64_t)i * n + j];
+    ref_matmul_f32(b, bt, bbt, l, n, l);
+    ref_rsvd_jacobi(bbt, l, u);
+    for (int i = 0; i < m; ++i)
+        for (int j = 0; j < r; ++j) {
+            float sum = 0.0f;
+            for (int k = 0; k < l; ++k) sum += y[(int64_t)i * l + k] * u[k * l + j];
+            p_out[(int64_t)i * r + j] = sum;
+        }
+    for (int i = 0; i < n; ++i)
+        for (int j = 0; j < r; ++j) {
+            float sum = 0.0f;
+            for (int k = 0; k < l; ++k) sum += b[(int64_t)k * n + i] * u[k * l + j];
+            q_out[(int64_t)i * r + j] = sum;
+        }
+    rsvd_mgs(q_out, n, r, 0);
+done:
+    free(omega); free(y); free(qt); free(b); free(bt); free(bbt); free(u);
+    return st;
+}
+
 /* galore/src/standard_adamw.rs:84-114; with step >= 1 the moments are bias
  * corrected by the host-computed factors 1 - beta^step. */
 void ref_full_adam_apply(float* param, const float* grad, float* m, float* v, int64_t n, float clip, float b1,

@@ -82,6 +82,12 @@ float ref_clip_coeff(double gsq, float max_norm);
 double ref_sqnorm_f64(const float* x, int64_t n);
 /* should_switch_subspace (galore/src/randomized_svd.rs:273-276) */
 int ref_should_switch(uint64_t step, uint64_t interval);
+/* Randomized SVD refresh (galore/src/randomized_svd.rs:38-271). */
+float ref_rsvd_gaussian(uint64_t* state);
+void ref_rsvd_omega(uint64_t seed, int64_t count, float* out);
+void ref_rsvd_jacobi(float* mat, int n, float* u);
+int ref_randomized_svd(const float* g, int m, int n, int r, int oversampling, uint64_t seed, float* p_out,
+                       float* q_out);
 
 /* StandardAdamW::apply_update (galore/src/standard_adamw.rs:84-114), plus the
  * bias-corrected form documented for doublepass_galore_apply's `step` argument

@@ -66,6 +66,9 @@ def lib():
             "ref_clip_coeff": (C.c_float, [C.c_double, C.c_float]),
             "ref_sqnorm_f64": (C.c_double, [_f32p, C.c_int64]),
             "ref_should_switch": (C.c_int, [C.c_uint64, C.c_uint64]),
+            "ref_rsvd_omega": (None, [C.c_uint64, C.c_int64, _f32p]),
+            "ref_rsvd_jacobi": (None, [_f32p, C.c_int, _f32p]),
+            "ref_randomized_svd": (C.c_int, [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, _f32p, _f32p]),
             "ref_full_adam_apply": (None, [_f32p, _f32p, _f32p, _f32p, C.c_int64, C.c_float, C.c_float, C.c_float,
                                            C.c_float, C.c_float, C.c_int]),
             "b2_dynamic_map": (None, [C.c_int, _f32p]),
@@ -235,6 +238,34 @@ def sqnorm_f64(x):
 
 def should_switch(step, interval):
     return bool(lib().ref_should_switch(step, interval))
+
+
+def rsvd_seed(step):
+    """process_pending_svd's seed (optimizer.rs:216-221): step * 0x9E3779B9, wrapping u64."""
+    return (int(step) * 0x9E3779B9) & 0xFFFFFFFFFFFFFFFF
+
+
+def rsvd_omega(seed, count):
+    out = np.empty(count, np.float32)
+    lib().ref_rsvd_omega(seed, count, out)
+    return out
+
+
+def rsvd_jacobi(a):
+    a = _c(a, np.float32).copy()
+    n = a.shape[0]
+    u = np.empty((n, n), np.float32)
+    lib().ref_rsvd_jacobi(a, n, u)
+    return u, a
+
+
+def randomized_svd(g, m, n, r, oversampling, seed):
+    """(status, P m x r, Q n x r) of randomized_svd_projections."""
+    g = _c(g, np.float32)
+    p = np.zeros((m, r), np.float32)
+    q = np.zeros((n, r), np.float32)
+    st = lib().ref_randomized_svd(g, m, n, r, oversampling, seed, p, q)
+    return st, p, q
 
 
 def full_adam_apply(param, grad, m, v, clip, b1, b2, eps, lr, step):

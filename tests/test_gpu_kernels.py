@@ -205,3 +205,14 @@ def test_lomo_step(oracle, L, lib, codec):
     assert np.array_equal(host(tm8), m8_ref) and np.array_equal(host(tms), ms_ref)
     assert np.array_equal(host(twp), wp_ref) and np.array_equal(host(twa), wa_ref)
     assert rel_fro(host(pre), w) < 0.2
+
+
+@pytest.mark.parametrize("which", [0, 1, 2], ids=["dmap_signed", "dmap_unsigned", "adam_dir"])
+def test_fast_paths_exhaustive(lib, which):
+    """Over all 2^32 float bit patterns: the bucket-table dynamic-map encoder
+    of the Adam and LOMO kernels returns the binary search's code, and the
+    approximate Adam direction rounds to the same bf16 as IEEE sqrt/div."""
+    bad = C.c_ulonglong(12345)
+    assert lib.aeth_selfcheck(which, C.byref(bad)) == 0
+    assert bad.value == 0
+    assert lib.aeth_selfcheck(3, C.byref(bad)) == -1  # unknown check

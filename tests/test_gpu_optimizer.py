@@ -185,3 +185,37 @@ def test_b200_fused_layer_step_equals_sequential(oracle):
     assert c0 == c1
     for x, y in zip(p0 + a0 + s0, p1 + a1 + s1):
         assert np.array_equal(x, y)
+
+
+def test_b200_step_with_hook_equals_fused_clip(oracle):
+    """With a squared-norm hook the step runs norms, hook and clip as separate
+    launches; without one the norm kernel also writes the clip.  Same results,
+    and the per-phase timing records every step."""
+    from aethelstream_b200 import nf4_quantize
+    specs = [(0, "d_wq", 256, 512, 64), (0, "d_wk", 512, 256, 64)]
+    rng = np.random.default_rng(47)
+    grads = [oracle.bf16_round((rng.standard_normal((m, n)) * 1e-3).astype(np.float32)) for _, _, m, n, _ in specs]
+    ws = [(rng.standard_normal((m, n)) * 0.02).astype(np.float32) for _, _, m, n, _ in specs]
+    results = []
+    for use_hook in (False, True):
+        opt = _opt("b200", specs, max_grad_norm=0.01)
+        opt.set_phase_timing(True)
+        W = [nf4_quantize(dev(w)) for w in ws]
+        G = [dev(g).to(torch.bfloat16) for g in grads]
+        seen = []
+        hook = (lambda sq: seen.append(float(sq.sum()))) if use_hook else None
+        clips = [float(host(opt.step_layer([(li, nm) for li, nm, *_ in specs], G, W, sq_hook=hook))[0])
+                 for _ in range(3)]
+        steps, ms = opt.phase_times()
+        assert steps == 3
+        assert all(v > 0.0 for v in ms.values()), ms
+        assert opt.phase_times()[0] == 0
+        if use_hook:
+            assert len(seen) == 3
+        results.append((clips, [host(w.packed) for w in W], [host(w.absmax) for w in W],
+                        [host(x) for li, nm, *_ in specs for x in opt.get_state(li, nm)]))
+        opt.close()
+    (c0, p0, a0, s0), (c1, p1, a1, s1) = results
+    assert c0 == c1 and c0[0] < 1.0
+    for x, y in zip(p0 + a0 + s0, p1 + a1 + s1):
+        assert np.array_equal(x, y)
