@@ -22,9 +22,11 @@ from .galore import (  # noqa: E402
     deferred_apply_with_clip,
     nf4_dequantize,
     nf4_quantize,
+    randomized_svd,
 )
 
 __all__ = [
     "AdamWConfig", "AethError", "ClipResult", "GaLoreConfig", "GaLoreOptimizer", "LayerRankConfig", "NF4Tensor",
-    "ProjectorKind", "deferred_apply_with_clip", "load", "nf4_dequantize", "nf4_quantize", "_lib",
+    "ProjectorKind", "deferred_apply_with_clip", "load", "nf4_dequantize", "nf4_quantize", "randomized_svd",
+    "_lib",
 ]

@@ -19,6 +19,7 @@ AETH_ERR_CONFIG = -3
 AETH_ERR_UNSUPPORTED = -4
 AETH_ERR_NOT_FOUND = -5
 AETH_ERR_TIMEOUT = -6
+AETH_ERR_LINALG = -7
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 MODE_REF, MODE_B200 = 0, 1
@@ -33,6 +34,7 @@ class GaloreConfig(C.Structure):
         ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float), ("lr", C.c_float),
         ("weight_decay", C.c_float), ("scale_lr_by_rank", C.c_int), ("max_grad_norm", C.c_float),
         ("state_codec", C.c_int), ("state_block", C.c_int), ("init_projectors", C.c_int),
+        ("svd_refresh", C.c_int), ("power_iters", C.c_int),
     ]
 
 
@@ -75,6 +77,11 @@ SIGNATURES = {
     "aeth_galore_apply_update": (_i, [_vp, _i, _f, _vp, C.POINTER(WeightRef), _vp]),
     "aeth_galore_zero_accum": (_i, [_vp, _i, _vp]),
     "aeth_galore_notify_step": (_i, [_vp, _u64]),
+    "aeth_galore_notify_step_async": (_i, [_vp, _u64, _vp]),
+    "aeth_galore_version": (_u64, [_vp]),
+    "aeth_randomized_svd": (_i, [_vp, _i, _i, _i, _i, _i, _u64, _vp, _vp, _vp]),
+    "aeth_rsvd_omega": (_i, [_u64, _i64, _vp, _vp]),
+    "aeth_rsvd_jacobi": (_i, [_vp, _i, _vp, _vp]),
     "aeth_galore_step_count": (_u64, [_vp]),
     "aeth_galore_step": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(_vp), _i, C.POINTER(WeightRef), SQ_HOOK, _vp, _vp,
                               _vp]),

@@ -20,6 +20,7 @@
 #include "layer_launch.cuh"
 #include "lomo.cuh"
 #include "nf4.cuh"
+#include "rsvd.cuh"
 
 using namespace aeth;
 
@@ -217,6 +218,9 @@ struct Param {
     uint16_t* projT = nullptr;
     uint16_t* nbuf = nullptr;
     uint16_t* gbf = nullptr;  // bf16 copy of a non-bf16 gradient (lazy)
+    // subspace refresh: full gradient captured at refresh steps (m x n f32, lazy)
+    float* capture = nullptr;
+    bool captured = false;
 };
 
 struct aeth_galore_ctx {
@@ -230,6 +234,7 @@ struct aeth_galore_ctx {
     float* clip_dev = nullptr;
     double* gnorm_dev = nullptr;
     unsigned int* sq_ticket = nullptr;  // sqnorm_group's completion counter, zero between launches
+    uint64_t version = 0;               // completed subspace refreshes (optimizer_version)
     std::vector<void*> allocs;
     // aeth_galore_set_phase_timing: five events per step (phase boundaries)
     bool phase_timing = false;
@@ -534,6 +539,90 @@ int b2_weight_tile(aeth_galore_ctx* c, Param& p, const aeth_weight_ref* w, cudaS
     return AETH_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Subspace refresh (optimizer.rs:208-246, 264-292, 373-398).
+// ---------------------------------------------------------------------------
+__global__ void capture_grad_kernel(const void* __restrict__ g, int dtype, int64_t n, float* __restrict__ cap,
+                                    int first) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = load_as_f32(g, i, dtype);
+        cap[i] = first ? v : __fadd_rn(cap[i], v);  // or_insert(grad.to_vec()) / and_modify(+=)
+    }
+}
+
+// project_and_accumulate's capture (optimizer.rs:266-286): at step + 1 == 1
+// or should_switch_subspace(step + 1, switch_interval), sum the full gradient.
+int capture_if_due(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, cudaStream_t st) {
+    if (!c->cfg.svd_refresh) return AETH_OK;
+    const uint64_t this_step = c->step + 1;
+    const uint64_t every = c->cfg.switch_interval;
+    if (!(this_step == 1 || (every > 0 && this_step % every == 0))) return AETH_OK;
+    const int64_t n = (int64_t)p.m * p.n;
+    if (!p.capture) AETH_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&p.capture), n * sizeof(float), st));
+    capture_grad_kernel<<<grid_for(n, 256), 256, 0, st>>>(grad, dtype, n, p.capture, p.captured ? 0 : 1);
+    AETH_LAUNCH_CHECK();
+    p.captured = true;
+    return AETH_OK;
+}
+
+void drop_capture(Param& p, cudaStream_t st) {
+    if (p.capture) cudaFreeAsync(p.capture, st);
+    p.capture = nullptr;
+    p.captured = false;
+}
+
+// New projectors for one captured parameter, then the Adam state reset
+// (optimizer.rs:229-240).  The projectors change only on success.
+int refresh_param(aeth_galore_ctx* c, Param& p, uint64_t seed, cudaStream_t st) {
+    const bool ref = c->cfg.mode == AETH_MODE_REF;
+    const bool want_p = ref || p.side == 1, want_q = ref || p.side == 2;
+    float* tp = nullptr;
+    float* tq = nullptr;
+    int status = AETH_OK;
+    cudaError_t e = cudaSuccess;
+    if (want_p) e = cudaMallocAsync(reinterpret_cast<void**>(&tp), sizeof(float) * (size_t)p.m * p.r, st);
+    if (e == cudaSuccess && want_q)
+        e = cudaMallocAsync(reinterpret_cast<void**>(&tq), sizeof(float) * (size_t)p.n * p.r, st);
+    if (e != cudaSuccess) status = (int)e;
+    if (status == AETH_OK)
+        status = rsvd_device(p.capture, p.m, p.n, p.r, c->cfg.oversampling, c->cfg.power_iters, seed, tp, tq, st);
+    if (status == AETH_OK) {
+        if (ref) {
+            e = cudaMemcpyAsync(p.P, tp, sizeof(float) * (size_t)p.m * p.r, cudaMemcpyDeviceToDevice, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(p.Q, tq, sizeof(float) * (size_t)p.n * p.r, cudaMemcpyDeviceToDevice, st);
+            if (e != cudaSuccess) status = (int)e;
+        } else {
+            const int s_dim = p.side == 1 ? p.m : p.n;
+            proj_to_bf16_kernel<<<grid_for((int64_t)s_dim * p.r, 256), 256, 0, st>>>(p.side == 1 ? tp : tq, s_dim,
+                                                                                     p.r, p.proj, p.projT);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) status = (int)e;
+        }
+        if (status == AETH_OK) status = reset_state(c, p, st);
+    }
+    if (tp) cudaFreeAsync(tp, st);
+    if (tq) cudaFreeAsync(tq, st);
+    drop_capture(p, st);
+    return status;
+}
+
+int notify_step_on(aeth_galore_ctx* c, uint64_t step, cudaStream_t st) {
+    c->step = step;
+    bool any = false;
+    for (Param& p : c->params) any = any || p.captured;
+    if (!any) return AETH_OK;
+    const uint64_t seed = step * 0x9E3779B9ull;  // wrapping_mul (optimizer.rs:216-221)
+    int status = AETH_OK;
+    for (Param& p : c->params) {
+        if (!p.captured) continue;
+        if (status == AETH_OK) status = refresh_param(c, p, seed, st);
+        else drop_capture(p, st);  // the reference drops the remaining jobs after an error
+    }
+    if (status == AETH_OK) ++c->version;
+    return status;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -552,6 +641,7 @@ const char* aeth_status_string(int st) {
         case AETH_ERR_UNSUPPORTED: return "unsupported shape or alignment";
         case AETH_ERR_NOT_FOUND: return "unknown parameter";
         case AETH_ERR_TIMEOUT: return "device wait timed out";
+        case AETH_ERR_LINALG: return "rank-deficient factorisation";
         default: return st > 0 ? cudaGetErrorString((cudaError_t)st) : "unknown error";
     }
 }
@@ -792,6 +882,8 @@ void aeth_galore_config_default(aeth_galore_config* c) {
     c->state_codec = AETH_CODEC_PER_TENSOR;
     c->state_block = 2048;
     c->init_projectors = 1;
+    c->svd_refresh = 1;  // the reference captures at step 1 and every switch_interval steps
+    c->power_iters = 0;  // RandomizedSvdConfig::default (randomized_svd.rs:19-28), never used by the reference
 }
 
 int aeth_galore_destroy(aeth_galore_ctx* ctx) {
@@ -804,6 +896,8 @@ int aeth_galore_destroy(aeth_galore_ctx* ctx) {
     for (void* p : ctx->allocs) cudaFree(p);
     for (Param& p : ctx->params)
         if (p.gbf) cudaFree(p.gbf);
+    for (Param& p : ctx->params)
+        if (p.capture) cudaFree(p.capture);
     delete ctx;
     return AETH_OK;
 }
@@ -938,6 +1032,7 @@ int aeth_galore_project_accumulate(aeth_galore_ctx* ctx, int idx, const void* gr
     DeviceGuard g(ctx->device);
     Param& p = ctx->params[idx];
     cudaStream_t st = to_stream(stream);
+    AETH_TRY(set_err(capture_if_due(ctx, p, grad, grad_dtype, st)));
     if (ctx->cfg.mode == AETH_MODE_REF) return set_err(ref_project_accumulate(p, grad, grad_dtype, st));
     return set_err(b2_project_accumulate(p, grad, grad_dtype, st));
 }
@@ -989,8 +1084,47 @@ int aeth_galore_zero_accum(aeth_galore_ctx* ctx, int idx, aeth_stream_t stream) 
 }
 
 int aeth_galore_notify_step(aeth_galore_ctx* ctx, uint64_t step) {
-    if (!ctx) return AETH_ERR_ARG;
-    ctx->step = step;
+    if (!ctx) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    AETH_TRY(set_err(notify_step_on(ctx, step, cudaStreamLegacy)));
+    AETH_CUDA(cudaStreamSynchronize(cudaStreamLegacy));
+    return AETH_OK;
+}
+
+int aeth_galore_notify_step_async(aeth_galore_ctx* ctx, uint64_t step, aeth_stream_t stream) {
+    if (!ctx) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    return set_err(notify_step_on(ctx, step, to_stream(stream)));
+}
+
+uint64_t aeth_galore_version(const aeth_galore_ctx* ctx) { return ctx ? ctx->version : 0; }
+
+int aeth_randomized_svd(const float* g, int m, int n, int rank, int oversampling, int power_iters, uint64_t seed,
+                        float* p_out, float* q_out, aeth_stream_t stream) {
+    if (!g || m <= 0 || n <= 0) return set_err(AETH_ERR_ARG);
+    return set_err(rsvd_device(g, m, n, rank, oversampling, power_iters, seed, p_out, q_out, to_stream(stream)));
+}
+
+int aeth_rsvd_omega(uint64_t seed, int64_t count, float* out, aeth_stream_t stream) {
+    if (!out || count <= 0) return set_err(AETH_ERR_ARG);
+    cudaStream_t st = to_stream(stream);
+    uint64_t* jump = nullptr;
+    AETH_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&jump), sizeof(uint64_t) * 64 * kOmegaLevels, st));
+    cudaError_t e = cudaMemcpyAsync(jump, omega_jump_host(), sizeof(Gf2Mat64) * kOmegaLevels, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) {
+        const int64_t chunks = (count + kOmegaChunk - 1) / kOmegaChunk;
+        rsvd_omega_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(jump, seed > 1 ? seed : 1, count, out);
+        e = cudaGetLastError();
+    }
+    cudaFreeAsync(jump, st);
+    AETH_CUDA(e);
+    return AETH_OK;
+}
+
+int aeth_rsvd_jacobi(float* mat, int n, float* u, aeth_stream_t stream) {
+    if (!mat || !u || n < 1) return set_err(AETH_ERR_ARG);
+    jacobi50_kernel<<<1, 1024, 0, to_stream(stream)>>>(mat, n, u);
+    AETH_CUDA(cudaGetLastError());
     return AETH_OK;
 }
 
@@ -1006,6 +1140,7 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     cudaStream_t st = to_stream(stream);
     const bool ref = ctx->cfg.mode == AETH_MODE_REF;
     float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
+    for (int i = 0; i < n; ++i) AETH_TRY(set_err(capture_if_due(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st)));
     if (ref) {
         // A3 hook: project_and_accumulate for every parameter (backward.rs:510-521).
         for (int i = 0; i < n; ++i) AETH_TRY(ref_project_accumulate(ctx->params[idx[i]], grads[i], grad_dtype, st));

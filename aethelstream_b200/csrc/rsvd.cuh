@@ -1,0 +1,480 @@
+// rsvd.cuh -- K8: randomized-SVD projector refresh on the device
+// (galore/src/randomized_svd.rs:38-271, called from optimizer.rs:208-246).
+//
+//   Omega (n x l, l = r + p) ~ N(0,1) by Box-Muller over xorshift64 from
+//   max(seed, 1), drawn in row-major order (randomized_svd.rs:38-66, 93-97);
+//   Y = G Omega; Q^ = orthonormal basis of Y; B = Q^T G; U = the reference's
+//   50-rotation Jacobi on B B^T; P = Q^ U[:, :r]; Q = orthonormalised B^T U[:, :r].
+//
+// Device mapping:
+//   * Omega: one thread per kOmegaChunk consecutive Gaussians; the xorshift64
+//     state at the start of chunk t is M^(2 kOmegaChunk t) applied to the
+//     seed, with M the generator's 64 x 64 matrix over GF(2) (the generator is
+//     linear), so every thread starts exactly where the sequential draw would
+//     be.  The host passes M^(2 kOmegaChunk 2^k) for every bit k of t.
+//   * G Omega, Q^T G, B B^T, Q^ U, B^T U: the exact-order SIMT GEMM
+//     (gemm_simt.cuh), the reference's f32 loops bit for bit on equal inputs.
+//   * The orthonormal bases: Cholesky QR twice with an f64 Gram matrix (two
+//     GEMMs and one small factorisation instead of l^2 / 2 sequential
+//     Gram-Schmidt dot products).  It equals modified Gram-Schmidt in exact
+//     arithmetic (both give the Q factor with a positive R diagonal); in f32
+//     the two differ by rounding.  A Gram matrix that is not positive definite
+//     is the rank-deficiency error of qr_columns.  The final orthonormalisation
+//     of Q (orthonormalize_columns, which clamps tiny norms instead of failing)
+//     falls back to a one-CTA modified Gram-Schmidt when its Gram matrix is
+//     not positive definite.
+//   * Jacobi: one CTA; every rotation reproduces the reference's in-place
+//     update loop, including the values it reads back for k = p and k = q.
+//   * Optional power iterations (a B200 extension; the reference never runs
+//     them): Y <- G (G^T Q^) re-orthonormalised, power_iters times.
+#pragma once
+#include "common.cuh"
+#include "gemm_simt.cuh"
+
+namespace aeth {
+
+// ---------------------------------------------------------------------------
+// xorshift64 over GF(2): 64 x 64 bit matrices stored by column.
+// ---------------------------------------------------------------------------
+struct Gf2Mat64 {
+    uint64_t col[64];
+};
+
+inline uint64_t xorshift64_step(uint64_t x) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    return x;
+}
+
+inline uint64_t gf2_apply(const Gf2Mat64& m, uint64_t x) {
+    uint64_t y = 0;
+    for (int j = 0; j < 64; ++j)
+        if ((x >> j) & 1u) y ^= m.col[j];
+    return y;
+}
+
+inline Gf2Mat64 gf2_mul(const Gf2Mat64& a, const Gf2Mat64& b) {
+    Gf2Mat64 c;
+    for (int j = 0; j < 64; ++j) c.col[j] = gf2_apply(a, b.col[j]);
+    return c;
+}
+
+inline Gf2Mat64 gf2_xorshift_matrix() {
+    Gf2Mat64 m;
+    for (int j = 0; j < 64; ++j) m.col[j] = xorshift64_step(1ull << j);
+    return m;
+}
+
+constexpr int kOmegaChunk = 128;  // Gaussians (256 draws) per thread
+constexpr int kOmegaLevels = 40;  // chunk indices below 2^40
+
+// jump[k] = M^(2 kOmegaChunk 2^k), k < kOmegaLevels.
+inline void omega_jump_tables(Gf2Mat64* jump) {
+    Gf2Mat64 step = gf2_xorshift_matrix();
+    for (int i = 0; i < 8; ++i) step = gf2_mul(step, step);  // M^256 = M^(2 kOmegaChunk)
+    static_assert(2 * kOmegaChunk == 256, "jump base assumes 256 draws per chunk");
+    jump[0] = step;
+    for (int k = 1; k < kOmegaLevels; ++k) jump[k] = gf2_mul(jump[k - 1], jump[k - 1]);
+}
+
+// The tables, built once per process (thread-safe static initialisation).
+inline const Gf2Mat64* omega_jump_host() {
+    static const std::vector<Gf2Mat64> tables = [] {
+        std::vector<Gf2Mat64> t(kOmegaLevels);
+        omega_jump_tables(t.data());
+        return t;
+    }();
+    return tables.data();
+}
+
+__device__ __forceinline__ uint64_t gf2_apply_dev(const uint64_t* __restrict__ col, uint64_t x) {
+    uint64_t y = 0;
+#pragma unroll 8
+    for (int j = 0; j < 64; ++j) y ^= ((x >> j) & 1u) ? col[j] : 0ull;
+    return y;
+}
+
+__device__ __forceinline__ uint64_t xorshift64_dev(uint64_t x) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    return x;
+}
+
+// Rng::next_gaussian (randomized_svd.rs:61-65).
+__device__ __forceinline__ float rsvd_gaussian(uint64_t& s) {
+    s = xorshift64_dev(s);
+    const float u1 = fmaxf(__fmul_rn((float)(s >> 40), 0x1p-24f), 1e-7f);
+    s = xorshift64_dev(s);
+    const float u2 = __fmul_rn((float)(s >> 40), 0x1p-24f);
+    const float two_pi = 2.0f * 3.14159265358979323846f;
+    return __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, logf(u1))), cosf(__fmul_rn(two_pi, u2)));
+}
+
+__global__ void rsvd_omega_kernel(const uint64_t* __restrict__ jump, uint64_t s0, int64_t count,
+                                  float* __restrict__ out) {
+    const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t first = t * kOmegaChunk;
+    if (first >= count) return;
+    uint64_t s = s0;
+    for (int k = 0; k < kOmegaLevels && (t >> k) != 0; ++k)
+        if ((t >> k) & 1) s = gf2_apply_dev(jump + 64 * k, s);
+    const int64_t last = first + kOmegaChunk < count ? first + kOmegaChunk : count;
+    for (int64_t i = first; i < last; ++i) out[i] = rsvd_gaussian(s);
+}
+
+// ---------------------------------------------------------------------------
+// C(i,j) = sum_k A(i,k) B(k,j), f64 accumulation in increasing k, strided
+// operands (A(i,k) = A[i*sai + k*sak], B(k,j) = B[k*sbk + j*sbj]).
+// ---------------------------------------------------------------------------
+template <typename TA, typename TB, typename TC>
+__global__ void __launch_bounds__(256) gemm_f64acc_kernel(const TA* __restrict__ A, int64_t sai, int64_t sak,
+                                                          const TB* __restrict__ B, int64_t sbk, int64_t sbj,
+                                                          TC* __restrict__ C, int64_t ldc, int M, int N, int K) {
+    __shared__ double As[16][65];
+    __shared__ double Bs[16][65];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int i0 = blockIdx.y * 64, j0 = blockIdx.x * 64;
+    double acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        for (int t = threadIdx.x; t < 16 * 64; t += 256) {
+            const int kk = t / 64, ii = t % 64;
+            const int gi = i0 + ii, gj = j0 + ii, gk = k0 + kk;
+            As[kk][ii] = (gi < M && gk < K) ? (double)A[gi * sai + gk * sak] : 0.0;
+            Bs[kk][ii] = (gj < N && gk < K) ? (double)B[gk * sbk + gj * sbj] : 0.0;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < 16; ++kk) {
+            double av[4], bv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) av[a] = As[kk][ty + 16 * a];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) bv[b] = Bs[kk][tx + 16 * b];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = fma(av[a], bv[b], acc[a][b]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int gi = i0 + ty + 16 * a, gj = j0 + tx + 16 * b;
+            if (gi < M && gj < N) C[gi * ldc + gj] = (TC)acc[a][b];
+        }
+}
+
+template <typename TA, typename TB, typename TC>
+inline int gemm_f64acc(const TA* A, int64_t sai, int64_t sak, const TB* B, int64_t sbk, int64_t sbj, TC* C,
+                       int64_t ldc, int M, int N, int K, cudaStream_t st) {
+    dim3 grid((N + 63) / 64, (M + 63) / 64);
+    gemm_f64acc_kernel<TA, TB, TC><<<grid, 256, 0, st>>>(A, sai, sak, B, sbk, sbj, C, ldc, M, N, K);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+// ---------------------------------------------------------------------------
+// One CTA: Cholesky of the l x l f64 Gram matrix in place (lower triangle),
+// then the inverse of the factor into Linv (lower; column c by thread c).
+// *fail = 1 when a pivot is not positive.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) chol_inverse_kernel(double* __restrict__ a, int l, double* __restrict__ linv,
+                                                            int* __restrict__ fail) {
+    __shared__ int bad;
+    __shared__ double piv;
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    for (int k = 0; k < l; ++k) {
+        if (threadIdx.x == 0) {
+            const double d = a[(int64_t)k * l + k];
+            if (!(d > 0.0)) bad = 1;
+            piv = d > 0.0 ? sqrt(d) : 1.0;
+            a[(int64_t)k * l + k] = piv;
+        }
+        __syncthreads();
+        if (bad) break;
+        for (int i = k + 1 + threadIdx.x; i < l; i += blockDim.x) a[(int64_t)i * l + k] /= piv;
+        __syncthreads();
+        const int rem = l - k - 1;
+        const int64_t pairs = (int64_t)rem * (rem + 1) / 2;
+        for (int64_t t = threadIdx.x; t < pairs; t += blockDim.x) {
+            // (i, j) with k < j <= i < l, enumerated row by row
+            int i = (int)((sqrt(8.0 * (double)t + 1.0) - 1.0) * 0.5);
+            while ((int64_t)(i + 1) * (i + 2) / 2 <= t) ++i;
+            while ((int64_t)i * (i + 1) / 2 > t) --i;
+            const int j = (int)(t - (int64_t)i * (i + 1) / 2);
+            const int gi = k + 1 + i, gj = k + 1 + j;
+            a[(int64_t)gi * l + gj] -= a[(int64_t)gi * l + k] * a[(int64_t)gj * l + k];
+        }
+        __syncthreads();
+    }
+    if (bad) {
+        if (threadIdx.x == 0) *fail = 1;
+        return;
+    }
+    for (int c = threadIdx.x; c < l; c += blockDim.x) {
+        for (int i = 0; i < c; ++i) linv[(int64_t)i * l + c] = 0.0;
+        for (int i = c; i < l; ++i) {
+            double s = i == c ? 1.0 : 0.0;
+            for (int k = c; k < i; ++k) s -= a[(int64_t)i * l + k] * linv[(int64_t)k * l + c];
+            linv[(int64_t)i * l + c] = s / a[(int64_t)i * l + i];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// One CTA: modified Gram-Schmidt with the norm clamp of
+// orthonormalize_columns (randomized_svd.rs:187-207); the rare fallback.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) mgs_clamped_kernel(float* __restrict__ q, int rows, int cols) {
+    __shared__ float red[32];
+    __shared__ float bcast;
+    auto block_sum = [&](float v) -> float {
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float t = 0.0f;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+            bcast = t;
+        }
+        __syncthreads();
+        const float r = bcast;
+        __syncthreads();
+        return r;
+    };
+    for (int j = 0; j < cols; ++j) {
+        for (int i = 0; i < j; ++i) {
+            float d = 0.0f;
+            for (int r = threadIdx.x; r < rows; r += blockDim.x)
+                d = __fadd_rn(d, __fmul_rn(q[(int64_t)r * cols + i], q[(int64_t)r * cols + j]));
+            d = block_sum(d);
+            for (int r = threadIdx.x; r < rows; r += blockDim.x)
+                q[(int64_t)r * cols + j] = __fsub_rn(q[(int64_t)r * cols + j], __fmul_rn(d, q[(int64_t)r * cols + i]));
+            __syncthreads();
+        }
+        float nn = 0.0f;
+        for (int r = threadIdx.x; r < rows; r += blockDim.x)
+            nn = __fadd_rn(nn, __fmul_rn(q[(int64_t)r * cols + j], q[(int64_t)r * cols + j]));
+        nn = __fsqrt_rn(fmaxf(block_sum(nn), 1e-12f));
+        for (int r = threadIdx.x; r < rows; r += blockDim.x)
+            q[(int64_t)r * cols + j] = __fdiv_rn(q[(int64_t)r * cols + j], nn);
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// One CTA: jacobi_eigenvectors (randomized_svd.rs:210-271) on the f32 l x l
+// matrix `mat` (destroyed), eigenvector estimate into u.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) jacobi50_kernel(float* __restrict__ mat, int n, float* __restrict__ u) {
+    __shared__ float red_v[32];
+    __shared__ int red_i[32];
+    __shared__ int s_p, s_q, s_stop;
+    __shared__ float s_c, s_s;
+    for (int64_t t = threadIdx.x; t < (int64_t)n * n; t += blockDim.x) u[t] = (t / n == t % n) ? 1.0f : 0.0f;
+    __syncthreads();
+    for (int it = 0; it < 50; ++it) {
+        // largest |a_ij|, i < j; the first in row-major order wins ties (strict > scan)
+        float bv = 0.0f;
+        int bi = -1;
+        for (int64_t f = threadIdx.x; f < (int64_t)n * n; f += blockDim.x) {
+            const int i = (int)(f / n), j = (int)(f % n);
+            if (j <= i) continue;
+            const float v = fabsf(mat[f]);
+            if (v > bv) { bv = v; bi = (int)f; }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi >= 0 && (bi < 0 || oi < bi))) { bv = ov; bi = oi; }
+        }
+        if ((threadIdx.x & 31) == 0) { red_v[threadIdx.x >> 5] = bv; red_i[threadIdx.x >> 5] = bi; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float v = 0.0f;
+            int idx = -1;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w)
+                if (red_v[w] > v || (red_v[w] == v && red_i[w] >= 0 && (idx < 0 || red_i[w] < idx))) {
+                    v = red_v[w];
+                    idx = red_i[w];
+                }
+            // reference defaults p = 0, q = 1 and stops when max_off < 1e-10
+            s_stop = v < 1e-10f;
+            const int p = idx >= 0 ? idx / n : 0, q = idx >= 0 ? idx % n : 1;
+            s_p = p;
+            s_q = q;
+            if (!s_stop) {
+                const float app = mat[(int64_t)p * n + p], aqq = mat[(int64_t)q * n + q], apq = mat[(int64_t)p * n + q];
+                const float tau = __fdiv_rn(__fsub_rn(aqq, app), __fmul_rn(2.0f, apq));
+                const float root = __fsqrt_rn(__fadd_rn(1.0f, __fmul_rn(tau, tau)));
+                const float t = tau >= 0.0f ? __fdiv_rn(1.0f, __fadd_rn(tau, root))
+                                            : __fdiv_rn(-1.0f, __fadd_rn(-tau, root));
+                const float c = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(1.0f, __fmul_rn(t, t))));
+                s_c = c;
+                s_s = __fmul_rn(t, c);
+            }
+        }
+        __syncthreads();
+        if (s_stop) break;
+        const int p = s_p, q = s_q;
+        const float c = s_c, s = s_s;
+        // rows k other than p, q read only their own (unchanged) entries
+        for (int k = threadIdx.x; k < n; k += blockDim.x) {
+            if (k != p && k != q) {
+                const float mkp = mat[(int64_t)k * n + p], mkq = mat[(int64_t)k * n + q];
+                const float np_ = __fsub_rn(__fmul_rn(c, mkp), __fmul_rn(s, mkq));
+                const float nq_ = __fadd_rn(__fmul_rn(s, mkp), __fmul_rn(c, mkq));
+                mat[(int64_t)k * n + p] = np_;
+                mat[(int64_t)p * n + k] = np_;
+                mat[(int64_t)k * n + q] = nq_;
+                mat[(int64_t)q * n + k] = nq_;
+            }
+            const float ukp = u[(int64_t)k * n + p], ukq = u[(int64_t)k * n + q];
+            u[(int64_t)k * n + p] = __fsub_rn(__fmul_rn(c, ukp), __fmul_rn(s, ukq));
+            u[(int64_t)k * n + q] = __fadd_rn(__fmul_rn(s, ukp), __fmul_rn(c, ukq));
+        }
+        if (threadIdx.x == 0) {
+            // k = p (p < q) runs first and rewrites a_pq, which k = q then reads
+            const float app = mat[(int64_t)p * n + p], aqq = mat[(int64_t)q * n + q], apq = mat[(int64_t)p * n + q];
+            const float npp = __fsub_rn(__fmul_rn(c, app), __fmul_rn(s, apq));
+            const float tpq = __fadd_rn(__fmul_rn(s, app), __fmul_rn(c, apq));
+            const float nqq = __fadd_rn(__fmul_rn(s, tpq), __fmul_rn(c, aqq));
+            mat[(int64_t)p * n + p] = npp;
+            mat[(int64_t)q * n + q] = nqq;
+            mat[(int64_t)p * n + q] = 0.0f;
+            mat[(int64_t)q * n + p] = 0.0f;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host orchestration.
+// ---------------------------------------------------------------------------
+struct RsvdWork {
+    float* omega = nullptr;  // n x l
+    float* y = nullptr;      // m x l (sketch, then Q^)
+    float* y2 = nullptr;     // max(m, n) x l scratch
+    float* b = nullptr;      // l x n
+    float* bbt = nullptr;    // l x l
+    float* u = nullptr;      // l x l
+    double* gram = nullptr;  // l x l
+    double* linv = nullptr;  // l x l
+    uint64_t* jump = nullptr;
+    int* fail = nullptr;
+};
+
+// Orthonormal basis of the columns of x (rows x cols) by Cholesky QR, in
+// place; `tmp` holds rows x cols floats.  Two passes.  Returns 1 in *fail_dev
+// when the Gram matrix is not positive definite.
+inline int cholqr2(float* x, float* tmp, int rows, int cols, RsvdWork& w, cudaStream_t st) {
+    for (int pass = 0; pass < 2; ++pass) {
+        AETH_TRY((gemm_f64acc<float, float, double>(x, 1, cols, x, cols, 1, w.gram, cols, cols, cols, rows, st)));
+        chol_inverse_kernel<<<1, 1024, 0, st>>>(w.gram, cols, w.linv, w.fail);
+        AETH_LAUNCH_CHECK();
+        // tmp = x Linv^T
+        AETH_TRY((gemm_f64acc<float, double, float>(x, cols, 1, w.linv, 1, cols, tmp, cols, rows, cols, cols, st)));
+        AETH_CUDA(cudaMemcpyAsync(x, tmp, sizeof(float) * (size_t)rows * cols, cudaMemcpyDeviceToDevice, st));
+    }
+    return AETH_OK;
+}
+
+// randomized_svd_projections on the device.  g: m x n f32; p_out (m x r) and
+// q_out (n x r) f32, either may be null.  Synchronises `st` once to read the
+// factorisation status.  Returns AETH_ERR_CONFIG for an invalid rank or
+// oversampling, AETH_ERR_LINALG for a rank-deficient sketch.
+inline int rsvd_device(const float* g, int m, int n, int r, int oversampling, int power_iters, uint64_t seed,
+                       float* p_out, float* q_out, cudaStream_t st) {
+    const int l = r + oversampling;
+    if (r <= 0 || oversampling < 0 || power_iters < 0 || l > (m < n ? m : n)) return AETH_ERR_CONFIG;
+    RsvdWork w;
+    const size_t big = (size_t)(m > n ? m : n) * l;
+    std::vector<void*> allocs;
+    auto alloc = [&](void** p, size_t bytes) -> int {
+        cudaError_t e = cudaMallocAsync(p, bytes, st);
+        if (e != cudaSuccess) return set_err((int)e);
+        allocs.push_back(*p);
+        return AETH_OK;
+    };
+    int status = AETH_OK;
+    do {
+        if ((status = alloc((void**)&w.omega, sizeof(float) * (size_t)n * l)) ||
+            (status = alloc((void**)&w.y, sizeof(float) * (size_t)m * l)) ||
+            (status = alloc((void**)&w.y2, sizeof(float) * big)) ||
+            (status = alloc((void**)&w.b, sizeof(float) * (size_t)l * n)) ||
+            (status = alloc((void**)&w.bbt, sizeof(float) * (size_t)l * l)) ||
+            (status = alloc((void**)&w.u, sizeof(float) * (size_t)l * l)) ||
+            (status = alloc((void**)&w.gram, sizeof(double) * (size_t)l * l)) ||
+            (status = alloc((void**)&w.linv, sizeof(double) * (size_t)l * l)) ||
+            (status = alloc((void**)&w.jump, sizeof(uint64_t) * 64 * kOmegaLevels)) ||
+            (status = alloc((void**)&w.fail, sizeof(int))))
+            break;
+        cudaError_t e =
+            cudaMemcpyAsync(w.jump, omega_jump_host(), sizeof(Gf2Mat64) * kOmegaLevels, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(w.fail, 0, sizeof(int), st);
+        if (e != cudaSuccess) { status = set_err((int)e); break; }
+        // 1. Omega, 2. Y = G Omega
+        const int64_t count = (int64_t)n * l;
+        const int64_t chunks = (count + kOmegaChunk - 1) / kOmegaChunk;
+        rsvd_omega_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w.jump, seed > 1 ? seed : 1, count,
+                                                                           w.omega);
+        if ((status = simt_gemm_exact(g, n, 1, w.omega, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st))) break;
+        // 3. Q^ = orthonormal basis of Y (+ optional power iterations)
+        if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
+        for (int it = 0; it < power_iters && status == AETH_OK; ++it) {
+            // Z = G^T Q^ (n x l) into y2, orthonormalise, Y = G Z, orthonormalise
+            if ((status = simt_gemm_exact(g, 1, n, w.y, l, 1, w.y2, l, n, l, m, SIMT_STORE, 1.0f, nullptr, st))) break;
+            if ((status = cholqr2(w.y2, w.omega, n, l, w, st))) break;
+            if ((status = simt_gemm_exact(g, n, 1, w.y2, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st))) break;
+            if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
+        }
+        if (status) break;
+        // 4. B = Q^T G (l x n), 5. B B^T (l x l), 6. Jacobi
+        if ((status = simt_gemm_exact(w.y, 1, l, g, n, 1, w.b, n, l, n, m, SIMT_STORE, 1.0f, nullptr, st))) break;
+        if ((status = simt_gemm_exact(w.b, n, 1, w.b, 1, n, w.bbt, l, l, l, n, SIMT_STORE, 1.0f, nullptr, st))) break;
+        jacobi50_kernel<<<1, 1024, 0, st>>>(w.bbt, l, w.u);
+        AETH_LAUNCH_CHECK();
+        // 7. P = Q^ U[:, :r]
+        if (p_out && (status = simt_gemm_exact(w.y, l, 1, w.u, l, 1, p_out, r, m, r, l, SIMT_STORE, 1.0f, nullptr, st)))
+            break;
+        // 8. Q = B^T U[:, :r], orthonormalised (9)
+        if (q_out) {
+            if ((status = simt_gemm_exact(w.b, 1, n, w.u, l, 1, q_out, r, n, r, l, SIMT_STORE, 1.0f, nullptr, st)))
+                break;
+            // Cholesky QR when the Gram matrix allows, else the clamped MGS;
+            // the choice needs the status of the first factorisation of Y too.
+            int fail_y = 0;
+            e = cudaMemcpyAsync(&fail_y, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            if (e != cudaSuccess) { status = set_err((int)e); break; }
+            if (fail_y) { status = set_err(AETH_ERR_LINALG); break; }
+            if ((status = cholqr2(q_out, w.y2, n, r, w, st))) break;
+            int fail_q = 0;
+            e = cudaMemcpyAsync(&fail_q, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            if (e != cudaSuccess) { status = set_err((int)e); break; }
+            if (fail_q) {
+                // redo from B^T U with the reference's clamped Gram-Schmidt
+                if ((status = simt_gemm_exact(w.b, 1, n, w.u, l, 1, q_out, r, n, r, l, SIMT_STORE, 1.0f, nullptr, st)))
+                    break;
+                mgs_clamped_kernel<<<1, 1024, 0, st>>>(q_out, n, r);
+                AETH_LAUNCH_CHECK();
+            }
+        } else {
+            int fail_y = 0;
+            e = cudaMemcpyAsync(&fail_y, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            if (e != cudaSuccess) { status = set_err((int)e); break; }
+            if (fail_y) { status = set_err(AETH_ERR_LINALG); break; }
+        }
+    } while (false);
+    for (void* p : allocs) cudaFreeAsync(p, st);
+    return status;
+}
+
+}  // namespace aeth

@@ -77,6 +77,9 @@ class GaLoreConfig:
     state_block: int = 2048
     max_grad_norm: float = 1.0
     init_projectors: bool = True
+    # subspace refresh in notify_step as the reference (False: fixed projectors)
+    svd_refresh: bool = True
+    power_iters: int = 0
 
     def to_c(self) -> L.GaloreConfig:
         c = L.GaloreConfig()
@@ -98,6 +101,8 @@ class GaLoreConfig:
                          "dynamic": L.CODEC_BLOCK_DYNAMIC}[codec]
         c.state_block = self.state_block
         c.init_projectors = int(self.init_projectors)
+        c.svd_refresh = int(self.svd_refresh)
+        c.power_iters = self.power_iters
         return c
 
 
@@ -145,6 +150,23 @@ def nf4_dequantize(t: NF4Tensor, dtype: torch.dtype = torch.float16, block: int 
     L.check(L.load().aeth_nf4_dequant(_ptr(t.packed), _ptr(t.absmax), t.numel, block, _ptr(out), _DTYPES[dtype],
                                       C.c_void_p(_stream_handle())), "aeth_nf4_dequant")
     return out
+
+
+def randomized_svd(g: torch.Tensor, rank: int, oversampling: int = 10, seed: int = 42, power_iters: int = 0,
+                   want_p: bool = True, want_q: bool = True):
+    """randomized_svd_projections (galore/src/randomized_svd.rs:76-149) on the
+    device: (P m x r, Q n x r) f32 for the f32 matrix g (m x n).  Raises
+    AethError(AETH_ERR_CONFIG) for rank 0 or rank + oversampling > min(m, n)
+    and AethError(AETH_ERR_LINALG) for a rank-deficient sketch."""
+    g = g.contiguous()
+    if g.dtype != torch.float32 or g.dim() != 2:
+        raise ValueError("g must be a 2-D float32 device tensor")
+    m, n = g.shape
+    p = torch.empty(m, rank, dtype=torch.float32, device=g.device) if want_p else None
+    q = torch.empty(n, rank, dtype=torch.float32, device=g.device) if want_q else None
+    L.check(L.load().aeth_randomized_svd(_ptr(g), m, n, rank, oversampling, power_iters, seed & (2**64 - 1),
+                                         _ptr(p), _ptr(q), C.c_void_p(_stream_handle())), "aeth_randomized_svd")
+    return p, q
 
 
 class GaLoreOptimizer:
@@ -251,7 +273,14 @@ class GaLoreOptimizer:
             L.check(self._lib.aeth_galore_zero_accum(self._ctx, k[0], C.c_void_p(_stream_handle())), "zero_accum")
 
     def notify_step(self, step: int) -> None:
-        L.check(self._lib.aeth_galore_notify_step(self._ctx, step), "notify_step")
+        """Records the step and runs pending subspace refreshes (optimizer.rs:373-398)
+        on the current stream."""
+        L.check(self._lib.aeth_galore_notify_step_async(self._ctx, step, C.c_void_p(_stream_handle())),
+                "notify_step")
+
+    def optimizer_version(self) -> int:
+        """Completed subspace refreshes (optimizer.rs:249-253)."""
+        return int(self._lib.aeth_galore_version(self._ctx))
 
     def projector_kind(self, layer_idx: int, param_name: str) -> ProjectorKind:
         return ProjectorKind.ORTHONORMAL

@@ -238,8 +238,9 @@ def run_b200(args):
     dev = torch.device("cuda", local)
     layer = rank  # weak scaling: one block per rank (round-robin layer ownership)
     specs = [(layer, name, m, n, RANK) for name, m, n in SHAPES]
+    # C2 holds the projectors fixed (no gradient capture, no refresh inside the timed steps)
     cfg = GaLoreConfig(mode="b200", state_codec="dynamic", state_block=STATE_BLOCK,
-                       layer_ranks=LayerRankConfig())
+                       layer_ranks=LayerRankConfig(), svd_refresh=False)
     opt = GaLoreOptimizer(cfg, specs, device=local)
     gen = torch.Generator(device=dev)
     weights = []

@@ -10,6 +10,7 @@
  *    -4  AETH_ERR_UNSUPPORTED  shape/alignment this build does not handle
  *    -5  AETH_ERR_NOT_FOUND    unknown parameter key
  *    -6  AETH_ERR_TIMEOUT      a bounded device-side wait gave up (kernel returned early)
+ *    -7  AETH_ERR_LINALG       rank-deficient factorisation (GaLoreError::Linalg)
  *    >0  a cudaError_t value
  * No entry point aborts the process.  All work is enqueued on the caller's
  * stream; only functions documented as synchronous wait on it.
@@ -38,6 +39,7 @@ enum {
     AETH_ERR_UNSUPPORTED = -4,
     AETH_ERR_NOT_FOUND = -5,
     AETH_ERR_TIMEOUT = -6,
+    AETH_ERR_LINALG = -7,
 };
 
 typedef enum { AETH_DTYPE_F32 = 0, AETH_DTYPE_F16 = 1, AETH_DTYPE_BF16 = 2 } aeth_dtype;
@@ -137,6 +139,8 @@ typedef struct {
     int state_codec;          /* aeth_state_codec; REF mode requires PER_TENSOR */
     int state_block;          /* 2048 */
     int init_projectors;      /* 1: init_random_projection at create; 0: zero, set with aeth_galore_set_projector */
+    int svd_refresh;          /* 1: capture gradients and refresh in notify_step as the reference; 0: fixed projectors */
+    int power_iters;          /* 0 (the reference); > 0 adds subspace iterations to the refresh */
 } aeth_galore_config;
 
 typedef struct {
@@ -204,10 +208,44 @@ int aeth_galore_apply_update(aeth_galore_ctx* ctx, int idx, float clip, const fl
                              const aeth_weight_ref* w, aeth_stream_t stream);
 /* OptimizerBackend::zero_accum (adamw.rs:107-109). */
 int aeth_galore_zero_accum(aeth_galore_ctx* ctx, int idx, aeth_stream_t stream);
-/* OptimizerBackend::notify_step (optimizer.rs:373-398): records the step.
- * Subspace refresh is driven by aeth_galore_set_projector in this build. */
+/* OptimizerBackend::notify_step (optimizer.rs:373-398): records the step,
+ * then runs the pending subspace refreshes (process_pending_svd,
+ * optimizer.rs:208-246).  With svd_refresh = 1, project_accumulate (and
+ * aeth_galore_step) capture the full gradient of every parameter -- summed
+ * over calls -- when step + 1 == 1 or should_switch_subspace(step + 1,
+ * switch_interval) (optimizer.rs:264-292, randomized_svd.rs:273-276).  Each
+ * captured parameter then gets new projectors from aeth_randomized_svd with
+ * seed = step * 0x9E3779B9 (wrapping), its own rank and config.oversampling
+ * (B200 mode keeps the projector of its side), and a reset Adam state; the
+ * optimizer version goes up by one when all succeed.  The first failure is
+ * returned and ends the refresh (later captures are dropped, as in the
+ * reference).  notify_step uses the legacy default stream and waits for the
+ * refresh; notify_step_async enqueues it on `stream` (it still waits once per
+ * refreshed parameter for the factorisation status). */
 int aeth_galore_notify_step(aeth_galore_ctx* ctx, uint64_t step);
+int aeth_galore_notify_step_async(aeth_galore_ctx* ctx, uint64_t step, aeth_stream_t stream);
 uint64_t aeth_galore_step_count(const aeth_galore_ctx* ctx);
+/* optimizer_version (optimizer.rs:249-253): subspace refreshes completed. */
+uint64_t aeth_galore_version(const aeth_galore_ctx* ctx);
+
+/* Device randomized SVD, K8 (randomized_svd_projections, randomized_svd.rs:
+ * 76-149; the reference's device entry point randomized_svd_on_device,
+ * :282-298, routes to an unimplemented kernel).  g: m x n f32 row-major;
+ * p_out (m x r) and q_out (n x r) f32 row-major, either may be NULL.
+ * power_iters > 0 adds subspace iterations, a B200 extension (the reference
+ * ignores its power_iters).  Returns AETH_ERR_CONFIG when rank == 0 or
+ * rank + oversampling > min(m, n) (GaLoreError::Config) and AETH_ERR_LINALG
+ * for a rank-deficient sketch (GaLoreError::Linalg).  Waits on `stream` once
+ * to read the factorisation status. */
+int aeth_randomized_svd(const float* g, int m, int n, int rank, int oversampling, int power_iters, uint64_t seed,
+                        float* p_out, float* q_out, aeth_stream_t stream);
+/* Two steps of it on their own.  aeth_rsvd_omega: `count` Gaussians of
+ * Rng::new(seed).next_gaussian() in order (randomized_svd.rs:38-66), every
+ * thread starting from the jumped-ahead xorshift64 state.  aeth_rsvd_jacobi:
+ * jacobi_eigenvectors (randomized_svd.rs:210-271) on the n x n f32 matrix
+ * `mat` (overwritten) with the eigenvector estimate in u (n x n). */
+int aeth_rsvd_omega(uint64_t seed, int64_t count, float* out, aeth_stream_t stream);
+int aeth_rsvd_jacobi(float* mat, int n, float* u, aeth_stream_t stream);
 
 /* Whole-layer step of deferred_apply_with_clip (hook.rs:115-203) for a
  * single micro-batch: for each listed parameter project_and_accumulate, then

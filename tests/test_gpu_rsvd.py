@@ -1,0 +1,165 @@
+"""K8: the randomized-SVD subspace refresh on the GPU against the CPU oracle.
+
+The Gaussian sketch and the Jacobi rotations follow the reference's
+sequential definitions (randomized_svd.rs:38-66, 210-271); the sketch is
+compared with the oracle within libm-vs-CUDA logf/cosf differences and the
+Jacobi bit for bit.  The orthonormal bases come from Cholesky QR instead of
+Gram-Schmidt (equal in exact arithmetic), so the projectors are compared
+within a stated tolerance, plus orthonormality and the captured energy.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from tests._gpu import DEV, dev, host, ptr, rel_fro, stream
+
+pytestmark = pytest.mark.gpu
+
+PROJ_TOL = 1e-3  # relative Frobenius distance of P / Q to the oracle's
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from aethelstream_b200 import _lib
+    return _lib.load()
+
+
+def _lowrank_plus_noise(m, n, k, seed):
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    s = np.geomspace(1.0, 0.05, k).astype(np.float32)
+    return ((a * s) @ b + 0.01 * rng.standard_normal((m, n))).astype(np.float32)
+
+
+@pytest.mark.parametrize("count", [1, 127, 129, 100_003])
+def test_omega_matches_oracle(oracle, lib, count):
+    seed = oracle.rsvd_seed(7)
+    out = torch.empty(count, dtype=torch.float32, device=DEV)
+    assert lib.aeth_rsvd_omega(seed, count, ptr(out), stream()) == 0
+    got, want = host(out), oracle.rsvd_omega(seed, count)
+    assert np.abs(got - want).max() <= 2e-6 * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("n", [2, 7, 40, 136])
+def test_jacobi_bitexact(oracle, lib, n):
+    rng = np.random.default_rng(n)
+    b = rng.standard_normal((n, n + 5)).astype(np.float32)
+    a = (b @ b.T).astype(np.float32)
+    ta = dev(a)
+    tu = torch.empty(n, n, dtype=torch.float32, device=DEV)
+    assert lib.aeth_rsvd_jacobi(ptr(ta), n, ptr(tu), stream()) == 0
+    u, mat = oracle.rsvd_jacobi(a)
+    assert np.array_equal(host(tu), u)
+    assert np.array_equal(host(ta), mat)
+
+
+@pytest.mark.parametrize("m,n,r,p", [(256, 384, 16, 8), (512, 256, 32, 10), (1024, 1024, 64, 8)])
+def test_randomized_svd_matches_oracle(oracle, m, n, r, p):
+    from aethelstream_b200 import randomized_svd
+    g = _lowrank_plus_noise(m, n, r + p + 8, m + n)
+    seed = oracle.rsvd_seed(200)
+    P, Q = randomized_svd(dev(g), r, p, seed)
+    st, p_ref, q_ref = oracle.randomized_svd(g, m, n, r, p, seed)
+    assert st == 0
+    P, Q = host(P), host(Q)
+    assert np.abs(P.T @ P - np.eye(r)).max() < 1e-4
+    assert np.abs(Q.T @ Q - np.eye(r)).max() < 1e-4
+    assert rel_fro(P, p_ref) < PROJ_TOL, rel_fro(P, p_ref)
+    assert rel_fro(Q, q_ref) < PROJ_TOL, rel_fro(Q, q_ref)
+
+
+def test_randomized_svd_errors(lib):
+    from aethelstream_b200 import AethError, randomized_svd, _lib
+    g = torch.ones(32, 32, dtype=torch.float32, device=DEV)
+    for r, p in [(0, 4), (30, 8)]:
+        with pytest.raises(AethError) as e:
+            randomized_svd(g, r, p, 1)
+        assert e.value.status == _lib.AETH_ERR_CONFIG
+    with pytest.raises(AethError) as e:
+        randomized_svd(torch.zeros(32, 32, dtype=torch.float32, device=DEV), 4, 4, 1)
+    assert e.value.status == _lib.AETH_ERR_LINALG
+
+
+def test_power_iterations_capture_more_energy():
+    from aethelstream_b200 import randomized_svd
+    rng = np.random.default_rng(3)
+    m, n, r = 512, 768, 16
+    # slowly decaying spectrum: plain range finding leaves energy behind
+    u, _ = np.linalg.qr(rng.standard_normal((m, m)))
+    v, _ = np.linalg.qr(rng.standard_normal((n, n)))
+    s = (1.0 / np.arange(1, m + 1) ** 0.5)
+    g = ((u * s) @ v[:, :m].T).astype(np.float32)
+    best = np.linalg.norm(s[:r]) / np.linalg.norm(s)
+    caught = []
+    for q in (0, 2):
+        P, _ = randomized_svd(dev(g), r, 8, 11, power_iters=q, want_q=False)
+        P = host(P)
+        assert np.abs(P.T @ P - np.eye(r)).max() < 1e-4
+        caught.append(np.linalg.norm(P.T @ g) / np.linalg.norm(g))
+    assert caught[1] > caught[0] and caught[1] <= best + 1e-4
+
+
+def _opt(mode, specs, **kw):
+    from aethelstream_b200 import GaLoreConfig, GaLoreOptimizer, LayerRankConfig
+    cfg = GaLoreConfig(mode=mode, layer_ranks=LayerRankConfig(), **kw)
+    return GaLoreOptimizer(cfg, specs, device=0)
+
+
+def test_ref_mode_refresh_on_notify_step(oracle):
+    """Step 1 captures the gradient (summed over two micro-batches); notify_step(1)
+    installs the refreshed P, Q (seed = 1 * 0x9E3779B9) and resets the Adam state."""
+    from aethelstream_b200 import randomized_svd
+    m, n = 128, 96
+    opt = _opt("ref", [(0, "d_wq", m, n)], switch_interval=200)
+    r = opt.param_info(0, "d_wq").rank
+    g1 = _lowrank_plus_noise(m, n, 40, 1)
+    g2 = _lowrank_plus_noise(m, n, 40, 2)
+    opt.project_and_accumulate(dev(g1), 0, "d_wq")
+    opt.project_and_accumulate(dev(g2), 0, "d_wq")
+    opt.apply_update(0, "d_wq", 1.0)
+    opt.zero_accum(0, "d_wq")
+    assert opt.optimizer_version() == 0
+    opt.notify_step(1)
+    assert opt.optimizer_version() == 1
+    P, Q = opt.get_projector(0, "d_wq")
+    g = (g1 + g2).astype(np.float32)
+    seed = oracle.rsvd_seed(1)
+    Pd, Qd = randomized_svd(dev(g), r, 10, seed)
+    assert np.array_equal(host(P), host(Pd)) and np.array_equal(host(Q), host(Qd))
+    st, p_ref, q_ref = oracle.randomized_svd(g, m, n, r, 10, seed)
+    assert st == 0 and rel_fro(host(P), p_ref) < PROJ_TOL and rel_fro(host(Q), q_ref) < PROJ_TOL
+    m8, v8, ms, vs = [host(x) for x in opt.get_state(0, "d_wq")]
+    assert not m8.any() and not v8.any() and (ms == 1.0).all() and (vs == 1.0).all()
+    # step 2 (not a refresh step): nothing captured, the projectors stay
+    opt.project_and_accumulate(dev(g1), 0, "d_wq")
+    opt.zero_accum(0, "d_wq")
+    opt.notify_step(2)
+    assert opt.optimizer_version() == 1
+    assert np.array_equal(host(opt.get_projector(0, "d_wq")[0]), host(P))
+    opt.close()
+
+
+def test_b200_mode_refresh_keeps_its_side(oracle):
+    from aethelstream_b200 import randomized_svd
+    m, n, r = 512, 256, 32  # m >= n: right side, the projector is Q (n x r)
+    opt = _opt("b200", [(0, "d_wq", m, n, r)], state_codec="dynamic", switch_interval=3)
+    g = _lowrank_plus_noise(m, n, 64, 9)
+    for step in range(3):  # this_step = 1 captures; 2 does not; 3 (= 3 % 3) captures
+        if step != 1:
+            opt.project_and_accumulate(dev(g).to(torch.bfloat16), 0, "d_wq")
+            opt.zero_accum(0, "d_wq")
+            opt.notify_step(step + 1)
+            assert opt.optimizer_version() == (1 if step == 0 else 2)
+        else:
+            opt.project_and_accumulate(dev(g).to(torch.bfloat16), 0, "d_wq")
+            opt.zero_accum(0, "d_wq")
+            opt.notify_step(step + 1)
+            assert opt.optimizer_version() == 1
+    gb = oracle.bf16_round(g)
+    _, Qd = randomized_svd(dev(gb), r, 10, oracle.rsvd_seed(3), want_p=False)
+    _, Q = opt.get_projector(0, "d_wq")
+    assert np.array_equal(host(Q), oracle.bf16_round(host(Qd)))
+    opt.close()
