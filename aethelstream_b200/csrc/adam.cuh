@@ -180,6 +180,7 @@ struct AdamGroupArgs {
     const float* clip_dev;
     float b1, b2, eps;
     int zero_accum;
+    unsigned int* work;  // [next block, CTAs done], zero between launches
 };
 
 // ---------------------------------------------------------------------------
@@ -265,21 +266,39 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     const float2 clipx2 = make_float2(clip, clip);
     const bool fast_dir = a.eps >= 0.0f;
     const int total = a.block_begin[a.np];
-    for (int gb = blockIdx.x; gb < total; gb += gridDim.x) {
-        int p = 0;
+    // Blocks: the first gridDim.x by CTA index, the rest handed out by a device
+    // counter (even finish times).  Each block's inputs are loaded one
+    // iteration ahead, during the previous block's encode.
+    __shared__ int s_next;
+    int gb = blockIdx.x;
+    int p = 0, b = 0;
+    int64_t e0 = 0;
+    bool valid = false;
+    float sm = 0.0f, sv = 0.0f;
+    float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+    uint2 qm = make_uint2(0u, 0u), qv = qm;
+    auto fetch = [&](int blk) {
+        p = 0;
 #pragma unroll 1
-        while (p + 1 < a.np && gb >= a.block_begin[p + 1]) ++p;
-        const int b = gb - a.block_begin[p];
-        const int64_t e0 = (int64_t)b * 2048 + threadIdx.x * 8;
-        const bool valid = e0 < a.count[p];  // counts are multiples of 8
-        const float sm = a.ms[p][b], sv = a.vs[p][b];
+        while (p + 1 < a.np && blk >= a.block_begin[p + 1]) ++p;
+        b = blk - a.block_begin[p];
+        e0 = (int64_t)b * 2048 + threadIdx.x * 8;
+        valid = e0 < a.count[p];  // counts are multiples of 8
+        sm = a.ms[p][b];
+        sv = a.vs[p][b];
+        if (valid) {
+            g0 = *reinterpret_cast<const float4*>(a.accum[p] + e0);
+            g1 = *reinterpret_cast<const float4*>(a.accum[p] + e0 + 4);
+            qm = *reinterpret_cast<const uint2*>(a.m8[p] + e0);
+            qv = *reinterpret_cast<const uint2*>(a.v8[p] + e0);
+        }
+    };
+    if (gb < total) fetch(gb);
+    while (gb < total) {
+        if (threadIdx.x == 0) s_next = (int)atomicAdd(a.work, 1u) + (int)gridDim.x;
         float mo[8], va[8];
         float am = 0.0f, av = 0.0f;
         if (valid) {
-            const float4 g0 = *reinterpret_cast<const float4*>(a.accum[p] + e0);
-            const float4 g1 = *reinterpret_cast<const float4*>(a.accum[p] + e0 + 4);
-            const uint2 qm = *reinterpret_cast<const uint2*>(a.m8[p] + e0);
-            const uint2 qv = *reinterpret_cast<const uint2*>(a.v8[p] + e0);
             const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
             const float2 smx2 = make_float2(sm, sm), svx2 = make_float2(sv, sv);
             uint32_t nb[4];
@@ -325,9 +344,15 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
         float bm = 0.0f, bv = 0.0f;
 #pragma unroll
         for (int w = 0; w < 8; ++w) { bm = fmaxf(bm, red_m[w]); bv = fmaxf(bv, red_v[w]); }
-        __syncthreads();  // red_* are rewritten by the next block
+        const int next = s_next;
+        __syncthreads();  // red_* and s_next are rewritten for the next block
+        // this block's coordinates, then the next block's inputs
+        const int cp = p, cb = b;
+        const int64_t ce0 = e0;
+        const bool cvalid = valid;
+        if (next < total) fetch(next);
         float nsm, nsv;
-        if (valid) {
+        if (cvalid) {
             uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
             if (!DYN) {
                 nsm = lin_scale_from_absmax(bm);
@@ -354,14 +379,23 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
                                    (dmap_encode_lut<false>(lut_u, map_u, xv.y) << 8)) << sh;
                 }
             }
-            *reinterpret_cast<uint2*>(a.m8[p] + e0) = make_uint2(om[0], om[1]);
-            *reinterpret_cast<uint2*>(a.v8[p] + e0) = make_uint2(ov[0], ov[1]);
+            *reinterpret_cast<uint2*>(a.m8[cp] + ce0) = make_uint2(om[0], om[1]);
+            *reinterpret_cast<uint2*>(a.v8[cp] + ce0) = make_uint2(ov[0], ov[1]);
             if (a.zero_accum) {
-                float* z = const_cast<float*>(a.accum[p]) + e0;
+                float* z = const_cast<float*>(a.accum[cp]) + ce0;
                 *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
                 *reinterpret_cast<float4*>(z + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (threadIdx.x == 0) { a.ms[p][b] = nsm; a.vs[p][b] = nsv; }
+            if (threadIdx.x == 0) { a.ms[cp][cb] = nsm; a.vs[cp][cb] = nsv; }
+        }
+        gb = next;
+    }
+    // The last CTA out resets the counters for the next launch.
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.work + 1, 1u) == gridDim.x - 1) {
+            a.work[0] = 0u;
+            a.work[1] = 0u;
         }
     }
 }

@@ -234,6 +234,7 @@ struct aeth_galore_ctx {
     float* clip_dev = nullptr;
     double* gnorm_dev = nullptr;
     unsigned int* sq_ticket = nullptr;  // sqnorm_group's completion counter, zero between launches
+    unsigned int* work = nullptr;       // b2_adam_group_kernel's block counters, zero between launches
     uint64_t version = 0;               // completed subspace refreshes (optimizer_version)
     std::vector<void*> allocs;
     // aeth_galore_set_phase_timing: five events per step (phase boundaries)
@@ -465,6 +466,7 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         a.b2 = cfg.beta2;
         a.eps = cfg.eps;
         a.zero_accum = zero_accum;
+        a.work = c->work;
         const int grid = std::min(blocks, num_sms() * (dyn ? 4 : 8));
         if (dyn)
             b2_adam_group_kernel<true><<<grid, 256, kAdamDynSmem, st>>>(a);
@@ -994,9 +996,12 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
     if ((st = ctx_alloc(c, &c->sq_slots, n_specs)) || (st = ctx_alloc(c, &c->sq_step, n_specs)) ||
         (st = ctx_alloc(c, &c->partials, std::max(kSqPartials, kSqGroupMax * kSqChunks))) ||
         (st = ctx_alloc(c, &c->clip_dev, 1)) ||
-        (st = ctx_alloc(c, &c->gnorm_dev, 1)) || (st = ctx_alloc(c, &c->sq_ticket, 1)))
+        (st = ctx_alloc(c, &c->gnorm_dev, 1)) || (st = ctx_alloc(c, &c->sq_ticket, 1)) ||
+        (st = ctx_alloc(c, &c->work, 2)))
         return fail(st);
-    if (cudaMemset(c->sq_ticket, 0, sizeof(unsigned int)) != cudaSuccess) return fail(AETH_ERR_CONFIG);
+    if (cudaMemset(c->sq_ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
+        cudaMemset(c->work, 0, 2 * sizeof(unsigned int)) != cudaSuccess)
+        return fail(AETH_ERR_CONFIG);
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(AETH_ERR_CONFIG);
     *out = c;
     return AETH_OK;

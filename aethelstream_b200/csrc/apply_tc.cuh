@@ -213,7 +213,8 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 const int64_t grow = (int64_t)(m0 + row);
                 float* dout = (pr.delta_out && grow < pr.m) ? pr.delta_out + grow * pr.n + n0 + cl : nullptr;
                 float* pout = (pr.prequant_out && grow < pr.m) ? pr.prequant_out + grow * pr.n + n0 + cl : nullptr;
-                // pass 1: w = CODES * absmax_old - fl(lr * dW) [* decay] -> TMEM; block absmax
+                // pass 1: w = CODES * absmax_old - fl(lr * dW) [* decay] -> TMEM; block absmax.
+                // The TMEM load of a chunk is in flight while its old weights are dequantised.
                 float amax = 0.0f;
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                         *reinterpret_cast<const uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
                     nf4_dequant_word_s(qq.x, amax_old, lut_s, w);
                     nf4_dequant_word_s(qq.y, amax_old, lut_s, w + 8);
-                    tmem_wait_ld();
+                    tmem_wait_ld_bind(v);
                     // Products paired: v <- fl(v * -lr) = -fl(lr * dW) (round-to-nearest is
                     // sign-symmetric); sums scalar: w <- fl(w + v) = fl(w - fl(lr * dW)); decay.
 #pragma unroll
@@ -252,18 +253,21 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     }
                 }
                 tmem_wait_st();
-                // pass 2: requantise from TMEM (fast classifier; exact fix-up next to boundaries)
+                // pass 2: requantise from TMEM (fast classifier; exact fix-up next to
+                // boundaries), again with the next chunk's load in flight.
                 const float safe = fmaxf(amax, 1e-8f), inv = __frcp_rn(safe);
                 float mind = 1.0f;
-#pragma unroll 1
+                float wbuf[2][16];
+                tmem_ld16<0>(tcol, wbuf[0]);
+                tmem_wait_ld_bind(wbuf[0]);
+#pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    float w[16];
-                    tmem_ld16<0>(tcol + (uint32_t)(c * 16), w);
-                    tmem_wait_ld();
-                    const uint32_t lo = nf4_fast_word8_s(w, inv, bucket_bias, mind);
-                    const uint32_t hi = nf4_fast_word8_s(w + 8, inv, bucket_bias, mind);
+                    if (c < 3) tmem_ld16<0>(tcol + (uint32_t)((c + 1) * 16), wbuf[(c + 1) & 1]);
+                    const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_bias, mind);
+                    const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_bias, mind);
                     *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
                         make_uint2(lo, hi);
+                    if (c < 3) tmem_wait_ld_bind(wbuf[(c + 1) & 1]);
                 }
                 if (__any_sync(0xffffffffu, mind < kNf4NearWindow32)) {
                     // Rare: redo words holding a near-boundary element with the

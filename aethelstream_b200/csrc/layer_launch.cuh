@@ -20,8 +20,10 @@ struct ProjJob {
 
 template <int BN>
 int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) {
-    constexpr int STAGES = 4;
+    // As many 32-48 KB operand stages as shared memory holds: more bytes in flight per SM.
+    constexpr int STAGES = BN <= 128 ? 6 : 4;
     using L = ProjLayout<BN, STAGES>;
+    static_assert(1024 + L::kTotal <= 227 * 1024, "projection kernel shared memory above the per-CTA limit");
     DeviceRuntime* rt = nullptr;
     AETH_TRY(runtime_for_current(&rt));
     ProjArgs a;
@@ -30,13 +32,28 @@ int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) 
     a.r = r;
     a.idesc_k = idesc_f16(128, BN, true, false, false);
     a.idesc_mn = idesc_f16(128, BN, true, true, false);
-    int64_t total_kb_tiles = 0;
-    for (int i = 0; i < nj; ++i) {
-        const int l = std::max(jobs[i].m, jobs[i].n), s = std::min(jobs[i].m, jobs[i].n);
-        total_kb_tiles += (int64_t)((l + 127) / 128) * ((s + 63) / 64);
+    // Split-K depth: the persistent CTAs take units round-robin, so the launch
+    // lasts about ceil(units / SMs) units of (k-blocks + epilogue) each.  Pick
+    // the k-blocks per unit (at least 8) that minimises that, counting an
+    // epilogue as 2 k-blocks of work.
+    int kb_target = 8;
+    {
+        int64_t best = -1;
+        for (int kt = 8; kt <= 64; ++kt) {
+            int64_t units_k = 0, per_unit = 0;
+            for (int i = 0; i < nj; ++i) {
+                const int l = std::max(jobs[i].m, jobs[i].n), s = std::min(jobs[i].m, jobs[i].n);
+                const int kbt = (s + 63) / 64;
+                int sp = (kbt + kt - 1) / kt;
+                const int kpu = (kbt + sp - 1) / sp;
+                sp = (kbt + kpu - 1) / kpu;
+                units_k += (int64_t)((l + 127) / 128) * sp;
+                per_unit = std::max<int64_t>(per_unit, kpu);
+            }
+            const int64_t span = (units_k + num_sms() - 1) / num_sms() * (per_unit + 2);
+            if (best < 0 || span < best) { best = span; kb_target = kt; }
+        }
     }
-    const int64_t target_units = (int64_t)num_sms() * 8;
-    const int kb_target = (int)std::max<int64_t>(8, (total_kb_tiles + target_units - 1) / target_units);
     int units = 0;
     for (int i = 0; i < nj; ++i) {
         const ProjJob& j = jobs[i];

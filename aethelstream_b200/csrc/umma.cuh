@@ -164,6 +164,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[N]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// wait::ld that also binds the 16 destination registers of an earlier
+// tcgen05.ld, so no use of them can be scheduled before the wait (needed when
+// another load is in flight while these registers are consumed).
+__device__ __forceinline__ void tmem_wait_ld_bind(float (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
+                   "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]),
+                   "+f"(v[15])
+                 :
+                 : "memory");
+}
+
 // 32 lanes x 16 consecutive 32-bit columns from registers into TMEM.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
     asm volatile(
