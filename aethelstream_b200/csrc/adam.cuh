@@ -194,22 +194,34 @@ struct AdamGroupArgs {
 // with IEEE sqrt and division.  aeth_selfcheck(AETH_SELFCHECK_ADAM_DIR)
 // compares the two paths over every float bit pattern of va.
 // ---------------------------------------------------------------------------
-constexpr uint32_t kAdamDirGuard = 128;  // ulp
+constexpr uint32_t kAdamDirGuard = 32;  // ulp, about three times the error bound
 
 __device__ __forceinline__ float adam_dir_exact(float mo, float va, float eps) {
     return __fdiv_rn(mo, __fadd_rn(__fsqrt_rn(va), eps));
 }
 
+// Out of line, so the fast path branches around it rather than evaluating
+// IEEE sqrt and division for every element under a predicate.
+__device__ __noinline__ float adam_dir_exact_rare(float mo, float va, float eps) { return adam_dir_exact(mo, va, eps); }
+
+// The .ftz forms are single hardware instructions.  They flush subnormals: a
+// subnormal v has a square root below 1.1e-19, under half an ulp of any
+// eps >= 1e-10 (callers use the fast path only then), so d is the same either
+// way and normal; q is formed by an ordinary multiply and tiny results take
+// the exact path.
 __device__ __forceinline__ float adam_dir_fast(float mo, float va, float eps) {
     float s, r;
-    asm("sqrt.approx.f32 %0, %1;" : "=f"(s) : "f"(va));
+    asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(s) : "f"(va));
     const float d = __fadd_rn(s, eps);
-    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
     const float q = __fmul_rn(mo, r);
     const uint32_t qb = __float_as_uint(q), mag = qb & 0x7fffffffu;
     const bool near_tie = ((qb & 0xffffu) + kAdamDirGuard - 0x8000u) < 2u * kAdamDirGuard;
-    const bool odd = (mag != 0u && mag < 0x0d800000u) || mag >= 0x7f800000u || !(d >= 1e-30f);  // tiny, inf/NaN
-    return (near_tie || odd) ? adam_dir_exact(mo, va, eps) : q;
+    // nonzero below 2^-100, inf or NaN, a tiny denominator, or v < 0 (a negative
+    // subnormal v flushes to -0 where IEEE sqrt gives NaN)
+    const bool odd = (mag - 1u) < 0x0d7fffffu || mag >= 0x7f800000u || !(d >= 1e-30f) || !(va >= 0.0f);
+    if (near_tie || odd) return adam_dir_exact_rare(mo, va, eps);
+    return q;
 }
 
 // Every float bit pattern as va, with mo drawn from [-0.5, 0.5) by a hash of
@@ -229,21 +241,21 @@ __global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ misma
     if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
-// Dynamic-codec shared memory of b2_adam_group_kernel: two 16-bank replicated
-// maps, the two sorted maps and the two bucket tables.
-constexpr int kAdamDynSmem = (2 * 256 * 16 + 2 * 256 + 2 * kDmapLutN) * 4;
+// Dynamic-codec shared memory of b2_adam_group_kernel: the two bucket tables,
+// two 16-bank replicated maps and the two sorted maps.
+constexpr int kAdamDynSmem = 2 * kDmapLutEntries * 8 + (2 * 256 * 16 + 2 * 256) * 4;
 
 template <bool DYN>
 __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
-    extern __shared__ __align__(16) float dyn_smem[];
+    extern __shared__ __align__(16) uint2 dyn_smem[];
     __shared__ float red_m[8], red_v[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, l16 = lane & 15;
-    float* rep_s = dyn_smem;
+    uint2* lut_s = dyn_smem;
+    uint2* lut_u = lut_s + kDmapLutEntries;
+    float* rep_s = reinterpret_cast<float*>(lut_u + kDmapLutEntries);
     float* rep_u = rep_s + 256 * 16;
     float* map_s = rep_u + 256 * 16;
     float* map_u = map_s + 256;
-    uint32_t* lut_s = reinterpret_cast<uint32_t*>(map_u + 256);
-    uint32_t* lut_u = lut_s + kDmapLutN;
     if (DYN) {
         for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
             rep_s[i] = c_dmap_signed[i >> 4];
@@ -253,7 +265,7 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
             map_s[i] = c_dmap_signed[i];
             map_u[i] = c_dmap_unsigned[i];
         }
-        for (int i = threadIdx.x; i < kDmapLutN; i += blockDim.x) {
+        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) {
             lut_s[i] = g_dmap_lut[0][i];
             lut_u[i] = g_dmap_lut[1][i];
         }
@@ -264,7 +276,7 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     const float2 b1x2 = make_float2(a.b1, a.b1), b2x2 = make_float2(a.b2, a.b2);
     const float2 omb1x2 = make_float2(omb1, omb1), omb2x2 = make_float2(omb2, omb2);
     const float2 clipx2 = make_float2(clip, clip);
-    const bool fast_dir = a.eps >= 0.0f;
+    const bool fast_dir = a.eps >= 1e-10f;  // the error bound and the flush-to-zero argument need it
     const int total = a.block_begin[a.np];
     // Blocks: the first gridDim.x by CTA index, the rest handed out by a device
     // counter (even finish times).  Each block's inputs are loaded one
@@ -327,7 +339,7 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
                 va[k] = va2.x;
                 va[k + 1] = va2.y;
                 // N is stored in bf16, so the approximate quotient serves where its
-                // bf16 rounding provably matches (eps >= 0 keeps the error bound).
+                // bf16 rounding provably matches (for eps >= 1e-10, see adam_dir_fast).
                 const float n0 = fast_dir ? adam_dir_fast(mo2.x, va2.x, a.eps) : adam_dir_exact(mo2.x, va2.x, a.eps);
                 const float n1 = fast_dir ? adam_dir_fast(mo2.y, va2.y, a.eps) : adam_dir_exact(mo2.y, va2.y, a.eps);
                 const __nv_bfloat162 nn = __floats2bfloat162_rn(n0, n1);  // .x = n0 in the low half

@@ -438,7 +438,16 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
     }
     AETH_TRY(codec_maps_ensure());
     const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
-    static_assert(kAdamDynSmem <= 48 * 1024, "dynamic-codec tables exceed the default shared-memory limit");
+    // 59 KB of tables per CTA: three CTAs per SM
+    static_assert(3 * (kAdamDynSmem + 1024) <= 228 * 1024, "three dynamic-codec Adam CTAs must fit an SM");
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    if (dyn && !attr_set[dev]) {
+        AETH_CUDA(cudaFuncSetAttribute(b2_adam_group_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kAdamDynSmem));
+        attr_set[dev] = true;
+    }
     for (int off = 0; off < np; off += kAdamGroupMax) {
         const int cnt = std::min(kAdamGroupMax, np - off);
         AdamGroupArgs a;
@@ -467,7 +476,7 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         a.eps = cfg.eps;
         a.zero_accum = zero_accum;
         a.work = c->work;
-        const int grid = std::min(blocks, num_sms() * (dyn ? 4 : 8));
+        const int grid = std::min(blocks, num_sms() * (dyn ? 3 : 8));
         if (dyn)
             b2_adam_group_kernel<true><<<grid, 256, kAdamDynSmem, st>>>(a);
         else

@@ -25,16 +25,19 @@ int build_dynamic_map(int is_signed, float out[256]);
 // binary search (dmap_encode) returns.
 //
 // The encode is a step function of the magnitude a = |xn|: the code changes
-// only at the decision points between neighbouring map entries, each within a
-// couple of ulp of the real midpoint of the two entries.  A magnitude selects
-// bucket b = (bits(a) >> 17) - (103 << 6): 64 buckets per octave over
-// [2^-24, 2), bucket 0 also taking everything below 2^-24.  An entry packs
-// the bucket's single decision threshold t (float bits, low 8 bits cleared) and
-// the code below it (low 8 bits): code = low + [bits(a) >= t].  A bucket with
-// no threshold stores t = bits(3.4e38).  Magnitudes within kDmapGuard ulp of t,
-// buckets with two thresholds (entry 0), a >= 2, infinities and NaN take the
-// binary search.  Midpoints up to kDmapGuard ulp outside a bucket count as
-// inside it, so a decision point never hides next to a bucket edge.
+// only at the decision points between neighbouring map entries, each within
+// 1.5 ulp of the real midpoint of the two entries (the binary search's two
+// distances each carry at most half an ulp of error, plus the rounding of the
+// midpoint to float).  A magnitude selects bucket b = (bits(a) >> 17) -
+// (103 << 6), clamped to [0, kDmapLutN]: 64 buckets per octave over
+// [2^-24, 2), bucket 0 also taking everything below 2^-24, and a last entry
+// for a >= 2, infinities and NaN.  An entry is {threshold bits, code below}:
+// the float bits of the one decision threshold within 56 bit steps of the
+// bucket (several midpoints of the map fall exactly on bucket edges), or
+// kDmapNoThr, which no magnitude reaches; code = below + [bits(a) >=
+// threshold].  The binary search handles magnitudes within kDmapGuard bit
+// steps of the threshold and entries flagged kDmapSearch: buckets with two
+// thresholds near them and the last entry.
 //
 // Table 0 covers the signed map's non-negative half (indices 127..255); the
 // map is symmetric about index 127 except for the extra entry 1.0 at 255, so a
@@ -45,41 +48,47 @@ int build_dynamic_map(int is_signed, float out[256]);
 // ---------------------------------------------------------------------------
 constexpr int kDmapLutExpLo = 103;                     // 2^-24
 constexpr int kDmapLutN = (128 - kDmapLutExpLo) << 6;  // 1600 buckets
-constexpr uint32_t kDmapGuard = 1024;                  // ulp
-constexpr uint32_t kDmapNoThreshold = 0x7f7fff00u;
-__device__ uint32_t g_dmap_lut[2][kDmapLutN];
+constexpr int kDmapLutEntries = kDmapLutN + 1;         // + the entry for a >= 2, inf, NaN
+constexpr uint32_t kDmapGuard = 8;                     // bit steps (ulp) around a threshold
+constexpr uint32_t kDmapReach = 56;                    // thresholds this far outside a bucket count
+constexpr uint32_t kDmapNoThr = 0xc0000000u;           // above every magnitude, far from all of them
+constexpr uint32_t kDmapSearch = 0x100u;               // in the code word: always search
+__device__ uint2 g_dmap_lut[2][kDmapLutEntries];
 
-inline void build_dmap_lut(const float map[256], int is_signed, uint32_t* out) {
+inline void build_dmap_lut(const float map[256], int is_signed, uint2* out) {
     std::vector<std::pair<double, int>> M;  // entries ascending by magnitude, with their codes
     for (int i = is_signed ? 127 : 0; i < 256; ++i) M.push_back({(double)map[i], i});
+    auto bits_of = [](double v) {
+        const float f = (float)v;
+        uint32_t u;
+        memcpy(&u, &f, 4);
+        return u;
+    };
     for (int b = 0; b < kDmapLutN; ++b) {
         const uint32_t lo_bits = (uint32_t)(b + (kDmapLutExpLo << 6)) << 17;
         const uint32_t hi_bits = lo_bits + (1u << 17);
-        float lof, hif, ulp;
-        memcpy(&lof, &lo_bits, 4);
-        memcpy(&hif, &hi_bits, 4);
-        const uint32_t ulp_bits = lo_bits & 0x7f800000u;  // 2^E; one ulp is 2^(E-23)
-        memcpy(&ulp, &ulp_bits, 4);
-        const double u = (double)ulp * 0x1p-23;
-        const double lo = b == 0 ? 0.0 : (double)lof - kDmapGuard * u, hi = (double)hif + kDmapGuard * u;
+        // midpoints (as floats) within kDmapReach bit steps of the bucket;
+        // bucket 0 also holds everything below 2^-24
+        const uint32_t ext_lo = b == 0 ? 0u : lo_bits - kDmapReach, ext_hi = hi_bits + kDmapReach;
         int nmid = 0, kmid = -1;
         for (size_t k = 0; k + 1 < M.size(); ++k) {
-            const double mid = 0.5 * (M[k].first + M[k + 1].first);
-            if (mid >= lo && mid < hi) { ++nmid; kmid = (int)k; }
+            const uint32_t tb = bits_of(0.5 * (M[k].first + M[k + 1].first));
+            if (tb >= ext_lo && tb < ext_hi) { ++nmid; kmid = (int)k; }
         }
         if (nmid == 0) {
+            float lof;
+            memcpy(&lof, &lo_bits, 4);
+            const double lo = b == 0 ? 0.0 : (double)lof;
             size_t k = 0;  // the nearest entry is the same over the whole bucket
             while (k + 1 < M.size() && 0.5 * (M[k].first + M[k + 1].first) < lo) ++k;
-            out[b] = kDmapNoThreshold | (uint32_t)M[k].second;
-        } else if (nmid == 1) {
-            const float thr = (float)(0.5 * (M[kmid].first + M[kmid + 1].first));
-            uint32_t tb;
-            memcpy(&tb, &thr, 4);
-            out[b] = (tb & ~0xffu) | (uint32_t)M[kmid].second;
+            out[b] = make_uint2(kDmapNoThr, (uint32_t)M[k].second);
+        } else if (nmid == 1 && b > 0) {
+            out[b] = make_uint2(bits_of(0.5 * (M[kmid].first + M[kmid + 1].first)), (uint32_t)M[kmid].second);
         } else {
-            out[b] = 0u;
+            out[b] = make_uint2(kDmapNoThr, kDmapSearch);
         }
     }
+    out[kDmapLutN] = make_uint2(kDmapNoThr, kDmapSearch);
 }
 
 inline bool g_maps_uploaded[kMaxDevices] = {};
@@ -94,7 +103,7 @@ inline int codec_maps_ensure() {
         build_dynamic_map(0, u);
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_signed, s, sizeof(s)));
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_unsigned, u, sizeof(u)));
-        static uint32_t lut[2][kDmapLutN];
+        static uint2 lut[2][kDmapLutEntries];
         build_dmap_lut(s, 1, lut[0]);
         build_dmap_lut(u, 0, lut[1]);
         AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut, lut, sizeof(lut)));
@@ -130,21 +139,24 @@ __device__ __forceinline__ uint32_t dmap_encode(const float* __restrict__ map, f
     return dh < dl ? (uint32_t)lo : (uint32_t)(lo - 1);
 }
 
+// The binary search as an out-of-line call for the rare cases of the bucket
+// encoder, so that the compiler branches around it instead of evaluating it
+// for every element under a predicate.
+__device__ __noinline__ uint32_t dmap_encode_rare(const float* map, float xn) { return dmap_encode(map, xn); }
+
 // Bucket-table encode (tables built by build_dmap_lut); `lut` is table 0 for
 // the signed map and table 1 for the unsigned one, `map` the sorted map for
 // the rare binary-search cases.  Returns dmap_encode(map, xn) for every xn.
 template <bool SIGNED>
-__device__ __forceinline__ uint32_t dmap_encode_lut(const uint32_t* __restrict__ lut, const float* __restrict__ map,
+__device__ __forceinline__ uint32_t dmap_encode_lut(const uint2* __restrict__ lut, const float* __restrict__ map,
                                                     float xn) {
     const uint32_t ab = __float_as_uint(xn) & 0x7fffffffu;
-    const int b = max((int)(ab >> 17) - (kDmapLutExpLo << 6), 0);
-    const bool in = b < kDmapLutN;
-    const uint32_t e = lut[in ? b : 0];
-    const uint32_t t = e & ~0xffu;
-    uint32_t code = (e & 0xffu) + (ab >= t ? 1u : 0u);
+    const int b = min(max((int)(ab >> 17) - (kDmapLutExpLo << 6), 0), kDmapLutN);
+    const uint2 e = lut[b];
+    uint32_t code = e.y + (ab >= e.x ? 1u : 0u);
     // signed: mirror image; unsigned: every negative value is nearest to entry 0 (= 0)
-    if (xn < 0.0f) code = SIGNED ? (code >= 254u ? 0u : 254u - code) : 0u;
-    if (!in || e == 0u || ab - t + kDmapGuard < 2u * kDmapGuard) code = dmap_encode(map, xn);
+    if (xn < 0.0f) code = SIGNED ? (uint32_t)max(254 - (int)code, 0) : 0u;
+    if (e.y > 0xffu || ab - e.x + kDmapGuard < 2u * kDmapGuard) code = dmap_encode_rare(map, xn);
     return code;
 }
 
@@ -152,9 +164,9 @@ __device__ __forceinline__ uint32_t dmap_encode_lut(const uint32_t* __restrict__
 // disagreements (a self-check of the bucket tables, run by the test suite).
 __global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restrict__ mismatches) {
     __shared__ float map[256];
-    __shared__ uint32_t lut[kDmapLutN];
+    __shared__ uint2 lut[kDmapLutEntries];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) map[i] = is_signed ? c_dmap_signed[i] : c_dmap_unsigned[i];
-    for (int i = threadIdx.x; i < kDmapLutN; i += blockDim.x) lut[i] = g_dmap_lut[is_signed ? 0 : 1][i];
+    for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) lut[i] = g_dmap_lut[is_signed ? 0 : 1][i];
     __syncthreads();
     unsigned long long bad = 0;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;

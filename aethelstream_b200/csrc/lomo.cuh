@@ -51,12 +51,12 @@ __global__ void __launch_bounds__(256) lomo_update_kernel(const uint16_t* __rest
                                                           float* __restrict__ wa, float* __restrict__ prequant) {
     __shared__ Nf4Tables tab;
     __shared__ float dm[256];
-    __shared__ uint32_t dlut[kDmapLutN];
+    __shared__ uint2 dlut[kDmapLutEntries];
     __shared__ float red[8];
     nf4_tables_init(&tab, threadIdx.x, blockDim.x);
     if (codec == AETH_CODEC_BLOCK_DYNAMIC) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) dm[i] = c_dmap_signed[i];
-        for (int i = threadIdx.x; i < kDmapLutN; i += blockDim.x) dlut[i] = g_dmap_lut[0][i];
+        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) dlut[i] = g_dmap_lut[0][i];
     }
     __syncthreads();
     double gnorm = sqrt(*sq);
