@@ -79,6 +79,8 @@ SIGNATURES = {
     "aeth_galore_notify_step": (_i, [_vp, _u64]),
     "aeth_galore_notify_step_async": (_i, [_vp, _u64, _vp]),
     "aeth_galore_version": (_u64, [_vp]),
+    "aeth_galore_save_state": (_i, [_vp, C.c_char_p, _vp]),
+    "aeth_galore_load_state": (_i, [_vp, C.c_char_p, _vp]),
     "aeth_randomized_svd": (_i, [_vp, _i, _i, _i, _i, _i, _u64, _vp, _vp, _vp]),
     "aeth_rsvd_omega": (_i, [_u64, _i64, _vp, _vp]),
     "aeth_rsvd_jacobi": (_i, [_vp, _i, _vp, _vp]),

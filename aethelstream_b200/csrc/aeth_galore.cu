@@ -21,6 +21,7 @@
 #include "lomo.cuh"
 #include "nf4.cuh"
 #include "rsvd.cuh"
+#include "state_file.h"
 
 using namespace aeth;
 
@@ -1112,6 +1113,226 @@ int aeth_galore_notify_step_async(aeth_galore_ctx* ctx, uint64_t step, aeth_stre
 }
 
 uint64_t aeth_galore_version(const aeth_galore_ctx* ctx) { return ctx ? ctx->version : 0; }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// optimizer_states.bin (state_file.h): REF mode writes and reads version 2
+// byte for byte as the reference; B200 mode writes version 3.
+// ---------------------------------------------------------------------------
+namespace {
+
+template <class T>
+int d2h(std::vector<T>& h, const void* d, size_t count, cudaStream_t st) {
+    h.resize(count);
+    AETH_CUDA(cudaMemcpyAsync(h.data(), d, count * sizeof(T), cudaMemcpyDeviceToHost, st));
+    return AETH_OK;
+}
+
+struct FileCloser {
+    FILE* f = nullptr;
+    ~FileCloser() {
+        if (f) fclose(f);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+int aeth_galore_save_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t stream) {
+    if (!ctx || !path) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    const bool ref = ctx->cfg.mode == AETH_MODE_REF;
+    const uint32_t nl = (uint32_t)ctx->params.size();
+    StateHeader h;
+    h.version = ref ? 2 : 3;
+    h.num_layers = nl;
+    h.rank = nl ? (uint32_t)ctx->params[0].r : 16u;
+    h.beta1 = ctx->cfg.beta1;
+    h.beta2 = ctx->cfg.beta2;
+    h.eps = ctx->cfg.eps;
+    h.step_count = ctx->step;
+    const uint32_t dsz = ref ? kStateDescV2 : kStateDescV3;
+    std::vector<StateDesc> descs(nl);
+    uint64_t off = kStateHeaderSize + (uint64_t)nl * dsz;
+    for (uint32_t i = 0; i < nl; ++i) {
+        const Param& p = ctx->params[i];
+        StateDesc& d = descs[i];
+        d.m = (uint32_t)p.m;
+        d.n = (uint32_t)p.n;
+        d.rank = (uint32_t)p.r;
+        d.side = (uint32_t)p.side;
+        d.codec = (uint32_t)ctx->cfg.state_codec;
+        d.block = (uint32_t)ctx->cfg.state_block;
+        d.state_elems = (uint64_t)p.state_elems;
+        d.byte_offset = off;
+        const uint64_t s = p.side == 1 ? p.m : p.n;
+        off += ref ? state_section_v2(p.m, p.n, p.r) : state_section_v3(s, p.r, p.state_elems, p.state_blocks);
+    }
+    h.total_size = off;
+    std::vector<uint8_t> head(kStateHeaderSize + (size_t)nl * dsz, 0);
+    encode_state_header(h, head);
+    for (uint32_t i = 0; i < nl; ++i) {
+        const size_t b = kStateHeaderSize + (size_t)i * dsz;
+        const StateDesc& d = descs[i];
+        if (ref) {
+            put_le(head, b, d.m);
+            put_le(head, b + 4, d.n);
+            put_le(head, b + 8, d.rank);
+            put_le(head, b + 12, d.byte_offset);
+        } else {
+            put_le(head, b, d.m);
+            put_le(head, b + 4, d.n);
+            put_le(head, b + 8, d.rank);
+            put_le(head, b + 12, d.side);
+            put_le(head, b + 16, d.codec);
+            put_le(head, b + 20, d.block);
+            put_le(head, b + 24, d.state_elems);
+            put_le(head, b + 32, d.byte_offset);
+        }
+    }
+    FileCloser fc;
+    fc.f = fopen(path, "wb");
+    if (!fc.f) return set_err(AETH_ERR_CONFIG);
+    if (fwrite(head.data(), 1, head.size(), fc.f) != head.size()) return set_err(AETH_ERR_CONFIG);
+    std::vector<float> pf, qf, ms, vs;
+    std::vector<uint16_t> pb;
+    std::vector<int8_t> m8, v8;
+    for (uint32_t i = 0; i < nl; ++i) {
+        const Param& p = ctx->params[i];
+        std::vector<uint8_t> sec;
+        if (ref) {
+            AETH_TRY(d2h(pf, p.P, (size_t)p.m * p.r, st));
+            AETH_TRY(d2h(qf, p.Q, (size_t)p.n * p.r, st));
+        } else {
+            AETH_TRY(d2h(pb, p.proj, (size_t)(p.side == 1 ? p.m : p.n) * p.r, st));
+        }
+        AETH_TRY(d2h(m8, p.m8, (size_t)p.state_elems, st));
+        AETH_TRY(d2h(v8, p.v8, (size_t)p.state_elems, st));
+        AETH_TRY(d2h(ms, p.mscale, (size_t)p.state_blocks, st));
+        AETH_TRY(d2h(vs, p.vscale, (size_t)p.state_blocks, st));
+        AETH_CUDA(cudaStreamSynchronize(st));
+        if (ref) {
+            // P f16, Q f16, momentum, variance, scale_m, scale_v (state_file.rs:484-527)
+            std::vector<uint16_t> ph(pf.size()), qh(qf.size());
+            for (size_t k = 0; k < pf.size(); ++k) ph[k] = galore_f32_to_f16(pf[k]);
+            for (size_t k = 0; k < qf.size(); ++k) qh[k] = galore_f32_to_f16(qf[k]);
+            bool ok = fwrite(ph.data(), 2, ph.size(), fc.f) == ph.size() && fwrite(qh.data(), 2, qh.size(), fc.f) == qh.size();
+            ok = ok && fwrite(m8.data(), 1, m8.size(), fc.f) == m8.size() && fwrite(v8.data(), 1, v8.size(), fc.f) == v8.size();
+            ok = ok && fwrite(ms.data(), 4, 1, fc.f) == 1 && fwrite(vs.data(), 4, 1, fc.f) == 1;
+            if (!ok) return set_err(AETH_ERR_CONFIG);
+        } else {
+            bool ok = fwrite(pb.data(), 2, pb.size(), fc.f) == pb.size();
+            ok = ok && fwrite(m8.data(), 1, m8.size(), fc.f) == m8.size() && fwrite(v8.data(), 1, v8.size(), fc.f) == v8.size();
+            ok = ok && fwrite(ms.data(), 4, ms.size(), fc.f) == ms.size() && fwrite(vs.data(), 4, vs.size(), fc.f) == vs.size();
+            if (!ok) return set_err(AETH_ERR_CONFIG);
+        }
+    }
+    if (fflush(fc.f) != 0) return set_err(AETH_ERR_CONFIG);
+    return AETH_OK;
+}
+
+int aeth_galore_load_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t stream) {
+    if (!ctx || !path) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    const bool ref = ctx->cfg.mode == AETH_MODE_REF;
+    std::vector<uint8_t> buf;
+    {
+        FileCloser fc;
+        fc.f = fopen(path, "rb");
+        if (!fc.f) return set_err(AETH_ERR_NOT_FOUND);
+        if (fseek(fc.f, 0, SEEK_END) != 0) return set_err(AETH_ERR_CONFIG);
+        const long len = ftell(fc.f);
+        if (len < (long)kStateHeaderSize || fseek(fc.f, 0, SEEK_SET) != 0) return set_err(AETH_ERR_CONFIG);
+        buf.resize((size_t)len);
+        if (fread(buf.data(), 1, buf.size(), fc.f) != buf.size()) return set_err(AETH_ERR_CONFIG);
+    }
+    const StateHeader h = decode_state_header(buf.data());
+    // version 1 files (16-byte descriptors, no hyperparameters) read as the reference does
+    const bool v1 = h.version < 2;
+    if (h.magic != kStateMagic || (ref ? h.version > 2 : h.version != 3)) return set_err(AETH_ERR_CONFIG);
+    const uint32_t nl = (uint32_t)ctx->params.size();
+    if (h.num_layers != nl) return set_err(AETH_ERR_SHAPE);
+    const uint32_t dsz = ref ? (v1 ? 16u : kStateDescV2) : kStateDescV3;
+    if (buf.size() < kStateHeaderSize + (size_t)nl * dsz) return set_err(AETH_ERR_CONFIG);
+    std::vector<StateDesc> descs(nl);
+    for (uint32_t i = 0; i < nl; ++i) {
+        const uint8_t* b = buf.data() + kStateHeaderSize + (size_t)i * dsz;
+        StateDesc& d = descs[i];
+        d.m = get_le<uint32_t>(b);
+        d.n = get_le<uint32_t>(b + 4);
+        if (ref) {
+            d.rank = v1 ? h.rank : get_le<uint32_t>(b + 8);
+            d.byte_offset = get_le<uint64_t>(b + (v1 ? 8 : 12));
+        } else {
+            d.rank = get_le<uint32_t>(b + 8);
+            d.side = get_le<uint32_t>(b + 12);
+            d.codec = get_le<uint32_t>(b + 16);
+            d.block = get_le<uint32_t>(b + 20);
+            d.state_elems = get_le<uint64_t>(b + 24);
+            d.byte_offset = get_le<uint64_t>(b + 32);
+        }
+        const Param& p = ctx->params[i];
+        if (d.m != (uint32_t)p.m || d.n != (uint32_t)p.n || d.rank != (uint32_t)p.r) return set_err(AETH_ERR_SHAPE);
+        if (!ref && (d.side != (uint32_t)p.side || d.codec != (uint32_t)ctx->cfg.state_codec ||
+                     d.block != (uint32_t)ctx->cfg.state_block || d.state_elems != (uint64_t)p.state_elems))
+            return set_err(AETH_ERR_SHAPE);
+        const uint64_t s = p.side == 1 ? p.m : p.n;
+        const uint64_t need = ref ? state_section_v2(p.m, p.n, p.r) : state_section_v3(s, p.r, p.state_elems, p.state_blocks);
+        if (d.byte_offset + need > buf.size()) return set_err(AETH_ERR_CONFIG);
+    }
+    // Stage every section on the device, then install.
+    for (uint32_t i = 0; i < nl; ++i) {
+        Param& p = ctx->params[i];
+        const uint8_t* b = buf.data() + descs[i].byte_offset;
+        const size_t elems = (size_t)p.state_elems, blocks = (size_t)p.state_blocks;
+        if (ref) {
+            std::vector<float> pf((size_t)p.m * p.r), qf((size_t)p.n * p.r);
+            for (size_t k = 0; k < pf.size(); ++k) pf[k] = galore_f16_to_f32(get_le<uint16_t>(b + 2 * k));
+            b += 2 * pf.size();
+            for (size_t k = 0; k < qf.size(); ++k) qf[k] = galore_f16_to_f32(get_le<uint16_t>(b + 2 * k));
+            b += 2 * qf.size();
+            AETH_CUDA(cudaMemcpyAsync(p.P, pf.data(), pf.size() * 4, cudaMemcpyHostToDevice, st));
+            AETH_CUDA(cudaMemcpyAsync(p.Q, qf.data(), qf.size() * 4, cudaMemcpyHostToDevice, st));
+            AETH_CUDA(cudaStreamSynchronize(st));  // the host vectors go out of scope
+        } else {
+            const int s_dim = p.side == 1 ? p.m : p.n;
+            std::vector<float> pf((size_t)s_dim * p.r);
+            for (size_t k = 0; k < pf.size(); ++k) pf[k] = bf16_bits_to_f32_host(get_le<uint16_t>(b + 2 * k));
+            b += 2 * pf.size();
+            float* tmp = nullptr;
+            AETH_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tmp), pf.size() * 4, st));
+            cudaError_t e = cudaMemcpyAsync(tmp, pf.data(), pf.size() * 4, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess) {
+                proj_to_bf16_kernel<<<grid_for((int64_t)s_dim * p.r, 256), 256, 0, st>>>(tmp, s_dim, p.r, p.proj,
+                                                                                          p.projT);
+                e = cudaGetLastError();
+            }
+            cudaFreeAsync(tmp, st);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            AETH_CUDA(e);
+        }
+        AETH_CUDA(cudaMemcpyAsync(p.m8, b, elems, cudaMemcpyHostToDevice, st));
+        AETH_CUDA(cudaMemcpyAsync(p.v8, b + elems, elems, cudaMemcpyHostToDevice, st));
+        AETH_CUDA(cudaMemcpyAsync(p.mscale, b + 2 * elems, blocks * 4, cudaMemcpyHostToDevice, st));
+        AETH_CUDA(cudaMemcpyAsync(p.vscale, b + 2 * elems + blocks * 4, blocks * 4, cudaMemcpyHostToDevice, st));
+        AETH_CUDA(cudaMemsetAsync(p.accum, 0, (size_t)p.state_elems * sizeof(float), st));  // new grad_accum
+        drop_capture(p, st);
+    }
+    AETH_CUDA(cudaStreamSynchronize(st));  // buf is read by the copies above
+    // OptimizerStateFile::open adopts the header's step and Adam constants
+    // (optimizer.rs:136-143); version 1 files carry neither.
+    ctx->step = v1 ? 0 : h.step_count;
+    if (!v1) {
+        ctx->cfg.beta1 = h.beta1;
+        ctx->cfg.beta2 = h.beta2;
+        ctx->cfg.eps = h.eps;
+    }
+    return AETH_OK;
+}
 
 int aeth_randomized_svd(const float* g, int m, int n, int rank, int oversampling, int power_iters, uint64_t seed,
                         float* p_out, float* q_out, aeth_stream_t stream) {

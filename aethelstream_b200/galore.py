@@ -282,6 +282,18 @@ class GaLoreOptimizer:
         """Completed subspace refreshes (optimizer.rs:249-253)."""
         return int(self._lib.aeth_galore_version(self._ctx))
 
+    def save_state(self, path) -> None:
+        """flush_all_to_file (optimizer.rs:180-192) to `path`: the reference's
+        version 2 layout in REF mode, version 3 in B200 mode."""
+        L.check(self._lib.aeth_galore_save_state(self._ctx, str(path).encode(), C.c_void_p(_stream_handle())),
+                "save_state")
+
+    def load_state(self, path) -> None:
+        """The state part of GaLoreOptimizer::open (optimizer.rs:135-176): projectors,
+        INT8 m/v and scales, step count and Adam constants from `path`."""
+        L.check(self._lib.aeth_galore_load_state(self._ctx, str(path).encode(), C.c_void_p(_stream_handle())),
+                "load_state")
+
     def projector_kind(self, layer_idx: int, param_name: str) -> ProjectorKind:
         return ProjectorKind.ORTHONORMAL
 

@@ -228,6 +228,23 @@ uint64_t aeth_galore_step_count(const aeth_galore_ctx* ctx);
 /* optimizer_version (optimizer.rs:249-253): subspace refreshes completed. */
 uint64_t aeth_galore_version(const aeth_galore_ctx* ctx);
 
+/* optimizer_states.bin (galore/src/state_file.rs:1-580; flush_all_to_file,
+ * optimizer.rs:180-192; GaLoreOptimizer::open, :135-176).  REF mode writes
+ * and reads the reference's version 2 byte for byte: P and Q as FP16 through
+ * galore's own conversion (project.rs:135-185), INT8 m/v, one scale each, the
+ * Adam constants and the step count in the header; layers in parameter order.
+ * Loading also reads version 1 files.  B200 mode writes version 3 (no
+ * reference counterpart), which keeps the one-sided state losslessly: the bf16
+ * projector of the parameter's side, INT8 m/v and their block scales.
+ * load_state checks every layer's m, n and rank (and, for version 3, side,
+ * codec, block and state size) against the context (AETH_ERR_SHAPE), installs
+ * the state, zeroes the accumulators, and adopts the file's step count and
+ * beta1, beta2, eps, as the reference's open does.  Both wait on `stream`.
+ * Status: AETH_ERR_NOT_FOUND when the file cannot be opened, AETH_ERR_CONFIG
+ * for I/O failures or a bad magic / version. */
+int aeth_galore_save_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t stream);
+int aeth_galore_load_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t stream);
+
 /* Device randomized SVD, K8 (randomized_svd_projections, randomized_svd.rs:
  * 76-149; the reference's device entry point randomized_svd_on_device,
  * :282-298, routes to an unimplemented kernel).  g: m x n f32 row-major;

@@ -308,6 +308,44 @@ int ref_should_switch(uint64_t step, uint64_t interval) {
     return interval > 0 && step > 0 && (step % interval) == 0;
 }
 
+/* galore's own half conversion (galore/src/project.rs:135-185), used by the
+ * state file for P and Q: add half an ulp and truncate, carry ORed into the
+ * exponent, NaN payload truncated. */
+uint16_t ref_galore_f32_to_f16(float x) {
+    uint32_t bits = f2u(x);
+    uint16_t sign = (uint16_t)((bits >> 16) & 0x8000u);
+    int exp = (int)((bits >> 23) & 0xffu);
+    uint32_t frac = bits & 0x7fffffu;
+    if (exp == 0xff) return (uint16_t)(sign | 0x7c00u | ((frac >> 13) & 0x3ffu));
+    int new_exp = exp - 127 + 15;
+    if (new_exp >= 0x1f) return (uint16_t)(sign | 0x7c00u);
+    if (new_exp <= 0) {
+        if (new_exp < -10) return sign;
+        uint32_t mant = (frac | 0x800000u) >> (1 - new_exp);
+        return (uint16_t)(sign | (uint16_t)((mant + 0x1000u) >> 13));
+    }
+    return (uint16_t)(sign | (uint16_t)(new_exp << 10) | (uint16_t)((frac + 0x1000u) >> 13));
+}
+
+float ref_galore_f16_to_f32(uint16_t h) {
+    uint32_t sign = h & 0x8000u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu, bits;
+    if (exp == 0) {
+        if (frac == 0) {
+            bits = sign << 16;
+        } else {
+            uint32_t e = 0;
+            while ((frac & 0x400u) == 0) { frac <<= 1; e++; }
+            frac &= 0x3ffu;
+            bits = (sign << 16) | ((127 - 15 - e) << 23) | (frac << 13);
+        }
+    } else if (exp == 0x1f) {
+        bits = (sign << 16) | 0x7f800000u | (frac << 13);
+    } else {
+        bits = (sign << 16) | ((exp + 127 - 15) << 23) | (frac << 13);
+    }
+    return u2f(bits);
+}
+
 /* ---------------------------------------------------------------------------
  * Randomized SVD subspace refresh (galore/src/randomized_svd.rs:38-271).
  * ------------------------------------------------------------------------- */

@@ -82,6 +82,9 @@ float ref_clip_coeff(double gsq, float max_norm);
 double ref_sqnorm_f64(const float* x, int64_t n);
 /* should_switch_subspace (galore/src/randomized_svd.rs:273-276) */
 int ref_should_switch(uint64_t step, uint64_t interval);
+/* galore's half conversion for the state file (galore/src/project.rs:135-185). */
+uint16_t ref_galore_f32_to_f16(float x);
+float ref_galore_f16_to_f32(uint16_t h);
 /* Randomized SVD refresh (galore/src/randomized_svd.rs:38-271). */
 float ref_rsvd_gaussian(uint64_t* state);
 void ref_rsvd_omega(uint64_t seed, int64_t count, float* out);

@@ -66,6 +66,8 @@ def lib():
             "ref_clip_coeff": (C.c_float, [C.c_double, C.c_float]),
             "ref_sqnorm_f64": (C.c_double, [_f32p, C.c_int64]),
             "ref_should_switch": (C.c_int, [C.c_uint64, C.c_uint64]),
+            "ref_galore_f32_to_f16": (C.c_uint16, [C.c_float]),
+            "ref_galore_f16_to_f32": (C.c_float, [C.c_uint16]),
             "ref_rsvd_omega": (None, [C.c_uint64, C.c_int64, _f32p]),
             "ref_rsvd_jacobi": (None, [_f32p, C.c_int, _f32p]),
             "ref_randomized_svd": (C.c_int, [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, _f32p, _f32p]),
@@ -426,3 +428,16 @@ def lomo_update(g_bits, clip, beta, lr, block, codec, mom8, mom_scales, w_packed
     lib().b2_lomo_update(g, n, clip, beta, lr, block, codec, mom8, ms, _c(w_packed, np.uint8).ravel(),
                          _c(w_absmax, np.float32).ravel(), wp, wa, _ptr(pre))
     return mom8, ms, wp, wa, pre
+
+
+def galore_f32_to_f16(x):
+    """galore's half conversion of the state file (project.rs:137-158), elementwise bits."""
+    x = np.asarray(x, np.float32).ravel()
+    f = lib().ref_galore_f32_to_f16
+    return np.array([f(float(v)) for v in x], np.uint16)
+
+
+def galore_f16_to_f32(h):
+    h = np.asarray(h, np.uint16).ravel()
+    f = lib().ref_galore_f16_to_f32
+    return np.array([f(int(v)) for v in h], np.float32)
