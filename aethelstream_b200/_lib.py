@@ -21,6 +21,11 @@ AETH_ERR_NOT_FOUND = -5
 AETH_ERR_TIMEOUT = -6
 AETH_ERR_LINALG = -7
 
+# bits of the device error word (aeth_device_error_bits)
+DEVERR_TIMEOUT_TMA, DEVERR_TIMEOUT_MMA, DEVERR_TIMEOUT_EPI = 1, 2, 4
+DEVERR_BAD_ARG, DEVERR_TIMEOUT_PEER = 8, 16
+CLIP_HANDLE_BYTES = 64
+
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 MODE_REF, MODE_B200 = 0, 1
 CODEC_PER_TENSOR, CODEC_BLOCK_LINEAR, CODEC_BLOCK_DYNAMIC = 0, 1, 2
@@ -89,6 +94,10 @@ SIGNATURES = {
                               _vp]),
     "aeth_galore_set_phase_timing": (_i, [_vp, _i]),
     "aeth_galore_phase_times": (_i, [_vp, C.POINTER(_d), C.POINTER(_i)]),
+    "aeth_galore_clip_handle": (_i, [_vp, _i, _vp]),
+    "aeth_galore_set_clip_group": (_i, [_vp, _i, _i, _vp, _u64]),
+    "aeth_galore_set_clip_group_ptrs": (_i, [_vp, _i, _i, C.POINTER(_vp), _u64]),
+    "aeth_galore_clip_slots": (_i, [_vp, C.POINTER(_vp)]),
     "aeth_galore_set_projector": (_i, [_vp, _i, _vp, _vp, _vp]),
     "aeth_galore_get_projector": (_i, [_vp, _i, _vp, _vp, _vp]),
     "aeth_galore_get_state": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp]),
@@ -105,6 +114,7 @@ SIGNATURES = {
     "aeth_status_string": (C.c_char_p, [_i]),
     "aeth_last_error": (_i, []),
     "aeth_device_error": (_i, [_i]),
+    "aeth_device_error_bits": (_i, [_i, C.POINTER(C.c_uint32)]),
     "aeth_version": (C.c_char_p, []),
 }
 
@@ -148,3 +158,11 @@ def check(st: int, what: str = "aeth call"):
     if st != AETH_OK:
         raise AethError(st, what)
     return st
+
+
+def device_error_bits(device: int) -> int:
+    """Reads and clears the device error word of `device` (synchronises it):
+    the DEVERR_* bits of the bounded waits that gave up."""
+    v = C.c_uint32(0)
+    check(load().aeth_device_error_bits(device, C.byref(v)), "aeth_device_error_bits")
+    return int(v.value)

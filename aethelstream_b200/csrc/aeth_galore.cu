@@ -237,6 +237,11 @@ struct aeth_galore_ctx {
     unsigned int* sq_ticket = nullptr;  // sqnorm_group's completion counter, zero between launches
     unsigned int* work = nullptr;       // b2_adam_group_kernel's block counters, zero between launches
     uint64_t version = 0;               // completed subspace refreshes (optimizer_version)
+    // global clip over several GPUs through peer memory (aeth_galore_set_clip_group)
+    ClipGroup group;
+    PeerSlot* own_slots = nullptr;      // 2 x world entries, cudaMalloc'd (exported by IPC handle)
+    int own_slots_world = 0;
+    std::vector<void*> peer_maps;       // IPC mappings of the other ranks' slots
     std::vector<void*> allocs;
     // aeth_galore_set_phase_timing: five events per step (phase boundaries)
     bool phase_timing = false;
@@ -660,7 +665,8 @@ const char* aeth_status_string(int st) {
 
 int aeth_last_error(void) { return tl_last_error; }
 
-int aeth_device_error(int device) {
+int aeth_device_error_bits(int device, uint32_t* bits) {
+    if (!bits) return set_err(AETH_ERR_ARG);
     DeviceGuard g(device);
     DeviceRuntime* rt = nullptr;
     AETH_TRY(runtime_for_current(&rt));
@@ -668,6 +674,13 @@ int aeth_device_error(int device) {
     uint32_t v = 0;
     AETH_CUDA(cudaMemcpy(&v, rt->err_word, sizeof(v), cudaMemcpyDeviceToHost));
     AETH_CUDA(cudaMemset(rt->err_word, 0, sizeof(uint32_t)));
+    *bits = v;
+    return AETH_OK;
+}
+
+int aeth_device_error(int device) {
+    uint32_t v = 0;
+    AETH_TRY(aeth_device_error_bits(device, &v));
     return v ? AETH_ERR_TIMEOUT : AETH_OK;
 }
 
@@ -910,6 +923,8 @@ int aeth_galore_destroy(aeth_galore_ctx* ctx) {
         if (p.gbf) cudaFree(p.gbf);
     for (Param& p : ctx->params)
         if (p.capture) cudaFree(p.capture);
+    for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+    if (ctx->own_slots) cudaFree(ctx->own_slots);
     delete ctx;
     return AETH_OK;
 }
@@ -1422,10 +1437,13 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     for (int i = 0; i < n; ++i) { xs[i] = ctx->params[idx[i]].accum; ns[i] = ctx->params[idx[i]].state_elems; }
     AETH_TRY(pm.mark(1, st));
     // Without a hook the norms and the clip coefficient come from one launch.
+    // With a clip group the same launch also exchanges the sum with the peers.
+    const bool grouped = ctx->group.world > 1;
+    if (grouped && (sq_hook || n > kSqGroupMax)) return set_err(grouped && sq_hook ? AETH_ERR_ARG : AETH_ERR_UNSUPPORTED);
     const bool fuse_clip = !sq_hook && n <= kSqGroupMax;
     AETH_TRY(sqnorm_group(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, ctx->sq_ticket,
                           ctx->cfg.max_grad_norm, fuse_clip ? clip : nullptr, fuse_clip ? ctx->gnorm_dev : nullptr,
-                          st));
+                          st, grouped ? &ctx->group : nullptr));
     if (!fuse_clip) {
         if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
         clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
@@ -1453,6 +1471,93 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     AETH_TRY(pm.mark(4, st));
     pm.commit();
     return AETH_OK;
+}
+
+int aeth_galore_clip_handle(aeth_galore_ctx* ctx, int world, void* handle_out) {
+    if (!ctx || !handle_out || world < 1 || world > kClipGroupMax) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    if (ctx->own_slots && ctx->own_slots_world != world) {
+        if (ctx->group.world > 1) return set_err(AETH_ERR_CONFIG);  // in use
+        cudaFree(ctx->own_slots);
+        ctx->own_slots = nullptr;
+    }
+    if (!ctx->own_slots) {
+        const size_t bytes = sizeof(PeerSlot) * 2 * (size_t)world;
+        AETH_CUDA(cudaMalloc(reinterpret_cast<void**>(&ctx->own_slots), bytes));
+        ctx->own_slots_world = world;
+        AETH_CUDA(cudaMemset(ctx->own_slots, 0, bytes));
+        AETH_CUDA(cudaDeviceSynchronize());
+    }
+    cudaIpcMemHandle_t h;
+    AETH_CUDA(cudaIpcGetMemHandle(&h, ctx->own_slots));
+    memcpy(handle_out, &h, sizeof(h));
+    return AETH_OK;
+}
+
+int aeth_galore_set_clip_group(aeth_galore_ctx* ctx, int rank, int world, const void* handles, uint64_t timeout_ns) {
+    if (!ctx || world < 1 || world > kClipGroupMax || rank < 0 || rank >= world) return set_err(AETH_ERR_ARG);
+    if (ctx->cfg.mode != AETH_MODE_B200) return set_err(AETH_ERR_UNSUPPORTED);
+    DeviceGuard g(ctx->device);
+    for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+    ctx->peer_maps.clear();
+    ctx->group = ClipGroup();
+    if (world == 1) return AETH_OK;
+    if (!handles || !ctx->own_slots || ctx->own_slots_world != world) return set_err(AETH_ERR_CONFIG);
+    // fresh slots: epochs restart at 1 (the ranks meet at a barrier after this)
+    AETH_CUDA(cudaMemset(ctx->own_slots, 0, sizeof(PeerSlot) * 2 * (size_t)world));
+    AETH_CUDA(cudaDeviceSynchronize());
+    ClipGroup grp;
+    grp.rank = rank;
+    grp.world = world;
+    grp.timeout_ns = timeout_ns ? timeout_ns : kWaitLimitNs;
+    for (int p = 0; p < world; ++p) {
+        if (p == rank) {
+            grp.slots[p] = ctx->own_slots;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)p * sizeof(h), sizeof(h));
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+            ctx->peer_maps.clear();
+            return set_err((int)e);
+        }
+        ctx->peer_maps.push_back(ptr);
+        grp.slots[p] = static_cast<PeerSlot*>(ptr);
+    }
+    ctx->group = grp;
+    return AETH_OK;
+}
+
+int aeth_galore_set_clip_group_ptrs(aeth_galore_ctx* ctx, int rank, int world, void* const* slots,
+                                    uint64_t timeout_ns) {
+    if (!ctx || world < 2 || world > kClipGroupMax || rank < 0 || rank >= world || !slots) return set_err(AETH_ERR_ARG);
+    if (ctx->cfg.mode != AETH_MODE_B200) return set_err(AETH_ERR_UNSUPPORTED);
+    if (!ctx->own_slots || ctx->own_slots_world != world || slots[rank] != ctx->own_slots)
+        return set_err(AETH_ERR_CONFIG);
+    for (int p = 0; p < world; ++p)
+        if (!slots[p]) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+    ctx->peer_maps.clear();
+    ctx->group = ClipGroup();
+    AETH_CUDA(cudaMemset(ctx->own_slots, 0, sizeof(PeerSlot) * 2 * (size_t)world));
+    AETH_CUDA(cudaDeviceSynchronize());
+    ClipGroup grp;
+    grp.rank = rank;
+    grp.world = world;
+    grp.timeout_ns = timeout_ns ? timeout_ns : kWaitLimitNs;
+    for (int p = 0; p < world; ++p) grp.slots[p] = static_cast<PeerSlot*>(slots[p]);
+    ctx->group = grp;
+    return AETH_OK;
+}
+
+int aeth_galore_clip_slots(aeth_galore_ctx* ctx, void** slots_out) {
+    if (!ctx || !slots_out) return set_err(AETH_ERR_ARG);
+    *slots_out = ctx->own_slots;
+    return ctx->own_slots ? AETH_OK : set_err(AETH_ERR_CONFIG);
 }
 
 int aeth_galore_set_phase_timing(aeth_galore_ctx* ctx, int enable) {

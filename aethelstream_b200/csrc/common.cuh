@@ -44,7 +44,13 @@ inline cudaStream_t to_stream(aeth_stream_t s) { return reinterpret_cast<cudaStr
 // and OR a code into this word instead of hanging; the host reads it with
 // aeth_device_error().  One word per device, allocated on first use.
 // ---------------------------------------------------------------------------
-enum : uint32_t { DEVERR_TIMEOUT_TMA = 1u, DEVERR_TIMEOUT_MMA = 2u, DEVERR_TIMEOUT_EPI = 4u, DEVERR_BAD_ARG = 8u };
+enum : uint32_t {
+    DEVERR_TIMEOUT_TMA = 1u,
+    DEVERR_TIMEOUT_MMA = 2u,
+    DEVERR_TIMEOUT_EPI = 4u,
+    DEVERR_BAD_ARG = 8u,
+    DEVERR_TIMEOUT_PEER = 16u,  // a peer GPU's squared-norm sum did not arrive in time
+};
 
 struct DeviceRuntime {
     uint32_t* err_word = nullptr;  // device

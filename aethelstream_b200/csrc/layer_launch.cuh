@@ -111,6 +111,20 @@ inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t 
 // ---------------------------------------------------------------------------
 constexpr int kSqGroupMax = 16;
 constexpr int kSqChunks = 128;
+constexpr int kClipGroupMax = 16;  // GPUs in a clip group
+
+struct PeerSlot {
+    double sum;
+    uint64_t epoch;
+};
+
+// A group of GPUs that share one global clip through peer memory.
+struct ClipGroup {
+    int rank = 0, world = 1;
+    PeerSlot* slots[kClipGroupMax] = {};
+    uint64_t epoch = 0;
+    uint64_t timeout_ns = kWaitLimitNs;
+};
 
 struct SqGroupArgs {
     const float* x[kSqGroupMax];
@@ -122,7 +136,51 @@ struct SqGroupArgs {
     double* out;           // np sums
     double* partials;      // kSqGroupMax * kSqChunks
     unsigned int* ticket;  // zero between launches
+    // Exchange of the local sum with the other GPUs of a clip group (world > 1):
+    // slots[p] is rank p's slot buffer (peer memory for p != rank), laid out as
+    // [parity][world] entries of {double sum, uint64 epoch}.
+    PeerSlot* slots[kClipGroupMax];
+    int rank, world;
+    uint64_t epoch;
+    uint64_t timeout_ns;
+    uint32_t* err;
 };
+
+// Peer exchange primitives: a release store of the epoch after the value, an
+// acquire load on the reader's side, both at system scope (NVLink peers).
+__device__ __forceinline__ void st_release_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Writes this rank's sum into every group member's slot for this epoch, waits
+// (bounded) for every member's sum, and returns the total in rank order, so
+// every rank gets the same bits.  On timeout: flags the error and returns NaN.
+__device__ inline double clip_group_total(const SqGroupArgs& a, double local) {
+    const int par = (int)(a.epoch & 1u);
+    for (int p = 0; p < a.world; ++p) {
+        PeerSlot* s = a.slots[p] + par * a.world + a.rank;
+        s->sum = local;
+        st_release_sys_u64(&s->epoch, a.epoch);
+    }
+    double total = 0.0;
+    const uint64_t t0 = global_ns();
+    for (int p = 0; p < a.world; ++p) {
+        PeerSlot* s = a.slots[a.rank] + par * a.world + p;
+        while (ld_acquire_sys_u64(&s->epoch) != a.epoch) {
+            if (global_ns() - t0 > a.timeout_ns) {
+                report_dev_error(a.err, DEVERR_TIMEOUT_PEER);
+                return __longlong_as_double(0x7ff8000000000000ll);
+            }
+        }
+        total += *reinterpret_cast<volatile double*>(&s->sum);
+    }
+    return total;
+}
 
 __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant__ SqGroupArgs a) {
     __shared__ double red[8];
@@ -177,9 +235,12 @@ __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant
         if (a.clip_out) {
             double t = 0.0;
             for (int k = 0; k < a.np; ++k) t += a.out[k];
+            if (a.world > 1) t = clip_group_total(a, t);
             const double gnorm = sqrt(t);
             const float c = (float)((double)a.max_norm / (gnorm + 1e-6));
-            *a.clip_out = c < 1.0f ? c : 1.0f;
+            // a missing peer: this step's gradients are dropped (clip 0); the
+            // error word tells the host, which restores the saved state
+            *a.clip_out = t != t ? 0.0f : (c < 1.0f ? c : 1.0f);
             if (a.gnorm_out) *a.gnorm_out = gnorm;
         }
         *a.ticket = 0u;
@@ -188,9 +249,15 @@ __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant
 
 // out[i] = sum of squares of xs[i] (f64).  With clip_out (np <= kSqGroupMax)
 // the same launch also writes the global clip coefficient for max_norm.
+// With a clip group of several GPUs the clip is computed from the sum over
+// the whole group (clip_group_total); group->epoch advances once per launch.
 inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, double* out, double* partials,
-                        unsigned int* ticket, float max_norm, float* clip_out, double* gnorm_out, cudaStream_t st) {
+                        unsigned int* ticket, float max_norm, float* clip_out, double* gnorm_out, cudaStream_t st,
+                        ClipGroup* group = nullptr) {
     if (clip_out && np > kSqGroupMax) return AETH_ERR_UNSUPPORTED;
+    if (group && group->world > 1 && !clip_out) return AETH_ERR_ARG;
+    DeviceRuntime* rt = nullptr;
+    AETH_TRY(runtime_for_current(&rt));
     for (int off = 0; off < np; off += kSqGroupMax) {
         const int cnt = std::min(kSqGroupMax, np - off);
         SqGroupArgs a;
@@ -209,6 +276,15 @@ inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, doubl
         a.out = out + off;
         a.partials = partials;
         a.ticket = ticket;
+        a.world = 1;
+        a.err = rt->err_word;
+        if (group && group->world > 1) {
+            a.rank = group->rank;
+            a.world = group->world;
+            for (int p = 0; p < group->world; ++p) a.slots[p] = group->slots[p];
+            a.epoch = ++group->epoch;
+            a.timeout_ns = group->timeout_ns;
+        }
         // about 8K elements per CTA, at most kSqChunks chunks per accumulator
         const int chunks = (int)std::min<int64_t>(kSqChunks, std::max<int64_t>(1, (largest + 8191) / 8192));
         sqnorm_group_kernel<<<dim3(chunks, cnt), 256, 0, st>>>(a);

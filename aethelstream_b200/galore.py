@@ -399,6 +399,38 @@ class GaLoreOptimizer:
         L.check(self._lib.aeth_galore_phase_times(self._ctx, out, C.byref(steps)), "phase_times")
         return steps.value, dict(zip(self.PHASES, list(out)))
 
+    # ---- global clip over several GPUs through peer memory ----
+    def clip_handle(self, world: int) -> bytes:
+        """Allocates this optimizer's clip slots for a group of `world` GPUs and
+        returns their CUDA IPC handle (64 bytes) for the other ranks."""
+        buf = C.create_string_buffer(L.CLIP_HANDLE_BYTES)
+        L.check(self._lib.aeth_galore_clip_handle(self._ctx, world, buf), "clip_handle")
+        return buf.raw
+
+    def set_clip_group(self, rank: int, world: int, handles, timeout_s: float = 2.0) -> None:
+        """Joins the clip group: `handles` lists every rank's clip_handle() in
+        rank order.  All ranks must meet at a barrier after this call and
+        then call step_layer equally often, without sq_hook."""
+        blob = b"".join(handles) if world > 1 else b""
+        if world > 1 and len(blob) != world * L.CLIP_HANDLE_BYTES:
+            raise ValueError("set_clip_group: one 64-byte handle per rank expected")
+        buf = C.create_string_buffer(blob, max(len(blob), 1))
+        L.check(self._lib.aeth_galore_set_clip_group(self._ctx, rank, world, buf, int(timeout_s * 1e9)),
+                "set_clip_group")
+
+    def set_clip_group_ptrs(self, rank: int, slots, timeout_s: float = 2.0) -> None:
+        """Joins a clip group whose slot pointers the caller mapped itself
+        (`slots[rank]` must be clip_slots())."""
+        arr = (C.c_void_p * len(slots))(*slots)
+        L.check(self._lib.aeth_galore_set_clip_group_ptrs(self._ctx, rank, len(slots), arr, int(timeout_s * 1e9)),
+                "set_clip_group_ptrs")
+
+    def clip_slots(self) -> int:
+        """Device address of this optimizer's clip slots (after clip_handle)."""
+        p = C.c_void_p()
+        L.check(self._lib.aeth_galore_clip_slots(self._ctx, C.byref(p)), "clip_slots")
+        return int(p.value)
+
 
 def _wrap_device_doubles(ptr: int, count: int, device: int) -> torch.Tensor:
     """A torch view of `count` device doubles owned by the library (no copy)."""

@@ -5,11 +5,13 @@ rank ``li % world_size`` and every rank keeps the NF4 weights, projectors and
 INT8 state of its own layers only.  The path has exactly two exchanges:
 
 1. the exact global-norm clip needs the sum of all ranks' low-rank squared
-   norms (doublepass/src/hook.rs:149-186): one f64 all-reduce per step;
+   norms (doublepass/src/hook.rs:149-186).  On B200s the squared-norm kernel
+   exchanges it itself: every rank stores its sum into a slot on each peer
+   GPU over NVLink and reads theirs (``setup_clip_group``), inside the launch
+   that computes the norms.  ``allreduce_sqnorm_hook`` is the alternative
+   through a ``torch.distributed`` all-reduce (NCCL, or gloo on CPU);
 2. a refreshed projector is broadcast from its owner (only to ranks that hold
    a replica; with exclusive sharding it is still timed).
-
-Both go through ``torch.distributed`` (NCCL over NVLink on GPUs, gloo on CPU).
 """
 from __future__ import annotations
 
@@ -24,6 +26,42 @@ def layer_owner(layer_idx: int, world_size: int) -> int:
 
 def owned_layers(n_layers: int, rank: int, world_size: int) -> list[int]:
     return [li for li in range(n_layers) if layer_owner(li, world_size) == rank]
+
+
+def setup_clip_group(optimizer, group=None, timeout_s: float = 2.0) -> bool:
+    """Joins every rank's optimizer into one peer-memory clip group: each
+    rank allocates its slots and publishes their IPC handle, the handles are
+    gathered in rank order, each rank opens its peers' slots, and the ranks
+    agree on the outcome (the agreement doubles as the barrier the group
+    needs before its first step).  Returns True when every rank joined;
+    otherwise every rank leaves the group and the caller exchanges the norms
+    another way (``allreduce_sqnorm_hook``).  Every rank takes the same
+    collective steps on either outcome."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    if world == 1:
+        optimizer.set_clip_group(0, 1, [])
+        return True
+    try:
+        handle, err = optimizer.clip_handle(world), ""
+    except Exception as e:  # noqa: BLE001 - reported to every rank below
+        handle, err = b"", repr(e)
+    handles: list = [None] * world
+    dist.all_gather_object(handles, handle, group=group)
+    if not err:
+        try:
+            if any(not h for h in handles):
+                raise RuntimeError("a rank has no clip handle")
+            optimizer.set_clip_group(rank, world, handles, timeout_s)
+        except Exception as e:  # noqa: BLE001 - reported to every rank below
+            err = repr(e)
+    outcomes: list = [None] * world
+    dist.all_gather_object(outcomes, err, group=group)
+    if any(outcomes):
+        if not err:
+            optimizer.set_clip_group(0, 1, [])
+        return False
+    return True
 
 
 def allreduce_sqnorm_hook(group=None):

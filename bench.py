@@ -233,7 +233,8 @@ def run_b200(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     from aethelstream_b200 import GaLoreConfig, GaLoreOptimizer, LayerRankConfig, nf4_quantize
-    from aethelstream_b200.sharding import allreduce_sqnorm_hook
+    from aethelstream_b200 import _lib
+    from aethelstream_b200.sharding import allreduce_sqnorm_hook, setup_clip_group
 
     dev = torch.device("cuda", local)
     layer = rank  # weak scaling: one block per rank (round-robin layer ownership)
@@ -258,9 +259,18 @@ def run_b200(args):
         ring.append(gs)
     keys = [(layer, name) for name, _, _ in SHAPES]
     stream = torch.cuda.current_stream()
-    # One GPU: no hook, so the squared norms and the clip come from one launch.
-    # Several GPUs: the hook all-reduces the per-matrix squared norms (8 B each).
-    hook = allreduce_sqnorm_hook() if world > 1 else None
+    # One GPU: the squared norms and the clip come from one launch.  Several
+    # GPUs: that launch also exchanges the local sum with the peer GPUs over
+    # NVLink (peer clip group); if the group cannot be set up, an NCCL
+    # all-reduce hook between the norm and Adam phases does it instead.
+    hook = None
+    clip_exchange = "local (one GPU)"
+    if world > 1:
+        if setup_clip_group(opt, timeout_s=5.0):
+            clip_exchange = "peer memory: NVLink stores and acquire loads inside the squared-norm launch"
+        else:
+            hook = allreduce_sqnorm_hook()
+            clip_exchange = "NCCL all-reduce hook (peer clip group unavailable)"
 
     def step(s):
         return opt.step_layer(keys, ring[s % 2], weights, sq_hook=hook)
@@ -329,6 +339,9 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = params_per_step * world * k_e2e / (float(e2e_ms.item()) / 1000.0)
+    dev_err = _lib.device_error_bits(local)
+    if dev_err:
+        raise RuntimeError(f"a bounded device wait gave up during the bench (error bits {dev_err:#x})")
 
     if rank == 0:
         hbm, tflops, tflops_sus, peak_kind = load_peaks()
@@ -349,6 +362,7 @@ def run_b200(args):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) bf16 grads)",
             "config": {"workload": WORKLOAD, "params_per_gpu_step": params_per_step, "rank": RANK,
                        "state": "int8 dynamic-map, 2048-element blocks", "parallelism": f"layer-sharded x{world}",
+                       "clip_exchange": clip_exchange,
                        "l2": (f"inputs larger than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients per "
                               "step, 2-deep ring)") if 2 * params_per_step > 126e6 else
                              f"inputs smaller than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients)"},
@@ -364,8 +378,9 @@ def run_b200(args):
                               "host_enqueue_ms_per_step": host_ms},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                     "steps": k_e2e},
-            # per step: grouped projection, sqnorm (+ clip with the multi-GPU hook), grouped Adam, grouped apply
-            "gpu_launches": (4 if world == 1 else 5) * args.steps,
+            # per step: grouped projection, sqnorm + clip (+ peer exchange), grouped Adam, grouped apply;
+            # the NCCL hook adds the clip kernel
+            "gpu_launches": (5 if hook is not None else 4) * args.steps,
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:

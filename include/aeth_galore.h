@@ -284,6 +284,33 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
 int aeth_galore_set_phase_timing(aeth_galore_ctx* ctx, int enable);
 int aeth_galore_phase_times(aeth_galore_ctx* ctx, double ms_out[4], int* steps);
 
+/* Global clip over a group of GPUs through peer memory (B200 mode; replaces
+ * the f64 all-reduce of hook.rs:149-186, no reference counterpart as an
+ * API).  Each rank's aeth_galore_step then computes its local sum of squared
+ * norms, writes it into a slot on every other rank's GPU (NVLink stores),
+ * waits for theirs and forms the clip from the total added in rank order, so
+ * every rank gets the same bits, all inside the one squared-norm launch.
+ *   aeth_galore_clip_handle allocates this context's slots for a group of
+ *   `world` GPUs (zeroed) and writes their 64-byte CUDA IPC handle;
+ *   aeth_galore_set_clip_group opens the other ranks' handles (`handles`:
+ *   world x 64 bytes in rank order) and zeroes the own slots.  world == 1
+ *   leaves the group.  After every rank's set_clip_group returned, the ranks
+ *   must meet at a host barrier before the first step; after that, every rank
+ *   calls aeth_galore_step the same number of times, without a hook.
+ *   aeth_galore_set_clip_group_ptrs takes the slot pointers directly (own
+ *   slots at `rank`, from aeth_galore_clip_slots), for callers that map the
+ *   peer memory themselves.
+ * Each wait is bounded by timeout_ns (0: two seconds).  When a peer's sum
+ * does not arrive, the step uses clip 0 (this step's gradients are dropped,
+ * the moments decay), AETH_DEVERR_TIMEOUT_PEER is set in the device error
+ * word, and the ranks' optimizer states may differ: the caller restores them
+ * from the last saved state. */
+int aeth_galore_clip_handle(aeth_galore_ctx* ctx, int world, void* handle_out);
+int aeth_galore_set_clip_group(aeth_galore_ctx* ctx, int rank, int world, const void* handles, uint64_t timeout_ns);
+int aeth_galore_set_clip_group_ptrs(aeth_galore_ctx* ctx, int rank, int world, void* const* slots,
+                                    uint64_t timeout_ns);
+int aeth_galore_clip_slots(aeth_galore_ctx* ctx, void** slots_out);
+
 /* Projector access.  REF: P (m x r) and Q (n x r).  B200: only the projector
  * of the chosen side (P for m < n, Q for m >= n; the other pointer is ignored).
  * fp32 device buffers.  set_projector resets the Adam state, as the subspace
@@ -351,6 +378,13 @@ int aeth_last_error(void);
 /* Reads and clears the device-side error word set by bounded waits on
  * `device` (synchronises the device).  Returns AETH_OK or AETH_ERR_TIMEOUT. */
 int aeth_device_error(int device);
+/* The same, returning the word's bits: which wait gave up. */
+#define AETH_DEVERR_TIMEOUT_TMA 1u
+#define AETH_DEVERR_TIMEOUT_MMA 2u
+#define AETH_DEVERR_TIMEOUT_EPI 4u
+#define AETH_DEVERR_BAD_ARG 8u
+#define AETH_DEVERR_TIMEOUT_PEER 16u
+int aeth_device_error_bits(int device, uint32_t* bits);
 /* Library version string. */
 const char* aeth_version(void);
 

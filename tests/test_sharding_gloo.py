@@ -64,3 +64,58 @@ def test_two_rank_clip_and_broadcast():
         assert clip == expect_clip
         assert abs(sq[0] - total) < 1e-12 and all(v == 0.0 for v in sq[1:])
         assert b == 1.0  # layer 3 belongs to rank 1
+
+
+class _FakeGroupOptimizer:
+    """Records the clip-group calls of sharding.setup_clip_group (host logic only)."""
+
+    def __init__(self, rank, fail_join):
+        self.rank, self.fail_join, self.calls = rank, fail_join, []
+
+    def clip_handle(self, world):
+        self.calls.append(("handle", world))
+        return bytes([self.rank + 1]) * 64
+
+    def set_clip_group(self, rank, world, handles, timeout_s=2.0):
+        self.calls.append(("join", rank, world, [h[0] for h in handles]))
+        if self.fail_join and world > 1:
+            raise RuntimeError("cannot open the peer's handle")
+
+
+def _group_worker(rank, world, port, fail_rank, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from aethelstream_b200 import sharding
+        opt = _FakeGroupOptimizer(rank, fail_join=(rank == fail_rank))
+        ok = sharding.setup_clip_group(opt)
+        q.put((rank, ok, opt.calls))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_setup_clip_group_agrees_on_outcome(fail_rank):
+    """Handles are gathered in rank order; if any rank cannot join, every rank
+    leaves the group and reports False (same collective steps either way)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_group_worker, args=(r, world, port, fail_rank, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=90) for _ in range(world))
+    for p in procs:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    for rank, ok, calls in res:
+        assert calls[0] == ("handle", 2)
+        assert calls[1] == ("join", rank, 2, [1, 2])  # every rank's handle, in rank order
+        assert ok == (fail_rank < 0)
+        if fail_rank < 0:
+            assert len(calls) == 2
+        elif rank != fail_rank:
+            assert calls[2] == ("join", 0, 1, [])  # left the group again
