@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                         w[i + 1] = ww.y;
                         v[i] = dl.x;
                         v[i + 1] = dl.y;
-                        amax = fmax3(amax, fabsf(ww.x), fabsf(ww.y));
+                        amax = fmax3_nan(amax, fabsf(ww.x), fabsf(ww.y));  // NaN-propagating, as torch's max
                     }
                     tmem_st16(tcol + (uint32_t)(c * 16), w);
                     if (dout) {
@@ -254,38 +254,48 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 }
                 tmem_wait_st();
                 // pass 2: requantise from TMEM (fast classifier; exact fix-up next to
-                // boundaries), again with the next chunk's load in flight.
-                const float safe = fmaxf(amax, 1e-8f), inv = __frcp_rn(safe);
-                float mind = 1.0f;
+                // boundaries), again with the next chunk's load in flight.  A block
+                // holding NaN or inf (amax NaN or inf) skips the fast classifier,
+                // whose table index needs a finite xn, and is requantised exactly.
+                const bool bad = !(amax <= 3.402823466e38f);
+                const float ninv = -__frcp_rn(nf4_safe(amax));
+                float mind = bad ? 0.0f : 1.0f;
                 float wbuf[2][16];
                 tmem_ld16<0>(tcol, wbuf[0]);
                 tmem_wait_ld_bind(wbuf[0]);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (c < 3) tmem_ld16<0>(tcol + (uint32_t)((c + 1) * 16), wbuf[(c + 1) & 1]);
-                    const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_bias, mind);
-                    const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_bias, mind);
-                    *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
-                        make_uint2(lo, hi);
+                    if (!bad) {
+                        const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], ninv, bucket_bias, mind);
+                        const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, ninv, bucket_bias, mind);
+                        *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
+                            make_uint2(lo, hi);
+                    }
                     if (c < 3) tmem_wait_ld_bind(wbuf[(c + 1) & 1]);
                 }
-                if (__any_sync(0xffffffffu, mind < kNf4NearWindow32)) {
-                    // Rare: redo words holding a near-boundary element with the
-                    // exact definition.  Warp-uniform loop (TMEM loads are
-                    // warp-collective).
+                if (__any_sync(0xffffffffu, mind < kNf4NearWindow)) {
+                    // Rare: redo words holding a near-boundary element, and every word
+                    // of a non-finite block, with the exact definition (a NaN scale
+                    // gives code 0 throughout, as the reference's argmin does).
+                    // Warp-uniform loop (TMEM loads are warp-collective).
+                    const float safe_x = nf4_safe(amax);
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         float w[16];
                         tmem_ld16<0>(tcol + (uint32_t)(c * 16), w);
                         tmem_wait_ld();
-                        float m0v = 1.0f, m1v = 1.0f;
-                        nf4_fast_word8_s(w, inv, bucket_bias, m0v);
-                        nf4_fast_word8_s(w + 8, inv, bucket_bias, m1v);
+                        float m0v = 0.0f, m1v = 0.0f;
+                        if (!bad) {
+                            m0v = m1v = 1.0f;
+                            nf4_fast_word8_s(w, ninv, bucket_bias, m0v);
+                            nf4_fast_word8_s(w + 8, ninv, bucket_bias, m1v);
+                        }
                         uint32_t* wa = reinterpret_cast<uint32_t*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
-                        if (m0v < kNf4NearWindow32)
-                            wa[0] = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe);
-                        if (m1v < kNf4NearWindow32)
-                            wa[1] = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe);
+                        if (m0v < kNf4NearWindow)
+                            wa[0] = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe_x);
+                        if (m1v < kNf4NearWindow)
+                            wa[1] = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe_x);
                     }
                 }
                 *sp = amax;

@@ -166,7 +166,7 @@ struct EpiNf4Update {
             float x = __fsub_rn(w[i], d);
             if (has_decay) x = __fmul_rn(x, decay_mul);
             w[i] = x;
-            amax = fmaxf(amax, fabsf(x));
+            amax = fmax_nan(amax, fabsf(x));
         }
         if (delta_out) {
 #pragma unroll

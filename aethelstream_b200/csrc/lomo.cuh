@@ -84,12 +84,12 @@ __global__ void __launch_bounds__(256) lomo_update_kernel(const uint16_t* __rest
             mo[k] = __fadd_rn(__fmul_rn(beta, m0), gs);
             w[k] = __fsub_rn(w[k], __fmul_rn(lr, mo[k]));
             am = fmaxf(am, fabsf(mo[k]));
-            aw = fmaxf(aw, fabsf(w[k]));
+            aw = fmax_nan(aw, fabsf(w[k]));
         }
         // NF4 block absmax across the 8 lanes owning this 64-element block.
-        aw = fmaxf(aw, __shfl_xor_sync(0xffffffffu, aw, 1));
-        aw = fmaxf(aw, __shfl_xor_sync(0xffffffffu, aw, 2));
-        aw = fmaxf(aw, __shfl_xor_sync(0xffffffffu, aw, 4));
+        aw = fmax_nan(aw, __shfl_xor_sync(0xffffffffu, aw, 1));
+        aw = fmax_nan(aw, __shfl_xor_sync(0xffffffffu, aw, 2));
+        aw = fmax_nan(aw, __shfl_xor_sync(0xffffffffu, aw, 4));
         uint32_t pk[1];
         nf4_quant_regs<8>(w, aw, tab.bucket, pk);
         *reinterpret_cast<uint32_t*>(wp + e0 / 2) = pk[0];

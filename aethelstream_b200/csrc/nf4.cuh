@@ -27,17 +27,31 @@ __constant__ float c_nf4_codes[16] = {
 
 constexpr float kNf4NearWindow = 1e-6f;
 
+// The block scale as the reference forms it (quantizer.py:35-36): absmax =
+// max|x| is NaN when the block holds a NaN (torch's max propagates it), and
+// clamp(min=1e-8) keeps a NaN.  Every element of such a block then gets code
+// 0 (argmin over NaN distances), and +-inf / inf gives NaN as well.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float nf4_safe(float amax) { return amax < 1e-8f ? 1e-8f : amax; }
+
 __device__ __forceinline__ uint32_t smem_u32_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 struct Nf4Tables {
     float2 byte_lut[256];  // (CODES[byte >> 4], CODES[byte & 15])
-    float2 bucket[33];     // {midpoint threshold or +inf, lower code index as int bits}
+    // {midpoint threshold or +inf, lower code index as int bits}; entries 33..63
+    // are reached only by a NaN xn (index bits & 63) and send it to the exact path
+    float2 bucket[64];
 };
 
 // Fill the shared tables; call with all threads of the CTA, then __syncthreads().
 __device__ __forceinline__ void nf4_tables_init(Nf4Tables* t, int tid, int nthreads) {
     for (int i = tid; i < 256; i += nthreads)
         t->byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
+    for (int b = 33 + tid; b < 64; b += nthreads) t->bucket[b] = make_float2(__int_as_float(0x7fc00000), 0.0f);
     for (int b = tid; b < 33; b += nthreads) {
         // bucket b holds xn with rint(16 xn) + 16 == b, i.e. [(b-16.5)/16, (b-15.5)/16)
         float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
@@ -75,7 +89,7 @@ __device__ __noinline__ uint32_t nf4_code_exact(float x, float safe) {
 template <int N>
 __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, const float2* __restrict__ bucket,
                                                uint32_t (&packed)[N / 8]) {
-    const float safe = fmaxf(amax, 1e-8f);
+    const float safe = nf4_safe(amax);
     const float inv = __frcp_rn(safe);
     uint32_t near[N / 8];
 #pragma unroll
@@ -88,7 +102,7 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
             float2 e = bucket[__float_as_int(t) & 63];
             float d = __fsub_rn(xn, e.x);
             uint32_t code = (uint32_t)__float_as_int(e.y) + (d > 0.0f ? 1u : 0u);
-            nb |= (fabsf(d) < kNf4NearWindow ? 1u : 0u) << j;
+            nb |= (fabsf(d) >= kNf4NearWindow ? 0u : 1u) << j;  // NaN: exact path
             word |= code << (8 * (j >> 1) + ((j & 1) ? 0 : 4));
         }
         packed[w] = word;
@@ -114,17 +128,13 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 // (CODES[byte >> 4], CODES[byte & 15]) in 16 copies, entry b of copy c at
 // float2 index 16 b + c, so the 16 lanes of a half-warp (copy = lane % 16)
 // read 16 different bank pairs whatever their bytes: one 8-byte lookup costs
-// the minimum two wavefronts per warp.  bucket32[b] = the NEGATED midpoint
-// threshold of bucket b (-2.0 when the bucket holds none) with (lower code + 1)
-// stored in its low 4 mantissa bits, so the signed distance to the threshold
-// is one addition, xn + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
-// is covered by the wider near-window kNf4NearWindow32.
+// the minimum two wavefronts per warp.  bucket64[b] = {midpoint threshold of
+// bucket b as float bits (2.0 when the bucket holds none), lower code}: the
+// code of xn is lower + [xn > threshold], one 8-byte lookup per element.
 // ---------------------------------------------------------------------------
-constexpr float kNf4NearWindow32 = 2.5e-6f;
-
 struct Nf4Tables32 {
     float2 byte_rep[256 * 16];
-    uint32_t bucket32[33];
+    uint2 bucket64[33];
 };
 
 __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
@@ -140,14 +150,20 @@ __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int n
             else if (mid < hi) { thr = mid; code = k; }
         }
         if (code < 0) code = below;
-        t->bucket32[b] = (__float_as_uint(-thr) & ~15u) | (uint32_t)(code + 1);
+        t->bucket64[b] = make_uint2(__float_as_uint(thr), (uint32_t)code);
     }
 }
 
-// Three-input min / max of sm_100 (one instruction each).
+// Three-input min / max of sm_100 (one instruction each).  fmax3 ignores a
+// NaN operand; fmax3_nan returns NaN when any operand is NaN.
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float r;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
     return r;
 }
 __device__ __forceinline__ float fmin3(float a, float b, float c) {
@@ -168,36 +184,41 @@ __device__ __noinline__ uint32_t nf4_exact_word8(float a0, float a1, float a2, f
 
 
 // Shared-address variants for the fused apply epilogue.
-// bucket_bias: shared address of bucket32[0] minus (0x4B400000 << 2) modulo
+// bucket_bias: shared address of bucket64[0] minus (0x4B400000 << 3) modulo
 // 2^32, so the entry of value t = fma(xn, 16, 1.5*2^23 + 16) sits at
-// bucket_bias + (bits(t) << 2) -- one add instead of mask, shift and add.
+// bucket_bias + (bits(t) << 3) -- one address operation.  Only finite
+// |xn| <= 1 + 2^-20 may be classified: NaN or infinite xn would index outside
+// the table, so callers route blocks holding a non-finite value to the exact
+// path without calling this.
 __device__ __forceinline__ uint32_t nf4_bucket_bias(const Nf4Tables32* t) {
-    return smem_u32_addr(t->bucket32) - (0x4B400000u << 2);
+    return smem_u32_addr(t->bucket64) - (0x4B400000u << 3);
 }
 
 // 8 values -> one packed word, two elements per step through the packed
-// f32x2 instructions.  Byte k of the word = code[2k] << 4 | code[2k+1]; pairs
-// enter from the bottom, (6,7) first.  The signed distance d = xn +
-// (-threshold) gives code = (lower + 1) - [d < 0]; d == 0 lies in the near
-// band.  ptxas may fuse the xn product into the distance add; that moves d by
-// under an ulp of xn, far inside kNf4NearWindow32, whose elements are decided
-// again exactly from the unscaled value.
-__device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t bucket_bias, float& mind) {
-    const float2 inv2 = make_float2(inv, inv);
-    const float2 k16 = make_float2(16.0f, 16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
+// f32x2 instructions, from ninv = -1/max(absmax, 1e-8).  Byte k of the word =
+// code[2k] << 4 | code[2k+1]; codes enter from the bottom, element 6 first.
+// With xq = -xn, the signed distance d = threshold + xq is negative exactly
+// when xn lies above the threshold, so code = lower + sign bit of d.  mind
+// collects min |d|: elements within kNf4NearWindow of a threshold are decided
+// again exactly.  ptxas may fuse the xq product into the distance add; that
+// moves d by under an ulp of xn, far inside the window.
+__device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float ninv, uint32_t bucket_bias, float& mind) {
+    const float2 ninv2 = make_float2(ninv, ninv);
+    const float2 km16 = make_float2(-16.0f, -16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
     uint32_t word = 0;
 #pragma unroll
     for (int s = 3; s >= 0; --s) {
-        const float2 xn = mul2_rn(make_float2(w[2 * s], w[2 * s + 1]), inv2);
-        const float2 t = fma2_rn(xn, k16, kbias);  // low bits: rint(16 xn) + 16
-        uint32_t e0, e1;
-        asm("ld.shared.u32 %0, [%1];" : "=r"(e0) : "r"(bucket_bias + (__float_as_uint(t.x) << 2)));
-        asm("ld.shared.u32 %0, [%1];" : "=r"(e1) : "r"(bucket_bias + (__float_as_uint(t.y) << 2)));
-        const float2 d = add2_rn(xn, make_float2(__uint_as_float(e0), __uint_as_float(e1)));
-        const uint32_t c0 = e0 + (uint32_t)(__float_as_int(d.x) >> 31);
-        const uint32_t c1 = e1 + (uint32_t)(__float_as_int(d.y) >> 31);
+        const float2 xq = mul2_rn(make_float2(w[2 * s], w[2 * s + 1]), ninv2);
+        const float2 t = fma2_rn(xq, km16, kbias);  // low bits: rint(16 xn) + 16
+        uint32_t th0, k0, th1, k1;
+        asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(th0), "=r"(k0) : "r"(bucket_bias + (__float_as_uint(t.x) << 3)));
+        asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(th1), "=r"(k1) : "r"(bucket_bias + (__float_as_uint(t.y) << 3)));
+        const float2 d = add2_rn(make_float2(__uint_as_float(th0), __uint_as_float(th1)), xq);
+        const uint32_t c0 = k0 + (__float_as_uint(d.x) >> 31);
+        const uint32_t c1 = k1 + (__float_as_uint(d.y) >> 31);
         mind = fmin3(mind, fabsf(d.x), fabsf(d.y));
-        word = (word << 8) | ((c0 & 15u) << 4) | (c1 & 15u);
+        word = (word << 4) + c0;
+        word = (word << 4) + c1;
     }
     return word;
 }
@@ -363,9 +384,9 @@ __global__ void __launch_bounds__(256) nf4_quant64_kernel(const void* __restrict
         }
         float a = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) a = fmaxf(a, fabsf(v[i]));
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+        for (int i = 0; i < 16; ++i) a = fmax_nan(a, fabsf(v[i]));
+        a = fmax_nan(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        a = fmax_nan(a, __shfl_xor_sync(0xffffffffu, a, 2));
         if (active) {
             uint32_t pk[2];
             nf4_quant_regs<16>(v, a, tab.bucket, pk);
@@ -385,9 +406,10 @@ __global__ void nf4_absmax_generic_kernel(const void* __restrict__ x, int x_dtyp
         float a = 0.0f;
         for (int64_t i = lane; i < block; i += 32) {
             int64_t e = b * block + i;
-            if (e < n) a = fmaxf(a, fabsf(load_as_f32(x, e, x_dtype)));
+            if (e < n) a = fmax_nan(a, fabsf(load_as_f32(x, e, x_dtype)));
         }
-        a = warp_max(a);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmax_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
         if (lane == 0) absmax[b] = a;
     }
 }
@@ -398,9 +420,9 @@ __global__ void nf4_pack_generic_kernel(const void* __restrict__ x, int x_dtype,
     int64_t nbytes = (n + 1) / 2;
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += (int64_t)gridDim.x * blockDim.x) {
         int64_t e0 = 2 * k, e1 = 2 * k + 1;
-        uint32_t c0 = nf4_code_exact(load_as_f32(x, e0, x_dtype), fmaxf(absmax[e0 / block], 1e-8f));
+        uint32_t c0 = nf4_code_exact(load_as_f32(x, e0, x_dtype), nf4_safe(absmax[e0 / block]));
         // quantizer.py:37-39: an odd element count is padded with code 0.
-        uint32_t c1 = e1 < n ? nf4_code_exact(load_as_f32(x, e1, x_dtype), fmaxf(absmax[e1 / block], 1e-8f)) : 0u;
+        uint32_t c1 = e1 < n ? nf4_code_exact(load_as_f32(x, e1, x_dtype), nf4_safe(absmax[e1 / block])) : 0u;
         packed[k] = (uint8_t)((c0 << 4) | c1);
     }
 }

@@ -79,12 +79,17 @@ void ref_nf4_quantize(const float* x, int64_t n, int block, uint8_t* packed, flo
     int64_t nblocks = (n + block - 1) / block;
     for (int64_t b = 0; b < nblocks; ++b) {
         int64_t s = b * block;
+        /* blocks.abs().max(dim=1) propagates a NaN; clamp(min=1e-8) keeps it, so
+         * every element of such a block gets code 0 (argmin over NaN distances) */
         float amax = 0.0f;
+        int has_nan = 0;
         for (int i = 0; i < block; ++i) {
             float v = (s + i < n) ? x[s + i] : 0.0f;
             float a = fabsf(v);
-            if (a > amax) amax = a;
+            if (a != a) has_nan = 1;
+            else if (a > amax) amax = a;
         }
+        if (has_nan) amax = NAN;
         absmax[b] = amax;
         float safe = amax < 1e-8f ? 1e-8f : amax;
         for (int i = 0; i < block && s + i < n; ++i) {

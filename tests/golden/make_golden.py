@@ -56,6 +56,16 @@ def cases():
     # Student-t like heavy tails (the 13B config's gradient distribution)
     t = torch.distributions.StudentT(3.0).sample((4096,))
     out["studentt_4096"] = t.float() * 1e-3
+    # non-finite values: a NaN makes the block's absmax NaN (all codes 0); an
+    # infinite absmax sends finite values to code 7 and +-inf to code 0
+    nf = torch.randn(320, generator=g) * 0.02
+    nf[3] = float("nan")
+    nf[70] = float("inf")
+    nf[140] = float("-inf")
+    nf[141] = float("inf")
+    nf[200] = float("nan")
+    nf[201] = float("-inf")
+    out["nonfinite_320"] = nf
     return out
 
 

@@ -72,6 +72,21 @@ def test_nf4_quant_reference_golden(L, lib):
         assert np.array_equal(host(absmax).view(np.uint32), z[f"{name}__absmax"].view(np.uint32)), name
 
 
+def test_nf4_quant_nonfinite_generic_block(oracle, L, lib):
+    """NaN / inf through the generic path (block 32, odd length) as the
+    reference quantiser treats them (absmax NaN propagates; codes from argmin)."""
+    rng = np.random.default_rng(77)
+    x = (rng.standard_normal(333) * 0.02).astype(np.float32)
+    x[[1, 40, 41, 100, 200]] = [np.nan, np.inf, -np.inf, np.inf, np.nan]
+    n = x.size
+    packed = torch.zeros((n + 1) // 2, dtype=torch.uint8, device=DEV)
+    absmax = torch.zeros((n + 31) // 32, dtype=torch.float32, device=DEV)
+    assert lib.aeth_nf4_quant(ptr(dev(x)), L.DTYPE_F32, n, 32, ptr(packed), ptr(absmax), stream()) == 0
+    p_ref, a_ref = oracle.nf4_quantize(x, block=32)
+    assert np.array_equal(host(packed), p_ref)
+    assert np.array_equal(host(absmax).view(np.uint32), a_ref.view(np.uint32))
+
+
 def _boundary_heavy(oracle, nblocks, seed):
     """Blocks whose values sit on, or one ulp either side of, the decision
     midpoints (scaled by the block absmax) -- the cases the fast classifier

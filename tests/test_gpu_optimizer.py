@@ -219,3 +219,36 @@ def test_b200_step_with_hook_equals_fused_clip(oracle):
     assert c0 == c1 and c0[0] < 1.0
     for x, y in zip(p0 + a0 + s0, p1 + a1 + s1):
         assert np.array_equal(x, y)
+
+
+def test_b200_apply_nonfinite_blocks(oracle):
+    """NF4 blocks whose weights turn NaN or infinite are requantised as the
+    reference's quantiser does (absmax NaN or inf, codes from the exact
+    argmin), without the fast classifier's table lookup; the other blocks of
+    the same tiles are unaffected."""
+    from aethelstream_b200 import nf4_quantize
+    m, n, r = 256, 512, 64
+    rng = np.random.default_rng(61)
+    opt = _opt("b200", [(0, "d_wq", m, n, r)])
+    w = (rng.standard_normal((m, n)) * 0.02).astype(np.float32)
+    W = nf4_quantize(dev(w))
+    W.absmax[5] = float("nan")         # every weight NaN
+    W.absmax[9] = float("inf")         # +-inf, and NaN where the code is 0.0
+    W.packed[13 * 32:14 * 32] = 0xFF   # code 1.0 throughout ...
+    W.absmax[13] = float("inf")        # ... so every weight is +inf
+    W.packed[17 * 32:18 * 32] = 0xFF
+    W.absmax[17] = 1e38                # large but finite
+    g = oracle.bf16_round((rng.standard_normal((m, n)) * 1e-3).astype(np.float32))
+    opt.project_and_accumulate(dev(g).to(torch.bfloat16), 0, "d_wq")
+    pre = torch.empty(m, n, dtype=torch.float32, device=DEV)
+    opt.apply_update(0, "d_wq", 1.0, weight=W, prequant_out=pre)
+    pre_h = host(pre).ravel()
+    assert np.isnan(pre_h[5 * 64:6 * 64]).all()
+    assert np.isposinf(pre_h[13 * 64:14 * 64]).all()
+    p_chk, a_chk = oracle.nf4_requant(pre_h)
+    a_gpu = host(W.absmax)
+    assert np.isnan(a_gpu[5]) and np.isnan(a_gpu[9]) and np.isposinf(a_gpu[13]) and np.isfinite(a_gpu[17])
+    assert np.array_equal(host(W.packed), p_chk)
+    assert np.array_equal(a_gpu.view(np.uint32), a_chk.view(np.uint32))
+    assert (host(W.packed)[5 * 32:6 * 32] == 0).all() and (host(W.packed)[13 * 32:14 * 32] == 0).all()
+    opt.close()
