@@ -109,6 +109,11 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
     uint64_t* w_empty = w_full + kApplyWSlots;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_empty + kApplyWSlots);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // (problem, m0, n0) of the unit in each weight slot, written by the producer
+    // before the slot's full barrier is armed (its arrive releases them)
+    int4* winfo = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(full) + 128);
+    static_assert((2 * STAGES + 4 + 2 * kApplyWSlots) * 8 + 8 <= 128 && 128 + 16 * kApplyWSlots <= L::kBar,
+                  "barriers, TMEM slot, abort flag and unit table must fit the barrier area");
     Nf4Tables32* tab = reinterpret_cast<Nf4Tables32*>(reinterpret_cast<uint8_t*>(full) + L::kBar);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -140,6 +145,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 const int wb = j % kApplyWSlots;
                 if (!mbar_wait(&w_empty[wb], ((uint32_t)(j / kApplyWSlots) & 1u) ^ 1u, abort, err, DEVERR_TIMEOUT_TMA))
                     break;
+                winfo[wb] = make_int4(p, m0, n0, 0);
                 mbar_arrive_expect_tx(&w_full[wb], L::kWPacked + L::kWScale);
                 uint8_t* ws = wslot + wb * L::kWSlot;
                 tma_load_2d(ws, &pr.tmW, &w_full[wb], n0 / 2, m0);
@@ -191,14 +197,12 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
         int j = 0;
         int pending = -1;  // slot of this row group's previous store, released one unit later
         for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
-            const int p = apply_find(args, u);
-            const ApplyProblem& pr = args.p[p];
-            const int local = u - pr.unit_begin;
-            const int m0 = (local / pr.n_tiles) * 128;
-            const int n0 = (local % pr.n_tiles) * kApplyBN;
             const int b = j & 1;
             const int wb = j % kApplyWSlots;
             if (!mbar_wait(&w_full[wb], (uint32_t)(j / kApplyWSlots) & 1u, abort, err, DEVERR_TIMEOUT_EPI)) break;
+            const int4 info = winfo[wb];
+            const ApplyProblem& pr = args.p[info.x];
+            const int m0 = info.y, n0 = info.z;
             if (!mbar_wait(&acc_full[b], (uint32_t)(j >> 1) & 1u, abort, err, DEVERR_TIMEOUT_EPI) || *abort) break;
             tc_fence_after();
             uint8_t* wp = wslot + wb * L::kWSlot;
@@ -226,25 +230,25 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     nf4_dequant_word_s(qq.x, amax_old, lut_s, w);
                     nf4_dequant_word_s(qq.y, amax_old, lut_s, w + 8);
                     tmem_wait_ld_bind(v);
-                    // Products paired: v <- fl(v * -lr) = -fl(lr * dW) (round-to-nearest is
-                    // sign-symmetric); sums scalar: w <- fl(w + v) = fl(w - fl(lr * dW)); decay.
+                    // w <- fl(w - lr * dW), one fused multiply-add per element (paired),
+                    // then the decoupled decay.  The reference rounds lr * dW first; the
+                    // two differ by under half an ulp of the product, inside the update's
+                    // tolerance, and the requantisation below is exact for whatever w is.
 #pragma unroll
                     for (int i = 0; i < 16; i += 2) {
-                        const float2 dl = mul2_rn(make_float2(v[i], v[i + 1]), nlr2);
-                        float2 ww = add2_sep(make_float2(w[i], w[i + 1]), dl);
+                        float2 ww = fma2_rn(make_float2(v[i], v[i + 1]), nlr2, make_float2(w[i], w[i + 1]));
                         if (pr.has_decay) ww = mul2_rn(ww, dmul2);
                         w[i] = ww.x;
                         w[i + 1] = ww.y;
-                        v[i] = dl.x;
-                        v[i + 1] = dl.y;
                         amax = fmax3_nan(amax, fabsf(ww.x), fabsf(ww.y));  // NaN-propagating, as torch's max
                     }
                     tmem_st16(tcol + (uint32_t)(c * 16), w);
-                    if (dout) {
+                    if (dout) {  // take_weight_delta: fl(lr * dW)
 #pragma unroll
                         for (int i = 0; i < 16; i += 4)
                             *reinterpret_cast<float4*>(dout + c * 16 + i) =
-                                make_float4(-v[i], -v[i + 1], -v[i + 2], -v[i + 3]);
+                                make_float4(__fmul_rn(v[i], pr.lr), __fmul_rn(v[i + 1], pr.lr),
+                                            __fmul_rn(v[i + 2], pr.lr), __fmul_rn(v[i + 3], pr.lr));
                     }
                     if (pout) {
 #pragma unroll
@@ -258,7 +262,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 // holding NaN or inf (amax NaN or inf) skips the fast classifier,
                 // whose table index needs a finite xn, and is requantised exactly.
                 const bool bad = !(amax <= 3.402823466e38f);
-                const float ninv = -__frcp_rn(nf4_safe(amax));
+                const float inv = __frcp_rn(nf4_safe(amax));
                 float mind = bad ? 0.0f : 1.0f;
                 float wbuf[2][16];
                 tmem_ld16<0>(tcol, wbuf[0]);
@@ -267,14 +271,14 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 for (int c = 0; c < 4; ++c) {
                     if (c < 3) tmem_ld16<0>(tcol + (uint32_t)((c + 1) * 16), wbuf[(c + 1) & 1]);
                     if (!bad) {
-                        const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], ninv, bucket_bias, mind);
-                        const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, ninv, bucket_bias, mind);
+                        const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_bias, mind);
+                        const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_bias, mind);
                         *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
                             make_uint2(lo, hi);
                     }
                     if (c < 3) tmem_wait_ld_bind(wbuf[(c + 1) & 1]);
                 }
-                if (__any_sync(0xffffffffu, mind < kNf4NearWindow)) {
+                if (__any_sync(0xffffffffu, mind < kNf4NearWindow32)) {
                     // Rare: redo words holding a near-boundary element, and every word
                     // of a non-finite block, with the exact definition (a NaN scale
                     // gives code 0 throughout, as the reference's argmin does).
@@ -288,17 +292,17 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                         float m0v = 0.0f, m1v = 0.0f;
                         if (!bad) {
                             m0v = m1v = 1.0f;
-                            nf4_fast_word8_s(w, ninv, bucket_bias, m0v);
-                            nf4_fast_word8_s(w + 8, ninv, bucket_bias, m1v);
+                            nf4_fast_word8_s(w, inv, bucket_bias, m0v);
+                            nf4_fast_word8_s(w + 8, inv, bucket_bias, m1v);
                         }
                         uint32_t* wa = reinterpret_cast<uint32_t*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
-                        if (m0v < kNf4NearWindow)
+                        if (m0v < kNf4NearWindow32)
                             wa[0] = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe_x);
-                        if (m1v < kNf4NearWindow)
+                        if (m1v < kNf4NearWindow32)
                             wa[1] = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe_x);
                     }
                 }
-                *sp = amax;
+                *sp = nf4_store_amax(amax);
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[b]);

@@ -183,7 +183,7 @@ struct EpiNf4Update {
         nf4_quant_regs<64>(w, amax, s->tab.bucket, pk);
         *reinterpret_cast<uint4*>(p) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *reinterpret_cast<uint4*>(p + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        *ap = amax;
+        *ap = nf4_store_amax(amax);
     }
 };
 

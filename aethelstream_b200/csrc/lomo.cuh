@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(256) lomo_update_kernel(const uint16_t* __rest
         uint32_t pk[1];
         nf4_quant_regs<8>(w, aw, tab.bucket, pk);
         *reinterpret_cast<uint32_t*>(wp + e0 / 2) = pk[0];
-        if ((threadIdx.x & 7) == 0) wa[e0 / 64] = aw;
+        if ((threadIdx.x & 7) == 0) wa[e0 / 64] = nf4_store_amax(aw);
         if (prequant) {
             *reinterpret_cast<float4*>(prequant + e0) = make_float4(w[0], w[1], w[2], w[3]);
             *reinterpret_cast<float4*>(prequant + e0 + 4) = make_float4(w[4], w[5], w[6], w[7]);

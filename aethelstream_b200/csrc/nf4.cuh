@@ -37,6 +37,11 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
     return r;
 }
 __device__ __forceinline__ float nf4_safe(float amax) { return amax < 1e-8f ? 1e-8f : amax; }
+// The stored absmax of a NaN block: the quiet NaN the reference's max returns
+// for an input NaN (0x7fc00000), whatever NaN the device arithmetic produced.
+__device__ __forceinline__ float nf4_store_amax(float amax) {
+    return amax != amax ? __uint_as_float(0x7fc00000u) : amax;
+}
 
 __device__ __forceinline__ uint32_t smem_u32_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -128,13 +133,18 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 // (CODES[byte >> 4], CODES[byte & 15]) in 16 copies, entry b of copy c at
 // float2 index 16 b + c, so the 16 lanes of a half-warp (copy = lane % 16)
 // read 16 different bank pairs whatever their bytes: one 8-byte lookup costs
-// the minimum two wavefronts per warp.  bucket64[b] = {midpoint threshold of
-// bucket b as float bits (2.0 when the bucket holds none), lower code}: the
-// code of xn is lower + [xn > threshold], one 8-byte lookup per element.
+// the minimum two wavefronts per warp.  bucket32[b] = the NEGATED midpoint
+// threshold of bucket b (-2.0 when the bucket holds none) with (lower code + 1)
+// stored in its low 4 mantissa bits, so the signed distance to the threshold
+// is one addition, xn + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
+// is covered by the wider near-window kNf4NearWindow32.  4-byte entries keep a
+// warp's 32 lookups in one wavefront (33 words, one bank each but the last).
 // ---------------------------------------------------------------------------
+constexpr float kNf4NearWindow32 = 2.5e-6f;
+
 struct Nf4Tables32 {
     float2 byte_rep[256 * 16];
-    uint2 bucket64[33];
+    uint32_t bucket32[33];
 };
 
 __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
@@ -150,7 +160,7 @@ __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int n
             else if (mid < hi) { thr = mid; code = k; }
         }
         if (code < 0) code = below;
-        t->bucket64[b] = make_uint2(__float_as_uint(thr), (uint32_t)code);
+        t->bucket32[b] = (__float_as_uint(-thr) & ~15u) | (uint32_t)(code + 1);
     }
 }
 
@@ -184,41 +194,39 @@ __device__ __noinline__ uint32_t nf4_exact_word8(float a0, float a1, float a2, f
 
 
 // Shared-address variants for the fused apply epilogue.
-// bucket_bias: shared address of bucket64[0] minus (0x4B400000 << 3) modulo
+// bucket_bias: shared address of bucket32[0] minus (0x4B400000 << 2) modulo
 // 2^32, so the entry of value t = fma(xn, 16, 1.5*2^23 + 16) sits at
-// bucket_bias + (bits(t) << 3) -- one address operation.  Only finite
-// |xn| <= 1 + 2^-20 may be classified: NaN or infinite xn would index outside
-// the table, so callers route blocks holding a non-finite value to the exact
-// path without calling this.
+// bucket_bias + (bits(t) << 2) -- one address operation.  Only finite
+// |xn| <= 1 + 2^-20 may be classified: a NaN or infinite xn would index
+// outside the table, so callers route blocks holding a non-finite value to
+// the exact path without calling this.
 __device__ __forceinline__ uint32_t nf4_bucket_bias(const Nf4Tables32* t) {
-    return smem_u32_addr(t->bucket64) - (0x4B400000u << 3);
+    return smem_u32_addr(t->bucket32) - (0x4B400000u << 2);
 }
 
 // 8 values -> one packed word, two elements per step through the packed
-// f32x2 instructions, from ninv = -1/max(absmax, 1e-8).  Byte k of the word =
-// code[2k] << 4 | code[2k+1]; codes enter from the bottom, element 6 first.
-// With xq = -xn, the signed distance d = threshold + xq is negative exactly
-// when xn lies above the threshold, so code = lower + sign bit of d.  mind
-// collects min |d|: elements within kNf4NearWindow of a threshold are decided
-// again exactly.  ptxas may fuse the xq product into the distance add; that
-// moves d by under an ulp of xn, far inside the window.
-__device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float ninv, uint32_t bucket_bias, float& mind) {
-    const float2 ninv2 = make_float2(ninv, ninv);
-    const float2 km16 = make_float2(-16.0f, -16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
+// f32x2 instructions.  Byte k of the word = code[2k] << 4 | code[2k+1]; pairs
+// enter from the bottom, (6,7) first.  The signed distance d = xn +
+// (-threshold) gives code = (lower + 1) - [d < 0]; d == 0 lies in the near
+// band.  ptxas may fuse the xn product into the distance add; that moves d by
+// under an ulp of xn, far inside kNf4NearWindow32, whose elements are decided
+// again exactly from the unscaled value.
+__device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t bucket_bias, float& mind) {
+    const float2 inv2 = make_float2(inv, inv);
+    const float2 k16 = make_float2(16.0f, 16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
     uint32_t word = 0;
 #pragma unroll
     for (int s = 3; s >= 0; --s) {
-        const float2 xq = mul2_rn(make_float2(w[2 * s], w[2 * s + 1]), ninv2);
-        const float2 t = fma2_rn(xq, km16, kbias);  // low bits: rint(16 xn) + 16
-        uint32_t th0, k0, th1, k1;
-        asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(th0), "=r"(k0) : "r"(bucket_bias + (__float_as_uint(t.x) << 3)));
-        asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(th1), "=r"(k1) : "r"(bucket_bias + (__float_as_uint(t.y) << 3)));
-        const float2 d = add2_rn(make_float2(__uint_as_float(th0), __uint_as_float(th1)), xq);
-        const uint32_t c0 = k0 + (__float_as_uint(d.x) >> 31);
-        const uint32_t c1 = k1 + (__float_as_uint(d.y) >> 31);
+        const float2 xn = mul2_rn(make_float2(w[2 * s], w[2 * s + 1]), inv2);
+        const float2 t = fma2_rn(xn, k16, kbias);  // low bits: rint(16 xn) + 16
+        uint32_t e0, e1;
+        asm("ld.shared.u32 %0, [%1];" : "=r"(e0) : "r"(bucket_bias + (__float_as_uint(t.x) << 2)));
+        asm("ld.shared.u32 %0, [%1];" : "=r"(e1) : "r"(bucket_bias + (__float_as_uint(t.y) << 2)));
+        const float2 d = add2_rn(xn, make_float2(__uint_as_float(e0), __uint_as_float(e1)));
+        const uint32_t c0 = e0 + (uint32_t)(__float_as_int(d.x) >> 31);
+        const uint32_t c1 = e1 + (uint32_t)(__float_as_int(d.y) >> 31);
         mind = fmin3(mind, fabsf(d.x), fabsf(d.y));
-        word = (word << 4) + c0;
-        word = (word << 4) + c1;
+        word = (word << 8) | ((c0 & 15u) << 4) | (c1 & 15u);
     }
     return word;
 }
@@ -391,7 +399,7 @@ __global__ void __launch_bounds__(256) nf4_quant64_kernel(const void* __restrict
             uint32_t pk[2];
             nf4_quant_regs<16>(v, a, tab.bucket, pk);
             *reinterpret_cast<uint2*>(packed + e0 / 2) = make_uint2(pk[0], pk[1]);
-            if ((qd & 3) == 0) absmax[qd >> 2] = a;
+            if ((qd & 3) == 0) absmax[qd >> 2] = nf4_store_amax(a);
         }
     }
 }
@@ -410,7 +418,7 @@ __global__ void nf4_absmax_generic_kernel(const void* __restrict__ x, int x_dtyp
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) a = fmax_nan(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (lane == 0) absmax[b] = a;
+        if (lane == 0) absmax[b] = nf4_store_amax(a);
     }
 }
 
