@@ -289,8 +289,10 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     float sm = 0.0f, sv = 0.0f;
     float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
     uint2 qm = make_uint2(0u, 0u), qv = qm;
+    // A CTA's blocks come in increasing order (its first by index, then from
+    // the counter, offset by the grid), so the owning parameter only moves
+    // forward: the search continues from the current one.
     auto fetch = [&](int blk) {
-        p = 0;
 #pragma unroll 1
         while (p + 1 < a.np && blk >= a.block_begin[p + 1]) ++p;
         b = blk - a.block_begin[p];

@@ -279,27 +279,31 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     if (c < 3) tmem_wait_ld_bind(wbuf[(c + 1) & 1]);
                 }
                 if (__any_sync(0xffffffffu, mind < kNf4NearWindow32)) {
-                    // Rare: redo words holding a near-boundary element, and every word
-                    // of a non-finite block, with the exact definition (a NaN scale
-                    // gives code 0 throughout, as the reference's argmin does).
-                    // Warp-uniform loop (TMEM loads are warp-collective).
+                    // Rare: words holding a near-boundary element get those elements
+                    // decided exactly; a non-finite block is requantised exactly
+                    // throughout (a NaN scale gives code 0, as the reference's argmin
+                    // does).  Warp-uniform loop (TMEM loads are warp-collective).
                     const float safe_x = nf4_safe(amax);
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         float w[16];
                         tmem_ld16<0>(tcol + (uint32_t)(c * 16), w);
                         tmem_wait_ld();
-                        float m0v = 0.0f, m1v = 0.0f;
-                        if (!bad) {
-                            m0v = m1v = 1.0f;
+                        uint32_t* wa = reinterpret_cast<uint32_t*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
+                        if (bad) {
+                            wa[0] = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe_x);
+                            wa[1] = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe_x);
+                        } else {
+                            float m0v = 1.0f, m1v = 1.0f;
                             nf4_fast_word8_s(w, inv, bucket_bias, m0v);
                             nf4_fast_word8_s(w + 8, inv, bucket_bias, m1v);
+                            if (m0v < kNf4NearWindow32)
+                                wa[0] = nf4_fix_word8(wa[0], w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], inv, safe_x,
+                                                      bucket_bias);
+                            if (m1v < kNf4NearWindow32)
+                                wa[1] = nf4_fix_word8(wa[1], w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], inv,
+                                                      safe_x, bucket_bias);
                         }
-                        uint32_t* wa = reinterpret_cast<uint32_t*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
-                        if (m0v < kNf4NearWindow32)
-                            wa[0] = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe_x);
-                        if (m1v < kNf4NearWindow32)
-                            wa[1] = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe_x);
                     }
                 }
                 *sp = nf4_store_amax(amax);

@@ -139,8 +139,14 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 // is one addition, xn + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
 // is covered by the wider near-window kNf4NearWindow32.  4-byte entries keep a
 // warp's 32 lookups in one wavefront (33 words, one bank each but the last).
+// Window budget: the stored threshold moves by at most 15 ulp of the largest
+// midpoint (0.8615: 8.9e-7); xn = x * rcp(absmax) is within 2 ulp of x / absmax
+// (2.4e-7); the fp32 midpoint and the reference's rounded distances add under
+// 5e-8.  Total 1.2e-6, so 1.5e-6 leaves a quarter in reserve.  Every midpoint
+// lies at least 8e-3 inside its bucket, so a near element is always near its
+// own bucket's threshold.
 // ---------------------------------------------------------------------------
-constexpr float kNf4NearWindow32 = 2.5e-6f;
+constexpr float kNf4NearWindow32 = 1.5e-6f;
 
 struct Nf4Tables32 {
     float2 byte_rep[256 * 16];
@@ -192,6 +198,34 @@ __device__ __noinline__ uint32_t nf4_exact_word8(float a0, float a1, float a2, f
     return word;
 }
 
+
+// Rare-path repair of one fast-classified word: elements within the near
+// window of their bucket's threshold (the lower code k = low bits - 1 of the
+// entry) get the reference's decision between codes k and k + 1 from the
+// IEEE quotient x / safe -- the other 14 codes are at least 0.03 further away
+// -- with the lower code winning a tie, as torch.argmin does.
+__device__ __noinline__ uint32_t nf4_fix_word8(uint32_t word, float a0, float a1, float a2, float a3, float a4,
+                                               float a5, float a6, float a7, float inv, float safe,
+                                               uint32_t bucket_bias) {
+    const float a[8] = {a0, a1, a2, a3, a4, a5, a6, a7};
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+        const float xn = __fmul_rn(a[j], inv);
+        const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);
+        uint32_t e;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(e) : "r"(bucket_bias + (__float_as_uint(t) << 2)));
+        const float d = __fadd_rn(xn, __uint_as_float(e));
+        if (fabsf(d) < kNf4NearWindow32) {
+            const uint32_t k = (e & 15u) - 1u;
+            const float xe = __fdiv_rn(a[j], safe);
+            const float dlo = fabsf(__fsub_rn(xe, c_nf4_codes[k])), dhi = fabsf(__fsub_rn(xe, c_nf4_codes[k + 1]));
+            const uint32_t code = dhi < dlo ? k + 1 : k;
+            const uint32_t sh = 8 * (j >> 1) + ((j & 1) ? 0 : 4);
+            word = (word & ~(0xfu << sh)) | (code << sh);
+        }
+    }
+    return word;
+}
 
 // Shared-address variants for the fused apply epilogue.
 // bucket_bias: shared address of bucket32[0] minus (0x4B400000 << 2) modulo

@@ -252,3 +252,31 @@ def test_b200_apply_nonfinite_blocks(oracle):
     assert np.array_equal(a_gpu.view(np.uint32), a_chk.view(np.uint32))
     assert (host(W.packed)[5 * 32:6 * 32] == 0).all() and (host(W.packed)[13 * 32:14 * 32] == 0).all()
     opt.close()
+
+
+def test_b200_apply_requant_bitexact_large(oracle):
+    """The fused requantisation at a size where hundreds of updated weights land
+    next to a decision midpoint (the exact repair path), bit-exact against the
+    reference quantiser on the kernel's own pre-quantisation values."""
+    from aethelstream_b200 import nf4_quantize
+    m, n, r = 2048, 4096, 128
+    rng = np.random.default_rng(62)
+    opt = _opt("b200", [(0, "d_wq", m, n, r)])
+    W = nf4_quantize(dev((rng.standard_normal((m, n)) * 0.02).astype(np.float32)))
+    pre = torch.empty(m, n, dtype=torch.float32, device=DEV)
+    for step in range(2):
+        g = (torch.randn(m, n, device=DEV) * 1e-3).to(torch.bfloat16)
+        opt.project_and_accumulate(g, 0, "d_wq")
+        opt.apply_update(0, "d_wq", 1.0, weight=W, prequant_out=pre)
+        opt.zero_accum(0, "d_wq")
+        pre_h = host(pre).ravel()
+        p_chk, a_chk = oracle.nf4_requant(pre_h)
+        assert np.array_equal(host(W.packed), p_chk), step
+        assert np.array_equal(host(W.absmax).view(np.uint32), a_chk.view(np.uint32)), step
+    # the repair path ran: weights within the near window of a midpoint
+    codes = oracle.NF4_CODES
+    mids = ((codes[:-1] + codes[1:]) * np.float32(0.5)).astype(np.float32)
+    xn = (pre_h.reshape(-1, 64) / np.maximum(a_chk, 1e-8)[:, None]).ravel()
+    near = np.abs(xn[:, None] - mids[None, :]).min(axis=1) < 1.5e-6
+    assert near.sum() > 20, near.sum()
+    opt.close()
