@@ -148,8 +148,8 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 winfo[wb] = make_int4(p, m0, n0, 0);
                 mbar_arrive_expect_tx(&w_full[wb], L::kWPacked + L::kWScale);
                 uint8_t* ws = wslot + wb * L::kWSlot;
-                tma_load_2d(ws, &pr.tmW, &w_full[wb], n0 / 2, m0);
-                tma_load_2d(ws + L::kWPacked, &pr.tmS, &w_full[wb], n0 / 64, m0);
+                tma_load_2d_hint(ws, &pr.tmW, &w_full[wb], n0 / 2, m0, l2_evict_first_policy());
+                tma_load_2d_hint(ws + L::kWPacked, &pr.tmS, &w_full[wb], n0 / 64, m0, l2_evict_first_policy());
                 for (int kb = 0; kb < kb_n; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -313,8 +313,8 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
             fence_proxy_async();
             named_bar(1 + q, 128);  // the four warps of this row group
             if (qleader) {
-                tma_store_2d(&pr.tmWq, wp + q * 32 * 128, n0 / 2, m0 + q * 32);
-                tma_store_2d(&pr.tmSq, wp + L::kWPacked + q * 32 * 16, n0 / 64, m0 + q * 32);
+                tma_store_2d_hint(&pr.tmWq, wp + q * 32 * 128, n0 / 2, m0 + q * 32, l2_evict_first_policy());
+                tma_store_2d_hint(&pr.tmSq, wp + L::kWPacked + q * 32 * 16, n0 / 64, m0 + q * 32, l2_evict_first_policy());
                 bulk_commit();
                 if (pending >= 0) {
                     bulk_wait_read<1>();  // this group's previous stores have read their slot

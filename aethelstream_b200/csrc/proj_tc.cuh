@@ -107,10 +107,10 @@ __global__ void __launch_bounds__(192, 1) proj_grouped_kernel(const __grid_const
                     mbar_arrive_expect_tx(&full[s], L::kStage);
                     uint8_t* a = sA + s * L::kA;
                     if (pr.a_mn) {
-                        tma_load_2d(a, &pr.tmA, &full[s], m0, kb * 64);
-                        tma_load_2d(a + 8192, &pr.tmA, &full[s], m0 + 64, kb * 64);
+                        tma_load_2d_hint(a, &pr.tmA, &full[s], m0, kb * 64, l2_evict_first_policy());
+                        tma_load_2d_hint(a + 8192, &pr.tmA, &full[s], m0 + 64, kb * 64, l2_evict_first_policy());
                     } else {
-                        tma_load_2d(a, &pr.tmA, &full[s], kb * 64, m0);
+                        tma_load_2d_hint(a, &pr.tmA, &full[s], kb * 64, m0, l2_evict_first_policy());
                     }
                     tma_load_2d(sB + s * L::kB, &pr.tmB, &full[s], kb * 64, 0);
                 }
