@@ -236,6 +236,7 @@ struct aeth_galore_ctx {
     double* gnorm_dev = nullptr;
     unsigned int* sq_ticket = nullptr;  // sqnorm_group's completion counter, zero between launches
     unsigned int* work = nullptr;       // b2_adam_group_kernel's block counters, zero between launches
+    uint64_t* clip_epoch = nullptr;     // clip group's exchange counter (device; zeroed on joining)
     uint64_t version = 0;               // completed subspace refreshes (optimizer_version)
     // global clip over several GPUs through peer memory (aeth_galore_set_clip_group)
     ClipGroup group;
@@ -1022,7 +1023,7 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
         (st = ctx_alloc(c, &c->partials, std::max(kSqPartials, kSqGroupMax * kSqChunks))) ||
         (st = ctx_alloc(c, &c->clip_dev, 1)) ||
         (st = ctx_alloc(c, &c->gnorm_dev, 1)) || (st = ctx_alloc(c, &c->sq_ticket, 1)) ||
-        (st = ctx_alloc(c, &c->work, 2)))
+        (st = ctx_alloc(c, &c->work, 2)) || (st = ctx_alloc(c, &c->clip_epoch, 1)))
         return fail(st);
     if (cudaMemset(c->sq_ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
         cudaMemset(c->work, 0, 2 * sizeof(unsigned int)) != cudaSuccess)
@@ -1390,6 +1391,13 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     cudaStream_t st = to_stream(stream);
     const bool ref = ctx->cfg.mode == AETH_MODE_REF;
     float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
+    // Under CUDA graph capture the step records only kernels: no phase events,
+    // and no gradient capture for a subspace refresh, whose schedule depends on
+    // the host step count that a replayed graph cannot follow.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AETH_CUDA(cudaStreamIsCapturing(st, &cap));
+    const bool capturing = cap != cudaStreamCaptureStatusNone;
+    if (capturing && ctx->cfg.svd_refresh) return set_err(AETH_ERR_UNSUPPORTED);
     for (int i = 0; i < n; ++i) AETH_TRY(set_err(capture_if_due(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st)));
     if (ref) {
         // A3 hook: project_and_accumulate for every parameter (backward.rs:510-521).
@@ -1409,7 +1417,7 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     }
     // B200: the layer's projections in grouped launches (one per rank value).
     PhaseMarks pm;
-    AETH_TRY(pm.begin(ctx));
+    if (!capturing) AETH_TRY(pm.begin(ctx));
     AETH_TRY(pm.mark(0, st));
     std::vector<ProjJob> jobs;
     std::vector<int> ranks;
@@ -1505,10 +1513,12 @@ int aeth_galore_set_clip_group(aeth_galore_ctx* ctx, int rank, int world, const 
     if (!handles || !ctx->own_slots || ctx->own_slots_world != world) return set_err(AETH_ERR_CONFIG);
     // fresh slots: epochs restart at 1 (the ranks meet at a barrier after this)
     AETH_CUDA(cudaMemset(ctx->own_slots, 0, sizeof(PeerSlot) * 2 * (size_t)world));
+    AETH_CUDA(cudaMemset(ctx->clip_epoch, 0, sizeof(uint64_t)));
     AETH_CUDA(cudaDeviceSynchronize());
     ClipGroup grp;
     grp.rank = rank;
     grp.world = world;
+    grp.epoch = ctx->clip_epoch;
     grp.timeout_ns = timeout_ns ? timeout_ns : kWaitLimitNs;
     for (int p = 0; p < world; ++p) {
         if (p == rank) {
@@ -1544,10 +1554,12 @@ int aeth_galore_set_clip_group_ptrs(aeth_galore_ctx* ctx, int rank, int world, v
     ctx->peer_maps.clear();
     ctx->group = ClipGroup();
     AETH_CUDA(cudaMemset(ctx->own_slots, 0, sizeof(PeerSlot) * 2 * (size_t)world));
+    AETH_CUDA(cudaMemset(ctx->clip_epoch, 0, sizeof(uint64_t)));
     AETH_CUDA(cudaDeviceSynchronize());
     ClipGroup grp;
     grp.rank = rank;
     grp.world = world;
+    grp.epoch = ctx->clip_epoch;
     grp.timeout_ns = timeout_ns ? timeout_ns : kWaitLimitNs;
     for (int p = 0; p < world; ++p) grp.slots[p] = static_cast<PeerSlot*>(slots[p]);
     ctx->group = grp;

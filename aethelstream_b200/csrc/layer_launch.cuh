@@ -122,7 +122,7 @@ struct PeerSlot {
 struct ClipGroup {
     int rank = 0, world = 1;
     PeerSlot* slots[kClipGroupMax] = {};
-    uint64_t epoch = 0;
+    uint64_t* epoch = nullptr;  // device counter of exchanges, advanced by the kernel (graph-replay safe)
     uint64_t timeout_ns = kWaitLimitNs;
 };
 
@@ -141,7 +141,7 @@ struct SqGroupArgs {
     // [parity][world] entries of {double sum, uint64 epoch}.
     PeerSlot* slots[kClipGroupMax];
     int rank, world;
-    uint64_t epoch;
+    uint64_t* epoch;  // advanced by one per launch by the last CTA
     uint64_t timeout_ns;
     uint32_t* err;
 };
@@ -161,17 +161,19 @@ __device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
 // (bounded) for every member's sum, and returns the total in rank order, so
 // every rank gets the same bits.  On timeout: flags the error and returns NaN.
 __device__ inline double clip_group_total(const SqGroupArgs& a, double local) {
-    const int par = (int)(a.epoch & 1u);
+    const uint64_t epoch = *a.epoch + 1;
+    *a.epoch = epoch;
+    const int par = (int)(epoch & 1u);
     for (int p = 0; p < a.world; ++p) {
         PeerSlot* s = a.slots[p] + par * a.world + a.rank;
         s->sum = local;
-        st_release_sys_u64(&s->epoch, a.epoch);
+        st_release_sys_u64(&s->epoch, epoch);
     }
     double total = 0.0;
     const uint64_t t0 = global_ns();
     for (int p = 0; p < a.world; ++p) {
         PeerSlot* s = a.slots[a.rank] + par * a.world + p;
-        while (ld_acquire_sys_u64(&s->epoch) != a.epoch) {
+        while (ld_acquire_sys_u64(&s->epoch) != epoch) {
             if (global_ns() - t0 > a.timeout_ns) {
                 report_dev_error(a.err, DEVERR_TIMEOUT_PEER);
                 return __longlong_as_double(0x7ff8000000000000ll);
@@ -250,7 +252,7 @@ __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant
 // out[i] = sum of squares of xs[i] (f64).  With clip_out (np <= kSqGroupMax)
 // the same launch also writes the global clip coefficient for max_norm.
 // With a clip group of several GPUs the clip is computed from the sum over
-// the whole group (clip_group_total); group->epoch advances once per launch.
+// the whole group (clip_group_total); the device epoch advances once per launch.
 inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, double* out, double* partials,
                         unsigned int* ticket, float max_norm, float* clip_out, double* gnorm_out, cudaStream_t st,
                         ClipGroup* group = nullptr) {
@@ -282,7 +284,7 @@ inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, doubl
             a.rank = group->rank;
             a.world = group->world;
             for (int p = 0; p < group->world; ++p) a.slots[p] = group->slots[p];
-            a.epoch = ++group->epoch;
+            a.epoch = group->epoch;
             a.timeout_ns = group->timeout_ns;
         }
         // about 8K elements per CTA, at most kSqChunks chunks per accumulator

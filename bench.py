@@ -309,6 +309,29 @@ def run_b200(args):
     params_per_step = sum(m * n for _, m, n in SHAPES)
     value = params_per_step * world * args.steps / (ms / 1000.0)
 
+    # ---- the same steps replayed from CUDA graphs (one per gradient-ring parity; N = 1,
+    # where the step has no host callback): one graph launch per step instead of four
+    graph_ms = None
+    if world == 1:
+        graphs = []
+        for parity in range(2):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                opt.step_layer(keys, ring[parity], weights)
+            graphs.append(gr)
+        for s in range(args.warmup):
+            graphs[s % 2].replay()
+        torch.cuda.synchronize()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for s in range(args.steps):
+            graphs[s % 2].replay()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        graph_ms = g0.elapsed_time(g1) / args.steps
+        del graphs
+
     # ---- end to end through the public API: pinned host grads -> device, step, clip -> host
     host_grads = [g.cpu().pin_memory() for g in ring[0]]
     dev_grads = [torch.empty_like(g) for g in ring[0]]
@@ -375,7 +398,7 @@ def run_b200(args):
                               "ideal_ms": ideal_s * 1000.0, "measured_ms": step_s * 1000.0,
                               "frac": ideal_s / step_s,
                               "phase_ms": per_ms, "phase_gbs": gbs, "phase_bytes": kb,
-                              "host_enqueue_ms_per_step": host_ms},
+                              "host_enqueue_ms_per_step": host_ms, "graph_replay_ms_per_step": graph_ms},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                     "steps": k_e2e},
             # per step: grouped projection, sqnorm + clip (+ peer exchange), grouped Adam, grouped apply;

@@ -269,7 +269,12 @@ int aeth_rsvd_jacobi(float* mat, int n, float* u, aeth_stream_t stream);
  * the exact global-norm clip on the device, then apply_update + zero_accum.
  * When `sq_hook` is set it is called between the sqnorm and apply phases with
  * the device array of per-parameter sqnorms (length n) so a multi-GPU caller
- * can all-reduce it in place on `stream`. */
+ * can all-reduce it in place on `stream`.
+ * The call can be recorded into a CUDA graph (stream capture) and replayed
+ * once per step: it neither synchronises nor allocates, and its counters live
+ * on the device.  While capturing it records no phase events, and it returns
+ * AETH_ERR_UNSUPPORTED when the subspace refresh is on, whose gradient capture
+ * follows the host step count. */
 typedef int (*aeth_sqnorm_hook)(double* sq_dev, int n, aeth_stream_t stream, void* user);
 int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
                      const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out,

@@ -280,3 +280,56 @@ def test_b200_apply_requant_bitexact_large(oracle):
     near = np.abs(xn[:, None] - mids[None, :]).min(axis=1) < 1.5e-6
     assert near.sum() > 20, near.sum()
     opt.close()
+
+
+def test_b200_step_cuda_graph_replay_equals_eager(oracle):
+    """The fused step records into a CUDA graph (no host synchronisation, no
+    allocation, device-side counters); replaying it equals running it eagerly,
+    bit for bit.  Phase timing is skipped while capturing, and a capture with
+    the gradient-driven subspace refresh on is refused."""
+    from aethelstream_b200 import _lib, nf4_quantize
+    specs = [(0, "d_wq", 256, 512, 64), (0, "d_wg", 512, 256, 64)]
+    keys = [(li, nm) for li, nm, *_ in specs]
+    rng = np.random.default_rng(71)
+    ring = [[dev((rng.standard_normal((m, n)) * 1e-3).astype(np.float32)).to(torch.bfloat16)
+             for _, _, m, n, _ in specs] for _ in range(2)]
+    w0 = [(rng.standard_normal((m, n)) * 0.02).astype(np.float32) for _, _, m, n, _ in specs]
+    results = []
+    for use_graph in (False, True):
+        opt = _opt("b200", specs, max_grad_norm=0.01, svd_refresh=False)
+        W = [nf4_quantize(dev(w)) for w in w0]
+        clips = []
+        if use_graph:
+            static = [torch.empty_like(g) for g in ring[0]]
+            for sg, g in zip(static, ring[0]):
+                sg.copy_(g)
+            graph = torch.cuda.CUDAGraph()
+            opt.set_phase_timing(True)
+            with torch.cuda.graph(graph):
+                clip = opt.step_layer(keys, static, W)
+            opt.set_phase_timing(False)
+            assert opt.phase_times()[0] == 0  # nothing recorded during capture
+            for s in range(4):
+                for sg, g in zip(static, ring[s % 2]):
+                    sg.copy_(g)
+                graph.replay()
+                clips.append(float(host(clip)[0]))
+            del graph
+        else:
+            for s in range(4):
+                clips.append(float(host(opt.step_layer(keys, ring[s % 2], W))[0]))
+        results.append((clips, [host(w.packed) for w in W], [host(w.absmax) for w in W],
+                        [host(x) for li, nm, *_ in specs for x in opt.get_state(li, nm)]))
+        opt.close()
+    (c0, p0, a0, s0), (c1, p1, a1, s1) = results
+    assert c0 == c1 and c0[0] < 1.0
+    for x, y in zip(p0 + a0 + s0, p1 + a1 + s1):
+        assert np.array_equal(x, y)
+    # the refresh schedule cannot be replayed: capture is refused with it on
+    opt = _opt("b200", specs, svd_refresh=True)
+    W = [nf4_quantize(dev(w)) for w in w0]
+    graph = torch.cuda.CUDAGraph()
+    with pytest.raises(_lib.AethError):
+        with torch.cuda.graph(graph):
+            opt.step_layer(keys, ring[0], W)
+    opt.close()
