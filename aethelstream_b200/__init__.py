@@ -17,16 +17,19 @@ from .galore import (  # noqa: E402
     GaLoreConfig,
     GaLoreOptimizer,
     LayerRankConfig,
+    LomoState,
     NF4Tensor,
     ProjectorKind,
     deferred_apply_with_clip,
+    lomo_sqnorm,
+    lomo_update,
     nf4_dequantize,
     nf4_quantize,
     randomized_svd,
 )
 
 __all__ = [
-    "AdamWConfig", "AethError", "ClipResult", "GaLoreConfig", "GaLoreOptimizer", "LayerRankConfig", "NF4Tensor",
-    "ProjectorKind", "deferred_apply_with_clip", "load", "nf4_dequantize", "nf4_quantize", "randomized_svd",
+    "AdamWConfig", "AethError", "ClipResult", "GaLoreConfig", "GaLoreOptimizer", "LayerRankConfig", "LomoState", "NF4Tensor",
+    "ProjectorKind", "deferred_apply_with_clip", "load", "lomo_sqnorm", "lomo_update", "nf4_dequantize", "nf4_quantize", "randomized_svd",
     "_lib",
 ]

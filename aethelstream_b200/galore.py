@@ -169,6 +169,39 @@ def randomized_svd(g: torch.Tensor, rank: int, oversampling: int = 10, seed: int
     return p, q
 
 
+class LomoState:
+    """INT8 blockwise momentum of a LOMO-updated NF4 tensor (codec 1: linear,
+    2: dynamic map; one fp32 scale per `block` elements)."""
+
+    def __init__(self, n: int, device, codec: int = L.CODEC_BLOCK_DYNAMIC, block: int = 2048):
+        self.n, self.codec, self.block = n, codec, block
+        self.mom8 = torch.zeros(n, dtype=torch.int8, device=device)
+        fill = 1.0 if codec == L.CODEC_BLOCK_LINEAR else 0.0
+        self.scales = torch.full(((n + block - 1) // block,), fill, dtype=torch.float32, device=device)
+        self.sq = torch.zeros(1, dtype=torch.float64, device=device)
+
+
+def lomo_sqnorm(grad: torch.Tensor, state: LomoState, accumulate: bool = False) -> torch.Tensor:
+    """Pass 1 of the LOMO step: state.sq (+)= sum(g^2) in f64 over the bf16
+    gradient.  Returns state.sq, which a multi-GPU caller all-reduces before
+    lomo_update."""
+    if not accumulate:
+        state.sq.zero_()
+    L.check(L.load().aeth_lomo_sqnorm(_ptr(grad), grad.numel(), _ptr(state.sq), C.c_void_p(_stream_handle())),
+            "aeth_lomo_sqnorm")
+    return state.sq
+
+
+def lomo_update(grad: torch.Tensor, weight: NF4Tensor, state: LomoState, max_norm: float, lr: float,
+                beta: float = 0.9, prequant_out: torch.Tensor | None = None) -> None:
+    """Pass 2: clip from state.sq, INT8 momentum m = beta m + clip g, w -= lr m,
+    NF4 requantisation of w in place (aeth_lomo_update)."""
+    L.check(L.load().aeth_lomo_update(_ptr(grad), grad.numel(), _ptr(state.sq), float(max_norm), float(lr), float(beta),
+                                      state.codec, state.block, _ptr(state.mom8), _ptr(state.scales),
+                                      _ptr(weight.packed), _ptr(weight.absmax), _ptr(prequant_out),
+                                      C.c_void_p(_stream_handle())), "aeth_lomo_update")
+
+
 class GaLoreOptimizer:
     """galore::GaLoreOptimizer on the B200 library (one device per instance)."""
 

@@ -9,10 +9,14 @@ dimension with fixed projectors, INT8 blockwise dynamic-map Adam state, 50
 consecutive steps by default.  A step is one full optimizer step of the block
 through the public API (GaLoreOptimizer.step_layer): projection of all seven
 gradients, exact global-norm clip on the device, Adam, back-projection and the
-NF4 weight write.  Gradients cycle through a two-deep ring generated on the
-device from seeds (step parity, matrix); all weights and state stay resident.
-Under torchrun each rank owns one block (weak scaling); the only exchange is
-the f64 all-reduce of the squared norms for the global clip.
+NF4 weight write -- four kernels, recorded once into a CUDA graph per
+gradient-ring parity and replayed in the timed loop.  A second, eager pass
+with CUDA events at the kernel boundaries gives the per-phase times.
+Gradients cycle through a two-deep ring generated on the device from seeds
+(step parity, matrix); all weights and state stay resident.  Under torchrun
+each rank owns one block (weak scaling); the only exchange is the global
+clip's sum of squared norms, which the squared-norm kernel swaps with the
+peer GPUs over NVLink.
 
 The reference arm (--impl reference) times the reference's CPU algorithm
 (oracle/ port of galore/src/{project,adamw,optimizer}.rs, nf4.rs; the Rust
@@ -45,9 +49,29 @@ CONFIGS = {
     "c1": dict(shapes=[("d_wq", 4096, 4096)],
                workload=("C1: one 4096x4096 weight, GaLore r=128, NF4 weight, bf16 grad, "
                          "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
+    # one Llama-2-13B block per GPU, r = 256, Student-t gradients
+    "c3": dict(shapes=[("d_wq", 5120, 5120), ("d_wk", 5120, 5120), ("d_wv", 5120, 5120), ("d_wo", 5120, 5120),
+                       ("d_wg", 13824, 5120), ("d_wu", 13824, 5120), ("d_wd", 5120, 13824)],
+               rank=256, grad="student_t3",
+               workload=("C3: one Llama-2-13B block per GPU (q/k/v/o 5120x5120, gate/up 13824x5120, down "
+                         "5120x13824), GaLore r=256 one-sided, fixed projectors, NF4 weights, bf16 Student-t(3) "
+                         "grads scaled to std 1e-3, INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
+    # one Llama-2-70B block per GPU, r = 512 (grouped-query k/v 1024x8192)
+    "c4": dict(shapes=[("d_wq", 8192, 8192), ("d_wk", 1024, 8192), ("d_wv", 1024, 8192), ("d_wo", 8192, 8192),
+                       ("d_wg", 28672, 8192), ("d_wu", 28672, 8192), ("d_wd", 8192, 28672)],
+               rank=512,
+               workload=("C4: one Llama-2-70B block per GPU (q/o 8192x8192, k/v 1024x8192, gate/up 28672x8192, "
+                         "down 8192x28672), GaLore r=512 one-sided, fixed projectors, NF4 weights, bf16 grads, "
+                         "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
+    # LOMO sweep over flat NF4 tensors
+    "c5": dict(shapes=[], lomo_sizes=[1 << k for k in (20, 22, 24, 26, 28, 30)],
+               workload=("C5: LOMO sweep, flat NF4 tensors of 2^20 .. 2^30 elements per GPU, bf16 grads N(0,1e-3), "
+                         "global-norm clip 1.0, INT8 blockwise-2048 dynamic-map momentum beta 0.9, lr 1e-3, fused "
+                         "NF4 requant")),
 }
 SHAPES = CONFIGS["c2"]["shapes"]
 RANK = 128
+GRAD = "normal"
 STATE_BLOCK = 2048
 WORKLOAD = CONFIGS["c2"]["workload"]
 
@@ -207,14 +231,190 @@ def run_reference(args):
         done += samp.step()
     dt = time.perf_counter() - t0
     v = done / dt
-    sample = (f"1/64 of each matrix's output rows per step (2 of 128 rows of P^T G, m/64 rows of the weight delta "
-              f"and NF4 weight apply) over the 7 matrices of the C2 block; params/s = 1/64 x 202.4M x steps / time")
+    total = sum(m * n for _, m, n in SHAPES)
+    sample = (f"1/64 of each matrix's output rows per step (1/64 of the rows of P^T G, m/64 rows of the weight "
+              f"delta and NF4 weight apply) over the {len(SHAPES)} matrices of the {args.config.upper()} block; "
+              f"params/s = 1/64 x {total / 1e6:.1f}M x steps / time")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * 202.4e6 / v,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(m * n for _, m, n in SHAPES) / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD + " -- reference CPU algorithm (two-sided fp32 GaLore, per-tensor "
                                               "INT8, NF4 dequant + fp32 apply)", "parallelism": "host threads"},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+LOMO_BYTES = 7.125          # per element and step: NF4 r/w 1.125, bf16 grad twice 4, INT8 momentum r/w 2
+LOMO_UPDATE_BYTES = 5.125   # the update kernel alone (one gradient read)
+
+
+def lomo_cpu_baseline(n=1 << 21):
+    """The oracle's LOMO step (restated reference algorithm, single thread) on n elements."""
+    import numpy as np
+    from oracle import oracle as O
+    O.build()
+    rng = np.random.default_rng(5)
+    g = O.f32_to_bf16_bits((rng.standard_normal(n) * 1e-3).astype(np.float32))
+    wp, wa = O.nf4_quantize((rng.standard_normal(n) * 0.02).astype(np.float32))
+    m8 = np.zeros(n, np.int8)
+    ms = np.zeros((n + 2047) // 2048, np.float32)
+    t0 = time.perf_counter()
+    k = 0
+    while time.perf_counter() - t0 < 10.0 or k < 2:
+        sq = O.lomo_sqnorm(g)
+        m8, ms, wp, wa, _ = O.lomo_update(g, float(O.clip_coeff(sq, 1.0)), 0.9, 1e-3, 2048, O.CODEC_DYNAMIC, m8, ms,
+                                          wp, wa)
+        k += 1
+    dt = time.perf_counter() - t0
+    return n * k / dt, dt, n, k
+
+
+def run_lomo(args):
+    """C5: the LOMO fused full-rank step (aeth_lomo_sqnorm + aeth_lomo_update)
+    swept over tensor sizes; weak scaling over ranks (each rank its own tensor,
+    the squared-norm sum all-reduced for the global clip)."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from aethelstream_b200 import LomoState, lomo_sqnorm, lomo_update, nf4_quantize
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    sweep = []
+    clk = e2e = None
+    for n in CONFIGS["c5"]["lomo_sizes"]:
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1000 + 7 * rank)
+        w = torch.randn(n, generator=gen, device=dev) * 0.02
+        W = nf4_quantize(w)
+        del w
+        grads = [(torch.randn(n, generator=gen, device=dev) * 1e-3).to(torch.bfloat16) for _ in range(2)]
+        st = LomoState(n, dev)
+
+        def step(s, ev=None):
+            g = grads[s % 2]
+            lomo_sqnorm(g, st)
+            if world > 1:
+                dist.all_reduce(st.sq)
+            if ev is not None:
+                ev.record(stream)
+            lomo_update(g, W, st, 1.0, 1e-3, 0.9)
+
+        for s in range(args.warmup):
+            step(s)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        big = n == CONFIGS["c5"]["lomo_sizes"][-1]
+        clocks = ClockSampler(local) if big else None
+        if clocks:
+            clocks.start()
+            time.sleep(0.3)
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        marks[0].record(stream)
+        for s in range(args.steps):
+            step(s, mids[s])
+            marks[s + 1].record(stream)
+        torch.cuda.synchronize()
+        if clocks:
+            clk = clocks.stop()
+        total = marks[0].elapsed_time(marks[-1])
+        upd = sum(mids[s].elapsed_time(marks[s + 1]) for s in range(args.steps))
+        t = torch.tensor([total, upd], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total, upd = t.tolist()
+        ms, ums = total / args.steps, upd / args.steps
+        sweep.append({"n": n, "ms_per_step": ms, "params_per_s": world * n / (ms / 1000.0),
+                      "step_gbs_per_gpu": LOMO_BYTES * n / (ms / 1000.0) / 1e9,
+                      "update_kernel_ms": ums, "update_kernel_gbs": LOMO_UPDATE_BYTES * n / (ums / 1000.0) / 1e9})
+        if big:
+            # end to end at the largest size: pinned host gradient -> device, both passes, squared norm -> host
+            host_g = grads[0].cpu().pin_memory()
+            sq_host = torch.empty(1, dtype=torch.float64).pin_memory()
+            k_e2e = 3
+
+            def e2e_step():
+                grads[1].copy_(host_g, non_blocking=True)
+                step(1)
+                sq_host.copy_(st.sq, non_blocking=True)
+                stream.synchronize()
+
+            e2e_step()
+            if world > 1:
+                dist.barrier()
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(k_e2e):
+                e2e_step()
+            a1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([a0.elapsed_time(a1)], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e = {"value": world * n * k_e2e / (t.item() / 1000.0), "unit": UNIT,
+                   "h2d_bytes_per_step": 2 * n, "d2h_bytes_per_step": 8, "steps": k_e2e}
+            del host_g
+        del W, grads, st
+        torch.cuda.empty_cache()
+    if rank == 0:
+        hbm, _, _, peak_kind = load_peaks()
+        top = sweep[-1]
+        line = {
+            "metric": "params updated/s (LOMO NF4 + INT8-momentum step)", "value": top["params_per_s"],
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": top["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) bf16 grads)",
+            "config": {"workload": CONFIGS["c5"]["workload"], "params_per_gpu_step": top["n"],
+                       "l2": "inputs larger than L2 at n >= 2^26 (the value is the 2^30 point)",
+                       "parallelism": f"tensor-sharded x{world}"},
+            "roofline": {"bound": "hbm", "kernel": "lomo_update_kernel (clip, INT8 momentum, NF4 dequant/update/requant)",
+                         "achieved": top["update_kernel_gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": top["update_kernel_gbs"] / hbm, "traffic": None,
+                         "algorithmic_bytes_per_launch": LOMO_UPDATE_BYTES * top["n"],
+                         "launch_ms": top["update_kernel_ms"], "peak_kind": peak_kind},
+            "roofline_step": {"algorithmic_bytes": LOMO_BYTES * top["n"],
+                              "ideal_ms": LOMO_BYTES * top["n"] / (hbm * 1e9) * 1000.0,
+                              "measured_ms": top["ms_per_step"],
+                              "frac": LOMO_BYTES * top["n"] / (hbm * 1e9) / (top["ms_per_step"] / 1000.0)},
+            "sweep": sweep,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, dt, n_s, k = lomo_cpu_baseline()
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
+                                    "sample": f"oracle LOMO step (norm + update), {n_s} elements x {k} steps, single "
+                                              f"thread, {dt:.1f} s"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_lomo_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    v, dt, n_s, k = lomo_cpu_baseline()
+    sample = f"oracle LOMO step (norm + update), {n_s} elements x {k} steps, single thread, {dt:.1f} s"
+    line = {"impl": "reference", "metric": "params updated/s (LOMO NF4 + INT8-momentum step)", "value": v,
+            "unit": UNIT, "n_gpus": args.gpus, "steps": k, "warmup": 1, "ms_per_step": 1000.0 * n_s / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": CONFIGS["c5"]["workload"] + " -- restated LOMO step on the host (the reference "
+                                   "has no LOMO; full-rank references are standard_adamw.rs and test_resume.rs SGD)",
+                       "parallelism": "one host thread"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -255,7 +455,13 @@ def run_b200(args):
         gs = []
         for i, (name, m, n) in enumerate(SHAPES):
             gen.manual_seed(7919 * (parity + 1) + 100 * layer + i)
-            gs.append((torch.randn(m, n, generator=gen, device=dev) * 1e-3).to(torch.bfloat16))
+            g = torch.randn(m, n, generator=gen, device=dev)
+            if GRAD == "student_t3":
+                # t(3) = z / sqrt(chi2_3 / 3), standard deviation sqrt(3)
+                chi2 = sum(torch.randn(m, n, generator=gen, device=dev) ** 2 for _ in range(3))
+                g = g / torch.sqrt(chi2 / 3.0) / (3.0 ** 0.5)
+            gs.append((g * 1e-3).to(torch.bfloat16))
+            del g
         ring.append(gs)
     keys = [(layer, name) for name, _, _ in SHAPES]
     stream = torch.cuda.current_stream()
@@ -278,42 +484,13 @@ def run_b200(args):
     for s in range(args.warmup):
         step(s)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)  # let the sampler start
-    opt.set_phase_timing(True)  # CUDA events at the phase boundaries, on this stream
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    h0 = time.perf_counter()
-    for s in range(args.steps):
-        step(s)
-    host_ms = (time.perf_counter() - h0) * 1000.0 / args.steps  # enqueue time only (the loop does not wait)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    opt.set_phase_timing(False)
-    n_timed, phase_ms = opt.phase_times()
-    assert n_timed == args.steps, (n_timed, args.steps)
-    if world > 1:
-        dist.barrier()
-    ms = t0.elapsed_time(t1)
-    t = torch.tensor([ms] + [phase_ms[k] for k in opt.PHASES], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t[0].item()
-    phase_ms = dict(zip(opt.PHASES, t[1:].tolist()))
-    params_per_step = sum(m * n for _, m, n in SHAPES)
-    value = params_per_step * world * args.steps / (ms / 1000.0)
 
-    # ---- the same steps replayed from CUDA graphs (one per gradient-ring parity; N = 1,
-    # where the step has no host callback): one graph launch per step instead of four
-    graph_ms = None
-    if world == 1:
-        graphs = []
+    # The timed steps replay the step from CUDA graphs, one per gradient-ring
+    # parity: the same four kernels per step, launched as one graph.  The step
+    # records into a graph whenever it has no host callback (every N with the
+    # peer clip group); with the NCCL hook it runs eagerly.
+    graphs = []
+    if hook is None:
         for parity in range(2):
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):
@@ -322,15 +499,58 @@ def run_b200(args):
         for s in range(args.warmup):
             graphs[s % 2].replay()
         torch.cuda.synchronize()
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for s in range(args.steps):
+    # every rank took the same branch (hook is None on all ranks or on none)
+
+    def timed_step(s):
+        if graphs:
             graphs[s % 2].replay()
-        g1.record(stream)
-        torch.cuda.synchronize()
-        graph_ms = g0.elapsed_time(g1) / args.steps
-        del graphs
+        else:
+            step(s)
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)  # let the sampler start
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    h0 = time.perf_counter()
+    for s in range(args.steps):
+        timed_step(s)
+    host_ms = (time.perf_counter() - h0) * 1000.0 / args.steps  # enqueue time only (the loop does not wait)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+
+    # Per-phase breakdown: the same steps run eagerly with CUDA events at the
+    # phase boundaries (events between kernels add a little to the total).
+    opt.set_phase_timing(True)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        step(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    opt.set_phase_timing(False)
+    n_timed, phase_ms = opt.phase_times()
+    assert n_timed == args.steps, (n_timed, args.steps)
+    eager_ms = e0.elapsed_time(e1)
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([ms, eager_ms] + [phase_ms[k] for k in opt.PHASES], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, eager_ms = t[0].item(), t[1].item()
+    phase_ms = dict(zip(opt.PHASES, t[2:].tolist()))
+    params_per_step = sum(m * n for _, m, n in SHAPES)
+    value = params_per_step * world * args.steps / (ms / 1000.0)
+    del graphs
 
     # ---- end to end through the public API: pinned host grads -> device, step, clip -> host
     host_grads = [g.cpu().pin_memory() for g in ring[0]]
@@ -384,6 +604,7 @@ def run_b200(args):
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) bf16 grads)",
             "config": {"workload": WORKLOAD, "params_per_gpu_step": params_per_step, "rank": RANK,
+                       "launch": "CUDA graph replay of the step" if hook is None else "eager (host hook)",
                        "state": "int8 dynamic-map, 2048-element blocks", "parallelism": f"layer-sharded x{world}",
                        "clip_exchange": clip_exchange,
                        "l2": (f"inputs larger than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients per "
@@ -398,7 +619,8 @@ def run_b200(args):
                               "ideal_ms": ideal_s * 1000.0, "measured_ms": step_s * 1000.0,
                               "frac": ideal_s / step_s,
                               "phase_ms": per_ms, "phase_gbs": gbs, "phase_bytes": kb,
-                              "host_enqueue_ms_per_step": host_ms, "graph_replay_ms_per_step": graph_ms},
+                              "host_enqueue_ms_per_step": host_ms,
+                              "eager_ms_per_step_with_phase_events": eager_ms / args.steps},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                     "steps": k_e2e},
             # per step: grouped projection, sqnorm + clip (+ peer exchange), grouped Adam, grouped apply;
@@ -410,7 +632,7 @@ def run_b200(args):
             v, dt = cpu_baseline(1.0 / 128, 1)
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
                                     "sample": "reference CPU algorithm (oracle port), 1/128 of each matrix's output "
-                                              f"rows over the 7 C2 matrices, single thread, {dt:.1f} s"}
+                                              f"rows over the {len(SHAPES)} matrices of the block, single thread, {dt:.1f} s"}
         print(json.dumps(line), flush=True)
     opt.close()
     if world > 1:
@@ -429,11 +651,17 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    global SHAPES, WORKLOAD
+    global SHAPES, WORKLOAD, RANK, GRAD
     SHAPES = CONFIGS[args.config]["shapes"]
     WORKLOAD = CONFIGS[args.config]["workload"]
+    RANK = CONFIGS[args.config].get("rank", 128)
+    GRAD = CONFIGS[args.config].get("grad", "normal")
     if args.impl == "reference":
+        if args.config == "c5":
+            return run_lomo_reference(args)
         return run_reference(args)
+    if args.config == "c5":
+        return run_lomo(args)
     return run_b200(args)
 
 

@@ -231,3 +231,23 @@ def test_fast_paths_exhaustive(lib, which):
     assert lib.aeth_selfcheck(which, C.byref(bad)) == 0
     assert bad.value == 0
     assert lib.aeth_selfcheck(3, C.byref(bad)) == -1  # unknown check
+
+
+def test_lomo_python_wrappers(oracle, L):
+    """lomo_sqnorm / lomo_update (the Python face of aeth_lomo_*) against the oracle's LOMO step."""
+    from aethelstream_b200 import LomoState, lomo_sqnorm, lomo_update, nf4_quantize
+    rng = np.random.default_rng(19)
+    n = 1 << 16
+    g_bits = oracle.f32_to_bf16_bits((rng.standard_normal(n) * 1e-3).astype(np.float32))
+    w = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    W = nf4_quantize(dev(w))
+    wp, wa = host(W.packed), host(W.absmax)
+    st = LomoState(n, DEV)
+    g = bf16_dev_from_bits(g_bits)
+    sq = lomo_sqnorm(g, st)
+    lomo_update(g, W, st, max_norm=1.0, lr=1e-3, beta=0.9)
+    clip = oracle.clip_coeff(float(host(sq)[0]), 1.0)
+    m8, ms, wp_ref, wa_ref, _ = oracle.lomo_update(g_bits, float(clip), 0.9, 1e-3, 2048, oracle.CODEC_DYNAMIC,
+                                                   np.zeros(n, np.int8), np.zeros(n // 2048, np.float32), wp, wa)
+    assert np.array_equal(host(st.mom8), m8) and np.array_equal(host(st.scales), ms)
+    assert np.array_equal(host(W.packed), wp_ref) and np.array_equal(host(W.absmax), wa_ref)
