@@ -1,6 +1,8 @@
 // layer_launch.cuh -- host launchers for the grouped (whole-layer) kernels:
 // projection (K4), squared norms, back-projection + NF4 write (K6).
 #pragma once
+#include <vector>
+
 #include "adam.cuh"
 #include "apply_tc.cuh"
 #include "gemm_tc.cuh"
@@ -16,6 +18,7 @@ struct ProjJob {
     const uint16_t* projT;  // bf16 r x s (s = min(m, n))
     float* racc;            // fp32 l x r
     int m, n;
+    int ldr = 0;            // row stride of racc in floats (0: r); a column slice of a wider R
 };
 
 template <int BN>
@@ -63,8 +66,8 @@ int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) 
         if (right) AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)j.m, j.n, 64, 128, true));
         else AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)j.m, j.n, 64, 64, true));
         AETH_TRY(make_tmap_16b(&p.tmB, j.projT, (uint64_t)s, (uint64_t)r, s, 64, BN, true));
-        AETH_TRY(make_tmap_2d(&p.tmC, j.racc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)r, (uint64_t)l, r, 32, 128,
-                              CU_TENSOR_MAP_SWIZZLE_128B));
+        AETH_TRY(make_tmap_2d(&p.tmC, j.racc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)r, (uint64_t)l,
+                              j.ldr > 0 ? j.ldr : r, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B));
         p.a_mn = right ? 0 : 1;
         p.kb_total = (s + 63) / 64;
         p.splits = (p.kb_total + kb_target - 1) / kb_target;
@@ -89,9 +92,27 @@ int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) 
     return AETH_OK;
 }
 
-// Projects and accumulates every job; jobs must share the rank r.
+// Projects and accumulates every job; jobs must share the rank r.  Ranks
+// above 256 (one MMA's N) run as column slices of at most 256 of R, each a
+// launch over its rows of projT: R[:, c0:c1] += G Q[:, c0:c1].  The gradient
+// is read once per slice.
 inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t st) {
-    if (r <= 0 || r > 256 || r % 8 != 0) return AETH_ERR_UNSUPPORTED;
+    if (r <= 0 || r > 1024 || r % 8 != 0) return AETH_ERR_UNSUPPORTED;
+    if (r > 256) {
+        if (r % 64 != 0) return AETH_ERR_UNSUPPORTED;
+        for (int c0 = 0; c0 < r; c0 += 256) {
+            const int w = std::min(256, r - c0);
+            std::vector<ProjJob> slice(jobs, jobs + nj);
+            for (ProjJob& j : slice) {
+                const int s = std::min(j.m, j.n);
+                j.projT += (size_t)c0 * s;
+                j.racc += c0;
+                j.ldr = r;
+            }
+            AETH_TRY(proj_grouped_launch(slice.data(), nj, w, st));
+        }
+        return AETH_OK;
+    }
     for (int off = 0; off < nj; off += kProjMaxProblems) {
         const int cnt = std::min(kProjMaxProblems, nj - off);
         if (r <= 64) AETH_TRY(proj_grouped_launch_bn<64>(jobs + off, cnt, r, st));
@@ -311,14 +332,15 @@ struct ApplyJob {
 };
 
 // The grouped kernel needs n % 256 == 0 (absmax rows a multiple of 16 bytes)
-// and r % 8 == 0, r <= 256.
+// and r % 8 == 0; the rank is the MMAs' K, taken 64 at a time.
 inline bool apply_grouped_supported(int m, int n, int r) {
-    return m > 0 && n > 0 && n % 256 == 0 && r > 0 && r % 8 == 0 && r <= 256;
+    return m > 0 && n > 0 && n % 256 == 0 && r > 0 && r % 8 == 0 && r <= 1024;
 }
 
 inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
-    // Two operand stages suffice: a unit's MMAs (K = r <= 256) take a fraction
-    // of its epilogue, and the freed 48 KB hold the replicated byte table.
+    // Two operand stages: up to r = 256 a unit's MMAs take a fraction of its
+    // epilogue, and the freed 48 KB hold the replicated byte table; larger
+    // ranks stream more k-blocks through the same two stages.
     constexpr int STAGES = 2;
     using L = ApplyLayout<STAGES>;
     static_assert(1024 + L::kTotal <= 227 * 1024, "apply kernel shared memory above the per-CTA limit");

@@ -76,7 +76,7 @@ STATE_BLOCK = 2048
 WORKLOAD = CONFIGS["c2"]["workload"]
 
 
-def algorithmic(shapes=None, r=RANK):
+def algorithmic(shapes=None, r=None):
     """Algorithmic bytes and flops per step, split by phase.
 
     projection phase (K4): read bf16 G (2 B/elem) + projector (2 s r).
@@ -84,6 +84,7 @@ def algorithmic(shapes=None, r=RANK):
     read + write (4 r l), block scales (8 r l / 2048), projector (2 s r).
     Flops: 2 r m n per GEMM (projection and back-projection) + ~12 r l (Adam).
     """
+    r = r or RANK
     bp = ba = fp = fa = 0
     for _, m, n in (shapes or SHAPES):
         s, l = min(m, n), max(m, n)
@@ -102,7 +103,7 @@ KERNEL_NAMES = {
 }
 
 
-def kernel_bytes(shapes=None, r=RANK):
+def kernel_bytes(shapes=None, r=None):
     """Compulsory HBM bytes per launch of each step kernel (one launch each per step).
 
     projection: read G bf16 (2 B/elem) + projector (2 s r), write R f32 (4 r l).
@@ -111,6 +112,7 @@ def kernel_bytes(shapes=None, r=RANK):
           block scales read + write (16 r l / 2048).
     apply: NF4 weight read + write (2 x 0.5625 B/elem), N bf16 read (2 r l), projector (2 s r).
     """
+    r = r or RANK
     out = dict.fromkeys(("projection", "sqnorm_clip", "adam", "apply"), 0.0)
     for _, m, n in (shapes or SHAPES):
         s, l = min(m, n), max(m, n)

@@ -81,7 +81,8 @@ def test_ref_mode_fp32_weight_inplace(oracle):
 
 # --------------------------------------------------------------------------- B200
 @pytest.mark.parametrize("m,n,r,codec", [(256, 128, 32, "linear"), (128, 384, 64, "linear"),
-                                         (512, 512, 128, "dynamic"), (384, 256, 64, "dynamic")])
+                                         (512, 512, 128, "dynamic"), (384, 256, 64, "dynamic"),
+                                         (1024, 512, 512, "dynamic"), (512, 768, 384, "dynamic")])
 def test_b200_step_matches_oracle(oracle, m, n, r, codec):
     from aethelstream_b200 import nf4_quantize
     rng = np.random.default_rng(m + n + r)
