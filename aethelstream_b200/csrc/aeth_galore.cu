@@ -1780,10 +1780,19 @@ int aeth_lomo_update(const void* grad_bf16, int64_t n, const double* sq_dev, flo
         (reinterpret_cast<uintptr_t>(w_packed) & 3))
         return set_err(AETH_ERR_UNSUPPORTED);
     AETH_TRY(codec_maps_ensure());
-    int64_t nb = n / 2048;
-    lomo_update_kernel<<<grid_for(nb, 1, 148 * 8), 256, 0, to_stream(stream)>>>(
-        static_cast<const uint16_t*>(grad_bf16), n, sq_dev, max_norm, lr, beta, codec, mom8, mom_scales, w_packed,
-        w_absmax, prequant_out);
+    if ((reinterpret_cast<uintptr_t>(mom8) & 15) || (reinterpret_cast<uintptr_t>(w_packed) & 7) ||
+        (prequant_out && (reinterpret_cast<uintptr_t>(prequant_out) & 15)))
+        return set_err(AETH_ERR_UNSUPPORTED);
+    // one resident wave: the kernel strides over the blocks and prefetches the next one
+    const int64_t nb = n / 2048;
+    const uint16_t* gb = static_cast<const uint16_t*>(grad_bf16);
+    auto kern = codec == AETH_CODEC_BLOCK_DYNAMIC ? lomo_update_kernel<AETH_CODEC_BLOCK_DYNAMIC>
+                                                  : lomo_update_kernel<AETH_CODEC_BLOCK_LINEAR>;
+    int per_sm = 0;
+    AETH_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, 0));
+    const int grid = (int)std::min<int64_t>(nb, (int64_t)num_sms() * std::max(per_sm, 1));
+    kern<<<grid, 128, 0, to_stream(stream)>>>(gb, n, sq_dev, max_norm, lr, beta, mom8, mom_scales, w_packed, w_absmax,
+                                              prequant_out);
     AETH_LAUNCH_CHECK();
     return AETH_OK;
 }

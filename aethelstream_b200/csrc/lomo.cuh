@@ -42,84 +42,158 @@ __global__ void __launch_bounds__(256) lomo_sqnorm_kernel(const uint16_t* __rest
     }
 }
 
-// One CTA of 256 threads per momentum block of 2048 elements; thread t owns 8
-// consecutive elements, so 8 consecutive threads form one NF4 block of 64.
-__global__ void __launch_bounds__(256) lomo_update_kernel(const uint16_t* __restrict__ g, int64_t n,
+// Shared tables of the update kernel: the NF4 byte table (dequant), the
+// 33-bucket classifier of the fused apply epilogue (requant), and for the
+// dynamic codec the signed map and its bucket table.
+struct LomoTables {
+    float2 byte_lut[256];
+    uint32_t bucket32[33];
+    uint32_t pad_[3];
+    float dm[256];
+    uint2 dlut[kDmapLutEntries];
+};
+
+// One CTA of 128 threads per momentum block of 2048 elements and iteration;
+// thread t owns 16 consecutive elements, so 4 consecutive threads form one
+// NF4 block of 64 and each warp a quarter of the momentum block.  The next
+// block's gradient, momentum and weight words are loaded while the current
+// one is processed.  Element pairs go through the packed f32x2 multiply;
+// sums that must round twice add with scalar adds (a packed add of fresh
+// products would be fused).
+template <int CODEC>
+__global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __restrict__ g, int64_t n,
                                                           const double* __restrict__ sq, float max_norm, float lr,
-                                                          float beta, int codec, int8_t* __restrict__ mom8,
+                                                          float beta, int8_t* __restrict__ mom8,
                                                           float* __restrict__ mom_scales, uint8_t* __restrict__ wp,
                                                           float* __restrict__ wa, float* __restrict__ prequant) {
-    __shared__ Nf4Tables tab;
-    __shared__ float dm[256];
-    __shared__ uint2 dlut[kDmapLutEntries];
-    __shared__ float red[8];
-    nf4_tables_init(&tab, threadIdx.x, blockDim.x);
-    if (codec == AETH_CODEC_BLOCK_DYNAMIC) {
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) dm[i] = c_dmap_signed[i];
-        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) dlut[i] = g_dmap_lut[0][i];
+    __shared__ LomoTables tab;
+    __shared__ float red[2][4];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+        tab.byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
+    for (int b = threadIdx.x; b < 33; b += blockDim.x) {
+        float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
+        int below = 0, code = -1;
+        float thr = 2.0f;
+        for (int k = 0; k < 15; ++k) {
+            float mid = (c_nf4_codes[k] + c_nf4_codes[k + 1]) * 0.5f;
+            if (mid < lo) below = k + 1;
+            else if (mid < hi) { thr = mid; code = k; }
+        }
+        if (code < 0) code = below;
+        tab.bucket32[b] = (__float_as_uint(-thr) & ~15u) | (uint32_t)(code + 1);
+    }
+    if (CODEC == AETH_CODEC_BLOCK_DYNAMIC) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) tab.dm[i] = c_dmap_signed[i];
+        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) tab.dlut[i] = g_dmap_lut[0][i];
     }
     __syncthreads();
-    double gnorm = sqrt(*sq);
+    const uint32_t bucket_bias = smem_u32_addr(tab.bucket32) - (0x4B400000u << 2);
+    const double gnorm = sqrt(*sq);
     float clip = (float)((double)max_norm / (gnorm + 1e-6));
     clip = clip < 1.0f ? clip : 1.0f;
+    const float2 clip2 = make_float2(clip, clip), beta2 = make_float2(beta, beta), nlr2 = make_float2(-lr, -lr);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t n_blocks = n / 2048;
-    for (int64_t b = blockIdx.x; b < n_blocks; b += gridDim.x) {
-        const int64_t e0 = b * 2048 + threadIdx.x * 8;
-        const float ms = mom_scales[b];
-        uint4 gu = __ldg(reinterpret_cast<const uint4*>(g + e0));
-        uint2 mq = *reinterpret_cast<const uint2*>(mom8 + e0);
-        uint32_t wq = *reinterpret_cast<const uint32_t*>(wp + e0 / 2);
-        float wamax = wa[e0 / 64];
-        float w[8], mo[8];
-        nf4_dequant_word(wq, wamax, tab.byte_lut, w);
-        uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
-        uint32_t mw[2] = {mq.x, mq.y};
+    int64_t b = blockIdx.x;
+    uint4 g0 = make_uint4(0u, 0u, 0u, 0u), g1 = g0, mq = g0;
+    uint2 wq = make_uint2(0u, 0u);
+    float ms = 0.0f, wamax = 0.0f;
+    auto fetch = [&](int64_t blk) {
+        const int64_t e = blk * 2048 + threadIdx.x * 16;
+        g0 = __ldcs(reinterpret_cast<const uint4*>(g + e));
+        g1 = __ldcs(reinterpret_cast<const uint4*>(g + e + 8));
+        mq = *reinterpret_cast<const uint4*>(mom8 + e);
+        wq = *reinterpret_cast<const uint2*>(wp + e / 2);
+        wamax = wa[e / 64];
+        ms = mom_scales[blk];
+    };
+    if (b < n_blocks) fetch(b);
+    for (int it = 0; b < n_blocks; b += gridDim.x, ++it) {
+        const int64_t e0 = b * 2048 + threadIdx.x * 16;
+        float w[16], mo[16];
+        // NF4 dequant (byte table), gradient, momentum decode
+        nf4_dequant_word(wq.x, wamax, tab.byte_lut, w);
+        nf4_dequant_word(wq.y, wamax, tab.byte_lut, w + 8);
+        const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const uint32_t mw[4] = {mq.x, mq.y, mq.z, mq.w};
+        const float cur_ms = ms;
+        if (b + gridDim.x < n_blocks) fetch(b + gridDim.x);
+        const float2 ms2 = make_float2(cur_ms, cur_ms);
         float am = 0.0f, aw = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            uint16_t gb = (uint16_t)((gw[k >> 1] >> (16 * (k & 1))) & 0xffffu);
-            float gs = __fmul_rn(bf16_bits_to_f32(gb), clip);
-            int8_t q = (int8_t)((mw[k >> 2] >> (8 * (k & 3))) & 0xffu);
-            float m0 = codec == AETH_CODEC_BLOCK_LINEAR ? __fmul_rn((float)q, ms) : __fmul_rn(dm[(uint8_t)q], ms);
-            mo[k] = __fadd_rn(__fmul_rn(beta, m0), gs);
-            w[k] = __fsub_rn(w[k], __fmul_rn(lr, mo[k]));
-            am = fmaxf(am, fabsf(mo[k]));
-            aw = fmax_nan(aw, fabsf(w[k]));
+        for (int k = 0; k < 16; k += 2) {
+            const uint32_t gp = gw[k >> 1];
+            const float2 gg = mul2_rn(make_float2(__uint_as_float(gp << 16), __uint_as_float(gp & 0xffff0000u)), clip2);
+            const uint32_t mword = mw[k >> 2];
+            const int sh = 8 * (k & 3);
+            float2 m0;
+            if (CODEC == AETH_CODEC_BLOCK_DYNAMIC)
+                m0 = make_float2(tab.dm[(mword >> sh) & 0xffu], tab.dm[(mword >> (sh + 8)) & 0xffu]);
+            else
+                m0 = make_float2((float)(int8_t)(mword >> sh), (float)(int8_t)(mword >> (sh + 8)));
+            m0 = mul2_rn(m0, ms2);
+            // m = fl(fl(beta m) + g clip); w = fl(w - fl(lr m))
+            const float2 mm = add2_sep(mul2_rn(beta2, m0), gg);
+            const float2 ww = add2_sep(make_float2(w[k], w[k + 1]), mul2_rn(mm, nlr2));
+            mo[k] = mm.x;
+            mo[k + 1] = mm.y;
+            w[k] = ww.x;
+            w[k + 1] = ww.y;
+            am = fmax3(am, fabsf(mm.x), fabsf(mm.y));
+            aw = fmax3_nan(aw, fabsf(ww.x), fabsf(ww.y));
         }
-        // NF4 block absmax across the 8 lanes owning this 64-element block.
+        // NF4 block absmax over the 4 threads of the block (NaN-propagating, as the reference's max)
         aw = fmax_nan(aw, __shfl_xor_sync(0xffffffffu, aw, 1));
         aw = fmax_nan(aw, __shfl_xor_sync(0xffffffffu, aw, 2));
-        aw = fmax_nan(aw, __shfl_xor_sync(0xffffffffu, aw, 4));
-        uint32_t pk[1];
-        nf4_quant_regs<8>(w, aw, tab.bucket, pk);
-        *reinterpret_cast<uint32_t*>(wp + e0 / 2) = pk[0];
-        if ((threadIdx.x & 7) == 0) wa[e0 / 64] = nf4_store_amax(aw);
-        if (prequant) {
-            *reinterpret_cast<float4*>(prequant + e0) = make_float4(w[0], w[1], w[2], w[3]);
-            *reinterpret_cast<float4*>(prequant + e0 + 4) = make_float4(w[4], w[5], w[6], w[7]);
+        const bool bad = !(aw <= 3.402823466e38f);
+        const float safe = nf4_safe(aw), inv = __frcp_rn(safe);
+        uint32_t pk0 = 0u, pk1 = 0u;
+        float mind = bad ? 0.0f : 1.0f;
+        if (!bad) {
+            pk0 = nf4_fast_word8_s(w, inv, bucket_bias, mind);
+            pk1 = nf4_fast_word8_s(w + 8, inv, bucket_bias, mind);
         }
-        // Momentum block absmax across the CTA.
+        if (mind < kNf4NearWindow32) {  // rare: exact decisions next to a boundary, or a non-finite block
+            if (bad) {
+                pk0 = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe);
+                pk1 = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe);
+            } else {
+                pk0 = nf4_fix_word8(pk0, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], inv, safe, bucket_bias);
+                pk1 = nf4_fix_word8(pk1, w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], inv, safe,
+                                    bucket_bias);
+            }
+        }
+        *reinterpret_cast<uint2*>(wp + e0 / 2) = make_uint2(pk0, pk1);
+        if ((threadIdx.x & 3) == 0) wa[e0 / 64] = nf4_store_amax(aw);
+        if (prequant) {
+#pragma unroll
+            for (int k = 0; k < 16; k += 4)
+                *reinterpret_cast<float4*>(prequant + e0 + k) = make_float4(w[k], w[k + 1], w[k + 2], w[k + 3]);
+        }
+        // momentum block absmax over the CTA (double-buffered slots: one barrier per block)
         am = warp_max(am);
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
+        if (lane == 0) red[it & 1][warp] = am;
         __syncthreads();
-        float bm = 0.0f;
+        const float bm = fmax3(fmaxf(red[it & 1][0], red[it & 1][1]), red[it & 1][2], red[it & 1][3]);
+        uint32_t out[4] = {0u, 0u, 0u, 0u};
+        if (CODEC == AETH_CODEC_BLOCK_LINEAR) {
+            const float nsm = lin_scale_from_absmax(bm), linv = lin_inv(nsm);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) bm = fmaxf(bm, red[i]);
-        uint32_t out[2] = {0u, 0u};
-        if (codec == AETH_CODEC_BLOCK_LINEAR) {
-            float nsm = lin_scale_from_absmax(bm), inv = lin_inv(nsm);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) out[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(mo[k], inv)) << (8 * (k & 3));
+            for (int k = 0; k < 16; ++k) out[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(mo[k], linv)) << (8 * (k & 3));
             if (threadIdx.x == 0) mom_scales[b] = nsm;
         } else {
-            const float inv = dyn_inv(bm);
+            const float dinv = dyn_inv(bm);
+            const float2 dinv2 = make_float2(dinv, dinv);
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-                out[k >> 2] |= dmap_encode_lut<true>(dlut, dm, dyn_xn(mo[k], inv)) << (8 * (k & 3));
+            for (int k = 0; k < 16; k += 2) {
+                const float2 xn = mul2_rn(make_float2(mo[k], mo[k + 1]), dinv2);
+                out[k >> 2] |= (dmap_encode_lut<true>(tab.dlut, tab.dm, xn.x) |
+                                (dmap_encode_lut<true>(tab.dlut, tab.dm, xn.y) << 8))
+                               << (8 * (k & 3));
+            }
             if (threadIdx.x == 0) mom_scales[b] = bm;
         }
-        *reinterpret_cast<uint2*>(mom8 + e0) = make_uint2(out[0], out[1]);
-        __syncthreads();
+        *reinterpret_cast<uint4*>(mom8 + e0) = make_uint4(out[0], out[1], out[2], out[3]);
     }
 }
 
