@@ -13,6 +13,9 @@ load()  # fail loudly at import time when the native library is absent
 
 from .galore import (  # noqa: E402
     AdamWConfig,
+    apply_galore_bf16_update,
+    decode_int4_to_fp16,
+    decode_int8_to_fp16,
     ClipResult,
     GaLoreConfig,
     GaLoreOptimizer,
@@ -29,7 +32,7 @@ from .galore import (  # noqa: E402
 )
 
 __all__ = [
-    "AdamWConfig", "AethError", "ClipResult", "GaLoreConfig", "GaLoreOptimizer", "LayerRankConfig", "LomoState", "NF4Tensor",
+    "AdamWConfig", "apply_galore_bf16_update", "decode_int4_to_fp16", "decode_int8_to_fp16", "AethError", "ClipResult", "GaLoreConfig", "GaLoreOptimizer", "LayerRankConfig", "LomoState", "NF4Tensor",
     "ProjectorKind", "deferred_apply_with_clip", "load", "lomo_sqnorm", "lomo_update", "nf4_dequantize", "nf4_quantize", "randomized_svd",
     "_lib",
 ]

@@ -110,6 +110,9 @@ SIGNATURES = {
     "aeth_dynamic_map": (_i, [_i, C.POINTER(_f)]),
     "aeth_selfcheck": (_i, [_i, C.POINTER(C.c_ulonglong)]),
     "aeth_lomo_sqnorm": (_i, [_vp, _i64, _vp, _vp]),
+    "aeth_fc_decode_int8": (_i, [_vp, _i64, _vp, _i64, _i, _vp, _vp]),
+    "aeth_fc_decode_nf4": (_i, [_vp, _i64, _f, _vp, _vp]),
+    "aeth_bf16_sr_update": (_i, [_vp, _vp, _i64, C.POINTER(C.c_uint64), _vp, _vp]),
     "aeth_lomo_update": (_i, [_vp, _i64, _vp, _f, _f, _f, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "aeth_status_string": (C.c_char_p, [_i]),
     "aeth_last_error": (_i, []),

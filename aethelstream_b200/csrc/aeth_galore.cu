@@ -22,6 +22,7 @@
 #include "nf4.cuh"
 #include "rsvd.cuh"
 #include "state_file.h"
+#include "stream_decode.cuh"
 
 using namespace aeth;
 
@@ -1758,6 +1759,61 @@ int aeth_int8_dequantize(const int8_t* q, const float* scales, int64_t n, int co
         return set_err(AETH_ERR_ARG);
     }
     AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_fc_decode_int8(const int8_t* src, int64_t n, const float* scales, int64_t n_scales, int num_channels,
+                        uint16_t* out_f16, aeth_stream_t stream) {
+    if (!src || !out_f16 || n < 0 || n_scales < 0 || num_channels < 0 || (n_scales > 0 && !scales))
+        return set_err(AETH_ERR_ARG);
+    if (n == 0) return AETH_OK;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(out_f16) & 15))
+        return set_err(AETH_ERR_UNSUPPORTED);
+    const int64_t per = num_channels > 0 ? std::max<int64_t>(n / num_channels, 1) : n;
+    fc_decode_int8_kernel<<<grid_for((n + 15) / 16, 256), 256, 0, to_stream(stream)>>>(
+        src, n, scales, n_scales, per, num_channels > 0 ? 1 : 0, out_f16);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_fc_decode_nf4(const uint8_t* src, int64_t nbytes, float absmax, uint16_t* out_f16, aeth_stream_t stream) {
+    if (!src || !out_f16 || nbytes < 0) return set_err(AETH_ERR_ARG);
+    if (nbytes == 0) return AETH_OK;
+    if ((reinterpret_cast<uintptr_t>(src) & 7) || (reinterpret_cast<uintptr_t>(out_f16) & 15))
+        return set_err(AETH_ERR_UNSUPPORTED);
+    fc_decode_nf4_kernel<<<grid_for((nbytes + 7) / 8, 256), 256, 0, to_stream(stream)>>>(src, nbytes, absmax, out_f16);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+int aeth_bf16_sr_update(float* master, const float* delta, int64_t n, uint64_t* rng_state, uint16_t* bf16_out,
+                        aeth_stream_t stream) {
+    if (!master || !delta || !rng_state || n < 0) return set_err(AETH_ERR_ARG);
+    if (n == 0) return AETH_OK;
+    if ((reinterpret_cast<uintptr_t>(master) & 15) || (reinterpret_cast<uintptr_t>(delta) & 15) ||
+        (bf16_out && (reinterpret_cast<uintptr_t>(bf16_out) & 7)))
+        return set_err(AETH_ERR_UNSUPPORTED);
+    static Affine64 pow2[64];
+    static bool pow2_init = false;
+    static bool uploaded[kMaxDevices] = {};
+    if (!pow2_init) {
+        lcg_pow2_host(pow2);
+        pow2_init = true;
+    }
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return set_err(AETH_ERR_UNSUPPORTED);
+    if (!uploaded[dev]) {
+        AETH_CUDA(cudaMemcpyToSymbol(c_lcg_pow2, pow2, sizeof(pow2)));
+        uploaded[dev] = true;
+    }
+    const int grid = grid_for((n + 3) / 4, 256, num_sms() * 8);
+    const Affine64 step = lcg_jump((uint64_t)grid * 256 * 4, pow2);
+    bf16_sr_update_kernel<<<grid, 256, 0, to_stream(stream)>>>(master, delta, n, *rng_state, step, bf16_out);
+    AETH_LAUNCH_CHECK();
+    // the state after n draws, as the sequential loop leaves it
+    const Affine64 all = lcg_jump((uint64_t)n, pow2);
+    *rng_state = all.a * *rng_state + all.c;
     return AETH_OK;
 }
 

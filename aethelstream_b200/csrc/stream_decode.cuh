@@ -1,0 +1,189 @@
+// stream_decode.cuh -- the steps on either side of the optimizer path in the
+// streaming pipeline: flowcast's decode of quantised weights to f16
+// (flowcast/src/decode.rs:63-104,191-210) and the BF16 stochastic-rounding
+// write-back of the master weights (doublepass/src/precision.rs:124-217).
+//
+// Decode: one thread expands 16 elements (16 INT8 bytes or 8 NF4 bytes) into
+// 32 bytes of f16 with 16-byte loads and stores: HBM-bound at 3 (INT8) or 2.5
+// (NF4) bytes per element.  The f16 conversion is flowcast's own: exponent
+// rebias and mantissa truncation, +-0 below the normal range, +-inf above it.
+// flowcast packs NF4 with the LOW nibble first and one absmax per tensor
+// (shard_engine's format, high nibble first with 64-element blocks, is
+// aeth_nf4_dequant's).
+//
+// Write-back: master += delta, then stochastic rounding to bf16 with 16 random
+// bits per element from a 64-bit LCG advanced once per element in order.  The
+// LCG is affine (x -> A x + C mod 2^64), so k steps are one affine map
+// (A^k, C (A^k - 1) / (A - 1)); maps for 2^j steps sit in constant memory, and
+// each thread starts from the state of its first element, as the sequential
+// loop would reach it, then steps forward.  The results are the reference's bit
+// for bit.
+#pragma once
+#include "nf4.cuh"
+
+namespace aeth {
+
+// precision.rs:212-217
+constexpr uint64_t kLcgA = 6364136223846793005ull;
+constexpr uint64_t kLcgC = 1442695040888963407ull;
+
+struct Affine64 {
+    uint64_t a, c;
+};
+
+// (second after first): x -> s.a (f.a x + f.c) + s.c
+__host__ __device__ inline Affine64 affine_then(Affine64 first, Affine64 second) {
+    return Affine64{second.a * first.a, second.a * first.c + second.c};
+}
+
+__constant__ Affine64 c_lcg_pow2[64];  // the map of 2^j LCG steps
+
+inline void lcg_pow2_host(Affine64 out[64]) {
+    Affine64 m{kLcgA, kLcgC};
+    for (int j = 0; j < 64; ++j) {
+        out[j] = m;
+        m = affine_then(m, m);
+    }
+}
+
+// The map of k steps, from the 2^j maps (host or constant-memory table).
+__host__ __device__ inline Affine64 lcg_jump(uint64_t k, const Affine64* pow2) {
+    Affine64 r{1ull, 0ull};
+    for (int j = 0; k != 0; ++j, k >>= 1)
+        if (k & 1ull) r = affine_then(r, pow2[j]);
+    return r;
+}
+
+// decode.rs:191-210
+__device__ __forceinline__ uint16_t fc_f32_to_f16(float v) {
+    const uint32_t bits = __float_as_uint(v);
+    const uint32_t sign = (bits >> 16) & 0x8000u;
+    const int exp = (int)((bits >> 23) & 0xffu);
+    const uint32_t mant = bits & 0x7fffffu;
+    if (exp == 0xff) return (uint16_t)(sign | 0x7c00u | (mant != 0u ? 0x0200u : 0u));
+    const int e16 = exp - 127 + 15;
+    if (e16 <= 0) return (uint16_t)sign;
+    if (e16 >= 31) return (uint16_t)(sign | 0x7c00u);
+    return (uint16_t)(sign | ((uint32_t)e16 << 10) | (mant >> 13));
+}
+
+__device__ __forceinline__ uint32_t fc_pack2(float lo, float hi) {
+    return (uint32_t)fc_f32_to_f16(lo) | ((uint32_t)fc_f32_to_f16(hi) << 16);
+}
+
+// decode.rs:63-86: out[i] = f16(i8 * scale[ch]), ch = i / per (per = max(n / channels, 1);
+// 0 without channels), a channel at or past n_scales decoding with 1.0.
+__global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __restrict__ src, int64_t n,
+                                                             const float* __restrict__ scales, int64_t n_scales,
+                                                             int64_t per, int has_channels,
+                                                             uint16_t* __restrict__ out) {
+    const int64_t n16 = n / 16;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n16; t += stride) {
+        const int64_t e0 = t * 16;
+        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src + e0));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        int64_t ch = has_channels ? e0 / per : 0;
+        int64_t next = has_channels ? (ch + 1) * per : INT64_MAX;
+        float s = ch < n_scales ? scales[ch] : 1.0f;
+        uint32_t o[8];
+#pragma unroll
+        for (int k = 0; k < 16; k += 2) {
+            float v[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (e0 + k + h >= next) {  // a channel boundary inside this thread's 16 elements
+                    ++ch;
+                    next += per;
+                    s = ch < n_scales ? scales[ch] : 1.0f;
+                }
+                const int8_t b = (int8_t)((w[(k + h) >> 2] >> (8 * ((k + h) & 3))) & 0xffu);
+                v[h] = __fmul_rn((float)b, s);
+            }
+            o[k >> 1] = fc_pack2(v[0], v[1]);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + e0);
+        __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
+        __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+    }
+    // ragged tail (n % 16 elements), one thread each
+    for (int64_t e = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += stride) {
+        const int64_t ch = has_channels ? e / per : 0;
+        out[e] = fc_f32_to_f16(__fmul_rn((float)src[e], ch < n_scales ? scales[ch] : 1.0f));
+    }
+}
+
+// decode.rs:88-104: byte k -> elements 2k (low nibble) and 2k + 1 (high nibble).
+__global__ void __launch_bounds__(256) fc_decode_nf4_kernel(const uint8_t* __restrict__ src, int64_t nbytes,
+                                                            float absmax, uint16_t* __restrict__ out) {
+    __shared__ float codes[16];
+    if (threadIdx.x < 16) codes[threadIdx.x] = __fmul_rn(c_nf4_codes[threadIdx.x], absmax);
+    __syncthreads();
+    const int64_t n8 = nbytes / 8;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n8; t += stride) {
+        const uint2 q = __ldcs(reinterpret_cast<const uint2*>(src + t * 8));
+        const uint32_t w[2] = {q.x, q.y};
+        uint32_t o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t b = (w[k >> 2] >> (8 * (k & 3))) & 0xffu;
+            o[k] = fc_pack2(codes[b & 0xfu], codes[b >> 4]);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + t * 16);
+        __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
+        __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+    }
+    for (int64_t k = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += stride) {
+        const uint32_t b = src[k];
+        reinterpret_cast<uint32_t*>(out)[k] = fc_pack2(codes[b & 0xfu], codes[b >> 4]);
+    }
+}
+
+// precision.rs:124-136: round up when the discarded 16 bits exceed the random
+// ones; saturating at 0xFFFF.
+__device__ __forceinline__ uint32_t sr_bf16(float v, uint32_t rand16) {
+    const uint32_t bits = __float_as_uint(v);
+    const uint32_t hi = bits >> 16;
+    return ((bits & 0xffffu) > rand16 && hi != 0xffffu) ? hi + 1u : hi;
+}
+
+// precision.rs:184-202 over 4 consecutive elements per thread and iteration.
+// x0 is the LCG state before element 0; element i draws from the state after
+// i + 1 steps.  `step` is the map of 4 x (threads in the grid) steps.
+__global__ void __launch_bounds__(256) bf16_sr_update_kernel(float* __restrict__ master,
+                                                             const float* __restrict__ delta, int64_t n, uint64_t x0,
+                                                             Affine64 step, uint16_t* __restrict__ bf16_out) {
+    const int64_t gtid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride4 = (int64_t)gridDim.x * blockDim.x * 4;
+    const Affine64 start = lcg_jump((uint64_t)(gtid * 4 + 1), c_lcg_pow2);
+    uint64_t xf = start.a * x0 + start.c;  // state drawn by this thread's first element
+    for (int64_t e0 = gtid * 4; e0 < n; e0 += stride4) {
+        uint64_t x = xf;
+        if (e0 + 4 <= n) {
+            float4 m = *reinterpret_cast<const float4*>(master + e0);
+            const float4 d = __ldcs(reinterpret_cast<const float4*>(delta + e0));
+            float v[4] = {__fadd_rn(m.x, d.x), __fadd_rn(m.y, d.y), __fadd_rn(m.z, d.z), __fadd_rn(m.w, d.w)};
+            uint32_t b[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                b[k] = sr_bf16(v[k], (uint32_t)(x >> 33) & 0xffffu);
+                x = kLcgA * x + kLcgC;
+            }
+            *reinterpret_cast<float4*>(master + e0) = make_float4(__uint_as_float(b[0] << 16), __uint_as_float(b[1] << 16),
+                                                                  __uint_as_float(b[2] << 16), __uint_as_float(b[3] << 16));
+            if (bf16_out)
+                *reinterpret_cast<uint2*>(bf16_out + e0) = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+        } else {
+            for (int64_t e = e0; e < n; ++e) {
+                const uint32_t bb = sr_bf16(__fadd_rn(master[e], delta[e]), (uint32_t)(x >> 33) & 0xffffu);
+                x = kLcgA * x + kLcgC;
+                master[e] = __uint_as_float(bb << 16);
+                if (bf16_out) bf16_out[e] = (uint16_t)bb;
+            }
+        }
+        xf = step.a * xf + step.c;
+    }
+}
+
+}  // namespace aeth

@@ -169,6 +169,38 @@ def randomized_svd(g: torch.Tensor, rank: int, oversampling: int = 10, seed: int
     return p, q
 
 
+def decode_int8_to_fp16(src: torch.Tensor, scales: torch.Tensor, num_channels: int) -> torch.Tensor:
+    """QuantizedDecoder::decode_int8_to_fp16 (flowcast/src/decode.rs:63-86) on
+    the device: int8 src, per-channel f32 scales -> float16 (flowcast's
+    truncating conversion)."""
+    src = src.contiguous()
+    out = torch.empty(src.numel(), dtype=torch.float16, device=src.device)
+    sc = scales.contiguous().float()
+    L.check(L.load().aeth_fc_decode_int8(_ptr(src), src.numel(), _ptr(sc), sc.numel(), num_channels, _ptr(out),
+                                         C.c_void_p(_stream_handle())), "aeth_fc_decode_int8")
+    return out
+
+
+def decode_int4_to_fp16(src: torch.Tensor, absmax: float) -> torch.Tensor:
+    """QuantizedDecoder::decode_int4_to_fp16 (decode.rs:88-104): packed NF4
+    bytes, low nibble first, one absmax -> float16 (2 values per byte)."""
+    src = src.contiguous()
+    out = torch.empty(2 * src.numel(), dtype=torch.float16, device=src.device)
+    L.check(L.load().aeth_fc_decode_nf4(_ptr(src), src.numel(), float(absmax), _ptr(out),
+                                        C.c_void_p(_stream_handle())), "aeth_fc_decode_nf4")
+    return out
+
+
+def apply_galore_bf16_update(master: torch.Tensor, delta: torch.Tensor, rng_state: int,
+                             bf16_out: torch.Tensor | None = None) -> int:
+    """apply_galore_bf16_update (doublepass/src/precision.rs:184-202) on the
+    device, in place on the f32 master weights; returns the advanced LCG state."""
+    st = C.c_uint64(rng_state & (2**64 - 1))
+    L.check(L.load().aeth_bf16_sr_update(_ptr(master), _ptr(delta), master.numel(), C.byref(st), _ptr(bf16_out),
+                                         C.c_void_p(_stream_handle())), "aeth_bf16_sr_update")
+    return int(st.value)
+
+
 class LomoState:
     """INT8 blockwise momentum of a LOMO-updated NF4 tensor (codec 1: linear,
     2: dynamic map; one fp32 scale per `block` elements)."""

@@ -368,8 +368,45 @@ def run_lomo(args):
             del host_g
         del W, grads, st
         torch.cuda.empty_cache()
+    # The steps on either side of the path in the streaming pipeline, at 2^28
+    # elements: flowcast's INT8 and NF4 decode to f16 and the BF16
+    # stochastic-rounding write-back (HBM bytes per element: 3, 2.5, 14).
+    from aethelstream_b200 import apply_galore_bf16_update, decode_int4_to_fp16, decode_int8_to_fp16
+    n_sd = 1 << 28
+    src8 = torch.randint(-128, 128, (n_sd,), dtype=torch.int8, device=dev)
+    src4 = torch.randint(0, 256, (n_sd // 2,), dtype=torch.uint8, device=dev)
+    scales = torch.rand(8192, device=dev) * 0.05
+    master = torch.randn(n_sd, device=dev)
+    delta = torch.randn(n_sd, device=dev) * 1e-3
+    bf = torch.empty(n_sd, dtype=torch.int16, device=dev)
+    rng_state = [0x1234_5678_9ABC_DEF0]
+
+    def sr_once():
+        rng_state[0] = apply_galore_bf16_update(master, delta, rng_state[0], bf)
+
+    stream_decode = {}
+    for name, fn, bpe in (("decode_int8_to_f16", lambda: decode_int8_to_fp16(src8, scales, 8192), 3.0),
+                          ("decode_nf4_to_f16", lambda: decode_int4_to_fp16(src4, 0.05), 2.5),
+                          ("bf16_sr_update", sr_once, 14.0)):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(10):
+            fn()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        ms_k = a0.elapsed_time(a1) / 10
+        stream_decode[name] = {"elements": n_sd, "ms": ms_k, "gbs": bpe * n_sd / (ms_k / 1000.0) / 1e9,
+                               "bytes_per_element": bpe}
+    del src8, src4, master, delta, bf
+    torch.cuda.empty_cache()
     if rank == 0:
         hbm, _, _, peak_kind = load_peaks()
+        for v in stream_decode.values():
+            v["frac"] = v["gbs"] / hbm
         top = sweep[-1]
         line = {
             "metric": "params updated/s (LOMO NF4 + INT8-momentum step)", "value": top["params_per_s"],
@@ -389,6 +426,7 @@ def run_lomo(args):
                               "measured_ms": top["ms_per_step"],
                               "frac": LOMO_BYTES * top["n"] / (hbm * 1e9) / (top["ms_per_step"] / 1000.0)},
             "sweep": sweep,
+            "stream_decode": stream_decode,
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,
             "clocks": clk,

@@ -370,6 +370,32 @@ int aeth_selfcheck(int which, unsigned long long* mismatches);
  * momentum m = beta m + g*clip, writes w = w - lr m and requantises w to NF4.
  * grad is bf16; n must be a multiple of 64 and of `block` / 64. */
 int aeth_lomo_sqnorm(const void* grad_bf16, int64_t n, double* sq_dev, aeth_stream_t stream);
+
+/* Streamed-weight decode, the step before the optimizer path in the streaming
+ * pipeline (QuantizedDecoder, flowcast/src/decode.rs:63-104): quantised
+ * weights to f16 with flowcast's own f32 -> f16 conversion (decode.rs:191-210:
+ * mantissa truncation; +-0 below the normal range, +-inf above it).
+ *   aeth_fc_decode_int8: out[i] = f16(src[i] * scales[ch]), ch = i / max(n /
+ *     num_channels, 1) (0 when num_channels == 0), a channel at or past
+ *     n_scales decoding with 1.0 (decode_int8_to_fp16).
+ *   aeth_fc_decode_nf4: nbytes packed NF4 bytes, LOW nibble first, one absmax
+ *     for the tensor -> 2 * nbytes f16 values (decode_int4_to_fp16).
+ *     shard_engine's layout (high nibble first, 64-element blocks) is
+ *     aeth_nf4_dequant's.
+ * Device pointers: src 16-byte (INT8) or 8-byte (NF4) aligned, out 16-byte
+ * aligned (AETH_ERR_UNSUPPORTED otherwise). */
+int aeth_fc_decode_int8(const int8_t* src, int64_t n, const float* scales, int64_t n_scales, int num_channels,
+                        uint16_t* out_f16, aeth_stream_t stream);
+int aeth_fc_decode_nf4(const uint8_t* src, int64_t nbytes, float absmax, uint16_t* out_f16, aeth_stream_t stream);
+/* The step after it: apply_galore_bf16_update (doublepass/src/precision.rs:
+ * 184-217).  master[i] += delta[i], then stochastic rounding to bf16 with the
+ * 16 bits drawn from the MMIX LCG for element i, in element order; master
+ * keeps the widened bf16 value and bf16_out (optional) the bf16 bits.
+ * *rng_state (host memory) is the state before element 0 and is advanced past
+ * element n - 1 on return, as the sequential loop leaves it.  master and
+ * delta 16-byte aligned, bf16_out 8-byte aligned. */
+int aeth_bf16_sr_update(float* master, const float* delta, int64_t n, uint64_t* rng_state, uint16_t* bf16_out,
+                        aeth_stream_t stream);
 int aeth_lomo_update(const void* grad_bf16, int64_t n, const double* sq_dev, float max_norm, float lr, float beta,
                      int codec, int block, int8_t* mom8, float* mom_scales, uint8_t* w_packed, float* w_absmax,
                      float* prequant_out, aeth_stream_t stream);

@@ -710,3 +710,61 @@ void b2_lomo_update(const uint16_t* g, int64_t n, float clip, float beta, float 
     free(mom);
     free(w);
 }
+
+/* ---------------------------------------------------------------------------
+ * Streamed-weight decode (flowcast/src/decode.rs) and the BF16
+ * stochastic-rounding write-back (doublepass/src/precision.rs), restated.
+ * ------------------------------------------------------------------------- */
+uint16_t fc_f32_to_f16(float v) {
+    /* decode.rs:191-210 */
+    uint32_t bits = f2u(v);
+    uint16_t sign = (uint16_t)(bits >> 31);
+    int32_t exp = (int32_t)((bits >> 23) & 0xFF);
+    uint32_t mant = bits & 0x7FFFFF;
+    if (exp == 0xFF) return (uint16_t)((sign << 15) | 0x7C00 | (mant != 0 ? 0x0200 : 0));
+    int32_t exp16 = exp - 127 + 15;
+    if (exp16 <= 0) return (uint16_t)(sign << 15);
+    if (exp16 >= 31) return (uint16_t)((sign << 15) | 0x7C00);
+    return (uint16_t)((sign << 15) | ((uint16_t)exp16 << 10) | (uint16_t)(mant >> 13));
+}
+
+void fc_decode_int8_to_f16(const int8_t* src, int64_t n, const float* scales, int64_t n_scales, int num_channels,
+                           uint16_t* out) {
+    /* decode.rs:63-86: channel = i / max(n / num_channels, 1) (0 when num_channels == 0);
+     * scale_per_channel.get(channel) or 1.0 */
+    int64_t per = num_channels > 0 ? n / num_channels : n;
+    if (per < 1) per = 1;
+    for (int64_t i = 0; i < n; ++i) {
+        int64_t ch = num_channels > 0 ? i / per : 0;
+        float s = ch < n_scales ? scales[ch] : 1.0f;
+        out[i] = fc_f32_to_f16((float)src[i] * s);
+    }
+}
+
+void fc_decode_int4_to_f16(const uint8_t* src, int64_t nbytes, float absmax, uint16_t* out) {
+    /* decode.rs:88-104: low nibble first */
+    for (int64_t k = 0; k < nbytes; ++k) {
+        out[2 * k] = fc_f32_to_f16(REF_NF4_CODES[src[k] & 0x0F] * absmax);
+        out[2 * k + 1] = fc_f32_to_f16(REF_NF4_CODES[(src[k] >> 4) & 0x0F] * absmax);
+    }
+}
+
+uint16_t dp_lcg_next(uint64_t* state) {
+    *state = *state * 6364136223846793005ull + 1442695040888963407ull;
+    return (uint16_t)((*state >> 33) & 0xFFFF);
+}
+
+uint16_t dp_stochastic_round_to_bf16(float v, uint16_t rand_bits) {
+    uint32_t bits = f2u(v);
+    uint16_t low16 = (uint16_t)(bits & 0xFFFF), high16 = (uint16_t)(bits >> 16);
+    if (low16 > rand_bits) return high16 == 0xFFFF ? high16 : (uint16_t)(high16 + 1); /* saturating_add */
+    return high16;
+}
+
+void dp_apply_galore_bf16_update(float* master, const float* delta, int64_t n, uint64_t* rng) {
+    for (int64_t i = 0; i < n; ++i) {
+        master[i] += delta[i];
+        uint16_t r = dp_lcg_next(rng);
+        master[i] = u2f((uint32_t)dp_stochastic_round_to_bf16(master[i], r) << 16);
+    }
+}

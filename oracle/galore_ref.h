@@ -118,6 +118,25 @@ void b2_apply_weight(const float* n_bf16, const float* proj, int m, int n, int r
  * requant bit-for-bit on the GPU's own pre-quant values). */
 void b2_nf4_requant(const float* w, int64_t n, uint8_t* packed, float* absmax);
 
+/* ---- Streamed-weight decode (flowcast) and the BF16 stochastic-rounding write-back ---- */
+/* flowcast/src/decode.rs:191-210: f32 -> f16 by exponent rebias and mantissa
+ * truncation; exponents below the f16 normal range give +-0, above it +-inf;
+ * NaN keeps the quiet bit only. */
+uint16_t fc_f32_to_f16(float v);
+/* decode.rs:63-86: out[i] = f16(i8 * scale[i / (n / num_channels)]); a
+ * channel without a scale (index >= n_scales) uses 1.0. */
+void fc_decode_int8_to_f16(const int8_t* src, int64_t n, const float* scales, int64_t n_scales, int num_channels,
+                           uint16_t* out);
+/* decode.rs:88-104: two codes per byte, LOW nibble first, per-tensor absmax. */
+void fc_decode_int4_to_f16(const uint8_t* src, int64_t nbytes, float absmax, uint16_t* out);
+/* doublepass/src/precision.rs:212-217: Knuth MMIX LCG; returns bits 33-48. */
+uint16_t dp_lcg_next(uint64_t* state);
+/* precision.rs:124-136 */
+uint16_t dp_stochastic_round_to_bf16(float v, uint16_t rand_bits);
+/* precision.rs:184-202: master += delta, then stochastic rounding to bf16
+ * with one LCG draw per element in order; master holds the widened value. */
+void dp_apply_galore_bf16_update(float* master, const float* delta, int64_t n, uint64_t* rng);
+
 /* LOMO fused full-rank SGD with INT8 momentum and NF4 requantisation. */
 double b2_lomo_sqnorm_bf16(const uint16_t* g, int64_t n);
 void b2_lomo_update(const uint16_t* g, int64_t n, float clip, float beta, float lr, int block, int codec,

@@ -86,6 +86,12 @@ def lib():
             "b2_lomo_sqnorm_bf16": (C.c_double, [_u16p, C.c_int64]),
             "b2_lomo_update": (None, [_u16p, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_int, C.c_int, _i8p,
                                       _f32p, _u8p, _f32p, _u8p, _f32p, _vp]),
+            "fc_f32_to_f16": (C.c_uint16, [C.c_float]),
+            "fc_decode_int8_to_f16": (None, [_i8p, C.c_int64, _f32p, C.c_int64, C.c_int, _u16p]),
+            "fc_decode_int4_to_f16": (None, [_u8p, C.c_int64, C.c_float, _u16p]),
+            "dp_lcg_next": (C.c_uint16, [C.POINTER(C.c_uint64)]),
+            "dp_stochastic_round_to_bf16": (C.c_uint16, [C.c_float, C.c_uint16]),
+            "dp_apply_galore_bf16_update": (None, [_f32p, _f32p, C.c_int64, C.POINTER(C.c_uint64)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -441,3 +447,43 @@ def galore_f16_to_f32(h):
     h = np.asarray(h, np.uint16).ravel()
     f = lib().ref_galore_f16_to_f32
     return np.array([f(int(v)) for v in h], np.float32)
+
+
+# ---- streamed-weight decode (flowcast/src/decode.rs) and the BF16 write-back (doublepass/src/precision.rs) ----
+def fc_f32_to_f16(x: float) -> int:
+    return int(lib().fc_f32_to_f16(float(x)))
+
+
+def fc_decode_int8(src, scales, num_channels: int):
+    src = _c(src, np.int8).ravel()
+    scales = _c(scales, np.float32).ravel()
+    out = np.empty(src.size, np.uint16)
+    lib().fc_decode_int8_to_f16(src, src.size, scales, scales.size, num_channels, out)
+    return out
+
+
+def fc_decode_int4(src, absmax: float):
+    src = _c(src, np.uint8).ravel()
+    out = np.empty(2 * src.size, np.uint16)
+    lib().fc_decode_int4_to_f16(src, src.size, float(absmax), out)
+    return out
+
+
+def lcg_next(state: int):
+    """(rand16, new_state) of precision.rs:212-217."""
+    st = C.c_uint64(state & (2**64 - 1))
+    r = lib().dp_lcg_next(C.byref(st))
+    return int(r), int(st.value)
+
+
+def stochastic_round_to_bf16(x: float, rand_bits: int) -> int:
+    return int(lib().dp_stochastic_round_to_bf16(float(x), int(rand_bits)))
+
+
+def apply_galore_bf16_update(master, delta, state: int):
+    """(new master, new rng state) of apply_galore_bf16_update (precision.rs:184-202)."""
+    m = _c(master, np.float32).ravel().copy()
+    d = _c(delta, np.float32).ravel()
+    st = C.c_uint64(state & (2**64 - 1))
+    lib().dp_apply_galore_bf16_update(m, d, m.size, C.byref(st))
+    return m, int(st.value)
