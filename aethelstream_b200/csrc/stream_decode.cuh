@@ -54,6 +54,26 @@ __host__ __device__ inline Affine64 lcg_jump(uint64_t k, const Affine64* pow2) {
     return r;
 }
 
+// The NaN an x86-64 scalar SSE operation returns, which is what the reference
+// (host code) produces: the first NaN operand, quieted, else the default NaN
+// 0xFFC00000 of an invalid operation (inf - inf, 0 x inf).  The device's own
+// NaN is 0x7FFFFFFF; its sign and low bits would decide the f16 sign and the
+// stochastic rounding differently.
+__device__ __forceinline__ float x86_nan(float a, float b) {
+    const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    if ((ua & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(ua | 0x00400000u);
+    if ((ub & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(ub | 0x00400000u);
+    return __uint_as_float(0xffc00000u);
+}
+__device__ __forceinline__ float x86_mul(float a, float b) {
+    const float p = __fmul_rn(a, b);
+    return p != p ? x86_nan(a, b) : p;
+}
+__device__ __forceinline__ float x86_add(float a, float b) {
+    const float s = __fadd_rn(a, b);
+    return s != s ? x86_nan(a, b) : s;
+}
+
 // decode.rs:191-210
 __device__ __forceinline__ uint16_t fc_f32_to_f16(float v) {
     const uint32_t bits = __float_as_uint(v);
@@ -98,7 +118,7 @@ __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __res
                     s = ch < n_scales ? scales[ch] : 1.0f;
                 }
                 const int8_t b = (int8_t)((w[(k + h) >> 2] >> (8 * ((k + h) & 3))) & 0xffu);
-                v[h] = __fmul_rn((float)b, s);
+                v[h] = x86_mul((float)b, s);
             }
             o[k >> 1] = fc_pack2(v[0], v[1]);
         }
@@ -109,7 +129,7 @@ __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __res
     // ragged tail (n % 16 elements), one thread each
     for (int64_t e = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += stride) {
         const int64_t ch = has_channels ? e / per : 0;
-        out[e] = fc_f32_to_f16(__fmul_rn((float)src[e], ch < n_scales ? scales[ch] : 1.0f));
+        out[e] = fc_f32_to_f16(x86_mul((float)src[e], ch < n_scales ? scales[ch] : 1.0f));
     }
 }
 
@@ -117,7 +137,7 @@ __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __res
 __global__ void __launch_bounds__(256) fc_decode_nf4_kernel(const uint8_t* __restrict__ src, int64_t nbytes,
                                                             float absmax, uint16_t* __restrict__ out) {
     __shared__ float codes[16];
-    if (threadIdx.x < 16) codes[threadIdx.x] = __fmul_rn(c_nf4_codes[threadIdx.x], absmax);
+    if (threadIdx.x < 16) codes[threadIdx.x] = x86_mul(c_nf4_codes[threadIdx.x], absmax);
     __syncthreads();
     const int64_t n8 = nbytes / 8;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -163,7 +183,7 @@ __global__ void __launch_bounds__(256) bf16_sr_update_kernel(float* __restrict__
         if (e0 + 4 <= n) {
             float4 m = *reinterpret_cast<const float4*>(master + e0);
             const float4 d = __ldcs(reinterpret_cast<const float4*>(delta + e0));
-            float v[4] = {__fadd_rn(m.x, d.x), __fadd_rn(m.y, d.y), __fadd_rn(m.z, d.z), __fadd_rn(m.w, d.w)};
+            float v[4] = {x86_add(m.x, d.x), x86_add(m.y, d.y), x86_add(m.z, d.z), x86_add(m.w, d.w)};
             uint32_t b[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -176,7 +196,7 @@ __global__ void __launch_bounds__(256) bf16_sr_update_kernel(float* __restrict__
                 *reinterpret_cast<uint2*>(bf16_out + e0) = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
         } else {
             for (int64_t e = e0; e < n; ++e) {
-                const uint32_t bb = sr_bf16(__fadd_rn(master[e], delta[e]), (uint32_t)(x >> 33) & 0xffffu);
+                const uint32_t bb = sr_bf16(x86_add(master[e], delta[e]), (uint32_t)(x >> 33) & 0xffffu);
                 x = kLcgA * x + kLcgC;
                 master[e] = __uint_as_float(bb << 16);
                 if (bf16_out) bf16_out[e] = (uint16_t)bb;

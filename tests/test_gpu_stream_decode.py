@@ -16,12 +16,14 @@ def test_decode_int8_bitexact(oracle, n, num_channels, n_scales):
     rng = np.random.default_rng(n)
     src = rng.integers(-128, 128, n).astype(np.int8)
     scales = (rng.random(max(n_scales, 1)) * 0.05).astype(np.float32)[:n_scales]
+    if n_scales > 2:
+        scales[1], scales[2] = np.inf, -np.nan  # 0 x inf and NaN products take the host's NaN
     out = decode_int8_to_fp16(dev(src), dev(scales) if n_scales else torch.empty(0, device="cuda"), num_channels)
     ref = oracle.fc_decode_int8(src, scales, num_channels)
     assert np.array_equal(host(out).view(np.uint16), ref)
 
 
-@pytest.mark.parametrize("absmax", [0.37, 1e10, 1e-9])
+@pytest.mark.parametrize("absmax", [0.37, 1e10, 1e-9, float("inf"), float("nan"), -float("nan")])
 def test_decode_nf4_bitexact(oracle, absmax):
     from aethelstream_b200 import decode_int4_to_fp16
     rng = np.random.default_rng(11)
