@@ -3,9 +3,9 @@
 // (flowcast/src/decode.rs:63-104,191-210) and the BF16 stochastic-rounding
 // write-back of the master weights (doublepass/src/precision.rs:124-217).
 //
-// Decode: one thread expands 16 elements (16 INT8 bytes or 8 NF4 bytes) into
-// 32 bytes of f16 with 16-byte loads and stores: HBM-bound at 3 (INT8) or 2.5
-// (NF4) bytes per element.  The f16 conversion is flowcast's own: exponent
+// Decode: a thread expands 16-byte chunks (16 INT8 or 32 NF4 elements) into
+// f16 with 16-byte loads and stores, several chunks per iteration in flight:
+// HBM-bound at 3 (INT8) or 2.5 (NF4) bytes per element.  The f16 conversion is flowcast's own: exponent
 // rebias and mantissa truncation, +-0 below the normal range, +-inf above it.
 // flowcast packs NF4 with the LOW nibble first and one absmax per tensor
 // (shard_engine's format, high nibble first with 64-element blocks, is
@@ -93,38 +93,52 @@ __device__ __forceinline__ uint32_t fc_pack2(float lo, float hi) {
 
 // decode.rs:63-86: out[i] = f16(i8 * scale[ch]), ch = i / per (per = max(n / channels, 1);
 // 0 without channels), a channel at or past n_scales decoding with 1.0.
+// Each thread loads four 16-element chunks (one grid stride apart) before
+// converting any, so that enough bytes are in flight to cover HBM latency.
+constexpr int kDecodeUnroll = 4;
+
+__device__ __forceinline__ void fc_int8_chunk(const uint4 q, int64_t e0, const float* __restrict__ scales,
+                                              int64_t n_scales, int64_t per, int has_channels,
+                                              uint16_t* __restrict__ out) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    int64_t ch = has_channels ? e0 / per : 0;
+    int64_t next = has_channels ? (ch + 1) * per : INT64_MAX;
+    float s = ch < n_scales ? scales[ch] : 1.0f;
+    uint32_t o[8];
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) {
+        float v[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (e0 + k + h >= next) {  // a channel boundary inside these 16 elements
+                ++ch;
+                next += per;
+                s = ch < n_scales ? scales[ch] : 1.0f;
+            }
+            const int8_t b = (int8_t)((w[(k + h) >> 2] >> (8 * ((k + h) & 3))) & 0xffu);
+            v[h] = x86_mul((float)b, s);
+        }
+        o[k >> 1] = fc_pack2(v[0], v[1]);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + e0);
+    __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
+    __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+}
+
 __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __restrict__ src, int64_t n,
                                                              const float* __restrict__ scales, int64_t n_scales,
                                                              int64_t per, int has_channels,
                                                              uint16_t* __restrict__ out) {
     const int64_t n16 = n / 16;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n16; t += stride) {
-        const int64_t e0 = t * 16;
-        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(src + e0));
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-        int64_t ch = has_channels ? e0 / per : 0;
-        int64_t next = has_channels ? (ch + 1) * per : INT64_MAX;
-        float s = ch < n_scales ? scales[ch] : 1.0f;
-        uint32_t o[8];
+    for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t0 < n16; t0 += stride * kDecodeUnroll) {
+        uint4 q[kDecodeUnroll];
 #pragma unroll
-        for (int k = 0; k < 16; k += 2) {
-            float v[2];
+        for (int u = 0; u < kDecodeUnroll; ++u)
+            if (t0 + u * stride < n16) q[u] = __ldcs(reinterpret_cast<const uint4*>(src) + t0 + u * stride);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (e0 + k + h >= next) {  // a channel boundary inside this thread's 16 elements
-                    ++ch;
-                    next += per;
-                    s = ch < n_scales ? scales[ch] : 1.0f;
-                }
-                const int8_t b = (int8_t)((w[(k + h) >> 2] >> (8 * ((k + h) & 3))) & 0xffu);
-                v[h] = x86_mul((float)b, s);
-            }
-            o[k >> 1] = fc_pack2(v[0], v[1]);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(out + e0);
-        __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
-        __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+        for (int u = 0; u < kDecodeUnroll; ++u)
+            if (t0 + u * stride < n16) fc_int8_chunk(q[u], (t0 + u * stride) * 16, scales, n_scales, per, has_channels, out);
     }
     // ragged tail (n % 16 elements), one thread each
     for (int64_t e = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += stride) {
@@ -134,27 +148,38 @@ __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __res
 }
 
 // decode.rs:88-104: byte k -> elements 2k (low nibble) and 2k + 1 (high nibble).
+// A chunk is 16 bytes (32 elements, 64 bytes of f16); two chunks per thread
+// and iteration are loaded before either is converted.
 __global__ void __launch_bounds__(256) fc_decode_nf4_kernel(const uint8_t* __restrict__ src, int64_t nbytes,
                                                             float absmax, uint16_t* __restrict__ out) {
     __shared__ float codes[16];
     if (threadIdx.x < 16) codes[threadIdx.x] = x86_mul(c_nf4_codes[threadIdx.x], absmax);
     __syncthreads();
-    const int64_t n8 = nbytes / 8;
+    const int64_t n16 = nbytes / 16;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n8; t += stride) {
-        const uint2 q = __ldcs(reinterpret_cast<const uint2*>(src + t * 8));
-        const uint32_t w[2] = {q.x, q.y};
-        uint32_t o[8];
+    for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t0 < n16; t0 += 2 * stride) {
+        uint4 q[2];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t b = (w[k >> 2] >> (8 * (k & 3))) & 0xffu;
-            o[k] = fc_pack2(codes[b & 0xfu], codes[b >> 4]);
+        for (int u = 0; u < 2; ++u)
+            if (t0 + u * stride < n16) q[u] = __ldcs(reinterpret_cast<const uint4*>(src) + t0 + u * stride);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (t0 + u * stride >= n16) break;
+            const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+            uint4* dst = reinterpret_cast<uint4*>(out + (t0 + u * stride) * 32);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                uint32_t o[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t b = (w[h] >> (8 * k)) & 0xffu;
+                    o[k] = fc_pack2(codes[b & 0xfu], codes[b >> 4]);
+                }
+                __stcs(dst + h, make_uint4(o[0], o[1], o[2], o[3]));
+            }
         }
-        uint4* dst = reinterpret_cast<uint4*>(out + t * 16);
-        __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
-        __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
     }
-    for (int64_t k = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += stride) {
+    for (int64_t k = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += stride) {
         const uint32_t b = src[k];
         reinterpret_cast<uint32_t*>(out)[k] = fc_pack2(codes[b & 0xfu], codes[b >> 4]);
     }
