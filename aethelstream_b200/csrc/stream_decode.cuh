@@ -74,17 +74,17 @@ __device__ __forceinline__ float x86_add(float a, float b) {
     return s != s ? x86_nan(a, b) : s;
 }
 
-// decode.rs:191-210
+// decode.rs:191-210, without branches: on |bits| the rebiased exponent and
+// truncated mantissa are (|bits| >> 13) - (112 << 10) for exponents 113..142;
+// below (f16 exponent <= 0) the result is +-0, above it +-inf, and NaN keeps
+// only the quiet bit (0x7E00).
 __device__ __forceinline__ uint16_t fc_f32_to_f16(float v) {
     const uint32_t bits = __float_as_uint(v);
-    const uint32_t sign = (bits >> 16) & 0x8000u;
-    const int exp = (int)((bits >> 23) & 0xffu);
-    const uint32_t mant = bits & 0x7fffffu;
-    if (exp == 0xff) return (uint16_t)(sign | 0x7c00u | (mant != 0u ? 0x0200u : 0u));
-    const int e16 = exp - 127 + 15;
-    if (e16 <= 0) return (uint16_t)sign;
-    if (e16 >= 31) return (uint16_t)(sign | 0x7c00u);
-    return (uint16_t)(sign | ((uint32_t)e16 << 10) | (mant >> 13));
+    const uint32_t mag = bits & 0x7fffffffu;
+    uint32_t h = (mag >> 13) - (112u << 10);
+    h = mag < 0x38800000u ? 0u : h;
+    h = mag >= 0x47800000u ? (mag > 0x7f800000u ? 0x7e00u : 0x7c00u) : h;
+    return (uint16_t)(((bits >> 16) & 0x8000u) | h);
 }
 
 __device__ __forceinline__ uint32_t fc_pack2(float lo, float hi) {
@@ -148,12 +148,15 @@ __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __res
 }
 
 // decode.rs:88-104: byte k -> elements 2k (low nibble) and 2k + 1 (high nibble).
-// A chunk is 16 bytes (32 elements, 64 bytes of f16); two chunks per thread
-// and iteration are loaded before either is converted.
+// The 16 decoded values depend only on the code, so a 256-entry table holds
+// the f16 pair of every byte: one lookup per two elements.  A chunk is 16
+// bytes (32 elements, 64 bytes of f16); two chunks per thread and iteration
+// are loaded before either is converted.
 __global__ void __launch_bounds__(256) fc_decode_nf4_kernel(const uint8_t* __restrict__ src, int64_t nbytes,
                                                             float absmax, uint16_t* __restrict__ out) {
-    __shared__ float codes[16];
-    if (threadIdx.x < 16) codes[threadIdx.x] = x86_mul(c_nf4_codes[threadIdx.x], absmax);
+    __shared__ uint32_t pair[256];
+    for (int b = threadIdx.x; b < 256; b += blockDim.x)
+        pair[b] = fc_pack2(x86_mul(c_nf4_codes[b & 15], absmax), x86_mul(c_nf4_codes[b >> 4], absmax));
     __syncthreads();
     const int64_t n16 = nbytes / 16;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -168,21 +171,13 @@ __global__ void __launch_bounds__(256) fc_decode_nf4_kernel(const uint8_t* __res
             const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
             uint4* dst = reinterpret_cast<uint4*>(out + (t0 + u * stride) * 32);
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                uint32_t o[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint32_t b = (w[h] >> (8 * k)) & 0xffu;
-                    o[k] = fc_pack2(codes[b & 0xfu], codes[b >> 4]);
-                }
-                __stcs(dst + h, make_uint4(o[0], o[1], o[2], o[3]));
-            }
+            for (int h = 0; h < 4; ++h)
+                __stcs(dst + h, make_uint4(pair[w[h] & 0xffu], pair[(w[h] >> 8) & 0xffu], pair[(w[h] >> 16) & 0xffu],
+                                           pair[w[h] >> 24]));
         }
     }
-    for (int64_t k = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += stride) {
-        const uint32_t b = src[k];
-        reinterpret_cast<uint32_t*>(out)[k] = fc_pack2(codes[b & 0xfu], codes[b >> 4]);
-    }
+    for (int64_t k = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += stride)
+        reinterpret_cast<uint32_t*>(out)[k] = pair[src[k]];
 }
 
 // precision.rs:124-136: round up when the discarded 16 bits exceed the random
