@@ -1767,10 +1767,11 @@ int aeth_fc_decode_int8(const int8_t* src, int64_t n, const float* scales, int64
     if (!src || !out_f16 || n < 0 || n_scales < 0 || num_channels < 0 || (n_scales > 0 && !scales))
         return set_err(AETH_ERR_ARG);
     if (n == 0) return AETH_OK;
-    if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(out_f16) & 15))
+    if ((reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(out_f16) & 7))
         return set_err(AETH_ERR_UNSUPPORTED);
     const int64_t per = num_channels > 0 ? std::max<int64_t>(n / num_channels, 1) : n;
-    fc_decode_int8_kernel<<<grid_for((n + 63) / 64, 256), 256, 0, to_stream(stream)>>>(
+    // 8 warps per CTA, 128 words (512 elements) per warp and iteration
+    fc_decode_int8_kernel<<<grid_for((n + 4095) / 4096, 1, num_sms() * 8), 256, 0, to_stream(stream)>>>(
         src, n, scales, n_scales, per, num_channels > 0 ? 1 : 0, out_f16);
     AETH_LAUNCH_CHECK();
     return AETH_OK;
@@ -1779,10 +1780,10 @@ int aeth_fc_decode_int8(const int8_t* src, int64_t n, const float* scales, int64
 int aeth_fc_decode_nf4(const uint8_t* src, int64_t nbytes, float absmax, uint16_t* out_f16, aeth_stream_t stream) {
     if (!src || !out_f16 || nbytes < 0) return set_err(AETH_ERR_ARG);
     if (nbytes == 0) return AETH_OK;
-    if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(out_f16) & 15))
+    if ((reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(out_f16) & 15))
         return set_err(AETH_ERR_UNSUPPORTED);
-    fc_decode_nf4_kernel<<<grid_for((nbytes + 31) / 32, 256), 256, 0, to_stream(stream)>>>(src, nbytes, absmax,
-                                                                                          out_f16);
+    fc_decode_nf4_kernel<<<grid_for((nbytes + 4095) / 4096, 1, num_sms() * 8), 256, 0, to_stream(stream)>>>(
+        src, nbytes, absmax, out_f16);
     AETH_LAUNCH_CHECK();
     return AETH_OK;
 }

@@ -3,9 +3,8 @@
 // (flowcast/src/decode.rs:63-104,191-210) and the BF16 stochastic-rounding
 // write-back of the master weights (doublepass/src/precision.rs:124-217).
 //
-// Decode: a thread expands 16-byte chunks (16 INT8 or 32 NF4 elements) into
-// f16 with 16-byte loads and stores, several chunks per iteration in flight:
-// HBM-bound at 3 (INT8) or 2.5 (NF4) bytes per element.  The f16 conversion is flowcast's own: exponent
+// Decode: HBM-bound at 3 (INT8) or 2.5 (NF4) bytes per element; each warp
+// moves whole contiguous spans per load and store instruction.  The f16 conversion is flowcast's own: exponent
 // rebias and mantissa truncation, +-0 below the normal range, +-inf above it.
 // flowcast packs NF4 with the LOW nibble first and one absmax per tensor
 // (shard_engine's format, high nibble first with 64-element blocks, is
@@ -91,57 +90,61 @@ __device__ __forceinline__ uint32_t fc_pack2(float lo, float hi) {
     return (uint32_t)fc_f32_to_f16(lo) | ((uint32_t)fc_f32_to_f16(hi) << 16);
 }
 
+// Both decoders give each warp 128 consecutive 32-bit input words per
+// iteration: lane l reads words l, 32 + l, 64 + l and 96 + l (128 contiguous
+// bytes per load instruction) and writes each word's f16 values to the
+// matching place, so every store instruction of the warp covers one
+// contiguous span of whole sectors.  (A lane writing its own contiguous 64
+// bytes as four 16-byte stores leaves half-written sectors per instruction,
+// which ran at half the bandwidth.)
+constexpr int kDecodeWords = 128;  // input words per warp and iteration
+
 // decode.rs:63-86: out[i] = f16(i8 * scale[ch]), ch = i / per (per = max(n / channels, 1);
 // 0 without channels), a channel at or past n_scales decoding with 1.0.
-// Each thread loads four 16-element chunks (one grid stride apart) before
-// converting any, so that enough bytes are in flight to cover HBM latency.
-constexpr int kDecodeUnroll = 4;
-
-__device__ __forceinline__ void fc_int8_chunk(const uint4 q, int64_t e0, const float* __restrict__ scales,
-                                              int64_t n_scales, int64_t per, int has_channels,
-                                              uint16_t* __restrict__ out) {
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+__device__ __forceinline__ uint2 fc_int8_word(uint32_t w, int64_t e0, const float* __restrict__ scales,
+                                              int64_t n_scales, int64_t per, int has_channels) {
     int64_t ch = has_channels ? e0 / per : 0;
-    int64_t next = has_channels ? (ch + 1) * per : INT64_MAX;
-    float s = ch < n_scales ? scales[ch] : 1.0f;
-    uint32_t o[8];
+    const int64_t next = has_channels ? (ch + 1) * per : INT64_MAX;
+    const float s0 = ch < n_scales ? scales[ch] : 1.0f;
+    float v[4];
 #pragma unroll
-    for (int k = 0; k < 16; k += 2) {
-        float v[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            if (e0 + k + h >= next) {  // a channel boundary inside these 16 elements
-                ++ch;
-                next += per;
-                s = ch < n_scales ? scales[ch] : 1.0f;
-            }
-            const int8_t b = (int8_t)((w[(k + h) >> 2] >> (8 * ((k + h) & 3))) & 0xffu);
-            v[h] = x86_mul((float)b, s);
+    for (int k = 0; k < 4; ++k) {
+        float s = s0;
+        if (e0 + k >= next) {  // a channel boundary inside these 4 elements (per >= 1)
+            const int64_t c = (e0 + k) / per;
+            s = c < n_scales ? scales[c] : 1.0f;
         }
-        o[k >> 1] = fc_pack2(v[0], v[1]);
+        v[k] = x86_mul((float)(int8_t)((w >> (8 * k)) & 0xffu), s);
     }
-    uint4* dst = reinterpret_cast<uint4*>(out + e0);
-    __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
-    __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+    return make_uint2(fc_pack2(v[0], v[1]), fc_pack2(v[2], v[3]));
 }
 
 __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __restrict__ src, int64_t n,
                                                              const float* __restrict__ scales, int64_t n_scales,
                                                              int64_t per, int has_channels,
                                                              uint16_t* __restrict__ out) {
-    const int64_t n16 = n / 16;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t0 < n16; t0 += stride * kDecodeUnroll) {
-        uint4 q[kDecodeUnroll];
+    const uint32_t* src32 = reinterpret_cast<const uint32_t*>(src);
+    const int64_t nw = n / 4;  // whole words
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w0 = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * kDecodeWords; w0 < nw;
+         w0 += warps * kDecodeWords) {
+        uint32_t q[4];
 #pragma unroll
-        for (int u = 0; u < kDecodeUnroll; ++u)
-            if (t0 + u * stride < n16) q[u] = __ldcs(reinterpret_cast<const uint4*>(src) + t0 + u * stride);
+        for (int h = 0; h < 4; ++h) {
+            const int64_t wi = w0 + h * 32 + lane;
+            q[h] = wi < nw ? __ldcs(src32 + wi) : 0u;
+        }
 #pragma unroll
-        for (int u = 0; u < kDecodeUnroll; ++u)
-            if (t0 + u * stride < n16) fc_int8_chunk(q[u], (t0 + u * stride) * 16, scales, n_scales, per, has_channels, out);
+        for (int h = 0; h < 4; ++h) {
+            const int64_t wi = w0 + h * 32 + lane;
+            if (wi < nw)
+                __stcs(reinterpret_cast<uint2*>(out) + wi, fc_int8_word(q[h], wi * 4, scales, n_scales, per, has_channels));
+        }
     }
-    // ragged tail (n % 16 elements), one thread each
-    for (int64_t e = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += stride) {
+    // ragged tail (n % 4 elements)
+    for (int64_t e = nw * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+         e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t ch = has_channels ? e / per : 0;
         out[e] = fc_f32_to_f16(x86_mul((float)src[e], ch < n_scales ? scales[ch] : 1.0f));
     }
@@ -149,34 +152,36 @@ __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __res
 
 // decode.rs:88-104: byte k -> elements 2k (low nibble) and 2k + 1 (high nibble).
 // The 16 decoded values depend only on the code, so a 256-entry table holds
-// the f16 pair of every byte: one lookup per two elements.  A chunk is 16
-// bytes (32 elements, 64 bytes of f16); two chunks per thread and iteration
-// are loaded before either is converted.
+// the f16 pair of every byte: one lookup per two elements.
 __global__ void __launch_bounds__(256) fc_decode_nf4_kernel(const uint8_t* __restrict__ src, int64_t nbytes,
                                                             float absmax, uint16_t* __restrict__ out) {
     __shared__ uint32_t pair[256];
     for (int b = threadIdx.x; b < 256; b += blockDim.x)
         pair[b] = fc_pack2(x86_mul(c_nf4_codes[b & 15], absmax), x86_mul(c_nf4_codes[b >> 4], absmax));
     __syncthreads();
-    const int64_t n16 = nbytes / 16;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t0 < n16; t0 += 2 * stride) {
-        uint4 q[2];
+    const uint32_t* src32 = reinterpret_cast<const uint32_t*>(src);
+    const int64_t nw = nbytes / 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w0 = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * kDecodeWords; w0 < nw;
+         w0 += warps * kDecodeWords) {
+        uint32_t q[4];
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
-            if (t0 + u * stride < n16) q[u] = __ldcs(reinterpret_cast<const uint4*>(src) + t0 + u * stride);
+        for (int h = 0; h < 4; ++h) {
+            const int64_t wi = w0 + h * 32 + lane;
+            q[h] = wi < nw ? __ldcs(src32 + wi) : 0u;
+        }
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            if (t0 + u * stride >= n16) break;
-            const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-            uint4* dst = reinterpret_cast<uint4*>(out + (t0 + u * stride) * 32);
-#pragma unroll
-            for (int h = 0; h < 4; ++h)
-                __stcs(dst + h, make_uint4(pair[w[h] & 0xffu], pair[(w[h] >> 8) & 0xffu], pair[(w[h] >> 16) & 0xffu],
-                                           pair[w[h] >> 24]));
+        for (int h = 0; h < 4; ++h) {
+            const int64_t wi = w0 + h * 32 + lane;
+            if (wi < nw)
+                __stcs(reinterpret_cast<uint4*>(out) + wi,
+                       make_uint4(pair[q[h] & 0xffu], pair[(q[h] >> 8) & 0xffu], pair[(q[h] >> 16) & 0xffu],
+                                  pair[q[h] >> 24]));
         }
     }
-    for (int64_t k = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes; k += stride)
+    for (int64_t k = nw * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < nbytes;
+         k += (int64_t)gridDim.x * blockDim.x)
         reinterpret_cast<uint32_t*>(out)[k] = pair[src[k]];
 }
 

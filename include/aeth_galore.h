@@ -382,8 +382,8 @@ int aeth_lomo_sqnorm(const void* grad_bf16, int64_t n, double* sq_dev, aeth_stre
  *     for the tensor -> 2 * nbytes f16 values (decode_int4_to_fp16).
  *     shard_engine's layout (high nibble first, 64-element blocks) is
  *     aeth_nf4_dequant's.
- * Device pointers: src and out 16-byte aligned (AETH_ERR_UNSUPPORTED
- * otherwise). */
+ * Device pointers: src 4-byte aligned, out 8-byte (INT8) or 16-byte (NF4)
+ * aligned (AETH_ERR_UNSUPPORTED otherwise). */
 int aeth_fc_decode_int8(const int8_t* src, int64_t n, const float* scales, int64_t n_scales, int num_channels,
                         uint16_t* out_f16, aeth_stream_t stream);
 int aeth_fc_decode_nf4(const uint8_t* src, int64_t nbytes, float absmax, uint16_t* out_f16, aeth_stream_t stream);
