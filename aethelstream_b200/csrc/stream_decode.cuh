@@ -100,28 +100,49 @@ __device__ __forceinline__ uint32_t fc_pack2(float lo, float hi) {
 constexpr int kDecodeWords = 128;  // input words per warp and iteration
 
 // decode.rs:63-86: out[i] = f16(i8 * scale[ch]), ch = i / per (per = max(n / channels, 1);
-// 0 without channels), a channel at or past n_scales decoding with 1.0.
+// 0 without channels), a channel at or past n_scales decoding with 1.0.  The
+// channel comes from a double-precision reciprocal of per (exact for element
+// indices below 2^53 after a one-step correction), once per word; a word
+// inside one channel with a finite scale multiplies without NaN handling.
+__device__ __forceinline__ int64_t fc_channel(int64_t e, int64_t per, double inv_per) {
+    int64_t c = (int64_t)((double)e * inv_per);
+    if (c * per > e) --c;
+    else if ((c + 1) * per <= e) ++c;
+    return c;
+}
+
 __device__ __forceinline__ uint2 fc_int8_word(uint32_t w, int64_t e0, const float* __restrict__ scales,
-                                              int64_t n_scales, int64_t per, int has_channels) {
-    int64_t ch = has_channels ? e0 / per : 0;
-    const int64_t next = has_channels ? (ch + 1) * per : INT64_MAX;
-    const float s0 = ch < n_scales ? scales[ch] : 1.0f;
+                                              int64_t n_scales, int64_t per, double inv_per, int has_channels) {
+    float s0 = n_scales > 0 ? scales[0] : 1.0f;
+    int64_t next = INT64_MAX;
+    if (has_channels) {
+        const int64_t ch = fc_channel(e0, per, inv_per);
+        s0 = ch < n_scales ? scales[ch] : 1.0f;
+        next = (ch + 1) * per;
+    } else {
+        s0 = n_scales > 0 ? scales[0] : 1.0f;
+    }
     float v[4];
+    if (e0 + 3 < next && fabsf(s0) <= 3.402823466e38f) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        float s = s0;
-        if (e0 + k >= next) {  // a channel boundary inside these 4 elements (per >= 1)
-            const int64_t c = (e0 + k) / per;
-            s = c < n_scales ? scales[c] : 1.0f;
+        for (int k = 0; k < 4; ++k) v[k] = __fmul_rn((float)(int8_t)((w >> (8 * k)) & 0xffu), s0);
+    } else {  // a channel boundary inside the word, or an infinite or NaN scale
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float s = s0;
+            if (e0 + k >= next) {
+                const int64_t c = fc_channel(e0 + k, per, inv_per);
+                s = c < n_scales ? scales[c] : 1.0f;
+            }
+            v[k] = x86_mul((float)(int8_t)((w >> (8 * k)) & 0xffu), s);
         }
-        v[k] = x86_mul((float)(int8_t)((w >> (8 * k)) & 0xffu), s);
     }
     return make_uint2(fc_pack2(v[0], v[1]), fc_pack2(v[2], v[3]));
 }
 
 __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __restrict__ src, int64_t n,
                                                              const float* __restrict__ scales, int64_t n_scales,
-                                                             int64_t per, int has_channels,
+                                                             int64_t per, double inv_per, int has_channels,
                                                              uint16_t* __restrict__ out) {
     const uint32_t* src32 = reinterpret_cast<const uint32_t*>(src);
     const int64_t nw = n / 4;  // whole words
@@ -139,13 +160,14 @@ __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __res
         for (int h = 0; h < 4; ++h) {
             const int64_t wi = w0 + h * 32 + lane;
             if (wi < nw)
-                __stcs(reinterpret_cast<uint2*>(out) + wi, fc_int8_word(q[h], wi * 4, scales, n_scales, per, has_channels));
+                __stcs(reinterpret_cast<uint2*>(out) + wi,
+                       fc_int8_word(q[h], wi * 4, scales, n_scales, per, inv_per, has_channels));
         }
     }
     // ragged tail (n % 4 elements)
     for (int64_t e = nw * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
          e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t ch = has_channels ? e / per : 0;
+        const int64_t ch = has_channels ? fc_channel(e, per, inv_per) : 0;
         out[e] = fc_f32_to_f16(x86_mul((float)src[e], ch < n_scales ? scales[ch] : 1.0f));
     }
 }
