@@ -111,6 +111,13 @@ __device__ __forceinline__ int64_t fc_channel(int64_t e, int64_t per, double inv
     return c;
 }
 
+// The signed byte k of w as a float, exactly, without a conversion instruction:
+// 1.5 * 2^23 + b has b in its low mantissa bits; subtracting 1.5 * 2^23 is exact.
+__device__ __forceinline__ float fc_byte_f32(uint32_t w, int k) {
+    const int32_t b = (int32_t)(w << (24 - 8 * k)) >> 24;
+    return __fsub_rn(__int_as_float(0x4B400000 + b), 12582912.0f);
+}
+
 __device__ __forceinline__ uint2 fc_int8_word(uint32_t w, int64_t e0, const float* __restrict__ scales,
                                               int64_t n_scales, int64_t per, double inv_per, int has_channels) {
     float s0 = n_scales > 0 ? scales[0] : 1.0f;
@@ -125,7 +132,7 @@ __device__ __forceinline__ uint2 fc_int8_word(uint32_t w, int64_t e0, const floa
     float v[4];
     if (e0 + 3 < next && fabsf(s0) <= 3.402823466e38f) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = __fmul_rn((float)(int8_t)((w >> (8 * k)) & 0xffu), s0);
+        for (int k = 0; k < 4; ++k) v[k] = __fmul_rn(fc_byte_f32(w, k), s0);
     } else {  // a channel boundary inside the word, or an infinite or NaN scale
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -134,7 +141,7 @@ __device__ __forceinline__ uint2 fc_int8_word(uint32_t w, int64_t e0, const floa
                 const int64_t c = fc_channel(e0 + k, per, inv_per);
                 s = c < n_scales ? scales[c] : 1.0f;
             }
-            v[k] = x86_mul((float)(int8_t)((w >> (8 * k)) & 0xffu), s);
+            v[k] = x86_mul(fc_byte_f32(w, k), s);
         }
     }
     return make_uint2(fc_pack2(v[0], v[1]), fc_pack2(v[2], v[3]));
