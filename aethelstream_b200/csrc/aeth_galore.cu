@@ -1770,8 +1770,10 @@ int aeth_fc_decode_int8(const int8_t* src, int64_t n, const float* scales, int64
     if ((reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(out_f16) & 7))
         return set_err(AETH_ERR_UNSUPPORTED);
     const int64_t per = num_channels > 0 ? std::max<int64_t>(n / num_channels, 1) : n;
-    // 8 warps per CTA, 128 words (512 elements) per warp and iteration
-    fc_decode_int8_kernel<<<grid_for((n + 4095) / 4096, 1, num_sms() * 8), 256, 0, to_stream(stream)>>>(
+    // 8 warps per CTA, 128 words (512 elements) per warp and iteration; the
+    // kernel's shared table needs exactly 256 threads
+    fc_decode_int8_kernel<<<grid_for((n + kDecodeSpan - 1) / kDecodeSpan, 1, num_sms() * 8), 256, 0,
+                            to_stream(stream)>>>(
         src, n, scales, n_scales, per, 1.0 / (double)per, num_channels > 0 ? 1 : 0, out_f16);
     AETH_LAUNCH_CHECK();
     return AETH_OK;

@@ -147,28 +147,63 @@ __device__ __forceinline__ uint2 fc_int8_word(uint32_t w, int64_t e0, const floa
     return make_uint2(fc_pack2(v[0], v[1]), fc_pack2(v[2], v[3]));
 }
 
+// A CTA's 8 warps cover 1024 consecutive words (4096 elements) per iteration.
+// When a channel spans at least that many elements, the span meets at most two
+// channels, and the 256 possible products of each are tabulated as f16 in
+// shared memory first: one table lookup per element.  Otherwise every word
+// computes its products.
+constexpr int kDecodeSpan = 8 * kDecodeWords * 4;  // elements per CTA iteration
+
 __global__ void __launch_bounds__(256) fc_decode_int8_kernel(const int8_t* __restrict__ src, int64_t n,
                                                              const float* __restrict__ scales, int64_t n_scales,
                                                              int64_t per, double inv_per, int has_channels,
                                                              uint16_t* __restrict__ out) {
+    __shared__ uint16_t tab[2][256];
     const uint32_t* src32 = reinterpret_cast<const uint32_t*>(src);
     const int64_t nw = n / 4;  // whole words
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t w0 = ((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5) * kDecodeWords; w0 < nw;
-         w0 += warps * kDecodeWords) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool tabulate = !has_channels || per >= kDecodeSpan;
+    for (int64_t base = (int64_t)blockIdx.x * kDecodeSpan; base < nw * 4; base += (int64_t)gridDim.x * kDecodeSpan) {
+        const int64_t w0 = base / 4 + warp * kDecodeWords;
         uint32_t q[4];
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
             const int64_t wi = w0 + h * 32 + lane;
             q[h] = wi < nw ? __ldcs(src32 + wi) : 0u;
         }
+        if (tabulate) {
+            // the span's channels: ch_a from its first element, ch_a + 1 from `split` on
+            const int64_t ch_a = has_channels ? fc_channel(base, per, inv_per) : 0;
+            const int64_t split = has_channels ? (ch_a + 1) * per : INT64_MAX;
+            __syncthreads();  // the previous iteration's lookups are done
+            {
+                const int t = threadIdx.x;  // 256 threads: one byte value each
+                const float b = fc_byte_f32((uint32_t)t, 0);
+                const float sa = ch_a < n_scales ? scales[ch_a] : 1.0f;
+                const float sb = ch_a + 1 < n_scales ? scales[ch_a + 1] : 1.0f;
+                tab[0][t] = fc_f32_to_f16(x86_mul(b, sa));
+                tab[1][t] = fc_f32_to_f16(x86_mul(b, has_channels ? sb : sa));
+            }
+            __syncthreads();
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            const int64_t wi = w0 + h * 32 + lane;
-            if (wi < nw)
-                __stcs(reinterpret_cast<uint2*>(out) + wi,
-                       fc_int8_word(q[h], wi * 4, scales, n_scales, per, inv_per, has_channels));
+            for (int h = 0; h < 4; ++h) {
+                const int64_t wi = w0 + h * 32 + lane;
+                if (wi < nw) {
+                    const int64_t e0 = wi * 4;
+                    uint32_t o[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) o[k] = tab[e0 + k >= split][(q[h] >> (8 * k)) & 0xffu];
+                    __stcs(reinterpret_cast<uint2*>(out) + wi, make_uint2(o[0] | (o[1] << 16), o[2] | (o[3] << 16)));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const int64_t wi = w0 + h * 32 + lane;
+                if (wi < nw)
+                    __stcs(reinterpret_cast<uint2*>(out) + wi,
+                           fc_int8_word(q[h], wi * 4, scales, n_scales, per, inv_per, has_channels));
+            }
         }
     }
     // ragged tail (n % 4 elements)
