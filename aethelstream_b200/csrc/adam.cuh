@@ -243,7 +243,7 @@ __global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ misma
 
 // Dynamic-codec shared memory of b2_adam_group_kernel: the two bucket tables,
 // two 16-bank replicated maps and the two sorted maps.
-constexpr int kAdamDynSmem = 2 * kDmapLutEntries * 8 + (2 * 256 * 16 + 2 * 256) * 4;
+constexpr int kAdamDynSmem = 3 * kDmapLutEntries * 8 + (2 * 256 * 16 + 2 * 256) * 4;
 
 template <bool DYN>
 __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     __shared__ float red_m[8], red_v[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, l16 = lane & 15;
     uint2* lut_s = dyn_smem;
-    uint2* lut_u = lut_s + kDmapLutEntries;
+    uint2* lut_u = lut_s + 2 * kDmapLutEntries;
     float* rep_s = reinterpret_cast<float*>(lut_u + kDmapLutEntries);
     float* rep_u = rep_s + 256 * 16;
     float* map_s = rep_u + 256 * 16;
@@ -265,10 +265,8 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
             map_s[i] = c_dmap_signed[i];
             map_u[i] = c_dmap_unsigned[i];
         }
-        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) {
-            lut_s[i] = g_dmap_lut[0][i];
-            lut_u[i] = g_dmap_lut[1][i];
-        }
+        for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) lut_s[i] = g_dmap_lut_s[i];
+        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) lut_u[i] = g_dmap_lut_u[i];
     }
     __syncthreads();
     const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;

@@ -24,71 +24,76 @@ int build_dynamic_map(int is_signed, float out[256]);
 // Bucket tables for a fast dynamic-map encode that always returns what the
 // binary search (dmap_encode) returns.
 //
-// The encode is a step function of the magnitude a = |xn|: the code changes
-// only at the decision points between neighbouring map entries, each within
-// 1.5 ulp of the real midpoint of the two entries (the binary search's two
-// distances each carry at most half an ulp of error, plus the rounding of the
-// midpoint to float).  A magnitude selects bucket b = (bits(a) >> 17) -
-// (103 << 6), clamped to [0, kDmapLutN]: 64 buckets per octave over
-// [2^-24, 2), bucket 0 also taking everything below 2^-24, and a last entry
-// for a >= 2, infinities and NaN.  An entry is {threshold bits, code below}:
-// the float bits of the one decision threshold within 56 bit steps of the
-// bucket (several midpoints of the map fall exactly on bucket edges), or
-// kDmapNoThr, which no magnitude reaches; code = below + [bits(a) >=
-// threshold].  The binary search handles magnitudes within kDmapGuard bit
-// steps of the threshold and entries flagged kDmapSearch: buckets with two
-// thresholds near them and the last entry.
+// For x of one sign the binary search's code is a non-decreasing step
+// function of the key bits(|x|) (x >= 0) or ~bits(|x|) (x < 0): between two
+// neighbouring map entries it compares two rounded distances, one shrinking
+// and one growing with x, so its decision flips exactly once, at a float that
+// the host finds by bisection over the search itself -- ties and rounding
+// included.  A magnitude selects bucket b = (bits(|x|) >> 17) - (103 << 6),
+// clamped to [0, kDmapLutN]: 64 buckets per octave over [2^-24, 2), bucket 0
+// also taking everything below 2^-24, and a last entry for |x| >= 2,
+// infinities and NaN.  An entry is {threshold key, code below}: code = below +
+// [key >= threshold], exact for every key of the bucket.  Buckets where the
+// code changes more than once, and the last entry, are flagged kDmapSearch
+// and sent to the binary search.
 //
-// Table 0 covers the signed map's non-negative half (indices 127..255); the
-// map is symmetric about index 127 except for the extra entry 1.0 at 255, so a
-// negative xn encodes as 254 - code(|xn|) (0 for codes 254 and 255).  Table 1
-// covers the unsigned map, whose entry 0 is 0.0 and nearest to every negative
-// xn.  Exact ties (xn on a real midpoint) always lie in the guard band, where
-// the binary search applies its own tie rule.
+// The signed map's table has a half per sign (negative keys at offset
+// kDmapLutEntries); the unsigned map's has only the non-negative half, and a
+// negative x (never an Adam v) takes the search.  aeth_selfcheck runs every
+// float bit pattern through both paths.
 // ---------------------------------------------------------------------------
 constexpr int kDmapLutExpLo = 103;                     // 2^-24
 constexpr int kDmapLutN = (128 - kDmapLutExpLo) << 6;  // 1600 buckets
-constexpr int kDmapLutEntries = kDmapLutN + 1;         // + the entry for a >= 2, inf, NaN
-constexpr uint32_t kDmapGuard = 8;                     // bit steps (ulp) around a threshold
-constexpr uint32_t kDmapReach = 56;                    // thresholds this far outside a bucket count
-constexpr uint32_t kDmapNoThr = 0xc0000000u;           // above every magnitude, far from all of them
+constexpr int kDmapLutEntries = kDmapLutN + 1;         // + the entry for |x| >= 2, inf, NaN
 constexpr uint32_t kDmapSearch = 0x100u;               // in the code word: always search
-__device__ uint2 g_dmap_lut[2][kDmapLutEntries];
+__device__ uint2 g_dmap_lut_s[2 * kDmapLutEntries];   // signed map: x >= 0, then x < 0
+__device__ uint2 g_dmap_lut_u[kDmapLutEntries];       // unsigned map: x >= 0
 
-inline void build_dmap_lut(const float map[256], int is_signed, uint2* out) {
-    std::vector<std::pair<double, int>> M;  // entries ascending by magnitude, with their codes
-    for (int i = is_signed ? 127 : 0; i < 256; ++i) M.push_back({(double)map[i], i});
-    auto bits_of = [](double v) {
-        const float f = (float)v;
-        uint32_t u;
-        memcpy(&u, &f, 4);
-        return u;
-    };
-    for (int b = 0; b < kDmapLutN; ++b) {
-        const uint32_t lo_bits = (uint32_t)(b + (kDmapLutExpLo << 6)) << 17;
-        const uint32_t hi_bits = lo_bits + (1u << 17);
-        // midpoints (as floats) within kDmapReach bit steps of the bucket;
-        // bucket 0 also holds everything below 2^-24
-        const uint32_t ext_lo = b == 0 ? 0u : lo_bits - kDmapReach, ext_hi = hi_bits + kDmapReach;
-        int nmid = 0, kmid = -1;
-        for (size_t k = 0; k + 1 < M.size(); ++k) {
-            const uint32_t tb = bits_of(0.5 * (M[k].first + M[k + 1].first));
-            if (tb >= ext_lo && tb < ext_hi) { ++nmid; kmid = (int)k; }
+// The binary search on the host (dmap_encode's arithmetic: IEEE single
+// subtraction and comparison).
+inline uint32_t host_dmap_encode(const float* map, float x) {
+    int lo = 0;
+    for (int step = 128; step > 0; step >>= 1)
+        if (map[lo + step - 1] < x) lo += step;
+    if (lo == 0) return 0u;
+    if (lo == 256) return 255u;
+    const float dl = fabsf(x - map[lo - 1]), dh = fabsf(x - map[lo]);
+    return dh < dl ? (uint32_t)lo : (uint32_t)(lo - 1);
+}
+
+// halves = 2 for the signed map (out: 2 * kDmapLutEntries), 1 for the unsigned one.
+inline void build_dmap_lut(const float map[256], int halves, uint2* out) {
+    for (int h = 0; h < halves; ++h) {
+        uint2* o = out + h * kDmapLutEntries;
+        auto code_of = [&](uint32_t key) {
+            const uint32_t bits = h ? (~key | 0x80000000u) : key;  // x of this half with that key
+            float x;
+            memcpy(&x, &bits, 4);
+            return host_dmap_encode(map, x);
+        };
+        for (int b = 0; b < kDmapLutN; ++b) {
+            const uint32_t lo_ab = b == 0 ? 0u : (uint32_t)(b + (kDmapLutExpLo << 6)) << 17;
+            const uint32_t hi_ab = ((uint32_t)(b + 1 + (kDmapLutExpLo << 6)) << 17) - 1u;
+            const uint32_t kmin = h ? ~hi_ab : lo_ab, kmax = h ? ~lo_ab : hi_ab;
+            const uint32_t cmin = code_of(kmin), cmax = code_of(kmax);
+            if (cmin == cmax) {  // one code throughout: a threshold no key of the bucket misses or reaches
+                if (cmin >= 1) o[b] = make_uint2(kmin, cmin - 1);
+                else if (kmax != 0xffffffffu) o[b] = make_uint2(kmax + 1u, 0u);
+                else o[b] = make_uint2(0xffffffffu, kDmapSearch);
+            } else if (cmax == cmin + 1) {  // one flip: the first key with the upper code
+                uint32_t lo = kmin, hi = kmax;
+                while (hi - lo > 1u) {
+                    const uint32_t mid = lo + (hi - lo) / 2u;
+                    if (code_of(mid) == cmin) lo = mid;
+                    else hi = mid;
+                }
+                o[b] = make_uint2(hi, cmin);
+            } else {
+                o[b] = make_uint2(0xffffffffu, kDmapSearch);
+            }
         }
-        if (nmid == 0) {
-            float lof;
-            memcpy(&lof, &lo_bits, 4);
-            const double lo = b == 0 ? 0.0 : (double)lof;
-            size_t k = 0;  // the nearest entry is the same over the whole bucket
-            while (k + 1 < M.size() && 0.5 * (M[k].first + M[k + 1].first) < lo) ++k;
-            out[b] = make_uint2(kDmapNoThr, (uint32_t)M[k].second);
-        } else if (nmid == 1 && b > 0) {
-            out[b] = make_uint2(bits_of(0.5 * (M[kmid].first + M[kmid + 1].first)), (uint32_t)M[kmid].second);
-        } else {
-            out[b] = make_uint2(kDmapNoThr, kDmapSearch);
-        }
+        o[kDmapLutN] = make_uint2(0xffffffffu, kDmapSearch);
     }
-    out[kDmapLutN] = make_uint2(kDmapNoThr, kDmapSearch);
 }
 
 inline bool g_maps_uploaded[kMaxDevices] = {};
@@ -103,10 +108,11 @@ inline int codec_maps_ensure() {
         build_dynamic_map(0, u);
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_signed, s, sizeof(s)));
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_unsigned, u, sizeof(u)));
-        static uint2 lut[2][kDmapLutEntries];
-        build_dmap_lut(s, 1, lut[0]);
-        build_dmap_lut(u, 0, lut[1]);
-        AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut, lut, sizeof(lut)));
+        static uint2 lut_s[2 * kDmapLutEntries], lut_u[kDmapLutEntries];
+        build_dmap_lut(s, 2, lut_s);
+        build_dmap_lut(u, 1, lut_u);
+        AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut_s, lut_s, sizeof(lut_s)));
+        AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut_u, lut_u, sizeof(lut_u)));
         g_maps_uploaded[dev] = true;
     }
     return AETH_OK;
@@ -144,29 +150,36 @@ __device__ __forceinline__ uint32_t dmap_encode(const float* __restrict__ map, f
 // for every element under a predicate.
 __device__ __noinline__ uint32_t dmap_encode_rare(const float* map, float xn) { return dmap_encode(map, xn); }
 
-// Bucket-table encode (tables built by build_dmap_lut); `lut` is table 0 for
-// the signed map and table 1 for the unsigned one, `map` the sorted map for
-// the rare binary-search cases.  Returns dmap_encode(map, xn) for every xn.
+// Bucket-table encode (tables built by build_dmap_lut): `lut` is the signed
+// map's table (both halves) for SIGNED, else the unsigned map's; `map` the
+// sorted map for the rare binary-search cases.  Returns dmap_encode(map, xn)
+// for every xn.
 template <bool SIGNED>
 __device__ __forceinline__ uint32_t dmap_encode_lut(const uint2* __restrict__ lut, const float* __restrict__ map,
                                                     float xn) {
-    const uint32_t ab = __float_as_uint(xn) & 0x7fffffffu;
+    const uint32_t bits = __float_as_uint(xn);
+    const uint32_t ab = bits & 0x7fffffffu;
     const int b = min(max((int)(ab >> 17) - (kDmapLutExpLo << 6), 0), kDmapLutN);
-    const uint2 e = lut[b];
-    uint32_t code = e.y + (ab >= e.x ? 1u : 0u);
-    // signed: mirror image; unsigned: every negative value is nearest to entry 0 (= 0)
-    if (xn < 0.0f) code = SIGNED ? (uint32_t)max(254 - (int)code, 0) : 0u;
-    if (e.y > 0xffu || ab - e.x + kDmapGuard < 2u * kDmapGuard) code = dmap_encode_rare(map, xn);
-    return code;
+    if (SIGNED) {
+        const uint32_t neg = (uint32_t)((int32_t)bits >> 31);  // all ones for x < 0
+        const uint2 e = lut[b + (neg & (uint32_t)kDmapLutEntries)];
+        if (e.y > 0xffu) return dmap_encode_rare(map, xn);
+        return e.y + ((ab ^ neg) >= e.x ? 1u : 0u);
+    } else {
+        const uint2 e = lut[b];
+        if ((e.y | ((bits >> 31) << 8)) > 0xffu) return dmap_encode_rare(map, xn);
+        return e.y + (ab >= e.x ? 1u : 0u);
+    }
 }
 
 // Every float bit pattern through dmap_encode_lut and dmap_encode; counts
 // disagreements (a self-check of the bucket tables, run by the test suite).
 __global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restrict__ mismatches) {
     __shared__ float map[256];
-    __shared__ uint2 lut[kDmapLutEntries];
+    __shared__ uint2 lut[2 * kDmapLutEntries];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) map[i] = is_signed ? c_dmap_signed[i] : c_dmap_unsigned[i];
-    for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) lut[i] = g_dmap_lut[is_signed ? 0 : 1][i];
+    for (int i = threadIdx.x; i < (is_signed ? 2 : 1) * kDmapLutEntries; i += blockDim.x)
+        lut[i] = is_signed ? g_dmap_lut_s[i] : g_dmap_lut_u[i];
     __syncthreads();
     unsigned long long bad = 0;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;

@@ -50,7 +50,7 @@ struct LomoTables {
     uint32_t bucket32[33];
     uint32_t pad_[3];
     float dm[256];
-    uint2 dlut[kDmapLutEntries];
+    uint2 dlut[2 * kDmapLutEntries];
 };
 
 // One CTA of 128 threads per momentum block of 2048 elements and iteration;
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
     }
     if (CODEC == AETH_CODEC_BLOCK_DYNAMIC) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) tab.dm[i] = c_dmap_signed[i];
-        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) tab.dlut[i] = g_dmap_lut[0][i];
+        for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) tab.dlut[i] = g_dmap_lut_s[i];
     }
     __syncthreads();
     const uint32_t bucket_bias = smem_u32_addr(tab.bucket32) - (0x4B400000u << 2);
