@@ -248,7 +248,7 @@ constexpr int kAdamDynSmem = 3 * kDmapLutEntries * 8 + (2 * 256 * 16 + 2 * 256) 
 template <bool DYN>
 __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
     extern __shared__ __align__(16) uint2 dyn_smem[];
-    __shared__ float red_m[8], red_v[8];
+    __shared__ float red_m[2][8], red_v[2][8];  // by block parity: one barrier per block
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, l16 = lane & 15;
     uint2* lut_s = dyn_smem;
     uint2* lut_u = lut_s + 2 * kDmapLutEntries;
@@ -279,7 +279,8 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     // Blocks: the first gridDim.x by CTA index, the rest handed out by a device
     // counter (even finish times).  Each block's inputs are loaded one
     // iteration ahead, during the previous block's encode.
-    __shared__ int s_next;
+    __shared__ int s_next[2];
+    int it = 0;
     int gb = blockIdx.x;
     int p = 0, b = 0;
     int64_t e0 = 0;
@@ -307,7 +308,8 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     };
     if (gb < total) fetch(gb);
     while (gb < total) {
-        if (threadIdx.x == 0) s_next = (int)atomicAdd(a.work, 1u) + (int)gridDim.x;
+        const int par = it & 1;
+        if (threadIdx.x == 0) s_next[par] = (int)atomicAdd(a.work, 1u) + (int)gridDim.x;
         float mo[8], va[8];
         float am = 0.0f, av = 0.0f;
         if (valid) {
@@ -351,13 +353,13 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
         }
         am = warp_max(am);
         av = warp_max(av);
-        if (lane == 0) { red_m[warp] = am; red_v[warp] = av; }
-        __syncthreads();
+        if (lane == 0) { red_m[par][warp] = am; red_v[par][warp] = av; }
+        __syncthreads();  // the slots of this parity are rewritten two blocks later, after the next barrier
         float bm = 0.0f, bv = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) { bm = fmaxf(bm, red_m[w]); bv = fmaxf(bv, red_v[w]); }
-        const int next = s_next;
-        __syncthreads();  // red_* and s_next are rewritten for the next block
+        for (int w = 0; w < 8; ++w) { bm = fmaxf(bm, red_m[par][w]); bv = fmaxf(bv, red_v[par][w]); }
+        const int next = s_next[par];
+        ++it;
         // this block's coordinates, then the next block's inputs
         const int cp = p, cb = b;
         const int64_t ce0 = e0;
