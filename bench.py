@@ -285,6 +285,7 @@ def run_lomo(args):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        os.environ["NCCL_DEBUG"] = "WARN"  # keep NCCL's version banner off stdout: the JSON line is the only output
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     from aethelstream_b200 import LomoState, lomo_sqnorm, lomo_update, nf4_quantize
     dev = torch.device("cuda", local)
@@ -471,6 +472,7 @@ def run_b200(args):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        os.environ["NCCL_DEBUG"] = "WARN"  # keep NCCL's version banner off stdout: the JSON line is the only output
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     from aethelstream_b200 import GaLoreConfig, GaLoreOptimizer, LayerRankConfig, nf4_quantize
     from aethelstream_b200 import _lib
