@@ -123,6 +123,19 @@ def kernel_bytes(shapes=None, r=None):
     return out
 
 
+def kernel_flops(shapes=None, r=None):
+    """Tensor-core flops per launch: 2 r m n for the projection and for the
+    back-projection; Adam's ~12 r l are CUDA-core work, listed for completeness."""
+    r = r or RANK
+    out = dict.fromkeys(("projection", "sqnorm_clip", "adam", "apply"), 0.0)
+    for _, m, n in (shapes or SHAPES):
+        s, l = min(m, n), max(m, n)
+        out["projection"] += 2 * r * m * n
+        out["adam"] += 12 * r * l
+        out["apply"] += 2 * r * m * n
+    return out
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -636,7 +649,14 @@ def run_b200(args):
         gbs = {k: kb[k] / (per_ms[k] / 1000.0) / 1e9 for k in opt.PHASES}
         traffic = load_traffic() if args.config == "c2" else {}  # the committed capture is of C2
         dom = max(opt.PHASES, key=lambda k: per_ms[k])
-        achieved = gbs[dom]
+        kf = kernel_flops()
+        tfs = {k: kf[k] / (per_ms[k] / 1000.0) / 1e12 for k in opt.PHASES}
+        # the dominant kernel against the roof it is closest to: HBM bytes, or
+        # tensor flops against the sustained bf16 rate (the kernel runs inside a
+        # long step)
+        byte_frac = gbs[dom] / hbm
+        flop_frac = tfs[dom] / tflops_sus
+        tensor_bound = flop_frac > byte_frac
         step_s = ms / args.steps / 1000.0
         total_bytes = alg["proj_bytes"] + alg["apply_bytes"]
         total_flops = alg["proj_flops"] + alg["apply_flops"]
@@ -652,15 +672,21 @@ def run_b200(args):
                        "l2": (f"inputs larger than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients per "
                               "step, 2-deep ring)") if 2 * params_per_step > 126e6 else
                              f"inputs smaller than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients)"},
-            "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dom], "achieved": achieved, "peak": hbm,
-                         "unit": "GB/s", "frac": achieved / hbm,
+            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": KERNEL_NAMES[dom],
+                         "achieved": tfs[dom] if tensor_bound else gbs[dom],
+                         "peak": tflops_sus if tensor_bound else hbm,
+                         "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                         "frac": flop_frac if tensor_bound else byte_frac,
                          "traffic": traffic.get(f"{dom}_bytes_per_launch"),
-                         "algorithmic_bytes_per_launch": kb[dom], "launch_ms": per_ms[dom],
-                         "peak_kind": peak_kind},
+                         "algorithmic_bytes_per_launch": kb[dom], "algorithmic_flops_per_launch": kf[dom],
+                         "hbm_frac": byte_frac, "tensor_frac_of_sustained": flop_frac,
+                         "tensor_frac_of_burst": tfs[dom] / tflops,
+                         "launch_ms": per_ms[dom], "peak_kind": peak_kind},
             "roofline_step": {"algorithmic_bytes": total_bytes, "algorithmic_flops": total_flops,
                               "ideal_ms": ideal_s * 1000.0, "measured_ms": step_s * 1000.0,
                               "frac": ideal_s / step_s,
                               "phase_ms": per_ms, "phase_gbs": gbs, "phase_bytes": kb,
+                              "phase_tflops": tfs, "phase_flops": kf,
                               "host_enqueue_ms_per_step": host_ms,
                               "eager_ms_per_step_with_phase_events": eager_ms / args.steps},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
