@@ -23,7 +23,7 @@ AETH_ERR_LINALG = -7
 
 # bits of the device error word (aeth_device_error_bits)
 DEVERR_TIMEOUT_TMA, DEVERR_TIMEOUT_MMA, DEVERR_TIMEOUT_EPI = 1, 2, 4
-DEVERR_BAD_ARG, DEVERR_TIMEOUT_PEER, DEVERR_TIMEOUT_GRID = 8, 16, 32
+DEVERR_BAD_ARG, DEVERR_TIMEOUT_PEER = 8, 16
 CLIP_HANDLE_BYTES = 64
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2

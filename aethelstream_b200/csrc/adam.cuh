@@ -2,7 +2,6 @@
 // full-rank fused Adam of doublepass_galore_apply.
 #pragma once
 #include "codec.cuh"
-#include "sqnorm.cuh"
 #include "common.cuh"
 
 namespace aeth {
@@ -246,18 +245,8 @@ __global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ misma
 // two 16-bank replicated maps and the two sorted maps.
 constexpr int kAdamDynSmem = 3 * kDmapLutEntries * 8 + (2 * 256 * 16 + 2 * 256) * 4;
 
-// With FUSE the launch first computes the step's squared norms and the global
-// clip (the stand-alone sqnorm_group_kernel's work, same chunks and
-// arithmetic): every CTA takes chunk units (c, p) in turn, the CTA that
-// arrives last at a device ticket finishes the sums, forms the clip (with the
-// clip group's exchange) and releases the others through `gen`, a counter
-// advanced once per launch.  The CTAs wait for one another, so the launch is
-// cooperative (all CTAs resident); the wait is bounded and, if it gives up,
-// flags DEVERR_TIMEOUT_GRID and uses clip 0.
-template <bool DYN, bool FUSE>
-__global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a,
-                                                            const __grid_constant__ SqGroupArgs sq, int sq_chunks,
-                                                            uint64_t* gen) {
+template <bool DYN>
+__global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
     extern __shared__ __align__(16) uint2 dyn_smem[];
     __shared__ float red_m[2][8], red_v[2][8];  // by block parity: one barrier per block
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, l16 = lane & 15;
@@ -280,46 +269,7 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
         for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) lut_u[i] = g_dmap_lut_u[i];
     }
     __syncthreads();
-    float clip;
-    if (FUSE) {
-        __shared__ double red_d[8];
-        __shared__ unsigned int s_taken;
-        __shared__ int s_ok;
-        uint64_t e = 0;
-        if (threadIdx.x == 0) e = ld_acquire_gpu_u64(gen);
-        const int units = sq_chunks * sq.np;
-        for (int u = blockIdx.x; u < units; u += gridDim.x) sq_chunk(sq, u % sq_chunks, u / sq_chunks, sq_chunks, red_d);
-        if (threadIdx.x == 0) {
-            __threadfence();
-            s_taken = atomicAdd(sq.ticket, 1u);
-        }
-        __syncthreads();
-        if (s_taken == gridDim.x - 1) {
-            __threadfence();
-            sq_finish(sq, sq_chunks);
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                __threadfence();
-                st_release_gpu_u64(gen, e + 1);
-                s_ok = 1;
-            }
-        } else if (threadIdx.x == 0) {
-            const uint64_t t0 = global_ns(), limit = sq.timeout_ns + kWaitLimitNs;
-            s_ok = 1;
-            while (ld_acquire_gpu_u64(gen) == e) {
-                if (global_ns() - t0 > limit) {
-                    report_dev_error(sq.err, DEVERR_TIMEOUT_GRID);
-                    s_ok = 0;
-                    break;
-                }
-                __nanosleep(200);
-            }
-        }
-        __syncthreads();
-        clip = s_ok ? *reinterpret_cast<const volatile float*>(sq.clip_out) : 0.0f;
-    } else {
-        clip = a.clip_dev ? *a.clip_dev : a.clip_host;
-    }
+    const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
     const float omb1 = __fsub_rn(1.0f, a.b1), omb2 = __fsub_rn(1.0f, a.b2);
     const float2 b1x2 = make_float2(a.b1, a.b1), b2x2 = make_float2(a.b2, a.b2);
     const float2 omb1x2 = make_float2(omb1, omb1), omb2x2 = make_float2(omb2, omb2);

@@ -238,7 +238,6 @@ struct aeth_galore_ctx {
     unsigned int* sq_ticket = nullptr;  // sqnorm_group's completion counter, zero between launches
     unsigned int* work = nullptr;       // b2_adam_group_kernel's block counters, zero between launches
     uint64_t* clip_epoch = nullptr;     // clip group's exchange counter (device; zeroed on joining)
-    uint64_t* sq_gen = nullptr;         // fused norm + Adam launches: grid-barrier release counter (device)
     uint64_t version = 0;               // completed subspace refreshes (optimizer_version)
     // global clip over several GPUs through peer memory (aeth_galore_set_clip_group)
     ClipGroup group;
@@ -438,35 +437,25 @@ int b2_adam(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, int
 }
 
 // K5 for several parameters in one persistent launch (2048-element blocks).
-// Grouped Adam over ps[0..np).  With `fused` (np <= kAdamGroupMax, the
-// arguments of the step's squared-norm launch with clip_out set) the launch
-// also computes the norms and the clip first (cooperative launch); when the
-// device cannot hold every CTA at once it returns AETH_ERR_UNSUPPORTED before
-// launching anything, and the caller runs the two launches.
 int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, const float* clip_dev, int zero_accum,
-                  cudaStream_t st, const SqGroupArgs* fused = nullptr, int sq_chunks = 0) {
+                  cudaStream_t st) {
     const aeth_galore_config& cfg = c->cfg;
     if (cfg.state_block != 2048) {
-        if (fused) return AETH_ERR_UNSUPPORTED;
         for (int i = 0; i < np; ++i) AETH_TRY(b2_adam(c, *ps[i], clip, clip_dev, zero_accum, st));
         return AETH_OK;
     }
-    if (fused && np > kAdamGroupMax) return AETH_ERR_UNSUPPORTED;
     AETH_TRY(codec_maps_ensure());
     const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
-    // 74 KB of tables per CTA: three CTAs per SM
+    // 59 KB of tables per CTA: three CTAs per SM
     static_assert(3 * (kAdamDynSmem + 1024) <= 228 * 1024, "three dynamic-codec Adam CTAs must fit an SM");
     static bool attr_set[kMaxDevices] = {};
     int dev = 0;
     AETH_TRY(current_device(&dev));
     if (dyn && !attr_set[dev]) {
-        AETH_CUDA(cudaFuncSetAttribute(b2_adam_group_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kAdamDynSmem));
-        AETH_CUDA(cudaFuncSetAttribute(b2_adam_group_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        AETH_CUDA(cudaFuncSetAttribute(b2_adam_group_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kAdamDynSmem));
         attr_set[dev] = true;
     }
-    static SqGroupArgs no_sq{};
     for (int off = 0; off < np; off += kAdamGroupMax) {
         const int cnt = std::min(kAdamGroupMax, np - off);
         AdamGroupArgs a;
@@ -495,38 +484,12 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         a.eps = cfg.eps;
         a.zero_accum = zero_accum;
         a.work = c->work;
-        if (!fused) {
-            const int grid = std::min(blocks, num_sms() * (dyn ? 3 : 8));
-            if (dyn)
-                b2_adam_group_kernel<true, false><<<grid, 256, kAdamDynSmem, st>>>(a, no_sq, 0, nullptr);
-            else
-                b2_adam_group_kernel<false, false><<<grid, 256, 0, st>>>(a, no_sq, 0, nullptr);
-            AETH_LAUNCH_CHECK();
-            continue;
-        }
-        // Fused: one resident wave (every CTA reaches the grid barrier), a cooperative launch.
-        auto kern = dyn ? b2_adam_group_kernel<true, true> : b2_adam_group_kernel<false, true>;
-        const int smem = dyn ? kAdamDynSmem : 0;
-        int per_sm = 0;
-        AETH_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem));
-        if (per_sm < 1) return AETH_ERR_UNSUPPORTED;
-        const int grid = num_sms() * std::min(per_sm, dyn ? 3 : 8);
-        cudaLaunchConfig_t lc = {};
-        lc.gridDim = dim3(grid);
-        lc.blockDim = dim3(256);
-        lc.dynamicSmemBytes = smem;
-        lc.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        lc.attrs = attr;
-        lc.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&lc, kern, a, *fused, sq_chunks, c->sq_gen);
-        if (e == cudaErrorCooperativeLaunchTooLarge) {  // another context holds part of the SMs
-            (void)cudaGetLastError();
-            return AETH_ERR_UNSUPPORTED;
-        }
-        AETH_CUDA(e);
+        const int grid = std::min(blocks, num_sms() * (dyn ? 3 : 8));
+        if (dyn)
+            b2_adam_group_kernel<true><<<grid, 256, kAdamDynSmem, st>>>(a);
+        else
+            b2_adam_group_kernel<false><<<grid, 256, 0, st>>>(a);
+        AETH_LAUNCH_CHECK();
     }
     return AETH_OK;
 }
@@ -1061,12 +1024,10 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
         (st = ctx_alloc(c, &c->partials, std::max(kSqPartials, kSqGroupMax * kSqChunks))) ||
         (st = ctx_alloc(c, &c->clip_dev, 1)) ||
         (st = ctx_alloc(c, &c->gnorm_dev, 1)) || (st = ctx_alloc(c, &c->sq_ticket, 1)) ||
-        (st = ctx_alloc(c, &c->work, 2)) || (st = ctx_alloc(c, &c->clip_epoch, 1)) ||
-        (st = ctx_alloc(c, &c->sq_gen, 1)))
+        (st = ctx_alloc(c, &c->work, 2)) || (st = ctx_alloc(c, &c->clip_epoch, 1)))
         return fail(st);
     if (cudaMemset(c->sq_ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
-        cudaMemset(c->work, 0, 2 * sizeof(unsigned int)) != cudaSuccess ||
-        cudaMemset(c->sq_gen, 0, sizeof(uint64_t)) != cudaSuccess)
+        cudaMemset(c->work, 0, 2 * sizeof(unsigned int)) != cudaSuccess)
         return fail(AETH_ERR_CONFIG);
     if (cudaDeviceSynchronize() != cudaSuccess) return fail(AETH_ERR_CONFIG);
     *out = c;
@@ -1489,38 +1450,18 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
     const bool grouped = ctx->group.world > 1;
     if (grouped && (sq_hook || n > kSqGroupMax)) return set_err(grouped && sq_hook ? AETH_ERR_ARG : AETH_ERR_UNSUPPORTED);
     const bool fuse_clip = !sq_hook && n <= kSqGroupMax;
-    std::vector<Param*> ps(n);
-    for (int i = 0; i < n; ++i) ps[i] = &ctx->params[idx[i]];
-    // Without a hook the norms, the clip (and a clip group's exchange) are the
-    // first phase of the Adam launch; the two-launch path below remains for
-    // the hook, for more than 16 matrices, and when the device cannot hold the
-    // fused launch's CTAs at once.
-    bool fused_done = false;
-    if (fuse_clip && n <= kAdamGroupMax) {
-        AETH_TRY(pm.mark(2, st));  // the fused launch counts as the Adam phase
-        DeviceRuntime* rt = nullptr;
-        AETH_TRY(runtime_for_current(&rt));
-        SqGroupArgs sq;
-        const int chunks = sq_fill_args(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, ctx->sq_ticket,
-                                        ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev,
-                                        grouped ? &ctx->group : nullptr, rt->err_word, &sq);
-        if (chunks < 0) return set_err(chunks);
-        const int s = b2_adam_group(ctx, ps.data(), n, 1.0f, clip, 1, st, &sq, chunks);
-        if (s == AETH_OK) fused_done = true;
-        else if (s != AETH_ERR_UNSUPPORTED) return set_err(s);
+    AETH_TRY(sqnorm_group(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, ctx->sq_ticket,
+                          ctx->cfg.max_grad_norm, fuse_clip ? clip : nullptr, fuse_clip ? ctx->gnorm_dev : nullptr,
+                          st, grouped ? &ctx->group : nullptr));
+    if (!fuse_clip) {
+        if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
+        clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
+        AETH_LAUNCH_CHECK();
     }
-    if (!fused_done) {
-        AETH_TRY(sqnorm_group(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, ctx->sq_ticket,
-                              ctx->cfg.max_grad_norm, fuse_clip ? clip : nullptr, fuse_clip ? ctx->gnorm_dev : nullptr,
-                              st, grouped ? &ctx->group : nullptr));
-        if (!fuse_clip) {
-            if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
-            clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
-            AETH_LAUNCH_CHECK();
-        }
-    }
-    if (!fused_done) {
-        AETH_TRY(pm.mark(2, st));
+    AETH_TRY(pm.mark(2, st));
+    {
+        std::vector<Param*> ps(n);
+        for (int i = 0; i < n; ++i) ps[i] = &ctx->params[idx[i]];
         AETH_TRY(b2_adam_group(ctx, ps.data(), n, 1.0f, clip, 1, st));
     }
     AETH_TRY(pm.mark(3, st));

@@ -50,7 +50,6 @@ enum : uint32_t {
     DEVERR_TIMEOUT_EPI = 4u,
     DEVERR_BAD_ARG = 8u,
     DEVERR_TIMEOUT_PEER = 16u,  // a peer GPU's squared-norm sum did not arrive in time
-    DEVERR_TIMEOUT_GRID = 32u,  // a CTA of a cooperative launch waited too long for the others
 };
 
 struct DeviceRuntime {

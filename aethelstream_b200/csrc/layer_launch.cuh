@@ -122,43 +122,158 @@ inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t 
     return AETH_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Squared norms of several accumulators in one launch, deterministic: CTA
+// (c, p) writes the f64 partial sum of chunk c of accumulator p into a fixed
+// slot; the CTA that takes the last ticket sums each accumulator's slots in
+// chunk order into out[p] and, when asked, also computes the global clip
+// coefficient of clip_coeff_kernel (hook.rs:184-187) from out[0..np), then
+// resets the ticket for the next launch.
+// ---------------------------------------------------------------------------
+constexpr int kSqGroupMax = 16;
+constexpr int kSqChunks = 128;
+constexpr int kClipGroupMax = 16;  // GPUs in a clip group
+
+struct PeerSlot {
+    double sum;
+    uint64_t epoch;
+};
+
+// A group of GPUs that share one global clip through peer memory.
+struct ClipGroup {
+    int rank = 0, world = 1;
+    PeerSlot* slots[kClipGroupMax] = {};
+    uint64_t* epoch = nullptr;  // device counter of exchanges, advanced by the kernel (graph-replay safe)
+    uint64_t timeout_ns = kWaitLimitNs;
+};
+
+struct SqGroupArgs {
+    const float* x[kSqGroupMax];
+    int64_t n[kSqGroupMax];
+    int np;
+    float max_norm;
+    float* clip_out;       // null: norms only
+    double* gnorm_out;     // optional, with clip_out
+    double* out;           // np sums
+    double* partials;      // kSqGroupMax * kSqChunks
+    unsigned int* ticket;  // zero between launches
+    // Exchange of the local sum with the other GPUs of a clip group (world > 1):
+    // slots[p] is rank p's slot buffer (peer memory for p != rank), laid out as
+    // [parity][world] entries of {double sum, uint64 epoch}.
+    PeerSlot* slots[kClipGroupMax];
+    int rank, world;
+    uint64_t* epoch;  // advanced by one per launch by the last CTA
+    uint64_t timeout_ns;
+    uint32_t* err;
+};
+
+// Peer exchange primitives: a release store of the epoch after the value, an
+// acquire load on the reader's side, both at system scope (NVLink peers).
+__device__ __forceinline__ void st_release_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Writes this rank's sum into every group member's slot for this epoch, waits
+// (bounded) for every member's sum, and returns the total in rank order, so
+// every rank gets the same bits.  On timeout: flags the error and returns NaN.
+__device__ inline double clip_group_total(const SqGroupArgs& a, double local) {
+    const uint64_t epoch = *a.epoch + 1;
+    *a.epoch = epoch;
+    const int par = (int)(epoch & 1u);
+    for (int p = 0; p < a.world; ++p) {
+        PeerSlot* s = a.slots[p] + par * a.world + a.rank;
+        s->sum = local;
+        st_release_sys_u64(&s->epoch, epoch);
+    }
+    double total = 0.0;
+    const uint64_t t0 = global_ns();
+    for (int p = 0; p < a.world; ++p) {
+        PeerSlot* s = a.slots[a.rank] + par * a.world + p;
+        while (ld_acquire_sys_u64(&s->epoch) != epoch) {
+            if (global_ns() - t0 > a.timeout_ns) {
+                report_dev_error(a.err, DEVERR_TIMEOUT_PEER);
+                return __longlong_as_double(0x7ff8000000000000ll);
+            }
+        }
+        total += *reinterpret_cast<volatile double*>(&s->sum);
+    }
+    return total;
+}
+
+__global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant__ SqGroupArgs a) {
+    __shared__ double red[8];
+    __shared__ unsigned int taken;
+    const int p = blockIdx.y;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x[p]);
+    const int64_t n = a.n[p], n4 = n / 4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    double s[4] = {0.0, 0.0, 0.0, 0.0};
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n4; i += 4 * stride) {  // four independent 16-byte loads in flight
+        float4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = __ldcg(x4 + i + k * stride);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            s[k] += (double)u[k].x * u[k].x + (double)u[k].y * u[k].y + (double)u[k].z * u[k].z +
+                    (double)u[k].w * u[k].w;
+    }
+    for (; i < n4; i += stride) {
+        const float4 u = __ldcg(x4 + i);
+        s[0] += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
+    }
+    for (int64_t k = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += stride) {
+        const double v = (double)a.x[p][k];
+        s[0] += v * v;
+    }
+    const double sum = warp_sum_d((s[0] + s[1]) + (s[2] + s[3]));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+        a.partials[p * kSqChunks + blockIdx.x] = t;
+        __threadfence();
+        taken = atomicAdd(a.ticket, 1u);
+    }
+    __syncthreads();
+    if (taken != gridDim.x * gridDim.y - 1) return;
+    __threadfence();
+    // Last CTA: warp w reduces accumulators w, w + 8, ... in a fixed order
+    // (lane L: chunks L, L + 32, ...; then a fixed shuffle tree).
+    const int lane = threadIdx.x & 31;
+    for (int q = threadIdx.x >> 5; q < a.np; q += (int)(blockDim.x >> 5)) {
+        double t = 0.0;
+        for (int c = lane; c < (int)gridDim.x; c += 32) t += __ldcg(a.partials + q * kSqChunks + c);
+        t = warp_sum_d(t);
+        if (lane == 0) a.out[q] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (a.clip_out) {
+            double t = 0.0;
+            for (int k = 0; k < a.np; ++k) t += a.out[k];
+            if (a.world > 1) t = clip_group_total(a, t);
+            const double gnorm = sqrt(t);
+            const float c = (float)((double)a.max_norm / (gnorm + 1e-6));
+            // a missing peer: this step's gradients are dropped (clip 0); the
+            // error word tells the host, which restores the saved state
+            *a.clip_out = t != t ? 0.0f : (c < 1.0f ? c : 1.0f);
+            if (a.gnorm_out) *a.gnorm_out = gnorm;
+        }
+        *a.ticket = 0u;
+    }
+}
+
 // out[i] = sum of squares of xs[i] (f64).  With clip_out (np <= kSqGroupMax)
 // the same launch also writes the global clip coefficient for max_norm.
 // With a clip group of several GPUs the clip is computed from the sum over
 // the whole group (clip_group_total); the device epoch advances once per launch.
-// Arguments of one squared-norm launch over cnt accumulators (cnt <=
-// kSqGroupMax); returns the chunks per accumulator, or a negative status.
-inline int sq_fill_args(const float* const* xs, const int64_t* ns, int cnt, double* out, double* partials,
-                        unsigned int* ticket, float max_norm, float* clip_out, double* gnorm_out,
-                        const ClipGroup* group, uint32_t* err, SqGroupArgs* a) {
-    memset(a, 0, sizeof(*a));
-    int64_t largest = 0;
-    for (int i = 0; i < cnt; ++i) {
-        a->x[i] = xs[i];
-        a->n[i] = ns[i];
-        largest = std::max(largest, a->n[i]);
-        if ((reinterpret_cast<uintptr_t>(a->x[i]) & 15) != 0) return AETH_ERR_UNSUPPORTED;
-    }
-    a->np = cnt;
-    a->max_norm = max_norm;
-    a->clip_out = clip_out;
-    a->gnorm_out = gnorm_out;
-    a->out = out;
-    a->partials = partials;
-    a->ticket = ticket;
-    a->world = 1;
-    a->err = err;
-    a->timeout_ns = 0;
-    if (group && group->world > 1) {
-        a->rank = group->rank;
-        a->world = group->world;
-        for (int p = 0; p < group->world; ++p) a->slots[p] = group->slots[p];
-        a->epoch = group->epoch;
-        a->timeout_ns = group->timeout_ns;
-    }
-    return sq_chunks_for(largest);
-}
-
 inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, double* out, double* partials,
                         unsigned int* ticket, float max_norm, float* clip_out, double* gnorm_out, cudaStream_t st,
                         ClipGroup* group = nullptr) {
@@ -169,9 +284,32 @@ inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, doubl
     for (int off = 0; off < np; off += kSqGroupMax) {
         const int cnt = std::min(kSqGroupMax, np - off);
         SqGroupArgs a;
-        const int chunks = sq_fill_args(xs + off, ns + off, cnt, out + off, partials, ticket, max_norm, clip_out,
-                                        gnorm_out, group, rt->err_word, &a);
-        if (chunks < 0) return chunks;
+        memset(&a, 0, sizeof(a));
+        int64_t largest = 0;
+        for (int i = 0; i < cnt; ++i) {
+            a.x[i] = xs[off + i];
+            a.n[i] = ns[off + i];
+            largest = std::max(largest, a.n[i]);
+            if ((reinterpret_cast<uintptr_t>(a.x[i]) & 15) != 0) return AETH_ERR_UNSUPPORTED;
+        }
+        a.np = cnt;
+        a.max_norm = max_norm;
+        a.clip_out = clip_out;
+        a.gnorm_out = gnorm_out;
+        a.out = out + off;
+        a.partials = partials;
+        a.ticket = ticket;
+        a.world = 1;
+        a.err = rt->err_word;
+        if (group && group->world > 1) {
+            a.rank = group->rank;
+            a.world = group->world;
+            for (int p = 0; p < group->world; ++p) a.slots[p] = group->slots[p];
+            a.epoch = group->epoch;
+            a.timeout_ns = group->timeout_ns;
+        }
+        // about 8K elements per CTA, at most kSqChunks chunks per accumulator
+        const int chunks = (int)std::min<int64_t>(kSqChunks, std::max<int64_t>(1, (largest + 8191) / 8192));
         sqnorm_group_kernel<<<dim3(chunks, cnt), 256, 0, st>>>(a);
         AETH_LAUNCH_CHECK();
     }

@@ -409,14 +409,12 @@ int aeth_last_error(void);
 /* Reads and clears the device-side error word set by bounded waits on
  * `device` (synchronises the device).  Returns AETH_OK or AETH_ERR_TIMEOUT. */
 int aeth_device_error(int device);
-/* The same, returning the word's bits: which wait gave up (GRID: a CTA of the
- * fused squared-norm + Adam launch waited too long for the others). */
+/* The same, returning the word's bits: which wait gave up. */
 #define AETH_DEVERR_TIMEOUT_TMA 1u
 #define AETH_DEVERR_TIMEOUT_MMA 2u
 #define AETH_DEVERR_TIMEOUT_EPI 4u
 #define AETH_DEVERR_BAD_ARG 8u
 #define AETH_DEVERR_TIMEOUT_PEER 16u
-#define AETH_DEVERR_TIMEOUT_GRID 32u
 int aeth_device_error_bits(int device, uint32_t* bits);
 /* Library version string. */
 const char* aeth_version(void);
