@@ -245,11 +245,17 @@ __global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ misma
 // two 16-bank replicated maps and the two sorted maps.
 constexpr int kAdamDynSmem = 3 * kDmapLutEntries * 8 + (2 * 256 * 16 + 2 * 256) * 4;
 
+// A CTA of 512 threads is two independent 256-thread halves: each takes its
+// own blocks and synchronises through its own named barrier, while both share
+// one copy of the code tables, so two CTAs (32 warps) fit an SM where three
+// 256-thread CTAs (24 warps) did.
 template <bool DYN>
-__global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
+__global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
     extern __shared__ __align__(16) uint2 dyn_smem[];
-    __shared__ float red_m[2][8], red_v[2][8];  // by block parity: one barrier per block
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, l16 = lane & 15;
+    __shared__ float red_m[2][2][8], red_v[2][2][8];  // [half][block parity][warp]: one barrier per block
+    const int half = threadIdx.x >> 8, tid = threadIdx.x & 255;
+    const int lane = tid & 31, warp = tid >> 5, l16 = lane & 15;
+    const int vcta = blockIdx.x * 2 + half, vgrid = gridDim.x * 2;
     uint2* lut_s = dyn_smem;
     uint2* lut_u = lut_s + 2 * kDmapLutEntries;
     float* rep_s = reinterpret_cast<float*>(lut_u + kDmapLutEntries);
@@ -276,26 +282,26 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     const float2 clipx2 = make_float2(clip, clip);
     const bool fast_dir = a.eps >= 1e-10f;  // the error bound and the flush-to-zero argument need it
     const int total = a.block_begin[a.np];
-    // Blocks: the first gridDim.x by CTA index, the rest handed out by a device
+    // Blocks: the first 2 * gridDim.x by half index, the rest handed out by a device
     // counter (even finish times).  Each block's inputs are loaded one
     // iteration ahead, during the previous block's encode.
-    __shared__ int s_next[2];
+    __shared__ int s_next[2][2];
     int it = 0;
-    int gb = blockIdx.x;
+    int gb = vcta;
     int p = 0, b = 0;
     int64_t e0 = 0;
     bool valid = false;
     float sm = 0.0f, sv = 0.0f;
     float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
     uint2 qm = make_uint2(0u, 0u), qv = qm;
-    // A CTA's blocks come in increasing order (its first by index, then from
+    // A half's blocks come in increasing order (its first by index, then from
     // the counter, offset by the grid), so the owning parameter only moves
     // forward: the search continues from the current one.
     auto fetch = [&](int blk) {
 #pragma unroll 1
         while (p + 1 < a.np && blk >= a.block_begin[p + 1]) ++p;
         b = blk - a.block_begin[p];
-        e0 = (int64_t)b * 2048 + threadIdx.x * 8;
+        e0 = (int64_t)b * 2048 + tid * 8;
         valid = e0 < a.count[p];  // counts are multiples of 8
         sm = a.ms[p][b];
         sv = a.vs[p][b];
@@ -309,7 +315,7 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
     if (gb < total) fetch(gb);
     while (gb < total) {
         const int par = it & 1;
-        if (threadIdx.x == 0) s_next[par] = (int)atomicAdd(a.work, 1u) + (int)gridDim.x;
+        if (tid == 0) s_next[half][par] = (int)atomicAdd(a.work, 1u) + vgrid;
         float mo[8], va[8];
         float am = 0.0f, av = 0.0f;
         if (valid) {
@@ -353,12 +359,16 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
         }
         am = warp_max(am);
         av = warp_max(av);
-        if (lane == 0) { red_m[par][warp] = am; red_v[par][warp] = av; }
-        __syncthreads();  // the slots of this parity are rewritten two blocks later, after the next barrier
+        if (lane == 0) { red_m[half][par][warp] = am; red_v[half][par][warp] = av; }
+        // this half's 256 threads; the slots of this parity are rewritten two blocks later
+        if (half)  // constant barrier ids (warp-uniform branch)
+            asm volatile("bar.sync 2, 256;" ::: "memory");
+        else
+            asm volatile("bar.sync 1, 256;" ::: "memory");
         float bm = 0.0f, bv = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) { bm = fmaxf(bm, red_m[par][w]); bv = fmaxf(bv, red_v[par][w]); }
-        const int next = s_next[par];
+        for (int w = 0; w < 8; ++w) { bm = fmaxf(bm, red_m[half][par][w]); bv = fmaxf(bv, red_v[half][par][w]); }
+        const int next = s_next[half][par];
         ++it;
         // this block's coordinates, then the next block's inputs
         const int cp = p, cb = b;
@@ -400,14 +410,14 @@ __global__ void __launch_bounds__(256) b2_adam_group_kernel(const __grid_constan
                 *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
                 *reinterpret_cast<float4*>(z + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (threadIdx.x == 0) { a.ms[cp][cb] = nsm; a.vs[cp][cb] = nsv; }
+            if (tid == 0) { a.ms[cp][cb] = nsm; a.vs[cp][cb] = nsv; }
         }
         gb = next;
     }
-    // The last CTA out resets the counters for the next launch.
-    if (threadIdx.x == 0) {
+    // The last half out resets the counters for the next launch.
+    if (tid == 0) {
         __threadfence();
-        if (atomicAdd(a.work + 1, 1u) == gridDim.x - 1) {
+        if (atomicAdd(a.work + 1, 1u) == (unsigned)vgrid - 1u) {
             a.work[0] = 0u;
             a.work[1] = 0u;
         }

@@ -446,8 +446,8 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
     }
     AETH_TRY(codec_maps_ensure());
     const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
-    // 59 KB of tables per CTA: three CTAs per SM
-    static_assert(3 * (kAdamDynSmem + 1024) <= 228 * 1024, "three dynamic-codec Adam CTAs must fit an SM");
+    // 59 KB of tables per 512-thread CTA: two CTAs (32 warps) per SM
+    static_assert(2 * (kAdamDynSmem + 1024) <= 228 * 1024, "two dynamic-codec Adam CTAs must fit an SM");
     static bool attr_set[kMaxDevices] = {};
     int dev = 0;
     AETH_TRY(current_device(&dev));
@@ -484,11 +484,12 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         a.eps = cfg.eps;
         a.zero_accum = zero_accum;
         a.work = c->work;
-        const int grid = std::min(blocks, num_sms() * (dyn ? 3 : 8));
+        // each CTA is two 256-thread halves, each half one block at a time
+        const int grid = std::min((blocks + 1) / 2, num_sms() * 2);
         if (dyn)
-            b2_adam_group_kernel<true><<<grid, 256, kAdamDynSmem, st>>>(a);
+            b2_adam_group_kernel<true><<<grid, 512, kAdamDynSmem, st>>>(a);
         else
-            b2_adam_group_kernel<false><<<grid, 256, 0, st>>>(a);
+            b2_adam_group_kernel<false><<<grid, 512, 0, st>>>(a);
         AETH_LAUNCH_CHECK();
     }
     return AETH_OK;
