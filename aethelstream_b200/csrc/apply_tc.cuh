@@ -125,7 +125,6 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
         fence_mbar_init();
     }
     if (warp == 0) { tmem_alloc(tmem_slot, 2 * kApplyBN); tmem_relinquish(); }
-    nf4_tables32_init(tab, threadIdx.x, blockDim.x);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -185,6 +184,10 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
             }
         }
     } else {
+        // The epilogue warps fill the code tables while the producer's first
+        // loads and MMAs are in flight, and meet at their own barrier.
+        nf4_tables32_init(tab, threadIdx.x - 64, kEpiThreads);
+        named_bar(5, kEpiThreads);
         const int ew = warp - 2;     // 0..15
         const int q = warp & 3;      // TMEM lane quarter this warp may access = its 32-row group
         const int blk = ew >> 2;     // 64-column NF4 block of the 256-wide tile
@@ -192,7 +195,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
         const int row = q * 32 + lane;
         const bool qleader = ew < 4 && lane == 0;  // one thread per row group issues its stores
         const uint32_t tcol0 = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cl;
-        const uint32_t lut_s = nf4_byte_rep_base(tab, lane);
+        const uint32_t rep_base = nf4_byte_rep_base(tab), rep_lane = nf4_byte_rep_lane(lane);
         const uint32_t bucket_bias = nf4_bucket_bias(tab);
         int j = 0;
         int pending = -1;  // slot of this row group's previous store, released one unit later
@@ -227,8 +230,8 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     // words 2c, 2c+1 of the block: 8 adjacent bytes of chunk ck + c/2
                     const uint2 qq =
                         *reinterpret_cast<const uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
-                    nf4_dequant_word_s(qq.x, amax_old, lut_s, w);
-                    nf4_dequant_word_s(qq.y, amax_old, lut_s, w + 8);
+                    nf4_dequant_word_s(qq.x, amax_old, rep_base, rep_lane, w);
+                    nf4_dequant_word_s(qq.y, amax_old, rep_base, rep_lane, w + 8);
                     tmem_wait_ld_bind(v);
                     // w <- fl(w - lr * dW), one fused multiply-add per element (paired),
                     // then the decoupled decay.  The reference rounds lr * dW first; the

@@ -70,18 +70,7 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
     __shared__ float red[2][4];
     for (int i = threadIdx.x; i < 256; i += blockDim.x)
         tab.byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
-    for (int b = threadIdx.x; b < 33; b += blockDim.x) {
-        float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
-        int below = 0, code = -1;
-        float thr = 2.0f;
-        for (int k = 0; k < 15; ++k) {
-            float mid = (c_nf4_codes[k] + c_nf4_codes[k + 1]) * 0.5f;
-            if (mid < lo) below = k + 1;
-            else if (mid < hi) { thr = mid; code = k; }
-        }
-        if (code < 0) code = below;
-        tab.bucket32[b] = (__float_as_uint(-thr) & ~15u) | (uint32_t)(code + 1);
-    }
+    for (int b = threadIdx.x; b < 33; b += blockDim.x) tab.bucket32[b] = nf4_bucket32_entry(b);
     if (CODEC == AETH_CODEC_BLOCK_DYNAMIC) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) tab.dm[i] = c_dmap_signed[i];
         for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) tab.dlut[i] = g_dmap_lut_s[i];

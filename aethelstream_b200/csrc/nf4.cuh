@@ -130,13 +130,14 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 
 // ---------------------------------------------------------------------------
 // Tables for the fused epilogues.  byte_rep: the 256-entry byte table
-// (CODES[byte >> 4], CODES[byte & 15]) in 16 copies, entry b of copy c at
-// float2 index 16 b + c, so the 16 lanes of a half-warp (copy = lane % 16)
-// read 16 different bank pairs whatever their bytes: one 8-byte lookup costs
-// the minimum two wavefronts per warp.  bucket32[b] = the NEGATED midpoint
-// threshold of bucket b (-2.0 when the bucket holds none) with (lower code + 1)
-// stored in its low 4 mantissa bits, so the signed distance to the threshold
-// is one addition, xn + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
+// (CODES[byte >> 4], CODES[byte & 15]) in 32 copies, entry b of copy c at
+// byte offset 256 b + 8 c, so the 16 lanes of a half-warp (copy = lane) read
+// 16 different bank pairs whatever their bytes: one 8-byte lookup costs the
+// minimum two wavefronts per warp, and the 256-byte entry stride lets one
+// byte permute form the whole offset (nf4_dequant_word_s).  bucket32[b] = the
+// NEGATED midpoint threshold of bucket b with (lower code + 1) stored in its
+// low 4 mantissa bits (nf4_bucket32_entry), so the signed distance to the
+// threshold is one addition, xn + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
 // is covered by the wider near-window kNf4NearWindow32.  4-byte entries keep a
 // warp's 32 lookups in one wavefront (33 words, one bank each but the last).
 // Window budget: the stored threshold moves by at most 15 ulp of the largest
@@ -149,25 +150,33 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 constexpr float kNf4NearWindow32 = 1.5e-6f;
 
 struct Nf4Tables32 {
-    float2 byte_rep[256 * 16];
+    float2 byte_rep[256 * 32];
     uint32_t bucket32[33];
 };
 
-__device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
-    for (int i = tid; i < 256 * 16; i += nthreads)
-        t->byte_rep[i] = make_float2(c_nf4_codes[i >> 8], c_nf4_codes[(i >> 4) & 15]);
-    for (int b = tid; b < 33; b += nthreads) {
-        float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
-        int below = 0, code = -1;
-        float thr = 2.0f;
-        for (int k = 0; k < 15; ++k) {
-            float mid = (c_nf4_codes[k] + c_nf4_codes[k + 1]) * 0.5f;
-            if (mid < lo) below = k + 1;
-            else if (mid < hi) { thr = mid; code = k; }
-        }
-        if (code < 0) code = below;
-        t->bucket32[b] = (__float_as_uint(-thr) & ~15u) | (uint32_t)(code + 1);
+// Entry of bucket b (xn with rint(16 xn) + 16 == b): with a midpoint between
+// codes k and k + 1 inside, -midpoint with k + 1 in the low 4 bits; without
+// one, +2.0 (the distance xn + 2 is positive for every |xn| <= 1 + 2^-20, so
+// nothing is subtracted and no element is near) with the bucket's code
+// itself.  Either way the low nibble is what the positive-distance case
+// keeps, and it is at least 1 wherever a negative distance subtracts 1.
+__device__ __forceinline__ uint32_t nf4_bucket32_entry(int b) {
+    const float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
+    int below = 0, code = -1;
+    float thr = 0.0f;
+    for (int k = 0; k < 15; ++k) {
+        const float mid = (c_nf4_codes[k] + c_nf4_codes[k + 1]) * 0.5f;
+        if (mid < lo) below = k + 1;
+        else if (mid < hi) { thr = mid; code = k; }
     }
+    if (code < 0) return __float_as_uint(2.0f) | (uint32_t)below;
+    return (__float_as_uint(-thr) & ~15u) | (uint32_t)(code + 1);
+}
+
+__device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
+    for (int i = tid; i < 256 * 32; i += nthreads)
+        t->byte_rep[i] = make_float2(c_nf4_codes[i >> 9], c_nf4_codes[(i >> 5) & 15]);
+    for (int b = tid; b < 33; b += nthreads) t->bucket32[b] = nf4_bucket32_entry(b);
 }
 
 // Three-input min / max of sm_100 (one instruction each).  fmax3 ignores a
@@ -238,46 +247,70 @@ __device__ __forceinline__ uint32_t nf4_bucket_bias(const Nf4Tables32* t) {
     return smem_u32_addr(t->bucket32) - (0x4B400000u << 2);
 }
 
+// prmt.b32 in its default mode: a selector nibble with bit 3 set fills the
+// output byte with the sign of the selected byte.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
 // 8 values -> one packed word, two elements per step through the packed
-// f32x2 instructions.  Byte k of the word = code[2k] << 4 | code[2k+1]; pairs
-// enter from the bottom, (6,7) first.  The signed distance d = xn +
-// (-threshold) gives code = (lower + 1) - [d < 0]; d == 0 lies in the near
-// band.  ptxas may fuse the xn product into the distance add; that moves d by
-// under an ulp of xn, far inside kNf4NearWindow32, whose elements are decided
-// again exactly from the unscaled value.
+// f32x2 instructions.  Byte k of the word = code[2k] << 4 | code[2k+1].  The
+// signed distance d = xn + (-threshold) gives code = (lower + 1) - [d < 0];
+// d == 0 lies in the near band.  Packing: the entries' low nibbles (lower + 1,
+// 1..15) are funnel-shifted in from the top, one instruction per element, in
+// the order 1,0,3,2,5,4,7,6 that puts element j at its nibble; the signs of
+// the eight distances are gathered as bytes (prmt sign fill) and subtracted
+// at the nibbles' low bits, which cannot borrow since every nibble is >= 1.
+// ptxas may fuse the xn product into the distance add; that moves d by under
+// an ulp of xn, far inside kNf4NearWindow32, whose elements are decided again
+// exactly from the unscaled value.
 __device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t bucket_bias, float& mind) {
     const float2 inv2 = make_float2(inv, inv);
     const float2 k16 = make_float2(16.0f, 16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
-    uint32_t word = 0;
+    uint32_t e[8], sg[8];
 #pragma unroll
-    for (int s = 3; s >= 0; --s) {
+    for (int s = 0; s < 4; ++s) {
         const float2 xn = mul2_rn(make_float2(w[2 * s], w[2 * s + 1]), inv2);
         const float2 t = fma2_rn(xn, k16, kbias);  // low bits: rint(16 xn) + 16
-        uint32_t e0, e1;
-        asm("ld.shared.u32 %0, [%1];" : "=r"(e0) : "r"(bucket_bias + (__float_as_uint(t.x) << 2)));
-        asm("ld.shared.u32 %0, [%1];" : "=r"(e1) : "r"(bucket_bias + (__float_as_uint(t.y) << 2)));
-        const float2 d = add2_rn(xn, make_float2(__uint_as_float(e0), __uint_as_float(e1)));
-        const uint32_t c0 = e0 + (uint32_t)(__float_as_int(d.x) >> 31);
-        const uint32_t c1 = e1 + (uint32_t)(__float_as_int(d.y) >> 31);
+        asm("ld.shared.u32 %0, [%1];" : "=r"(e[2 * s]) : "r"(bucket_bias + (__float_as_uint(t.x) << 2)));
+        asm("ld.shared.u32 %0, [%1];" : "=r"(e[2 * s + 1]) : "r"(bucket_bias + (__float_as_uint(t.y) << 2)));
+        const float2 d = add2_rn(xn, make_float2(__uint_as_float(e[2 * s]), __uint_as_float(e[2 * s + 1])));
+        sg[2 * s] = __float_as_uint(d.x);
+        sg[2 * s + 1] = __float_as_uint(d.y);
         mind = fmin3(mind, fabsf(d.x), fabsf(d.y));
-        word = (word << 8) | ((c0 & 15u) << 4) | (c1 & 15u);
     }
-    return word;
+    uint32_t word = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        word = __funnelshift_r(word, e[2 * k + 1], 4);
+        word = __funnelshift_r(word, e[2 * k], 4);
+    }
+    // sign bytes (0xff for d < 0) of the odd and the even elements, byte k for pair k
+    const uint32_t odd = prmt(prmt(sg[1], sg[3], 0xFBu), prmt(sg[5], sg[7], 0xFBu), 0x5410u);
+    const uint32_t even = prmt(prmt(sg[0], sg[2], 0xFBu), prmt(sg[4], sg[6], 0xFBu), 0x5410u);
+    return word - (odd & 0x01010101u) - (even & 0x10101010u);
 }
 
-// Shared address of this lane's copy of the replicated byte table.
-__device__ __forceinline__ uint32_t nf4_byte_rep_base(const Nf4Tables32* t, int lane) {
-    return smem_u32_addr(t->byte_rep) + (uint32_t)(lane & 15) * 8u;
-}
+// Shared address of the replicated byte table, and this lane's copy offset
+// (lane * 8, below 256: one byte).
+__device__ __forceinline__ uint32_t nf4_byte_rep_base(const Nf4Tables32* t) { return smem_u32_addr(t->byte_rep); }
+__device__ __forceinline__ uint32_t nf4_byte_rep_lane(int lane) { return (uint32_t)(lane & 31) * 8u; }
 
 // Dequantise one packed word (8 elements) with this lane's copy of the byte
-// table (rep_s = nf4_byte_rep_base); one packed multiply per byte.
-__device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, uint32_t rep_s, float* out8) {
+// table; one packed multiply per byte.  The offset 256 byte + 8 lane is one
+// byte permute: byte 0 = the lane offset, byte 1 = byte k of the word, bytes
+// 2 and 3 = the lane offset's zero byte 1.
+__device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, uint32_t rep_base, uint32_t lane_off,
+                                                   float* out8) {
     const float2 a2 = make_float2(amax, amax);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         float2 c;
-        asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(c.x), "=f"(c.y) : "r"(rep_s + (__byte_perm(word, 0, 0x4440 + k) << 7)));
+        asm("ld.shared.v2.f32 {%0, %1}, [%2];"
+            : "=f"(c.x), "=f"(c.y)
+            : "r"(rep_base + prmt(word, lane_off, 0x5504u | ((uint32_t)k << 4))));
         const float2 p = mul2_rn(c, a2);
         out8[2 * k] = p.x;
         out8[2 * k + 1] = p.y;
