@@ -266,29 +266,35 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 // whose table index needs a finite xn, and is requantised exactly.
                 const bool bad = !(amax <= 3.402823466e38f);
                 const float inv = __frcp_rn(nf4_safe(amax));
-                float mind = bad ? 0.0f : 1.0f;
+                float mw[8];  // per packed word: the smallest distance to a threshold (0: exact path)
                 float wbuf[2][16];
                 tmem_ld16<0>(tcol, wbuf[0]);
                 tmem_wait_ld_bind(wbuf[0]);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (c < 3) tmem_ld16<0>(tcol + (uint32_t)((c + 1) * 16), wbuf[(c + 1) & 1]);
+                    mw[2 * c] = mw[2 * c + 1] = bad ? 0.0f : 1.0f;
                     if (!bad) {
-                        const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_bias, mind);
-                        const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_bias, mind);
+                        const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_bias, mw[2 * c]);
+                        const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_bias, mw[2 * c + 1]);
                         *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
                             make_uint2(lo, hi);
                     }
                     if (c < 3) tmem_wait_ld_bind(wbuf[(c + 1) & 1]);
                 }
+                const float mind = fmin3(fmin3(mw[0], mw[1], mw[2]), fmin3(mw[3], mw[4], mw[5]), fminf(mw[6], mw[7]));
                 if (__any_sync(0xffffffffu, mind < kNf4NearWindow32)) {
-                    // Rare: words holding a near-boundary element get those elements
-                    // decided exactly; a non-finite block is requantised exactly
-                    // throughout (a NaN scale gives code 0, as the reference's argmin
-                    // does).  Warp-uniform loop (TMEM loads are warp-collective).
+                    // Rare: the chunks holding a near-boundary element are loaded
+                    // again and their flagged words get those elements decided
+                    // exactly; a non-finite block is requantised exactly
+                    // throughout (a NaN scale gives code 0, as the reference's
+                    // argmin does).  Warp-uniform per chunk (TMEM loads are
+                    // warp-collective).
                     const float safe_x = nf4_safe(amax);
-#pragma unroll 1
+#pragma unroll
                     for (int c = 0; c < 4; ++c) {
+                        const bool n0w = mw[2 * c] < kNf4NearWindow32, n1w = mw[2 * c + 1] < kNf4NearWindow32;
+                        if (!__any_sync(0xffffffffu, n0w || n1w)) continue;
                         float w[16];
                         tmem_ld16<0>(tcol + (uint32_t)(c * 16), w);
                         tmem_wait_ld();
@@ -297,13 +303,10 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                             wa[0] = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe_x);
                             wa[1] = nf4_exact_word8(w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], safe_x);
                         } else {
-                            float m0v = 1.0f, m1v = 1.0f;
-                            nf4_fast_word8_s(w, inv, bucket_bias, m0v);
-                            nf4_fast_word8_s(w + 8, inv, bucket_bias, m1v);
-                            if (m0v < kNf4NearWindow32)
+                            if (n0w)
                                 wa[0] = nf4_fix_word8(wa[0], w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], inv, safe_x,
                                                       bucket_bias);
-                            if (m1v < kNf4NearWindow32)
+                            if (n1w)
                                 wa[1] = nf4_fix_word8(wa[1], w[8], w[9], w[10], w[11], w[12], w[13], w[14], w[15], inv,
                                                       safe_x, bucket_bias);
                         }

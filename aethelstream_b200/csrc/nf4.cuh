@@ -137,7 +137,7 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 // byte permute form the whole offset (nf4_dequant_word_s).  bucket32[b] = the
 // NEGATED midpoint threshold of bucket b with (lower code + 1) stored in its
 // low 4 mantissa bits (nf4_bucket32_entry), so the signed distance to the
-// threshold is one addition, xn + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
+// threshold is one fused multiply-add, inv x + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
 // is covered by the wider near-window kNf4NearWindow32.  4-byte entries keep a
 // warp's 32 lookups in one wavefront (33 words, one bank each but the last).
 // Window budget: the stored threshold moves by at most 15 ulp of the largest
@@ -217,13 +217,14 @@ __device__ __noinline__ uint32_t nf4_fix_word8(uint32_t word, float a0, float a1
                                                float a5, float a6, float a7, float inv, float safe,
                                                uint32_t bucket_bias) {
     const float a[8] = {a0, a1, a2, a3, a4, a5, a6, a7};
+    const float inv16 = inv * 16.0f;
 #pragma unroll 1
     for (int j = 0; j < 8; ++j) {
-        const float xn = __fmul_rn(a[j], inv);
-        const float t = __fmaf_rn(xn, 16.0f, 12582928.0f);
+        // the fast classifier's bucket and distance, bit for bit (nf4_fast_word8_s)
+        const float t = __fmaf_rn(a[j], inv16, 12582928.0f);
         uint32_t e;
         asm volatile("ld.shared.u32 %0, [%1];" : "=r"(e) : "r"(bucket_bias + (__float_as_uint(t) << 2)));
-        const float d = __fadd_rn(xn, __uint_as_float(e));
+        const float d = __fmaf_rn(a[j], inv, __uint_as_float(e));
         if (fabsf(d) < kNf4NearWindow32) {
             const uint32_t k = (e & 15u) - 1u;
             const float xe = __fdiv_rn(a[j], safe);
@@ -263,20 +264,24 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 // the order 1,0,3,2,5,4,7,6 that puts element j at its nibble; the signs of
 // the eight distances are gathered as bytes (prmt sign fill) and subtracted
 // at the nibbles' low bits, which cannot borrow since every nibble is >= 1.
-// ptxas may fuse the xn product into the distance add; that moves d by under
-// an ulp of xn, far inside kNf4NearWindow32, whose elements are decided again
-// exactly from the unscaled value.
+// Both the bucket index and the distance are single fused multiply-adds of the
+// unscaled value: t = rn(16 inv w + 1.5*2^23 + 16) (16 inv is exact) and d =
+// rn(inv w - threshold).  The exact product moves d by under an ulp of xn from
+// the separately rounded xn + entry, far inside kNf4NearWindow32, whose
+// elements are decided again exactly; a bucket index that rounding moves
+// across a bucket edge still classifies correctly, since every midpoint lies
+// at least 8e-3 inside its bucket.
 __device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t bucket_bias, float& mind) {
     const float2 inv2 = make_float2(inv, inv);
-    const float2 k16 = make_float2(16.0f, 16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
+    const float2 inv16 = make_float2(inv * 16.0f, inv * 16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
     uint32_t e[8], sg[8];
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
-        const float2 xn = mul2_rn(make_float2(w[2 * s], w[2 * s + 1]), inv2);
-        const float2 t = fma2_rn(xn, k16, kbias);  // low bits: rint(16 xn) + 16
+        const float2 x = make_float2(w[2 * s], w[2 * s + 1]);
+        const float2 t = fma2_rn(x, inv16, kbias);  // low bits: rint(16 xn) + 16
         asm("ld.shared.u32 %0, [%1];" : "=r"(e[2 * s]) : "r"(bucket_bias + (__float_as_uint(t.x) << 2)));
         asm("ld.shared.u32 %0, [%1];" : "=r"(e[2 * s + 1]) : "r"(bucket_bias + (__float_as_uint(t.y) << 2)));
-        const float2 d = add2_rn(xn, make_float2(__uint_as_float(e[2 * s]), __uint_as_float(e[2 * s + 1])));
+        const float2 d = fma2_rn(x, inv2, make_float2(__uint_as_float(e[2 * s]), __uint_as_float(e[2 * s + 1])));
         sg[2 * s] = __float_as_uint(d.x);
         sg[2 * s + 1] = __float_as_uint(d.y);
         mind = fmin3(mind, fabsf(d.x), fabsf(d.y));
