@@ -693,14 +693,17 @@ int aeth_dynamic_map(int is_signed, float out[256]) {
 }
 
 int aeth_selfcheck(int which, unsigned long long* mismatches) {
-    if (!mismatches || which < AETH_SELFCHECK_DMAP_SIGNED || which > AETH_SELFCHECK_ADAM_DIR)
+    if (!mismatches || which < AETH_SELFCHECK_DMAP_SIGNED || which > AETH_SELFCHECK_NF4_CLASSIFY)
         return set_err(AETH_ERR_ARG);
     AETH_TRY(codec_maps_ensure());
     unsigned long long* d = nullptr;
     AETH_CUDA(cudaMalloc(&d, sizeof(*d)));
     cudaError_t e = cudaMemset(d, 0, sizeof(*d));
     if (e == cudaSuccess) {
-        if (which == AETH_SELFCHECK_ADAM_DIR)
+        if (which == AETH_SELFCHECK_NF4_CLASSIFY) {
+            const float amaxes[] = {1.0f, 0.37f, 0.02f, 3.3e-5f, 1e-9f, 7.7e30f};
+            for (float amax : amaxes) nf4_classify_selfcheck_kernel<<<num_sms() * 8, 256>>>(amax, d);
+        } else if (which == AETH_SELFCHECK_ADAM_DIR)
             adam_dir_selfcheck_kernel<<<num_sms() * 8, 256>>>(d);
         else
             dmap_selfcheck_kernel<<<num_sms() * 8, 256>>>(which == AETH_SELFCHECK_DMAP_SIGNED ? 1 : 0, d);

@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
         const bool qleader = ew < 4 && lane == 0;  // one thread per row group issues its stores
         const uint32_t tcol0 = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cl;
         const uint32_t rep_base = nf4_byte_rep_base(tab), rep_lane = nf4_byte_rep_lane(lane);
-        const uint32_t bucket_bias = nf4_bucket_bias(tab);
+        const uint32_t bucket_bias = nf4_bucket_bias(tab), bucket_lane = tab->bucket32[lane];
         int j = 0;
         int pending = -1;  // slot of this row group's previous store, released one unit later
         for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
@@ -273,13 +273,14 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (c < 3) tmem_ld16<0>(tcol + (uint32_t)((c + 1) * 16), wbuf[(c + 1) & 1]);
-                    mw[2 * c] = mw[2 * c + 1] = bad ? 0.0f : 1.0f;
-                    if (!bad) {
-                        const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_bias, mw[2 * c]);
-                        const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_bias, mw[2 * c + 1]);
-                        *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
-                            make_uint2(lo, hi);
-                    }
+                    // all lanes classify (the entries come by shuffle); a non-finite
+                    // block's words are rewritten on the exact path below
+                    mw[2 * c] = mw[2 * c + 1] = 1.0f;
+                    const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_lane, mw[2 * c]);
+                    const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_lane, mw[2 * c + 1]);
+                    if (bad) mw[2 * c] = mw[2 * c + 1] = 0.0f;
+                    *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
+                        make_uint2(lo, hi);
                     if (c < 3) tmem_wait_ld_bind(wbuf[(c + 1) & 1]);
                 }
                 const float mind = fmin3(fmin3(mw[0], mw[1], mw[2]), fmin3(mw[3], mw[4], mw[5]), fminf(mw[6], mw[7]));

@@ -43,12 +43,12 @@ __global__ void __launch_bounds__(256) lomo_sqnorm_kernel(const uint16_t* __rest
 }
 
 // Shared tables of the update kernel: the NF4 byte table (dequant), the
-// 33-bucket classifier of the fused apply epilogue (requant), and for the
+// 29-bucket classifier of the fused apply epilogue (requant), and for the
 // dynamic codec the signed map and its bucket table.
 struct LomoTables {
     float2 byte_lut[256];
-    uint32_t bucket32[33];
-    uint32_t pad_[3];
+    uint32_t bucket32[32];
+    uint32_t pad_[4];  // keeps dlut 16-byte aligned
     float dm[256];
     uint2 dlut[2 * kDmapLutEntries];
 };
@@ -70,13 +70,14 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
     __shared__ float red[2][4];
     for (int i = threadIdx.x; i < 256; i += blockDim.x)
         tab.byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
-    for (int b = threadIdx.x; b < 33; b += blockDim.x) tab.bucket32[b] = nf4_bucket32_entry(b);
+    for (int b = threadIdx.x; b < 32; b += blockDim.x) tab.bucket32[b] = nf4_bucket32_entry(b);
     if (CODEC == AETH_CODEC_BLOCK_DYNAMIC) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) tab.dm[i] = c_dmap_signed[i];
         for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) tab.dlut[i] = g_dmap_lut_s[i];
     }
     __syncthreads();
     const uint32_t bucket_bias = smem_u32_addr(tab.bucket32) - (0x4B400000u << 2);
+    const uint32_t bucket_lane = tab.bucket32[threadIdx.x & 31];
     const double gnorm = sqrt(*sq);
     float clip = (float)((double)max_norm / (gnorm + 1e-6));
     clip = clip < 1.0f ? clip : 1.0f;
@@ -137,11 +138,10 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
         const bool bad = !(aw <= 3.402823466e38f);
         const float safe = nf4_safe(aw), inv = __frcp_rn(safe);
         uint32_t pk0 = 0u, pk1 = 0u;
-        float mind = bad ? 0.0f : 1.0f;
-        if (!bad) {
-            pk0 = nf4_fast_word8_s(w, inv, bucket_bias, mind);
-            pk1 = nf4_fast_word8_s(w + 8, inv, bucket_bias, mind);
-        }
+        float mind = 1.0f;
+        pk0 = nf4_fast_word8_s(w, inv, bucket_lane, mind);  // all lanes: entries come by shuffle
+        pk1 = nf4_fast_word8_s(w + 8, inv, bucket_lane, mind);
+        if (bad) mind = 0.0f;
         if (mind < kNf4NearWindow32) {  // rare: exact decisions next to a boundary, or a non-finite block
             if (bad) {
                 pk0 = nf4_exact_word8(w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], safe);

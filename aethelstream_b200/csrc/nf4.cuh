@@ -134,34 +134,42 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 // byte offset 256 b + 8 c, so the 16 lanes of a half-warp (copy = lane) read
 // 16 different bank pairs whatever their bytes: one 8-byte lookup costs the
 // minimum two wavefronts per warp, and the 256-byte entry stride lets one
-// byte permute form the whole offset (nf4_dequant_word_s).  bucket32[b] = the
-// NEGATED midpoint threshold of bucket b with (lower code + 1) stored in its
-// low 4 mantissa bits (nf4_bucket32_entry), so the signed distance to the
-// threshold is one fused multiply-add, inv x + entry; the perturbation (< 16 ulp, < 1e-6 absolute)
-// is covered by the wider near-window kNf4NearWindow32.  4-byte entries keep a
-// warp's 32 lookups in one wavefront (33 words, one bank each but the last).
+// byte permute form the whole offset (nf4_dequant_word_s).
+//
+// Buckets: bucket b = rint(14 xn) + 14 (0..28; width 1/14 is narrower than the
+// smallest gap between midpoints, 0.085, and every midpoint lies at least
+// 3.4e-3 inside its bucket), read from the float bits of t = fma(x, 14 inv,
+// 1.5*2^23 + 14) as bits(t) - 0x4B400000.  29 entries fit one warp: lane b
+// holds entry b in a register and the fast path fetches entries with one
+// shuffle; bucket32 keeps the same entries in shared memory for the
+// divergent rare path.  Entry b = the NEGATED midpoint threshold of bucket b
+// with (lower code + 1) stored in its low 4 mantissa bits (nf4_bucket32_entry),
+// so the signed distance to the threshold is one fused multiply-add, inv x +
+// entry; the perturbation (< 16 ulp, < 1e-6 absolute) is covered by the wider
+// near-window kNf4NearWindow32.
 // Window budget: the stored threshold moves by at most 15 ulp of the largest
-// midpoint (0.8615: 8.9e-7); xn = x * rcp(absmax) is within 2 ulp of x / absmax
+// midpoint (0.8615: 8.9e-7); x * rcp(absmax) is within 2 ulp of x / absmax
 // (2.4e-7); the fp32 midpoint and the reference's rounded distances add under
-// 5e-8.  Total 1.2e-6, so 1.5e-6 leaves a quarter in reserve.  Every midpoint
-// lies at least 8e-3 inside its bucket, so a near element is always near its
-// own bucket's threshold.
+// 5e-8.  Total 1.2e-6, so 1.5e-6 leaves a quarter in reserve.  A near element
+// is always near its own bucket's threshold (the 3.4e-3 margin).
 // ---------------------------------------------------------------------------
 constexpr float kNf4NearWindow32 = 1.5e-6f;
+constexpr float kNf4BucketScale = 14.0f;
+constexpr float kNf4BucketMagic = 12582926.0f;  // 1.5 * 2^23 + 14
 
 struct Nf4Tables32 {
     float2 byte_rep[256 * 32];
-    uint32_t bucket32[33];
+    uint32_t bucket32[32];  // entries 0..28 used; 29..31 hold the top code, as the lanes do
 };
 
-// Entry of bucket b (xn with rint(16 xn) + 16 == b): with a midpoint between
-// codes k and k + 1 inside, -midpoint with k + 1 in the low 4 bits; without
-// one, +2.0 (the distance xn + 2 is positive for every |xn| <= 1 + 2^-20, so
-// nothing is subtracted and no element is near) with the bucket's code
-// itself.  Either way the low nibble is what the positive-distance case
-// keeps, and it is at least 1 wherever a negative distance subtracts 1.
+// Entry of bucket b: with a midpoint between codes k and k + 1 inside,
+// -midpoint with k + 1 in the low 4 bits; without one, +2.0 (the distance
+// xn + 2 is positive for every |xn| <= 1 + 2^-20, so nothing is subtracted and
+// no element is near) with the bucket's code itself.  Either way the low
+// nibble is what the positive-distance case keeps, and it is at least 1
+// wherever a negative distance subtracts 1.
 __device__ __forceinline__ uint32_t nf4_bucket32_entry(int b) {
-    const float lo = ((float)b - 16.5f) * 0.0625f, hi = ((float)b - 15.5f) * 0.0625f;
+    const float lo = ((float)b - 14.5f) / kNf4BucketScale, hi = ((float)b - 13.5f) / kNf4BucketScale;
     int below = 0, code = -1;
     float thr = 0.0f;
     for (int k = 0; k < 15; ++k) {
@@ -176,7 +184,7 @@ __device__ __forceinline__ uint32_t nf4_bucket32_entry(int b) {
 __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
     for (int i = tid; i < 256 * 32; i += nthreads)
         t->byte_rep[i] = make_float2(c_nf4_codes[i >> 9], c_nf4_codes[(i >> 5) & 15]);
-    for (int b = tid; b < 33; b += nthreads) t->bucket32[b] = nf4_bucket32_entry(b);
+    for (int b = tid; b < 32; b += nthreads) t->bucket32[b] = nf4_bucket32_entry(b);
 }
 
 // Three-input min / max of sm_100 (one instruction each).  fmax3 ignores a
@@ -217,11 +225,11 @@ __device__ __noinline__ uint32_t nf4_fix_word8(uint32_t word, float a0, float a1
                                                float a5, float a6, float a7, float inv, float safe,
                                                uint32_t bucket_bias) {
     const float a[8] = {a0, a1, a2, a3, a4, a5, a6, a7};
-    const float inv16 = inv * 16.0f;
+    const float invs = inv * kNf4BucketScale;
 #pragma unroll 1
     for (int j = 0; j < 8; ++j) {
         // the fast classifier's bucket and distance, bit for bit (nf4_fast_word8_s)
-        const float t = __fmaf_rn(a[j], inv16, 12582928.0f);
+        const float t = __fmaf_rn(a[j], invs, kNf4BucketMagic);
         uint32_t e;
         asm volatile("ld.shared.u32 %0, [%1];" : "=r"(e) : "r"(bucket_bias + (__float_as_uint(t) << 2)));
         const float d = __fmaf_rn(a[j], inv, __uint_as_float(e));
@@ -237,13 +245,11 @@ __device__ __noinline__ uint32_t nf4_fix_word8(uint32_t word, float a0, float a1
     return word;
 }
 
-// Shared-address variants for the fused apply epilogue.
 // bucket_bias: shared address of bucket32[0] minus (0x4B400000 << 2) modulo
-// 2^32, so the entry of value t = fma(xn, 16, 1.5*2^23 + 16) sits at
-// bucket_bias + (bits(t) << 2) -- one address operation.  Only finite
-// |xn| <= 1 + 2^-20 may be classified: a NaN or infinite xn would index
-// outside the table, so callers route blocks holding a non-finite value to
-// the exact path without calling this.
+// 2^32, so the entry of value t = fma(x, 14 inv, 1.5*2^23 + 14) sits at
+// bucket_bias + (bits(t) << 2).  Only finite |xn| <= 1 + 2^-20 may be looked
+// up there: callers decide elements of blocks holding a non-finite value on
+// the exact path.
 __device__ __forceinline__ uint32_t nf4_bucket_bias(const Nf4Tables32* t) {
     return smem_u32_addr(t->bucket32) - (0x4B400000u << 2);
 }
@@ -265,22 +271,26 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 // the eight distances are gathered as bytes (prmt sign fill) and subtracted
 // at the nibbles' low bits, which cannot borrow since every nibble is >= 1.
 // Both the bucket index and the distance are single fused multiply-adds of the
-// unscaled value: t = rn(16 inv w + 1.5*2^23 + 16) (16 inv is exact) and d =
-// rn(inv w - threshold).  The exact product moves d by under an ulp of xn from
-// the separately rounded xn + entry, far inside kNf4NearWindow32, whose
-// elements are decided again exactly; a bucket index that rounding moves
-// across a bucket edge still classifies correctly, since every midpoint lies
-// at least 8e-3 inside its bucket.
-__device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t bucket_bias, float& mind) {
+// unscaled value: t = rn(fl(14 inv) w + 1.5*2^23 + 14) and d = rn(inv w -
+// threshold).  The exact product moves d by under an ulp of xn from the
+// separately rounded xn + entry, far inside kNf4NearWindow32, whose elements
+// are decided again exactly; a bucket index that rounding moves across a
+// bucket edge still classifies correctly, since every midpoint lies at least
+// 3.4e-3 inside its bucket.  The entry comes from lane bits(t) mod 32 of the
+// warp (lane_entry = bucket32[lane]): all 32 lanes must call this together.
+// A non-finite value reads some lane's entry and gives a meaningless code,
+// which callers replace on the exact path (their near flag is forced).
+__device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, uint32_t lane_entry, float& mind) {
     const float2 inv2 = make_float2(inv, inv);
-    const float2 inv16 = make_float2(inv * 16.0f, inv * 16.0f), kbias = make_float2(12582928.0f, 12582928.0f);
+    const float invs1 = inv * kNf4BucketScale;
+    const float2 invs = make_float2(invs1, invs1), kbias = make_float2(kNf4BucketMagic, kNf4BucketMagic);
     uint32_t e[8], sg[8];
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const float2 x = make_float2(w[2 * s], w[2 * s + 1]);
-        const float2 t = fma2_rn(x, inv16, kbias);  // low bits: rint(16 xn) + 16
-        asm("ld.shared.u32 %0, [%1];" : "=r"(e[2 * s]) : "r"(bucket_bias + (__float_as_uint(t.x) << 2)));
-        asm("ld.shared.u32 %0, [%1];" : "=r"(e[2 * s + 1]) : "r"(bucket_bias + (__float_as_uint(t.y) << 2)));
+        const float2 t = fma2_rn(x, invs, kbias);  // low bits: rint(14 xn) + 14
+        e[2 * s] = __shfl_sync(0xffffffffu, lane_entry, (int)__float_as_uint(t.x));
+        e[2 * s + 1] = __shfl_sync(0xffffffffu, lane_entry, (int)__float_as_uint(t.y));
         const float2 d = fma2_rn(x, inv2, make_float2(__uint_as_float(e[2 * s]), __uint_as_float(e[2 * s + 1])));
         sg[2 * s] = __float_as_uint(d.x);
         sg[2 * s + 1] = __float_as_uint(d.y);
@@ -296,6 +306,49 @@ __device__ __forceinline__ uint32_t nf4_fast_word8_s(const float* w, float inv, 
     const uint32_t odd = prmt(prmt(sg[1], sg[3], 0xFBu), prmt(sg[5], sg[7], 0xFBu), 0x5410u);
     const uint32_t even = prmt(prmt(sg[0], sg[2], 0xFBu), prmt(sg[4], sg[6], 0xFBu), 0x5410u);
     return word - (odd & 0x01010101u) - (even & 0x10101010u);
+}
+
+// Self-check of the classifier as the fused epilogues run it (fast word, then
+// the near-window repair of flagged words) against nf4_code_exact, for one
+// block scale: every magnitude bit pattern 0 .. bits(amax), each with both
+// signs, eight values (four magnitudes) per word.  The loop trip count is the
+// same for every lane (the classifier shuffles across the warp); words past
+// the end repeat the top magnitude and are not counted.
+__global__ void nf4_classify_selfcheck_kernel(float amax, unsigned long long* __restrict__ mismatches) {
+    __shared__ uint32_t bucket32[32];
+    if (threadIdx.x < 32) bucket32[threadIdx.x] = nf4_bucket32_entry((int)threadIdx.x);
+    __syncthreads();
+    const uint32_t lane_entry = bucket32[threadIdx.x & 31];
+    const uint32_t bias = smem_u32_addr(bucket32) - (0x4B400000u << 2);
+    const float safe = nf4_safe(amax), inv = __frcp_rn(safe);
+    const uint32_t top = __float_as_uint(amax);
+    const uint64_t nwords = ((uint64_t)top + 4) / 4;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t iters = (nwords + stride - 1) / stride;
+    unsigned long long bad = 0;
+    for (uint64_t it = 0; it < iters; ++it) {
+        const uint64_t wi = it * stride + blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+        float w[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint64_t u = wi * 4 + j;
+            w[2 * j] = __uint_as_float(u < top ? (uint32_t)u : top);
+            w[2 * j + 1] = -w[2 * j];
+        }
+        float mind = 1.0f;
+        uint32_t word = nf4_fast_word8_s(w, inv, lane_entry, mind);
+        if (mind < kNf4NearWindow32)
+            word = nf4_fix_word8(word, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7], inv, safe, bias);
+        if (wi < nwords) {
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t got = (word >> (8 * (j >> 1) + ((j & 1) ? 0 : 4))) & 15u;
+                bad += got != nf4_code_exact(w[j], safe);
+            }
+        }
+    }
+    bad = warp_sum_u64(bad);
+    if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
 // Shared address of the replicated byte table, and this lane's copy offset

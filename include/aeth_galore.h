@@ -352,15 +352,26 @@ int aeth_int8_dequantize(const int8_t* q, const float* scales, int64_t n, int co
                          float* out, aeth_stream_t stream);
 /* The 256-entry dynamic map used by AETH_CODEC_BLOCK_DYNAMIC (host copy). */
 int aeth_dynamic_map(int is_signed, float out[256]);
-/* Self-checks with no reference counterpart.  Each runs every one of the 2^32
- * float bit patterns through a fast device path and the plain definition it
- * replaces, on the current device, and stores the number of disagreements in
- * *mismatches (synchronous):
- *   DMAP_SIGNED / DMAP_UNSIGNED: the bucket-table dynamic-map encoder of the
- *     Adam and LOMO kernels against the binary search over the map;
- *   ADAM_DIR: the bf16 Adam direction from approximate sqrt and reciprocal
- *     against IEEE sqrt and division (the pattern is v; m is hashed from it). */
-enum { AETH_SELFCHECK_DMAP_SIGNED = 0, AETH_SELFCHECK_DMAP_UNSIGNED = 1, AETH_SELFCHECK_ADAM_DIR = 2 };
+/* Self-checks with no reference counterpart.  Each runs float bit patterns
+ * through a fast device path and the plain definition it replaces, on the
+ * current device, and stores the number of disagreements in *mismatches
+ * (synchronous):
+ *   DMAP_SIGNED / DMAP_UNSIGNED: all 2^32 patterns through the bucket-table
+ *     dynamic-map encoder of the Adam and LOMO kernels against the binary
+ *     search over the map;
+ *   ADAM_DIR: all 2^32 patterns; the bf16 Adam direction from approximate
+ *     sqrt and reciprocal against IEEE sqrt and division (the pattern is v; m
+ *     is hashed from it);
+ *   NF4_CLASSIFY: for block absmax values 1, 0.37, 0.02, 3.3e-5, 1e-9 (below
+ *     the 1e-8 clamp) and 7.7e30, every x with |x| <= absmax, both signs,
+ *     through the fused epilogues' NF4 classifier (bucket shuffle, near-window
+ *     repair) against the reference's argmin over IEEE x / absmax. */
+enum {
+    AETH_SELFCHECK_DMAP_SIGNED = 0,
+    AETH_SELFCHECK_DMAP_UNSIGNED = 1,
+    AETH_SELFCHECK_ADAM_DIR = 2,
+    AETH_SELFCHECK_NF4_CLASSIFY = 3
+};
 int aeth_selfcheck(int which, unsigned long long* mismatches);
 
 /* LOMO fused full-rank update over a flat NF4 tensor (Lv et al. 2023):

@@ -222,15 +222,17 @@ def test_lomo_step(oracle, L, lib, codec):
     assert rel_fro(host(pre), w) < 0.2
 
 
-@pytest.mark.parametrize("which", [0, 1, 2], ids=["dmap_signed", "dmap_unsigned", "adam_dir"])
+@pytest.mark.parametrize("which", [0, 1, 2, 3], ids=["dmap_signed", "dmap_unsigned", "adam_dir", "nf4_classify"])
 def test_fast_paths_exhaustive(lib, which):
     """Over all 2^32 float bit patterns: the bucket-table dynamic-map encoder
     of the Adam and LOMO kernels returns the binary search's code, and the
-    approximate Adam direction rounds to the same bf16 as IEEE sqrt/div."""
+    approximate Adam direction rounds to the same bf16 as IEEE sqrt/div.  Over
+    every |x| <= absmax for six block scales: the fused epilogues' NF4
+    classifier returns quantizer.py's argmin code."""
     bad = C.c_ulonglong(12345)
     assert lib.aeth_selfcheck(which, C.byref(bad)) == 0
     assert bad.value == 0
-    assert lib.aeth_selfcheck(3, C.byref(bad)) == -1  # unknown check
+    assert lib.aeth_selfcheck(4, C.byref(bad)) == -1  # unknown check
 
 
 def test_lomo_python_wrappers(oracle, L):
