@@ -123,15 +123,17 @@ inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t 
 }
 
 // ---------------------------------------------------------------------------
-// Squared norms of several accumulators in one launch, deterministic: CTA
-// (c, p) writes the f64 partial sum of chunk c of accumulator p into a fixed
-// slot; the CTA that takes the last ticket sums each accumulator's slots in
-// chunk order into out[p] and, when asked, also computes the global clip
-// coefficient of clip_coeff_kernel (hook.rs:184-187) from out[0..np), then
-// resets the ticket for the next launch.
+// Squared norms of several accumulators in one launch, deterministic: the
+// accumulators are cut into chunks of chunk_elems elements (a chunk never
+// spans two accumulators), one CTA per chunk, about four per SM; each CTA
+// writes the f64 partial sum of its chunk into a fixed slot; the CTA that
+// takes the last ticket sums each accumulator's slots in chunk order into
+// out[p] and, when asked, also computes the global clip coefficient of
+// clip_coeff_kernel (hook.rs:184-187) from out[0..np), then resets the ticket
+// for the next launch.
 // ---------------------------------------------------------------------------
 constexpr int kSqGroupMax = 16;
-constexpr int kSqChunks = 128;
+constexpr int kSqChunks = 128;  // partial slots per accumulator: kSqGroupMax * kSqChunks in all
 constexpr int kClipGroupMax = 16;  // GPUs in a clip group
 
 struct PeerSlot {
@@ -150,6 +152,8 @@ struct ClipGroup {
 struct SqGroupArgs {
     const float* x[kSqGroupMax];
     int64_t n[kSqGroupMax];
+    int chunk_begin[kSqGroupMax + 1];  // first chunk of each accumulator; chunk_begin[np] = chunks
+    int64_t chunk_elems;               // a multiple of 1024
     int np;
     float max_norm;
     float* clip_out;       // null: norms only
@@ -207,27 +211,31 @@ __device__ inline double clip_group_total(const SqGroupArgs& a, double local) {
 
 __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant__ SqGroupArgs a) {
     __shared__ double red[8];
+    __shared__ double sums[kSqGroupMax];
     __shared__ unsigned int taken;
-    const int p = blockIdx.y;
-    const float4* x4 = reinterpret_cast<const float4*>(a.x[p]);
-    const int64_t n = a.n[p], n4 = n / 4;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int chunk = blockIdx.x;
+    int p = 0;
+    while (p + 1 < a.np && chunk >= a.chunk_begin[p + 1]) ++p;
+    const int64_t c0 = (int64_t)(chunk - a.chunk_begin[p]) * a.chunk_elems;
+    const int64_t c1 = c0 + a.chunk_elems < a.n[p] ? c0 + a.chunk_elems : a.n[p];
+    const float4* x4 = reinterpret_cast<const float4*>(a.x[p] + c0);  // c0 % 4 == 0: still 16-byte aligned
+    const int n4 = (int)((c1 - c0) / 4);
     double s[4] = {0.0, 0.0, 0.0, 0.0};
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    for (; i + 3 * stride < n4; i += 4 * stride) {  // four independent 16-byte loads in flight
+    int i = threadIdx.x;
+    for (; i + 3 * 256 < n4; i += 4 * 256) {  // four independent 16-byte loads in flight
         float4 u[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) u[k] = __ldcg(x4 + i + k * stride);
+        for (int k = 0; k < 4; ++k) u[k] = __ldcg(x4 + i + k * 256);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
             s[k] += (double)u[k].x * u[k].x + (double)u[k].y * u[k].y + (double)u[k].z * u[k].z +
                     (double)u[k].w * u[k].w;
     }
-    for (; i < n4; i += stride) {
+    for (; i < n4; i += 256) {
         const float4 u = __ldcg(x4 + i);
         s[0] += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
     }
-    for (int64_t k = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += stride) {
+    for (int64_t k = c0 + 4 * (int64_t)n4 + threadIdx.x; k < c1; k += 256) {
         const double v = (double)a.x[p][k];
         s[0] += v * v;
     }
@@ -236,28 +244,31 @@ __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant
     __syncthreads();
     if (threadIdx.x == 0) {
         double t = 0.0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-        a.partials[p * kSqChunks + blockIdx.x] = t;
+        for (int w = 0; w < 8; ++w) t += red[w];
+        a.partials[chunk] = t;
         __threadfence();
         taken = atomicAdd(a.ticket, 1u);
     }
     __syncthreads();
-    if (taken != gridDim.x * gridDim.y - 1) return;
+    if (taken != gridDim.x - 1) return;
     __threadfence();
-    // Last CTA: warp w reduces accumulators w, w + 8, ... in a fixed order
-    // (lane L: chunks L, L + 32, ...; then a fixed shuffle tree).
+    // Last CTA: warp w sums accumulators w, w + 8 (lane L: chunks L, L + 32,
+    // ... of the accumulator in order; then a fixed shuffle tree).
     const int lane = threadIdx.x & 31;
-    for (int q = threadIdx.x >> 5; q < a.np; q += (int)(blockDim.x >> 5)) {
+    for (int q = threadIdx.x >> 5; q < a.np; q += 8) {
         double t = 0.0;
-        for (int c = lane; c < (int)gridDim.x; c += 32) t += __ldcg(a.partials + q * kSqChunks + c);
+        for (int c = a.chunk_begin[q] + lane; c < a.chunk_begin[q + 1]; c += 32) t += __ldcg(a.partials + c);
         t = warp_sum_d(t);
-        if (lane == 0) a.out[q] = t;
+        if (lane == 0) {
+            a.out[q] = t;
+            sums[q] = t;
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         if (a.clip_out) {
             double t = 0.0;
-            for (int k = 0; k < a.np; ++k) t += a.out[k];
+            for (int k = 0; k < a.np; ++k) t += sums[k];
             if (a.world > 1) t = clip_group_total(a, t);
             const double gnorm = sqrt(t);
             const float c = (float)((double)a.max_norm / (gnorm + 1e-6));
@@ -285,11 +296,9 @@ inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, doubl
         const int cnt = std::min(kSqGroupMax, np - off);
         SqGroupArgs a;
         memset(&a, 0, sizeof(a));
-        int64_t largest = 0;
         for (int i = 0; i < cnt; ++i) {
             a.x[i] = xs[off + i];
             a.n[i] = ns[off + i];
-            largest = std::max(largest, a.n[i]);
             if ((reinterpret_cast<uintptr_t>(a.x[i]) & 15) != 0) return AETH_ERR_UNSUPPORTED;
         }
         a.np = cnt;
@@ -308,9 +317,22 @@ inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, doubl
             a.epoch = group->epoch;
             a.timeout_ns = group->timeout_ns;
         }
-        // about 8K elements per CTA, at most kSqChunks chunks per accumulator
-        const int chunks = (int)std::min<int64_t>(kSqChunks, std::max<int64_t>(1, (largest + 8191) / 8192));
-        sqnorm_group_kernel<<<dim3(chunks, cnt), 256, 0, st>>>(a);
+        // Chunks of at least 4096 elements, about four CTAs per SM, within the
+        // kSqGroupMax * kSqChunks partial slots (a chunk per accumulator more
+        // than total / chunk_elems at most).
+        int64_t total = 0;
+        for (int i = 0; i < cnt; ++i) total += a.n[i];
+        const int64_t slots = (int64_t)kSqGroupMax * kSqChunks - kSqGroupMax;
+        int64_t ce = std::max<int64_t>(total / (4 * (int64_t)num_sms()), (total + slots - 1) / slots);
+        ce = std::max<int64_t>(4096, (ce + 1023) / 1024 * 1024);
+        a.chunk_elems = ce;
+        int chunks = 0;
+        for (int i = 0; i < cnt; ++i) {
+            a.chunk_begin[i] = chunks;
+            chunks += (int)std::max<int64_t>(1, (a.n[i] + ce - 1) / ce);
+        }
+        a.chunk_begin[cnt] = chunks;
+        sqnorm_group_kernel<<<chunks, 256, 0, st>>>(a);
         AETH_LAUNCH_CHECK();
     }
     return AETH_OK;
