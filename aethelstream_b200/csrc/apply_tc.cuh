@@ -221,18 +221,21 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 float* dout = (pr.delta_out && grow < pr.m) ? pr.delta_out + grow * pr.n + n0 + cl : nullptr;
                 float* pout = (pr.prequant_out && grow < pr.m) ? pr.prequant_out + grow * pr.n + n0 + cl : nullptr;
                 // pass 1: w = CODES * absmax_old - fl(lr * dW) [* decay] -> TMEM; block absmax.
-                // The TMEM load of a chunk is in flight while its old weights are dequantised.
+                // The next chunk's TMEM load is in flight while this chunk is updated.
                 float amax = 0.0f;
-#pragma unroll 1
+                float vb[2][16];
+                tmem_ld16<0>(tcol, vb[0]);
+                tmem_wait_ld_bind(vb[0]);
+#pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    float v[16], w[16];
-                    tmem_ld16<0>(tcol + (uint32_t)(c * 16), v);
+                    if (c < 3) tmem_ld16<0>(tcol + (uint32_t)((c + 1) * 16), vb[(c + 1) & 1]);
+                    float* v = vb[c & 1];
+                    float w[16];
                     // words 2c, 2c+1 of the block: 8 adjacent bytes of chunk ck + c/2
                     const uint2 qq =
                         *reinterpret_cast<const uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
                     nf4_dequant_word_s(qq.x, amax_old, rep_base, rep_lane, w);
                     nf4_dequant_word_s(qq.y, amax_old, rep_base, rep_lane, w + 8);
-                    tmem_wait_ld_bind(v);
                     // w <- fl(w - lr * dW), one fused multiply-add per element (paired),
                     // then the decoupled decay.  The reference rounds lr * dW first; the
                     // two differ by under half an ulp of the product, inside the update's
@@ -258,6 +261,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                         for (int i = 0; i < 16; i += 4)
                             *reinterpret_cast<float4*>(pout + c * 16 + i) = make_float4(w[i], w[i + 1], w[i + 2], w[i + 3]);
                     }
+                    if (c < 3) tmem_wait_ld_bind(vb[(c + 1) & 1]);
                 }
                 tmem_wait_st();
                 // pass 2: requantise from TMEM (fast classifier; exact fix-up next to
