@@ -207,9 +207,13 @@ __device__ __noinline__ float adam_dir_exact_rare(float mo, float va, float eps)
 // The .ftz forms are single hardware instructions.  They flush subnormals: a
 // subnormal v has a square root below 1.1e-19, under half an ulp of any
 // eps >= 1e-10 (callers use the fast path only then), so d is the same either
-// way and normal; q is formed by an ordinary multiply and tiny results take
-// the exact path.
-__device__ __forceinline__ float adam_dir_fast(float mo, float va, float eps) {
+// way and at least eps; q is formed by an ordinary multiply.  Returns q and
+// sets `flag` where the exact path is needed: q within the guard of a bf16
+// tie; q nonzero below 2^-100, infinite or NaN (a NaN v or a NaN / infinite m
+// gives a NaN q); or v with its sign bit set (a negative subnormal v flushes
+// to -0 where IEEE sqrt gives NaN; -0 itself gives the same either way).
+// Callers OR the flags of several elements and branch once.
+__device__ __forceinline__ float adam_dir_q(float mo, float va, float eps, uint32_t& flag) {  // flag: 0 or 1
     float s, r;
     asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(s) : "f"(va));
     const float d = __fadd_rn(s, eps);
@@ -217,11 +221,16 @@ __device__ __forceinline__ float adam_dir_fast(float mo, float va, float eps) {
     const float q = __fmul_rn(mo, r);
     const uint32_t qb = __float_as_uint(q), mag = qb & 0x7fffffffu;
     const bool near_tie = ((qb & 0xffffu) + kAdamDirGuard - 0x8000u) < 2u * kAdamDirGuard;
-    // nonzero below 2^-100, inf or NaN, a tiny denominator, or v < 0 (a negative
-    // subnormal v flushes to -0 where IEEE sqrt gives NaN)
-    const bool odd = (mag - 1u) < 0x0d7fffffu || mag >= 0x7f800000u || !(d >= 1e-30f) || !(va >= 0.0f);
-    if (near_tie || odd) return adam_dir_exact_rare(mo, va, eps);
+    // mag in [1, 2^-100) wraps to the top of the range, [inf, NaN] lands just above 0x72000000
+    const bool odd = (mag - 0x0d800000u) >= 0x72000000u && mag != 0u;
+    flag = (uint32_t)(near_tie || odd) | (__float_as_uint(va) >> 31);
     return q;
+}
+
+__device__ __forceinline__ float adam_dir_fast(float mo, float va, float eps) {
+    uint32_t flag = 0;
+    const float q = adam_dir_q(mo, va, eps, flag);
+    return flag ? adam_dir_exact_rare(mo, va, eps) : q;
 }
 
 // Every float bit pattern as va, with mo drawn from [-0.5, 0.5) by a hash of
@@ -243,7 +252,7 @@ __global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ misma
 
 // Dynamic-codec shared memory of b2_adam_group_kernel: the two bucket tables,
 // two 16-bank replicated maps and the two sorted maps.
-constexpr int kAdamDynSmem = 3 * kDmapLutEntries * 8 + (2 * 256 * 16 + 2 * 256) * 4;
+constexpr int kAdamDynSmem = (2 * kDmapLutEntries + kDmapLutUEntries) * 8 + (2 * 256 * 16 + 2 * 256) * 4;
 
 // A CTA of 512 threads is two independent 256-thread halves: each takes its
 // own blocks and synchronises through its own named barrier, while both share
@@ -258,7 +267,7 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
     const int vcta = blockIdx.x * 2 + half, vgrid = gridDim.x * 2;
     uint2* lut_s = dyn_smem;
     uint2* lut_u = lut_s + 2 * kDmapLutEntries;
-    float* rep_s = reinterpret_cast<float*>(lut_u + kDmapLutEntries);
+    float* rep_s = reinterpret_cast<float*>(lut_u + kDmapLutUEntries);
     float* rep_u = rep_s + 256 * 16;
     float* map_s = rep_u + 256 * 16;
     float* map_u = map_s + 256;
@@ -272,7 +281,7 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
             map_u[i] = c_dmap_unsigned[i];
         }
         for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) lut_s[i] = g_dmap_lut_s[i];
-        for (int i = threadIdx.x; i < kDmapLutEntries; i += blockDim.x) lut_u[i] = g_dmap_lut_u[i];
+        for (int i = threadIdx.x; i < kDmapLutUEntries; i += blockDim.x) lut_u[i] = g_dmap_lut_u[i];
     }
     __syncthreads();
     const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
@@ -321,7 +330,8 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
         if (valid) {
             const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
             const float2 smx2 = make_float2(sm, sm), svx2 = make_float2(sv, sv);
-            uint32_t nb[4];
+            float nq[8];
+            uint32_t dmask = fast_dir ? 0u : 0xffu;  // elements whose quotient needs the IEEE path
 #pragma unroll
             for (int k = 0; k < 8; k += 2) {
                 const uint32_t wm = k < 4 ? qm.x : qm.y, wv = k < 4 ? qv.x : qv.y;
@@ -347,13 +357,24 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
                 va[k] = va2.x;
                 va[k + 1] = va2.y;
                 // N is stored in bf16, so the approximate quotient serves where its
-                // bf16 rounding provably matches (for eps >= 1e-10, see adam_dir_fast).
-                const float n0 = fast_dir ? adam_dir_fast(mo2.x, va2.x, a.eps) : adam_dir_exact(mo2.x, va2.x, a.eps);
-                const float n1 = fast_dir ? adam_dir_fast(mo2.y, va2.y, a.eps) : adam_dir_exact(mo2.y, va2.y, a.eps);
-                const __nv_bfloat162 nn = __floats2bfloat162_rn(n0, n1);  // .x = n0 in the low half
+                // bf16 rounding provably matches (for eps >= 1e-10, see adam_dir_q).
+                uint32_t f0, f1;
+                nq[k] = adam_dir_q(mo2.x, va2.x, a.eps, f0);
+                nq[k + 1] = adam_dir_q(mo2.y, va2.y, a.eps, f1);
+                dmask |= (f0 | (f1 << 1)) << k;
+                am = fmax3(am, fabsf(mo2.x), fabsf(mo2.y));
+                av = fmax3(av, fabsf(va2.x), fabsf(va2.y));
+            }
+            if (dmask) {  // rare (or eps < 1e-10): the flagged quotients the IEEE way
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (dmask & (1u << k)) nq[k] = adam_dir_exact_rare(mo[k], va[k], a.eps);
+            }
+            uint32_t nb[4];
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                const __nv_bfloat162 nn = __floats2bfloat162_rn(nq[k], nq[k + 1]);  // .x = nq[k] in the low half
                 nb[k >> 1] = *reinterpret_cast<const uint32_t*>(&nn);
-                am = fmaxf(am, fmaxf(fabsf(mo2.x), fabsf(mo2.y)));
-                av = fmaxf(av, fmaxf(fabsf(va2.x), fabsf(va2.y)));
             }
             *reinterpret_cast<uint4*>(a.nout[p] + e0) = make_uint4(nb[0], nb[1], nb[2], nb[3]);
         }
@@ -392,15 +413,24 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
                 nsv = bv;
                 const float im = dyn_inv(bm), iv = dyn_inv(bv);
                 const float2 imx2 = make_float2(im, im), ivx2 = make_float2(iv, iv);
+                uint32_t ef = 0;
 #pragma unroll
                 for (int k = 0; k < 8; k += 2) {
-                    const float2 xm = mul2_rn(make_float2(mo[k], mo[k + 1]), imx2);  // dyn_xn, paired
-                    const float2 xv = mul2_rn(make_float2(va[k], va[k + 1]), ivx2);
+                    const float2 m2 = mul2_rn(make_float2(mo[k], mo[k + 1]), imx2);  // dyn_xn, paired
+                    const float2 v2 = mul2_rn(make_float2(va[k], va[k + 1]), ivx2);
                     const int sh = 8 * (k & 3);
-                    om[k >> 2] |= (dmap_encode_lut<true>(lut_s, map_s, xm.x) |
-                                   (dmap_encode_lut<true>(lut_s, map_s, xm.y) << 8)) << sh;
-                    ov[k >> 2] |= (dmap_encode_lut<false>(lut_u, map_u, xv.x) |
-                                   (dmap_encode_lut<false>(lut_u, map_u, xv.y) << 8)) << sh;
+                    om[k >> 2] |= (dmap_encode_lut_flag<true>(lut_s, m2.x, ef) |
+                                   (dmap_encode_lut_flag<true>(lut_s, m2.y, ef) << 8)) << sh;
+                    ov[k >> 2] |= (dmap_encode_lut_flag<false>(lut_u, v2.x, ef) |
+                                   (dmap_encode_lut_flag<false>(lut_u, v2.y, ef) << 8)) << sh;
+                }
+                if (ef > 0xffu) {  // rare: a bucket that needs the search; redo this thread's 16 codes
+                    om[0] = om[1] = ov[0] = ov[1] = 0u;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {  // the same normalised values, formed again
+                        om[k >> 2] |= dmap_encode_rare(map_s, __fmul_rn(mo[k], im)) << (8 * (k & 3));
+                        ov[k >> 2] |= dmap_encode_rare(map_u, __fmul_rn(va[k], iv)) << (8 * (k & 3));
+                    }
                 }
             }
             *reinterpret_cast<uint2*>(a.m8[cp] + ce0) = make_uint2(om[0], om[1]);

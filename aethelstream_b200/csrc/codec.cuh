@@ -29,25 +29,32 @@ int build_dynamic_map(int is_signed, float out[256]);
 // neighbouring map entries it compares two rounded distances, one shrinking
 // and one growing with x, so its decision flips exactly once, at a float that
 // the host finds by bisection over the search itself -- ties and rounding
-// included.  A magnitude selects bucket b = (bits(|x|) >> 17) - (103 << 6),
-// clamped to [0, kDmapLutN]: 64 buckets per octave over [2^-24, 2), bucket 0
-// also taking everything below 2^-24, and a last entry for |x| >= 2,
-// infinities and NaN.  An entry is {threshold key, code below}: code = below +
+// included.  A magnitude selects bucket b = (bits(|x|) >> S) - 103 P, clamped
+// to [0, N]: P buckets per octave over [2^-24, 2) (P = 64, S = 17 for the
+// signed map; P = 128, S = 16 for the unsigned map, whose entries near 1 lie
+// closer than 1/64 of an octave), bucket 0 also taking everything below
+// 2^-24, and a last entry for |x| >= 2, infinities and NaN.  An entry is {threshold key, code below}: code = below +
 // [key >= threshold], exact for every key of the bucket.  Buckets where the
 // code changes more than once, and the last entry, are flagged kDmapSearch
 // and sent to the binary search.
 //
 // The signed map's table has a half per sign (negative keys at offset
 // kDmapLutEntries); the unsigned map's has only the non-negative half, and a
-// negative x (never an Adam v) takes the search.  aeth_selfcheck runs every
-// float bit pattern through both paths.
+// negative x (never an Adam v) takes the search.  With these resolutions no
+// bucket of either map holds two code changes, so only |x| >= 2, infinities
+// and NaN (and a negative unsigned x) search.  aeth_selfcheck runs every float
+// bit pattern through both paths.
 // ---------------------------------------------------------------------------
-constexpr int kDmapLutExpLo = 103;                     // 2^-24
-constexpr int kDmapLutN = (128 - kDmapLutExpLo) << 6;  // 1600 buckets
-constexpr int kDmapLutEntries = kDmapLutN + 1;         // + the entry for |x| >= 2, inf, NaN
-constexpr uint32_t kDmapSearch = 0x100u;               // in the code word: always search
-__device__ uint2 g_dmap_lut_s[2 * kDmapLutEntries];   // signed map: x >= 0, then x < 0
-__device__ uint2 g_dmap_lut_u[kDmapLutEntries];       // unsigned map: x >= 0
+constexpr int kDmapLutExpLo = 103;                      // 2^-24
+constexpr int kDmapLutLog2P = 6;                        // signed map: 64 buckets per octave
+constexpr int kDmapLutULog2P = 7;                       // unsigned map: 128 buckets per octave
+constexpr int kDmapLutN = (128 - kDmapLutExpLo) << kDmapLutLog2P;     // 1600 buckets
+constexpr int kDmapLutEntries = kDmapLutN + 1;                        // + the entry for |x| >= 2, inf, NaN
+constexpr int kDmapLutUN = (128 - kDmapLutExpLo) << kDmapLutULog2P;   // 3200 buckets
+constexpr int kDmapLutUEntries = kDmapLutUN + 1;
+constexpr uint32_t kDmapSearch = 0x100u;                // in the code word: always search
+__device__ uint2 g_dmap_lut_s[2 * kDmapLutEntries];    // signed map: x >= 0, then x < 0
+__device__ uint2 g_dmap_lut_u[kDmapLutUEntries];       // unsigned map: x >= 0
 
 // The binary search on the host (dmap_encode's arithmetic: IEEE single
 // subtraction and comparison).
@@ -61,19 +68,21 @@ inline uint32_t host_dmap_encode(const float* map, float x) {
     return dh < dl ? (uint32_t)lo : (uint32_t)(lo - 1);
 }
 
-// halves = 2 for the signed map (out: 2 * kDmapLutEntries), 1 for the unsigned one.
-inline void build_dmap_lut(const float map[256], int halves, uint2* out) {
+// halves = 2 for the signed map (out: 2 * (nb + 1)), 1 for the unsigned one;
+// 2^log2p buckets per octave, nb = 25 * 2^log2p buckets and the last entry.
+inline void build_dmap_lut(const float map[256], int halves, int log2p, uint2* out) {
+    const int nb = (128 - kDmapLutExpLo) << log2p, sh = 23 - log2p;
     for (int h = 0; h < halves; ++h) {
-        uint2* o = out + h * kDmapLutEntries;
+        uint2* o = out + h * (nb + 1);
         auto code_of = [&](uint32_t key) {
             const uint32_t bits = h ? (~key | 0x80000000u) : key;  // x of this half with that key
             float x;
             memcpy(&x, &bits, 4);
             return host_dmap_encode(map, x);
         };
-        for (int b = 0; b < kDmapLutN; ++b) {
-            const uint32_t lo_ab = b == 0 ? 0u : (uint32_t)(b + (kDmapLutExpLo << 6)) << 17;
-            const uint32_t hi_ab = ((uint32_t)(b + 1 + (kDmapLutExpLo << 6)) << 17) - 1u;
+        for (int b = 0; b < nb; ++b) {
+            const uint32_t lo_ab = b == 0 ? 0u : (uint32_t)(b + (kDmapLutExpLo << log2p)) << sh;
+            const uint32_t hi_ab = ((uint32_t)(b + 1 + (kDmapLutExpLo << log2p)) << sh) - 1u;
             const uint32_t kmin = h ? ~hi_ab : lo_ab, kmax = h ? ~lo_ab : hi_ab;
             const uint32_t cmin = code_of(kmin), cmax = code_of(kmax);
             if (cmin == cmax) {  // one code throughout: a threshold no key of the bucket misses or reaches
@@ -92,7 +101,7 @@ inline void build_dmap_lut(const float map[256], int halves, uint2* out) {
                 o[b] = make_uint2(0xffffffffu, kDmapSearch);
             }
         }
-        o[kDmapLutN] = make_uint2(0xffffffffu, kDmapSearch);
+        o[nb] = make_uint2(0xffffffffu, kDmapSearch);
     }
 }
 
@@ -108,9 +117,9 @@ inline int codec_maps_ensure() {
         build_dynamic_map(0, u);
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_signed, s, sizeof(s)));
         AETH_CUDA(cudaMemcpyToSymbol(c_dmap_unsigned, u, sizeof(u)));
-        static uint2 lut_s[2 * kDmapLutEntries], lut_u[kDmapLutEntries];
-        build_dmap_lut(s, 2, lut_s);
-        build_dmap_lut(u, 1, lut_u);
+        static uint2 lut_s[2 * kDmapLutEntries], lut_u[kDmapLutUEntries];
+        build_dmap_lut(s, 2, kDmapLutLog2P, lut_s);
+        build_dmap_lut(u, 1, kDmapLutULog2P, lut_u);
         AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut_s, lut_s, sizeof(lut_s)));
         AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut_u, lut_u, sizeof(lut_u)));
         g_maps_uploaded[dev] = true;
@@ -150,26 +159,39 @@ __device__ __forceinline__ uint32_t dmap_encode(const float* __restrict__ map, f
 // for every element under a predicate.
 __device__ __noinline__ uint32_t dmap_encode_rare(const float* map, float xn) { return dmap_encode(map, xn); }
 
-// Bucket-table encode (tables built by build_dmap_lut): `lut` is the signed
-// map's table (both halves) for SIGNED, else the unsigned map's; `map` the
-// sorted map for the rare binary-search cases.  Returns dmap_encode(map, xn)
-// for every xn.
+// Bucket-table encode without a branch (tables built by build_dmap_lut): `lut`
+// is the signed map's table (both halves) for SIGNED, else the unsigned map's.
+// Returns dmap_encode(map, xn) unless the bucket is flagged for the search (or,
+// unsigned, xn is negative): then the result is meaningless and `flags` gets
+// a bit above 0xff.  Callers OR the flags of several elements and search once.
 template <bool SIGNED>
-__device__ __forceinline__ uint32_t dmap_encode_lut(const uint2* __restrict__ lut, const float* __restrict__ map,
-                                                    float xn) {
+__device__ __forceinline__ uint32_t dmap_encode_lut_flag(const uint2* __restrict__ lut, float xn, uint32_t& flags) {
     const uint32_t bits = __float_as_uint(xn);
     const uint32_t ab = bits & 0x7fffffffu;
-    const int b = min(max((int)(ab >> 17) - (kDmapLutExpLo << 6), 0), kDmapLutN);
+    constexpr int kLog2P = SIGNED ? kDmapLutLog2P : kDmapLutULog2P;
+    constexpr int kN = SIGNED ? kDmapLutN : kDmapLutUN;
+    const int b = min(max((int)(ab >> (23 - kLog2P)) - (kDmapLutExpLo << kLog2P), 0), kN);
     if (SIGNED) {
         const uint32_t neg = (uint32_t)((int32_t)bits >> 31);  // all ones for x < 0
         const uint2 e = lut[b + (neg & (uint32_t)kDmapLutEntries)];
-        if (e.y > 0xffu) return dmap_encode_rare(map, xn);
+        flags |= e.y;
         return e.y + ((ab ^ neg) >= e.x ? 1u : 0u);
     } else {
         const uint2 e = lut[b];
-        if ((e.y | ((bits >> 31) << 8)) > 0xffu) return dmap_encode_rare(map, xn);
+        flags |= e.y | ((bits >> 31) << 8);
         return e.y + (ab >= e.x ? 1u : 0u);
     }
+}
+
+// The same with the search taken for a flagged element: dmap_encode(map, xn)
+// for every xn (`map` is the sorted map).
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t dmap_encode_lut(const uint2* __restrict__ lut, const float* __restrict__ map,
+                                                    float xn) {
+    uint32_t flags = 0;
+    const uint32_t code = dmap_encode_lut_flag<SIGNED>(lut, xn, flags);
+    if (flags > 0xffu) return dmap_encode_rare(map, xn);
+    return code;
 }
 
 // Every float bit pattern through dmap_encode_lut and dmap_encode; counts
@@ -178,7 +200,8 @@ __global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restr
     __shared__ float map[256];
     __shared__ uint2 lut[2 * kDmapLutEntries];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) map[i] = is_signed ? c_dmap_signed[i] : c_dmap_unsigned[i];
-    for (int i = threadIdx.x; i < (is_signed ? 2 : 1) * kDmapLutEntries; i += blockDim.x)
+    static_assert(kDmapLutUEntries <= 2 * kDmapLutEntries, "the unsigned table must fit the signed one's space");
+    for (int i = threadIdx.x; i < (is_signed ? 2 * kDmapLutEntries : kDmapLutUEntries); i += blockDim.x)
         lut[i] = is_signed ? g_dmap_lut_s[i] : g_dmap_lut_u[i];
     __syncthreads();
     unsigned long long bad = 0;

@@ -121,6 +121,24 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
+// Three-input min / max of sm_100 (one instruction each).  fmax3 ignores a
+// NaN operand; fmax3_nan returns NaN when any operand is NaN.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // Packed f32x2 arithmetic of sm_100 (two lanes per instruction); each lane
 // rounds exactly as the scalar __fmul_rn / __fadd_rn / __fmaf_rn does.
 // Caution, measured on sm_100a with this toolchain: ptxas contracts a packed

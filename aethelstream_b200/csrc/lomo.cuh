@@ -173,12 +173,19 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
         } else {
             const float dinv = dyn_inv(bm);
             const float2 dinv2 = make_float2(dinv, dinv);
+            uint32_t ef = 0;
 #pragma unroll
             for (int k = 0; k < 16; k += 2) {
-                const float2 xn = mul2_rn(make_float2(mo[k], mo[k + 1]), dinv2);
-                out[k >> 2] |= (dmap_encode_lut<true>(tab.dlut, tab.dm, xn.x) |
-                                (dmap_encode_lut<true>(tab.dlut, tab.dm, xn.y) << 8))
+                const float2 x2 = mul2_rn(make_float2(mo[k], mo[k + 1]), dinv2);
+                out[k >> 2] |= (dmap_encode_lut_flag<true>(tab.dlut, x2.x, ef) |
+                                (dmap_encode_lut_flag<true>(tab.dlut, x2.y, ef) << 8))
                                << (8 * (k & 3));
+            }
+            if (ef > 0xffu) {  // rare: a bucket that needs the search; redo this thread's 16 codes
+                out[0] = out[1] = out[2] = out[3] = 0u;
+#pragma unroll
+                for (int k = 0; k < 16; ++k)  // the same normalised values, formed again
+                    out[k >> 2] |= dmap_encode_rare(tab.dm, __fmul_rn(mo[k], dinv)) << (8 * (k & 3));
             }
             if (threadIdx.x == 0) mom_scales[b] = bm;
         }

@@ -187,23 +187,6 @@ __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int n
     for (int b = tid; b < 32; b += nthreads) t->bucket32[b] = nf4_bucket32_entry(b);
 }
 
-// Three-input min / max of sm_100 (one instruction each).  fmax3 ignores a
-// NaN operand; fmax3_nan returns NaN when any operand is NaN.
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-    float r;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
-__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
-    float r;
-    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
-__device__ __forceinline__ float fmin3(float a, float b, float c) {
-    float r;
-    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
 
 // Exact decisions for 8 elements (rare path; kept out of line).
 __device__ __noinline__ uint32_t nf4_exact_word8(float a0, float a1, float a2, float a3, float a4, float a5, float a6,
