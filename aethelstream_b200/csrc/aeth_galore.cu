@@ -1852,11 +1852,21 @@ int aeth_lomo_update(const void* grad_bf16, int64_t n, const double* sq_dev, flo
     const uint16_t* gb = static_cast<const uint16_t*>(grad_bf16);
     auto kern = codec == AETH_CODEC_BLOCK_DYNAMIC ? lomo_update_kernel<AETH_CODEC_BLOCK_DYNAMIC>
                                                   : lomo_update_kernel<AETH_CODEC_BLOCK_LINEAR>;
+    static bool attr_set[2][kMaxDevices] = {};
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    const int ci = codec == AETH_CODEC_BLOCK_DYNAMIC ? 1 : 0;
+    if (!attr_set[ci][dev]) {
+        AETH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kLomoSmem));
+        attr_set[ci][dev] = true;
+    }
     int per_sm = 0;
-    AETH_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, 0));
-    const int grid = (int)std::min<int64_t>(nb, (int64_t)num_sms() * std::max(per_sm, 1));
-    kern<<<grid, 128, 0, to_stream(stream)>>>(gb, n, sq_dev, max_norm, lr, beta, mom8, mom_scales, w_packed, w_absmax,
-                                              prequant_out);
+    AETH_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kLomoThreads, kLomoSmem));
+    // each CTA runs kLomoGroups independent 128-thread groups, one block each at a time
+    const int grid = (int)std::min<int64_t>((nb + kLomoGroups - 1) / kLomoGroups,
+                                            (int64_t)num_sms() * std::max(per_sm, 1));
+    kern<<<grid, kLomoThreads, kLomoSmem, to_stream(stream)>>>(gb, n, sq_dev, max_norm, lr, beta, mom8, mom_scales,
+                                                               w_packed, w_absmax, prequant_out);
     AETH_LAUNCH_CHECK();
     return AETH_OK;
 }

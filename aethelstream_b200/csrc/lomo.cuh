@@ -42,54 +42,72 @@ __global__ void __launch_bounds__(256) lomo_sqnorm_kernel(const uint16_t* __rest
     }
 }
 
-// Shared tables of the update kernel: the NF4 byte table (dequant), the
-// 29-bucket classifier of the fused apply epilogue (requant), and for the
-// dynamic codec the signed map and its bucket table.
+// Shared tables of the update kernel.  rep: 256 entries of 256 bytes; entry b
+// holds the NF4 byte table's pair (CODES[b >> 4], CODES[b & 15]) in 16 copies
+// at 8 c (c = lane % 16) and, for the dynamic codec, map entry b in 32 copies
+// at 128 + 4 lane -- so one byte permute forms either offset from the packed
+// code word and the lane (nf4_dequant_word_s), and no lookup of a warp meets a
+// bank conflict whatever the codes.  bucket32: the 29-bucket classifier of the
+// fused apply epilogue (requant); dm and dlut: the signed map and its bucket
+// table (dm only for the rare binary search).
+constexpr int kLomoGroups = 5;  // independent 128-thread groups per CTA
+constexpr int kLomoThreads = 128 * kLomoGroups;
 struct LomoTables {
-    float2 byte_lut[256];
+    uint8_t rep[256 * 256];
     uint32_t bucket32[32];
-    uint32_t pad_[4];  // keeps dlut 16-byte aligned
     float dm[256];
     uint2 dlut[2 * kDmapLutEntries];
 };
+constexpr int kLomoSmem = (int)sizeof(LomoTables);
 
-// One CTA of 128 threads per momentum block of 2048 elements and iteration;
-// thread t owns 16 consecutive elements, so 4 consecutive threads form one
-// NF4 block of 64 and each warp a quarter of the momentum block.  The next
-// block's gradient, momentum and weight words are loaded while the current
-// one is processed.  Element pairs go through the packed f32x2 multiply;
-// sums that must round twice add with scalar adds (a packed add of fresh
-// products would be fused).
+// A CTA is kLomoGroups independent groups of 128 threads that share one copy
+// of the tables.  A group takes one momentum block of 2048 elements per
+// iteration and synchronises on its own named barrier; thread t of the group
+// owns 16 consecutive elements, so 4 consecutive threads form one NF4 block of
+// 64 and each warp a quarter of the momentum block.  The next block's
+// gradient, momentum and weight words are loaded while the current one is
+// processed.  Element pairs go through the packed f32x2 multiply; sums that
+// must round twice add with scalar adds (a packed add of fresh products would
+// be fused).
 template <int CODEC>
-__global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __restrict__ g, int64_t n,
-                                                          const double* __restrict__ sq, float max_norm, float lr,
-                                                          float beta, int8_t* __restrict__ mom8,
-                                                          float* __restrict__ mom_scales, uint8_t* __restrict__ wp,
-                                                          float* __restrict__ wa, float* __restrict__ prequant) {
-    __shared__ LomoTables tab;
-    __shared__ float red[2][4];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x)
-        tab.byte_lut[i] = make_float2(c_nf4_codes[i >> 4], c_nf4_codes[i & 15]);
-    for (int b = threadIdx.x; b < 32; b += blockDim.x) tab.bucket32[b] = nf4_bucket32_entry(b);
+__global__ void __launch_bounds__(kLomoThreads, 1)
+    lomo_update_kernel(const uint16_t* __restrict__ g, int64_t n, const double* __restrict__ sq, float max_norm,
+                       float lr, float beta, int8_t* __restrict__ mom8, float* __restrict__ mom_scales,
+                       uint8_t* __restrict__ wp, float* __restrict__ wa, float* __restrict__ prequant) {
+    extern __shared__ __align__(16) uint8_t lomo_smem[];
+    LomoTables& tab = *reinterpret_cast<LomoTables*>(lomo_smem);
+    __shared__ float red[kLomoGroups][2][4];
+    for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
+        const int b = i >> 4;
+        *reinterpret_cast<float2*>(tab.rep + b * 256 + (i & 15) * 8) =
+            make_float2(c_nf4_codes[b >> 4], c_nf4_codes[b & 15]);
+    }
     if (CODEC == AETH_CODEC_BLOCK_DYNAMIC) {
+        for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x)
+            *reinterpret_cast<float*>(tab.rep + (i >> 5) * 256 + 128 + (i & 31) * 4) = c_dmap_signed[i >> 5];
         for (int i = threadIdx.x; i < 256; i += blockDim.x) tab.dm[i] = c_dmap_signed[i];
         for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) tab.dlut[i] = g_dmap_lut_s[i];
     }
+    for (int b = threadIdx.x; b < 32; b += blockDim.x) tab.bucket32[b] = nf4_bucket32_entry(b);
     __syncthreads();
+    const int group = threadIdx.x >> 7, tid = threadIdx.x & 127;
+    const int lane = tid & 31, warp = tid >> 5;
     const uint32_t bucket_bias = smem_u32_addr(tab.bucket32) - (0x4B400000u << 2);
-    const uint32_t bucket_lane = tab.bucket32[threadIdx.x & 31];
+    const uint32_t bucket_lane = tab.bucket32[lane];
+    const uint32_t rep_base = smem_u32_addr(tab.rep);
+    const uint32_t byte_lane = (uint32_t)(lane & 15) * 8u, map_lane = 128u + (uint32_t)lane * 4u;
     const double gnorm = sqrt(*sq);
     float clip = (float)((double)max_norm / (gnorm + 1e-6));
     clip = clip < 1.0f ? clip : 1.0f;
     const float2 clip2 = make_float2(clip, clip), beta2 = make_float2(beta, beta), nlr2 = make_float2(-lr, -lr);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t n_blocks = n / 2048;
-    int64_t b = blockIdx.x;
+    const int64_t vgrid = (int64_t)gridDim.x * kLomoGroups;
+    int64_t b = (int64_t)blockIdx.x * kLomoGroups + group;
     uint4 g0 = make_uint4(0u, 0u, 0u, 0u), g1 = g0, mq = g0;
     uint2 wq = make_uint2(0u, 0u);
     float ms = 0.0f, wamax = 0.0f;
     auto fetch = [&](int64_t blk) {
-        const int64_t e = blk * 2048 + threadIdx.x * 16;
+        const int64_t e = blk * 2048 + tid * 16;
         g0 = __ldcs(reinterpret_cast<const uint4*>(g + e));
         g1 = __ldcs(reinterpret_cast<const uint4*>(g + e + 8));
         mq = *reinterpret_cast<const uint4*>(mom8 + e);
@@ -98,16 +116,16 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
         ms = mom_scales[blk];
     };
     if (b < n_blocks) fetch(b);
-    for (int it = 0; b < n_blocks; b += gridDim.x, ++it) {
-        const int64_t e0 = b * 2048 + threadIdx.x * 16;
+    for (int it = 0; b < n_blocks; b += vgrid, ++it) {
+        const int64_t e0 = b * 2048 + tid * 16;
         float w[16], mo[16];
         // NF4 dequant (byte table), gradient, momentum decode
-        nf4_dequant_word(wq.x, wamax, tab.byte_lut, w);
-        nf4_dequant_word(wq.y, wamax, tab.byte_lut, w + 8);
+        nf4_dequant_word_s(wq.x, wamax, rep_base, byte_lane, w);
+        nf4_dequant_word_s(wq.y, wamax, rep_base, byte_lane, w + 8);
         const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         const uint32_t mw[4] = {mq.x, mq.y, mq.z, mq.w};
         const float cur_ms = ms;
-        if (b + gridDim.x < n_blocks) fetch(b + gridDim.x);
+        if (b + vgrid < n_blocks) fetch(b + vgrid);
         const float2 ms2 = make_float2(cur_ms, cur_ms);
         float am = 0.0f, aw = 0.0f;
 #pragma unroll
@@ -117,10 +135,18 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
             const uint32_t mword = mw[k >> 2];
             const int sh = 8 * (k & 3);
             float2 m0;
-            if (CODEC == AETH_CODEC_BLOCK_DYNAMIC)
-                m0 = make_float2(tab.dm[(mword >> sh) & 0xffu], tab.dm[(mword >> (sh + 8)) & 0xffu]);
-            else
+            if (CODEC == AETH_CODEC_BLOCK_DYNAMIC) {
+                // map entries of code bytes k % 4 and k % 4 + 1 of the word, this lane's copy
+                const uint32_t kb = (uint32_t)(k & 3);
+                float m_lo, m_hi;
+                asm("ld.shared.f32 %0, [%1];" : "=f"(m_lo) : "r"(rep_base + prmt(mword, map_lane, 0x5504u | (kb << 4))));
+                asm("ld.shared.f32 %0, [%1];"
+                    : "=f"(m_hi)
+                    : "r"(rep_base + prmt(mword, map_lane, 0x5504u | ((kb + 1u) << 4))));
+                m0 = make_float2(m_lo, m_hi);
+            } else {
                 m0 = make_float2((float)(int8_t)(mword >> sh), (float)(int8_t)(mword >> (sh + 8)));
+            }
             m0 = mul2_rn(m0, ms2);
             // m = fl(fl(beta m) + g clip); w = fl(w - fl(lr m))
             const float2 mm = add2_sep(mul2_rn(beta2, m0), gg);
@@ -153,23 +179,24 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
             }
         }
         *reinterpret_cast<uint2*>(wp + e0 / 2) = make_uint2(pk0, pk1);
-        if ((threadIdx.x & 3) == 0) wa[e0 / 64] = nf4_store_amax(aw);
+        if ((tid & 3) == 0) wa[e0 / 64] = nf4_store_amax(aw);
         if (prequant) {
 #pragma unroll
             for (int k = 0; k < 16; k += 4)
                 *reinterpret_cast<float4*>(prequant + e0 + k) = make_float4(w[k], w[k + 1], w[k + 2], w[k + 3]);
         }
-        // momentum block absmax over the CTA (double-buffered slots: one barrier per block)
+        // momentum block absmax over the group (double-buffered slots: one barrier per block)
         am = warp_max(am);
-        if (lane == 0) red[it & 1][warp] = am;
-        __syncthreads();
-        const float bm = fmax3(fmaxf(red[it & 1][0], red[it & 1][1]), red[it & 1][2], red[it & 1][3]);
+        float* rs = red[group][it & 1];
+        if (lane == 0) rs[warp] = am;
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + group) : "memory");
+        const float bm = fmax3(fmaxf(rs[0], rs[1]), rs[2], rs[3]);
         uint32_t out[4] = {0u, 0u, 0u, 0u};
         if (CODEC == AETH_CODEC_BLOCK_LINEAR) {
             const float nsm = lin_scale_from_absmax(bm), linv = lin_inv(nsm);
 #pragma unroll
             for (int k = 0; k < 16; ++k) out[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(mo[k], linv)) << (8 * (k & 3));
-            if (threadIdx.x == 0) mom_scales[b] = nsm;
+            if (tid == 0) mom_scales[b] = nsm;
         } else {
             const float dinv = dyn_inv(bm);
             const float2 dinv2 = make_float2(dinv, dinv);
@@ -187,7 +214,7 @@ __global__ void __launch_bounds__(128) lomo_update_kernel(const uint16_t* __rest
                 for (int k = 0; k < 16; ++k)  // the same normalised values, formed again
                     out[k >> 2] |= dmap_encode_rare(tab.dm, __fmul_rn(mo[k], dinv)) << (8 * (k & 3));
             }
-            if (threadIdx.x == 0) mom_scales[b] = bm;
+            if (tid == 0) mom_scales[b] = bm;
         }
         *reinterpret_cast<uint4*>(mom8 + e0) = make_uint4(out[0], out[1], out[2], out[3]);
     }
