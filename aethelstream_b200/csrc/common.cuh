@@ -121,6 +121,16 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
+__device__ __forceinline__ uint32_t smem_u32_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// prmt.b32 in its default mode: a selector nibble with bit 3 set fills the
+// output byte with the sign of the selected byte.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
 // Three-input min / max of sm_100 (one instruction each).  fmax3 ignores a
 // NaN operand; fmax3_nan returns NaN when any operand is NaN.
 __device__ __forceinline__ float fmax3(float a, float b, float c) {

@@ -43,8 +43,6 @@ __device__ __forceinline__ float nf4_store_amax(float amax) {
     return amax != amax ? __uint_as_float(0x7fc00000u) : amax;
 }
 
-__device__ __forceinline__ uint32_t smem_u32_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
 struct Nf4Tables {
     float2 byte_lut[256];  // (CODES[byte >> 4], CODES[byte & 15])
     // {midpoint threshold or +inf, lower code index as int bits}; entries 33..63
@@ -237,13 +235,6 @@ __device__ __forceinline__ uint32_t nf4_bucket_bias(const Nf4Tables32* t) {
     return smem_u32_addr(t->bucket32) - (0x4B400000u << 2);
 }
 
-// prmt.b32 in its default mode: a selector nibble with bit 3 set fills the
-// output byte with the sign of the selected byte.
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
 
 // 8 values -> one packed word, two elements per step through the packed
 // f32x2 instructions.  Byte k of the word = code[2k] << 4 | code[2k+1].  The
