@@ -257,7 +257,7 @@ def run_reference(args):
                                               "INT8, NF4 dequant + fp32 apply)", "parallelism": "host threads"},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -326,13 +326,14 @@ def run_lomo(args):
         for s in range(args.warmup):
             step(s)
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
         big = n == CONFIGS["c5"]["lomo_sizes"][-1]
         clocks = ClockSampler(local) if big else None
         if clocks:
             clocks.start()
             time.sleep(0.3)
+        if world > 1:  # after the sampler start: the ranks enter the timed steps together
+            dist.barrier()
+        torch.cuda.synchronize()
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
         mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         marks[0].record(stream)
@@ -450,7 +451,7 @@ def run_lomo(args):
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
                                     "sample": f"oracle LOMO step (norm + update), {n_s} elements x {k} steps, single "
                                               f"thread, {dt:.1f} s"}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -470,7 +471,7 @@ def run_lomo_reference(args):
                        "parallelism": "one host thread"},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -562,12 +563,15 @@ def run_b200(args):
         else:
             step(s)
 
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)  # let the sampler start
+    # the barrier comes after each rank's sampler start, so the ranks enter the
+    # timed steps together (a rank that starts late holds the others at their
+    # first clip exchange, which would count in their time)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -701,14 +705,29 @@ def run_b200(args):
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
                                     "sample": "reference CPU algorithm (oracle port), 1/128 of each matrix's output "
                                               f"rows over the {len(SHAPES)} matrices of the block, single thread, {dt:.1f} s"}
-        print(json.dumps(line), flush=True)
+        emit(line)
     opt.close()
     if world > 1:
         dist.destroy_process_group()
     return 0
 
 
+_JSON_FD = None
+
+
+def emit(line):
+    """Writes the one JSON result line to the process's original stdout."""
+    os.write(_JSON_FD if _JSON_FD is not None else 1, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    global _JSON_FD
+    # Everything else that reaches file descriptor 1 -- Python prints and
+    # library banners written from C (NCCL's version line under torchrun) --
+    # goes to stderr; stdout carries only the JSON line.
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
