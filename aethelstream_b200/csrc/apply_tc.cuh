@@ -225,17 +225,20 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 float amax = 0.0f;
                 float vb[2][16];
                 tmem_ld16<0>(tcol, vb[0]);
+                // the block's 32 packed bytes as two 16-byte chunks (whole-chunk accesses:
+                // the swizzle spreads 8 consecutive rows over all 32 banks)
+                const uint4 q01 = *reinterpret_cast<const uint4*>(rowp + ((ck ^ (row & 7)) * 16));
+                const uint4 q23 = *reinterpret_cast<const uint4*>(rowp + (((ck + 1) ^ (row & 7)) * 16));
                 tmem_wait_ld_bind(vb[0]);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (c < 3) tmem_ld16<0>(tcol + (uint32_t)((c + 1) * 16), vb[(c + 1) & 1]);
                     float* v = vb[c & 1];
                     float w[16];
-                    // words 2c, 2c+1 of the block: 8 adjacent bytes of chunk ck + c/2
-                    const uint2 qq =
-                        *reinterpret_cast<const uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8);
-                    nf4_dequant_word_s(qq.x, amax_old, rep_base, rep_lane, w);
-                    nf4_dequant_word_s(qq.y, amax_old, rep_base, rep_lane, w + 8);
+                    // words 2c, 2c+1 of the block
+                    const uint4 qa = c < 2 ? q01 : q23;
+                    nf4_dequant_word_s((c & 1) ? qa.z : qa.x, amax_old, rep_base, rep_lane, w);
+                    nf4_dequant_word_s((c & 1) ? qa.w : qa.y, amax_old, rep_base, rep_lane, w + 8);
                     // w <- fl(w - lr * dW), one fused multiply-add per element (paired),
                     // then the decoupled decay.  The reference rounds lr * dW first; the
                     // two differ by under half an ulp of the product, inside the update's
@@ -271,6 +274,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 const bool bad = !(amax <= 3.402823466e38f);
                 const float inv = __frcp_rn(nf4_safe(amax));
                 float mw[8];  // per packed word: the smallest distance to a threshold (0: exact path)
+                uint32_t pw[8];
                 float wbuf[2][16];
                 tmem_ld16<0>(tcol, wbuf[0]);
                 tmem_wait_ld_bind(wbuf[0]);
@@ -280,11 +284,12 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     // all lanes classify (the entries come by shuffle); a non-finite
                     // block's words are rewritten on the exact path below
                     mw[2 * c] = mw[2 * c + 1] = 1.0f;
-                    const uint32_t lo = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_lane, mw[2 * c]);
-                    const uint32_t hi = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_lane, mw[2 * c + 1]);
+                    pw[2 * c] = nf4_fast_word8_s(wbuf[c & 1], inv, bucket_lane, mw[2 * c]);
+                    pw[2 * c + 1] = nf4_fast_word8_s(wbuf[c & 1] + 8, inv, bucket_lane, mw[2 * c + 1]);
                     if (bad) mw[2 * c] = mw[2 * c + 1] = 0.0f;
-                    *reinterpret_cast<uint2*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16) + (c & 1) * 8) =
-                        make_uint2(lo, hi);
+                    if (c & 1)  // a whole 16-byte chunk: words 2c-2 .. 2c+1
+                        *reinterpret_cast<uint4*>(rowp + (((ck + (c >> 1)) ^ (row & 7)) * 16)) =
+                            make_uint4(pw[2 * c - 2], pw[2 * c - 1], pw[2 * c], pw[2 * c + 1]);
                     if (c < 3) tmem_wait_ld_bind(wbuf[(c + 1) & 1]);
                 }
                 const float mind = fmin3(fmin3(mw[0], mw[1], mw[2]), fmin3(mw[3], mw[4], mw[5]), fminf(mw[6], mw[7]));
