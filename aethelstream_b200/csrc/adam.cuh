@@ -378,8 +378,8 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
             }
             *reinterpret_cast<uint4*>(a.nout[p] + e0) = make_uint4(nb[0], nb[1], nb[2], nb[3]);
         }
-        am = warp_max(am);
-        av = warp_max(av);
+        am = warp_max_nonneg(am);  // fmax3 from 0 ignores NaN: am, av >= 0 and not NaN
+        av = warp_max_nonneg(av);
         if (lane == 0) { red_m[half][par][warp] = am; red_v[half][par][warp] = av; }
         // this half's 256 threads; the slots of this parity are rewritten two blocks later
         if (half)  // constant barrier ids (warp-uniform branch)

@@ -115,6 +115,12 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Warp maximum of values that are >= 0 and not NaN (+inf allowed): their bit
+// patterns order like unsigned integers, so one redux.sync does it.
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
+}
+
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kLomoThreads, 1)
                 *reinterpret_cast<float4*>(prequant + e0 + k) = make_float4(w[k], w[k + 1], w[k + 2], w[k + 3]);
         }
         // momentum block absmax over the group (double-buffered slots: one barrier per block)
-        am = warp_max(am);
+        am = warp_max_nonneg(am);  // fmax3 from 0 ignores NaN: am >= 0 and not NaN
         float* rs = red[group][it & 1];
         if (lane == 0) rs[warp] = am;
         asm volatile("bar.sync %0, 128;" ::"r"(1 + group) : "memory");
