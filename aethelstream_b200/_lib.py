@@ -10,7 +10,7 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.environ.get("AETH_GALORE_LIB", os.path.join(HERE, "libaeth_galore.so"))
+LIB_PATH = os.path.join(HERE, "libaeth_galore.so")
 
 AETH_OK = 0
 AETH_ERR_ARG = -1
@@ -39,7 +39,7 @@ class GaloreConfig(C.Structure):
         ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float), ("lr", C.c_float),
         ("weight_decay", C.c_float), ("scale_lr_by_rank", C.c_int), ("max_grad_norm", C.c_float),
         ("state_codec", C.c_int), ("state_block", C.c_int), ("init_projectors", C.c_int),
-        ("svd_refresh", C.c_int), ("power_iters", C.c_int),
+        ("svd_refresh", C.c_int), ("power_iters", C.c_int), ("grad_dtype", C.c_int),
     ]
 
 
@@ -92,6 +92,8 @@ SIGNATURES = {
     "aeth_galore_step_count": (_u64, [_vp]),
     "aeth_galore_step": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(_vp), _i, C.POINTER(WeightRef), SQ_HOOK, _vp, _vp,
                               _vp]),
+    "aeth_galore_project_layer": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(_vp), _i, _vp]),
+    "aeth_galore_finish_step": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(WeightRef), SQ_HOOK, _vp, _vp, _vp]),
     "aeth_galore_set_phase_timing": (_i, [_vp, _i]),
     "aeth_galore_phase_times": (_i, [_vp, C.POINTER(_d), C.POINTER(_i)]),
     "aeth_galore_clip_handle": (_i, [_vp, _i, _vp]),

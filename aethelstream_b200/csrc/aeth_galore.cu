@@ -132,6 +132,59 @@ __global__ void to_bf16_kernel(const void* __restrict__ x, int dtype, int64_t n,
         y[i] = f32_to_bf16_bits(load_as_f32(x, i, dtype));
 }
 
+// Exact bf16 split of an fp32 or f16 gradient for the tensor-core projection:
+// x = hi + lo (+ lo2), each term bf16 (RNE of the remainder so far), so the
+// terms hold all 24 (fp32) or 11 (f16) significant bits and their products
+// with the bf16 projector are exact.  The terms are stacked along the
+// contraction dimension -- right side (m >= n, contraction over columns):
+// row i of the output is [hi(i, :) | lo(i, :) | lo2(i, :)] (m x nsplit*n);
+// left side (contraction over rows): the m x n blocks hi, lo, lo2 one below
+// the other (nsplit*m x n) -- so one projection with the contraction
+// nsplit times longer, against the projector repeated nsplit times, adds the
+// terms' contributions.  A non-finite x keeps only hi (inf / NaN as in the
+// bf16 path).  Eight elements per thread, 16-byte stores.
+__global__ void grad_split_kernel(const void* __restrict__ g, int dtype, int64_t m, int64_t n, int nsplit, int right,
+                                  uint16_t* __restrict__ out) {
+    const int64_t total8 = m * n / 8;
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total8; v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e0 = v * 8;
+        float x[8];
+        if (dtype == AETH_DTYPE_F32) {
+            const float4 a = reinterpret_cast<const float4*>(g)[2 * v];
+            const float4 b = reinterpret_cast<const float4*>(g)[2 * v + 1];
+            x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        } else {
+            const uint4 a = reinterpret_cast<const uint4*>(g)[v];
+            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                x[2 * k] = __half2float(__ushort_as_half((unsigned short)(w[k] & 0xffffu)));
+                x[2 * k + 1] = __half2float(__ushort_as_half((unsigned short)(w[k] >> 16)));
+            }
+        }
+        const int64_t i = e0 / n, j = e0 % n;  // n % 8 == 0: the 8 elements share a row
+#pragma unroll 1
+        for (int t = 0; t < nsplit; ++t) {
+            uint32_t packed[4];
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                uint16_t b[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float r = x[k + h];
+                    const uint16_t q = f32_to_bf16_bits(r);
+                    const bool finite = fabsf(r) <= 3.402823466e38f;
+                    b[h] = (t == 0 || finite) ? q : (uint16_t)0;
+                    x[k + h] = finite ? __fsub_rn(r, bf16_bits_to_f32(q)) : 0.0f;  // exact remainder
+                }
+                packed[k / 2] = (uint32_t)b[0] | ((uint32_t)b[1] << 16);
+            }
+            const int64_t o = right ? (i * nsplit + t) * n + j : ((int64_t)t * m + i) * n + j;
+            *reinterpret_cast<uint4*>(out + o) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
+    }
+}
+
 __global__ void fill_f32_kernel(float* __restrict__ x, int64_t n, float v) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) x[i] = v;
 }
@@ -219,7 +272,10 @@ struct Param {
     uint16_t* proj = nullptr;
     uint16_t* projT = nullptr;
     uint16_t* nbuf = nullptr;
-    uint16_t* gbf = nullptr;  // bf16 copy of a non-bf16 gradient (lazy)
+    // fp32 / f16 gradients: projT repeated ksplit times along the contraction
+    // (r x ksplit*s), matching the stacked bf16 terms of grad_split_kernel
+    uint16_t* projTk = nullptr;
+    int ksplit = 0;
     // subspace refresh: full gradient captured at refresh steps (m x n f32, lazy)
     float* capture = nullptr;
     bool captured = false;
@@ -239,47 +295,67 @@ struct aeth_galore_ctx {
     unsigned int* work = nullptr;       // b2_adam_group_kernel's block counters, zero between launches
     uint64_t* clip_epoch = nullptr;     // clip group's exchange counter (device; zeroed on joining)
     uint64_t version = 0;               // completed subspace refreshes (optimizer_version)
+    // stacked bf16 terms of one fp32 / f16 gradient (grad_split_kernel), shared
+    // by the parameters: their projections run one after another on the stream
+    uint16_t* gsplit = nullptr;
+    int64_t gsplit_elems = 0;
     // global clip over several GPUs through peer memory (aeth_galore_set_clip_group)
     ClipGroup group;
     PeerSlot* own_slots = nullptr;      // 2 x world entries, cudaMalloc'd (exported by IPC handle)
     int own_slots_world = 0;
     std::vector<void*> peer_maps;       // IPC mappings of the other ranks' slots
     std::vector<void*> allocs;
-    // aeth_galore_set_phase_timing: five events per step (phase boundaries)
+    // aeth_galore_set_phase_timing: events at the phase boundaries of every
+    // step, projection and finishing call
     bool phase_timing = false;
-    std::vector<std::array<cudaEvent_t, 5>> phase_pending, phase_pool;
+    struct PhaseRecord {
+        std::vector<cudaEvent_t> ev;  // boundaries; interval k belongs to phase[k]
+        std::vector<int> phase;
+        int steps = 0;                // 1 for a call that ends a step
+    };
+    std::vector<PhaseRecord> phase_pending;
+    std::vector<cudaEvent_t> event_pool;
 };
 
 namespace {
 
-// Phase-boundary events of one aeth_galore_step; the set goes back to the
-// pool unless the step finished and committed it.
+// Phase-boundary events of one call (aeth_galore_step, project_layer or
+// finish_step); the events go back to the pool unless the call finished and
+// committed them.
 struct PhaseMarks {
     aeth_galore_ctx* c = nullptr;
-    std::array<cudaEvent_t, 5> ev{};
+    aeth_galore_ctx::PhaseRecord rec;
     bool committed = false;
     int begin(aeth_galore_ctx* ctx) {
-        if (!ctx->phase_timing) return AETH_OK;
-        if (ctx->phase_pool.empty()) {
-            std::array<cudaEvent_t, 5> e{};
-            for (cudaEvent_t& x : e) AETH_CUDA(cudaEventCreate(&x));
-            ctx->phase_pool.push_back(e);
+        if (ctx->phase_timing) c = ctx;
+        return AETH_OK;
+    }
+    // A boundary; the interval that it closes (if any) counts for `phase`,
+    // the one it opens for the phase given to the next mark.
+    int mark(cudaStream_t st, int phase_after) {
+        if (!c) return AETH_OK;
+        cudaEvent_t e = nullptr;
+        if (c->event_pool.empty()) {
+            AETH_CUDA(cudaEventCreate(&e));
+        } else {
+            e = c->event_pool.back();
+            c->event_pool.pop_back();
         }
-        ev = ctx->phase_pool.back();
-        ctx->phase_pool.pop_back();
-        c = ctx;
+        rec.ev.push_back(e);
+        rec.phase.push_back(phase_after);
+        AETH_CUDA(cudaEventRecord(e, st));
         return AETH_OK;
     }
-    int mark(int k, cudaStream_t st) {
-        if (c) AETH_CUDA(cudaEventRecord(ev[k], st));
-        return AETH_OK;
-    }
-    void commit() {
-        if (c) c->phase_pending.push_back(ev);
+    void commit(int steps) {
+        if (c) {
+            rec.steps = steps;
+            c->phase_pending.push_back(std::move(rec));
+        }
         committed = true;
     }
     ~PhaseMarks() {
-        if (c && !committed) c->phase_pool.push_back(ev);
+        if (c && !committed)
+            for (cudaEvent_t e : rec.ev) c->event_pool.push_back(e);
     }
 };
 
@@ -302,6 +378,14 @@ int ctx_alloc(aeth_galore_ctx* c, T** p, int64_t count) {
     c->allocs.push_back(v);
     *p = static_cast<T*>(v);
     return AETH_OK;
+}
+
+// Frees a buffer that ctx_alloc made.
+void ctx_free(aeth_galore_ctx* c, void* p) {
+    if (!p) return;
+    auto it = std::find(c->allocs.begin(), c->allocs.end(), p);
+    if (it != c->allocs.end()) c->allocs.erase(it);
+    cudaFree(p);
 }
 
 int reset_state(aeth_galore_ctx* c, Param& p, cudaStream_t st) {
@@ -375,36 +459,93 @@ int ref_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, c
 }
 
 // ---- B200 mode ------------------------------------------------------------
-// bf16 view of a gradient: f32 / f16 gradients are rounded to bf16 (RNE) into
-// the parameter's buffer, allocated on the first such call.
-int b2_grad_bf16(Param& p, const void* grad, int dtype, cudaStream_t st, const void** out) {
-    *out = grad;
-    if (dtype == AETH_DTYPE_BF16) return AETH_OK;
-    const int64_t mn = (int64_t)p.m * p.n;
-    if (!p.gbf) AETH_CUDA(cudaMalloc(&p.gbf, (size_t)mn * sizeof(uint16_t)));
-    to_bf16_kernel<<<grid_for(mn, 256), 256, 0, st>>>(grad, dtype, mn, p.gbf);
-    AETH_LAUNCH_CHECK();
-    *out = p.gbf;
+// Number of exact bf16 terms of a gradient dtype (fp32: 24 significant bits
+// in three terms of 8; f16: 11 bits in two).
+int grad_terms(int dtype) { return dtype == AETH_DTYPE_F32 ? 3 : dtype == AETH_DTYPE_F16 ? 2 : 1; }
+
+// projTk = projT repeated p.ksplit times along the contraction.
+int sync_projk(Param& p, cudaStream_t st) {
+    if (!p.projTk) return AETH_OK;
+    const size_t s = (size_t)(p.side == 1 ? p.m : p.n);
+    for (int t = 0; t < p.ksplit; ++t)
+        AETH_CUDA(cudaMemcpy2DAsync(p.projTk + t * s, (size_t)p.ksplit * s * 2, p.projT, s * 2, s * 2, (size_t)p.r,
+                                    cudaMemcpyDeviceToDevice, st));
     return AETH_OK;
 }
 
-// One-CTA-per-tile tcgen05 projection, for shapes the grouped kernel does not take.
-int b2_project_tile(Param& p, const void* grad, cudaStream_t st) {
-    const int m = p.m, n = p.n, r = p.r;
-    EpiAccum epi{p.accum, r};
-    if (p.side == 2) {
-        // R(m x r) += G Q : A = G (K-major, ld n), B(k,j) = Q[k][j] = projT[j*n + k] (K-major, ld n)
-        return tc_gemm<false, false>(TcOperand{grad, n}, TcOperand{p.projT, n}, m, r, n, true, epi, st);
+// Buffers of the split path for `terms` bf16 terms: allocated at create when
+// the configuration declares an fp32 / f16 gradient, else on first use
+// (never while the stream is being captured into a graph).
+int ensure_split(aeth_galore_ctx* c, Param& p, int terms, cudaStream_t st) {
+    const int64_t need = (int64_t)terms * p.m * p.n;
+    const bool have = p.projTk && p.ksplit >= terms && c->gsplit && c->gsplit_elems >= need;
+    if (have) return AETH_OK;
+    bool capturing = false;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    AETH_CUDA(cudaStreamIsCapturing(st, &cap));
+    capturing = cap != cudaStreamCaptureStatusNone;
+    if (capturing) return AETH_ERR_UNSUPPORTED;
+    AETH_CUDA(cudaStreamSynchronize(st));  // a smaller buffer may still be in use
+    if (!c->gsplit || c->gsplit_elems < need) {
+        ctx_free(c, c->gsplit);
+        c->gsplit = nullptr;
+        c->gsplit_elems = 0;
+        AETH_TRY(ctx_alloc(c, &c->gsplit, need));
+        c->gsplit_elems = need;
     }
-    // R^T(n x r) += G^T P : A(i,k) = G[k*n + i] (MN-major, ld n), B(k,j) = P[k][j] = projT[j*m + k] (K-major, ld m)
-    return tc_gemm<true, false>(TcOperand{grad, n}, TcOperand{p.projT, m}, n, r, m, true, epi, st);
+    if (!p.projTk || p.ksplit < terms) {
+        ctx_free(c, p.projTk);
+        p.projTk = nullptr;
+        p.ksplit = 0;
+        const int64_t s = p.side == 1 ? p.m : p.n;
+        AETH_TRY(ctx_alloc(c, &p.projTk, (int64_t)terms * s * p.r));
+        p.ksplit = terms;
+        AETH_TRY(sync_projk(p, st));
+    }
+    return AETH_OK;
 }
 
-int b2_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t st) {
-    AETH_TRY(b2_grad_bf16(p, grad, dtype, st, &grad));
-    ProjJob j{grad, p.projT, p.accum, p.m, p.n};
+// The projection job of one gradient: a bf16 gradient as it is; an fp32 or
+// f16 gradient as its exact bf16 terms stacked along the contraction
+// (grad_split_kernel), against the repeated projector.  No narrowing.
+int b2_grad_job(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, cudaStream_t st, ProjJob* job) {
+    *job = ProjJob{grad, p.projT, p.accum, p.m, p.n};
+    if (dtype == AETH_DTYPE_BF16) return AETH_OK;
+    if (dtype != AETH_DTYPE_F32 && dtype != AETH_DTYPE_F16) return AETH_ERR_ARG;
+    const int terms = grad_terms(dtype);
+    const int64_t mn = (int64_t)p.m * p.n;
+    if (p.n % 8 != 0) return AETH_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(grad) & 15) != 0) return AETH_ERR_UNSUPPORTED;
+    AETH_TRY(ensure_split(c, p, terms, st));
+    grad_split_kernel<<<grid_for(mn / 8, 256), 256, 0, st>>>(grad, dtype, p.m, p.n, terms, p.side == 2 ? 1 : 0,
+                                                           c->gsplit);
+    AETH_LAUNCH_CHECK();
+    // projTk holds p.ksplit >= terms copies; the first `terms` are read
+    *job = ProjJob{c->gsplit, p.projTk, p.accum, p.m, p.n};
+    job->ksplit = terms;
+    job->projk_ld = p.ksplit;
+    return AETH_OK;
+}
+
+// One-CTA-per-tile tcgen05 projection, for shapes the grouped kernel does not
+// take.  With k terms (the split path) the contraction is k times longer.
+int b2_project_tile(Param& p, const ProjJob& j, cudaStream_t st) {
+    const int m = p.m, n = p.n, r = p.r;
+    const int k = j.ksplit, kl = j.projk_ld;
+    EpiAccum epi{p.accum, r};
+    if (p.side == 2) {
+        // R(m x r) += G Q : A = G (K-major, ld k n), B(k,j) = Q[k][j] = projT[j*n + k] (K-major, ld kl n)
+        return tc_gemm<false, false>(TcOperand{j.grad, k * n}, TcOperand{j.projT, kl * n}, m, r, k * n, true, epi, st);
+    }
+    // R^T(n x r) += G^T P : A(i,k) = G[k*n + i] (MN-major, ld n), B(k,j) = P[k][j] = projT[j*m + k] (K-major, ld kl m)
+    return tc_gemm<true, false>(TcOperand{j.grad, n}, TcOperand{j.projT, kl * m}, n, r, k * m, true, epi, st);
+}
+
+int b2_project_accumulate(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, cudaStream_t st) {
+    ProjJob j;
+    AETH_TRY(b2_grad_job(c, p, grad, dtype, st, &j));
     int s = proj_grouped_launch(&j, 1, p.r, st);
-    return s == AETH_ERR_UNSUPPORTED ? b2_project_tile(p, grad, st) : s;
+    return s == AETH_ERR_UNSUPPORTED ? b2_project_tile(p, j, st) : s;
 }
 
 float b2_lr(const aeth_galore_config& cfg, int r) {
@@ -618,6 +759,7 @@ int refresh_param(aeth_galore_ctx* c, Param& p, uint64_t seed, cudaStream_t st) 
                                                                                      p.r, p.proj, p.projT);
             e = cudaGetLastError();
             if (e != cudaSuccess) status = (int)e;
+            if (status == AETH_OK) status = sync_projk(p, st);
         }
         if (status == AETH_OK) status = reset_state(c, p, st);
     }
@@ -776,7 +918,6 @@ struct NoAllocDevice {
     bool ready = false;
 };
 NoAllocDevice g_noalloc[kMaxDevices];
-std::mutex g_noalloc_mu;
 
 // Once per device, with that device current: device addresses of the static
 // arrays.  If the library's per-device runtime is not set up yet, its error
@@ -786,18 +927,20 @@ int noalloc_setup(void** temp) {
     int dev = 0;
     AETH_TRY(current_device(&dev));
     if (dev < 0 || dev >= kMaxDevices) return AETH_ERR_UNSUPPORTED;
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    // g_rt_mu also guards runtime_for_current's first use, so the error word
+    // is chosen exactly once per device whichever path comes first.
+    std::lock_guard<std::mutex> lock(g_rt_mu);
     NoAllocDevice& d = g_noalloc[dev];
     if (!d.ready) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_temp);
         if (e != cudaSuccess) return (int)e;
-        if (!g_rt[dev].init) {
+        if (!g_rt[dev].init.load(std::memory_order_relaxed)) {
             void* w = nullptr;
             e = cudaGetSymbolAddress(&w, g_noalloc_err_word);
             if (e != cudaSuccess) return (int)e;
             g_rt[dev].err_word = static_cast<uint32_t*>(w);
-            g_rt[dev].init = true;
+            g_rt[dev].init.store(true, std::memory_order_release);
         }
         d.temp = p;
         d.ready = true;
@@ -915,18 +1058,17 @@ void aeth_galore_config_default(aeth_galore_config* c) {
     c->init_projectors = 1;
     c->svd_refresh = 1;  // the reference captures at step 1 and every switch_interval steps
     c->power_iters = 0;  // RandomizedSvdConfig::default (randomized_svd.rs:19-28), never used by the reference
+    c->grad_dtype = AETH_DTYPE_BF16;
 }
 
 int aeth_galore_destroy(aeth_galore_ctx* ctx) {
     if (!ctx) return AETH_ERR_ARG;
     DeviceGuard g(ctx->device);
     cudaDeviceSynchronize();
-    for (auto* v : {&ctx->phase_pending, &ctx->phase_pool})
-        for (auto& evs : *v)
-            for (cudaEvent_t e : evs) cudaEventDestroy(e);
+    for (auto& rec : ctx->phase_pending)
+        for (cudaEvent_t e : rec.ev) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
     for (void* p : ctx->allocs) cudaFree(p);
-    for (Param& p : ctx->params)
-        if (p.gbf) cudaFree(p.gbf);
     for (Param& p : ctx->params)
         if (p.capture) cudaFree(p.capture);
     for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
@@ -944,6 +1086,8 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
     if (cfg->mode == AETH_MODE_B200 &&
         (cfg->state_codec == AETH_CODEC_PER_TENSOR || cfg->state_block <= 0))
         return set_err(AETH_ERR_CONFIG);
+    if (cfg->grad_dtype != AETH_DTYPE_F32 && cfg->grad_dtype != AETH_DTYPE_F16 && cfg->grad_dtype != AETH_DTYPE_BF16)
+        return set_err(AETH_ERR_CONFIG);
     DeviceGuard g(device);
     aeth_galore_ctx* c = new aeth_galore_ctx();
     c->cfg = *cfg;
@@ -955,6 +1099,7 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
     int st = AETH_OK;
     if ((st = codec_maps_ensure()) != AETH_OK) return fail(st);
     c->params.resize(n_specs);
+    int64_t split_need = 0;
     for (int i = 0; i < n_specs; ++i) {
         const aeth_param_spec& s = specs[i];
         if (s.m <= 0 || s.n <= 0) return fail(AETH_ERR_SHAPE);
@@ -1022,14 +1167,27 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
             if (cudaMemcpy(p.proj, b.data(), b.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
                 cudaMemcpy(p.projT, bt.data(), bt.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess)
                 return fail(AETH_ERR_CONFIG);
+            // a declared fp32 / f16 gradient: the split path's buffers now, so
+            // no step allocates (and every step can be captured into a graph)
+            const int terms = grad_terms(cfg->grad_dtype);
+            if (terms > 1) {
+                if ((st = ctx_alloc(c, &p.projTk, (int64_t)terms * s_dim * r)) != AETH_OK) return fail(st);
+                p.ksplit = terms;
+                if ((st = sync_projk(p, 0)) != AETH_OK) return fail(st);
+                split_need = std::max(split_need, (int64_t)terms * m * n);
+            }
         }
     }
     if ((st = ctx_alloc(c, &c->sq_slots, n_specs)) || (st = ctx_alloc(c, &c->sq_step, n_specs)) ||
-        (st = ctx_alloc(c, &c->partials, std::max(kSqPartials, kSqGroupMax * kSqChunks))) ||
+        (st = ctx_alloc(c, &c->partials, std::max(kSqPartials, kSqPartialSlots))) ||
         (st = ctx_alloc(c, &c->clip_dev, 1)) ||
         (st = ctx_alloc(c, &c->gnorm_dev, 1)) || (st = ctx_alloc(c, &c->sq_ticket, 1)) ||
         (st = ctx_alloc(c, &c->work, 2)) || (st = ctx_alloc(c, &c->clip_epoch, 1)))
         return fail(st);
+    if (split_need > 0) {
+        if ((st = ctx_alloc(c, &c->gsplit, split_need)) != AETH_OK) return fail(st);
+        c->gsplit_elems = split_need;
+    }
     if (cudaMemset(c->sq_ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
         cudaMemset(c->work, 0, 2 * sizeof(unsigned int)) != cudaSuccess)
         return fail(AETH_ERR_CONFIG);
@@ -1070,7 +1228,7 @@ int aeth_galore_project_accumulate(aeth_galore_ctx* ctx, int idx, const void* gr
     cudaStream_t st = to_stream(stream);
     AETH_TRY(set_err(capture_if_due(ctx, p, grad, grad_dtype, st)));
     if (ctx->cfg.mode == AETH_MODE_REF) return set_err(ref_project_accumulate(p, grad, grad_dtype, st));
-    return set_err(b2_project_accumulate(p, grad, grad_dtype, st));
+    return set_err(b2_project_accumulate(ctx, p, grad, grad_dtype, st));
 }
 
 int aeth_galore_sqnorm_device(aeth_galore_ctx* ctx, int idx, double* out_dev, aeth_stream_t stream) {
@@ -1303,9 +1461,14 @@ int aeth_galore_load_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t
             return set_err(AETH_ERR_SHAPE);
         const uint64_t s = p.side == 1 ? p.m : p.n;
         const uint64_t need = ref ? state_section_v2(p.m, p.n, p.r) : state_section_v3(s, p.r, p.state_elems, p.state_blocks);
-        if (d.byte_offset + need > buf.size()) return set_err(AETH_ERR_CONFIG);
+        // written so that a byte_offset near 2^64 cannot wrap the sum
+        if (d.byte_offset > buf.size() || need > buf.size() - d.byte_offset) return set_err(AETH_ERR_CONFIG);
     }
-    // Stage every section on the device, then install.
+    // Every descriptor is checked above, before anything is installed, so a
+    // malformed file leaves the optimizer as it was.  The sections are then
+    // installed layer by layer straight into the live state; a CUDA error
+    // during that loop leaves the optimizer state undefined (reload a good
+    // file or recreate the optimizer).
     for (uint32_t i = 0; i < nl; ++i) {
         Param& p = ctx->params[i];
         const uint8_t* b = buf.data() + descs[i].byte_offset;
@@ -1331,6 +1494,7 @@ int aeth_galore_load_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t
                 proj_to_bf16_kernel<<<grid_for((int64_t)s_dim * p.r, 256), 256, 0, st>>>(tmp, s_dim, p.r, p.proj,
                                                                                           p.projT);
                 e = cudaGetLastError();
+                if (e == cudaSuccess && sync_projk(p, st) != AETH_OK) e = cudaGetLastError();
             }
             cudaFreeAsync(tmp, st);
             if (e == cudaSuccess) e = cudaStreamSynchronize(st);
@@ -1386,52 +1550,50 @@ int aeth_rsvd_jacobi(float* mat, int n, float* u, aeth_stream_t stream) {
 
 uint64_t aeth_galore_step_count(const aeth_galore_ctx* ctx) { return ctx ? ctx->step : 0; }
 
-int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
-                     const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out,
-                     aeth_stream_t stream) {
-    if (!ctx || n <= 0 || !idx || !grads) return set_err(AETH_ERR_ARG);
-    if (n > (int)ctx->params.size()) return set_err(AETH_ERR_ARG);
+}  // extern "C"
+
+namespace {
+
+// Phase ids of aeth_galore_phase_times.
+enum { PH_PROJ = 0, PH_NORM = 1, PH_ADAM = 2, PH_APPLY = 3 };
+
+int check_list(const aeth_galore_ctx* ctx, int n, const int* idx) {
+    if (!ctx || n <= 0 || !idx) return AETH_ERR_ARG;
+    if (n > (int)ctx->params.size()) return AETH_ERR_ARG;
     for (int i = 0; i < n; ++i) AETH_TRY(check_idx(ctx, idx[i]));
-    DeviceGuard g(ctx->device);
-    cudaStream_t st = to_stream(stream);
-    const bool ref = ctx->cfg.mode == AETH_MODE_REF;
-    float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
-    // Under CUDA graph capture the step records only kernels: no phase events,
-    // and no gradient capture for a subspace refresh, whose schedule depends on
-    // the host step count that a replayed graph cannot follow.
+    return AETH_OK;
+}
+
+int stream_capturing(cudaStream_t st, bool* capturing) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     AETH_CUDA(cudaStreamIsCapturing(st, &cap));
-    const bool capturing = cap != cudaStreamCaptureStatusNone;
-    if (capturing && ctx->cfg.svd_refresh) return set_err(AETH_ERR_UNSUPPORTED);
-    for (int i = 0; i < n; ++i) AETH_TRY(set_err(capture_if_due(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st)));
-    if (ref) {
-        // A3 hook: project_and_accumulate for every parameter (backward.rs:510-521).
+    *capturing = cap != cudaStreamCaptureStatusNone;
+    return AETH_OK;
+}
+
+// project_and_accumulate for every listed parameter (backward.rs:509-521).
+// B200 mode: grouped launches, one per rank value (column slices of 256 above
+// rank 256), the per-tile kernel for shapes the grouped kernel does not take.
+int project_group(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
+                  cudaStream_t st) {
+    for (int i = 0; i < n; ++i) AETH_TRY(capture_if_due(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st));
+    if (ctx->cfg.mode == AETH_MODE_REF) {
         for (int i = 0; i < n; ++i) AETH_TRY(ref_project_accumulate(ctx->params[idx[i]], grads[i], grad_dtype, st));
-        // A6 pass 1: squared norms (hook.rs:149-182).
-        for (int i = 0; i < n; ++i) AETH_TRY(sqnorm_into(ctx, ctx->params[idx[i]], ctx->sq_step + i, st));
-        if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
-        clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
-        AETH_LAUNCH_CHECK();
-        // A6 pass 2: apply_update + zero_accum (hook.rs:190-194).
-        for (int i = 0; i < n; ++i) {
-            Param& p = ctx->params[idx[i]];
-            AETH_TRY(ref_apply(ctx, p, 1.0f, clip, weights ? &weights[i] : nullptr, st));
-            AETH_CUDA(cudaMemsetAsync(p.accum, 0, p.state_elems * sizeof(float), st));
-        }
         return AETH_OK;
     }
-    // B200: the layer's projections in grouped launches (one per rank value).
-    PhaseMarks pm;
-    if (!capturing) AETH_TRY(pm.begin(ctx));
-    AETH_TRY(pm.mark(0, st));
+    if (grad_dtype != AETH_DTYPE_BF16) {
+        // fp32 / f16: each gradient's bf16 terms go through the one staging
+        // buffer, so the parameters are projected one after another
+        for (int i = 0; i < n; ++i)
+            AETH_TRY(b2_project_accumulate(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st));
+        return AETH_OK;
+    }
     std::vector<ProjJob> jobs;
     std::vector<int> ranks;
     for (int i = 0; i < n; ++i) {
         Param& p = ctx->params[idx[i]];
-        const void* g = nullptr;
-        AETH_TRY(b2_grad_bf16(p, grads[i], grad_dtype, st, &g));
         if (std::find(ranks.begin(), ranks.end(), p.r) == ranks.end()) ranks.push_back(p.r);
-        jobs.push_back(ProjJob{g, p.projT, p.accum, p.m, p.n});
+        jobs.push_back(ProjJob{grads[i], p.projT, p.accum, p.m, p.n});
     }
     for (int r : ranks) {
         std::vector<ProjJob> grp;
@@ -1440,19 +1602,43 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
             if (ctx->params[idx[i]].r == r) { grp.push_back(jobs[i]); members.push_back(i); }
         int s = proj_grouped_launch(grp.data(), (int)grp.size(), r, st);
         if (s == AETH_ERR_UNSUPPORTED) {
-            for (int i : members) AETH_TRY(b2_project_tile(ctx->params[idx[i]], jobs[i].grad, st));
+            for (int i : members) AETH_TRY(b2_project_tile(ctx->params[idx[i]], jobs[i], st));
         } else if (s != AETH_OK) {
-            return set_err(s);
+            return s;
         }
+    }
+    return AETH_OK;
+}
+
+// The rest of deferred_apply_with_clip (hook.rs:139-203) for the listed
+// parameters: squared norms and the exact global clip, then apply_update and
+// zero_accum for each.  Marks the phase boundaries in pm.
+int finish_group(aeth_galore_ctx* ctx, int n, const int* idx, const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook,
+                 void* hook_user, float* clip, aeth_stream_t stream, PhaseMarks& pm) {
+    cudaStream_t st = to_stream(stream);
+    if (ctx->cfg.mode == AETH_MODE_REF) {
+        // A6 pass 1: squared norms (hook.rs:149-182).
+        for (int i = 0; i < n; ++i) AETH_TRY(sqnorm_into(ctx, ctx->params[idx[i]], ctx->sq_step + i, st));
+        if (sq_hook) AETH_TRY(sq_hook(ctx->sq_step, n, stream, hook_user));
+        clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
+        AETH_LAUNCH_CHECK();
+        AETH_TRY(pm.mark(st, PH_APPLY));
+        // A6 pass 2: apply_update + zero_accum (hook.rs:190-194).
+        for (int i = 0; i < n; ++i) {
+            Param& p = ctx->params[idx[i]];
+            AETH_TRY(ref_apply(ctx, p, 1.0f, clip, weights ? &weights[i] : nullptr, st));
+            AETH_CUDA(cudaMemsetAsync(p.accum, 0, p.state_elems * sizeof(float), st));
+        }
+        return AETH_OK;
     }
     std::vector<const float*> xs(n);
     std::vector<int64_t> ns(n);
     for (int i = 0; i < n; ++i) { xs[i] = ctx->params[idx[i]].accum; ns[i] = ctx->params[idx[i]].state_elems; }
-    AETH_TRY(pm.mark(1, st));
     // Without a hook the norms and the clip coefficient come from one launch.
     // With a clip group the same launch also exchanges the sum with the peers.
     const bool grouped = ctx->group.world > 1;
-    if (grouped && (sq_hook || n > kSqGroupMax)) return set_err(grouped && sq_hook ? AETH_ERR_ARG : AETH_ERR_UNSUPPORTED);
+    if (grouped && sq_hook) return AETH_ERR_ARG;
+    if (grouped && n > kSqGroupMax) return AETH_ERR_UNSUPPORTED;
     const bool fuse_clip = !sq_hook && n <= kSqGroupMax;
     AETH_TRY(sqnorm_group(xs.data(), ns.data(), n, ctx->sq_step, ctx->partials, ctx->sq_ticket,
                           ctx->cfg.max_grad_norm, fuse_clip ? clip : nullptr, fuse_clip ? ctx->gnorm_dev : nullptr,
@@ -1462,13 +1648,17 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
         clip_coeff_kernel<<<1, 32, 0, st>>>(ctx->sq_step, n, ctx->cfg.max_grad_norm, clip, ctx->gnorm_dev);
         AETH_LAUNCH_CHECK();
     }
-    AETH_TRY(pm.mark(2, st));
+    AETH_TRY(pm.mark(st, PH_ADAM));
     {
         std::vector<Param*> ps(n);
         for (int i = 0; i < n; ++i) ps[i] = &ctx->params[idx[i]];
         AETH_TRY(b2_adam_group(ctx, ps.data(), n, 1.0f, clip, 1, st));
     }
-    AETH_TRY(pm.mark(3, st));
+    AETH_TRY(pm.mark(st, PH_APPLY));
+    std::vector<int> ranks;
+    for (int i = 0; i < n; ++i)
+        if (std::find(ranks.begin(), ranks.end(), ctx->params[idx[i]].r) == ranks.end())
+            ranks.push_back(ctx->params[idx[i]].r);
     for (int r : ranks) {
         std::vector<ApplyJob> grp;
         for (int i = 0; i < n; ++i) {
@@ -1481,8 +1671,84 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
         }
         if (!grp.empty()) AETH_TRY(apply_grouped_launch(grp.data(), (int)grp.size(), r, st));
     }
-    AETH_TRY(pm.mark(4, st));
-    pm.commit();
+    return AETH_OK;
+}
+
+int check_weights(int n, const aeth_weight_ref* weights) {
+    if (!weights) return AETH_OK;
+    for (int i = 0; i < n; ++i) {
+        const aeth_weight_ref& w = weights[i];
+        if (w.kind != AETH_WEIGHT_NONE && !w.data) return AETH_ERR_ARG;
+        if (w.kind == AETH_WEIGHT_NF4 && !w.absmax) return AETH_ERR_ARG;
+    }
+    return AETH_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
+                     const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out,
+                     aeth_stream_t stream) {
+    AETH_TRY(set_err(check_list(ctx, n, idx)));
+    if (!grads) return set_err(AETH_ERR_ARG);
+    AETH_TRY(set_err(check_weights(n, weights)));
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
+    // Under CUDA graph capture the step records only kernels: no phase events,
+    // and no gradient capture for a subspace refresh, whose schedule depends on
+    // the host step count that a replayed graph cannot follow.
+    bool capturing = false;
+    AETH_TRY(set_err(stream_capturing(st, &capturing)));
+    if (capturing && ctx->cfg.svd_refresh) return set_err(AETH_ERR_UNSUPPORTED);
+    PhaseMarks pm;
+    if (!capturing) AETH_TRY(pm.begin(ctx));
+    AETH_TRY(pm.mark(st, PH_PROJ));
+    AETH_TRY(set_err(project_group(ctx, n, idx, grads, grad_dtype, st)));
+    AETH_TRY(pm.mark(st, PH_NORM));
+    AETH_TRY(set_err(finish_group(ctx, n, idx, weights, sq_hook, hook_user, clip, stream, pm)));
+    AETH_TRY(pm.mark(st, -1));
+    pm.commit(1);
+    return AETH_OK;
+}
+
+int aeth_galore_project_layer(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads,
+                              int grad_dtype, aeth_stream_t stream) {
+    AETH_TRY(set_err(check_list(ctx, n, idx)));
+    if (!grads) return set_err(AETH_ERR_ARG);
+    for (int i = 0; i < n; ++i)
+        if (!grads[i]) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    bool capturing = false;
+    AETH_TRY(set_err(stream_capturing(st, &capturing)));
+    if (capturing && ctx->cfg.svd_refresh) return set_err(AETH_ERR_UNSUPPORTED);
+    PhaseMarks pm;
+    if (!capturing) AETH_TRY(pm.begin(ctx));
+    AETH_TRY(pm.mark(st, PH_PROJ));
+    AETH_TRY(set_err(project_group(ctx, n, idx, grads, grad_dtype, st)));
+    AETH_TRY(pm.mark(st, -1));
+    pm.commit(0);
+    return AETH_OK;
+}
+
+int aeth_galore_finish_step(aeth_galore_ctx* ctx, int n, const int* idx, const aeth_weight_ref* weights,
+                            aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out, aeth_stream_t stream) {
+    AETH_TRY(set_err(check_list(ctx, n, idx)));
+    AETH_TRY(set_err(check_weights(n, weights)));
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    float* clip = clip_dev_out ? clip_dev_out : ctx->clip_dev;
+    bool capturing = false;
+    AETH_TRY(set_err(stream_capturing(st, &capturing)));
+    PhaseMarks pm;
+    if (!capturing) AETH_TRY(pm.begin(ctx));
+    AETH_TRY(pm.mark(st, PH_NORM));
+    AETH_TRY(set_err(finish_group(ctx, n, idx, weights, sq_hook, hook_user, clip, stream, pm)));
+    AETH_TRY(pm.mark(st, -1));
+    pm.commit(1);
     return AETH_OK;
 }
 
@@ -1589,18 +1855,18 @@ int aeth_galore_phase_times(aeth_galore_ctx* ctx, double ms_out[4], int* steps) 
     for (int k = 0; k < 4; ++k) ms_out[k] = 0.0;
     int done = 0;
     int status = AETH_OK;
-    for (auto& ev : ctx->phase_pending) {
-        if (status == AETH_OK) {
-            cudaError_t e = cudaEventSynchronize(ev[4]);
-            for (int k = 0; k < 4 && e == cudaSuccess; ++k) {
+    for (auto& rec : ctx->phase_pending) {
+        if (status == AETH_OK && !rec.ev.empty()) {
+            cudaError_t e = cudaEventSynchronize(rec.ev.back());
+            for (size_t k = 0; k + 1 < rec.ev.size() && e == cudaSuccess; ++k) {
                 float ms = 0.0f;
-                e = cudaEventElapsedTime(&ms, ev[k], ev[k + 1]);
-                ms_out[k] += ms;
+                e = cudaEventElapsedTime(&ms, rec.ev[k], rec.ev[k + 1]);
+                if (rec.phase[k] >= 0 && rec.phase[k] < 4) ms_out[rec.phase[k]] += ms;
             }
             if (e != cudaSuccess) status = set_err((int)e);
-            else ++done;
+            else done += rec.steps;
         }
-        ctx->phase_pool.push_back(ev);
+        for (cudaEvent_t e : rec.ev) ctx->event_pool.push_back(e);
     }
     ctx->phase_pending.clear();
     if (steps) *steps = done;
@@ -1622,6 +1888,7 @@ int aeth_galore_set_projector(aeth_galore_ctx* ctx, int idx, const float* P, con
         const int s_dim = p.side == 1 ? p.m : p.n;
         proj_to_bf16_kernel<<<grid_for((int64_t)s_dim * p.r, 256), 256, 0, st>>>(src, s_dim, p.r, p.proj, p.projT);
         AETH_LAUNCH_CHECK();
+        AETH_TRY(set_err(sync_projk(p, st)));
     }
     // Subspace switch resets the Adam state (optimizer.rs:236-238).
     return set_err(reset_state(ctx, p, st));

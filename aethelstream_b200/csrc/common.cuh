@@ -7,6 +7,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/aeth_galore.h"
 
 namespace aeth {
@@ -53,12 +56,16 @@ enum : uint32_t {
 };
 
 struct DeviceRuntime {
-    uint32_t* err_word = nullptr;  // device
-    bool init = false;
+    uint32_t* err_word = nullptr;   // device
+    std::atomic<bool> init{false};  // published (release) after err_word is stored
 };
 
 constexpr int kMaxDevices = 64;
 inline DeviceRuntime g_rt[kMaxDevices];
+// Serialises the first-use set-up of g_rt (and of any other per-device state
+// that shares its error word), so two host threads that touch a device for
+// the first time together neither allocate two words nor read a half-set one.
+inline std::mutex g_rt_mu;
 
 inline int current_device(int* dev) { return cuda_status(cudaGetDevice(dev)); }
 
@@ -67,10 +74,19 @@ inline int runtime_for_current(DeviceRuntime** out) {
     AETH_TRY(current_device(&dev));
     if (dev < 0 || dev >= kMaxDevices) return set_err(AETH_ERR_UNSUPPORTED);
     DeviceRuntime& rt = g_rt[dev];
-    if (!rt.init) {
-        AETH_CUDA(cudaMalloc(&rt.err_word, sizeof(uint32_t)));
-        AETH_CUDA(cudaMemset(rt.err_word, 0, sizeof(uint32_t)));
-        rt.init = true;
+    if (!rt.init.load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lock(g_rt_mu);
+        if (!rt.init.load(std::memory_order_relaxed)) {
+            uint32_t* w = nullptr;
+            AETH_CUDA(cudaMalloc(&w, sizeof(uint32_t)));
+            cudaError_t e = cudaMemset(w, 0, sizeof(uint32_t));
+            if (e != cudaSuccess) {
+                cudaFree(w);
+                return set_err((int)e);
+            }
+            rt.err_word = w;
+            rt.init.store(true, std::memory_order_release);
+        }
     }
     *out = &rt;
     return AETH_OK;

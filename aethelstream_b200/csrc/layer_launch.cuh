@@ -14,11 +14,13 @@ namespace aeth {
 // K4
 // ---------------------------------------------------------------------------
 struct ProjJob {
-    const void* grad;       // bf16 m x n
-    const uint16_t* projT;  // bf16 r x s (s = min(m, n))
+    const void* grad;       // bf16 m x n (ksplit > 1: the stacked terms of grad_split_kernel)
+    const uint16_t* projT;  // bf16 r x s (s = min(m, n)); ksplit > 1: r x projk_ld*s, the projector repeated
     float* racc;            // fp32 l x r
     int m, n;
     int ldr = 0;            // row stride of racc in floats (0: r); a column slice of a wider R
+    int ksplit = 1;         // bf16 terms stacked along the contraction (1, or 2 / 3 for f16 / fp32 gradients)
+    int projk_ld = 1;       // copies of the projector in each row of projT (>= ksplit)
 };
 
 template <int BN>
@@ -45,7 +47,7 @@ int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) 
         for (int kt = 8; kt <= 64; ++kt) {
             int64_t units_k = 0, per_unit = 0;
             for (int i = 0; i < nj; ++i) {
-                const int l = std::max(jobs[i].m, jobs[i].n), s = std::min(jobs[i].m, jobs[i].n);
+                const int l = std::max(jobs[i].m, jobs[i].n), s = std::min(jobs[i].m, jobs[i].n) * jobs[i].ksplit;
                 const int kbt = (s + 63) / 64;
                 int sp = (kbt + kt - 1) / kt;
                 const int kpu = (kbt + sp - 1) / sp;
@@ -62,10 +64,14 @@ int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) 
         const ProjJob& j = jobs[i];
         ProjProblem& p = a.p[i];
         const bool right = j.m >= j.n;
-        const int l = right ? j.m : j.n, s = right ? j.n : j.m;
-        if (right) AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)j.m, j.n, 64, 128, true));
-        else AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)j.m, j.n, 64, 64, true));
-        AETH_TRY(make_tmap_16b(&p.tmB, j.projT, (uint64_t)s, (uint64_t)r, s, 64, BN, true));
+        // contraction length s: the smaller dimension times the stacked terms
+        const int l = right ? j.m : j.n, s = (right ? j.n : j.m) * j.ksplit;
+        const int s1 = right ? j.n : j.m;
+        if (right)
+            AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)s, (uint64_t)j.m, s, 64, 128, true));
+        else
+            AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)s, j.n, 64, 64, true));
+        AETH_TRY(make_tmap_16b(&p.tmB, j.projT, (uint64_t)s, (uint64_t)r, (int64_t)s1 * j.projk_ld, 64, BN, true));
         AETH_TRY(make_tmap_2d(&p.tmC, j.racc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)r, (uint64_t)l,
                               j.ldr > 0 ? j.ldr : r, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B));
         p.a_mn = right ? 0 : 1;
@@ -104,7 +110,7 @@ inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t 
             const int w = std::min(256, r - c0);
             std::vector<ProjJob> slice(jobs, jobs + nj);
             for (ProjJob& j : slice) {
-                const int s = std::min(j.m, j.n);
+                const int s = std::min(j.m, j.n) * j.projk_ld;  // row stride of projT
                 j.projT += (size_t)c0 * s;
                 j.racc += c0;
                 j.ldr = r;
@@ -130,11 +136,15 @@ inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t 
 // takes the last ticket sums each accumulator's slots in chunk order into
 // out[p] and, when asked, also computes the global clip coefficient of
 // clip_coeff_kernel (hook.rs:184-187) from out[0..np), then resets the ticket
-// for the next launch.
+// for the next launch.  One launch takes up to kSqGroupMax accumulators (a
+// whole model's parameters on one GPU: 560 for the 80-layer 70B sweep); the
+// per-accumulator tables travel in the kernel parameters, sized by the
+// template capacity so a single layer's launch stays small.
 // ---------------------------------------------------------------------------
-constexpr int kSqGroupMax = 16;
-constexpr int kSqChunks = 128;  // partial slots per accumulator: kSqGroupMax * kSqChunks in all
-constexpr int kClipGroupMax = 16;  // GPUs in a clip group
+constexpr int kSqGroupSmall = 16;     // capacity of the launch of one layer's step
+constexpr int kSqGroupMax = 1024;     // capacity of a whole-model launch (20 KB of kernel parameters)
+constexpr int kSqPartialSlots = 4096; // chunk partials per launch
+constexpr int kClipGroupMax = 16;     // GPUs in a clip group
 
 struct PeerSlot {
     double sum;
@@ -149,17 +159,15 @@ struct ClipGroup {
     uint64_t timeout_ns = kWaitLimitNs;
 };
 
-struct SqGroupArgs {
-    const float* x[kSqGroupMax];
-    int64_t n[kSqGroupMax];
-    int chunk_begin[kSqGroupMax + 1];  // first chunk of each accumulator; chunk_begin[np] = chunks
-    int64_t chunk_elems;               // a multiple of 1024
+// Scalars and pointers shared by every capacity.
+struct SqGroupCommon {
+    int64_t chunk_elems;   // a multiple of 1024
     int np;
     float max_norm;
     float* clip_out;       // null: norms only
     double* gnorm_out;     // optional, with clip_out
     double* out;           // np sums
-    double* partials;      // kSqGroupMax * kSqChunks
+    double* partials;      // kSqPartialSlots
     unsigned int* ticket;  // zero between launches
     // Exchange of the local sum with the other GPUs of a clip group (world > 1):
     // slots[p] is rank p's slot buffer (peer memory for p != rank), laid out as
@@ -169,6 +177,14 @@ struct SqGroupArgs {
     uint64_t* epoch;  // advanced by one per launch by the last CTA
     uint64_t timeout_ns;
     uint32_t* err;
+};
+
+template <int CAP>
+struct SqGroupArgs {
+    const float* x[CAP];
+    int64_t n[CAP];
+    int chunk_begin[CAP + 1];  // first chunk of each accumulator; chunk_begin[np] = chunks
+    SqGroupCommon c;
 };
 
 // Peer exchange primitives: a release store of the epoch after the value, an
@@ -185,7 +201,7 @@ __device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
 // Writes this rank's sum into every group member's slot for this epoch, waits
 // (bounded) for every member's sum, and returns the total in rank order, so
 // every rank gets the same bits.  On timeout: flags the error and returns NaN.
-__device__ inline double clip_group_total(const SqGroupArgs& a, double local) {
+__device__ inline double clip_group_total(const SqGroupCommon& a, double local) {
     const uint64_t epoch = *a.epoch + 1;
     *a.epoch = epoch;
     const int par = (int)(epoch & 1u);
@@ -209,15 +225,23 @@ __device__ inline double clip_group_total(const SqGroupArgs& a, double local) {
     return total;
 }
 
-__global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant__ SqGroupArgs a) {
+template <int CAP>
+__global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant__ SqGroupArgs<CAP> a) {
     __shared__ double red[8];
-    __shared__ double sums[kSqGroupMax];
+    __shared__ double sums[CAP];
     __shared__ unsigned int taken;
+    const SqGroupCommon& cm = a.c;
     const int chunk = blockIdx.x;
-    int p = 0;
-    while (p + 1 < a.np && chunk >= a.chunk_begin[p + 1]) ++p;
-    const int64_t c0 = (int64_t)(chunk - a.chunk_begin[p]) * a.chunk_elems;
-    const int64_t c1 = c0 + a.chunk_elems < a.n[p] ? c0 + a.chunk_elems : a.n[p];
+    // the accumulator of this chunk: the last p with chunk_begin[p] <= chunk
+    int lo = 0, hi = cm.np - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.chunk_begin[mid] <= chunk) lo = mid;
+        else hi = mid - 1;
+    }
+    const int p = lo;
+    const int64_t c0 = (int64_t)(chunk - a.chunk_begin[p]) * cm.chunk_elems;
+    const int64_t c1 = c0 + cm.chunk_elems < a.n[p] ? c0 + cm.chunk_elems : a.n[p];
     const float4* x4 = reinterpret_cast<const float4*>(a.x[p] + c0);  // c0 % 4 == 0: still 16-byte aligned
     const int n4 = (int)((c1 - c0) / 4);
     double s[4] = {0.0, 0.0, 0.0, 0.0};
@@ -245,40 +269,73 @@ __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         double t = 0.0;
         for (int w = 0; w < 8; ++w) t += red[w];
-        a.partials[chunk] = t;
+        cm.partials[chunk] = t;
         __threadfence();
-        taken = atomicAdd(a.ticket, 1u);
+        taken = atomicAdd(cm.ticket, 1u);
     }
     __syncthreads();
     if (taken != gridDim.x - 1) return;
     __threadfence();
-    // Last CTA: warp w sums accumulators w, w + 8 (lane L: chunks L, L + 32,
-    // ... of the accumulator in order; then a fixed shuffle tree).
+    // Last CTA: warp w sums accumulators w, w + 8, ... (lane L: chunks L,
+    // L + 32, ... of the accumulator in order; then a fixed shuffle tree).
     const int lane = threadIdx.x & 31;
-    for (int q = threadIdx.x >> 5; q < a.np; q += 8) {
+    for (int q = threadIdx.x >> 5; q < cm.np; q += 8) {
         double t = 0.0;
-        for (int c = a.chunk_begin[q] + lane; c < a.chunk_begin[q + 1]; c += 32) t += __ldcg(a.partials + c);
+        for (int c = a.chunk_begin[q] + lane; c < a.chunk_begin[q + 1]; c += 32) t += __ldcg(cm.partials + c);
         t = warp_sum_d(t);
         if (lane == 0) {
-            a.out[q] = t;
+            cm.out[q] = t;
             sums[q] = t;
         }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        if (a.clip_out) {
+        if (cm.clip_out) {
             double t = 0.0;
-            for (int k = 0; k < a.np; ++k) t += sums[k];
-            if (a.world > 1) t = clip_group_total(a, t);
+            for (int k = 0; k < cm.np; ++k) t += sums[k];
+            if (cm.world > 1) t = clip_group_total(cm, t);
             const double gnorm = sqrt(t);
-            const float c = (float)((double)a.max_norm / (gnorm + 1e-6));
+            const float c = (float)((double)cm.max_norm / (gnorm + 1e-6));
             // a missing peer: this step's gradients are dropped (clip 0); the
             // error word tells the host, which restores the saved state
-            *a.clip_out = t != t ? 0.0f : (c < 1.0f ? c : 1.0f);
-            if (a.gnorm_out) *a.gnorm_out = gnorm;
+            *cm.clip_out = t != t ? 0.0f : (c < 1.0f ? c : 1.0f);
+            if (cm.gnorm_out) *cm.gnorm_out = gnorm;
         }
-        *a.ticket = 0u;
+        *cm.ticket = 0u;
     }
+}
+
+template <int CAP>
+int sqnorm_group_launch(const float* const* xs, const int64_t* ns, int cnt, const SqGroupCommon& common,
+                        cudaStream_t st) {
+    SqGroupArgs<CAP> a;
+    memset(&a, 0, sizeof(a));
+    a.c = common;
+    a.c.np = cnt;
+    for (int i = 0; i < cnt; ++i) {
+        a.x[i] = xs[i];
+        a.n[i] = ns[i];
+        if ((reinterpret_cast<uintptr_t>(a.x[i]) & 15) != 0) return AETH_ERR_UNSUPPORTED;
+    }
+    // Chunks of at least 4096 elements, about four CTAs per SM, within the
+    // kSqPartialSlots partial slots (a chunk per accumulator more than
+    // total / chunk_elems at most).
+    int64_t total = 0;
+    for (int i = 0; i < cnt; ++i) total += a.n[i];
+    const int64_t slots = (int64_t)kSqPartialSlots - cnt;
+    int64_t ce = std::max<int64_t>(total / (4 * (int64_t)num_sms()), (total + slots - 1) / slots);
+    ce = std::max<int64_t>(4096, (ce + 1023) / 1024 * 1024);
+    a.c.chunk_elems = ce;
+    int chunks = 0;
+    for (int i = 0; i < cnt; ++i) {
+        a.chunk_begin[i] = chunks;
+        chunks += (int)std::max<int64_t>(1, (a.n[i] + ce - 1) / ce);
+    }
+    a.chunk_begin[cnt] = chunks;
+    if (chunks > kSqPartialSlots) return AETH_ERR_UNSUPPORTED;
+    sqnorm_group_kernel<CAP><<<chunks, 256, 0, st>>>(a);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
 }
 
 // out[i] = sum of squares of xs[i] (f64).  With clip_out (np <= kSqGroupMax)
@@ -288,52 +345,32 @@ __global__ void __launch_bounds__(256) sqnorm_group_kernel(const __grid_constant
 inline int sqnorm_group(const float* const* xs, const int64_t* ns, int np, double* out, double* partials,
                         unsigned int* ticket, float max_norm, float* clip_out, double* gnorm_out, cudaStream_t st,
                         ClipGroup* group = nullptr) {
+    if (np <= 0) return AETH_ERR_ARG;
     if (clip_out && np > kSqGroupMax) return AETH_ERR_UNSUPPORTED;
     if (group && group->world > 1 && !clip_out) return AETH_ERR_ARG;
     DeviceRuntime* rt = nullptr;
     AETH_TRY(runtime_for_current(&rt));
+    SqGroupCommon c;
+    memset(&c, 0, sizeof(c));
+    c.max_norm = max_norm;
+    c.clip_out = clip_out;
+    c.gnorm_out = gnorm_out;
+    c.partials = partials;
+    c.ticket = ticket;
+    c.world = 1;
+    c.err = rt->err_word;
+    if (group && group->world > 1) {
+        c.rank = group->rank;
+        c.world = group->world;
+        for (int p = 0; p < group->world; ++p) c.slots[p] = group->slots[p];
+        c.epoch = group->epoch;
+        c.timeout_ns = group->timeout_ns;
+    }
     for (int off = 0; off < np; off += kSqGroupMax) {
         const int cnt = std::min(kSqGroupMax, np - off);
-        SqGroupArgs a;
-        memset(&a, 0, sizeof(a));
-        for (int i = 0; i < cnt; ++i) {
-            a.x[i] = xs[off + i];
-            a.n[i] = ns[off + i];
-            if ((reinterpret_cast<uintptr_t>(a.x[i]) & 15) != 0) return AETH_ERR_UNSUPPORTED;
-        }
-        a.np = cnt;
-        a.max_norm = max_norm;
-        a.clip_out = clip_out;
-        a.gnorm_out = gnorm_out;
-        a.out = out + off;
-        a.partials = partials;
-        a.ticket = ticket;
-        a.world = 1;
-        a.err = rt->err_word;
-        if (group && group->world > 1) {
-            a.rank = group->rank;
-            a.world = group->world;
-            for (int p = 0; p < group->world; ++p) a.slots[p] = group->slots[p];
-            a.epoch = group->epoch;
-            a.timeout_ns = group->timeout_ns;
-        }
-        // Chunks of at least 4096 elements, about four CTAs per SM, within the
-        // kSqGroupMax * kSqChunks partial slots (a chunk per accumulator more
-        // than total / chunk_elems at most).
-        int64_t total = 0;
-        for (int i = 0; i < cnt; ++i) total += a.n[i];
-        const int64_t slots = (int64_t)kSqGroupMax * kSqChunks - kSqGroupMax;
-        int64_t ce = std::max<int64_t>(total / (4 * (int64_t)num_sms()), (total + slots - 1) / slots);
-        ce = std::max<int64_t>(4096, (ce + 1023) / 1024 * 1024);
-        a.chunk_elems = ce;
-        int chunks = 0;
-        for (int i = 0; i < cnt; ++i) {
-            a.chunk_begin[i] = chunks;
-            chunks += (int)std::max<int64_t>(1, (a.n[i] + ce - 1) / ce);
-        }
-        a.chunk_begin[cnt] = chunks;
-        sqnorm_group_kernel<<<chunks, 256, 0, st>>>(a);
-        AETH_LAUNCH_CHECK();
+        c.out = out + off;
+        if (cnt <= kSqGroupSmall) AETH_TRY(sqnorm_group_launch<kSqGroupSmall>(xs + off, ns + off, cnt, c, st));
+        else AETH_TRY(sqnorm_group_launch<kSqGroupMax>(xs + off, ns + off, cnt, c, st));
     }
     return AETH_OK;
 }

@@ -80,6 +80,9 @@ class GaLoreConfig:
     # subspace refresh in notify_step as the reference (False: fixed projectors)
     svd_refresh: bool = True
     power_iters: int = 0
+    # B200: dtype of the gradients ("bf16", "f32", "f16"); f32 / f16 set up the
+    # exact split path's buffers at construction, so no step allocates
+    grad_dtype: str = "bf16"
 
     def to_c(self) -> L.GaloreConfig:
         c = L.GaloreConfig()
@@ -103,6 +106,7 @@ class GaLoreConfig:
         c.init_projectors = int(self.init_projectors)
         c.svd_refresh = int(self.svd_refresh)
         c.power_iters = self.power_iters
+        c.grad_dtype = {"f32": L.DTYPE_F32, "f16": L.DTYPE_F16, "bf16": L.DTYPE_BF16}[self.grad_dtype]
         return c
 
 
@@ -417,6 +421,35 @@ class GaLoreOptimizer:
         return out
 
     # ---- fused whole-layer step (device-side deferred_apply_with_clip) ----
+    def _indices(self, keys):
+        return (C.c_int * len(keys))(*[self._key(*k)[0] for k in keys])
+
+    @staticmethod
+    def _weight_refs(weights):
+        if weights is None:
+            return None
+        wrefs = (L.WeightRef * len(weights))()
+        for i, w in enumerate(weights):
+            if isinstance(w, NF4Tensor):
+                wrefs[i].kind, wrefs[i].data, wrefs[i].absmax = L.WEIGHT_NF4, w.packed.data_ptr(), w.absmax.data_ptr()
+            elif w is None:
+                wrefs[i].kind = L.WEIGHT_NONE
+            else:
+                wrefs[i].kind, wrefs[i].data = L.WEIGHT_F32, w.data_ptr()
+        return wrefs
+
+    def _hook(self, sq_hook):
+        if sq_hook is None:
+            return L.SQ_HOOK(0)
+
+        def _cb(sq_ptr, count, stream, user):  # noqa: ARG001 - C callback signature
+            try:
+                sq_hook(_wrap_device_doubles(sq_ptr, count, self.device))
+                return 0
+            except Exception:  # noqa: BLE001 - reported as a status to C
+                return L.AETH_ERR_CONFIG
+        return L.SQ_HOOK(_cb)
+
     def step_layer(self, keys, grads, weights=None, sq_hook=None):
         """project_and_accumulate for every (layer, name) in `keys`, the exact
         global-norm clip on the device, then apply_update + zero_accum
@@ -424,31 +457,35 @@ class GaLoreOptimizer:
         may all-reduce the per-parameter squared norms (multi-GPU).  Returns
         the device clip coefficient (a 1-element tensor)."""
         n = len(keys)
-        idx = (C.c_int * n)(*[self._key(*k)[0] for k in keys])
         gp = (C.c_void_p * n)(*[g.data_ptr() for g in grads])
-        dtype = _DTYPES[grads[0].dtype]
-        wrefs = None
-        if weights is not None:
-            wrefs = (L.WeightRef * n)()
-            for i, w in enumerate(weights):
-                if isinstance(w, NF4Tensor):
-                    wrefs[i].kind, wrefs[i].data, wrefs[i].absmax = L.WEIGHT_NF4, w.packed.data_ptr(), w.absmax.data_ptr()
-                elif w is None:
-                    wrefs[i].kind = L.WEIGHT_NONE
-                else:
-                    wrefs[i].kind, wrefs[i].data = L.WEIGHT_F32, w.data_ptr()
         clip = torch.empty(1, dtype=torch.float32, device=f"cuda:{self.device}")
-        hook = L.SQ_HOOK(0)
-        if sq_hook is not None:
-            def _cb(sq_ptr, count, stream, user):  # noqa: ARG001 - C callback signature
-                try:
-                    sq_hook(_wrap_device_doubles(sq_ptr, count, self.device))
-                    return 0
-                except Exception:  # noqa: BLE001 - reported as a status to C
-                    return L.AETH_ERR_CONFIG
-            hook = L.SQ_HOOK(_cb)
-        L.check(self._lib.aeth_galore_step(self._ctx, n, idx, gp, dtype, wrefs, hook, None, _ptr(clip),
+        hook = self._hook(sq_hook)
+        L.check(self._lib.aeth_galore_step(self._ctx, n, self._indices(keys), gp, _DTYPES[grads[0].dtype],
+                                           self._weight_refs(weights), hook, None, _ptr(clip),
                                            C.c_void_p(_stream_handle())), "aeth_galore_step")
+        return clip
+
+    def project_layer(self, keys, grads):
+        """project_and_accumulate for the (layer, name) keys of one layer, in
+        grouped launches, as backward.rs:509-521 calls it when the layer's
+        gradients are ready; the gradient buffers may be refilled once this
+        work has run on the current stream."""
+        n = len(keys)
+        gp = (C.c_void_p * n)(*[g.data_ptr() for g in grads])
+        L.check(self._lib.aeth_galore_project_layer(self._ctx, n, self._indices(keys), gp, _DTYPES[grads[0].dtype],
+                                                    C.c_void_p(_stream_handle())), "aeth_galore_project_layer")
+
+    def finish_step(self, keys, weights=None, sq_hook=None, clip_out: torch.Tensor | None = None):
+        """The exact global-norm clip over every listed parameter (all that this
+        GPU owns) in one launch, then Adam and the weight write for all of them
+        (hook.rs:115-203 on the device).  Returns the device clip coefficient."""
+        n = len(keys)
+        clip = clip_out if clip_out is not None else torch.empty(1, dtype=torch.float32,
+                                                                 device=f"cuda:{self.device}")
+        hook = self._hook(sq_hook)
+        L.check(self._lib.aeth_galore_finish_step(self._ctx, n, self._indices(keys), self._weight_refs(weights), hook,
+                                                  None, _ptr(clip), C.c_void_p(_stream_handle())),
+                "aeth_galore_finish_step")
         return clip
 
     # ---- per-phase device timing of step_layer ----
@@ -458,7 +495,9 @@ class GaLoreOptimizer:
         L.check(self._lib.aeth_galore_set_phase_timing(self._ctx, 1 if enable else 0), "set_phase_timing")
 
     def phase_times(self):
-        """(steps, {phase: total device ms}) over the step_layer calls since the last call."""
+        """(steps, {phase: total device ms}) over the step_layer, project_layer and
+        finish_step calls since the last call (steps counts step_layer and
+        finish_step calls)."""
         out = (C.c_double * 4)()
         steps = C.c_int(0)
         L.check(self._lib.aeth_galore_phase_times(self._ctx, out, C.byref(steps)), "phase_times")

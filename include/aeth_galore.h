@@ -141,6 +141,8 @@ typedef struct {
     int init_projectors;      /* 1: init_random_projection at create; 0: zero, set with aeth_galore_set_projector */
     int svd_refresh;          /* 1: capture gradients and refresh in notify_step as the reference; 0: fixed projectors */
     int power_iters;          /* 0 (the reference); > 0 adds subspace iterations to the refresh */
+    int grad_dtype;           /* B200: the gradients' aeth_dtype (BF16).  F32 / F16 allocate the split
+                                 path's buffers at create, so no step allocates */
 } aeth_galore_config;
 
 typedef struct {
@@ -189,8 +191,18 @@ int aeth_galore_param_info(const aeth_galore_ctx* ctx, int idx, aeth_param_info*
 int aeth_galore_num_params(const aeth_galore_ctx* ctx);
 
 /* OptimizerBackend::project_and_accumulate (optimizer.rs:264-292):
- * accum += projection(grad).  grad is m*n device values of `grad_dtype`
- * (REF: F32 or BF16/F16 upcast; B200: BF16). */
+ * accum += projection(grad).  grad is m*n device values of `grad_dtype`.
+ * REF: F32, or BF16 / F16 widened exactly.  B200: BF16 goes to the tensor
+ * cores as it is; F32 and F16 are never narrowed: each gradient is split
+ * exactly into three (F32) or two (F16) bf16 terms, stacked along the
+ * contraction and projected in one launch against the projector repeated
+ * that many times (16-byte aligned gradient, n % 8 == 0).  The terms go
+ * through one staging buffer of the optimizer (terms * m * n bf16 of the
+ * largest such parameter), so F32 / F16 projections of one optimizer must be
+ * issued on one stream.  The buffer is allocated at create when
+ * config.grad_dtype declares F32 / F16; otherwise on the first such call,
+ * which then synchronises the stream and is refused (AETH_ERR_UNSUPPORTED)
+ * while the stream is being captured into a CUDA graph. */
 int aeth_galore_project_accumulate(aeth_galore_ctx* ctx, int idx, const void* grad, int grad_dtype,
                                    aeth_stream_t stream);
 /* OptimizerBackend::lowrank_grad_sqnorm (optimizer.rs:294-301): sum of squares
@@ -241,7 +253,10 @@ uint64_t aeth_galore_version(const aeth_galore_ctx* ctx);
  * the state, zeroes the accumulators, and adopts the file's step count and
  * beta1, beta2, eps, as the reference's open does.  Both wait on `stream`.
  * Status: AETH_ERR_NOT_FOUND when the file cannot be opened, AETH_ERR_CONFIG
- * for I/O failures or a bad magic / version. */
+ * for I/O failures, a bad magic / version or a section outside the file.
+ * load_state checks the whole file before it installs anything, so those
+ * errors leave the optimizer unchanged; a CUDA error while the checked
+ * sections are installed leaves its state undefined. */
 int aeth_galore_save_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t stream);
 int aeth_galore_load_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t stream);
 
@@ -280,12 +295,39 @@ int aeth_galore_step(aeth_galore_ctx* ctx, int n, const int* idx, const void* co
                      const aeth_weight_ref* weights, aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out,
                      aeth_stream_t stream);
 
-/* Per-phase device timing of aeth_galore_step (no reference counterpart).
- * While enabled, every B200-mode step records CUDA events on its stream at
- * the phase boundaries: projection | squared norms and clip | Adam |
- * back-projection with the weight write.  aeth_galore_phase_times waits for
- * the recorded steps, adds their elapsed milliseconds per phase into
- * ms_out[0..3], stores the number of steps in *steps and forgets them. */
+/* The same step for a whole model whose gradients arrive layer by layer, as
+ * doublepass's backward produces them: backward.rs:509-521 calls
+ * project_and_accumulate for each layer's parameters as soon as that layer's
+ * gradients exist, and the clip and the update then run once for the model
+ * (deferred_apply_with_clip, hook.rs:115-203).  A full gradient set of a
+ * 70B model (137 GB in bf16) is never resident at once; only the projected
+ * accumulators are.
+ *   aeth_galore_project_layer: project_and_accumulate for the n listed
+ *     parameters (normally one layer's matrices), in grouped launches.  The
+ *     gradient buffers can be refilled once the work this call enqueued on
+ *     `stream` has run (record an event after it).
+ *   aeth_galore_finish_step: the exact global-norm clip over the n listed
+ *     parameters -- every parameter of the model that this GPU owns -- in one
+ *     squared-norm launch (n <= 1024 with a clip group; the clip group
+ *     exchanges the sum with the peer GPUs inside that launch), then Adam for
+ *     all of them, then the back-projection with the weight write, zeroing
+ *     the accumulators.  weights[i], sq_hook and clip_dev_out as in
+ *     aeth_galore_step.
+ * Calling project_layer for every layer and then finish_step gives the same
+ * bits as aeth_galore_step over the same parameters.  Both record into a
+ * CUDA graph under the conditions aeth_galore_step states. */
+int aeth_galore_project_layer(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
+                              aeth_stream_t stream);
+int aeth_galore_finish_step(aeth_galore_ctx* ctx, int n, const int* idx, const aeth_weight_ref* weights,
+                            aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out, aeth_stream_t stream);
+
+/* Per-phase device timing of the step (no reference counterpart).  While
+ * enabled, every B200-mode aeth_galore_step, project_layer and finish_step
+ * call records CUDA events on its stream at the phase boundaries: projection
+ * | squared norms and clip | Adam | back-projection with the weight write.
+ * aeth_galore_phase_times waits for the recorded calls, adds their elapsed
+ * milliseconds per phase into ms_out[0..3], stores the number of completed
+ * steps (aeth_galore_step and finish_step calls) in *steps and forgets them. */
 int aeth_galore_set_phase_timing(aeth_galore_ctx* ctx, int enable);
 int aeth_galore_phase_times(aeth_galore_ctx* ctx, double ms_out[4], int* steps);
 

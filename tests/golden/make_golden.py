@@ -89,4 +89,8 @@ def main(ref_root: str):
 
 if __name__ == "__main__":
     torch.manual_seed(0)
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference checkout: first argument, else $AETH_REFERENCE_ROOT
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AETH_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <reference checkout> (or set AETH_REFERENCE_ROOT)")
+    main(root)
