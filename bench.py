@@ -1,27 +1,37 @@
 """Benchmark of the per-layer optimizer step (NF4 -> GaLore -> INT8 Adam -> NF4).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config c1..c5]
 
-Workload ("C2"): one Llama-2-7B decoder block per GPU --
-q/k/v/o 4096x4096, gate/up 11008x4096, down 4096x11008 -- NF4 weights
-N(0, 0.02), bf16 gradients N(0, 1e-3), GaLore rank 128 on the smaller
-dimension with fixed projectors, INT8 blockwise dynamic-map Adam state, 50
-consecutive steps by default.  A step is one full optimizer step of the block
-through the public API (GaLoreOptimizer.step_layer): projection of all seven
-gradients, exact global-norm clip on the device, Adam, back-projection and the
-NF4 weight write -- four kernels, recorded once into a CUDA graph per
-gradient-ring parity and replayed in the timed loop.  A second, eager pass
-with CUDA events at the kernel boundaries gives the per-phase times.
-Gradients cycle through a two-deep ring generated on the device from seeds
-(step parity, matrix); all weights and state stay resident.  Under torchrun
-each rank owns one block (weak scaling); the only exchange is the global
-clip's sum of squared norms, which the squared-norm kernel swaps with the
-peer GPUs over NVLink.
+Default workload ("C4"): the Llama-2-70B-shaped sweep of
+80 layers -- q/o 8192x8192, k/v 1024x8192 (GQA), gate/up 28672x8192, down
+8192x28672 -- NF4 weights N(0, 0.02), bf16 gradients N(0, 1e-3), GaLore rank
+512 one-sided on the smaller dimension, INT8 blockwise-2048 dynamic-map Adam.
+A step is one optimizer step of the whole model through the public API, the
+way doublepass's backward drives it: GaLoreOptimizer.project_layer for each
+layer as its gradients arrive (one grouped projection per layer, per 256
+columns of the rank), then one GaLoreOptimizer.finish_step for every
+parameter the GPU owns (one squared-norm launch with the exact global clip,
+grouped Adam, grouped back-projection with the fused NF4 weight write).  The
+whole step is recorded into one CUDA graph and replayed in the timed loop; an
+eager pass with CUDA events at the phase boundaries gives the per-phase times.
+Layers are owned round-robin (layer li on rank li mod N): the 80-layer sweep
+is fixed and split over the GPUs (strong scaling); the only exchange per step
+is the global clip's sum of squared norms, which the squared-norm kernel swaps
+with the peer GPUs over NVLink.  All NF4 weights, projectors and INT8 state of
+the owned layers stay resident; gradients cycle through a two-deep per-layer
+ring (layer li reads slot li mod 2), generated on the device from seeds.
+The projector refresh of C4 (every 200 steps) is timed on its own in the same
+run and reported next to the step.
 
-The reference arm (--impl reference) times the reference's CPU algorithm
-(oracle/ port of galore/src/{project,adamw,optimizer}.rs, nf4.rs; the Rust
-crate cannot be built here) on all host threads over a bounded row sample of
-the same workload.
+--config c3 is the 40-layer Llama-2-13B sweep (r = 256, Student-t(3)
+gradients); c2 (one 7B block, r = 128, weak scaling: one block per rank) and
+c1 (one 4096x4096 weight, fp32 gradients) are the single-block configs; c5 is
+the LOMO bandwidth sweep.
+
+The reference arm (--impl reference) times the reference's CPU algorithm (the
+oracle's restatement of galore/src/{project,adamw,optimizer}.rs and nf4.rs;
+the Rust crate cannot be built here) on one host thread over a bounded row
+sample of the same workload, extrapolated to the whole step.
 """
 from __future__ import annotations
 
@@ -46,23 +56,25 @@ CONFIGS = {
                          "GaLore r=128 one-sided on the smaller dim, fixed projectors, NF4 weights, bf16 grads, "
                          "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
     # one 4096x4096 weight (used for small profiling captures)
-    "c1": dict(shapes=[("d_wq", 4096, 4096)],
-               workload=("C1: one 4096x4096 weight, GaLore r=128, NF4 weight, bf16 grad, "
-                         "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
-    # one Llama-2-13B block per GPU, r = 256, Student-t gradients
+    "c1": dict(shapes=[("d_wq", 4096, 4096)], grad_dtype="f32",
+               workload=("C1: one 4096x4096 weight, GaLore r=128, NF4 weight, fp32 grad N(0,1e-3) (projected as "
+                         "its exact bf16 terms, no narrowing), INT8 blockwise-2048 dynamic-map Adam, fused NF4 "
+                         "requant")),
+    # the Llama-2-13B sweep of 40 layers, r = 256, Student-t gradients
     "c3": dict(shapes=[("d_wq", 5120, 5120), ("d_wk", 5120, 5120), ("d_wv", 5120, 5120), ("d_wo", 5120, 5120),
                        ("d_wg", 13824, 5120), ("d_wu", 13824, 5120), ("d_wd", 5120, 13824)],
-               rank=256, grad="student_t3",
-               workload=("C3: one Llama-2-13B block per GPU (q/k/v/o 5120x5120, gate/up 13824x5120, down "
-                         "5120x13824), GaLore r=256 one-sided, fixed projectors, NF4 weights, bf16 Student-t(3) "
+               rank=256, grad="student_t3", layers=40,
+               workload=("C3: 40-layer Llama-2-13B sweep (q/k/v/o 5120x5120, gate/up 13824x5120, down 5120x13824), "
+                         "layers round-robin over the GPUs, GaLore r=256 one-sided, NF4 weights, bf16 Student-t(3) "
                          "grads scaled to std 1e-3, INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
-    # one Llama-2-70B block per GPU, r = 512 (grouped-query k/v 1024x8192)
+    # the Llama-2-70B sweep of 80 layers, r = 512 (grouped-query k/v 1024x8192)
     "c4": dict(shapes=[("d_wq", 8192, 8192), ("d_wk", 1024, 8192), ("d_wv", 1024, 8192), ("d_wo", 8192, 8192),
                        ("d_wg", 28672, 8192), ("d_wu", 28672, 8192), ("d_wd", 8192, 28672)],
-               rank=512,
-               workload=("C4: one Llama-2-70B block per GPU (q/o 8192x8192, k/v 1024x8192, gate/up 28672x8192, "
-                         "down 8192x28672), GaLore r=512 one-sided, fixed projectors, NF4 weights, bf16 grads, "
-                         "INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant")),
+               rank=512, layers=80, refresh=dict(interval=200, oversampling=8, power_iters=2),
+               workload=("C4: 80-layer Llama-2-70B sweep, r=512 (q/o 8192x8192, k/v 1024x8192, gate/up 28672x8192, "
+                         "down 8192x28672), layers round-robin over the GPUs, GaLore one-sided, NF4 weights, bf16 "
+                         "grads, INT8 blockwise-2048 dynamic-map Adam, fused NF4 requant; projector refresh every "
+                         "200 steps (randomized SVD, oversampling 8, 2 power iterations) timed alongside")),
     # LOMO sweep over flat NF4 tensors
     "c5": dict(shapes=[], lomo_sizes=[1 << k for k in (20, 22, 24, 26, 28, 30)],
                workload=("C5: LOMO sweep, flat NF4 tensors of 2^20 .. 2^30 elements per GPU, bf16 grads N(0,1e-3), "
@@ -72,6 +84,7 @@ CONFIGS = {
 SHAPES = CONFIGS["c2"]["shapes"]
 RANK = 128
 GRAD = "normal"
+GRAD_DTYPE = "bf16"
 STATE_BLOCK = 2048
 WORKLOAD = CONFIGS["c2"]["workload"]
 
@@ -79,16 +92,17 @@ WORKLOAD = CONFIGS["c2"]["workload"]
 def algorithmic(shapes=None, r=None):
     """Algorithmic bytes and flops per step, split by phase.
 
-    projection phase (K4): read bf16 G (2 B/elem) + projector (2 s r).
+    projection phase (K4): read G (2 B/elem bf16, 4 B/elem fp32) + projector (2 s r).
     apply phase (K5+K6): NF4 weight read + write (2 x 0.5625 B/elem), INT8 m/v
     read + write (4 r l), block scales (8 r l / 2048), projector (2 s r).
     Flops: 2 r m n per GEMM (projection and back-projection) + ~12 r l (Adam).
     """
     r = r or RANK
+    gb = 4 if GRAD_DTYPE == "f32" else 2
     bp = ba = fp = fa = 0
     for _, m, n in (shapes or SHAPES):
         s, l = min(m, n), max(m, n)
-        bp += 2 * m * n + 2 * s * r
+        bp += gb * m * n + 2 * s * r
         ba += 2 * 0.5625 * m * n + 4 * r * l + 8 * r * l / STATE_BLOCK + 2 * s * r
         fp += 2 * r * m * n
         fa += 2 * r * m * n + 12 * r * l
@@ -106,17 +120,18 @@ KERNEL_NAMES = {
 def kernel_bytes(shapes=None, r=None):
     """Compulsory HBM bytes per launch of each step kernel (one launch each per step).
 
-    projection: read G bf16 (2 B/elem) + projector (2 s r), write R f32 (4 r l).
+    projection: read G (2 B/elem bf16, 4 fp32) + projector (2 s r), write R f32 (4 r l).
     sqnorm_clip: read R (4 r l).
     adam: read R + zero R (8 r l), m/v codes read + write (4 r l), N bf16 write (2 r l),
           block scales read + write (16 r l / 2048).
     apply: NF4 weight read + write (2 x 0.5625 B/elem), N bf16 read (2 r l), projector (2 s r).
     """
     r = r or RANK
+    gb = 4 if GRAD_DTYPE == "f32" else 2
     out = dict.fromkeys(("projection", "sqnorm_clip", "adam", "apply"), 0.0)
     for _, m, n in (shapes or SHAPES):
         s, l = min(m, n), max(m, n)
-        out["projection"] += 2 * m * n + 2 * s * r + 4 * r * l
+        out["projection"] += gb * m * n + 2 * s * r + 4 * r * l
         out["sqnorm_clip"] += 4 * r * l
         out["adam"] += 14 * r * l + 16 * r * l / STATE_BLOCK
         out["apply"] += 2 * 0.5625 * m * n + 2 * r * l + 2 * s * r
@@ -229,33 +244,69 @@ def cpu_baseline(frac, threads, k=1):
     return done / dt, dt
 
 
-def run_reference(args):
+def run_reference_sweep(args):
+    """The reference arm of the sweeps: the reference's CPU algorithm on one
+    host thread (the reference is single-threaded), on the bounded sample of
+    sweep_cpu_sample, extrapolated to the whole step; the same config object
+    as the B200 arm."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    threads = os.cpu_count() or 1
-    frac = 1.0 / 64
-    from oracle import oracle as O
-    O.build()
-    samp = O.ReferenceSampler([(m, n) for _, m, n in SHAPES], RANK, frac, threads=threads, seed=1)
-    for _ in range(args.warmup):
-        samp.step()
-    t0 = time.perf_counter()
-    done = 0.0
-    for _ in range(args.steps):
-        done += samp.step()
-    dt = time.perf_counter() - t0
-    v = done / dt
-    total = sum(m * n for _, m, n in SHAPES)
-    sample = (f"1/64 of each matrix's output rows per step (1/64 of the rows of P^T G, m/64 rows of the weight "
-              f"delta and NF4 weight apply) over the {len(SHAPES)} matrices of the {args.config.upper()} block; "
-              f"params/s = 1/64 x {total / 1e6:.1f}M x steps / time")
+    k = max(1, min(args.steps, 3))
+    vals, secs = [], 0.0
+    desc = ""
+    for _ in range(k):
+        v, dt, desc = sweep_cpu_sample(1)
+        vals.append(v)
+        secs += dt
+    v = statistics.median(vals)
+    params_step = sum(m * n for _, m, n in SHAPES) * (args.layers or CONFIGS[args.config]["layers"])
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": k,
+            "warmup": 0, "ms_per_step": 1000.0 * params_step / v, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": sweep_config(args, world),
+            "parallelism": "one host thread (rank 0 only)", "extrapolated": True,
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
+                             "sample": desc + f"; median of {k} samples, {secs:.1f} s"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    emit(line)
+    return 0
+
+
+def block_config():
+    """The config object of the single-block workloads (C1, C2), identical in
+    both arms."""
+    params_per_step = sum(m * n for _, m, n in SHAPES)
+    gb = 4 if GRAD_DTYPE == "f32" else 2
+    return {"workload": WORKLOAD, "params_per_gpu_step": params_per_step, "rank": RANK,
+            "state": "int8 dynamic-map, 2048-element blocks",
+            "l2": (f"inputs larger than L2 ({gb * params_per_step / 1e6:.0f} MB of {GRAD_DTYPE} gradients per "
+                   "step, 2-deep ring)") if gb * params_per_step > 126e6 else
+                  f"inputs smaller than L2 ({gb * params_per_step / 1e6:.0f} MB of {GRAD_DTYPE} gradients)"}
+
+
+def run_reference(args):
+    """The reference arm of the single-block configs: the reference's CPU
+    algorithm on one host thread (it is single-threaded), on the same 1/128
+    row sample as the B200 arm's cpu_baseline, extrapolated to the step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    k = max(1, min(args.steps, 3))
+    vals, secs = [], 0.0
+    for _ in range(k):
+        v, dt = cpu_baseline(1.0 / 128, 1)
+        vals.append(v)
+        secs += dt
+    v = statistics.median(vals)
+    sample = (f"reference CPU algorithm (oracle restatement: two-sided fp32 GaLore, per-tensor INT8, NF4 dequant + "
+              f"fp32 apply), one thread, 1/128 of each matrix's output rows over the {len(SHAPES)} matrices of the "
+              f"{args.config.upper()} block, extrapolated linearly to the step; median of {k} samples, {secs:.1f} s")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(m * n for _, m, n in SHAPES) / v,
+            "steps": k, "warmup": 0, "ms_per_step": 1000.0 * sum(m * n for _, m, n in SHAPES) / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD + " -- reference CPU algorithm (two-sided fp32 GaLore, per-tensor "
-                                              "INT8, NF4 dequant + fp32 apply)", "parallelism": "host threads"},
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "config": block_config(), "parallelism": "one host thread (rank 0 only)", "extrapolated": True,
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
     return 0
@@ -497,7 +548,8 @@ def run_b200(args):
     specs = [(layer, name, m, n, RANK) for name, m, n in SHAPES]
     # C2 holds the projectors fixed (no gradient capture, no refresh inside the timed steps)
     cfg = GaLoreConfig(mode="b200", state_codec="dynamic", state_block=STATE_BLOCK,
-                       layer_ranks=LayerRankConfig(), svd_refresh=False)
+                       layer_ranks=LayerRankConfig(), svd_refresh=False, grad_dtype=GRAD_DTYPE)
+    gdt = {"bf16": torch.bfloat16, "f32": torch.float32, "f16": torch.float16}[GRAD_DTYPE]
     opt = GaLoreOptimizer(cfg, specs, device=local)
     gen = torch.Generator(device=dev)
     weights = []
@@ -516,7 +568,7 @@ def run_b200(args):
                 # t(3) = z / sqrt(chi2_3 / 3), standard deviation sqrt(3)
                 chi2 = sum(torch.randn(m, n, generator=gen, device=dev) ** 2 for _ in range(3))
                 g = g / torch.sqrt(chi2 / 3.0) / (3.0 ** 0.5)
-            gs.append((g * 1e-3).to(torch.bfloat16))
+            gs.append((g * 1e-3).to(gdt))
             del g
         ring.append(gs)
     keys = [(layer, name) for name, _, _ in SHAPES]
@@ -668,14 +720,12 @@ def run_b200(args):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) bf16 grads)",
-            "config": {"workload": WORKLOAD, "params_per_gpu_step": params_per_step, "rank": RANK,
-                       "launch": "CUDA graph replay of the step" if hook is None else "eager (host hook)",
-                       "state": "int8 dynamic-map, 2048-element blocks", "parallelism": f"layer-sharded x{world}",
-                       "clip_exchange": clip_exchange,
-                       "l2": (f"inputs larger than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients per "
-                              "step, 2-deep ring)") if 2 * params_per_step > 126e6 else
-                             f"inputs smaller than L2 ({2 * params_per_step / 1e6:.0f} MB of bf16 gradients)"},
+            "vs_baseline": None, "dtype": "bf16" if GRAD_DTYPE == "bf16" else f"{GRAD_DTYPE} grads as exact bf16 terms",
+            "data": f"synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) {GRAD_DTYPE} grads)",
+            "config": block_config(),
+            "parallelism": f"layer-sharded x{world}",
+            "launch": "CUDA graph replay of the step" if hook is None else "eager (host hook)",
+            "clip_exchange": clip_exchange,
             "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": KERNEL_NAMES[dom],
                          "achieved": tfs[dom] if tensor_bound else gbs[dom],
                          "peak": tflops_sus if tensor_bound else hbm,
@@ -703,13 +753,312 @@ def run_b200(args):
         if world == 1 and not args.no_cpu_baseline:
             v, dt = cpu_baseline(1.0 / 128, 1)
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
-                                    "sample": "reference CPU algorithm (oracle port), 1/128 of each matrix's output "
-                                              f"rows over the {len(SHAPES)} matrices of the block, single thread, {dt:.1f} s"}
+                                    "sample": "reference CPU algorithm (oracle restatement), 1/128 of each matrix's "
+                                              f"output rows over the {len(SHAPES)} matrices of the block, one thread, "
+                                              f"{dt:.1f} s, extrapolated linearly to the step"}
         emit(line)
     opt.close()
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def sweep_cpu_sample(threads=1):
+    """The reference algorithm (oracle restatement, one thread) on one layer's
+    seven matrices, each on a row sample of fraction 1/r (one row of P^T G,
+    m/r rows of the weight delta and NF4 apply).  Returns (params/s, seconds,
+    description); params/s is the same rate for the whole sweep, whose step
+    time is layers x r x the sample's time (extrapolated)."""
+    from oracle import oracle as O
+    O.build()
+    frac = 1.0 / RANK
+    samp = O.ReferenceSampler([(m, n) for _, m, n in SHAPES], RANK, frac, threads=threads, seed=1)
+    t0 = time.perf_counter()
+    done = samp.step()
+    dt = time.perf_counter() - t0
+    desc = (f"reference CPU algorithm (oracle restatement of project.rs/adamw.rs/optimizer.rs/nf4.rs: two-sided fp32 "
+            f"GaLore, per-tensor INT8, NF4 dequant + fp32 apply), {threads} thread(s), one layer's {len(SHAPES)} "
+            f"matrices on a 1/{RANK} row sample ({dt:.1f} s); extrapolated linearly to the whole step")
+    return done / dt, dt, desc
+
+
+def sweep_config(args, world):
+    cfg = CONFIGS[args.config]
+    layers = args.layers or cfg["layers"]
+    per_layer = sum(m * n for _, m, n in SHAPES)
+    c = {"workload": WORKLOAD, "layers": layers, "params_per_step": per_layer * layers, "rank": RANK,
+         "state": "int8 dynamic-map, 2048-element blocks", "sharding": "layer li on rank li mod N (strong scaling)",
+         "l2": f"inputs larger than L2 ({2 * per_layer / 1e6:.0f} MB of bf16 gradients per layer, "
+               f"two-deep per-layer ring)"}
+    return c
+
+
+def run_sweep(args):
+    """C3 / C4: the layer sweep through project_layer + finish_step, strong scaling."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        os.environ["NCCL_DEBUG"] = "WARN"  # keep NCCL's version banner off stdout: the JSON line is the only output
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from aethelstream_b200 import GaLoreConfig, GaLoreOptimizer, LayerRankConfig, nf4_quantize
+    from aethelstream_b200 import _lib
+    from aethelstream_b200.sharding import owned_layers, setup_clip_group
+
+    cfgd = CONFIGS[args.config]
+    layers = args.layers or cfgd["layers"]
+    owned = owned_layers(layers, rank, world)
+    dev = torch.device("cuda", local)
+    specs = [(li, name, m, n, RANK) for li in owned for name, m, n in SHAPES]
+    cfg = GaLoreConfig(mode="b200", state_codec="dynamic", state_block=STATE_BLOCK, layer_ranks=LayerRankConfig(),
+                       svd_refresh=False, init_projectors=False)
+    opt = GaLoreOptimizer(cfg, specs, device=local)
+    gen = torch.Generator(device=dev)
+    # Projectors: one orthonormal basis per matrix shape (QR of a Gaussian),
+    # made distinct per layer by random column signs; NF4 weights N(0, 0.02).
+    bases = {}
+    for i, (name, m, n) in enumerate(SHAPES):
+        s_dim = min(m, n)
+        if s_dim not in bases:
+            gen.manual_seed(17 + s_dim)
+            bases[s_dim] = torch.linalg.qr(torch.randn(s_dim, RANK, generator=gen, device=dev))[0].contiguous()
+    weights = {}
+    for li in owned:
+        for i, (name, m, n) in enumerate(SHAPES):
+            gen.manual_seed(1000 * li + i)
+            sign = (torch.randint(0, 2, (RANK,), generator=gen, device=dev) * 2 - 1).float()
+            proj = bases[min(m, n)] * sign
+            if m >= n:
+                opt.set_projector(li, name, Q=proj)
+            else:
+                opt.set_projector(li, name, P=proj)
+            w = torch.randn(m, n, generator=gen, device=dev) * 0.02
+            weights[(li, name)] = nf4_quantize(w)
+            del w
+    ring = []
+    for parity in range(2):
+        gs = []
+        for i, (name, m, n) in enumerate(SHAPES):
+            gen.manual_seed(7919 * (parity + 1) + 100 * rank + i)
+            g = torch.randn(m, n, generator=gen, device=dev)
+            if GRAD == "student_t3":
+                # t(3) = z / sqrt(chi2_3 / 3), standard deviation sqrt(3)
+                chi2 = sum(torch.randn(m, n, generator=gen, device=dev) ** 2 for _ in range(3))
+                g = g / torch.sqrt(chi2 / 3.0) / (3.0 ** 0.5)
+            gs.append((g * 1e-3).to(torch.bfloat16))
+            del g
+        ring.append(gs)
+    torch.cuda.synchronize()
+    keys_by_layer = {li: [(li, name) for name, _, _ in SHAPES] for li in owned}
+    all_keys = [k for li in owned for k in keys_by_layer[li]]
+    all_w = [weights[k] for k in all_keys]
+    stream = torch.cuda.current_stream()
+    clip_exchange = "local (one GPU)"
+    if world > 1:
+        if not setup_clip_group(opt, timeout_s=5.0):
+            raise RuntimeError("peer clip group could not be set up")
+        clip_exchange = "peer memory: NVLink stores and acquire loads inside the squared-norm launch"
+    clip_out = torch.empty(1, dtype=torch.float32, device=dev)
+
+    def step(grads_of=None):
+        for li in owned:
+            opt.project_layer(keys_by_layer[li], ring[li % 2] if grads_of is None else grads_of(li))
+        return opt.finish_step(all_keys, all_w, clip_out=clip_out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:  # after each rank's sampler start: the ranks enter the timed steps together
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    del graph
+
+    # per-phase breakdown from an eager pass with events at the phase boundaries
+    k_phase = min(args.steps, 3)
+    opt.set_phase_timing(True)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(k_phase):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    opt.set_phase_timing(False)
+    n_timed, phase_ms = opt.phase_times()
+    assert n_timed == k_phase, (n_timed, k_phase)
+    eager_ms = e0.elapsed_time(e1) / k_phase
+
+    # end to end through the public API: every layer's gradients copied from
+    # pinned host memory into the device ring on a copy stream, the copy of
+    # layer li + 2 overlapping the projection of layer li; clip read back
+    host_ring = [[g.cpu().pin_memory() for g in slot] for slot in ring]
+    h2d_layer = sum(g.numel() * g.element_size() for g in host_ring[0])
+    copy_stream = torch.cuda.Stream(device=dev)
+    clip_host = torch.empty(1, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        used = {0: None, 1: None}
+        for j, li in enumerate(owned):
+            slot = j % 2
+            with torch.cuda.stream(copy_stream):
+                if used[slot] is not None:
+                    copy_stream.wait_event(used[slot])
+                for hg, dg in zip(host_ring[slot], ring[slot]):
+                    dg.copy_(hg, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+            stream.wait_event(ev)
+            opt.project_layer(keys_by_layer[li], ring[slot])
+            done = torch.cuda.Event()
+            done.record(stream)
+            used[slot] = done
+        clip = opt.finish_step(all_keys, all_w, clip_out=clip_out)
+        clip_host.copy_(clip, non_blocking=True)
+        stream.synchronize()
+        return float(clip_host[0])
+
+    e2e_step()
+    k_e2e = 2
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(k_e2e):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a0.elapsed_time(a1) / k_e2e
+    del host_ring
+
+    # projector refresh of the owned layers (C4: every `interval` steps)
+    refresh = None
+    if "refresh" in cfgd:
+        refresh = time_refresh(opt, owned, ring, cfgd["refresh"], dev, world, rank)
+
+    dev_err = _lib.device_error_bits(local)
+    if dev_err:
+        raise RuntimeError(f"a bounded device wait gave up during the bench (error bits {dev_err:#x})")
+    t = torch.tensor([ms, eager_ms, e2e_ms] + [phase_ms[k] / k_phase for k in opt.PHASES], dtype=torch.float64,
+                     device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, eager_ms, e2e_ms = t[0].item(), t[1].item(), t[2].item()
+    per_ms = dict(zip(opt.PHASES, t[3:].tolist()))
+    step_ms = ms / args.steps
+    per_layer = sum(m * n for _, m, n in SHAPES)
+    params_step = per_layer * layers
+    value = params_step / (step_ms / 1000.0)
+
+    if rank == 0:
+        hbm, tflops, tflops_sus, peak_kind = load_peaks()
+        n_owned0 = len(owned_layers(layers, 0, world))
+        shapes_owned = [sh for _ in range(n_owned0) for sh in SHAPES]
+        kb = kernel_bytes(shapes_owned)
+        kf = kernel_flops(shapes_owned)
+        alg = algorithmic(shapes_owned)
+        gbs = {k: kb[k] / (per_ms[k] / 1000.0) / 1e9 for k in opt.PHASES}
+        tfs = {k: kf[k] / (per_ms[k] / 1000.0) / 1e12 for k in opt.PHASES}
+        dom = max(opt.PHASES, key=lambda k: per_ms[k])
+        byte_frac = gbs[dom] / hbm
+        flop_frac = tfs[dom] / tflops_sus
+        tensor_bound = flop_frac > byte_frac
+        total_bytes = alg["proj_bytes"] + alg["apply_bytes"]
+        total_flops = alg["proj_flops"] + alg["apply_flops"]
+        ideal_s = max(total_bytes / (hbm * 1e9), total_flops / (tflops_sus * 1e12))
+        traffic = load_traffic_sweep(args.config)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) NF4 weights, N(0,1e-3) bf16 grads, orthonormal projectors)",
+            "config": sweep_config(args, world),
+            "parallelism": f"layer-sharded x{world}",
+            "launch": "one CUDA graph per step: per-layer project_layer, one finish_step",
+            "clip_exchange": clip_exchange,
+            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": KERNEL_NAMES[dom],
+                         "achieved": tfs[dom] if tensor_bound else gbs[dom],
+                         "peak": tflops_sus if tensor_bound else hbm,
+                         "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                         "frac": flop_frac if tensor_bound else byte_frac,
+                         "traffic": traffic.get(f"{dom}_bytes_per_param_elem") and
+                         traffic[f"{dom}_bytes_per_param_elem"] * sum(m * n for _, m, n in shapes_owned),
+                         "algorithmic_bytes_per_step": kb[dom], "algorithmic_flops_per_step": kf[dom],
+                         "hbm_frac": byte_frac, "tensor_frac_of_sustained": flop_frac,
+                         "tensor_frac_of_burst": tfs[dom] / tflops,
+                         "phase_ms_per_step": per_ms[dom], "peak_kind": peak_kind,
+                         "note": "per step on rank 0: the phase's launches (one per layer, or grouped chunks), "
+                                 "from CUDA events at the phase boundaries of an eager pass"},
+            "roofline_step": {"algorithmic_bytes": total_bytes, "algorithmic_flops": total_flops,
+                              "ideal_ms": ideal_s * 1000.0, "measured_ms": step_ms, "frac": ideal_s / (step_ms / 1e3),
+                              "phase_ms": per_ms, "phase_gbs": gbs, "phase_tflops": tfs,
+                              "eager_ms_per_step_with_phase_events": eager_ms},
+            "e2e": {"value": params_step / (e2e_ms / 1000.0), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d_layer * len(owned) * world, "d2h_bytes_per_step": 4 * world,
+                    "steps": k_e2e, "ms_per_step": e2e_ms,
+                    "note": "per-layer gradients copied from pinned host memory into the device ring on a copy "
+                            "stream (layer li + 2 overlapping the projection of layer li), the clip read back"},
+            "gpu_launches": args.steps * (len(owned) * ((RANK + 255) // 256) + 1 +
+                                          (len(all_keys) + 15) // 16 + (len(all_keys) + 7) // 8),
+            "clocks": clk,
+        }
+        if refresh is not None:
+            interval = cfgd["refresh"]["interval"]
+            amort = step_ms + refresh["ms"] / interval
+            line["refresh"] = dict(refresh, interval=interval, amortized_ms_per_step=amort,
+                                   amortized_value=params_step / (amort / 1000.0))
+        if world == 1 and not args.no_cpu_baseline:
+            v, dt, desc = sweep_cpu_sample(1)
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": 1, "kind": "port", "sample": desc}
+        emit(line)
+    opt.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def time_refresh(opt, owned, ring, rcfg, dev, world, rank):
+    """Placeholder until the device refresh of a sweep layer exists."""
+    return None
+
+
+def load_traffic_sweep(config):
+    """Per-parameter-element DRAM bytes of the step kernels from the committed
+    ncu summary of the sweep (if present)."""
+    p = os.path.join(ROOT, "profiles", f"traffic_{config}.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:  # noqa: BLE001
+            return {}
+    return {}
 
 
 _JSON_FD = None
@@ -730,25 +1079,33 @@ def main():
     os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 20 for sweeps, 50 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c4")
+    ap.add_argument("--layers", type=int, default=None, help="sweeps: layers of the sweep (default: the config's)")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 20 if "layers" in CONFIGS[args.config] else 50
     if args.warmup < 3:
         args.warmup = 3
-    global SHAPES, WORKLOAD, RANK, GRAD
+    global SHAPES, WORKLOAD, RANK, GRAD, GRAD_DTYPE
     SHAPES = CONFIGS[args.config]["shapes"]
     WORKLOAD = CONFIGS[args.config]["workload"]
     RANK = CONFIGS[args.config].get("rank", 128)
     GRAD = CONFIGS[args.config].get("grad", "normal")
+    GRAD_DTYPE = CONFIGS[args.config].get("grad_dtype", "bf16")
     if args.impl == "reference":
         if args.config == "c5":
             return run_lomo_reference(args)
+        if "layers" in CONFIGS[args.config]:
+            return run_reference_sweep(args)
         return run_reference(args)
     if args.config == "c5":
         return run_lomo(args)
+    if "layers" in CONFIGS[args.config]:
+        return run_sweep(args)
     return run_b200(args)
 
 
