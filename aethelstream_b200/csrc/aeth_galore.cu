@@ -18,6 +18,7 @@
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "layer_launch.cuh"
+#include "small_rank.cuh"
 #include "lomo.cuh"
 #include "nf4.cuh"
 #include "rsvd.cuh"
@@ -206,13 +207,13 @@ __global__ void nf4_apply_delta_kernel(uint8_t* __restrict__ wp, float* __restri
         float amax = 0.0f;
         for (int i = 0; i < 64; ++i) {
             w[i] = __fsub_rn(w[i], delta[b * 64 + i]);
-            amax = fmaxf(amax, fabsf(w[i]));
+            amax = fmax_nan(amax, fabsf(w[i]));  // a NaN weight makes the block's absmax NaN, as the reference's max
             if (prequant) prequant[b * 64 + i] = w[i];
         }
         uint32_t pk[8];
         nf4_quant_regs<64>(w, amax, tab.bucket, pk);
         for (int k = 0; k < 8; ++k) reinterpret_cast<uint32_t*>(p)[k] = pk[k];
-        wa[b] = amax;
+        wa[b] = nf4_store_amax(amax);
     }
 }
 
@@ -541,7 +542,21 @@ int b2_project_tile(Param& p, const ProjJob& j, cudaStream_t st) {
     return tc_gemm<true, false>(TcOperand{j.grad, n}, TcOperand{j.projT, kl * m}, n, r, k * m, true, epi, st);
 }
 
+// Whether the TMA-fed tensor-core kernels can describe this parameter: every
+// row pitch of the gradient, the projector and the l x r state a multiple of
+// 16 bytes.  Otherwise (the rank-1 RMS-norm vectors) small_rank.cuh serves it.
+bool b2_tma_shape(const Param& p) { return p.r % 8 == 0 && p.m % 8 == 0 && p.n % 8 == 0; }
+
+int b2_project_small(Param& p, const void* grad, int dtype, cudaStream_t st) {
+    const int64_t cnt = (int64_t)std::max(p.m, p.n) * p.r;
+    small_project_kernel<<<grid_for(cnt, 128), 128, 0, st>>>(grad, dtype, p.m, p.n, p.r, p.side == 2 ? 1 : 0, p.proj,
+                                                            p.accum);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
 int b2_project_accumulate(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, cudaStream_t st) {
+    if (!b2_tma_shape(p) || (reinterpret_cast<uintptr_t>(grad) & 15) != 0) return b2_project_small(p, grad, dtype, st);
     ProjJob j;
     AETH_TRY(b2_grad_job(c, p, grad, dtype, st, &j));
     int s = proj_grouped_launch(&j, 1, p.r, st);
@@ -586,6 +601,18 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         return AETH_OK;
     }
     AETH_TRY(codec_maps_ensure());
+    {
+        // a state whose size is not a multiple of 8 goes through the per-parameter kernel
+        std::vector<Param*> grouped;
+        for (int i = 0; i < np; ++i) {
+            if (ps[i]->state_elems % 8 != 0) AETH_TRY(b2_adam(c, *ps[i], clip, clip_dev, zero_accum, st));
+            else grouped.push_back(ps[i]);
+        }
+        if ((int)grouped.size() != np) {
+            if (grouped.empty()) return AETH_OK;
+            return b2_adam_group(c, grouped.data(), (int)grouped.size(), clip, clip_dev, zero_accum, st);
+        }
+    }
     const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
     // 59 KB of tables per 512-thread CTA: two CTAs (32 warps) per SM
     static_assert(2 * (kAdamDynSmem + 1024) <= 228 * 1024, "two dynamic-codec Adam CTAs must fit an SM");
@@ -604,7 +631,7 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         int blocks = 0;
         for (int i = 0; i < cnt; ++i) {
             Param& p = *ps[off + i];
-            if (p.state_elems % 8 != 0) return AETH_ERR_UNSUPPORTED;
+            if (p.state_elems % 8 != 0) return AETH_ERR_UNSUPPORTED;  // filtered out by the caller
             a.accum[i] = p.accum;
             a.m8[i] = p.m8;
             a.v8[i] = p.v8;
@@ -678,6 +705,19 @@ int b2_weight_tile(aeth_galore_ctx* c, Param& p, const aeth_weight_ref* w, cudaS
     const float lr = b2_lr(cfg, r);
     const int has_decay = cfg.weight_decay > 0.0f;
     const float decay_mul = 1.0f - lr * cfg.weight_decay;
+    if (!b2_tma_shape(p)) {
+        const int kind = w ? w->kind : AETH_WEIGHT_NONE;
+        if (((int64_t)m * n) % 64 != 0) return AETH_ERR_UNSUPPORTED;
+        if (kind == AETH_WEIGHT_NONE && !(w && w->delta_out)) return AETH_OK;
+        const uint16_t* X = p.side == 2 ? p.nbuf : p.proj;
+        const uint16_t* Y = p.side == 2 ? p.proj : p.nbuf;
+        const int64_t blocks = (int64_t)m * n / 64;
+        small_apply_kernel<<<grid_for(blocks * 32, 256), 256, 0, st>>>(
+            X, Y, m, n, r, lr, decay_mul, has_decay, kind, w ? w->data : nullptr, w ? w->absmax : nullptr,
+            w ? w->prequant_out : nullptr, w ? w->delta_out : nullptr);
+        AETH_LAUNCH_CHECK();
+        return AETH_OK;
+    }
     // dW = X Y^T with X (m x r), Y (n x r), both K-major.
     TcOperand X = p.side == 2 ? TcOperand{p.nbuf, r} : TcOperand{p.proj, r};
     TcOperand Y = p.side == 2 ? TcOperand{p.proj, r} : TcOperand{p.nbuf, r};
@@ -1590,16 +1630,22 @@ int project_group(aeth_galore_ctx* ctx, int n, const int* idx, const void* const
     }
     std::vector<ProjJob> jobs;
     std::vector<int> ranks;
+    std::vector<char> small(n, 0);
     for (int i = 0; i < n; ++i) {
         Param& p = ctx->params[idx[i]];
-        if (std::find(ranks.begin(), ranks.end(), p.r) == ranks.end()) ranks.push_back(p.r);
+        small[i] = !b2_tma_shape(p) || (reinterpret_cast<uintptr_t>(grads[i]) & 15) != 0;
+        if (small[i]) {
+            AETH_TRY(b2_project_small(p, grads[i], grad_dtype, st));
+        } else if (std::find(ranks.begin(), ranks.end(), p.r) == ranks.end()) {
+            ranks.push_back(p.r);
+        }
         jobs.push_back(ProjJob{grads[i], p.projT, p.accum, p.m, p.n});
     }
     for (int r : ranks) {
         std::vector<ProjJob> grp;
         std::vector<int> members;
         for (int i = 0; i < n; ++i)
-            if (ctx->params[idx[i]].r == r) { grp.push_back(jobs[i]); members.push_back(i); }
+            if (!small[i] && ctx->params[idx[i]].r == r) { grp.push_back(jobs[i]); members.push_back(i); }
         int s = proj_grouped_launch(grp.data(), (int)grp.size(), r, st);
         if (s == AETH_ERR_UNSUPPORTED) {
             for (int i : members) AETH_TRY(b2_project_tile(ctx->params[idx[i]], jobs[i], st));

@@ -425,7 +425,7 @@ class GaLoreOptimizer:
         return (C.c_int * len(keys))(*[self._key(*k)[0] for k in keys])
 
     @staticmethod
-    def _weight_refs(weights):
+    def _weight_refs(weights, prequant_outs=None):
         if weights is None:
             return None
         wrefs = (L.WeightRef * len(weights))()
@@ -436,6 +436,8 @@ class GaLoreOptimizer:
                 wrefs[i].kind = L.WEIGHT_NONE
             else:
                 wrefs[i].kind, wrefs[i].data = L.WEIGHT_F32, w.data_ptr()
+            if prequant_outs is not None and prequant_outs[i] is not None:
+                wrefs[i].prequant_out = prequant_outs[i].data_ptr()
         return wrefs
 
     def _hook(self, sq_hook):
@@ -475,17 +477,20 @@ class GaLoreOptimizer:
         L.check(self._lib.aeth_galore_project_layer(self._ctx, n, self._indices(keys), gp, _DTYPES[grads[0].dtype],
                                                     C.c_void_p(_stream_handle())), "aeth_galore_project_layer")
 
-    def finish_step(self, keys, weights=None, sq_hook=None, clip_out: torch.Tensor | None = None):
+    def finish_step(self, keys, weights=None, sq_hook=None, clip_out: torch.Tensor | None = None,
+                    prequant_outs=None):
         """The exact global-norm clip over every listed parameter (all that this
         GPU owns) in one launch, then Adam and the weight write for all of them
-        (hook.rs:115-203 on the device).  Returns the device clip coefficient."""
+        (hook.rs:115-203 on the device).  Returns the device clip coefficient.
+        `prequant_outs` (optional, one fp32 tensor or None per weight) receive
+        the updated weights before NF4 requantisation."""
         n = len(keys)
         clip = clip_out if clip_out is not None else torch.empty(1, dtype=torch.float32,
                                                                  device=f"cuda:{self.device}")
         hook = self._hook(sq_hook)
-        L.check(self._lib.aeth_galore_finish_step(self._ctx, n, self._indices(keys), self._weight_refs(weights), hook,
-                                                  None, _ptr(clip), C.c_void_p(_stream_handle())),
-                "aeth_galore_finish_step")
+        L.check(self._lib.aeth_galore_finish_step(self._ctx, n, self._indices(keys),
+                                                  self._weight_refs(weights, prequant_outs), hook, None, _ptr(clip),
+                                                  C.c_void_p(_stream_handle())), "aeth_galore_finish_step")
         return clip
 
     # ---- per-phase device timing of step_layer ----
