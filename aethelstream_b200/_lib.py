@@ -30,6 +30,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 MODE_REF, MODE_B200 = 0, 1
 CODEC_PER_TENSOR, CODEC_BLOCK_LINEAR, CODEC_BLOCK_DYNAMIC = 0, 1, 2
 WEIGHT_NONE, WEIGHT_F32, WEIGHT_NF4 = 0, 1, 2
+REF_GEMM_EXACT, REF_GEMM_SPLIT3 = 0, 1
 
 
 class GaloreConfig(C.Structure):
@@ -40,6 +41,7 @@ class GaloreConfig(C.Structure):
         ("weight_decay", C.c_float), ("scale_lr_by_rank", C.c_int), ("max_grad_norm", C.c_float),
         ("state_codec", C.c_int), ("state_block", C.c_int), ("init_projectors", C.c_int),
         ("svd_refresh", C.c_int), ("power_iters", C.c_int), ("grad_dtype", C.c_int),
+        ("ref_gemm", C.c_int),
     ]
 
 

@@ -19,6 +19,7 @@
 #include "gemm_tc.cuh"
 #include "layer_launch.cuh"
 #include "small_rank.cuh"
+#include "split_gemm.cuh"
 #include "lomo.cuh"
 #include "nf4.cuh"
 #include "rsvd.cuh"
@@ -300,6 +301,9 @@ struct aeth_galore_ctx {
     // by the parameters: their projections run one after another on the stream
     uint16_t* gsplit = nullptr;
     int64_t gsplit_elems = 0;
+    // REF mode on the tensor cores (config.ref_gemm): the bf16 terms of one
+    // product's operands, shared by the parameters (one stream)
+    uint16_t* rsplit = nullptr;
     // global clip over several GPUs through peer memory (aeth_galore_set_clip_group)
     ClipGroup group;
     PeerSlot* own_slots = nullptr;      // 2 x world entries, cudaMalloc'd (exported by IPC handle)
@@ -415,7 +419,25 @@ int sqnorm_into(aeth_galore_ctx* c, Param& p, double* out_dev, cudaStream_t st) 
 }
 
 // ---- REF mode -------------------------------------------------------------
-int ref_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t st) {
+// Whether REF mode's products of this parameter run on the tensor cores
+// (config.ref_gemm; every pitch a multiple of 8 elements for TMA).
+bool ref_split(const aeth_galore_ctx* c, const Param& p) {
+    return c->cfg.ref_gemm == AETH_REF_GEMM_SPLIT3 && p.r % 8 == 0 && p.m % 8 == 0 && p.n % 8 == 0;
+}
+
+// dW = fl(lr D) elementwise (optimizer.rs:337-340, weight_delta *= lr); with
+// w: w = fl(w - dW); delta_out and scaled_out (either may be null) get dW.
+__global__ void ref_delta_apply_kernel(const float* __restrict__ d, int64_t n, float lr, float* __restrict__ w,
+                                       float* __restrict__ delta_out, float* __restrict__ scaled_out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float dw = __fmul_rn(d[i], lr);
+        if (w) w[i] = __fsub_rn(w[i], dw);
+        if (delta_out) delta_out[i] = dw;
+        if (scaled_out) scaled_out[i] = dw;
+    }
+}
+
+int ref_project_accumulate(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, cudaStream_t st) {
     const float* g = static_cast<const float*>(grad);
     if (dtype != AETH_DTYPE_F32) {
         to_f32_kernel<<<grid_for((int64_t)p.m * p.n, 256), 256, 0, st>>>(grad, dtype, (int64_t)p.m * p.n, p.gtmp);
@@ -423,6 +445,13 @@ int ref_project_accumulate(Param& p, const void* grad, int dtype, cudaStream_t s
         g = p.gtmp;
     }
     const int m = p.m, n = p.n, r = p.r;
+    if (ref_split(c, p)) {
+        // Temp(r x n) = P^T G: A = P^T (P read MN-major), B = G (MN-major), K = m
+        AETH_TRY(split3_gemm(F32Op{p.P, m, r, true}, F32Op{g, m, n, true}, p.temp, n, r, n, m, false, c->rsplit, st));
+        // R += Temp Q: A = Temp (K-major), B = Q (MN-major), K = n
+        return split3_gemm(F32Op{p.temp, r, n, false}, F32Op{p.Q, n, r, true}, p.accum, r, r, r, n, true, c->rsplit,
+                           st);
+    }
     // project.rs:36-46: Temp(r x n) = P^T G, sum over k of p[k*r+i] * g[k*n+j].
     AETH_TRY(simt_gemm_exact(p.P, 1, r, g, n, 1, p.temp, n, r, n, m, SIMT_STORE, 1.0f, nullptr, st));
     // project.rs:46 + adamw.rs:91-96: accum += Temp Q.
@@ -438,9 +467,31 @@ int ref_apply(aeth_galore_ctx* c, Param& p, float clip, const float* clip_dev, c
                                         (int64_t)r * r, clip, clip_dev, cfg.beta1, cfg.beta2, cfg.eps);
     AETH_LAUNCH_CHECK();
     const float lr = cfg.scale_lr_by_rank ? cfg.lr / (float)(r < 1 ? 1 : r) : cfg.lr;  // adamw.rs:37-43
+    const int kind = w ? w->kind : AETH_WEIGHT_NONE;
+    if (ref_split(c, p)) {
+        // project.rs:50-58 on the tensor cores: Temp(m x r) = P N (A = P K-major,
+        // B = N MN-major, K = r); D(m x n) = Temp Q^T (B(k, j) = Q[j][k]: K-major,
+        // K = r) into dtmp; then dW = lr D and the weight write elementwise.
+        AETH_TRY(split3_gemm(F32Op{p.P, m, r, false}, F32Op{p.normalized, r, r, true}, p.temp, r, m, r, r, false,
+                             c->rsplit, st));
+        AETH_TRY(split3_gemm(F32Op{p.temp, m, r, false}, F32Op{p.Q, n, r, false}, p.dtmp, n, m, n, r, false,
+                             c->rsplit, st));
+        const int64_t mn = (int64_t)m * n;
+        float* wf = kind == AETH_WEIGHT_F32 ? static_cast<float*>(w->data) : nullptr;
+        float* delta = w ? w->delta_out : nullptr;
+        ref_delta_apply_kernel<<<grid_for(mn, 256), 256, 0, st>>>(p.dtmp, mn, lr, wf, delta,
+                                                                 kind == AETH_WEIGHT_NF4 ? p.dtmp : nullptr);
+        AETH_LAUNCH_CHECK();
+        if (kind == AETH_WEIGHT_NF4) {
+            if (mn % 64 != 0) return AETH_ERR_SHAPE;
+            nf4_apply_delta_kernel<<<grid_for(mn / 64, 128), 128, 0, st>>>(static_cast<uint8_t*>(w->data), w->absmax,
+                                                                          p.dtmp, mn / 64, w->prequant_out);
+            AETH_LAUNCH_CHECK();
+        }
+        return AETH_OK;
+    }
     // project.rs:50-58: Temp(m x r) = P N; dW = Temp Q^T; dW *= lr.
     AETH_TRY(simt_gemm_exact(p.P, r, 1, p.normalized, r, 1, p.temp, r, m, r, r, SIMT_STORE, 1.0f, nullptr, st));
-    const int kind = w ? w->kind : AETH_WEIGHT_NONE;
     if (kind == AETH_WEIGHT_F32) {
         AETH_TRY(simt_gemm_exact(p.temp, r, 1, p.Q, 1, r, static_cast<float*>(w->data), n, m, n, r, SIMT_SUB_SCALED,
                                  lr, w->delta_out, st));
@@ -1099,6 +1150,7 @@ void aeth_galore_config_default(aeth_galore_config* c) {
     c->svd_refresh = 1;  // the reference captures at step 1 and every switch_interval steps
     c->power_iters = 0;  // RandomizedSvdConfig::default (randomized_svd.rs:19-28), never used by the reference
     c->grad_dtype = AETH_DTYPE_BF16;
+    c->ref_gemm = AETH_REF_GEMM_EXACT;
 }
 
 int aeth_galore_destroy(aeth_galore_ctx* ctx) {
@@ -1128,6 +1180,7 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
         return set_err(AETH_ERR_CONFIG);
     if (cfg->grad_dtype != AETH_DTYPE_F32 && cfg->grad_dtype != AETH_DTYPE_F16 && cfg->grad_dtype != AETH_DTYPE_BF16)
         return set_err(AETH_ERR_CONFIG);
+    if (cfg->ref_gemm != AETH_REF_GEMM_EXACT && cfg->ref_gemm != AETH_REF_GEMM_SPLIT3) return set_err(AETH_ERR_CONFIG);
     DeviceGuard g(device);
     aeth_galore_ctx* c = new aeth_galore_ctx();
     c->cfg = *cfg;
@@ -1228,6 +1281,13 @@ int aeth_galore_create(const aeth_galore_config* cfg, const aeth_param_spec* spe
         if ((st = ctx_alloc(c, &c->gsplit, split_need)) != AETH_OK) return fail(st);
         c->gsplit_elems = split_need;
     }
+    if (cfg->mode == AETH_MODE_REF && cfg->ref_gemm == AETH_REF_GEMM_SPLIT3) {
+        // three terms of each operand of the largest product, P^T G (r m + m n)
+        int64_t need = 0;
+        for (const Param& p : c->params)
+            need = std::max(need, 3 * ((int64_t)p.r * std::max(p.m, p.n) + (int64_t)p.m * p.n + (int64_t)p.r * p.r));
+        if ((st = ctx_alloc(c, &c->rsplit, need)) != AETH_OK) return fail(st);
+    }
     if (cudaMemset(c->sq_ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
         cudaMemset(c->work, 0, 2 * sizeof(unsigned int)) != cudaSuccess)
         return fail(AETH_ERR_CONFIG);
@@ -1267,7 +1327,7 @@ int aeth_galore_project_accumulate(aeth_galore_ctx* ctx, int idx, const void* gr
     Param& p = ctx->params[idx];
     cudaStream_t st = to_stream(stream);
     AETH_TRY(set_err(capture_if_due(ctx, p, grad, grad_dtype, st)));
-    if (ctx->cfg.mode == AETH_MODE_REF) return set_err(ref_project_accumulate(p, grad, grad_dtype, st));
+    if (ctx->cfg.mode == AETH_MODE_REF) return set_err(ref_project_accumulate(ctx, p, grad, grad_dtype, st));
     return set_err(b2_project_accumulate(ctx, p, grad, grad_dtype, st));
 }
 
@@ -1618,7 +1678,7 @@ int project_group(aeth_galore_ctx* ctx, int n, const int* idx, const void* const
                   cudaStream_t st) {
     for (int i = 0; i < n; ++i) AETH_TRY(capture_if_due(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st));
     if (ctx->cfg.mode == AETH_MODE_REF) {
-        for (int i = 0; i < n; ++i) AETH_TRY(ref_project_accumulate(ctx->params[idx[i]], grads[i], grad_dtype, st));
+        for (int i = 0; i < n; ++i) AETH_TRY(ref_project_accumulate(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st));
         return AETH_OK;
     }
     if (grad_dtype != AETH_DTYPE_BF16) {

@@ -83,6 +83,9 @@ class GaLoreConfig:
     # B200: dtype of the gradients ("bf16", "f32", "f16"); f32 / f16 set up the
     # exact split path's buffers at construction, so no step allocates
     grad_dtype: str = "bf16"
+    # REF: "exact" (the reference's loop order, bit for bit, CUDA cores) or
+    # "split3" (tensor cores on exact bf16 terms, fp32 accuracy)
+    ref_gemm: str = "exact"
 
     def to_c(self) -> L.GaloreConfig:
         c = L.GaloreConfig()
@@ -107,6 +110,7 @@ class GaLoreConfig:
         c.svd_refresh = int(self.svd_refresh)
         c.power_iters = self.power_iters
         c.grad_dtype = {"f32": L.DTYPE_F32, "f16": L.DTYPE_F16, "bf16": L.DTYPE_BF16}[self.grad_dtype]
+        c.ref_gemm = {"exact": L.REF_GEMM_EXACT, "split3": L.REF_GEMM_SPLIT3}[self.ref_gemm]
         return c
 
 

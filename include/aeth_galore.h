@@ -143,7 +143,19 @@ typedef struct {
     int power_iters;          /* 0 (the reference); > 0 adds subspace iterations to the refresh */
     int grad_dtype;           /* B200: the gradients' aeth_dtype (BF16).  F32 / F16 allocate the split
                                  path's buffers at create, so no step allocates */
+    int ref_gemm;             /* REF: AETH_REF_GEMM_EXACT (the reference's loop order, bit for bit) or
+                                 AETH_REF_GEMM_SPLIT3 (tensor cores, fp32 accuracy) */
 } aeth_galore_config;
+
+/* REF mode's projection and back-projection (galore/src/project.rs:33-58):
+ *   EXACT:  CUDA-core GEMMs that sum each output in the reference's loop order
+ *           with separately rounded multiply and add -- bit-identical results.
+ *   SPLIT3: tcgen05 GEMMs; each fp32 operand is split exactly into three bf16
+ *           terms and the six term products above 2^-24 are summed in fp32 --
+ *           within about 1e-6 of the reference (its own rounding error), not
+ *           bit-identical.  Parameters whose m, n or rank is not a multiple of
+ *           8 stay on the EXACT path. */
+enum { AETH_REF_GEMM_EXACT = 0, AETH_REF_GEMM_SPLIT3 = 1 };
 
 typedef struct {
     uint32_t layer_idx;

@@ -173,3 +173,59 @@ def test_ref_full_layer_nine_parameters(oracle):
         assert host(gms)[0] == sm and host(gvs)[0] == sv, nm
         assert np.array_equal(host(t), (w - wd).astype(np.float32)), nm
     opt.close()
+
+
+@pytest.mark.parametrize("m,n,r", [(256, 384, 32), (512, 256, 64)])
+def test_ref_split3_small(oracle, m, n, r):
+    """REF mode on the tensor cores (exact bf16 terms): accumulator and weight
+    delta within 1e-6 of the reference's loops; the INT8 state, fed the GPU's
+    accumulator, bit-exact."""
+    specs = [(1, "d_wq", m, n, r)]
+    opt = _opt("ref", specs, ref_gemm="split3")
+    rng = np.random.default_rng(m + 3 * n)
+    g = (rng.standard_normal((m, n)) * 1e-2).astype(np.float32)
+    opt.project_and_accumulate(dev(g), 1, "d_wq")
+    acc = host(opt.get_accum(1, "d_wq"))
+    p = oracle.init_random_projection(m, r, 17)
+    q = oracle.init_random_projection(n, r, 31)
+    acc_ref = oracle.project_forward(g, p, q, m, n, r).ravel()
+    assert rel_fro(acc, acc_ref) < 1e-6, rel_fro(acc, acc_ref)
+    opt.apply_update(1, "d_wq", 0.7)
+    delta = host(opt.take_weight_delta(1, "d_wq"))
+    wd, _, m8, v8, sm, sv = oracle.galore_apply_update(acc, p, q, np.zeros(r * r, np.int8), np.zeros(r * r, np.int8),
+                                                       1.0, 1.0, m, n, r, 0.7)
+    gm8, gv8, gms, gvs = opt.get_state(1, "d_wq")
+    assert np.array_equal(host(gm8), m8) and np.array_equal(host(gv8), v8)
+    assert host(gms)[0] == sm and host(gvs)[0] == sv
+    assert rel_fro(delta, wd) < 1e-6, rel_fro(delta, wd)
+    opt.close()
+
+
+def test_ref_split3_c1_fp32(oracle):
+    """C1's shape in REF mode (two-sided, fp32 gradient) on the tensor cores:
+    the projection within 1e-5 of oracle.project_forward, the INT8 state
+    bit-exact on the GPU's accumulator, and the fp32 weight after the update
+    within 1e-5 of oracle.galore_apply_update's."""
+    m = n = 4096
+    r = 128
+    opt = _opt("ref", [(0, "d_wq", m, n, r)], ref_gemm="split3")
+    g = (torch.randn(m, n, generator=torch.Generator().manual_seed(1)) * 1e-3).numpy()
+    w = (torch.randn(m, n, generator=torch.Generator().manual_seed(0)) * 0.02).numpy()
+    tw = dev(w)
+    opt.project_and_accumulate(dev(g), 0, "d_wq")
+    acc = host(opt.get_accum(0, "d_wq"))
+    p = oracle.init_random_projection(m, r, 0)
+    q = oracle.init_random_projection(n, r, 0)
+    acc_ref = oracle.project_forward(g, p, q, m, n, r).ravel()
+    assert rel_fro(acc, acc_ref) < 1e-5, rel_fro(acc, acc_ref)
+    sq = opt.lowrank_grad_sqnorm(0, "d_wq")
+    clip = float(oracle.clip_coeff(sq, 1.0))
+    opt.apply_update(0, "d_wq", clip, weight=tw)
+    wd, _, m8, v8, sm, sv = oracle.galore_apply_update(acc, p, q, np.zeros(r * r, np.int8), np.zeros(r * r, np.int8),
+                                                       1.0, 1.0, m, n, r, clip)
+    gm8, gv8, gms, gvs = opt.get_state(0, "d_wq")
+    assert np.array_equal(host(gm8), m8) and np.array_equal(host(gv8), v8)
+    assert host(gms)[0] == sm and host(gvs)[0] == sv
+    w_ref = (w - wd).astype(np.float32)
+    assert rel_fro(host(tw) - w, w_ref - w) < 1e-5
+    opt.close()
