@@ -89,6 +89,7 @@ SIGNATURES = {
     "aeth_galore_save_state": (_i, [_vp, C.c_char_p, _vp]),
     "aeth_galore_load_state": (_i, [_vp, C.c_char_p, _vp]),
     "aeth_randomized_svd": (_i, [_vp, _i, _i, _i, _i, _i, _u64, _vp, _vp, _vp]),
+    "aeth_randomized_svd_ex": (_i, [_vp, _i, _i, _i, _i, _i, _i, _u64, _i, _vp, _vp, _vp]),
     "aeth_rsvd_omega": (_i, [_u64, _i64, _vp, _vp]),
     "aeth_rsvd_jacobi": (_i, [_vp, _i, _vp, _vp]),
     "aeth_galore_step_count": (_u64, [_vp]),
@@ -96,6 +97,8 @@ SIGNATURES = {
                               _vp]),
     "aeth_galore_project_layer": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(_vp), _i, _vp]),
     "aeth_galore_finish_step": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(WeightRef), SQ_HOOK, _vp, _vp, _vp]),
+    "aeth_galore_refresh_layer": (_i, [_vp, _i, C.POINTER(_i), C.POINTER(_vp), _i, _vp]),
+    "aeth_galore_projector_buffer": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_i), C.POINTER(_i)]),
     "aeth_galore_set_phase_timing": (_i, [_vp, _i]),
     "aeth_galore_phase_times": (_i, [_vp, C.POINTER(_d), C.POINTER(_i)]),
     "aeth_galore_clip_handle": (_i, [_vp, _i, _vp]),

@@ -281,6 +281,11 @@ struct Param {
     // subspace refresh: full gradient captured at refresh steps (m x n f32, lazy)
     float* capture = nullptr;
     bool captured = false;
+    // streamed refresh (aeth_galore_refresh_layer): the new bf16 projector of
+    // the parameter's side, installed by the next notify_step
+    uint16_t* pend_proj = nullptr;
+    uint16_t* pend_projT = nullptr;
+    bool pending = false;
 };
 
 struct aeth_galore_ctx {
@@ -836,8 +841,12 @@ int refresh_param(aeth_galore_ctx* c, Param& p, uint64_t seed, cudaStream_t st) 
     if (e == cudaSuccess && want_q)
         e = cudaMallocAsync(reinterpret_cast<void**>(&tq), sizeof(float) * (size_t)p.n * p.r, st);
     if (e != cudaSuccess) status = (int)e;
+    // REF mode with the exact GEMMs keeps the reference's f32 loop order;
+    // otherwise the products run on the tensor cores
+    const bool fast = !ref || c->cfg.ref_gemm == AETH_REF_GEMM_SPLIT3;
     if (status == AETH_OK)
-        status = rsvd_device(p.capture, p.m, p.n, p.r, c->cfg.oversampling, c->cfg.power_iters, seed, tp, tq, st);
+        status = rsvd_device(p.capture, false, p.m, p.n, p.r, c->cfg.oversampling, c->cfg.power_iters, seed, fast,
+                             tp, tq, st);
     if (status == AETH_OK) {
         if (ref) {
             e = cudaMemcpyAsync(p.P, tp, sizeof(float) * (size_t)p.m * p.r, cudaMemcpyDeviceToDevice, st);
@@ -860,11 +869,75 @@ int refresh_param(aeth_galore_ctx* c, Param& p, uint64_t seed, cudaStream_t st) 
     return status;
 }
 
+// New projector of one B200 parameter from this step's gradient, kept aside
+// (pend_proj / pend_projT) until notify_step installs it: the step's own
+// back-projection still uses the projector its accumulator was projected
+// with, as the reference's refresh in notify_step after the update does
+// (optimizer.rs:208-246, 373-398).  Seed of the step in progress.
+int refresh_from_grad(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, cudaStream_t st) {
+    const int s_dim = p.side == 1 ? p.m : p.n;
+    const size_t pe = (size_t)s_dim * p.r;
+    if (!p.pend_proj) {
+        AETH_TRY(ctx_alloc(c, &p.pend_proj, (int64_t)pe));
+        AETH_TRY(ctx_alloc(c, &p.pend_projT, (int64_t)pe));
+    }
+    const uint64_t seed = (c->step + 1) * 0x9E3779B9ull;  // the step notify_step will record
+    float* tproj = nullptr;
+    float* gf = nullptr;
+    const int64_t mn = (int64_t)p.m * p.n;
+    AETH_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tproj), sizeof(float) * pe, st));
+    int status = AETH_OK;
+    const void* g = grad;
+    if (dtype == AETH_DTYPE_F16) {  // widened exactly; the refresh reads bf16 or fp32
+        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&gf), sizeof(float) * (size_t)mn, st);
+        if (e != cudaSuccess) status = (int)e;
+        else {
+            to_f32_kernel<<<grid_for(mn, 256), 256, 0, st>>>(grad, dtype, mn, gf);
+            g = gf;
+        }
+    }
+    if (status == AETH_OK)
+        status = rsvd_device(g, dtype == AETH_DTYPE_BF16, p.m, p.n, p.r, c->cfg.oversampling, c->cfg.power_iters,
+                             seed, true, p.side == 1 ? tproj : nullptr, p.side == 2 ? tproj : nullptr, st);
+    if (status == AETH_OK) {
+        proj_to_bf16_kernel<<<grid_for((int64_t)pe, 256), 256, 0, st>>>(tproj, s_dim, p.r, p.pend_proj,
+                                                                       p.pend_projT);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) status = (int)e;
+    }
+    cudaFreeAsync(tproj, st);
+    if (gf) cudaFreeAsync(gf, st);
+    if (status == AETH_OK) p.pending = true;
+    return status;
+}
+
+// Installs the pending projectors (stable buffers, so recorded graphs stay
+// valid) and resets their Adam state.  Returns whether any was installed.
+int install_pending(aeth_galore_ctx* c, cudaStream_t st, bool* any) {
+    *any = false;
+    for (Param& p : c->params) {
+        if (!p.pending) continue;
+        const size_t bytes = sizeof(uint16_t) * (size_t)(p.side == 1 ? p.m : p.n) * p.r;
+        AETH_CUDA(cudaMemcpyAsync(p.proj, p.pend_proj, bytes, cudaMemcpyDeviceToDevice, st));
+        AETH_CUDA(cudaMemcpyAsync(p.projT, p.pend_projT, bytes, cudaMemcpyDeviceToDevice, st));
+        AETH_TRY(sync_projk(p, st));
+        AETH_TRY(reset_state(c, p, st));
+        p.pending = false;
+        *any = true;
+    }
+    return AETH_OK;
+}
+
 int notify_step_on(aeth_galore_ctx* c, uint64_t step, cudaStream_t st) {
     c->step = step;
+    bool installed = false;
+    AETH_TRY(install_pending(c, st, &installed));
     bool any = false;
     for (Param& p : c->params) any = any || p.captured;
-    if (!any) return AETH_OK;
+    if (!any) {
+        if (installed) ++c->version;
+        return AETH_OK;
+    }
     const uint64_t seed = step * 0x9E3779B9ull;  // wrapping_mul (optimizer.rs:216-221)
     int status = AETH_OK;
     for (Param& p : c->params) {
@@ -1622,7 +1695,16 @@ int aeth_galore_load_state(aeth_galore_ctx* ctx, const char* path, aeth_stream_t
 int aeth_randomized_svd(const float* g, int m, int n, int rank, int oversampling, int power_iters, uint64_t seed,
                         float* p_out, float* q_out, aeth_stream_t stream) {
     if (!g || m <= 0 || n <= 0) return set_err(AETH_ERR_ARG);
-    return set_err(rsvd_device(g, m, n, rank, oversampling, power_iters, seed, p_out, q_out, to_stream(stream)));
+    return set_err(
+        rsvd_device(g, false, m, n, rank, oversampling, power_iters, seed, false, p_out, q_out, to_stream(stream)));
+}
+
+int aeth_randomized_svd_ex(const void* g, int g_dtype, int m, int n, int rank, int oversampling, int power_iters,
+                           uint64_t seed, int fast, float* p_out, float* q_out, aeth_stream_t stream) {
+    if (!g || m <= 0 || n <= 0) return set_err(AETH_ERR_ARG);
+    if (g_dtype != AETH_DTYPE_F32 && g_dtype != AETH_DTYPE_BF16) return set_err(AETH_ERR_ARG);
+    return set_err(rsvd_device(g, g_dtype == AETH_DTYPE_BF16, m, n, rank, oversampling, power_iters, seed, fast != 0,
+                               p_out, q_out, to_stream(stream)));
 }
 
 int aeth_rsvd_omega(uint64_t seed, int64_t count, float* out, aeth_stream_t stream) {
@@ -1837,6 +1919,34 @@ int aeth_galore_project_layer(aeth_galore_ctx* ctx, int n, const int* idx, const
     AETH_TRY(set_err(project_group(ctx, n, idx, grads, grad_dtype, st)));
     AETH_TRY(pm.mark(st, -1));
     pm.commit(0);
+    return AETH_OK;
+}
+
+int aeth_galore_refresh_layer(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads,
+                              int grad_dtype, aeth_stream_t stream) {
+    AETH_TRY(set_err(check_list(ctx, n, idx)));
+    if (!grads) return set_err(AETH_ERR_ARG);
+    if (ctx->cfg.mode != AETH_MODE_B200) return set_err(AETH_ERR_CONFIG);
+    if (grad_dtype != AETH_DTYPE_F32 && grad_dtype != AETH_DTYPE_F16 && grad_dtype != AETH_DTYPE_BF16)
+        return set_err(AETH_ERR_ARG);
+    for (int i = 0; i < n; ++i)
+        if (!grads[i]) return set_err(AETH_ERR_ARG);
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = to_stream(stream);
+    bool capturing = false;
+    AETH_TRY(set_err(stream_capturing(st, &capturing)));
+    if (capturing) return set_err(AETH_ERR_UNSUPPORTED);
+    for (int i = 0; i < n; ++i) AETH_TRY(set_err(refresh_from_grad(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st)));
+    return AETH_OK;
+}
+
+int aeth_galore_projector_buffer(aeth_galore_ctx* ctx, int idx, void** proj_bf16, int* rows, int* cols) {
+    AETH_TRY(check_idx(ctx, idx));
+    if (!proj_bf16 || ctx->cfg.mode != AETH_MODE_B200) return set_err(AETH_ERR_ARG);
+    const Param& p = ctx->params[idx];
+    *proj_bf16 = p.proj;
+    if (rows) *rows = p.side == 1 ? p.m : p.n;
+    if (cols) *cols = p.r;
     return AETH_OK;
 }
 

@@ -197,6 +197,8 @@ struct TcLayout {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kOperandBytes = STAGES * kStageBytes;
     static constexpr int kBarrierBytes = 256;
+    // TMEM is allocated in powers of two of at least 32 columns
+    static constexpr int kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : BN <= 256 ? 256 : 512;
 };
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
@@ -225,7 +227,7 @@ __global__ void __launch_bounds__(192, 1)
         *abort = 0;
         fence_mbar_init();
     }
-    if (warp == 0) { tmem_alloc(tmem_slot, BN); tmem_relinquish(); }
+    if (warp == 0) { tmem_alloc(tmem_slot, L::kTmemCols); tmem_relinquish(); }
     epi.init_shared(eshared, threadIdx.x, blockDim.x);
     tc_fence_before();
     __syncthreads();
@@ -298,7 +300,7 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, L::kTmemCols);
     }
 }
 

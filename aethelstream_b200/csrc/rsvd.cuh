@@ -30,6 +30,7 @@
 #pragma once
 #include "common.cuh"
 #include "gemm_simt.cuh"
+#include "split_gemm.cuh"
 
 namespace aeth {
 
@@ -353,6 +354,11 @@ __global__ void __launch_bounds__(1024) jacobi50_kernel(float* __restrict__ mat,
     }
 }
 
+__global__ void bf16_to_f32_rsvd_kernel(const uint16_t* __restrict__ x, int64_t n, float* __restrict__ y) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = bf16_bits_to_f32(x[i]);
+}
+
 // ---------------------------------------------------------------------------
 // Host orchestration.
 // ---------------------------------------------------------------------------
@@ -363,6 +369,7 @@ struct RsvdWork {
     float* b = nullptr;      // l x n
     float* bbt = nullptr;    // l x l
     float* u = nullptr;      // l x l
+    float* ur = nullptr;     // l x r: the first r columns of u
     double* gram = nullptr;  // l x l
     double* linv = nullptr;  // l x l
     uint64_t* jump = nullptr;
@@ -384,16 +391,72 @@ inline int cholqr2(float* x, float* tmp, int rows, int cols, RsvdWork& w, cudaSt
     return AETH_OK;
 }
 
-// randomized_svd_projections on the device.  g: m x n f32; p_out (m x r) and
-// q_out (n x r) f32, either may be null.  Synchronises `st` once to read the
-// factorisation status.  Returns AETH_ERR_CONFIG for an invalid rank or
+// The tensor-core refresh: every product of randomized_svd_projections on
+// tcgen05 GEMMs over exact bf16 terms (split_gemm.cuh; G is its own single
+// term when it is bf16), the orthonormal bases by Cholesky QR with f64 Gram
+// matrices, the reference's Jacobi.  fp32-accurate products, not the
+// reference's summation order.  Needs every pitch a multiple of 8 elements.
+inline bool rsvd_fast_shape(int m, int n, int r, int l) { return m % 8 == 0 && n % 8 == 0 && r % 8 == 0 && l % 8 == 0; }
+
+inline int rsvd_fast(const void* g, bool g_bf16, int m, int n, int r, int l, int power_iters, RsvdWork& w,
+                     uint16_t* gt, uint16_t* at, uint16_t* bt, uint16_t* ut, float* p_out, float* q_out,
+                     cudaStream_t st) {
+    const int64_t mn = (int64_t)m * n;
+    if (!g_bf16) AETH_TRY(split3_terms(static_cast<const float*>(g), mn, gt, st));
+    const uint16_t* gterms = g_bf16 ? static_cast<const uint16_t*>(g) : gt;
+    const int gk = g_bf16 ? 1 : 3;
+    const TermOp G_k{gterms, gk, mn, n, false};   // G read K-major (A = G, K = n)
+    const TermOp G_mn{gterms, gk, mn, n, true};   // G read MN-major (A = G^T or B = G, K = m)
+    // 2. Y = G Omega (m x l)
+    AETH_TRY(split3_terms(w.omega, (int64_t)n * l, at, st));
+    AETH_TRY(terms_gemm(G_k, TermOp{at, 3, (int64_t)n * l, l, true}, w.y, l, m, l, n, false, st));
+    // 3. Q^ = orthonormal basis of Y, optional power iterations
+    AETH_TRY(cholqr2(w.y, w.y2, m, l, w, st));
+    for (int it = 0; it < power_iters; ++it) {
+        // Z = G^T Q^ (n x l), orthonormalised; Y = G Z, orthonormalised
+        AETH_TRY(split3_terms(w.y, (int64_t)m * l, at, st));
+        AETH_TRY(terms_gemm(G_mn, TermOp{at, 3, (int64_t)m * l, l, true}, w.y2, l, n, l, m, false, st));
+        AETH_TRY(cholqr2(w.y2, w.omega, n, l, w, st));
+        AETH_TRY(split3_terms(w.y2, (int64_t)n * l, at, st));
+        AETH_TRY(terms_gemm(G_k, TermOp{at, 3, (int64_t)n * l, l, true}, w.y, l, m, l, n, false, st));
+        AETH_TRY(cholqr2(w.y, w.y2, m, l, w, st));
+    }
+    // 4. B = Q^T G (l x n): A = Q^T (Q^ read MN-major), B = G (MN-major), K = m
+    AETH_TRY(split3_terms(w.y, (int64_t)m * l, at, st));
+    AETH_TRY(terms_gemm(TermOp{at, 3, (int64_t)m * l, l, true}, G_mn, w.b, n, l, n, m, false, st));
+    // 5. B B^T (l x l), K = n: both operands B read K-major; 6. Jacobi
+    AETH_TRY(split3_terms(w.b, (int64_t)l * n, bt, st));
+    const TermOp B_k{bt, 3, (int64_t)l * n, n, false};
+    AETH_TRY(terms_gemm(B_k, B_k, w.bbt, l, l, l, n, false, st));
+    jacobi50_kernel<<<1, 1024, 0, st>>>(w.bbt, l, w.u);
+    AETH_LAUNCH_CHECK();
+    // U[:, :r] compact (l x r), as terms
+    AETH_CUDA(cudaMemcpy2DAsync(w.ur, sizeof(float) * r, w.u, sizeof(float) * l, sizeof(float) * r, l,
+                                cudaMemcpyDeviceToDevice, st));
+    AETH_TRY(split3_terms(w.ur, (int64_t)l * r, ut, st));
+    const TermOp U_mn{ut, 3, (int64_t)l * r, r, true};
+    // 7. P = Q^ U[:, :r] (A = Q^ K-major, K = l)
+    if (p_out) AETH_TRY(terms_gemm(TermOp{at, 3, (int64_t)m * l, l, false}, U_mn, p_out, r, m, r, l, false, st));
+    // 8. Q = B^T U[:, :r] (A = B^T: B read MN-major, K = l)
+    if (q_out) AETH_TRY(terms_gemm(TermOp{bt, 3, (int64_t)l * n, n, true}, U_mn, q_out, r, n, r, l, false, st));
+    return AETH_OK;
+}
+
+// randomized_svd_projections on the device.  g: m x n, f32 or (g_bf16) bf16;
+// p_out (m x r) and q_out (n x r) f32, either may be null.  fast selects the
+// tensor-core products (rsvd_fast) when the shape allows; otherwise the
+// exact-order CUDA-core GEMM reproduces the reference's f32 loops on equal
+// inputs (a bf16 g is widened exactly first).  Synchronises `st` once to read
+// the factorisation status.  Returns AETH_ERR_CONFIG for an invalid rank or
 // oversampling, AETH_ERR_LINALG for a rank-deficient sketch.
-inline int rsvd_device(const float* g, int m, int n, int r, int oversampling, int power_iters, uint64_t seed,
-                       float* p_out, float* q_out, cudaStream_t st) {
+inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int oversampling, int power_iters,
+                       uint64_t seed, bool fast, float* p_out, float* q_out, cudaStream_t st) {
     const int l = r + oversampling;
     if (r <= 0 || oversampling < 0 || power_iters < 0 || l > (m < n ? m : n)) return AETH_ERR_CONFIG;
+    fast = fast && rsvd_fast_shape(m, n, r, l);
     RsvdWork w;
     const size_t big = (size_t)(m > n ? m : n) * l;
+    const int64_t mn = (int64_t)m * n;
     std::vector<void*> allocs;
     auto alloc = [&](void** p, size_t bytes) -> int {
         cudaError_t e = cudaMallocAsync(p, bytes, st);
@@ -402,57 +465,86 @@ inline int rsvd_device(const float* g, int m, int n, int r, int oversampling, in
         return AETH_OK;
     };
     int status = AETH_OK;
+    uint16_t *gt = nullptr, *at = nullptr, *bt = nullptr, *ut = nullptr;
+    const float* g = static_cast<const float*>(gin);
     do {
-        if ((status = alloc((void**)&w.omega, sizeof(float) * (size_t)n * l)) ||
+        if ((status = alloc((void**)&w.omega, sizeof(float) * big)) ||
             (status = alloc((void**)&w.y, sizeof(float) * (size_t)m * l)) ||
             (status = alloc((void**)&w.y2, sizeof(float) * big)) ||
             (status = alloc((void**)&w.b, sizeof(float) * (size_t)l * n)) ||
             (status = alloc((void**)&w.bbt, sizeof(float) * (size_t)l * l)) ||
             (status = alloc((void**)&w.u, sizeof(float) * (size_t)l * l)) ||
+            (status = alloc((void**)&w.ur, sizeof(float) * (size_t)l * r)) ||
             (status = alloc((void**)&w.gram, sizeof(double) * (size_t)l * l)) ||
             (status = alloc((void**)&w.linv, sizeof(double) * (size_t)l * l)) ||
             (status = alloc((void**)&w.jump, sizeof(uint64_t) * 64 * kOmegaLevels)) ||
             (status = alloc((void**)&w.fail, sizeof(int))))
             break;
+        if (fast) {
+            if ((!g_bf16 && (status = alloc((void**)&gt, sizeof(uint16_t) * 3 * (size_t)mn))) ||
+                (status = alloc((void**)&at, sizeof(uint16_t) * 3 * big)) ||
+                (status = alloc((void**)&bt, sizeof(uint16_t) * 3 * (size_t)l * n)) ||
+                (status = alloc((void**)&ut, sizeof(uint16_t) * 3 * (size_t)l * r)))
+                break;
+        } else if (g_bf16) {
+            // the exact path reads fp32: widen the bf16 gradient exactly
+            float* gf = nullptr;
+            if ((status = alloc((void**)&gf, sizeof(float) * (size_t)mn))) break;
+            bf16_to_f32_rsvd_kernel<<<grid_for(mn, 256), 256, 0, st>>>(static_cast<const uint16_t*>(gin), mn, gf);
+            g = gf;
+        }
         cudaError_t e =
             cudaMemcpyAsync(w.jump, omega_jump_host(), sizeof(Gf2Mat64) * kOmegaLevels, cudaMemcpyHostToDevice, st);
         if (e == cudaSuccess) e = cudaMemsetAsync(w.fail, 0, sizeof(int), st);
         if (e != cudaSuccess) { status = set_err((int)e); break; }
-        // 1. Omega, 2. Y = G Omega
+        // 1. Omega (n x l)
         const int64_t count = (int64_t)n * l;
         const int64_t chunks = (count + kOmegaChunk - 1) / kOmegaChunk;
         rsvd_omega_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w.jump, seed > 1 ? seed : 1, count,
                                                                            w.omega);
-        if ((status = simt_gemm_exact(g, n, 1, w.omega, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st))) break;
-        // 3. Q^ = orthonormal basis of Y (+ optional power iterations)
-        if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
-        for (int it = 0; it < power_iters && status == AETH_OK; ++it) {
-            // Z = G^T Q^ (n x l) into y2, orthonormalise, Y = G Z, orthonormalise
-            if ((status = simt_gemm_exact(g, 1, n, w.y, l, 1, w.y2, l, n, l, m, SIMT_STORE, 1.0f, nullptr, st))) break;
-            if ((status = cholqr2(w.y2, w.omega, n, l, w, st))) break;
-            if ((status = simt_gemm_exact(g, n, 1, w.y2, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st))) break;
-            if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
-        }
-        if (status) break;
-        // 4. B = Q^T G (l x n), 5. B B^T (l x l), 6. Jacobi
-        if ((status = simt_gemm_exact(w.y, 1, l, g, n, 1, w.b, n, l, n, m, SIMT_STORE, 1.0f, nullptr, st))) break;
-        if ((status = simt_gemm_exact(w.b, n, 1, w.b, 1, n, w.bbt, l, l, l, n, SIMT_STORE, 1.0f, nullptr, st))) break;
-        jacobi50_kernel<<<1, 1024, 0, st>>>(w.bbt, l, w.u);
-        AETH_LAUNCH_CHECK();
-        // 7. P = Q^ U[:, :r]
-        if (p_out && (status = simt_gemm_exact(w.y, l, 1, w.u, l, 1, p_out, r, m, r, l, SIMT_STORE, 1.0f, nullptr, st)))
-            break;
-        // 8. Q = B^T U[:, :r], orthonormalised (9)
-        if (q_out) {
-            if ((status = simt_gemm_exact(w.b, 1, n, w.u, l, 1, q_out, r, n, r, l, SIMT_STORE, 1.0f, nullptr, st)))
+        if (fast) {
+            if ((status = rsvd_fast(gin, g_bf16, m, n, r, l, power_iters, w, gt, at, bt, ut, p_out, q_out, st)))
                 break;
-            // Cholesky QR when the Gram matrix allows, else the clamped MGS;
-            // the choice needs the status of the first factorisation of Y too.
-            int fail_y = 0;
-            e = cudaMemcpyAsync(&fail_y, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
-            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-            if (e != cudaSuccess) { status = set_err((int)e); break; }
-            if (fail_y) { status = set_err(AETH_ERR_LINALG); break; }
+        } else {
+            // 2. Y = G Omega
+            if ((status = simt_gemm_exact(g, n, 1, w.omega, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st)))
+                break;
+            // 3. Q^ = orthonormal basis of Y (+ optional power iterations)
+            if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
+            for (int it = 0; it < power_iters && status == AETH_OK; ++it) {
+                // Z = G^T Q^ (n x l) into y2, orthonormalise, Y = G Z, orthonormalise
+                if ((status = simt_gemm_exact(g, 1, n, w.y, l, 1, w.y2, l, n, l, m, SIMT_STORE, 1.0f, nullptr, st)))
+                    break;
+                if ((status = cholqr2(w.y2, w.omega, n, l, w, st))) break;
+                if ((status = simt_gemm_exact(g, n, 1, w.y2, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st)))
+                    break;
+                if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
+            }
+            if (status) break;
+            // 4. B = Q^T G (l x n), 5. B B^T (l x l), 6. Jacobi
+            if ((status = simt_gemm_exact(w.y, 1, l, g, n, 1, w.b, n, l, n, m, SIMT_STORE, 1.0f, nullptr, st))) break;
+            if ((status = simt_gemm_exact(w.b, n, 1, w.b, 1, n, w.bbt, l, l, l, n, SIMT_STORE, 1.0f, nullptr, st)))
+                break;
+            jacobi50_kernel<<<1, 1024, 0, st>>>(w.bbt, l, w.u);
+            AETH_LAUNCH_CHECK();
+            // 7. P = Q^ U[:, :r]
+            if (p_out &&
+                (status = simt_gemm_exact(w.y, l, 1, w.u, l, 1, p_out, r, m, r, l, SIMT_STORE, 1.0f, nullptr, st)))
+                break;
+            // 8. Q = B^T U[:, :r]
+            if (q_out &&
+                (status = simt_gemm_exact(w.b, 1, n, w.u, l, 1, q_out, r, n, r, l, SIMT_STORE, 1.0f, nullptr, st)))
+                break;
+        }
+        // 9. Q orthonormalised.  Cholesky QR when the Gram matrix allows, else
+        // the clamped MGS; the choice needs the status of the first
+        // factorisation of Y too.
+        int fail_y = 0;
+        e = cudaMemcpyAsync(&fail_y, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) { status = set_err((int)e); break; }
+        if (fail_y) { status = set_err(AETH_ERR_LINALG); break; }
+        if (q_out) {
             if ((status = cholqr2(q_out, w.y2, n, r, w, st))) break;
             int fail_q = 0;
             e = cudaMemcpyAsync(&fail_q, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
@@ -465,12 +557,6 @@ inline int rsvd_device(const float* g, int m, int n, int r, int oversampling, in
                 mgs_clamped_kernel<<<1, 1024, 0, st>>>(q_out, n, r);
                 AETH_LAUNCH_CHECK();
             }
-        } else {
-            int fail_y = 0;
-            e = cudaMemcpyAsync(&fail_y, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
-            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-            if (e != cudaSuccess) { status = set_err((int)e); break; }
-            if (fail_y) { status = set_err(AETH_ERR_LINALG); break; }
         }
     } while (false);
     for (void* p : allocs) cudaFreeAsync(p, st);

@@ -177,6 +177,23 @@ def randomized_svd(g: torch.Tensor, rank: int, oversampling: int = 10, seed: int
     return p, q
 
 
+def randomized_svd_fast(g: torch.Tensor, rank: int, oversampling: int = 10, seed: int = 42, power_iters: int = 0,
+                        want_p: bool = True, want_q: bool = True):
+    """randomized_svd with every product on the tensor cores over exact bf16
+    terms (fp32-accurate, not the reference's summation order); g is a float32
+    or bfloat16 device matrix."""
+    g = g.contiguous()
+    if g.dtype not in (torch.float32, torch.bfloat16) or g.dim() != 2:
+        raise ValueError("g must be a 2-D float32 or bfloat16 device tensor")
+    m, n = g.shape
+    p = torch.empty(m, rank, dtype=torch.float32, device=g.device) if want_p else None
+    q = torch.empty(n, rank, dtype=torch.float32, device=g.device) if want_q else None
+    L.check(L.load().aeth_randomized_svd_ex(_ptr(g), _DTYPES[g.dtype], m, n, rank, oversampling, power_iters,
+                                            seed & (2**64 - 1), 1, _ptr(p), _ptr(q), C.c_void_p(_stream_handle())),
+            "aeth_randomized_svd_ex")
+    return p, q
+
+
 def decode_int8_to_fp16(src: torch.Tensor, scales: torch.Tensor, num_channels: int) -> torch.Tensor:
     """QuantizedDecoder::decode_int8_to_fp16 (flowcast/src/decode.rs:63-86) on
     the device: int8 src, per-channel f32 scales -> float16 (flowcast's
@@ -481,6 +498,32 @@ class GaLoreOptimizer:
         L.check(self._lib.aeth_galore_project_layer(self._ctx, n, self._indices(keys), gp, _DTYPES[grads[0].dtype],
                                                     C.c_void_p(_stream_handle())), "aeth_galore_project_layer")
 
+    def refresh_layer(self, keys, grads):
+        """The streamed subspace refresh (B200 mode): new projectors for these
+        parameters from this step's gradients, by the tensor-core randomized
+        SVD, installed (with an Adam state reset) by the next notify_step."""
+        n = len(keys)
+        gp = (C.c_void_p * n)(*[g.data_ptr() for g in grads])
+        L.check(self._lib.aeth_galore_refresh_layer(self._ctx, n, self._indices(keys), gp, _DTYPES[grads[0].dtype],
+                                                    C.c_void_p(_stream_handle())), "aeth_galore_refresh_layer")
+
+    def refresh_due(self) -> bool:
+        """Whether the step in progress is a refresh step: step + 1 == 1 or a
+        multiple of switch_interval (optimizer.rs:264-292)."""
+        nxt = self.step_count() + 1
+        every = self.config.switch_interval
+        return nxt == 1 or (every > 0 and nxt % every == 0)
+
+    def projector_buffer(self, layer_idx, param_name) -> torch.Tensor:
+        """The bf16 projector of a B200 parameter's side as a torch view of the
+        optimizer's own buffer (s x rank), for broadcasting it; read-only."""
+        idx, _ = self._key(layer_idx, param_name)
+        ptr_ = C.c_void_p()
+        rows, cols = C.c_int(), C.c_int()
+        L.check(self._lib.aeth_galore_projector_buffer(self._ctx, idx, C.byref(ptr_), C.byref(rows), C.byref(cols)),
+                "aeth_galore_projector_buffer")
+        return _wrap_device(int(ptr_.value), (rows.value, cols.value), "<i2", self.device).view(torch.bfloat16)
+
     def finish_step(self, keys, weights=None, sq_hook=None, clip_out: torch.Tensor | None = None,
                     prequant_outs=None):
         """The exact global-norm clip over every listed parameter (all that this
@@ -545,14 +588,19 @@ class GaLoreOptimizer:
         return int(p.value)
 
 
-def _wrap_device_doubles(ptr: int, count: int, device: int) -> torch.Tensor:
-    """A torch view of `count` device doubles owned by the library (no copy)."""
+def _wrap_device(ptr: int, shape, typestr: str, device: int) -> torch.Tensor:
+    """A torch view of device memory owned by the library (no copy)."""
     class _Holder:
         def __init__(self):
-            self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<f8", "data": (ptr, False),
+            self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
                                              "version": 2, "strides": None}
     with torch.cuda.device(device):
         return torch.as_tensor(_Holder(), device=f"cuda:{device}")
+
+
+def _wrap_device_doubles(ptr: int, count: int, device: int) -> torch.Tensor:
+    """A torch view of `count` device doubles owned by the library (no copy)."""
+    return _wrap_device(ptr, (count,), "<f8", device)
 
 
 @dataclass

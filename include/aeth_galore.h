@@ -288,6 +288,13 @@ int aeth_randomized_svd(const float* g, int m, int n, int rank, int oversampling
  * thread starting from the jumped-ahead xorshift64 state.  aeth_rsvd_jacobi:
  * jacobi_eigenvectors (randomized_svd.rs:210-271) on the n x n f32 matrix
  * `mat` (overwritten) with the eigenvector estimate in u (n x n). */
+/* aeth_randomized_svd with a bf16 or f32 g (g_dtype) and, with fast != 0,
+ * every product on the tensor cores over exact bf16 terms (fp32-accurate, not
+ * the reference's summation order; a bf16 g is its own single term) when m, n,
+ * rank and rank + oversampling are multiples of 8 -- otherwise, and with
+ * fast == 0, the exact-order path of aeth_randomized_svd. */
+int aeth_randomized_svd_ex(const void* g, int g_dtype, int m, int n, int rank, int oversampling, int power_iters,
+                           uint64_t seed, int fast, float* p_out, float* q_out, aeth_stream_t stream);
 int aeth_rsvd_omega(uint64_t seed, int64_t count, float* out, aeth_stream_t stream);
 int aeth_rsvd_jacobi(float* mat, int n, float* u, aeth_stream_t stream);
 
@@ -332,6 +339,28 @@ int aeth_galore_project_layer(aeth_galore_ctx* ctx, int n, const int* idx, const
                               aeth_stream_t stream);
 int aeth_galore_finish_step(aeth_galore_ctx* ctx, int n, const int* idx, const aeth_weight_ref* weights,
                             aeth_sqnorm_hook sq_hook, void* hook_user, float* clip_dev_out, aeth_stream_t stream);
+
+/* The subspace refresh of a streamed step (B200 mode; no reference
+ * counterpart as an entry point: the reference captures every parameter's
+ * full gradient during project_and_accumulate and refreshes in notify_step,
+ * optimizer.rs:208-246, 264-292, 373-398, which a 70B sweep cannot hold).
+ * For each listed parameter, the randomized SVD of this gradient (rank,
+ * config.oversampling and config.power_iters; seed (step + 1) * 0x9E3779B9,
+ * the step notify_step will record) runs on the tensor cores right away and
+ * its projector is kept aside; the next notify_step installs it and resets
+ * the parameter's Adam state, as the reference's refresh does, and counts one
+ * optimizer version.  The step's own back-projection still uses the old
+ * projector.  Call it on refresh steps (step + 1 == 1 or a multiple of
+ * switch_interval), with svd_refresh = 0, after or before project_layer for
+ * the same gradients.  Allocates (workspace, and the pending projector on
+ * first use) and waits on `stream` once per parameter for the factorisation
+ * status; refused while the stream is being captured. */
+int aeth_galore_refresh_layer(aeth_galore_ctx* ctx, int n, const int* idx, const void* const* grads, int grad_dtype,
+                              aeth_stream_t stream);
+/* The bf16 projector of a B200 parameter's side (rows x cols = s x rank,
+ * row-major, device memory owned by the optimizer): for broadcasting a
+ * refreshed projector from its owner (NCCL), read-only. */
+int aeth_galore_projector_buffer(aeth_galore_ctx* ctx, int idx, void** proj_bf16, int* rows, int* cols);
 
 /* Per-phase device timing of the step (no reference counterpart).  While
  * enabled, every B200-mode aeth_galore_step, project_layer and finish_step

@@ -163,3 +163,78 @@ def test_b200_mode_refresh_keeps_its_side(oracle):
     _, Q = opt.get_projector(0, "d_wq")
     assert np.array_equal(host(Q), oracle.bf16_round(host(Qd)))
     opt.close()
+
+
+@pytest.mark.parametrize("m,n,r,p", [(256, 384, 16, 8), (512, 256, 32, 8), (1024, 1024, 64, 8)])
+@pytest.mark.parametrize("power_iters", [0, 2])
+def test_randomized_svd_fast_matches_exact(oracle, m, n, r, p, power_iters):
+    """The tensor-core refresh (exact bf16 terms) against the exact-order one:
+    orthonormal projectors spanning the same subspaces, and equal to it
+    within the tolerance the two orthonormalisations leave."""
+    from aethelstream_b200 import randomized_svd, randomized_svd_fast
+    g = dev(_lowrank_plus_noise(m, n, r + p + 8, m + 2 * n))
+    seed = oracle.rsvd_seed(400)
+    P0, Q0 = randomized_svd(g, r, p, seed, power_iters=power_iters)
+    P1, Q1 = randomized_svd_fast(g, r, p, seed, power_iters=power_iters)
+    P0, Q0, P1, Q1 = host(P0), host(Q0), host(P1), host(Q1)
+    for X in (P1, Q1):
+        assert np.abs(X.T @ X - np.eye(r)).max() < 1e-4
+    assert rel_fro(P1, P0) < PROJ_TOL and rel_fro(Q1, Q0) < PROJ_TOL
+    # same subspaces: the projection of one basis onto the other is complete
+    assert np.linalg.norm(P0.T @ P1) ** 2 > r * (1 - 1e-4)
+
+
+def test_randomized_svd_fast_bf16_input(oracle):
+    """A bf16 gradient is its own single term: the fast refresh of the bf16
+    matrix equals the fast refresh of the same values widened to fp32."""
+    from aethelstream_b200 import randomized_svd_fast
+    m, n, r, p = 512, 768, 32, 8
+    g = dev(_lowrank_plus_noise(m, n, r + p + 8, 77)).to(torch.bfloat16)
+    seed = oracle.rsvd_seed(600)
+    P0, Q0 = randomized_svd_fast(g.float(), r, p, seed)
+    P1, Q1 = randomized_svd_fast(g, r, p, seed)
+    assert np.array_equal(host(P0), host(P1)) and np.array_equal(host(Q0), host(Q1))
+
+
+def test_refresh_layer_installs_at_notify(oracle):
+    """The streamed refresh: the new projector is computed from this step's
+    gradient, the step itself still back-projects with the old projector, and
+    notify_step installs the new one with a reset Adam state and one more
+    optimizer version."""
+    from aethelstream_b200 import GaLoreConfig, GaLoreOptimizer, nf4_quantize, randomized_svd_fast
+    specs = [(4, "d_wq", 512, 256, 64), (4, "d_wd", 256, 512, 64)]
+    keys = [(li, nm) for li, nm, *_ in specs]
+    rng = np.random.default_rng(12)
+    gs = [dev(_lowrank_plus_noise(m, n, 90, 5 + m)).mul(1e-3).to(torch.bfloat16) for _, _, m, n, _ in specs]
+    w0 = [(rng.standard_normal((m, n)) * 0.02).astype(np.float32) for _, _, m, n, _ in specs]
+    out = []
+    for refresh in (False, True):
+        cfg = GaLoreConfig(mode="b200", state_codec="dynamic", svd_refresh=False, oversampling=8, power_iters=1)
+        opt = GaLoreOptimizer(cfg, specs, device=0)
+        W = [nf4_quantize(dev(w)) for w in w0]
+        assert opt.refresh_due()
+        before = [opt.get_projector(li, nm) for li, nm in keys]
+        opt.project_layer(keys, gs)
+        if refresh:
+            opt.refresh_layer(keys, gs)
+        opt.finish_step(keys, W)
+        out.append([host(w.packed) for w in W] + [host(w.absmax) for w in W])
+        if refresh:
+            # nothing installed yet
+            for (li, nm), (p0, q0) in zip(keys, before):
+                p1, q1 = opt.get_projector(li, nm)
+                assert np.array_equal(host(p1 if p1 is not None else q1), host(p0 if p0 is not None else q0))
+            opt.notify_step(1)
+            assert opt.optimizer_version() == 1
+            for (li, nm, m, n, r), g in zip(specs, gs):
+                want_p, want_q = randomized_svd_fast(g, r, 8, oracle.rsvd_seed(1), power_iters=1,
+                                                     want_p=m < n, want_q=m >= n)
+                want = host(want_p if m < n else want_q)
+                P, Q = opt.get_projector(li, nm)
+                got = host(P if m < n else Q)
+                assert np.array_equal(got, oracle.bf16_round(want))
+                m8, v8, ms, vs = opt.get_state(li, nm)
+                assert not host(m8).any() and not host(v8).any()
+        opt.close()
+    for x, y in zip(*out):
+        assert np.array_equal(x, y)
