@@ -314,6 +314,7 @@ struct aeth_galore_ctx {
     PeerSlot* own_slots = nullptr;      // 2 x world entries, cudaMalloc'd (exported by IPC handle)
     int own_slots_world = 0;
     std::vector<void*> peer_maps;       // IPC mappings of the other ranks' slots
+    std::vector<cudaStream_t> side_streams;  // aeth_galore_refresh_layer's concurrent refreshes
     std::vector<void*> allocs;
     // aeth_galore_set_phase_timing: events at the phase boundaries of every
     // step, projection and finishing call
@@ -873,14 +874,12 @@ int refresh_param(aeth_galore_ctx* c, Param& p, uint64_t seed, cudaStream_t st) 
 // (pend_proj / pend_projT) until notify_step installs it: the step's own
 // back-projection still uses the projector its accumulator was projected
 // with, as the reference's refresh in notify_step after the update does
-// (optimizer.rs:208-246, 373-398).  Seed of the step in progress.
-int refresh_from_grad(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, cudaStream_t st) {
+// (optimizer.rs:208-246, 373-398).  Seed of the step in progress.  Enqueued
+// on `st` without waiting; *status_dev becomes 1 for a rank-deficient sketch.
+// pend_proj / pend_projT must be allocated.
+int refresh_enqueue(aeth_galore_ctx* c, Param& p, const void* grad, int dtype, int* status_dev, cudaStream_t st) {
     const int s_dim = p.side == 1 ? p.m : p.n;
     const size_t pe = (size_t)s_dim * p.r;
-    if (!p.pend_proj) {
-        AETH_TRY(ctx_alloc(c, &p.pend_proj, (int64_t)pe));
-        AETH_TRY(ctx_alloc(c, &p.pend_projT, (int64_t)pe));
-    }
     const uint64_t seed = (c->step + 1) * 0x9E3779B9ull;  // the step notify_step will record
     float* tproj = nullptr;
     float* gf = nullptr;
@@ -897,8 +896,8 @@ int refresh_from_grad(aeth_galore_ctx* c, Param& p, const void* grad, int dtype,
         }
     }
     if (status == AETH_OK)
-        status = rsvd_device(g, dtype == AETH_DTYPE_BF16, p.m, p.n, p.r, c->cfg.oversampling, c->cfg.power_iters,
-                             seed, true, p.side == 1 ? tproj : nullptr, p.side == 2 ? tproj : nullptr, st);
+        status = rsvd_launch(g, dtype == AETH_DTYPE_BF16, p.m, p.n, p.r, c->cfg.oversampling, c->cfg.power_iters,
+                             seed, true, p.side == 1 ? tproj : nullptr, p.side == 2 ? tproj : nullptr, status_dev, st);
     if (status == AETH_OK) {
         proj_to_bf16_kernel<<<grid_for((int64_t)pe, 256), 256, 0, st>>>(tproj, s_dim, p.r, p.pend_proj,
                                                                        p.pend_projT);
@@ -907,7 +906,6 @@ int refresh_from_grad(aeth_galore_ctx* c, Param& p, const void* grad, int dtype,
     }
     cudaFreeAsync(tproj, st);
     if (gf) cudaFreeAsync(gf, st);
-    if (status == AETH_OK) p.pending = true;
     return status;
 }
 
@@ -1237,6 +1235,7 @@ int aeth_galore_destroy(aeth_galore_ctx* ctx) {
     for (Param& p : ctx->params)
         if (p.capture) cudaFree(p.capture);
     for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+    for (cudaStream_t s : ctx->side_streams) cudaStreamDestroy(s);
     if (ctx->own_slots) cudaFree(ctx->own_slots);
     delete ctx;
     return AETH_OK;
@@ -1736,6 +1735,9 @@ uint64_t aeth_galore_step_count(const aeth_galore_ctx* ctx) { return ctx ? ctx->
 
 namespace {
 
+// Concurrent refreshes of aeth_galore_refresh_layer.
+constexpr int kRefreshStreams = 8;
+
 // Phase ids of aeth_galore_phase_times.
 enum { PH_PROJ = 0, PH_NORM = 1, PH_ADAM = 2, PH_APPLY = 3 };
 
@@ -1936,8 +1938,62 @@ int aeth_galore_refresh_layer(aeth_galore_ctx* ctx, int n, const int* idx, const
     bool capturing = false;
     AETH_TRY(set_err(stream_capturing(st, &capturing)));
     if (capturing) return set_err(AETH_ERR_UNSUPPORTED);
-    for (int i = 0; i < n; ++i) AETH_TRY(set_err(refresh_from_grad(ctx, ctx->params[idx[i]], grads[i], grad_dtype, st)));
-    return AETH_OK;
+    for (int i = 0; i < n; ++i) {
+        Param& p = ctx->params[idx[i]];
+        if (!p.pend_proj) {
+            const int64_t pe = (int64_t)(p.side == 1 ? p.m : p.n) * p.r;
+            AETH_TRY(set_err(ctx_alloc(ctx, &p.pend_proj, pe)));
+            AETH_TRY(set_err(ctx_alloc(ctx, &p.pend_projT, pe)));
+        }
+    }
+    // The parameters' refreshes run concurrently on the optimizer's side
+    // streams (their factorisations are one-CTA kernels that overlap the
+    // others' GEMMs), forked from and joined back into `stream`; one wait at
+    // the end reads every status.
+    if (ctx->side_streams.empty()) {
+        for (int k = 0; k < kRefreshStreams; ++k) {
+            cudaStream_t s = nullptr;
+            AETH_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+            ctx->side_streams.push_back(s);
+        }
+    }
+    int* flags = nullptr;
+    AETH_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&flags), sizeof(int) * (size_t)n, st));
+    int status = AETH_OK;
+    cudaEvent_t fork = nullptr;
+    std::vector<cudaEvent_t> joins;
+    cudaError_t e = cudaMemsetAsync(flags, 0, sizeof(int) * (size_t)n, st);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(fork, st);
+    if (e != cudaSuccess) status = (int)e;
+    const int nside = std::min<int>(kRefreshStreams, n);
+    for (int k = 0; k < nside && status == AETH_OK; ++k) {
+        e = cudaStreamWaitEvent(ctx->side_streams[k], fork, 0);
+        if (e != cudaSuccess) status = (int)e;
+    }
+    for (int i = 0; i < n && status == AETH_OK; ++i)
+        status = refresh_enqueue(ctx, ctx->params[idx[i]], grads[i], grad_dtype, flags + i,
+                                 ctx->side_streams[i % nside]);
+    for (int k = 0; k < nside; ++k) {
+        cudaEvent_t j = nullptr;
+        if (cudaEventCreateWithFlags(&j, cudaEventDisableTiming) != cudaSuccess) continue;
+        cudaEventRecord(j, ctx->side_streams[k]);
+        cudaStreamWaitEvent(st, j, 0);
+        joins.push_back(j);
+    }
+    std::vector<int> h((size_t)n, 0);
+    e = cudaMemcpyAsync(h.data(), flags, sizeof(int) * (size_t)n, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (status == AETH_OK && e != cudaSuccess) status = (int)e;
+    cudaFreeAsync(flags, st);
+    if (fork) cudaEventDestroy(fork);
+    for (cudaEvent_t j : joins) cudaEventDestroy(j);
+    if (status != AETH_OK) return set_err(status);
+    for (int i = 0; i < n; ++i) {
+        if (h[i]) status = AETH_ERR_LINALG;  // the reference drops such a refresh with an error
+        else ctx->params[idx[i]].pending = true;
+    }
+    return set_err(status);
 }
 
 int aeth_galore_projector_buffer(aeth_galore_ctx* ctx, int idx, void** proj_bf16, int* rows, int* cols) {
@@ -1994,6 +2050,7 @@ int aeth_galore_set_clip_group(aeth_galore_ctx* ctx, int rank, int world, const 
     if (ctx->cfg.mode != AETH_MODE_B200) return set_err(AETH_ERR_UNSUPPORTED);
     DeviceGuard g(ctx->device);
     for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+    for (cudaStream_t s : ctx->side_streams) cudaStreamDestroy(s);
     ctx->peer_maps.clear();
     ctx->group = ClipGroup();
     if (world == 1) return AETH_OK;
@@ -2018,6 +2075,7 @@ int aeth_galore_set_clip_group(aeth_galore_ctx* ctx, int rank, int world, const 
         cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
         if (e != cudaSuccess) {
             for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+    for (cudaStream_t s : ctx->side_streams) cudaStreamDestroy(s);
             ctx->peer_maps.clear();
             return set_err((int)e);
         }
@@ -2038,6 +2096,7 @@ int aeth_galore_set_clip_group_ptrs(aeth_galore_ctx* ctx, int rank, int world, v
         if (!slots[p]) return set_err(AETH_ERR_ARG);
     DeviceGuard g(ctx->device);
     for (void* m : ctx->peer_maps) cudaIpcCloseMemHandle(m);
+    for (cudaStream_t s : ctx->side_streams) cudaStreamDestroy(s);
     ctx->peer_maps.clear();
     ctx->group = ClipGroup();
     AETH_CUDA(cudaMemset(ctx->own_slots, 0, sizeof(PeerSlot) * 2 * (size_t)world));

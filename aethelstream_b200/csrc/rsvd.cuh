@@ -179,6 +179,84 @@ inline int gemm_f64acc(const TA* A, int64_t sai, int64_t sak, const TB* B, int64
 }
 
 // ---------------------------------------------------------------------------
+// Gram matrix G = X^T X (cols x cols, f64) of an f32 rows x cols matrix:
+// only the lower-triangle 64 x 64 tiles, each over `chunks` slices of the
+// rows (gridDim.y), the slice sums written to part[slice] and added in slice
+// order by gram_reduce_kernel (deterministic); far more CTAs than one per
+// output tile for the tall operands of the refresh (rows up to 28672).
+// ---------------------------------------------------------------------------
+constexpr int kGramMaxChunks = 8;
+
+__global__ void __launch_bounds__(256) gram_f64_kernel(const float* __restrict__ x, int rows, int cols,
+                                                       int rows_per_chunk, double* __restrict__ part) {
+    __shared__ double As[16][65];
+    __shared__ double Bs[16][65];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    int bi = (int)((sqrt(8.0 * blockIdx.x + 1.0) - 1.0) * 0.5);
+    while ((bi + 1) * (bi + 2) / 2 <= (int)blockIdx.x) ++bi;
+    while (bi * (bi + 1) / 2 > (int)blockIdx.x) --bi;
+    const int bj = blockIdx.x - bi * (bi + 1) / 2;
+    const int i0 = bi * 64, j0 = bj * 64;
+    const int r0 = blockIdx.y * rows_per_chunk, r1 = min(rows, r0 + rows_per_chunk);
+    double acc[4][4] = {};
+    for (int k0 = r0; k0 < r1; k0 += 16) {
+        for (int t = threadIdx.x; t < 16 * 64; t += 256) {
+            const int kk = t / 64, ii = t % 64;
+            const int gk = k0 + kk;
+            const bool kin = gk < r1;
+            As[kk][ii] = (kin && i0 + ii < cols) ? (double)x[(int64_t)gk * cols + i0 + ii] : 0.0;
+            Bs[kk][ii] = (kin && j0 + ii < cols) ? (double)x[(int64_t)gk * cols + j0 + ii] : 0.0;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < 16; ++kk) {
+            double av[4], bv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) av[a] = As[kk][ty + 16 * a];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) bv[b] = Bs[kk][tx + 16 * b];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = fma(av[a], bv[b], acc[a][b]);
+        }
+        __syncthreads();
+    }
+    double* out = part + (int64_t)blockIdx.y * cols * cols;
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int gi = i0 + ty + 16 * a, gj = j0 + tx + 16 * b;
+            if (gi < cols && gj < cols) out[(int64_t)gi * cols + gj] = acc[a][b];
+        }
+}
+
+__global__ void gram_reduce_kernel(const double* __restrict__ part, int chunks, int cols, double* __restrict__ g) {
+    const int64_t n = (int64_t)cols * cols;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(t / cols), j = (int)(t % cols);
+        if (j > i) continue;  // the lower triangle is all the factorisation reads
+        double s = 0.0;
+        for (int z = 0; z < chunks; ++z) s += part[z * n + t];
+        g[t] = s;
+    }
+}
+
+inline int gram_f64(const float* x, int rows, int cols, double* part, double* g, cudaStream_t st) {
+    const int tiles_1d = (cols + 63) / 64;
+    const int tiles = tiles_1d * (tiles_1d + 1) / 2;
+    int chunks = (2 * num_sms() + tiles - 1) / tiles;
+    chunks = std::max(1, std::min(chunks, std::min(kGramMaxChunks, (rows + 255) / 256)));
+    const int per = ((rows + chunks - 1) / chunks + 15) / 16 * 16;
+    chunks = (rows + per - 1) / per;
+    gram_f64_kernel<<<dim3(tiles, chunks), 256, 0, st>>>(x, rows, cols, per, part);
+    gram_reduce_kernel<<<grid_for((int64_t)cols * cols, 256), 256, 0, st>>>(part, chunks, cols, g);
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+// ---------------------------------------------------------------------------
 // One CTA: Cholesky of the l x l f64 Gram matrix in place (lower triangle),
 // then the inverse of the factor into Linv (lower; column c by thread c).
 // *fail = 1 when a pivot is not positive.
@@ -228,10 +306,211 @@ __global__ void __launch_bounds__(1024) chol_inverse_kernel(double* __restrict__
 }
 
 // ---------------------------------------------------------------------------
+// One CTA, blocked by 32 columns: the same factorisation and inverse as
+// chol_inverse_kernel for l <= kCholMaxL, in far fewer passes over memory.
+//   Cholesky (right-looking): the 32-column panel below the diagonal is held
+//   in shared memory (pitch 33 doubles); warp 0 factors the diagonal block,
+//   one thread per row solves the panel against it, and the warps then update
+//   the trailing lower triangle one 32 x 32 block each (lane = row, 32
+//   accumulators; the panel rows of the column block are broadcast reads).
+//   Inverse: each diagonal block's inverse by one warp (lane = column,
+//   forward substitution), then block column jb of L^-1 by warp jb % warps:
+//   X_ij = -inv(L_ii) sum_{k = j}^{i-1} L_ik X_kj, i increasing.
+// *fail = 1 when a pivot is not positive (or NaN).
+// ---------------------------------------------------------------------------
+constexpr int kCholMaxL = 640;
+constexpr int kCholThreads = 512;
+constexpr size_t kCholSmem = sizeof(double) * kCholMaxL * 33;  // also holds 16 warps x 32 x 33 in the inverse
+static_assert(kCholMaxL >= (kCholThreads / 32) * 32, "the inverse's per-warp scratch must fit the panel buffer");
+
+__global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __restrict__ a, int l,
+                                                                    double* __restrict__ linv, int* __restrict__ fail) {
+    extern __shared__ double pan[];  // (l - k0) x 33
+    __shared__ int bad;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int nb = (l + 31) / 32;
+    if (tid == 0) bad = 0;
+    __syncthreads();
+    for (int kb = 0; kb < nb; ++kb) {
+        const int k0 = kb * 32, kw = min(32, l - k0), prow = l - k0;
+        for (int t = tid; t < prow * 32; t += blockDim.x) {
+            const int i = t >> 5, c = t & 31;
+            pan[i * 33 + c] = (c < kw && c <= i) ? a[(int64_t)(k0 + i) * l + k0 + c] : 0.0;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            for (int c = 0; c < kw; ++c) {
+                const double d = pan[c * 33 + c];
+                const bool ok = d > 0.0;
+                const double piv = ok ? sqrt(d) : 1.0;
+                __syncwarp();
+                if (!ok && lane == 0) bad = 1;
+                if (lane == c) pan[c * 33 + c] = piv;
+                if (lane > c && lane < kw) pan[lane * 33 + c] /= piv;
+                __syncwarp();
+                if (lane > c && lane < kw) {
+                    const double lic = pan[lane * 33 + c];
+                    for (int j = c + 1; j <= lane; ++j) pan[lane * 33 + j] -= lic * pan[j * 33 + c];
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        if (bad) break;
+        // the panel below the diagonal block: row i solves x L_kk^T = a_i
+        for (int i = kw + tid; i < prow; i += blockDim.x) {
+            double x[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                if (c < kw) {
+                    double v = pan[i * 33 + c];
+#pragma unroll
+                    for (int t = 0; t < c; ++t) v -= x[t] * pan[c * 33 + t];
+                    x[c] = v / pan[c * 33 + c];
+                } else {
+                    x[c] = 0.0;
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+                if (c < kw) pan[i * 33 + c] = x[c];
+        }
+        __syncthreads();
+        for (int t = tid; t < prow * 32; t += blockDim.x) {
+            const int i = t >> 5, c = t & 31;
+            if (c < kw && c <= i) a[(int64_t)(k0 + i) * l + k0 + c] = pan[i * 33 + c];
+        }
+        // trailing update of the lower triangle: blocks (ib, jb), kb < jb <= ib
+        const int q = nb - kb - 1;
+        const int pairs = q * (q + 1) / 2;
+        for (int p = warp; p < pairs; p += nwarps) {
+            int bi = (int)((sqrt(8.0 * p + 1.0) - 1.0) * 0.5);
+            while ((bi + 1) * (bi + 2) / 2 <= p) ++bi;
+            while (bi * (bi + 1) / 2 > p) --bi;
+            const int bj = p - bi * (bi + 1) / 2;
+            const int gi = (kb + 1 + bi) * 32 + lane, gj0 = (kb + 1 + bj) * 32;
+            double acc[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = 0.0;
+            if (gi < l) {
+                for (int t = 0; t < kw; ++t) {
+                    const double li = pan[(gi - k0) * 33 + t];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int gj = gj0 + j;
+                        acc[j] += li * (gj < l ? pan[(gj - k0) * 33 + t] : 0.0);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int gj = gj0 + j;
+                    if (gj < l && gj <= gi) a[(int64_t)gi * l + gj] -= acc[j];
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (bad) {
+        if (tid == 0) *fail = 1;
+        return;
+    }
+    // L^-1: diagonal blocks first (lane = column c of the block's inverse)
+    for (int db = warp; db < nb; db += nwarps) {
+        const int d0 = db * 32, dw = min(32, l - d0);
+        double x[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (i < dw) {
+                double v = (i == lane) ? 1.0 : 0.0;
+                for (int t = 0; t < i; ++t) v -= a[(int64_t)(d0 + i) * l + d0 + t] * x[t];
+                x[i] = lane < dw ? v / a[(int64_t)(d0 + i) * l + d0 + i] : 0.0;
+            } else {
+                x[i] = 0.0;
+            }
+        }
+        if (lane < dw)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (i < dw) linv[(int64_t)(d0 + i) * l + d0 + lane] = x[i];
+    }
+    __syncthreads();
+    // off-diagonal blocks, one block column per warp, rows in increasing order
+    for (int jb = warp; jb < nb; jb += nwarps) {
+        const int j0 = jb * 32, jw = min(32, l - j0);
+        for (int ib = jb + 1; ib < nb; ++ib) {
+            const int i0 = ib * 32, iw = min(32, l - i0);
+            double acc[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) acc[c] = 0.0;
+            const int gi = i0 + lane;
+            for (int k = j0; k < i0; ++k) {
+                const double lik = gi < l ? a[(int64_t)gi * l + k] : 0.0;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) acc[c] += lik * (c < jw ? linv[(int64_t)k * l + j0 + c] : 0.0);
+            }
+            // X_ij = -inv(L_ii) S: row r = lane; S goes through this warp's
+            // slice of the (now free) panel buffer
+            double* sw = pan + warp * 32 * 33;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) sw[lane * 33 + c] = acc[c];
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) acc[c] = 0.0;
+            for (int t = 0; t < iw; ++t) {
+                const double dinv = gi < l ? linv[(int64_t)gi * l + i0 + t] : 0.0;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) acc[c] -= dinv * sw[t * 33 + c];
+            }
+            if (lane < iw)
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    if (c < jw) linv[(int64_t)gi * l + j0 + c] = acc[c];
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    // zero the strict upper triangle of L^-1 (callers read all of it)
+    for (int64_t t = tid; t < (int64_t)l * l; t += blockDim.x) {
+        const int i = (int)(t / l), j = (int)(t % l);
+        if (j > i) linv[t] = 0.0;
+    }
+}
+
+// Cholesky and inverse of the l x l Gram matrix: the blocked kernel when its
+// panel fits shared memory, else the per-element one.
+inline int chol_inverse(double* gram, int l, double* linv, int* fail, cudaStream_t st) {
+    if (l <= kCholMaxL) {
+        static bool attr_set[kMaxDevices] = {};
+        int dev = 0;
+        AETH_TRY(current_device(&dev));
+        if (!attr_set[dev]) {
+            AETH_CUDA(cudaFuncSetAttribute(chol_blocked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kCholSmem));
+            attr_set[dev] = true;
+        }
+        chol_blocked_kernel<<<1, kCholThreads, kCholSmem, st>>>(gram, l, linv, fail);
+    } else {
+        chol_inverse_kernel<<<1, 1024, 0, st>>>(gram, l, linv, fail);
+    }
+    AETH_LAUNCH_CHECK();
+    return AETH_OK;
+}
+
+// dst = src where *flag is set (the fallback's starting point), else nothing.
+__global__ void copy_if_flag_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t n,
+                                    const int* __restrict__ flag) {
+    if (!*flag) return;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+
+// ---------------------------------------------------------------------------
 // One CTA: modified Gram-Schmidt with the norm clamp of
 // orthonormalize_columns (randomized_svd.rs:187-207); the rare fallback.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) mgs_clamped_kernel(float* __restrict__ q, int rows, int cols) {
+__global__ void __launch_bounds__(1024) mgs_clamped_kernel(float* __restrict__ q, int rows, int cols,
+                                                           const int* __restrict__ only_if = nullptr) {
+    if (only_if && !*only_if) return;
     __shared__ float red[32];
     __shared__ float bcast;
     auto block_sum = [&](float v) -> float {
@@ -370,6 +649,7 @@ struct RsvdWork {
     float* bbt = nullptr;    // l x l
     float* u = nullptr;      // l x l
     float* ur = nullptr;     // l x r: the first r columns of u
+    double* gpart = nullptr; // kGramMaxChunks x l x l: slice sums of the Gram matrix
     double* gram = nullptr;  // l x l
     double* linv = nullptr;  // l x l
     uint64_t* jump = nullptr;
@@ -379,11 +659,10 @@ struct RsvdWork {
 // Orthonormal basis of the columns of x (rows x cols) by Cholesky QR, in
 // place; `tmp` holds rows x cols floats.  Two passes.  Returns 1 in *fail_dev
 // when the Gram matrix is not positive definite.
-inline int cholqr2(float* x, float* tmp, int rows, int cols, RsvdWork& w, cudaStream_t st) {
+inline int cholqr2(float* x, float* tmp, int rows, int cols, RsvdWork& w, cudaStream_t st, int* fail = nullptr) {
     for (int pass = 0; pass < 2; ++pass) {
-        AETH_TRY((gemm_f64acc<float, float, double>(x, 1, cols, x, cols, 1, w.gram, cols, cols, cols, rows, st)));
-        chol_inverse_kernel<<<1, 1024, 0, st>>>(w.gram, cols, w.linv, w.fail);
-        AETH_LAUNCH_CHECK();
+        AETH_TRY(gram_f64(x, rows, cols, w.gpart, w.gram, st));
+        AETH_TRY(chol_inverse(w.gram, cols, w.linv, fail ? fail : w.fail, st));
         // tmp = x Linv^T
         AETH_TRY((gemm_f64acc<float, double, float>(x, cols, 1, w.linv, 1, cols, tmp, cols, rows, cols, cols, st)));
         AETH_CUDA(cudaMemcpyAsync(x, tmp, sizeof(float) * (size_t)rows * cols, cudaMemcpyDeviceToDevice, st));
@@ -442,19 +721,24 @@ inline int rsvd_fast(const void* g, bool g_bf16, int m, int n, int r, int l, int
     return AETH_OK;
 }
 
-// randomized_svd_projections on the device.  g: m x n, f32 or (g_bf16) bf16;
-// p_out (m x r) and q_out (n x r) f32, either may be null.  fast selects the
-// tensor-core products (rsvd_fast) when the shape allows; otherwise the
-// exact-order CUDA-core GEMM reproduces the reference's f32 loops on equal
-// inputs (a bf16 g is widened exactly first).  Synchronises `st` once to read
-// the factorisation status.  Returns AETH_ERR_CONFIG for an invalid rank or
-// oversampling, AETH_ERR_LINALG for a rank-deficient sketch.
-inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int oversampling, int power_iters,
-                       uint64_t seed, bool fast, float* p_out, float* q_out, cudaStream_t st) {
+// randomized_svd_projections on the device, enqueued on `st` without waiting:
+// g m x n, f32 or (g_bf16) bf16; p_out (m x r) and q_out (n x r) f32, either
+// may be null.  fast selects the tensor-core products (rsvd_fast) when the
+// shape allows; otherwise the exact-order CUDA-core GEMM reproduces the
+// reference's f32 loops on equal inputs (a bf16 g is widened exactly first).
+// *status_dev becomes 1 when the sketch is rank-deficient (the reference's
+// GaLoreError::Linalg from qr_columns); the outputs are then meaningless.
+// Q's orthonormalisation falls back to the reference's clamped Gram-Schmidt
+// on the device when its Cholesky factorisation fails.  Workspace comes from
+// the stream-ordered pool.  Returns AETH_ERR_CONFIG for an invalid rank or
+// oversampling.
+inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int oversampling, int power_iters,
+                       uint64_t seed, bool fast, float* p_out, float* q_out, int* status_dev, cudaStream_t st) {
     const int l = r + oversampling;
     if (r <= 0 || oversampling < 0 || power_iters < 0 || l > (m < n ? m : n)) return AETH_ERR_CONFIG;
     fast = fast && rsvd_fast_shape(m, n, r, l);
     RsvdWork w;
+    w.fail = status_dev;
     const size_t big = (size_t)(m > n ? m : n) * l;
     const int64_t mn = (int64_t)m * n;
     std::vector<void*> allocs;
@@ -466,6 +750,8 @@ inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int ov
     };
     int status = AETH_OK;
     uint16_t *gt = nullptr, *at = nullptr, *bt = nullptr, *ut = nullptr;
+    float* qraw = nullptr;
+    int* fail_q = nullptr;
     const float* g = static_cast<const float*>(gin);
     do {
         if ((status = alloc((void**)&w.omega, sizeof(float) * big)) ||
@@ -476,10 +762,12 @@ inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int ov
             (status = alloc((void**)&w.u, sizeof(float) * (size_t)l * l)) ||
             (status = alloc((void**)&w.ur, sizeof(float) * (size_t)l * r)) ||
             (status = alloc((void**)&w.gram, sizeof(double) * (size_t)l * l)) ||
+            (status = alloc((void**)&w.gpart, sizeof(double) * kGramMaxChunks * (size_t)l * l)) ||
             (status = alloc((void**)&w.linv, sizeof(double) * (size_t)l * l)) ||
             (status = alloc((void**)&w.jump, sizeof(uint64_t) * 64 * kOmegaLevels)) ||
-            (status = alloc((void**)&w.fail, sizeof(int))))
+            (status = alloc((void**)&fail_q, sizeof(int))))
             break;
+        if (q_out && (status = alloc((void**)&qraw, sizeof(float) * (size_t)n * r))) break;
         if (fast) {
             if ((!g_bf16 && (status = alloc((void**)&gt, sizeof(uint16_t) * 3 * (size_t)mn))) ||
                 (status = alloc((void**)&at, sizeof(uint16_t) * 3 * big)) ||
@@ -495,7 +783,7 @@ inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int ov
         }
         cudaError_t e =
             cudaMemcpyAsync(w.jump, omega_jump_host(), sizeof(Gf2Mat64) * kOmegaLevels, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = cudaMemsetAsync(w.fail, 0, sizeof(int), st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(fail_q, 0, sizeof(int), st);
         if (e != cudaSuccess) { status = set_err((int)e); break; }
         // 1. Omega (n x l)
         const int64_t count = (int64_t)n * l;
@@ -536,31 +824,41 @@ inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int ov
                 (status = simt_gemm_exact(w.b, 1, n, w.u, l, 1, q_out, r, n, r, l, SIMT_STORE, 1.0f, nullptr, st)))
                 break;
         }
-        // 9. Q orthonormalised.  Cholesky QR when the Gram matrix allows, else
-        // the clamped MGS; the choice needs the status of the first
-        // factorisation of Y too.
-        int fail_y = 0;
-        e = cudaMemcpyAsync(&fail_y, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-        if (e != cudaSuccess) { status = set_err((int)e); break; }
-        if (fail_y) { status = set_err(AETH_ERR_LINALG); break; }
+        // 9. Q orthonormalised (orthonormalize_columns): Cholesky QR, or, where
+        // its Gram matrix is not positive definite, the reference's clamped
+        // Gram-Schmidt from B^T U again -- chosen on the device.
         if (q_out) {
-            if ((status = cholqr2(q_out, w.y2, n, r, w, st))) break;
-            int fail_q = 0;
-            e = cudaMemcpyAsync(&fail_q, w.fail, sizeof(int), cudaMemcpyDeviceToHost, st);
-            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            e = cudaMemcpyAsync(qraw, q_out, sizeof(float) * (size_t)n * r, cudaMemcpyDeviceToDevice, st);
             if (e != cudaSuccess) { status = set_err((int)e); break; }
-            if (fail_q) {
-                // redo from B^T U with the reference's clamped Gram-Schmidt
-                if ((status = simt_gemm_exact(w.b, 1, n, w.u, l, 1, q_out, r, n, r, l, SIMT_STORE, 1.0f, nullptr, st)))
-                    break;
-                mgs_clamped_kernel<<<1, 1024, 0, st>>>(q_out, n, r);
-                AETH_LAUNCH_CHECK();
-            }
+            if ((status = cholqr2(q_out, w.y2, n, r, w, st, fail_q))) break;
+            copy_if_flag_kernel<<<grid_for((int64_t)n * r, 256), 256, 0, st>>>(qraw, q_out, (int64_t)n * r, fail_q);
+            mgs_clamped_kernel<<<1, 1024, 0, st>>>(q_out, n, r, fail_q);
+            AETH_LAUNCH_CHECK();
         }
     } while (false);
     for (void* p : allocs) cudaFreeAsync(p, st);
     return status;
+}
+
+// rsvd_launch, then waits on `st` for the factorisation status: returns
+// AETH_ERR_LINALG for a rank-deficient sketch.
+inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int oversampling, int power_iters,
+                       uint64_t seed, bool fast, float* p_out, float* q_out, cudaStream_t st) {
+    int* flag = nullptr;
+    AETH_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&flag), sizeof(int), st));
+    cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), st);
+    int status = e == cudaSuccess ? AETH_OK : (int)e;
+    if (status == AETH_OK)
+        status = rsvd_launch(gin, g_bf16, m, n, r, oversampling, power_iters, seed, fast, p_out, q_out, flag, st);
+    int h = 0;
+    if (status == AETH_OK) {
+        e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) status = (int)e;
+    }
+    cudaFreeAsync(flag, st);
+    if (status == AETH_OK && h) status = AETH_ERR_LINALG;
+    return status == AETH_OK ? AETH_OK : set_err(status);
 }
 
 }  // namespace aeth

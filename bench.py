@@ -1067,8 +1067,10 @@ def time_refresh(opt, owned, ring, layers, rcfg, dev, world, rank):
     t1 = torch.cuda.Event(enable_timing=True)
     t2 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for li in owned:
-        opt.refresh_layer([(li, name) for name, _, _ in SHAPES], ring[li % 2])
+    # every owned matrix in one call: the refreshes run concurrently on the
+    # optimizer's side streams
+    opt.refresh_layer([(li, name) for li in owned for name, _, _ in SHAPES],
+                      [g for li in owned for g in ring[li % 2]])
     opt.notify_step(opt.step_count() + 1)
     t1.record(stream)
     bcast_bytes = 0
