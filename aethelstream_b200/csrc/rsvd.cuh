@@ -320,12 +320,13 @@ __global__ void __launch_bounds__(1024) chol_inverse_kernel(double* __restrict__
 // ---------------------------------------------------------------------------
 constexpr int kCholMaxL = 640;
 constexpr int kCholThreads = 512;
-constexpr size_t kCholSmem = sizeof(double) * kCholMaxL * 33;  // also holds 16 warps x 32 x 33 in the inverse
-static_assert(kCholMaxL >= (kCholThreads / 32) * 32, "the inverse's per-warp scratch must fit the panel buffer");
+constexpr size_t kCholSmem = sizeof(double) * kCholMaxL * 33;  // also a 32-row block of L in the inverse
+static_assert(32 * (kCholMaxL + 1) <= kCholMaxL * 33, "the inverse's block row of L must fit the panel buffer");
 
 __global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __restrict__ a, int l,
                                                                     double* __restrict__ linv, int* __restrict__ fail) {
     extern __shared__ double pan[];  // (l - k0) x 33
+    __shared__ double rdiag[32];
     __shared__ int bad;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     const int nb = (l + 31) / 32;
@@ -358,6 +359,9 @@ __global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __re
         __syncthreads();
         if (bad) break;
         // the panel below the diagonal block: row i solves x L_kk^T = a_i
+        // (one reciprocal per pivot instead of a division per element)
+        if (tid < 32) rdiag[tid] = tid < kw ? 1.0 / pan[tid * 33 + tid] : 0.0;
+        __syncthreads();
         for (int i = kw + tid; i < prow; i += blockDim.x) {
             double x[32];
 #pragma unroll
@@ -366,7 +370,7 @@ __global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __re
                     double v = pan[i * 33 + c];
 #pragma unroll
                     for (int t = 0; t < c; ++t) v -= x[t] * pan[c * 33 + t];
-                    x[c] = v / pan[c * 33 + c];
+                    x[c] = v * rdiag[c];
                 } else {
                     x[c] = 0.0;
                 }
@@ -434,38 +438,52 @@ __global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __re
                 if (i < dw) linv[(int64_t)(d0 + i) * l + d0 + lane] = x[i];
     }
     __syncthreads();
-    // off-diagonal blocks, one block column per warp, rows in increasing order
-    for (int jb = warp; jb < nb; jb += nwarps) {
-        const int j0 = jb * 32, jw = min(32, l - j0);
-        for (int ib = jb + 1; ib < nb; ++ib) {
-            const int i0 = ib * 32, iw = min(32, l - i0);
+    // off-diagonal blocks by block rows: X_ij = -inv(L_ii) sum_{k = j}^{i-1}
+    // L_ik X_kj needs only earlier block rows of L^-1.  For block row ib the
+    // CTA stages L's rows i0 .. i0 + 31 (columns < i0) in shared memory,
+    // then warp jb (< ib) forms block (ib, jb): lane = row, 32 accumulators,
+    // the rows of X_kj read as coalesced broadcasts, eight k in flight.
+    const int pitch = l + 1;  // odd pitch: the lanes' rows fall in different banks
+    for (int ib = 1; ib < nb; ++ib) {
+        const int i0 = ib * 32, iw = min(32, l - i0);
+        __syncthreads();
+        // columns 0 .. i0 - 1 of the block row (i0 < l < pitch)
+        for (int t = tid; t < 32 * i0; t += blockDim.x) {
+            const int r = t / i0, k = t % i0;
+            pan[r * pitch + k] = r < iw ? a[(int64_t)(i0 + r) * l + k] : 0.0;
+        }
+        __syncthreads();
+        for (int jb = warp; jb < ib; jb += nwarps) {
+            const int j0 = jb * 32, jw = min(32, l - j0);
             double acc[32];
 #pragma unroll
             for (int c = 0; c < 32; ++c) acc[c] = 0.0;
-            const int gi = i0 + lane;
+            const double* lrow = pan + lane * pitch;
+#pragma unroll 4
             for (int k = j0; k < i0; ++k) {
-                const double lik = gi < l ? a[(int64_t)gi * l + k] : 0.0;
+                const double lik = lrow[k];
+                const double* xr = linv + (int64_t)k * l + j0;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) acc[c] += lik * (c < jw ? linv[(int64_t)k * l + j0 + c] : 0.0);
+                for (int c = 0; c < 32; ++c) acc[c] += lik * (c < jw ? xr[c] : 0.0);
             }
-            // X_ij = -inv(L_ii) S: row r = lane; S goes through this warp's
-            // slice of the (now free) panel buffer
-            double* sw = pan + warp * 32 * 33;
+            // acc = S row `lane`; X_ij = -inv(L_ii) S through shuffles of S's
+            // rows, 16 output columns at a time
+            const double* drow = linv + (int64_t)(i0 + min(lane, iw - 1)) * l + i0;
 #pragma unroll
-            for (int c = 0; c < 32; ++c) sw[lane * 33 + c] = acc[c];
-            __syncwarp();
+            for (int h = 0; h < 2; ++h) {
+                double out[16];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) acc[c] = 0.0;
-            for (int t = 0; t < iw; ++t) {
-                const double dinv = gi < l ? linv[(int64_t)gi * l + i0 + t] : 0.0;
+                for (int c = 0; c < 16; ++c) out[c] = 0.0;
+                for (int t = 0; t < iw; ++t) {
+                    const double dinv = lane < iw ? drow[t] : 0.0;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) acc[c] -= dinv * sw[t * 33 + c];
+                    for (int c = 0; c < 16; ++c) out[c] -= dinv * __shfl_sync(0xffffffffu, acc[16 * h + c], t);
+                }
+                if (lane < iw)
+#pragma unroll
+                    for (int c = 0; c < 16; ++c)
+                        if (16 * h + c < jw) linv[(int64_t)(i0 + lane) * l + j0 + 16 * h + c] = out[c];
             }
-            if (lane < iw)
-#pragma unroll
-                for (int c = 0; c < 32; ++c)
-                    if (c < jw) linv[(int64_t)gi * l + j0 + c] = acc[c];
-            __syncwarp();
         }
     }
     __syncthreads();
@@ -650,6 +668,9 @@ struct RsvdWork {
     float* u = nullptr;      // l x l
     float* ur = nullptr;     // l x r: the first r columns of u
     double* gpart = nullptr; // kGramMaxChunks x l x l: slice sums of the Gram matrix
+    uint16_t* xt = nullptr;  // fast path: bf16 terms of the matrix being orthonormalised (3 x rows x l)
+    uint16_t* lt = nullptr;  // fast path: bf16 terms of Linv (3 x l x l)
+    float* linv32 = nullptr; // fast path: Linv in f32
     double* gram = nullptr;  // l x l
     double* linv = nullptr;  // l x l
     uint64_t* jump = nullptr;
@@ -659,12 +680,31 @@ struct RsvdWork {
 // Orthonormal basis of the columns of x (rows x cols) by Cholesky QR, in
 // place; `tmp` holds rows x cols floats.  Two passes.  Returns 1 in *fail_dev
 // when the Gram matrix is not positive definite.
-inline int cholqr2(float* x, float* tmp, int rows, int cols, RsvdWork& w, cudaStream_t st, int* fail = nullptr) {
-    for (int pass = 0; pass < 2; ++pass) {
+__global__ void f64_to_f32_kernel(const double* __restrict__ x, int64_t n, float* __restrict__ y) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = (float)x[i];
+}
+
+inline int cholqr2(float* x, float* tmp, int rows, int cols, RsvdWork& w, cudaStream_t st, int* fail = nullptr,
+                   int passes = 2) {
+    // with the tensor-core workspace (fast path) the product x Linv^T runs
+    // on tcgen05 over exact bf16 terms of x and of Linv rounded to f32
+    const bool tc = w.xt && w.lt && cols % 8 == 0;
+    for (int pass = 0; pass < passes; ++pass) {
         AETH_TRY(gram_f64(x, rows, cols, w.gpart, w.gram, st));
         AETH_TRY(chol_inverse(w.gram, cols, w.linv, fail ? fail : w.fail, st));
         // tmp = x Linv^T
-        AETH_TRY((gemm_f64acc<float, double, float>(x, cols, 1, w.linv, 1, cols, tmp, cols, rows, cols, cols, st)));
+        if (tc) {
+            const int64_t xc = (int64_t)rows * cols, lc = (int64_t)cols * cols;
+            f64_to_f32_kernel<<<grid_for(lc, 256), 256, 0, st>>>(w.linv, lc, w.linv32);
+            AETH_TRY(split3_terms(w.linv32, lc, w.lt, st));
+            AETH_TRY(split3_terms(x, xc, w.xt, st));
+            // A = x K-major (rows x cols), B(k, j) = Linv[j][k]: K-major (cols x cols)
+            AETH_TRY(terms_gemm(TermOp{w.xt, 3, xc, cols, false}, TermOp{w.lt, 3, lc, cols, false}, tmp, cols, rows,
+                                cols, cols, false, st));
+        } else {
+            AETH_TRY((gemm_f64acc<float, double, float>(x, cols, 1, w.linv, 1, cols, tmp, cols, rows, cols, cols, st)));
+        }
         AETH_CUDA(cudaMemcpyAsync(x, tmp, sizeof(float) * (size_t)rows * cols, cudaMemcpyDeviceToDevice, st));
     }
     return AETH_OK;
@@ -689,16 +729,18 @@ inline int rsvd_fast(const void* g, bool g_bf16, int m, int n, int r, int l, int
     // 2. Y = G Omega (m x l)
     AETH_TRY(split3_terms(w.omega, (int64_t)n * l, at, st));
     AETH_TRY(terms_gemm(G_k, TermOp{at, 3, (int64_t)n * l, l, true}, w.y, l, m, l, n, false, st));
-    // 3. Q^ = orthonormal basis of Y, optional power iterations
-    AETH_TRY(cholqr2(w.y, w.y2, m, l, w, st));
+    // 3. Q^ = orthonormal basis of Y, optional power iterations.  The bases
+    // between the power iterations only keep the iterates well conditioned:
+    // one Cholesky QR pass each; the final Q^ gets the second pass.
+    AETH_TRY(cholqr2(w.y, w.y2, m, l, w, st, nullptr, power_iters > 0 ? 1 : 2));
     for (int it = 0; it < power_iters; ++it) {
         // Z = G^T Q^ (n x l), orthonormalised; Y = G Z, orthonormalised
         AETH_TRY(split3_terms(w.y, (int64_t)m * l, at, st));
         AETH_TRY(terms_gemm(G_mn, TermOp{at, 3, (int64_t)m * l, l, true}, w.y2, l, n, l, m, false, st));
-        AETH_TRY(cholqr2(w.y2, w.omega, n, l, w, st));
+        AETH_TRY(cholqr2(w.y2, w.omega, n, l, w, st, nullptr, 1));
         AETH_TRY(split3_terms(w.y2, (int64_t)n * l, at, st));
         AETH_TRY(terms_gemm(G_k, TermOp{at, 3, (int64_t)n * l, l, true}, w.y, l, m, l, n, false, st));
-        AETH_TRY(cholqr2(w.y, w.y2, m, l, w, st));
+        AETH_TRY(cholqr2(w.y, w.y2, m, l, w, st, nullptr, it + 1 == power_iters ? 2 : 1));
     }
     // 4. B = Q^T G (l x n): A = Q^T (Q^ read MN-major), B = G (MN-major), K = m
     AETH_TRY(split3_terms(w.y, (int64_t)m * l, at, st));
@@ -772,7 +814,10 @@ inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int ov
             if ((!g_bf16 && (status = alloc((void**)&gt, sizeof(uint16_t) * 3 * (size_t)mn))) ||
                 (status = alloc((void**)&at, sizeof(uint16_t) * 3 * big)) ||
                 (status = alloc((void**)&bt, sizeof(uint16_t) * 3 * (size_t)l * n)) ||
-                (status = alloc((void**)&ut, sizeof(uint16_t) * 3 * (size_t)l * r)))
+                (status = alloc((void**)&ut, sizeof(uint16_t) * 3 * (size_t)l * r)) ||
+                (status = alloc((void**)&w.xt, sizeof(uint16_t) * 3 * big)) ||
+                (status = alloc((void**)&w.lt, sizeof(uint16_t) * 3 * (size_t)l * l)) ||
+                (status = alloc((void**)&w.linv32, sizeof(float) * (size_t)l * l)))
                 break;
         } else if (g_bf16) {
             // the exact path reads fp32: widen the bf16 gradient exactly
