@@ -20,6 +20,15 @@
 // k-blocks (64 columns of r of X and Y) flow through a separate STAGES-deep
 // ring.  TMEM holds two 256-column accumulators so the epilogue of one tile
 // overlaps the MMAs of the next.
+//
+// PAIR = true runs the same unit on a cluster of two CTAs (tcgen05
+// cta_group::2): the unit is 256 rows x 256 columns, each CTA holds its 128
+// rows of X and 128 of the 256 rows of Y per k-block (32 KB instead of 48 KB),
+// CTA 0 issues the pair's MMAs (M = 256) and its commits reach both CTAs'
+// barriers, and each CTA's epilogue processes its own 128 rows as above.  At
+// large ranks the single-CTA kernel is bound by the operand bytes it can keep
+// in flight per SM (two 48 KB stages for 384 KB per unit at r = 512); the pair
+// moves a third fewer bytes per SM through three stages of the same memory.
 #pragma once
 #include "nf4.cuh"
 #include "umma.cuh"
@@ -57,10 +66,10 @@ struct ApplyArgs {
     uint32_t idesc;
 };
 
-template <int STAGES>
+template <int STAGES, bool PAIR = false>
 struct ApplyLayout {
-    static constexpr int kA = 128 * 64 * 2;        // 16 KB
-    static constexpr int kB = kApplyBN * 64 * 2;   // 32 KB
+    static constexpr int kA = 128 * 64 * 2;                       // 16 KB
+    static constexpr int kB = (PAIR ? kApplyBN / 2 : kApplyBN) * 64 * 2;  // 32 KB (16 KB: half of Y per CTA)
     static constexpr int kStage = kA + kB;
     static constexpr int kWPacked = 128 * 128;     // 128 rows x 128 bytes
     static constexpr int kWScale = 128 * 16;       // 128 rows x 4 floats
@@ -91,10 +100,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[N]) {
     for (int i = 0; i < 16; ++i) v[OFF + i] = __uint_as_float(r[i]);
 }
 
-template <int STAGES>
+template <int STAGES, bool PAIR>
 __global__ void __launch_bounds__(kApplyThreads, 1)
     apply_grouped_kernel(const __grid_constant__ ApplyArgs args, uint32_t* err) {
-    using L = ApplyLayout<STAGES>;
+    using L = ApplyLayout<STAGES, PAIR>;
     constexpr int kEpiThreads = 32 * kApplyEpiWarps;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -111,22 +120,41 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     // (problem, m0, n0) of the unit in each weight slot, written by the producer
     // before the slot's full barrier is armed (its arrive releases them)
-    int4* winfo = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(full) + 128);
-    static_assert((2 * STAGES + 4 + 2 * kApplyWSlots) * 8 + 8 <= 128 && 128 + 16 * kApplyWSlots <= L::kBar,
+    int4* winfo = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(full) + 160);
+    static_assert((2 * STAGES + 4 + 2 * kApplyWSlots) * 8 + 8 <= 160 && 160 + 16 * kApplyWSlots <= L::kBar,
                   "barriers, TMEM slot, abort flag and unit table must fit the barrier area");
     Nf4Tables32* tab = reinterpret_cast<Nf4Tables32*>(reinterpret_cast<uint8_t*>(full) + L::kBar);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // PAIR: rank in the cluster (CTA 0 issues the MMAs), units per cluster
+    const int crank = PAIR ? (int)cluster_ctarank() : 0;
+    const int ustart = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int ustep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int rows_per_unit = PAIR ? 256 : 128;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiThreads); }
+        // acc_empty: every epilogue thread (single CTA), or one arrival per
+        // epilogue warp of both CTAs on CTA 0's barrier (pair)
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], PAIR ? 2 * kApplyEpiWarps : kEpiThreads);
+        }
         for (int b = 0; b < kApplyWSlots; ++b) { mbar_init(&w_full[b], 1); mbar_init(&w_empty[b], 4); }
         *abort = 0;
         fence_mbar_init();
     }
-    if (warp == 0) { tmem_alloc(tmem_slot, 2 * kApplyBN); tmem_relinquish(); }
+    if (warp == 0) {
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, 2 * kApplyBN);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, 2 * kApplyBN);
+            tmem_relinquish();
+        }
+    }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // both CTAs' barriers initialised before any remote arrival
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int total = args.total_units;
@@ -135,11 +163,11 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             int it = 0, j = 0;
-            for (int u = blockIdx.x; u < total && !*abort; u += gridDim.x, ++j) {
+            for (int u = ustart; u < total && !*abort; u += ustep, ++j) {
                 const int p = apply_find(args, u);
                 const ApplyProblem& pr = args.p[p];
                 const int local = u - pr.unit_begin;
-                const int m0 = (local / pr.n_tiles) * 128;
+                const int m0 = (local / pr.n_tiles) * rows_per_unit + crank * 128;  // this CTA's 128 rows
                 const int n0 = (local % pr.n_tiles) * kApplyBN;
                 const int wb = j % kApplyWSlots;
                 if (!mbar_wait(&w_empty[wb], ((uint32_t)(j / kApplyWSlots) & 1u) ^ 1u, abort, err, DEVERR_TIMEOUT_TMA))
@@ -153,16 +181,23 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     const int s = it % STAGES;
                     const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort, err, DEVERR_TIMEOUT_TMA)) break;
-                    mbar_arrive_expect_tx(&full[s], L::kStage);
-                    tma_load_2d(sA + s * L::kA, &pr.tmX, &full[s], kb * 64, m0);
-                    tma_load_2d(sB + s * L::kB, &pr.tmY, &full[s], kb * 64, n0);
+                    if (PAIR) {
+                        // CTA 0 expects both CTAs' bytes; each CTA loads its own halves
+                        if (crank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStage);
+                        tma_load_2d_pair(sA + s * L::kA, &pr.tmX, &full[s], kb * 64, m0);
+                        tma_load_2d_pair(sB + s * L::kB, &pr.tmY, &full[s], kb * 64, n0 + crank * (kApplyBN / 2));
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], L::kStage);
+                        tma_load_2d(sA + s * L::kA, &pr.tmX, &full[s], kb * 64, m0);
+                        tma_load_2d(sB + s * L::kB, &pr.tmY, &full[s], kb * 64, n0);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && crank == 0) {
             int it = 0, j = 0;
-            for (int u = blockIdx.x; u < total && !*abort; u += gridDim.x, ++j) {
+            for (int u = ustart; u < total && !*abort; u += ustep, ++j) {
                 const int b = j & 1;
                 if (!mbar_wait(&acc_empty[b], ((uint32_t)(j >> 1) & 1u) ^ 1u, abort, err, DEVERR_TIMEOUT_MMA)) break;
                 tc_fence_after();
@@ -175,12 +210,17 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     const uint32_t a_addr = smem_u32(sA + s * L::kA);
                     const uint32_t b_addr = smem_u32(sB + s * L::kB);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_f16_ss(d, sdesc_sw128(a_addr + kk * 32, 16, 1024), sdesc_sw128(b_addr + kk * 32, 16, 1024),
-                                    args.idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(&empty[s]);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t ad = sdesc_sw128(a_addr + kk * 32, 16, 1024);
+                        const uint64_t bd = sdesc_sw128(b_addr + kk * 32, 16, 1024);
+                        if (PAIR) umma_f16_ss_pair(d, ad, bd, args.idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                        else umma_f16_ss(d, ad, bd, args.idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    if (PAIR) umma_commit_pair(&empty[s]);
+                    else umma_commit(&empty[s]);
                 }
-                umma_commit(&acc_full[b]);
+                if (PAIR) umma_commit_pair(&acc_full[b]);
+                else umma_commit(&acc_full[b]);
             }
         }
     } else {
@@ -199,7 +239,7 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
         const uint32_t bucket_bias = nf4_bucket_bias(tab), bucket_lane = tab->bucket32[lane];
         int j = 0;
         int pending = -1;  // slot of this row group's previous store, released one unit later
-        for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
+        for (int u = ustart; u < total; u += ustep, ++j) {
             const int b = j & 1;
             const int wb = j % kApplyWSlots;
             if (!mbar_wait(&w_full[wb], (uint32_t)(j / kApplyWSlots) & 1u, abort, err, DEVERR_TIMEOUT_EPI)) break;
@@ -325,7 +365,13 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 *sp = nf4_store_amax(amax);
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[b]);
+            if (PAIR) {
+                // one arrival per warp, on CTA 0's barrier (the pair's MMA issuer)
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(smem_leader(&acc_empty[b]));
+            } else {
+                mbar_arrive(&acc_empty[b]);
+            }
             fence_proxy_async();
             named_bar(1 + q, 128);  // the four warps of this row group
             if (qleader) {
@@ -346,9 +392,11 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // the pair's MMAs and both epilogues are done with TMEM
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * kApplyBN);
+        if (PAIR) tmem_dealloc_pair(tmem, 2 * kApplyBN);
+        else tmem_dealloc(tmem, 2 * kApplyBN);
     }
 }
 

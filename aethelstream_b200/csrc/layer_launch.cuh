@@ -396,13 +396,22 @@ inline bool apply_grouped_supported(int m, int n, int r) {
     return m > 0 && n > 0 && n % 256 == 0 && r > 0 && r % 8 == 0 && r <= 1024;
 }
 
-inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
-    // Two operand stages: up to r = 256 a unit's MMAs take a fraction of its
-    // epilogue, and the freed 48 KB hold the replicated byte table; larger
-    // ranks stream more k-blocks through the same two stages.
-    constexpr int STAGES = 2;
-    using L = ApplyLayout<STAGES>;
+// Whether the apply launches use CTA pairs (cluster of two, cta_group::2).
+// On by default; AETH_APPLY_PAIR=0 in the environment selects the single-CTA
+// kernel (for comparison).
+inline bool apply_use_pair() {
+    static const bool on = [] {
+        const char* e = getenv("AETH_APPLY_PAIR");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <int STAGES, bool PAIR>
+int apply_grouped_launch_t(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
+    using L = ApplyLayout<STAGES, PAIR>;
     static_assert(1024 + L::kTotal <= 227 * 1024, "apply kernel shared memory above the per-CTA limit");
+    constexpr int rows_per_unit = PAIR ? 256 : 128;
     DeviceRuntime* rt = nullptr;
     AETH_TRY(runtime_for_current(&rt));
     for (int off = 0; off < nj; off += kApplyMaxProblems) {
@@ -411,14 +420,15 @@ inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_
         memset(&a, 0, sizeof(a));
         a.nprob = cnt;
         a.kb = (r + 63) / 64;
-        a.idesc = idesc_f16(128, kApplyBN, true, false, false);
+        a.idesc = idesc_f16(rows_per_unit, kApplyBN, true, false, false);
         int units = 0;
         for (int i = 0; i < cnt; ++i) {
             const ApplyJob& j = jobs[off + i];
             if (!apply_grouped_supported(j.m, j.n, r)) return AETH_ERR_UNSUPPORTED;
             ApplyProblem& p = a.p[i];
             AETH_TRY(make_tmap_16b(&p.tmX, j.X, (uint64_t)r, (uint64_t)j.m, r, 64, 128, true));
-            AETH_TRY(make_tmap_16b(&p.tmY, j.Y, (uint64_t)r, (uint64_t)j.n, r, 64, kApplyBN, true));
+            AETH_TRY(make_tmap_16b(&p.tmY, j.Y, (uint64_t)r, (uint64_t)j.n, r, 64, PAIR ? kApplyBN / 2 : kApplyBN,
+                                   true));
             AETH_TRY(make_tmap_2d(&p.tmW, j.wp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)(j.n / 2), (uint64_t)j.m,
                                   j.n / 2, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B));
             AETH_TRY(make_tmap_2d(&p.tmS, j.wa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(j.n / 64), (uint64_t)j.m,
@@ -436,11 +446,11 @@ inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_
             p.lr = j.lr;
             p.decay_mul = j.decay_mul;
             p.has_decay = j.has_decay;
-            units += ((j.m + 127) / 128) * p.n_tiles;
+            units += ((j.m + rows_per_unit - 1) / rows_per_unit) * p.n_tiles;
         }
         a.total_units = units;
         const int smem = 1024 + L::kTotal;
-        auto kern = apply_grouped_kernel<STAGES>;
+        auto kern = apply_grouped_kernel<STAGES, PAIR>;
         static bool attr_set[kMaxDevices] = {};
         int dev = 0;
         AETH_TRY(current_device(&dev));
@@ -448,11 +458,38 @@ inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_
             AETH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
             attr_set[dev] = true;
         }
-        const int grid = std::min(num_sms(), units);
-        kern<<<grid, kApplyThreads, smem, st>>>(a, rt->err_word);
-        AETH_LAUNCH_CHECK();
+        if (PAIR) {
+            // one cluster of two CTAs per pair unit, at most a CTA per SM
+            const int grid = 2 * std::min(num_sms() / 2, units);
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(grid);
+            cfg.blockDim = dim3(kApplyThreads);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            AETH_CUDA(cudaLaunchKernelEx(&cfg, kern, a, rt->err_word));
+        } else {
+            const int grid = std::min(num_sms(), units);
+            kern<<<grid, kApplyThreads, smem, st>>>(a, rt->err_word);
+            AETH_LAUNCH_CHECK();
+        }
     }
     return AETH_OK;
+}
+
+inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
+    // Two operand stages of 48 KB (single CTA) or three of 32 KB (pair): up to
+    // r = 256 a unit's MMAs take a fraction of its epilogue; larger ranks
+    // stream more k-blocks through the same ring, where the pair's smaller
+    // per-SM operand bytes matter.
+    if (apply_use_pair()) return apply_grouped_launch_t<3, true>(jobs, nj, r, st);
+    return apply_grouped_launch_t<2, false>(jobs, nj, r, st);
 }
 
 }  // namespace aeth
