@@ -28,7 +28,8 @@
 // barriers, and each CTA's epilogue processes its own 128 rows as above.  At
 // large ranks the single-CTA kernel is bound by the operand bytes it can keep
 // in flight per SM (two 48 KB stages for 384 KB per unit at r = 512); the pair
-// moves a third fewer bytes per SM through three stages of the same memory.
+// moves a third fewer bytes per SM through four stages of nearly the same
+// memory (the NF4 byte table needs 16 copies, not 32).
 #pragma once
 #include "nf4.cuh"
 #include "umma.cuh"

@@ -13,6 +13,16 @@ namespace aeth {
 // ---------------------------------------------------------------------------
 // K4
 // ---------------------------------------------------------------------------
+// Whether the projection uses CTA pairs where the rank allows (on by
+// default; AETH_PROJ_PAIR=0 selects the single-CTA kernel, for comparison).
+inline bool proj_use_pair() {
+    static const bool on = [] {
+        const char* e = getenv("AETH_PROJ_PAIR");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 struct ProjJob {
     const void* grad;       // bf16 m x n (ksplit > 1: the stacked terms of grad_split_kernel)
     const uint16_t* projT;  // bf16 r x s (s = min(m, n)); ksplit > 1: r x projk_ld*s, the projector repeated
@@ -98,12 +108,107 @@ int proj_grouped_launch_bn(const ProjJob* jobs, int nj, int r, cudaStream_t st) 
     return AETH_OK;
 }
 
-// Projects and accumulates every job; jobs must share the rank r.  Ranks
-// above 256 (one MMA's N) run as column slices of at most 256 of R, each a
-// launch over its rows of projT: R[:, c0:c1] += G Q[:, c0:c1].  The gradient
-// is read once per slice.
+// The CTA-pair projection (proj_pair_kernel) for rank RT: all of R's columns
+// in one pass over each gradient.
+template <int RT, int STAGES>
+int proj_pair_launch(const ProjJob* jobs, int nj, cudaStream_t st) {
+    using L = ProjPairLayout<RT, STAGES>;
+    static_assert(1024 + L::kTotal <= 227 * 1024, "paired projection shared memory above the per-CTA limit");
+    DeviceRuntime* rt = nullptr;
+    AETH_TRY(runtime_for_current(&rt));
+    const int clusters = num_sms() / 2;
+    for (int off = 0; off < nj; off += kProjMaxProblems) {
+        const int cnt = std::min(kProjMaxProblems, nj - off);
+        const ProjJob* js = jobs + off;
+        ProjArgs a;
+        memset(&a, 0, sizeof(a));
+        a.nprob = cnt;
+        a.r = RT;
+        a.idesc_k = idesc_f16(256, L::kNmma, true, false, false);
+        a.idesc_mn = idesc_f16(256, L::kNmma, true, true, false);
+        // split-K depth minimising the round-robin makespan over the clusters
+        // (an epilogue counted as RT / 64 k-blocks of work)
+        int kb_target = 8;
+        {
+            int64_t best = -1;
+            for (int kt = 8; kt <= 256; kt += (kt < 64 ? 1 : 8)) {
+                int64_t units_k = 0, per_unit = 0;
+                for (int i = 0; i < cnt; ++i) {
+                    const int l = std::max(js[i].m, js[i].n), s = std::min(js[i].m, js[i].n) * js[i].ksplit;
+                    const int kbt = (s + 63) / 64;
+                    int sp = (kbt + kt - 1) / kt;
+                    const int kpu = (kbt + sp - 1) / sp;
+                    sp = (kbt + kpu - 1) / kpu;
+                    units_k += (int64_t)((l + 255) / 256) * sp;
+                    per_unit = std::max<int64_t>(per_unit, kpu);
+                }
+                const int64_t span = (units_k + clusters - 1) / clusters * (per_unit + RT / 64);
+                if (best < 0 || span < best) { best = span; kb_target = kt; }
+            }
+        }
+        int units = 0;
+        for (int i = 0; i < cnt; ++i) {
+            const ProjJob& j = js[i];
+            ProjProblem& p = a.p[i];
+            const bool right = j.m >= j.n;
+            const int l = right ? j.m : j.n, s = (right ? j.n : j.m) * j.ksplit;
+            const int s1 = right ? j.n : j.m;
+            if (right) AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)s, (uint64_t)j.m, s, 64, 128, true));
+            else AETH_TRY(make_tmap_16b(&p.tmA, j.grad, (uint64_t)j.n, (uint64_t)s, j.n, 64, 64, true));
+            AETH_TRY(make_tmap_16b(&p.tmB, j.projT, (uint64_t)s, (uint64_t)RT, (int64_t)s1 * j.projk_ld, 64,
+                                   L::kNmma / 2, true));
+            AETH_TRY(make_tmap_2d(&p.tmC, j.racc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)RT, (uint64_t)l,
+                                  j.ldr > 0 ? j.ldr : RT, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B));
+            p.a_mn = right ? 0 : 1;
+            p.kb_total = (s + 63) / 64;
+            p.splits = (p.kb_total + kb_target - 1) / kb_target;
+            p.kb_per_unit = (p.kb_total + p.splits - 1) / p.splits;
+            p.splits = (p.kb_total + p.kb_per_unit - 1) / p.kb_per_unit;
+            p.unit_begin = units;
+            units += ((l + 255) / 256) * p.splits;
+        }
+        a.total_units = units;
+        const int smem = 1024 + L::kTotal;
+        auto kern = proj_pair_kernel<RT, STAGES>;
+        static bool attr_set[kMaxDevices] = {};
+        int dev = 0;
+        AETH_TRY(current_device(&dev));
+        if (!attr_set[dev]) {
+            AETH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            attr_set[dev] = true;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * std::min(clusters, units));
+        cfg.blockDim = dim3(192);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        AETH_CUDA(cudaLaunchKernelEx(&cfg, kern, a, rt->err_word));
+    }
+    return AETH_OK;
+}
+
+// Projects and accumulates every job; jobs must share the rank r.  Ranks 64,
+// 128, 256 and 512 run on CTA pairs in one pass over each gradient
+// (proj_pair_kernel).  Other ranks run on single CTAs; above 256 (one MMA's
+// N) as column slices of at most 256 of R, each a launch over its rows of
+// projT (R[:, c0:c1] += G Q[:, c0:c1]), reading the gradient once per slice.
 inline int proj_grouped_launch(const ProjJob* jobs, int nj, int r, cudaStream_t st) {
     if (r <= 0 || r > 1024 || r % 8 != 0) return AETH_ERR_UNSUPPORTED;
+    bool plain = true;  // the pair kernel writes R with its own row stride r
+    for (int i = 0; i < nj; ++i) plain = plain && (jobs[i].ldr == 0 || jobs[i].ldr == r);
+    if (plain && proj_use_pair()) {
+        if (r == 512) return proj_pair_launch<512, 4>(jobs, nj, st);
+        if (r == 256) return proj_pair_launch<256, 6>(jobs, nj, st);
+        if (r == 128) return proj_pair_launch<128, 8>(jobs, nj, st);
+        if (r == 64) return proj_pair_launch<64, 8>(jobs, nj, st);
+    }
     if (r > 256) {
         if (r % 64 != 0) return AETH_ERR_UNSUPPORTED;
         for (int c0 = 0; c0 < r; c0 += 256) {
@@ -484,11 +589,11 @@ int apply_grouped_launch_t(const ApplyJob* jobs, int nj, int r, cudaStream_t st)
 }
 
 inline int apply_grouped_launch(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
-    // Two operand stages of 48 KB (single CTA) or three of 32 KB (pair): up to
+    // Two operand stages of 48 KB (single CTA) or four of 32 KB (pair): up to
     // r = 256 a unit's MMAs take a fraction of its epilogue; larger ranks
     // stream more k-blocks through the same ring, where the pair's smaller
     // per-SM operand bytes matter.
-    if (apply_use_pair()) return apply_grouped_launch_t<3, true>(jobs, nj, r, st);
+    if (apply_use_pair()) return apply_grouped_launch_t<4, true>(jobs, nj, r, st);
     return apply_grouped_launch_t<2, false>(jobs, nj, r, st);
 }
 

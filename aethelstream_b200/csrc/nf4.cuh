@@ -128,11 +128,11 @@ __device__ __forceinline__ void nf4_quant_regs(const float (&v)[N], float amax, 
 
 // ---------------------------------------------------------------------------
 // Tables for the fused epilogues.  byte_rep: the 256-entry byte table
-// (CODES[byte >> 4], CODES[byte & 15]) in 32 copies, entry b of copy c at
-// byte offset 256 b + 8 c, so the 16 lanes of a half-warp (copy = lane) read
-// 16 different bank pairs whatever their bytes: one 8-byte lookup costs the
-// minimum two wavefronts per warp, and the 256-byte entry stride lets one
-// byte permute form the whole offset (nf4_dequant_word_s).
+// (CODES[byte >> 4], CODES[byte & 15]) in 16 copies, entry b of copy c at
+// byte offset 128 b + 8 c, so the 16 lanes of a half-warp (copy = lane % 16;
+// an 8-byte load is served per half-warp) read 16 different bank pairs
+// whatever their bytes: one lookup costs the minimum two wavefronts per warp.
+// One byte permute and a shift form the offset (nf4_dequant_word_s).
 //
 // Buckets: bucket b = rint(14 xn) + 14 (0..28; width 1/14 is narrower than the
 // smallest gap between midpoints, 0.085, and every midpoint lies at least
@@ -156,7 +156,7 @@ constexpr float kNf4BucketScale = 14.0f;
 constexpr float kNf4BucketMagic = 12582926.0f;  // 1.5 * 2^23 + 14
 
 struct Nf4Tables32 {
-    float2 byte_rep[256 * 32];
+    float2 byte_rep[256 * 16];
     uint32_t bucket32[32];  // entries 0..28 used; 29..31 hold the top code, as the lanes do
 };
 
@@ -180,8 +180,8 @@ __device__ __forceinline__ uint32_t nf4_bucket32_entry(int b) {
 }
 
 __device__ __forceinline__ void nf4_tables32_init(Nf4Tables32* t, int tid, int nthreads) {
-    for (int i = tid; i < 256 * 32; i += nthreads)
-        t->byte_rep[i] = make_float2(c_nf4_codes[i >> 9], c_nf4_codes[(i >> 5) & 15]);
+    for (int i = tid; i < 256 * 16; i += nthreads)  // entry i >> 4, copy i & 15
+        t->byte_rep[i] = make_float2(c_nf4_codes[i >> 8], c_nf4_codes[(i >> 4) & 15]);
     for (int b = tid; b < 32; b += nthreads) t->bucket32[b] = nf4_bucket32_entry(b);
 }
 
@@ -326,14 +326,14 @@ __global__ void nf4_classify_selfcheck_kernel(float amax, unsigned long long* __
 }
 
 // Shared address of the replicated byte table, and this lane's copy offset
-// (lane * 8, below 256: one byte).
+// before the final halving ((lane % 16) * 16, below 256: one byte).
 __device__ __forceinline__ uint32_t nf4_byte_rep_base(const Nf4Tables32* t) { return smem_u32_addr(t->byte_rep); }
-__device__ __forceinline__ uint32_t nf4_byte_rep_lane(int lane) { return (uint32_t)(lane & 31) * 8u; }
+__device__ __forceinline__ uint32_t nf4_byte_rep_lane(int lane) { return (uint32_t)(lane & 15) * 16u; }
 
 // Dequantise one packed word (8 elements) with this lane's copy of the byte
-// table; one packed multiply per byte.  The offset 256 byte + 8 lane is one
-// byte permute: byte 0 = the lane offset, byte 1 = byte k of the word, bytes
-// 2 and 3 = the lane offset's zero byte 1.
+// table; one packed multiply per byte.  The offset 128 byte + 8 copy is half
+// of one byte permute: byte 0 = the lane offset, byte 1 = byte k of the word,
+// bytes 2 and 3 = the lane offset's zero byte 1.
 __device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, uint32_t rep_base, uint32_t lane_off,
                                                    float* out8) {
     const float2 a2 = make_float2(amax, amax);
@@ -342,7 +342,7 @@ __device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, ui
         float2 c;
         asm("ld.shared.v2.f32 {%0, %1}, [%2];"
             : "=f"(c.x), "=f"(c.y)
-            : "r"(rep_base + prmt(word, lane_off, 0x5504u | ((uint32_t)k << 4))));
+            : "r"(rep_base + (prmt(word, lane_off, 0x5504u | ((uint32_t)k << 4)) >> 1)));
         const float2 p = mul2_rn(c, a2);
         out8[2 * k] = p.x;
         out8[2 * k + 1] = p.y;

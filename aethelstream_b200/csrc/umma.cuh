@@ -186,7 +186,7 @@ __device__ __forceinline__ void cluster_sync() {
 // CTA rank is bit 24 of a shared-window address).
 __device__ __forceinline__ uint32_t smem_leader(const void* p) { return smem_u32(p) & 0xFEFFFFFFu; }
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA tile load into this CTA's shared memory whose completed bytes count on
 // the barrier at the same offset in CTA 0 (the pair's MMA issuer waits there).
