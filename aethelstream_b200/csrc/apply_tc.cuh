@@ -278,8 +278,8 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                     float w[16];
                     // words 2c, 2c+1 of the block
                     const uint4 qa = c < 2 ? q01 : q23;
-                    nf4_dequant_word_s((c & 1) ? qa.z : qa.x, amax_old, rep_base, rep_lane, w);
-                    nf4_dequant_word_s((c & 1) ? qa.w : qa.y, amax_old, rep_base, rep_lane, w + 8);
+                    nf4_dequant_word_s<true>((c & 1) ? qa.z : qa.x, amax_old, rep_base, rep_lane, w);
+                    nf4_dequant_word_s<true>((c & 1) ? qa.w : qa.y, amax_old, rep_base, rep_lane, w + 8);
                     // w <- fl(w - lr * dW), one fused multiply-add per element (paired),
                     // then the decoupled decay.  The reference rounds lr * dW first; the
                     // two differ by under half an ulp of the product, inside the update's

@@ -330,19 +330,24 @@ __global__ void nf4_classify_selfcheck_kernel(float amax, unsigned long long* __
 __device__ __forceinline__ uint32_t nf4_byte_rep_base(const Nf4Tables32* t) { return smem_u32_addr(t->byte_rep); }
 __device__ __forceinline__ uint32_t nf4_byte_rep_lane(int lane) { return (uint32_t)(lane & 15) * 16u; }
 
-// Dequantise one packed word (8 elements) with this lane's copy of the byte
-// table; one packed multiply per byte.  The offset 128 byte + 8 copy is half
-// of one byte permute: byte 0 = the lane offset, byte 1 = byte k of the word,
-// bytes 2 and 3 = the lane offset's zero byte 1.
+// Dequantise one packed word (8 elements) with this lane's copy of a
+// replicated byte table; one packed multiply per byte.  One byte permute
+// forms 256 byte + lane_off (byte 0 = the lane offset, byte 1 = byte k of the
+// word, bytes 2 and 3 = the lane offset's zero byte 1): the offset itself for
+// a table with a 256-byte entry stride (STRIDE128 = false: LOMO's, lane_off =
+// 8 x copy), half of it for Nf4Tables32's 128-byte stride (lane_off = 16 x
+// copy, nf4_byte_rep_lane).
+template <bool STRIDE128 = false>
 __device__ __forceinline__ void nf4_dequant_word_s(uint32_t word, float amax, uint32_t rep_base, uint32_t lane_off,
                                                    float* out8) {
     const float2 a2 = make_float2(amax, amax);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         float2 c;
+        const uint32_t off = prmt(word, lane_off, 0x5504u | ((uint32_t)k << 4));
         asm("ld.shared.v2.f32 {%0, %1}, [%2];"
             : "=f"(c.x), "=f"(c.y)
-            : "r"(rep_base + (prmt(word, lane_off, 0x5504u | ((uint32_t)k << 4)) >> 1)));
+            : "r"(rep_base + (STRIDE128 ? off >> 1 : off)));
         const float2 p = mul2_rn(c, a2);
         out8[2 * k] = p.x;
         out8[2 * k + 1] = p.y;
