@@ -1724,6 +1724,7 @@ int aeth_rsvd_omega(uint64_t seed, int64_t count, float* out, aeth_stream_t stre
 
 int aeth_rsvd_jacobi(float* mat, int n, float* u, aeth_stream_t stream) {
     if (!mat || !u || n < 1) return set_err(AETH_ERR_ARG);
+    if (n > kJacobiMaxN) return set_err(AETH_ERR_UNSUPPORTED);
     jacobi50_kernel<<<1, 1024, 0, to_stream(stream)>>>(mat, n, u);
     AETH_CUDA(cudaGetLastError());
     return AETH_OK;

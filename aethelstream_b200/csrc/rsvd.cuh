@@ -306,58 +306,97 @@ __global__ void __launch_bounds__(1024) chol_inverse_kernel(double* __restrict__
 }
 
 // ---------------------------------------------------------------------------
-// One CTA, blocked by 32 columns: the same factorisation and inverse as
-// chol_inverse_kernel for l <= kCholMaxL, in far fewer passes over memory.
-//   Cholesky (right-looking): the 32-column panel below the diagonal is held
-//   in shared memory (pitch 33 doubles); warp 0 factors the diagonal block,
-//   one thread per row solves the panel against it, and the warps then update
-//   the trailing lower triangle one 32 x 32 block each (lane = row, 32
-//   accumulators; the panel rows of the column block are broadcast reads).
+// A cluster of kCholCtas CTAs, blocked by 32 columns: the same factorisation
+// and inverse as chol_inverse_kernel for l <= kCholMaxL.  The matrix stays in
+// global memory (L2-resident); the CTAs meet at hardware cluster barriers,
+// whose release / acquire order their global writes for each other.
+//   Cholesky (right-looking), per 32-column step: every CTA loads the panel
+//   below the diagonal into shared memory (pitch 33 doubles) and factors it
+//   redundantly -- warp 0 the diagonal block in registers (lane = row, the
+//   pivots and scaled columns by shuffle), one thread per row the solve
+//   against it -- so all CTAs hold the same panel without an exchange; the
+//   32 x 32 blocks of the trailing lower triangle are then shared out over
+//   the cluster's warps (lane = row, 32 accumulators; the panel rows of the
+//   column block are broadcast reads).  CTA 0 writes each factored panel
+//   back after the step's closing barrier, when no CTA still reads it.
 //   Inverse: each diagonal block's inverse by one warp (lane = column,
-//   forward substitution), then block column jb of L^-1 by warp jb % warps:
-//   X_ij = -inv(L_ii) sum_{k = j}^{i-1} L_ik X_kj, i increasing.
-// *fail = 1 when a pivot is not positive (or NaN).
+//   forward substitution); then block rows ib in order,
+//   X_ij = -inv(L_ii) sum_{k = j}^{i-1} L_ik X_kj, with the (jb, 4-column
+//   group) pieces of block row ib shared out over the cluster's warps.
+// *fail = 1 when a pivot is not positive (or NaN); every CTA reaches the same
+// decision at the same step (identical redundant arithmetic), so all leave
+// together.
 // ---------------------------------------------------------------------------
 constexpr int kCholMaxL = 640;
 constexpr int kCholThreads = 512;
+constexpr int kCholCtas = 8;
 constexpr size_t kCholSmem = sizeof(double) * kCholMaxL * 33;  // also a 32-row block of L in the inverse
 static_assert(32 * (kCholMaxL + 1) <= kCholMaxL * 33, "the inverse's block row of L must fit the panel buffer");
 
-__global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __restrict__ a, int l,
+__device__ __forceinline__ void chol_store_panel(double* __restrict__ a, const double* __restrict__ pan, int l, int k0,
+                                                 int kw) {
+    const int prow = l - k0;
+    for (int t = threadIdx.x; t < prow * 32; t += blockDim.x) {
+        const int i = t >> 5, c = t & 31;
+        if (c < kw && c <= i) a[(int64_t)(k0 + i) * l + k0 + c] = pan[i * 33 + c];
+    }
+}
+
+__global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __restrict__ a, int l,
                                                                     double* __restrict__ linv, int* __restrict__ fail) {
     extern __shared__ double pan[];  // (l - k0) x 33
     __shared__ double rdiag[32];
     __shared__ int bad;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int crank = (int)cluster_ctarank();
+    const int gw = crank * nwarps + warp, gwarps = kCholCtas * nwarps;  // warp index over the cluster
     const int nb = (l + 31) / 32;
     if (tid == 0) bad = 0;
     __syncthreads();
-    for (int kb = 0; kb < nb; ++kb) {
+    int kb = 0;
+    for (; kb < nb; ++kb) {
         const int k0 = kb * 32, kw = min(32, l - k0), prow = l - k0;
+        if (kb > 0 && crank == 0) {  // the previous panel, which no CTA reads any more
+            chol_store_panel(a, pan, l, k0 - 32, 32);
+            __syncthreads();
+        }
         for (int t = tid; t < prow * 32; t += blockDim.x) {
             const int i = t >> 5, c = t & 31;
             pan[i * 33 + c] = (c < kw && c <= i) ? a[(int64_t)(k0 + i) * l + k0 + c] : 0.0;
         }
         __syncthreads();
         if (warp == 0) {
-            for (int c = 0; c < kw; ++c) {
-                const double d = pan[c * 33 + c];
-                const bool ok = d > 0.0;
-                const double piv = ok ? sqrt(d) : 1.0;
-                __syncwarp();
-                if (!ok && lane == 0) bad = 1;
-                if (lane == c) pan[c * 33 + c] = piv;
-                if (lane > c && lane < kw) pan[lane * 33 + c] /= piv;
-                __syncwarp();
-                if (lane > c && lane < kw) {
-                    const double lic = pan[lane * 33 + c];
-                    for (int j = c + 1; j <= lane; ++j) pan[lane * 33 + j] -= lic * pan[j * 33 + c];
+            // the diagonal block in registers, lane = row: column c's pivot comes
+            // by shuffle, the lanes below scale their entry, and every lane
+            // updates its row's later columns with the scaled column (shuffled)
+            double r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = (lane < kw && j <= lane) ? pan[lane * 33 + j] : 0.0;
+            bool okall = true;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                if (c < kw) {  // warp-uniform
+                    const double d = __shfl_sync(0xffffffffu, r[c], c);
+                    const bool ok = d > 0.0;
+                    okall = okall && ok;
+                    const double piv = ok ? sqrt(d) : 1.0;
+                    if (lane == c) r[c] = piv;
+                    else if (lane > c) r[c] = r[c] / piv;
+#pragma unroll
+                    for (int j = c + 1; j < 32; ++j) {
+                        const double ljc = __shfl_sync(0xffffffffu, r[c], j);
+                        if (lane >= j) r[j] -= r[c] * ljc;
+                    }
                 }
-                __syncwarp();
             }
+            if (!okall && lane == 0) bad = 1;
+            if (lane < kw)
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (j <= lane) pan[lane * 33 + j] = r[j];
         }
         __syncthreads();
-        if (bad) break;
+        if (bad) break;  // the same step in every CTA
         // the panel below the diagonal block: row i solves x L_kk^T = a_i
         // (one reciprocal per pivot instead of a division per element)
         if (tid < 32) rdiag[tid] = tid < kw ? 1.0 / pan[tid * 33 + tid] : 0.0;
@@ -380,14 +419,11 @@ __global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __re
                 if (c < kw) pan[i * 33 + c] = x[c];
         }
         __syncthreads();
-        for (int t = tid; t < prow * 32; t += blockDim.x) {
-            const int i = t >> 5, c = t & 31;
-            if (c < kw && c <= i) a[(int64_t)(k0 + i) * l + k0 + c] = pan[i * 33 + c];
-        }
-        // trailing update of the lower triangle: blocks (ib, jb), kb < jb <= ib
+        // trailing update of the lower triangle: blocks (ib, jb), kb < jb <= ib,
+        // shared out over the cluster's warps
         const int q = nb - kb - 1;
         const int pairs = q * (q + 1) / 2;
-        for (int p = warp; p < pairs; p += nwarps) {
+        for (int p = gw; p < pairs; p += gwarps) {
             int bi = (int)((sqrt(8.0 * p + 1.0) - 1.0) * 0.5);
             while ((bi + 1) * (bi + 2) / 2 <= p) ++bi;
             while (bi * (bi + 1) / 2 > p) --bi;
@@ -412,14 +448,16 @@ __global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __re
                 }
             }
         }
-        __syncthreads();
+        cluster_sync();  // the trailing updates of every CTA before the next panel load
     }
     if (bad) {
-        if (tid == 0) *fail = 1;
-        return;
+        if (crank == 0 && tid == 0) *fail = 1;
+        return;  // every CTA of the cluster leaves here, with no barrier outstanding
     }
+    if (crank == 0) chol_store_panel(a, pan, l, (nb - 1) * 32, l - (nb - 1) * 32);
+    cluster_sync();
     // L^-1: diagonal blocks first (lane = column c of the block's inverse)
-    for (int db = warp; db < nb; db += nwarps) {
+    for (int db = gw; db < nb; db += gwarps) {
         const int d0 = db * 32, dw = min(32, l - d0);
         double x[32];
 #pragma unroll
@@ -437,64 +475,57 @@ __global__ void __launch_bounds__(kCholThreads) chol_blocked_kernel(double* __re
             for (int i = 0; i < 32; ++i)
                 if (i < dw) linv[(int64_t)(d0 + i) * l + d0 + lane] = x[i];
     }
-    __syncthreads();
+    cluster_sync();
     // off-diagonal blocks by block rows: X_ij = -inv(L_ii) sum_{k = j}^{i-1}
-    // L_ik X_kj needs only earlier block rows of L^-1.  For block row ib the
-    // CTA stages L's rows i0 .. i0 + 31 (columns < i0) in shared memory,
-    // then warp jb (< ib) forms block (ib, jb): lane = row, 32 accumulators,
-    // the rows of X_kj read as coalesced broadcasts, eight k in flight.
+    // L_ik X_kj needs only earlier block rows of L^-1.  For block row ib every
+    // CTA stages L's rows i0 .. i0 + 31 (columns < i0) in shared memory; the
+    // pieces (jb < ib, 4-column group g) go to the cluster's warps: lane =
+    // row, 4 accumulators, the rows of X_kj read as broadcasts, then the
+    // 4 columns of -inv(L_ii) S through shuffles of S's rows.
     const int pitch = l + 1;  // odd pitch: the lanes' rows fall in different banks
     for (int ib = 1; ib < nb; ++ib) {
         const int i0 = ib * 32, iw = min(32, l - i0);
-        __syncthreads();
         // columns 0 .. i0 - 1 of the block row (i0 < l < pitch)
         for (int t = tid; t < 32 * i0; t += blockDim.x) {
             const int r = t / i0, k = t % i0;
             pan[r * pitch + k] = r < iw ? a[(int64_t)(i0 + r) * l + k] : 0.0;
         }
         __syncthreads();
-        for (int jb = warp; jb < ib; jb += nwarps) {
-            const int j0 = jb * 32, jw = min(32, l - j0);
-            double acc[32];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) acc[c] = 0.0;
+        const double* drow = linv + (int64_t)(i0 + min(lane, iw - 1)) * l + i0;
+        for (int piece = gw; piece < ib * 8; piece += gwarps) {
+            const int jb = piece >> 3, c0 = jb * 32 + (piece & 7) * 4;
+            const int jw = min(32, l - jb * 32);
+            if ((piece & 7) * 4 >= jw) continue;  // a ragged last block column
+            double acc[4] = {0.0, 0.0, 0.0, 0.0};
             const double* lrow = pan + lane * pitch;
 #pragma unroll 4
-            for (int k = j0; k < i0; ++k) {
+            for (int k = jb * 32; k < i0; ++k) {
                 const double lik = lrow[k];
-                const double* xr = linv + (int64_t)k * l + j0;
+                const double* xr = linv + (int64_t)k * l + c0;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) acc[c] += lik * (c < jw ? xr[c] : 0.0);
+                for (int c = 0; c < 4; ++c) acc[c] += lik * (c0 + c < l ? xr[c] : 0.0);
             }
-            // acc = S row `lane`; X_ij = -inv(L_ii) S through shuffles of S's
-            // rows, 16 output columns at a time
-            const double* drow = linv + (int64_t)(i0 + min(lane, iw - 1)) * l + i0;
+            double out[4] = {0.0, 0.0, 0.0, 0.0};
+            for (int t = 0; t < iw; ++t) {
+                const double dinv = lane < iw ? drow[t] : 0.0;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                double out[16];
-#pragma unroll
-                for (int c = 0; c < 16; ++c) out[c] = 0.0;
-                for (int t = 0; t < iw; ++t) {
-                    const double dinv = lane < iw ? drow[t] : 0.0;
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) out[c] -= dinv * __shfl_sync(0xffffffffu, acc[16 * h + c], t);
-                }
-                if (lane < iw)
-#pragma unroll
-                    for (int c = 0; c < 16; ++c)
-                        if (16 * h + c < jw) linv[(int64_t)(i0 + lane) * l + j0 + 16 * h + c] = out[c];
+                for (int c = 0; c < 4; ++c) out[c] -= dinv * __shfl_sync(0xffffffffu, acc[c], t);
             }
+            if (lane < iw)
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (c0 + c < l && c0 + c < jb * 32 + jw) linv[(int64_t)(i0 + lane) * l + c0 + c] = out[c];
         }
+        cluster_sync();  // block row ib of L^-1 for every CTA; the staging buffer is free again
     }
-    __syncthreads();
     // zero the strict upper triangle of L^-1 (callers read all of it)
-    for (int64_t t = tid; t < (int64_t)l * l; t += blockDim.x) {
+    for (int64_t t = (int64_t)crank * blockDim.x + tid; t < (int64_t)l * l; t += (int64_t)kCholCtas * blockDim.x) {
         const int i = (int)(t / l), j = (int)(t % l);
         if (j > i) linv[t] = 0.0;
     }
 }
 
-// Cholesky and inverse of the l x l Gram matrix: the blocked kernel when its
+// Cholesky and inverse of the l x l Gram matrix: the cluster kernel when its
 // panel fits shared memory, else the per-element one.
 inline int chol_inverse(double* gram, int l, double* linv, int* fail, cudaStream_t st) {
     if (l <= kCholMaxL) {
@@ -502,11 +533,24 @@ inline int chol_inverse(double* gram, int l, double* linv, int* fail, cudaStream
         int dev = 0;
         AETH_TRY(current_device(&dev));
         if (!attr_set[dev]) {
-            AETH_CUDA(cudaFuncSetAttribute(chol_blocked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            AETH_CUDA(cudaFuncSetAttribute(chol_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)kCholSmem));
             attr_set[dev] = true;
         }
-        chol_blocked_kernel<<<1, kCholThreads, kCholSmem, st>>>(gram, l, linv, fail);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(kCholCtas);
+        cfg.blockDim = dim3(kCholThreads);
+        cfg.dynamicSmemBytes = kCholSmem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = kCholCtas;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        AETH_CUDA(cudaLaunchKernelEx(&cfg, chol_cluster_kernel, gram, l, linv, fail));
+        return AETH_OK;
     } else {
         chol_inverse_kernel<<<1, 1024, 0, st>>>(gram, l, linv, fail);
     }
@@ -566,46 +610,88 @@ __global__ void __launch_bounds__(1024) mgs_clamped_kernel(float* __restrict__ q
 }
 
 // ---------------------------------------------------------------------------
-// One CTA: jacobi_eigenvectors (randomized_svd.rs:210-271) on the f32 l x l
-// matrix `mat` (destroyed), eigenvector estimate into u.
+// One CTA: jacobi_eigenvectors (randomized_svd.rs:210-271) on the f32 n x n
+// matrix `mat` (destroyed), eigenvector estimate into u.  Bit-exact with the
+// reference's loop: each rotation zeroes the largest |a_ij|, i < j, the first
+// in row-major order winning ties (a strict > scan, so NaN and zero entries
+// are never picked), with the reference's arithmetic.
+//
+// The pick keeps a running maximum per row in shared memory (value and first
+// column of the row's upper part) instead of rescanning the matrix: the
+// global pick is the largest row maximum, the first row winning ties, which
+// is the first maximal element in row-major order.  A rotation of (p, q)
+// rewrites rows p and q (rescanned by one warp each) and, in every other row
+// k < q, the upper entries (k, p) and (k, q): a row whose maximum sat in one
+// of those columns is rescanned, any other takes the new entries into its
+// maximum by the same comparison rules.
 // ---------------------------------------------------------------------------
+constexpr int kJacobiMaxN = 2048;
+
+// First maximum of |mat[i][j]|, j > i, over the warp's lanes (strict >; the
+// smaller column on equal values).
+__device__ __forceinline__ void jacobi_row_scan(const float* __restrict__ mat, int n, int i, int lane, float& v,
+                                                int& idx) {
+    float bv = 0.0f;
+    int bi = -1;
+    for (int j = i + 1 + lane; j < n; j += 32) {
+        const float x = fabsf(mat[(int64_t)i * n + j]);
+        if (x > bv) { bv = x; bi = j; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi >= 0 && (bi < 0 || oi < bi))) { bv = ov; bi = oi; }
+    }
+    v = bv;
+    idx = bi;
+}
+
 __global__ void __launch_bounds__(1024) jacobi50_kernel(float* __restrict__ mat, int n, float* __restrict__ u) {
+    __shared__ float rmax[kJacobiMaxN];
+    __shared__ int ridx[kJacobiMaxN];
+    __shared__ int rescan[kJacobiMaxN];
     __shared__ float red_v[32];
     __shared__ int red_i[32];
-    __shared__ int s_p, s_q, s_stop;
+    __shared__ int s_p, s_q, s_stop, s_nres;
     __shared__ float s_c, s_s;
-    for (int64_t t = threadIdx.x; t < (int64_t)n * n; t += blockDim.x) u[t] = (t / n == t % n) ? 1.0f : 0.0f;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    for (int64_t t = tid; t < (int64_t)n * n; t += blockDim.x) u[t] = (t / n == t % n) ? 1.0f : 0.0f;
+    for (int i = warp; i < n; i += nwarps) {
+        float v;
+        int idx;
+        jacobi_row_scan(mat, n, i, lane, v, idx);
+        if (lane == 0) { rmax[i] = v; ridx[i] = idx; }
+    }
     __syncthreads();
     for (int it = 0; it < 50; ++it) {
-        // largest |a_ij|, i < j; the first in row-major order wins ties (strict > scan)
+        // the largest row maximum, the first row on ties
         float bv = 0.0f;
         int bi = -1;
-        for (int64_t f = threadIdx.x; f < (int64_t)n * n; f += blockDim.x) {
-            const int i = (int)(f / n), j = (int)(f % n);
-            if (j <= i) continue;
-            const float v = fabsf(mat[f]);
-            if (v > bv) { bv = v; bi = (int)f; }
-        }
+        for (int i = tid; i < n; i += blockDim.x)
+            if (ridx[i] >= 0 && rmax[i] > bv) { bv = rmax[i]; bi = i; }
+#pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov > bv || (ov == bv && oi >= 0 && (bi < 0 || oi < bi))) { bv = ov; bi = oi; }
         }
-        if ((threadIdx.x & 31) == 0) { red_v[threadIdx.x >> 5] = bv; red_i[threadIdx.x >> 5] = bi; }
+        if (lane == 0) { red_v[warp] = bv; red_i[warp] = bi; }
         __syncthreads();
-        if (threadIdx.x == 0) {
+        if (tid == 0) {
             float v = 0.0f;
-            int idx = -1;
-            for (int w = 0; w < (int)(blockDim.x >> 5); ++w)
-                if (red_v[w] > v || (red_v[w] == v && red_i[w] >= 0 && (idx < 0 || red_i[w] < idx))) {
+            int row = -1;
+            for (int w = 0; w < nwarps; ++w)
+                if (red_v[w] > v || (red_v[w] == v && red_i[w] >= 0 && (row < 0 || red_i[w] < row))) {
                     v = red_v[w];
-                    idx = red_i[w];
+                    row = red_i[w];
                 }
             // reference defaults p = 0, q = 1 and stops when max_off < 1e-10
             s_stop = v < 1e-10f;
-            const int p = idx >= 0 ? idx / n : 0, q = idx >= 0 ? idx % n : 1;
+            const int p = row >= 0 ? row : 0, q = row >= 0 ? ridx[row] : 1;
             s_p = p;
             s_q = q;
+            s_nres = 0;
             if (!s_stop) {
                 const float app = mat[(int64_t)p * n + p], aqq = mat[(int64_t)q * n + q], apq = mat[(int64_t)p * n + q];
                 const float tau = __fdiv_rn(__fsub_rn(aqq, app), __fmul_rn(2.0f, apq));
@@ -622,7 +708,7 @@ __global__ void __launch_bounds__(1024) jacobi50_kernel(float* __restrict__ mat,
         const int p = s_p, q = s_q;
         const float c = s_c, s = s_s;
         // rows k other than p, q read only their own (unchanged) entries
-        for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        for (int k = tid; k < n; k += blockDim.x) {
             if (k != p && k != q) {
                 const float mkp = mat[(int64_t)k * n + p], mkq = mat[(int64_t)k * n + q];
                 const float np_ = __fsub_rn(__fmul_rn(c, mkp), __fmul_rn(s, mkq));
@@ -631,12 +717,29 @@ __global__ void __launch_bounds__(1024) jacobi50_kernel(float* __restrict__ mat,
                 mat[(int64_t)p * n + k] = np_;
                 mat[(int64_t)k * n + q] = nq_;
                 mat[(int64_t)q * n + k] = nq_;
+                // row k's maximum over its upper part (k < p: column p; k < q: column q)
+                if (k < q) {
+                    if (ridx[k] == p || ridx[k] == q) {
+                        rescan[atomicAdd(&s_nres, 1)] = k;
+                    } else {
+                        float v = rmax[k];
+                        int idx = ridx[k];
+                        if (k < p) {
+                            const float x = fabsf(np_);
+                            if (x > v || (x == v && idx >= 0 && p < idx)) { v = x; idx = p; }
+                        }
+                        const float x = fabsf(nq_);
+                        if (x > v || (x == v && idx >= 0 && q < idx)) { v = x; idx = q; }
+                        rmax[k] = v;
+                        ridx[k] = idx;
+                    }
+                }
             }
             const float ukp = u[(int64_t)k * n + p], ukq = u[(int64_t)k * n + q];
             u[(int64_t)k * n + p] = __fsub_rn(__fmul_rn(c, ukp), __fmul_rn(s, ukq));
             u[(int64_t)k * n + q] = __fadd_rn(__fmul_rn(s, ukp), __fmul_rn(c, ukq));
         }
-        if (threadIdx.x == 0) {
+        if (tid == 0) {
             // k = p (p < q) runs first and rewrites a_pq, which k = q then reads
             const float app = mat[(int64_t)p * n + p], aqq = mat[(int64_t)q * n + q], apq = mat[(int64_t)p * n + q];
             const float npp = __fsub_rn(__fmul_rn(c, app), __fmul_rn(s, apq));
@@ -646,6 +749,18 @@ __global__ void __launch_bounds__(1024) jacobi50_kernel(float* __restrict__ mat,
             mat[(int64_t)q * n + q] = nqq;
             mat[(int64_t)p * n + q] = 0.0f;
             mat[(int64_t)q * n + p] = 0.0f;
+            rescan[atomicAdd(&s_nres, 1)] = p;
+            rescan[atomicAdd(&s_nres, 1)] = q;
+        }
+        __syncthreads();
+        // rows p, q and the rows whose maximum was rewritten: one warp each
+        const int nres = s_nres;
+        for (int w = warp; w < nres; w += nwarps) {
+            const int i = rescan[w];
+            float v;
+            int idx;
+            jacobi_row_scan(mat, n, i, lane, v, idx);
+            if (lane == 0) { rmax[i] = v; ridx[i] = idx; }
         }
         __syncthreads();
     }
@@ -777,7 +892,7 @@ inline int rsvd_fast(const void* g, bool g_bf16, int m, int n, int r, int l, int
 inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int oversampling, int power_iters,
                        uint64_t seed, bool fast, float* p_out, float* q_out, int* status_dev, cudaStream_t st) {
     const int l = r + oversampling;
-    if (r <= 0 || oversampling < 0 || power_iters < 0 || l > (m < n ? m : n)) return AETH_ERR_CONFIG;
+    if (r <= 0 || oversampling < 0 || power_iters < 0 || l > (m < n ? m : n) || l > kJacobiMaxN) return AETH_ERR_CONFIG;
     fast = fast && rsvd_fast_shape(m, n, r, l);
     RsvdWork w;
     w.fail = status_dev;

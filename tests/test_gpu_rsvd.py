@@ -43,10 +43,16 @@ def test_omega_matches_oracle(oracle, lib, count):
     assert np.abs(got - want).max() <= 2e-6 * max(1.0, np.abs(want).max())
 
 
-@pytest.mark.parametrize("n", [2, 7, 40, 136])
-def test_jacobi_bitexact(oracle, lib, n):
+@pytest.mark.parametrize("n,ties", [(2, False), (7, False), (40, False), (136, False), (520, False), (7, True),
+                                    (96, True)])
+def test_jacobi_bitexact(oracle, lib, n, ties):
+    """The running per-row maxima pick the same rotations as the reference's
+    full scan, ties (equal magnitudes in several rows and columns) included."""
     rng = np.random.default_rng(n)
-    b = rng.standard_normal((n, n + 5)).astype(np.float32)
+    if ties:
+        b = rng.integers(-2, 3, size=(n, n + 5)).astype(np.float32)
+    else:
+        b = rng.standard_normal((n, n + 5)).astype(np.float32)
     a = (b @ b.T).astype(np.float32)
     ta = dev(a)
     tu = torch.empty(n, n, dtype=torch.float32, device=DEV)
