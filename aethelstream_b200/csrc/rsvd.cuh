@@ -456,33 +456,44 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
     }
     if (crank == 0) chol_store_panel(a, pan, l, (nb - 1) * 32, l - (nb - 1) * 32);
     cluster_sync();
-    // L^-1: diagonal blocks first (lane = column c of the block's inverse)
-    for (int db = gw; db < nb; db += gwarps) {
-        const int d0 = db * 32, dw = min(32, l - d0);
-        double x[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            if (i < dw) {
-                double v = (i == lane) ? 1.0 : 0.0;
-                for (int t = 0; t < i; ++t) v -= a[(int64_t)(d0 + i) * l + d0 + t] * x[t];
-                x[i] = lane < dw ? v / a[(int64_t)(d0 + i) * l + d0 + i] : 0.0;
-            } else {
-                x[i] = 0.0;
+    // L^-1: diagonal blocks first, on the first four warps of each CTA (lane =
+    // column c of the block's inverse, forward substitution); each such warp
+    // stages its 32 x 32 block of L and keeps the inverse's columns in its own
+    // part of the panel buffer (pitch 33: lane-private columns, broadcast rows)
+    if (warp < 4) {
+        for (int db = warp * kCholCtas + crank; db < nb; db += 4 * kCholCtas) {
+            const int d0 = db * 32, dw = min(32, l - d0);
+            double* ld = pan + warp * (2 * 32 * 33);
+            double* xc = ld + 32 * 33;
+            for (int t = lane; t < 32 * 32; t += 32) {
+                const int i = t >> 5, j = t & 31;
+                ld[i * 33 + j] = (i < dw && j <= i) ? a[(int64_t)(d0 + i) * l + d0 + j] : (i == j ? 1.0 : 0.0);
             }
+            __syncwarp();
+            for (int i = 0; i < 32; ++i) {
+                double v = (i == lane) ? 1.0 : 0.0;
+#pragma unroll 8
+                for (int t = 0; t < i; ++t) v -= ld[i * 33 + t] * xc[t * 33 + lane];
+                xc[i * 33 + lane] = v / ld[i * 33 + i];
+            }
+            if (lane < dw)
+                for (int i = 0; i < dw; ++i) linv[(int64_t)(d0 + i) * l + d0 + lane] = xc[i * 33 + lane];
+            __syncwarp();
         }
-        if (lane < dw)
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (i < dw) linv[(int64_t)(d0 + i) * l + d0 + lane] = x[i];
     }
     cluster_sync();
     // off-diagonal blocks by block rows: X_ij = -inv(L_ii) sum_{k = j}^{i-1}
     // L_ik X_kj needs only earlier block rows of L^-1.  For block row ib every
-    // CTA stages L's rows i0 .. i0 + 31 (columns < i0) in shared memory; the
-    // pieces (jb < ib, 4-column group g) go to the cluster's warps: lane =
-    // row, 4 accumulators, the rows of X_kj read as broadcasts, then the
-    // 4 columns of -inv(L_ii) S through shuffles of S's rows.
+    // CTA stages L's rows i0 .. i0 + 31 (columns < i0) and inv(L_ii) in shared
+    // memory; the pieces (jb < ib, 4-column group g) go to the cluster's warps:
+    // lane = row, 4 accumulators.  X_kj comes 32 rows at a time: each lane
+    // loads one row's 4 values into the warp's staging tile, the next batch's
+    // loads in flight while the lanes read the tile as broadcasts; then
+    // -inv(L_ii) S from S's rows staged the same way.
+    __shared__ double xs[kCholThreads / 32][32 * 4];
+    __shared__ double dinv_s[32 * 33];
     const int pitch = l + 1;  // odd pitch: the lanes' rows fall in different banks
+    double* xw = xs[warp];
     for (int ib = 1; ib < nb; ++ib) {
         const int i0 = ib * 32, iw = min(32, l - i0);
         // columns 0 .. i0 - 1 of the block row (i0 < l < pitch)
@@ -490,33 +501,53 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
             const int r = t / i0, k = t % i0;
             pan[r * pitch + k] = r < iw ? a[(int64_t)(i0 + r) * l + k] : 0.0;
         }
+        for (int t = tid; t < 32 * 32; t += blockDim.x) {
+            const int r = t >> 5, c = t & 31;
+            dinv_s[r * 33 + c] = (r < iw && c < iw) ? linv[(int64_t)(i0 + r) * l + i0 + c] : 0.0;
+        }
         __syncthreads();
-        const double* drow = linv + (int64_t)(i0 + min(lane, iw - 1)) * l + i0;
+        const double* lrow = pan + lane * pitch;
         for (int piece = gw; piece < ib * 8; piece += gwarps) {
-            const int jb = piece >> 3, c0 = jb * 32 + (piece & 7) * 4;
-            const int jw = min(32, l - jb * 32);
-            if ((piece & 7) * 4 >= jw) continue;  // a ragged last block column
+            const int jb = piece >> 3, c0 = jb * 32 + (piece & 7) * 4;  // jb < ib: a full block column
             double acc[4] = {0.0, 0.0, 0.0, 0.0};
-            const double* lrow = pan + lane * pitch;
-#pragma unroll 4
-            for (int k = jb * 32; k < i0; ++k) {
-                const double lik = lrow[k];
-                const double* xr = linv + (int64_t)k * l + c0;
+            double nx[4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) acc[c] += lik * (c0 + c < l ? xr[c] : 0.0);
+            for (int c = 0; c < 4; ++c) nx[c] = linv[(int64_t)(jb * 32 + lane) * l + c0 + c];
+            for (int kb2 = jb; kb2 < ib; ++kb2) {
+                __syncwarp();  // the previous batch's tile is read
+#pragma unroll
+                for (int c = 0; c < 4; ++c) xw[lane * 4 + c] = nx[c];
+                __syncwarp();
+                if (kb2 + 1 < ib)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) nx[c] = linv[(int64_t)((kb2 + 1) * 32 + lane) * l + c0 + c];
+                const double* lk = lrow + kb2 * 32;
+#pragma unroll
+                for (int t = 0; t < 32; ++t) {
+                    const double lik = lk[t];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[c] += lik * xw[t * 4 + c];
+                }
             }
-            double out[4] = {0.0, 0.0, 0.0, 0.0};
-            for (int t = 0; t < iw; ++t) {
-                const double dinv = lane < iw ? drow[t] : 0.0;
+            // X_ij (4 columns) = -inv(L_ii) S: S's rows through the staging tile
+            __syncwarp();
 #pragma unroll
-                for (int c = 0; c < 4; ++c) out[c] -= dinv * __shfl_sync(0xffffffffu, acc[c], t);
+            for (int c = 0; c < 4; ++c) xw[lane * 4 + c] = acc[c];
+            __syncwarp();
+            double out[4] = {0.0, 0.0, 0.0, 0.0};
+            const double* drow = dinv_s + lane * 33;
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+                const double dv = drow[t];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) out[c] -= dv * xw[t * 4 + c];
             }
             if (lane < iw)
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (c0 + c < l && c0 + c < jb * 32 + jw) linv[(int64_t)(i0 + lane) * l + c0 + c] = out[c];
+                for (int c = 0; c < 4; ++c) linv[(int64_t)(i0 + lane) * l + c0 + c] = out[c];
+            __syncwarp();
         }
-        cluster_sync();  // block row ib of L^-1 for every CTA; the staging buffer is free again
+        cluster_sync();  // block row ib of L^-1 for every CTA; the staging buffers are free again
     }
     // zero the strict upper triangle of L^-1 (callers read all of it)
     for (int64_t t = (int64_t)crank * blockDim.x + tid; t < (int64_t)l * l; t += (int64_t)kCholCtas * blockDim.x) {
