@@ -30,10 +30,11 @@ from .galore import (  # noqa: E402
     nf4_quantize,
     randomized_svd,
     randomized_svd_fast,
+    randomized_svd_sketch,
 )
 
 __all__ = [
     "AdamWConfig", "apply_galore_bf16_update", "decode_int4_to_fp16", "decode_int8_to_fp16", "AethError", "ClipResult", "GaLoreConfig", "GaLoreOptimizer", "LayerRankConfig", "LomoState", "NF4Tensor",
-    "ProjectorKind", "deferred_apply_with_clip", "load", "lomo_sqnorm", "lomo_update", "nf4_dequantize", "nf4_quantize", "randomized_svd", "randomized_svd_fast",
+    "ProjectorKind", "deferred_apply_with_clip", "load", "lomo_sqnorm", "lomo_update", "nf4_dequantize", "nf4_quantize", "randomized_svd", "randomized_svd_fast", "randomized_svd_sketch",
     "_lib",
 ]

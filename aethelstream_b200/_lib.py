@@ -90,6 +90,7 @@ SIGNATURES = {
     "aeth_galore_load_state": (_i, [_vp, C.c_char_p, _vp]),
     "aeth_randomized_svd": (_i, [_vp, _i, _i, _i, _i, _i, _u64, _vp, _vp, _vp]),
     "aeth_randomized_svd_ex": (_i, [_vp, _i, _i, _i, _i, _i, _i, _u64, _i, _vp, _vp, _vp]),
+    "aeth_randomized_svd_sketch": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "aeth_rsvd_omega": (_i, [_u64, _i64, _vp, _vp]),
     "aeth_rsvd_jacobi": (_i, [_vp, _i, _vp, _vp]),
     "aeth_galore_step_count": (_u64, [_vp]),

@@ -1706,6 +1706,14 @@ int aeth_randomized_svd_ex(const void* g, int g_dtype, int m, int n, int rank, i
                                p_out, q_out, to_stream(stream)));
 }
 
+int aeth_randomized_svd_sketch(const void* g, int g_dtype, int m, int n, int rank, int oversampling,
+                               const float* omega, int fast, float* p_out, float* q_out, aeth_stream_t stream) {
+    if (!g || !omega || m <= 0 || n <= 0) return set_err(AETH_ERR_ARG);
+    if (g_dtype != AETH_DTYPE_F32 && g_dtype != AETH_DTYPE_BF16) return set_err(AETH_ERR_ARG);
+    return set_err(rsvd_device(g, g_dtype == AETH_DTYPE_BF16, m, n, rank, oversampling, 0, 1, fast != 0, p_out,
+                               q_out, to_stream(stream), omega));
+}
+
 int aeth_rsvd_omega(uint64_t seed, int64_t count, float* out, aeth_stream_t stream) {
     if (!out || count <= 0) return set_err(AETH_ERR_ARG);
     cudaStream_t st = to_stream(stream);

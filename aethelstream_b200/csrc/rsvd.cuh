@@ -14,15 +14,18 @@
 //     be.  The host passes M^(2 kOmegaChunk 2^k) for every bit k of t.
 //   * G Omega, Q^T G, B B^T, Q^ U, B^T U: the exact-order SIMT GEMM
 //     (gemm_simt.cuh), the reference's f32 loops bit for bit on equal inputs.
-//   * The orthonormal bases: Cholesky QR twice with an f64 Gram matrix (two
-//     GEMMs and one small factorisation instead of l^2 / 2 sequential
-//     Gram-Schmidt dot products).  It equals modified Gram-Schmidt in exact
-//     arithmetic (both give the Q factor with a positive R diagonal); in f32
-//     the two differ by rounding.  A Gram matrix that is not positive definite
-//     is the rank-deficiency error of qr_columns.  The final orthonormalisation
-//     of Q (orthonormalize_columns, which clamps tiny norms instead of failing)
-//     falls back to a one-CTA modified Gram-Schmidt when its Gram matrix is
-//     not positive definite.
+//   * The orthonormal bases, exact path: the reference's modified
+//     Gram-Schmidt in its own operation order (mgs_exact_kernel), so with the
+//     same sketch the exact path gives the reference's P and Q bit for bit.
+//   * The orthonormal bases, tensor-core path: Cholesky QR with an f64 Gram
+//     matrix (two GEMMs and one small factorisation instead of l^2 / 2
+//     sequential Gram-Schmidt dot products).  It equals modified Gram-Schmidt
+//     in exact arithmetic (both give the Q factor with a positive R
+//     diagonal); in f32 the two differ by rounding.  A Gram matrix that is not
+//     positive definite is the rank-deficiency error of qr_columns.  The final
+//     orthonormalisation of Q (orthonormalize_columns, which clamps tiny
+//     norms instead of failing) falls back to a one-CTA modified Gram-Schmidt
+//     when its Gram matrix is not positive definite.
 //   * Jacobi: one CTA; every rotation reproduces the reference's in-place
 //     update loop, including the values it reads back for k = p and k = q.
 //   * Optional power iterations (a B200 extension; the reference never runs
@@ -110,7 +113,13 @@ __device__ __forceinline__ float rsvd_gaussian(uint64_t& s) {
     s = xorshift64_dev(s);
     const float u2 = __fmul_rn((float)(s >> 40), 0x1p-24f);
     const float two_pi = 2.0f * 3.14159265358979323846f;
-    return __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, logf(u1))), cosf(__fmul_rn(two_pi, u2)));
+    // ln and cos of the f32 arguments in f64, rounded once to f32: the
+    // correctly rounded values except where the f64 result lies within its
+    // own error of an f32 rounding boundary.  A host libm that is not
+    // correctly rounded differs from them by one ulp on a few inputs.
+    const float ln_u1 = (float)log((double)u1);
+    const float cos_a = (float)cos((double)__fmul_rn(two_pi, u2));
+    return __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, ln_u1)), cos_a);
 }
 
 __global__ void rsvd_omega_kernel(const uint64_t* __restrict__ jump, uint64_t s0, int64_t count,
@@ -641,6 +650,102 @@ __global__ void __launch_bounds__(1024) mgs_clamped_kernel(float* __restrict__ q
 }
 
 // ---------------------------------------------------------------------------
+// One CTA: modified Gram-Schmidt in the reference's exact order, bit for bit:
+// qr_columns (randomized_svd.rs:160-185; fail_on_small: a column norm below
+// 1e-12 sets *status to 1 and ends the kernel) or orthonormalize_columns
+// (:187-207, the norm clamped to 1e-12).  q is rows x cols, row-major.
+//
+// The reference runs left-looking: for column j, the dots with columns
+// 0 .. j-1 in turn, each followed by its subtraction, then the norm.  This
+// kernel runs the same operations right-looking: once column i is final
+// (normalised), every column j > i takes its dot with column i and its
+// subtraction.  Column j sees exactly the same values in the same order
+// (the subtractions of columns 0 .. i-1 before the dot with column i), so
+// every rounding is the reference's; only the dots of different columns now
+// run side by side, one thread per column, each summing its rows in
+// increasing order with separately rounded products and sums.  Column i's
+// values are staged in shared memory kMgsChunk rows at a time and read as
+// broadcasts.  The thread that updates column i + 1 sums that column's
+// squares in row order as it writes them: the next step's norm.
+// ---------------------------------------------------------------------------
+constexpr int kMgsThreads = 1024;
+constexpr int kMgsChunk = 4096;
+constexpr int kMgsMaxCols = 2 * kMgsThreads;
+
+__global__ void __launch_bounds__(kMgsThreads) mgs_exact_kernel(float* __restrict__ q, int rows, int cols,
+                                                                int fail_on_small, int* __restrict__ status) {
+    __shared__ float ci[kMgsChunk];
+    __shared__ float s_sumsq;
+    const int tid = threadIdx.x;
+    auto norm_of = [&](float s) -> float {
+        return fail_on_small ? __fsqrt_rn(s) : __fsqrt_rn(fmaxf(s, 1e-12f));
+    };
+    if (tid == 0) {
+        float s = 0.0f;
+        for (int r = 0; r < rows; ++r) {
+            const float x = q[(int64_t)r * cols];
+            s = __fadd_rn(s, __fmul_rn(x, x));
+        }
+        s_sumsq = s;
+    }
+    for (int i = 0; i < cols; ++i) {
+        __syncthreads();  // s_sumsq of column i; column i's subtractions done
+        const float nrm = norm_of(s_sumsq);
+        if (fail_on_small && nrm < 1e-12f) {
+            if (tid == 0 && status) *status = 1;
+            return;
+        }
+        for (int r = tid; r < rows; r += kMgsThreads)
+            q[(int64_t)r * cols + i] = __fdiv_rn(q[(int64_t)r * cols + i], nrm);
+        if (i + 1 == cols) break;
+        // this thread's columns of the trailing block: j0 = i + 1 + tid and j0 + kMgsThreads
+        const int j0 = i + 1 + tid, j1 = j0 + kMgsThreads;
+        const bool h0 = j0 < cols, h1 = j1 < cols;
+        float d0 = 0.0f, d1 = 0.0f;
+        for (int c0 = 0; c0 < rows; c0 += kMgsChunk) {
+            const int cn = min(kMgsChunk, rows - c0);
+            __syncthreads();  // the previous chunk is read; column i is normalised
+            for (int r = tid; r < cn; r += kMgsThreads) ci[r] = q[(int64_t)(c0 + r) * cols + i];
+            __syncthreads();
+            const float* p0 = q + (int64_t)c0 * cols + j0;
+            if (h1) {
+                const float* p1 = p0 + kMgsThreads;
+#pragma unroll 8
+                for (int r = 0; r < cn; ++r) {
+                    d0 = __fadd_rn(d0, __fmul_rn(ci[r], p0[(int64_t)r * cols]));
+                    d1 = __fadd_rn(d1, __fmul_rn(ci[r], p1[(int64_t)r * cols]));
+                }
+            } else if (h0) {
+#pragma unroll 8
+                for (int r = 0; r < cn; ++r) d0 = __fadd_rn(d0, __fmul_rn(ci[r], p0[(int64_t)r * cols]));
+            }
+        }
+        float s = 0.0f;  // column i + 1's squared norm (thread 0 owns j0 = i + 1)
+        for (int c0 = 0; c0 < rows; c0 += kMgsChunk) {
+            const int cn = min(kMgsChunk, rows - c0);
+            __syncthreads();
+            for (int r = tid; r < cn; r += kMgsThreads) ci[r] = q[(int64_t)(c0 + r) * cols + i];
+            __syncthreads();
+            float* p0 = q + (int64_t)c0 * cols + j0;
+            if (h0) {
+#pragma unroll 8
+                for (int r = 0; r < cn; ++r) {
+                    const float x = __fsub_rn(p0[(int64_t)r * cols], __fmul_rn(d0, ci[r]));
+                    p0[(int64_t)r * cols] = x;
+                    s = __fadd_rn(s, __fmul_rn(x, x));
+                }
+            }
+            if (h1) {
+                float* p1 = p0 + kMgsThreads;
+#pragma unroll 8
+                for (int r = 0; r < cn; ++r) p1[(int64_t)r * cols] = __fsub_rn(p1[(int64_t)r * cols], __fmul_rn(d1, ci[r]));
+            }
+        }
+        if (tid == 0) s_sumsq = s;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // One CTA: jacobi_eigenvectors (randomized_svd.rs:210-271) on the f32 n x n
 // matrix `mat` (destroyed), eigenvector estimate into u.  Bit-exact with the
 // reference's loop: each rotation zeroes the largest |a_ij|, i < j, the first
@@ -921,7 +1026,8 @@ inline int rsvd_fast(const void* g, bool g_bf16, int m, int n, int r, int l, int
 // the stream-ordered pool.  Returns AETH_ERR_CONFIG for an invalid rank or
 // oversampling.
 inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int oversampling, int power_iters,
-                       uint64_t seed, bool fast, float* p_out, float* q_out, int* status_dev, cudaStream_t st) {
+                       uint64_t seed, bool fast, float* p_out, float* q_out, int* status_dev, cudaStream_t st,
+                       const float* omega_in = nullptr) {
     const int l = r + oversampling;
     if (r <= 0 || oversampling < 0 || power_iters < 0 || l > (m < n ? m : n) || l > kJacobiMaxN) return AETH_ERR_CONFIG;
     fast = fast && rsvd_fast_shape(m, n, r, l);
@@ -976,11 +1082,16 @@ inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int ov
             cudaMemcpyAsync(w.jump, omega_jump_host(), sizeof(Gf2Mat64) * kOmegaLevels, cudaMemcpyHostToDevice, st);
         if (e == cudaSuccess) e = cudaMemsetAsync(fail_q, 0, sizeof(int), st);
         if (e != cudaSuccess) { status = set_err((int)e); break; }
-        // 1. Omega (n x l)
+        // 1. Omega (n x l), drawn here or the caller's
         const int64_t count = (int64_t)n * l;
-        const int64_t chunks = (count + kOmegaChunk - 1) / kOmegaChunk;
-        rsvd_omega_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w.jump, seed > 1 ? seed : 1, count,
-                                                                           w.omega);
+        if (omega_in) {
+            e = cudaMemcpyAsync(w.omega, omega_in, sizeof(float) * (size_t)count, cudaMemcpyDeviceToDevice, st);
+            if (e != cudaSuccess) { status = set_err((int)e); break; }
+        } else {
+            const int64_t chunks = (count + kOmegaChunk - 1) / kOmegaChunk;
+            rsvd_omega_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w.jump, seed > 1 ? seed : 1, count,
+                                                                               w.omega);
+        }
         if (fast) {
             if ((status = rsvd_fast(gin, g_bf16, m, n, r, l, power_iters, w, gt, at, bt, ut, p_out, q_out, st)))
                 break;
@@ -988,16 +1099,20 @@ inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int ov
             // 2. Y = G Omega
             if ((status = simt_gemm_exact(g, n, 1, w.omega, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st)))
                 break;
-            // 3. Q^ = orthonormal basis of Y (+ optional power iterations)
-            if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
+            // 3. Q^ = qr_columns(Y), the reference's Gram-Schmidt in its own order
+            // (+ optional power iterations, each basis by the same Gram-Schmidt)
+            mgs_exact_kernel<<<1, kMgsThreads, 0, st>>>(w.y, m, l, 1, w.fail);
+            if ((status = cuda_status(cudaGetLastError()))) break;
             for (int it = 0; it < power_iters && status == AETH_OK; ++it) {
                 // Z = G^T Q^ (n x l) into y2, orthonormalise, Y = G Z, orthonormalise
                 if ((status = simt_gemm_exact(g, 1, n, w.y, l, 1, w.y2, l, n, l, m, SIMT_STORE, 1.0f, nullptr, st)))
                     break;
-                if ((status = cholqr2(w.y2, w.omega, n, l, w, st))) break;
+                mgs_exact_kernel<<<1, kMgsThreads, 0, st>>>(w.y2, n, l, 1, w.fail);
+                if ((status = cuda_status(cudaGetLastError()))) break;
                 if ((status = simt_gemm_exact(g, n, 1, w.y2, l, 1, w.y, l, m, l, n, SIMT_STORE, 1.0f, nullptr, st)))
                     break;
-                if ((status = cholqr2(w.y, w.y2, m, l, w, st))) break;
+                mgs_exact_kernel<<<1, kMgsThreads, 0, st>>>(w.y, m, l, 1, w.fail);
+                if ((status = cuda_status(cudaGetLastError()))) break;
             }
             if (status) break;
             // 4. B = Q^T G (l x n), 5. B B^T (l x l), 6. Jacobi
@@ -1015,10 +1130,14 @@ inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int ov
                 (status = simt_gemm_exact(w.b, 1, n, w.u, l, 1, q_out, r, n, r, l, SIMT_STORE, 1.0f, nullptr, st)))
                 break;
         }
-        // 9. Q orthonormalised (orthonormalize_columns): Cholesky QR, or, where
-        // its Gram matrix is not positive definite, the reference's clamped
-        // Gram-Schmidt from B^T U again -- chosen on the device.
-        if (q_out) {
+        // 9. Q orthonormalised (orthonormalize_columns).  Exact path: the
+        // reference's clamped Gram-Schmidt in its own order.  Tensor-core path:
+        // Cholesky QR, or, where its Gram matrix is not positive definite, the
+        // clamped Gram-Schmidt from B^T U again -- chosen on the device.
+        if (q_out && !fast) {
+            mgs_exact_kernel<<<1, kMgsThreads, 0, st>>>(q_out, n, r, 0, nullptr);
+            if ((status = cuda_status(cudaGetLastError()))) break;
+        } else if (q_out) {
             e = cudaMemcpyAsync(qraw, q_out, sizeof(float) * (size_t)n * r, cudaMemcpyDeviceToDevice, st);
             if (e != cudaSuccess) { status = set_err((int)e); break; }
             if ((status = cholqr2(q_out, w.y2, n, r, w, st, fail_q))) break;
@@ -1034,13 +1153,15 @@ inline int rsvd_launch(const void* gin, bool g_bf16, int m, int n, int r, int ov
 // rsvd_launch, then waits on `st` for the factorisation status: returns
 // AETH_ERR_LINALG for a rank-deficient sketch.
 inline int rsvd_device(const void* gin, bool g_bf16, int m, int n, int r, int oversampling, int power_iters,
-                       uint64_t seed, bool fast, float* p_out, float* q_out, cudaStream_t st) {
+                       uint64_t seed, bool fast, float* p_out, float* q_out, cudaStream_t st,
+                       const float* omega_in = nullptr) {
     int* flag = nullptr;
     AETH_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&flag), sizeof(int), st));
     cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), st);
     int status = e == cudaSuccess ? AETH_OK : (int)e;
     if (status == AETH_OK)
-        status = rsvd_launch(gin, g_bf16, m, n, r, oversampling, power_iters, seed, fast, p_out, q_out, flag, st);
+        status = rsvd_launch(gin, g_bf16, m, n, r, oversampling, power_iters, seed, fast, p_out, q_out, flag, st,
+                             omega_in);
     int h = 0;
     if (status == AETH_OK) {
         e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, st);

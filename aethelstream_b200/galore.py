@@ -194,6 +194,28 @@ def randomized_svd_fast(g: torch.Tensor, rank: int, oversampling: int = 10, seed
     return p, q
 
 
+def randomized_svd_sketch(g: torch.Tensor, rank: int, oversampling: int, omega: torch.Tensor, fast: bool = False,
+                          want_p: bool = True, want_q: bool = True):
+    """randomized_svd_projections (galore/src/randomized_svd.rs:95-149) from
+    the caller's sketch omega (n x (rank + oversampling) float32 on the
+    device) instead of the seeded draw.  With fast=False the products and the
+    Gram-Schmidt run in the reference's own order, so the sketch the
+    reference drew gives its P and Q bit for bit."""
+    g = g.contiguous()
+    omega = omega.contiguous()
+    if g.dtype not in (torch.float32, torch.bfloat16) or g.dim() != 2:
+        raise ValueError("g must be a 2-D float32 or bfloat16 device tensor")
+    m, n = g.shape
+    if omega.dtype != torch.float32 or omega.shape != (n, rank + oversampling) or omega.device != g.device:
+        raise ValueError("omega must be a float32 (n, rank + oversampling) tensor on g's device")
+    p = torch.empty(m, rank, dtype=torch.float32, device=g.device) if want_p else None
+    q = torch.empty(n, rank, dtype=torch.float32, device=g.device) if want_q else None
+    L.check(L.load().aeth_randomized_svd_sketch(_ptr(g), _DTYPES[g.dtype], m, n, rank, oversampling, _ptr(omega),
+                                                int(bool(fast)), _ptr(p), _ptr(q), C.c_void_p(_stream_handle())),
+            "aeth_randomized_svd_sketch")
+    return p, q
+
+
 def decode_int8_to_fp16(src: torch.Tensor, scales: torch.Tensor, num_channels: int) -> torch.Tensor:
     """QuantizedDecoder::decode_int8_to_fp16 (flowcast/src/decode.rs:63-86) on
     the device: int8 src, per-channel f32 scales -> float16 (flowcast's

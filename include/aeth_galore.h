@@ -297,6 +297,15 @@ int aeth_randomized_svd_ex(const void* g, int g_dtype, int m, int n, int rank, i
                            uint64_t seed, int fast, float* p_out, float* q_out, aeth_stream_t stream);
 int aeth_rsvd_omega(uint64_t seed, int64_t count, float* out, aeth_stream_t stream);
 int aeth_rsvd_jacobi(float* mat, int n, float* u, aeth_stream_t stream);
+/* Steps 2-5 of randomized_svd_projections (randomized_svd.rs:95-149) from the
+ * caller's sketch omega (n x (rank + oversampling) f32 row-major, device
+ * memory) instead of step 1's draw; no power iterations, as in the reference.
+ * fast == 0 runs the exact-order path, whose products and Gram-Schmidt are the
+ * reference's own loops: with the sketch the reference drew on the host (its
+ * Box-Muller goes through the host libm's ln and cos), P and Q equal the
+ * reference's bit for bit.  Statuses as aeth_randomized_svd_ex. */
+int aeth_randomized_svd_sketch(const void* g, int g_dtype, int m, int n, int rank, int oversampling,
+                               const float* omega, int fast, float* p_out, float* q_out, aeth_stream_t stream);
 
 /* Whole-layer step of deferred_apply_with_clip (hook.rs:115-203) for a
  * single micro-batch: for each listed parameter project_and_accumulate, then

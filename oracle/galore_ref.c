@@ -448,6 +448,18 @@ int ref_randomized_svd(const float* g, int m, int n, int r, int oversampling, ui
     const int l = r + oversampling;
     if (r == 0 || l > (n < m ? n : m)) return -2;
     float* omega = (float*)malloc(sizeof(float) * (size_t)n * l);
+    ref_rsvd_omega(seed, (int64_t)n * l, omega);
+    const int st = ref_randomized_svd_sketch(g, m, n, r, oversampling, omega, p_out, q_out);
+    free(omega);
+    return st;
+}
+
+/* Steps 2-5 of randomized_svd_projections (randomized_svd.rs:95-149) from a
+ * given n x l sketch omega (step 1's draw). */
+int ref_randomized_svd_sketch(const float* g, int m, int n, int r, int oversampling, const float* omega,
+                              float* p_out, float* q_out) {
+    const int l = r + oversampling;
+    if (r == 0 || l > (n < m ? n : m)) return -2;
     float* y = (float*)malloc(sizeof(float) * (size_t)m * l);
     float* qt = (float*)malloc(sizeof(float) * (size_t)l * m);
     float* b = (float*)malloc(sizeof(float) * (size_t)l * n);
@@ -455,7 +467,6 @@ int ref_randomized_svd(const float* g, int m, int n, int r, int oversampling, ui
     float* bbt = (float*)malloc(sizeof(float) * (size_t)l * l);
     float* u = (float*)malloc(sizeof(float) * (size_t)l * l);
     int st = 0;
-    ref_rsvd_omega(seed, (int64_t)n * l, omega);
     ref_matmul_f32(g, omega, y, m, n, l);
     if (rsvd_mgs(y, m, l, 1) != 0) { st = -3; goto done; }
     for (int i = 0; i < m; ++i)
@@ -479,7 +490,7 @@ int ref_randomized_svd(const float* g, int m, int n, int r, int oversampling, ui
         }
     rsvd_mgs(q_out, n, r, 0);
 done:
-    free(omega); free(y); free(qt); free(b); free(bt); free(bbt); free(u);
+    free(y); free(qt); free(b); free(bt); free(bbt); free(u);
     return st;
 }
 

@@ -91,6 +91,9 @@ void ref_rsvd_omega(uint64_t seed, int64_t count, float* out);
 void ref_rsvd_jacobi(float* mat, int n, float* u);
 int ref_randomized_svd(const float* g, int m, int n, int r, int oversampling, uint64_t seed, float* p_out,
                        float* q_out);
+/* The same from a given n x (r + oversampling) row-major sketch omega. */
+int ref_randomized_svd_sketch(const float* g, int m, int n, int r, int oversampling, const float* omega,
+                              float* p_out, float* q_out);
 
 /* StandardAdamW::apply_update (galore/src/standard_adamw.rs:84-114), plus the
  * bias-corrected form documented for doublepass_galore_apply's `step` argument

@@ -71,6 +71,7 @@ def lib():
             "ref_rsvd_omega": (None, [C.c_uint64, C.c_int64, _f32p]),
             "ref_rsvd_jacobi": (None, [_f32p, C.c_int, _f32p]),
             "ref_randomized_svd": (C.c_int, [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, _f32p, _f32p]),
+            "ref_randomized_svd_sketch": (C.c_int, [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p]),
             "ref_full_adam_apply": (None, [_f32p, _f32p, _f32p, _f32p, C.c_int64, C.c_float, C.c_float, C.c_float,
                                            C.c_float, C.c_float, C.c_int]),
             "b2_dynamic_map": (None, [C.c_int, _f32p]),
@@ -267,12 +268,18 @@ def rsvd_jacobi(a):
     return u, a
 
 
-def randomized_svd(g, m, n, r, oversampling, seed):
-    """(status, P m x r, Q n x r) of randomized_svd_projections."""
+def randomized_svd(g, m, n, r, oversampling, seed, omega=None):
+    """(status, P m x r, Q n x r) of randomized_svd_projections; with `omega`
+    (n x (r + oversampling) f32) that sketch replaces step 1's draw."""
     g = _c(g, np.float32)
     p = np.zeros((m, r), np.float32)
     q = np.zeros((n, r), np.float32)
-    st = lib().ref_randomized_svd(g, m, n, r, oversampling, seed, p, q)
+    if omega is None:
+        st = lib().ref_randomized_svd(g, m, n, r, oversampling, seed, p, q)
+    else:
+        omega = _c(omega, np.float32)
+        assert omega.size == n * (r + oversampling)
+        st = lib().ref_randomized_svd_sketch(g, m, n, r, oversampling, omega, p, q)
     return st, p, q
 
 

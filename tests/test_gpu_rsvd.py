@@ -2,10 +2,13 @@
 
 The Gaussian sketch and the Jacobi rotations follow the reference's
 sequential definitions (randomized_svd.rs:38-66, 210-271); the sketch is
-compared with the oracle within libm-vs-CUDA logf/cosf differences and the
-Jacobi bit for bit.  The orthonormal bases come from Cholesky QR instead of
-Gram-Schmidt (equal in exact arithmetic), so the projectors are compared
-within a stated tolerance, plus orthonormality and the captured energy.
+compared with the oracle within one ulp (the host libm's ln and cos are not
+correctly rounded on every input) and the Jacobi bit for bit.  The exact-order
+path runs the reference's products and Gram-Schmidt in the reference's own
+order: from the oracle's sketch it gives the oracle's P and Q bit for bit, and
+from its own sketch within EXACT_TOL.  The tensor-core path orthonormalises by
+Cholesky QR instead of Gram-Schmidt (equal in exact arithmetic) and is
+compared within PROJ_TOL, plus orthonormality and the captured energy.
 """
 import ctypes as C
 
@@ -17,7 +20,8 @@ from tests._gpu import DEV, dev, host, ptr, rel_fro, stream
 
 pytestmark = pytest.mark.gpu
 
-PROJ_TOL = 1e-3  # relative Frobenius distance of P / Q to the oracle's
+PROJ_TOL = 1e-5  # tensor-core path: relative Frobenius distance of P / Q to the oracle's
+EXACT_TOL = 1e-5  # exact-order path with the device's own sketch
 
 
 @pytest.fixture(scope="module")
@@ -40,7 +44,11 @@ def test_omega_matches_oracle(oracle, lib, count):
     out = torch.empty(count, dtype=torch.float32, device=DEV)
     assert lib.aeth_rsvd_omega(seed, count, ptr(out), stream()) == 0
     got, want = host(out), oracle.rsvd_omega(seed, count)
-    assert np.abs(got - want).max() <= 2e-6 * max(1.0, np.abs(want).max())
+    # the host libm's ln and cos are off by one ulp on some inputs, which
+    # moves the Gaussian by at most a few ulps (about 1.5 % of the draws)
+    assert np.all(np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32)) <= 4)
+    if count > 1000:
+        assert np.mean(got != want) < 0.05
 
 
 @pytest.mark.parametrize("n,ties", [(2, False), (7, False), (40, False), (136, False), (520, False), (7, True),
@@ -73,8 +81,75 @@ def test_randomized_svd_matches_oracle(oracle, m, n, r, p):
     P, Q = host(P), host(Q)
     assert np.abs(P.T @ P - np.eye(r)).max() < 1e-4
     assert np.abs(Q.T @ Q - np.eye(r)).max() < 1e-4
-    assert rel_fro(P, p_ref) < PROJ_TOL, rel_fro(P, p_ref)
-    assert rel_fro(Q, q_ref) < PROJ_TOL, rel_fro(Q, q_ref)
+    assert rel_fro(P, p_ref) < EXACT_TOL, rel_fro(P, p_ref)
+    assert rel_fro(Q, q_ref) < EXACT_TOL, rel_fro(Q, q_ref)
+
+
+@pytest.mark.parametrize("m,n,r,p", [(256, 384, 16, 8), (512, 256, 32, 10), (200, 130, 12, 5), (1024, 1024, 64, 8),
+                                     (96, 1500, 40, 10)])
+@pytest.mark.parametrize("g_dtype", ["f32", "bf16"])
+def test_randomized_svd_sketch_bitexact(oracle, m, n, r, p, g_dtype):
+    """From the sketch the reference draws, the exact-order path gives the
+    reference's P and Q bit for bit (a bf16 gradient is widened exactly)."""
+    from aethelstream_b200 import randomized_svd_sketch
+    g = _lowrank_plus_noise(m, n, r + p + 8, 3 * m + n)
+    if g_dtype == "bf16":
+        g = oracle.bf16_round(g)
+    l = r + p
+    omega = oracle.rsvd_omega(oracle.rsvd_seed(200 + m), n * l).reshape(n, l)
+    gd = dev(g).to(torch.bfloat16) if g_dtype == "bf16" else dev(g)
+    P, Q = randomized_svd_sketch(gd, r, p, dev(omega))
+    st, p_ref, q_ref = oracle.randomized_svd(g, m, n, r, p, 0, omega=omega)
+    assert st == 0
+    assert np.array_equal(host(P), p_ref)
+    assert np.array_equal(host(Q), q_ref)
+    # a second call on the same stream (pooled workspace reused) gives the same bits
+    P2, _ = randomized_svd_sketch(gd, r, p, dev(omega), want_q=False)
+    assert np.array_equal(host(P2), p_ref)
+
+
+def test_randomized_svd_sketch_errors(oracle):
+    from aethelstream_b200 import AethError, randomized_svd_sketch, _lib
+    n, l = 48, 12
+    omega = dev(oracle.rsvd_omega(5, n * l).reshape(n, l))
+    with pytest.raises(AethError) as e:
+        randomized_svd_sketch(torch.zeros(64, n, dtype=torch.float32, device=DEV), 8, 4, omega)
+    assert e.value.status == _lib.AETH_ERR_LINALG
+    with pytest.raises(AethError) as e:
+        randomized_svd_sketch(torch.ones(64, n, dtype=torch.float32, device=DEV), 0, 12, omega)
+    assert e.value.status == _lib.AETH_ERR_CONFIG
+    with pytest.raises(ValueError):
+        randomized_svd_sketch(torch.ones(64, n, dtype=torch.float32, device=DEV), 8, 3, omega)
+
+
+@pytest.mark.parametrize("m,n,r,p", [(256, 384, 16, 8), (1024, 1024, 64, 8), (2048, 1024, 128, 8),
+                                     (1024, 2048, 128, 8)])
+@pytest.mark.parametrize("g_dtype", ["f32", "bf16"])
+def test_randomized_svd_fast_matches_oracle(oracle, lib, m, n, r, p, g_dtype):
+    """The tensor-core refresh (products over exact bf16 terms, Cholesky QR
+    with f64 Gram matrices) from the device's own sketch lies within 1e-5 of
+    the same algorithm in f64 on that sketch.  The reference's f32 loops are
+    themselves up to about 1e-5 away from it at these sizes (sequential f32
+    sums over 2048 terms), so against the oracle the bound is the sum of the
+    two, 2e-5."""
+    from aethelstream_b200 import randomized_svd_fast
+    from tests.test_oracle_rsvd import _f64_projections
+    g = _lowrank_plus_noise(m, n, r + p + 8, 5 * m + n)
+    if g_dtype == "bf16":
+        g = oracle.bf16_round(g)
+    seed = oracle.rsvd_seed(800)
+    gd = dev(g).to(torch.bfloat16) if g_dtype == "bf16" else dev(g)
+    P, Q = randomized_svd_fast(gd, r, p, seed)
+    om = torch.empty(n * (r + p), dtype=torch.float32, device=DEV)
+    assert lib.aeth_rsvd_omega(seed, om.numel(), ptr(om), stream()) == 0
+    p64, q64 = _f64_projections(g, host(om).reshape(n, r + p), r)
+    st, p_ref, q_ref = oracle.randomized_svd(g, m, n, r, p, seed)
+    assert st == 0
+    P, Q = host(P), host(Q)
+    assert rel_fro(P, p64) < PROJ_TOL, rel_fro(P, p64)
+    assert rel_fro(Q, q64) < PROJ_TOL, rel_fro(Q, q64)
+    assert rel_fro(P, p_ref) < 2 * PROJ_TOL, rel_fro(P, p_ref)
+    assert rel_fro(Q, q_ref) < 2 * PROJ_TOL, rel_fro(Q, q_ref)
 
 
 def test_randomized_svd_errors(lib):
@@ -136,7 +211,7 @@ def test_ref_mode_refresh_on_notify_step(oracle):
     Pd, Qd = randomized_svd(dev(g), r, 10, seed)
     assert np.array_equal(host(P), host(Pd)) and np.array_equal(host(Q), host(Qd))
     st, p_ref, q_ref = oracle.randomized_svd(g, m, n, r, 10, seed)
-    assert st == 0 and rel_fro(host(P), p_ref) < PROJ_TOL and rel_fro(host(Q), q_ref) < PROJ_TOL
+    assert st == 0 and rel_fro(host(P), p_ref) < EXACT_TOL and rel_fro(host(Q), q_ref) < EXACT_TOL
     m8, v8, ms, vs = [host(x) for x in opt.get_state(0, "d_wq")]
     assert not m8.any() and not v8.any() and (ms == 1.0).all() and (vs == 1.0).all()
     # step 2 (not a refresh step): nothing captured, the projectors stay
@@ -185,7 +260,8 @@ def test_randomized_svd_fast_matches_exact(oracle, m, n, r, p, power_iters):
     P0, Q0, P1, Q1 = host(P0), host(Q0), host(P1), host(Q1)
     for X in (P1, Q1):
         assert np.abs(X.T @ X - np.eye(r)).max() < 1e-4
-    assert rel_fro(P1, P0) < PROJ_TOL and rel_fro(Q1, Q0) < PROJ_TOL
+    assert rel_fro(P1, P0) < PROJ_TOL, rel_fro(P1, P0)
+    assert rel_fro(Q1, Q0) < PROJ_TOL, rel_fro(Q1, Q0)
     # same subspaces: the projection of one basis onto the other is complete
     assert np.linalg.norm(P0.T @ P1) ** 2 > r * (1 - 1e-4)
 

@@ -121,3 +121,76 @@ def test_errors(oracle):
     assert oracle.randomized_svd(g, 16, 16, 0, 4, 1)[0] == -2    # rank 0: GaLoreError::Config
     assert oracle.randomized_svd(g, 16, 16, 10, 8, 1)[0] == -2   # r + p > min(m, n)
     assert oracle.randomized_svd(np.zeros((16, 16), np.float32), 16, 16, 2, 2, 1)[0] == -3  # Linalg
+
+
+def test_sketch_entry_equals_the_seeded_draw(oracle):
+    """ref_randomized_svd_sketch from the drawn sketch is ref_randomized_svd."""
+    rng = np.random.default_rng(4)
+    m, n, r, p = 96, 80, 8, 6
+    g = rng.standard_normal((m, n)).astype(np.float32)
+    seed = oracle.rsvd_seed(7)
+    omega = oracle.rsvd_omega(seed, n * (r + p)).reshape(n, r + p)
+    a = oracle.randomized_svd(g, m, n, r, p, seed)
+    b = oracle.randomized_svd(g, m, n, r, p, 0, omega=omega)
+    assert a[0] == b[0] == 0
+    assert np.array_equal(a[1], b[1]) and np.array_equal(a[2], b[2])
+
+
+def _f64_projections(g, omega, r):
+    """The same algorithm in f64 (numpy), with the reference's Gram-Schmidt
+    and its 50-rotation Jacobi."""
+    def mgs(q, clamp):
+        q = q.copy()
+        for j in range(q.shape[1]):
+            for i in range(j):
+                q[:, j] -= (q[:, i] @ q[:, j]) * q[:, i]
+            s = q[:, j] @ q[:, j]
+            q[:, j] /= math.sqrt(max(s, 1e-12) if clamp else s)
+        return q
+
+    def jacobi(a):
+        a = a.copy()
+        n = a.shape[0]
+        u = np.eye(n)
+        for _ in range(50):
+            t = np.abs(np.triu(a, 1))
+            p, q = divmod(int(np.argmax(t)), n)
+            if t[p, q] < 1e-10:
+                break
+            tau = (a[q, q] - a[p, p]) / (2 * a[p, q])
+            t_ = 1 / (tau + math.sqrt(1 + tau * tau)) if tau >= 0 else -1 / (-tau + math.sqrt(1 + tau * tau))
+            c = 1 / math.sqrt(1 + t_ * t_)
+            s = t_ * c
+            for k in range(n):
+                akp, akq = a[k, p], a[k, q]
+                a[k, p] = c * akp - s * akq
+                a[p, k] = a[k, p]
+                a[k, q] = s * akp + c * akq
+                a[q, k] = a[k, q]
+            a[p, q] = a[q, p] = 0.0
+            up, uq = u[:, p].copy(), u[:, q].copy()
+            u[:, p], u[:, q] = c * up - s * uq, s * up + c * uq
+        return u
+
+    g, omega = g.astype(np.float64), omega.astype(np.float64)
+    y = mgs(g @ omega, False)
+    b = y.T @ g
+    u = jacobi(b @ b.T)
+    return y @ u[:, :r], mgs(b.T @ u[:, :r], True)
+
+
+def test_f32_reference_is_close_to_its_f64_restatement(oracle):
+    """At these shapes the reference's f32 loops land within 1e-5 of the same
+    algorithm in f64: a device refresh within 1e-5 of the oracle is within
+    the reference's own rounding."""
+    rng = np.random.default_rng(20)
+    m, n, r, p = 256, 384, 16, 8
+    k = r + p + 8
+    g = ((rng.standard_normal((m, k)) * np.geomspace(1.0, 0.05, k)) @ rng.standard_normal((k, n))
+         + 0.01 * rng.standard_normal((m, n))).astype(np.float32)
+    omega = oracle.rsvd_omega(oracle.rsvd_seed(200), n * (r + p)).reshape(n, r + p)
+    st, p32, q32 = oracle.randomized_svd(g, m, n, r, p, 0, omega=omega)
+    p64, q64 = _f64_projections(g, omega, r)
+    assert st == 0
+    assert np.linalg.norm(p32 - p64) / np.linalg.norm(p64) < 1e-5
+    assert np.linalg.norm(q32 - q64) / np.linalg.norm(q64) < 1e-5
