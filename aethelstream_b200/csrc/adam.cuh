@@ -153,15 +153,14 @@ __global__ void __launch_bounds__(256) b2_adam_kernel(AdamB2Args a) {
 
 // ---------------------------------------------------------------------------
 // B200 mode, grouped: the Adam step of every parameter of a layer in one
-// persistent launch.  State blocks of 2048 elements, one per 256-thread CTA
+// persistent launch.  State blocks of 2048 elements, one per 256-thread group
 // iteration; thread t owns elements [8t, 8t+8) of the block, so the update,
 // the block absmax and the encode run from registers in a single HBM pass:
 // read R (4 B) + m, v codes (2 B), write m, v codes (2 B) + N bf16 (2 B)
-// [+ zero R (4 B)] per element.  Dynamic-map decode reads a copy of the map
-// replicated over 16 banks (entry i for lane L at word 16 i + L % 16); the
-// encode is one bucket-table lookup (dmap_encode_lut).  Element pairs go
-// through the packed f32x2 helpers (mul2_rn, add2_rn), which round every lane like the
-// scalar __fmul_rn / __fadd_rn.
+// [+ zero R (4 B)] per element.  b2_adam_group_kernel runs the linear codec,
+// b2_adam_dyn_kernel the dynamic map.  Element pairs go through the packed
+// f32x2 helpers (mul2_rn, add2_sep), which round every lane like the scalar
+// __fmul_rn / __fadd_rn.
 // ---------------------------------------------------------------------------
 constexpr int kAdamGroupMax = 16;
 
@@ -181,6 +180,7 @@ struct AdamGroupArgs {
     float b1, b2, eps;
     int zero_accum;
     unsigned int* work;  // [next block, CTAs done], zero between launches
+    uint32_t one;        // 1 (b2_adam_dyn_kernel's run-time multipliers)
 };
 
 // ---------------------------------------------------------------------------
@@ -250,40 +250,14 @@ __global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ misma
     if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
-// Dynamic-codec shared memory of b2_adam_group_kernel: the two bucket tables,
-// two 16-bank replicated maps and the two sorted maps.
-constexpr int kAdamDynSmem = (2 * kDmapLutEntries + kDmapLutUEntries) * 8 + (2 * 256 * 16 + 2 * 256) * 4;
-
-// A CTA of 512 threads is two independent 256-thread halves: each takes its
-// own blocks and synchronises through its own named barrier, while both share
-// one copy of the code tables, so two CTAs (32 warps) fit an SM where three
-// 256-thread CTAs (24 warps) did.
-template <bool DYN>
+// Linear codec.  A CTA of 512 threads is two independent 256-thread halves,
+// each taking its own blocks and synchronising through its own named barrier,
+// so two CTAs (32 warps) fit an SM.
 __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_constant__ AdamGroupArgs a) {
-    extern __shared__ __align__(16) uint2 dyn_smem[];
     __shared__ float red_m[2][2][8], red_v[2][2][8];  // [half][block parity][warp]: one barrier per block
     const int half = threadIdx.x >> 8, tid = threadIdx.x & 255;
-    const int lane = tid & 31, warp = tid >> 5, l16 = lane & 15;
+    const int lane = tid & 31, warp = tid >> 5;
     const int vcta = blockIdx.x * 2 + half, vgrid = gridDim.x * 2;
-    uint2* lut_s = dyn_smem;
-    uint2* lut_u = lut_s + 2 * kDmapLutEntries;
-    float* rep_s = reinterpret_cast<float*>(lut_u + kDmapLutUEntries);
-    float* rep_u = rep_s + 256 * 16;
-    float* map_s = rep_u + 256 * 16;
-    float* map_u = map_s + 256;
-    if (DYN) {
-        for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
-            rep_s[i] = c_dmap_signed[i >> 4];
-            rep_u[i] = c_dmap_unsigned[i >> 4];
-        }
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-            map_s[i] = c_dmap_signed[i];
-            map_u[i] = c_dmap_unsigned[i];
-        }
-        for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) lut_s[i] = g_dmap_lut_s[i];
-        for (int i = threadIdx.x; i < kDmapLutUEntries; i += blockDim.x) lut_u[i] = g_dmap_lut_u[i];
-    }
-    __syncthreads();
     const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
     const float omb1 = __fsub_rn(1.0f, a.b1), omb2 = __fsub_rn(1.0f, a.b2);
     const float2 b1x2 = make_float2(a.b1, a.b1), b2x2 = make_float2(a.b2, a.b2);
@@ -337,14 +311,8 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
                 const uint32_t wm = k < 4 ? qm.x : qm.y, wv = k < 4 ? qv.x : qv.y;
                 const uint32_t cm0 = (wm >> (8 * (k & 3))) & 0xffu, cm1 = (wm >> (8 * (k & 3) + 8)) & 0xffu;
                 const uint32_t cv0 = (wv >> (8 * (k & 3))) & 0xffu, cv1 = (wv >> (8 * (k & 3) + 8)) & 0xffu;
-                float2 m0, v0;
-                if (DYN) {
-                    m0 = make_float2(rep_s[cm0 * 16 + l16], rep_s[cm1 * 16 + l16]);
-                    v0 = make_float2(rep_u[cv0 * 16 + l16], rep_u[cv1 * 16 + l16]);
-                } else {
-                    m0 = make_float2((float)(int8_t)cm0, (float)(int8_t)cm1);
-                    v0 = make_float2((float)(int8_t)cv0, (float)(int8_t)cv1);
-                }
+                float2 m0 = make_float2((float)(int8_t)cm0, (float)(int8_t)cm1);
+                float2 v0 = make_float2((float)(int8_t)cv0, (float)(int8_t)cv1);
                 m0 = mul2_rn(m0, smx2);
                 v0 = mul2_rn(v0, svx2);
                 float2 gg = make_float2(g[k], g[k + 1]);
@@ -399,39 +367,13 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
         float nsm, nsv;
         if (cvalid) {
             uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
-            if (!DYN) {
-                nsm = lin_scale_from_absmax(bm);
-                nsv = lin_scale_from_absmax(bv);
-                const float im = lin_inv(nsm), iv = lin_inv(nsv);
+            nsm = lin_scale_from_absmax(bm);
+            nsv = lin_scale_from_absmax(bv);
+            const float im = lin_inv(nsm), iv = lin_inv(nsv);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    om[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(mo[k], im)) << (8 * (k & 3));
-                    ov[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(va[k], iv)) << (8 * (k & 3));
-                }
-            } else {
-                nsm = bm;
-                nsv = bv;
-                const float im = dyn_inv(bm), iv = dyn_inv(bv);
-                const float2 imx2 = make_float2(im, im), ivx2 = make_float2(iv, iv);
-                uint32_t ef = 0;
-#pragma unroll
-                for (int k = 0; k < 8; k += 2) {
-                    const float2 m2 = mul2_rn(make_float2(mo[k], mo[k + 1]), imx2);  // dyn_xn, paired
-                    const float2 v2 = mul2_rn(make_float2(va[k], va[k + 1]), ivx2);
-                    const int sh = 8 * (k & 3);
-                    om[k >> 2] |= (dmap_encode_lut_flag<true>(lut_s, m2.x, ef) |
-                                   (dmap_encode_lut_flag<true>(lut_s, m2.y, ef) << 8)) << sh;
-                    ov[k >> 2] |= (dmap_encode_lut_flag<false>(lut_u, v2.x, ef) |
-                                   (dmap_encode_lut_flag<false>(lut_u, v2.y, ef) << 8)) << sh;
-                }
-                if (ef > 0xffu) {  // rare: a bucket that needs the search; redo this thread's 16 codes
-                    om[0] = om[1] = ov[0] = ov[1] = 0u;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {  // the same normalised values, formed again
-                        om[k >> 2] |= dmap_encode_rare(map_s, __fmul_rn(mo[k], im)) << (8 * (k & 3));
-                        ov[k >> 2] |= dmap_encode_rare(map_u, __fmul_rn(va[k], iv)) << (8 * (k & 3));
-                    }
-                }
+            for (int k = 0; k < 8; ++k) {
+                om[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(mo[k], im)) << (8 * (k & 3));
+                ov[k >> 2] |= ((uint32_t)(uint8_t)lin_encode(va[k], iv)) << (8 * (k & 3));
             }
             *reinterpret_cast<uint2*>(a.m8[cp] + ce0) = make_uint2(om[0], om[1]);
             *reinterpret_cast<uint2*>(a.v8[cp] + ce0) = make_uint2(ov[0], ov[1]);
@@ -445,6 +387,223 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
         gb = next;
     }
     // The last half out resets the counters for the next launch.
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(a.work + 1, 1u) == (unsigned)vgrid - 1u) {
+            a.work[0] = 0u;
+            a.work[1] = 0u;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// B200 mode, dynamic codec: the grouped Adam with its CUDA-core work laid out
+// for the sm_100 pipes.  The integer/logic pipe issues at half the FMA pipe's
+// rate and was the busiest one (mostly the encode's index arithmetic), so:
+//   * a 1024-thread CTA is four independent 256-thread groups, each taking
+//     whole 2048-element blocks (8 elements per thread) from the device
+//     counter, all four sharing one copy of the tables; one CTA per SM;
+//   * decode: both maps in one 64 KB table whose row c holds 32 copies of
+//     the signed map's entry c, then 32 of the unsigned map's (256 bytes), so
+//     one byte permute of the packed codes forms a lane's bank-private offset
+//     c * 256 + 4 lane (+ 128 for v);
+//   * the block maxima are reduced NaN-propagating (a redux over the bit
+//     patterns); a block whose maxima are finite encodes every value with the
+//     flag-free bucket lookup (dmap_enc_fast_*), the rare other blocks reduce
+//     again ignoring NaN, as the reference's max does, and encode by the
+//     binary search -- the same codes and scales as b2_adam_group_kernel;
+//   * the codes are packed into words by multiply-adds with run-time powers
+//     of two, the group's eight warp maxima combined by one redux per warp.
+// ---------------------------------------------------------------------------
+constexpr int kAdamDynThreads = 1024;
+constexpr int kAdamDynDecBytes = 256 * 256;
+constexpr int kAdamDynSmem2 = kAdamDynDecBytes + (2 * kDmapLutEntries + kDmapLutUEntries) * 8 + 2 * 256 * 4;
+
+// Barrier `id` (1..4) of one 256-thread group (group-uniform id).
+__device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+__global__ void __launch_bounds__(kAdamDynThreads, 1) b2_adam_dyn_kernel(const __grid_constant__ AdamGroupArgs a) {
+    extern __shared__ __align__(16) uint8_t adam_smem[];
+    float* dec = reinterpret_cast<float*>(adam_smem);
+    uint2* lut_s = reinterpret_cast<uint2*>(adam_smem + kAdamDynDecBytes);
+    uint2* lut_u = lut_s + 2 * kDmapLutEntries;
+    float* map_s = reinterpret_cast<float*>(lut_u + kDmapLutUEntries);
+    float* map_u = map_s + 256;
+    __shared__ uint32_t red[4][2][2][8];  // [group][block parity][m, v][warp]: NaN-propagating maxima (bits)
+    __shared__ uint32_t red2[4][2][8];    // [group][m, v][warp]: NaN-ignoring maxima (rare blocks)
+    __shared__ int s_next[4][2];
+    const int grp = threadIdx.x >> 8, tid = threadIdx.x & 255;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int vcta = blockIdx.x * 4 + grp, vgrid = gridDim.x * 4;
+    for (int i = threadIdx.x; i < 256 * 64; i += blockDim.x)
+        dec[i] = (i & 63) < 32 ? c_dmap_signed[i >> 6] : c_dmap_unsigned[i >> 6];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        map_s[i] = c_dmap_signed[i];
+        map_u[i] = c_dmap_unsigned[i];
+    }
+    for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) lut_s[i] = g_dmap_lut_s[i];
+    for (int i = threadIdx.x; i < kDmapLutUEntries; i += blockDim.x) lut_u[i] = g_dmap_lut_u[i];
+    __syncthreads();
+    // run-time powers of two: the products below stay multiplies (FMA pipe)
+    const uint32_t one = a.one;
+    const uint32_t m1 = one << 1, m15 = one << 15, m16 = one << 16, p8 = one << 8, p24 = one << 24;
+    const uint32_t dec_base = smem_u32_addr(dec), off_m = (uint32_t)lane * 4u, off_v = off_m + 128u;
+    const uint32_t lut_s_adj = smem_u32_addr(lut_s) - (uint32_t)(kDmapLutExpLo << kDmapLutLog2P) * 8u;
+    const uint32_t lut_u_adj = smem_u32_addr(lut_u) - (uint32_t)(kDmapLutExpLo << kDmapLutULog2P) * 8u;
+    const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
+    const float omb1 = __fsub_rn(1.0f, a.b1), omb2 = __fsub_rn(1.0f, a.b2);
+    const float2 b1x2 = make_float2(a.b1, a.b1), b2x2 = make_float2(a.b2, a.b2);
+    const float2 omb1x2 = make_float2(omb1, omb1), omb2x2 = make_float2(omb2, omb2);
+    const float2 clipx2 = make_float2(clip, clip);
+    const bool fast_dir = a.eps >= 1e-10f;  // the error bound and the flush-to-zero argument need it
+    const int total = a.block_begin[a.np];
+    int it = 0;
+    int gb = vcta;
+    int p = 0, b = 0;
+    int64_t e0 = 0;
+    bool valid = false;
+    float sm = 0.0f, sv = 0.0f;
+    float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0;
+    uint2 qm = make_uint2(0u, 0u), qv = qm;
+    // a group's blocks come in increasing order, so the owning parameter only moves forward
+    auto fetch = [&](int blk) {
+#pragma unroll 1
+        while (p + 1 < a.np && blk >= a.block_begin[p + 1]) ++p;
+        b = blk - a.block_begin[p];
+        e0 = (int64_t)b * 2048 + tid * 8;
+        valid = e0 < a.count[p];  // counts are multiples of 8
+        sm = a.ms[p][b];
+        sv = a.vs[p][b];
+        if (valid) {
+            g0 = *reinterpret_cast<const float4*>(a.accum[p] + e0);
+            g1 = *reinterpret_cast<const float4*>(a.accum[p] + e0 + 4);
+            qm = *reinterpret_cast<const uint2*>(a.m8[p] + e0);
+            qv = *reinterpret_cast<const uint2*>(a.v8[p] + e0);
+        }
+    };
+    if (gb < total) fetch(gb);
+    while (gb < total) {
+        const int par = it & 1;
+        if (tid == 0) s_next[grp][par] = (int)atomicAdd(a.work, 1u) + vgrid;
+        float mo[8], va[8];
+        float am = 0.0f, av = 0.0f;
+        if (valid) {
+            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            const float2 smx2 = make_float2(sm, sm), svx2 = make_float2(sv, sv);
+            float nq[8];
+            uint32_t dmask = fast_dir ? 0u : 0xffu;  // elements whose quotient needs the IEEE path
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                const uint32_t wm = k < 4 ? qm.x : qm.y, wv = k < 4 ? qv.x : qv.y;
+                const uint32_t s0 = 0x5504u | ((uint32_t)(k & 3) << 4), s1 = s0 + 0x10u;  // byte k & 3, (k & 3) + 1
+                float2 m0 = make_float2(lds_f32(dec_base + prmt(wm, off_m, s0)), lds_f32(dec_base + prmt(wm, off_m, s1)));
+                float2 v0 = make_float2(lds_f32(dec_base + prmt(wv, off_v, s0)), lds_f32(dec_base + prmt(wv, off_v, s1)));
+                m0 = mul2_rn(m0, smx2);
+                v0 = mul2_rn(v0, svx2);
+                float2 gg = make_float2(g[k], g[k + 1]);
+                if (clip != 1.0f) gg = mul2_rn(gg, clipx2);
+                // products paired, sums scalar (a packed add of fresh products would be fused)
+                const float2 mo2 = add2_sep(mul2_rn(b1x2, m0), mul2_rn(omb1x2, gg));
+                const float2 va2 = add2_sep(mul2_rn(b2x2, v0), mul2_rn(mul2_rn(omb2x2, gg), gg));
+                mo[k] = mo2.x;
+                mo[k + 1] = mo2.y;
+                va[k] = va2.x;
+                va[k + 1] = va2.y;
+                uint32_t f0, f1;
+                nq[k] = adam_dir_q(mo2.x, va2.x, a.eps, f0);
+                nq[k + 1] = adam_dir_q(mo2.y, va2.y, a.eps, f1);
+                dmask |= (f0 | (f1 << 1)) << k;
+                am = fmax3_nan(am, fabsf(mo2.x), fabsf(mo2.y));
+                av = fmax3_nan(av, fabsf(va2.x), fabsf(va2.y));
+            }
+            if (dmask) {  // rare (or eps < 1e-10): the flagged quotients the IEEE way
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (dmask & (1u << k)) nq[k] = adam_dir_exact_rare(mo[k], va[k], a.eps);
+            }
+            uint32_t nb[4];
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+                const __nv_bfloat162 nn = __floats2bfloat162_rn(nq[k], nq[k + 1]);  // .x = nq[k] in the low half
+                nb[k >> 1] = *reinterpret_cast<const uint32_t*>(&nn);
+            }
+            *reinterpret_cast<uint4*>(a.nout[p] + e0) = make_uint4(nb[0], nb[1], nb[2], nb[3]);
+        }
+        // non-negative or NaN (canonical 0x7fffffff): NaN-propagating maxima as unsigned bit patterns
+        const uint32_t amb = __reduce_max_sync(0xffffffffu, __float_as_uint(am));
+        const uint32_t avb = __reduce_max_sync(0xffffffffu, __float_as_uint(av));
+        if (lane == 0) { red[grp][par][0][warp] = amb; red[grp][par][1][warp] = avb; }
+        group_bar(1 + grp);  // this group's 256 threads; the parity's slots are rewritten two blocks later
+        const uint32_t bmb = __reduce_max_sync(0xffffffffu, lane < 8 ? red[grp][par][0][lane] : 0u);
+        const uint32_t bvb = __reduce_max_sync(0xffffffffu, lane < 8 ? red[grp][par][1][lane] : 0u);
+        const int next = s_next[grp][par];
+        ++it;
+        const int cp = p, cb = b;
+        const int64_t ce0 = e0;
+        const bool cvalid = valid;
+        if (next < total) fetch(next);
+        // group-uniform: finite maxima that are 0 or normal, so 1 / max is finite
+        // and every normalised value lies within 1 + 2^-23
+        const bool finite = bmb < 0x7f800000u && bvb < 0x7f800000u && (bmb == 0u || bmb >= 0x00800000u) &&
+                            (bvb == 0u || bvb >= 0x00800000u);
+        float nsm = __uint_as_float(bmb), nsv = __uint_as_float(bvb);
+        if (!finite) {
+            // rare: a NaN or an infinity in the block -- the maxima again, ignoring NaN
+            float am2 = 0.0f, av2 = 0.0f;
+            if (cvalid) {
+#pragma unroll
+                for (int k = 0; k < 8; k += 2) {
+                    am2 = fmax3(am2, fabsf(mo[k]), fabsf(mo[k + 1]));
+                    av2 = fmax3(av2, fabsf(va[k]), fabsf(va[k + 1]));
+                }
+            }
+            am2 = warp_max_nonneg(am2);
+            av2 = warp_max_nonneg(av2);
+            if (lane == 0) { red2[grp][0][warp] = __float_as_uint(am2); red2[grp][1][warp] = __float_as_uint(av2); }
+            group_bar(1 + grp);
+            nsm = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < 8 ? red2[grp][0][lane] : 0u));
+            nsv = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < 8 ? red2[grp][1][lane] : 0u));
+        }
+        if (cvalid) {
+            const float im = dyn_inv(nsm), iv = dyn_inv(nsv);
+            uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
+            if (finite) {
+                const float2 imx2 = make_float2(im, im), ivx2 = make_float2(iv, iv);
+#pragma unroll
+                for (int k = 0; k < 8; k += 2) {
+                    const float2 m2 = mul2_rn(make_float2(mo[k], mo[k + 1]), imx2);  // dyn_xn, paired
+                    const float2 v2 = mul2_rn(make_float2(va[k], va[k + 1]), ivx2);
+                    // byte (k & 3) and (k & 3) + 1 of the words: multiply-adds by 2^(8 j)
+                    const uint32_t lo = (k & 2) ? m16 : one, hi = (k & 2) ? p24 : p8;
+                    om[k >> 2] += dmap_enc_fast_s(lut_s_adj, m2.x, m1, m15) * lo +
+                                  dmap_enc_fast_s(lut_s_adj, m2.y, m1, m15) * hi;
+                    ov[k >> 2] += dmap_enc_fast_u(lut_u_adj, v2.x, m16) * lo + dmap_enc_fast_u(lut_u_adj, v2.y, m16) * hi;
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    om[k >> 2] |= dmap_encode_rare(map_s, __fmul_rn(mo[k], im)) << (8 * (k & 3));
+                    ov[k >> 2] |= dmap_encode_rare(map_u, __fmul_rn(va[k], iv)) << (8 * (k & 3));
+                }
+            }
+            *reinterpret_cast<uint2*>(a.m8[cp] + ce0) = make_uint2(om[0], om[1]);
+            *reinterpret_cast<uint2*>(a.v8[cp] + ce0) = make_uint2(ov[0], ov[1]);
+            if (a.zero_accum) {
+                float* z = const_cast<float*>(a.accum[cp]) + ce0;
+                *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4*>(z + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (tid == 0) { a.ms[cp][cb] = nsm; a.vs[cp][cb] = nsv; }
+        }
+        gb = next;
+    }
+    // The last group out resets the counters for the next launch.
     if (tid == 0) {
         __threadfence();
         if (atomicAdd(a.work + 1, 1u) == (unsigned)vgrid - 1u) {

@@ -671,14 +671,13 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         }
     }
     const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
-    // 59 KB of tables per 512-thread CTA: two CTAs (32 warps) per SM
-    static_assert(2 * (kAdamDynSmem + 1024) <= 228 * 1024, "two dynamic-codec Adam CTAs must fit an SM");
+    // 116 KB of tables per 1024-thread CTA, one CTA (32 warps) per SM
+    static_assert(kAdamDynSmem2 + 1024 <= 227 * 1024, "the dynamic-codec Adam tables must fit one CTA");
     static bool attr_set[kMaxDevices] = {};
     int dev = 0;
     AETH_TRY(current_device(&dev));
     if (dyn && !attr_set[dev]) {
-        AETH_CUDA(cudaFuncSetAttribute(b2_adam_group_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kAdamDynSmem));
+        AETH_CUDA(cudaFuncSetAttribute(b2_adam_dyn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAdamDynSmem2));
         attr_set[dev] = true;
     }
     for (int off = 0; off < np; off += kAdamGroupMax) {
@@ -709,12 +708,13 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         a.eps = cfg.eps;
         a.zero_accum = zero_accum;
         a.work = c->work;
-        // each CTA is two 256-thread halves, each half one block at a time
-        const int grid = std::min((blocks + 1) / 2, num_sms() * 2);
+        a.one = 1u;
+        // dynamic codec: 1024-thread CTAs of four 256-thread groups, one per SM;
+        // linear: 512-thread CTAs of two groups, two per SM; each group one block at a time
         if (dyn)
-            b2_adam_group_kernel<true><<<grid, 512, kAdamDynSmem, st>>>(a);
+            b2_adam_dyn_kernel<<<std::min((blocks + 3) / 4, num_sms()), kAdamDynThreads, kAdamDynSmem2, st>>>(a);
         else
-            b2_adam_group_kernel<false><<<grid, 512, 0, st>>>(a);
+            b2_adam_group_kernel<<<std::min((blocks + 1) / 2, num_sms() * 2), 512, 0, st>>>(a);
         AETH_LAUNCH_CHECK();
     }
     return AETH_OK;
@@ -1010,7 +1010,7 @@ int aeth_selfcheck(int which, unsigned long long* mismatches) {
         } else if (which == AETH_SELFCHECK_ADAM_DIR)
             adam_dir_selfcheck_kernel<<<num_sms() * 8, 256>>>(d);
         else
-            dmap_selfcheck_kernel<<<num_sms() * 8, 256>>>(which == AETH_SELFCHECK_DMAP_SIGNED ? 1 : 0, d);
+            dmap_selfcheck_kernel<<<num_sms() * 8, 256>>>(which == AETH_SELFCHECK_DMAP_SIGNED ? 1 : 0, d, 1u);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaMemcpy(mismatches, d, sizeof(*d), cudaMemcpyDeviceToHost);

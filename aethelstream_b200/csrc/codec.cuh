@@ -194,9 +194,45 @@ __device__ __forceinline__ uint32_t dmap_encode_lut(const uint2* __restrict__ lu
     return code;
 }
 
+// Flag-free bucket encodes for a block whose normalised values are all
+// finite, |xn| <= 1 + 2^-22 (x = xn * (1 / absmax) of a finite absmax): no
+// bucket in that range holds two code changes or needs the search, so the
+// entry's code word carries no flag and the index needs no upper clamp.  A
+// magnitude below 2^-24 is raised to 2^-24: every key of bucket 0 has the
+// code of 0.0 in both maps (their smallest non-zero entries are above
+// 1.6e-7), so the raised key encodes the same.  The bucket index is formed by
+// a multiply-high with a power of two known only at run time (m15 = 2^15:
+// bits >> 17, m16 = 2^16: bits >> 16, m1 = 2: the sign bit), which issues on
+// the FMA pipe rather than as a shift on the integer pipe.  lut_adj is the
+// table's shared address minus 8 x the first bucket's (kDmapLutExpLo << log2 P)
+// index.  `code + 1` never carries out of the byte (a bucket's lower code is
+// below 255 wherever the compare can add one).
+__device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
+    uint2 e;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(e.x), "=r"(e.y) : "r"(addr));
+    return e;
+}
+
+__device__ __forceinline__ uint32_t dmap_enc_fast_s(uint32_t lut_adj, float xn, uint32_t m1, uint32_t m15) {
+    const uint32_t xb = __float_as_uint(xn);
+    const uint32_t km = __float_as_uint(fmaxf(fabsf(xn), 0x1p-24f));
+    const uint32_t neg = (uint32_t)((int32_t)xb >> 31);
+    const uint32_t idx = __umulhi(km, m15) + __umulhi(xb, m1) * (uint32_t)kDmapLutEntries;
+    const uint2 e = lds_u2(lut_adj + idx * 8u);
+    return e.y + ((km ^ neg) >= e.x ? 1u : 0u);
+}
+
+__device__ __forceinline__ uint32_t dmap_enc_fast_u(uint32_t lut_adj, float xn, uint32_t m16) {
+    const uint32_t k = __float_as_uint(fmaxf(xn, 0x1p-24f));
+    const uint2 e = lds_u2(lut_adj + __umulhi(k, m16) * 8u);
+    return e.y + (k >= e.x ? 1u : 0u);
+}
+
 // Every float bit pattern through dmap_encode_lut and dmap_encode; counts
 // disagreements (a self-check of the bucket tables, run by the test suite).
-__global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restrict__ mismatches) {
+// Patterns with |x| <= 1 + 2^-22 (signed map) or 0 <= x <= 1 + 2^-22
+// (unsigned map; -0.0 included) also go through the flag-free encode.
+__global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restrict__ mismatches, uint32_t one) {
     __shared__ float map[256];
     __shared__ uint2 lut[2 * kDmapLutEntries];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) map[i] = is_signed ? c_dmap_signed[i] : c_dmap_unsigned[i];
@@ -204,6 +240,9 @@ __global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restr
     for (int i = threadIdx.x; i < (is_signed ? 2 * kDmapLutEntries : kDmapLutUEntries); i += blockDim.x)
         lut[i] = is_signed ? g_dmap_lut_s[i] : g_dmap_lut_u[i];
     __syncthreads();
+    const uint32_t adj = smem_u32_addr(lut) - (uint32_t)(kDmapLutExpLo << (is_signed ? kDmapLutLog2P : kDmapLutULog2P)) * 8u;
+    const uint32_t m1 = one << 1, m15 = one << 15, m16 = one << 16;
+    const uint32_t top = __float_as_uint(1.0f) + 2u;  // bits of 1 + 2^-22
     unsigned long long bad = 0;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < (1ull << 32); i += stride) {
@@ -211,6 +250,9 @@ __global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restr
         const uint32_t want = dmap_encode(map, x);
         const uint32_t got = is_signed ? dmap_encode_lut<true>(lut, map, x) : dmap_encode_lut<false>(lut, map, x);
         bad += got != want;
+        const uint32_t ab = (uint32_t)i & 0x7fffffffu;
+        if (is_signed && ab <= top) bad += dmap_enc_fast_s(adj, x, m1, m15) != want;
+        if (!is_signed && ((uint32_t)i <= top || (uint32_t)i == 0x80000000u)) bad += dmap_enc_fast_u(adj, x, m16) != want;
     }
     bad = warp_sum_u64(bad);
     if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);

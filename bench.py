@@ -172,8 +172,8 @@ def load_traffic():
 
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons sampled during the timed
-    region: NVML in a thread every 10 ms (read-only queries), else
-    nvidia-smi -lms 200."""
+    region by NVML in a thread every 10 ms (read-only queries); without NVML
+    the line reports no clocks."""
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, gpu_index):
