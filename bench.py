@@ -160,7 +160,9 @@ def load_peaks():
 
 
 def load_traffic():
-    """Per-launch DRAM bytes of the dominant kernels from the committed ncu summary (if present)."""
+    """Per-launch DRAM bytes of the C2 step kernels from a committed ncu summary,
+    profiles/traffic_c2.json, when one exists (none for the current kernels:
+    the roofline's traffic is then null)."""
     p = os.path.join(ROOT, "profiles", "traffic_c2.json")
     if os.path.exists(p):
         try:
