@@ -233,18 +233,81 @@ __device__ __forceinline__ float adam_dir_fast(float mo, float va, float eps) {
     return flag ? adam_dir_exact_rare(mo, va, eps) : q;
 }
 
+// adam_dir_q's approximate quotient with its checks folded into two running
+// minima over a thread's elements instead of a flag per element:
+//   tie_min  = min of (bits(q) << 16) + ((kAdamDirGuard - 0x8000) << 16): below
+//              2 kAdamDirGuard << 16 exactly when some q's low 16 bits lie within
+//              the guard of the bf16 tie;
+//   tiny_min = min of 2 bits(q) - 2: below (27 << 24) - 2 exactly when some q is
+//              non-zero with magnitude below 2^-100 (q = 0 maps to the top).
+// m16 = 2^16 and m2 = 2 at run time (multiply-adds on the FMA pipe).
+__device__ __forceinline__ float adam_dir_q_raw(float mo, float va, float eps, uint32_t m16, uint32_t m2,
+                                                uint32_t& tie_min, uint32_t& tiny_min) {
+    float s, r;
+    asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(s) : "f"(va));
+    const float d = __fadd_rn(s, eps);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+    const float q = __fmul_rn(mo, r);
+    const uint32_t qb = __float_as_uint(q);
+    tie_min = min(tie_min, qb * m16 + ((kAdamDirGuard - 0x8000u) << 16));
+    tiny_min = min(tiny_min, qb * m2 - 2u);
+    return q;
+}
+
+// True when none of a thread's approximate quotients needs the IEEE path,
+// given the two minima of adam_dir_q_raw and the thread's NaN-propagating
+// maxima of |mo| and |va| and minimum of va: then no element would carry
+// adam_dir_q's flag.  A q near a bf16 tie or tiny and non-zero shows in the
+// minima; an infinite or NaN q needs |mo| >= 2^90 (|q| <= |mo| / eps and
+// eps >= 1e-10), a NaN or infinite mo, or a NaN va; a negative va shows in
+// vmin (-0 passes, as adam_dir_q lets it).  A thread that fails re-checks
+// each element with adam_dir_q, so the results equal the per-element flags'.
+__device__ __forceinline__ bool adam_dir_fast_thread_ok(uint32_t tie_min, uint32_t tiny_min, float am, float av,
+                                                        float vmin) {
+    return tie_min >= (2u * kAdamDirGuard << 16) && tiny_min >= (27u << 24) - 2u &&
+           __float_as_uint(am) < 0x5c800000u && __float_as_uint(av) < 0x7f800000u && !(vmin < 0.0f);
+}
+
 // Every float bit pattern as va, with mo drawn from [-0.5, 0.5) by a hash of
 // the pattern and eps = 1e-8: counts bf16 disagreements of the two paths.
+// The same patterns in groups of 8 consecutive ones through the per-thread
+// folded checks (adam_dir_q_raw, adam_dir_fast_thread_ok, then each element's
+// own check when the group fails), with mo also scaled by 2^s, s = 4 (g mod 61)
+// - 120 for group g, so groups with huge, tiny, infinite or zero quotients
+// occur too.
 __global__ void adam_dir_selfcheck_kernel(unsigned long long* __restrict__ mismatches) {
     unsigned long long bad = 0;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < (1ull << 32); i += stride) {
-        const float va = __uint_as_float((uint32_t)i);
-        const float mo = (float)(((uint32_t)i * 2654435761u) >> 8) * 0x1p-24f - 0.5f;
-        const uint16_t f = f32_to_bf16_bits(adam_dir_fast(mo, va, 1e-8f));
-        const uint16_t e = f32_to_bf16_bits(adam_dir_exact(mo, va, 1e-8f));
-        // NaN results may differ in payload only
-        bad += f != e && !((f & 0x7fffu) > 0x7f80u && (e & 0x7fffu) > 0x7f80u);
+    auto differ = [](uint16_t f, uint16_t e) {  // NaN results may differ in payload only
+        return f != e && !((f & 0x7fffu) > 0x7f80u && (e & 0x7fffu) > 0x7f80u);
+    };
+    const uint32_t m16 = 1u << 16, m2 = 2u;
+    for (uint64_t g = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; g < (1ull << 29); g += stride) {
+        const float scale = ldexpf(1.0f, 4 * (int)(g % 61) - 120);
+        float mo[8], va[8], nq[8];
+        uint32_t tie_min = 0xffffffffu, tiny_min = 0xffffffffu;
+        float am = 0.0f, av = 0.0f, vmin = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t i = (uint32_t)(g * 8 + j);
+            va[j] = __uint_as_float(i);
+            const float m = (float)((i * 2654435761u) >> 8) * 0x1p-24f - 0.5f;
+            bad += differ(f32_to_bf16_bits(adam_dir_fast(m, va[j], 1e-8f)),
+                          f32_to_bf16_bits(adam_dir_exact(m, va[j], 1e-8f)));
+            mo[j] = __fmul_rn(m, scale);
+            nq[j] = adam_dir_q_raw(mo[j], va[j], 1e-8f, m16, m2, tie_min, tiny_min);
+            am = fmax3_nan(am, fabsf(mo[j]), fabsf(mo[j]));
+            av = fmax3_nan(av, fabsf(va[j]), fabsf(va[j]));
+            vmin = fminf(vmin, va[j]);
+        }
+        const bool ok = adam_dir_fast_thread_ok(tie_min, tiny_min, am, av, vmin);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            uint32_t f = 0;
+            if (!ok) adam_dir_q(mo[j], va[j], 1e-8f, f);
+            const float q = f ? adam_dir_exact(mo[j], va[j], 1e-8f) : nq[j];
+            bad += differ(f32_to_bf16_bits(q), f32_to_bf16_bits(adam_dir_exact(mo[j], va[j], 1e-8f)));
+        }
     }
     bad = warp_sum_u64(bad);
     if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
@@ -409,15 +472,16 @@ __global__ void __launch_bounds__(512, 2) b2_adam_group_kernel(const __grid_cons
 //     c * 256 + 4 lane (+ 128 for v);
 //   * the block maxima are reduced NaN-propagating (a redux over the bit
 //     patterns); a block whose maxima are finite encodes every value with the
-//     flag-free bucket lookup (dmap_enc_fast_*), the rare other blocks reduce
+//     flag-free bucket lookup (dmap_enc4_*, 4-byte entries: a warp's 32
+//     lookups are one 128-byte wavefront when they hit distinct banks), the
+//     rare other blocks reduce
 //     again ignoring NaN, as the reference's max does, and encode by the
 //     binary search -- the same codes and scales as b2_adam_group_kernel;
-//   * the codes are packed into words by multiply-adds with run-time powers
-//     of two, the group's eight warp maxima combined by one redux per warp.
+//   * the group's eight warp maxima are combined by one redux per warp.
 // ---------------------------------------------------------------------------
 constexpr int kAdamDynThreads = 1024;
 constexpr int kAdamDynDecBytes = 256 * 256;
-constexpr int kAdamDynSmem2 = kAdamDynDecBytes + (2 * kDmapLutEntries + kDmapLutUEntries) * 8 + 2 * 256 * 4;
+constexpr int kAdamDynSmem2 = kAdamDynDecBytes + (2 * kDmapLutEntries + kDmapLutUEntries) * 4 + 2 * 256 * 4;
 
 // Barrier `id` (1..4) of one 256-thread group (group-uniform id).
 __device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
@@ -431,8 +495,8 @@ __device__ __forceinline__ float lds_f32(uint32_t addr) {
 __global__ void __launch_bounds__(kAdamDynThreads, 1) b2_adam_dyn_kernel(const __grid_constant__ AdamGroupArgs a) {
     extern __shared__ __align__(16) uint8_t adam_smem[];
     float* dec = reinterpret_cast<float*>(adam_smem);
-    uint2* lut_s = reinterpret_cast<uint2*>(adam_smem + kAdamDynDecBytes);
-    uint2* lut_u = lut_s + 2 * kDmapLutEntries;
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(adam_smem + kAdamDynDecBytes);
+    uint32_t* lut_u = lut_s + 2 * kDmapLutEntries;
     float* map_s = reinterpret_cast<float*>(lut_u + kDmapLutUEntries);
     float* map_u = map_s + 256;
     __shared__ uint32_t red[4][2][2][8];  // [group][block parity][m, v][warp]: NaN-propagating maxima (bits)
@@ -447,15 +511,15 @@ __global__ void __launch_bounds__(kAdamDynThreads, 1) b2_adam_dyn_kernel(const _
         map_s[i] = c_dmap_signed[i];
         map_u[i] = c_dmap_unsigned[i];
     }
-    for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) lut_s[i] = g_dmap_lut_s[i];
-    for (int i = threadIdx.x; i < kDmapLutUEntries; i += blockDim.x) lut_u[i] = g_dmap_lut_u[i];
+    for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) lut_s[i] = g_dmap_lut4_s[i];
+    for (int i = threadIdx.x; i < kDmapLutUEntries; i += blockDim.x) lut_u[i] = g_dmap_lut4_u[i];
     __syncthreads();
     // run-time powers of two: the products below stay multiplies (FMA pipe)
     const uint32_t one = a.one;
-    const uint32_t m1 = one << 1, m15 = one << 15, m16 = one << 16, p8 = one << 8, p24 = one << 24;
+    const uint32_t m1 = one << 1, m8 = one << 8, m15 = one << 15, m16 = one << 16;
     const uint32_t dec_base = smem_u32_addr(dec), off_m = (uint32_t)lane * 4u, off_v = off_m + 128u;
-    const uint32_t lut_s_adj = smem_u32_addr(lut_s) - (uint32_t)(kDmapLutExpLo << kDmapLutLog2P) * 8u;
-    const uint32_t lut_u_adj = smem_u32_addr(lut_u) - (uint32_t)(kDmapLutExpLo << kDmapLutULog2P) * 8u;
+    const uint32_t lut_s_adj = smem_u32_addr(lut_s) - (uint32_t)(kDmapLutExpLo << kDmapLutLog2P) * 4u;
+    const uint32_t lut_u_adj = smem_u32_addr(lut_u) - (uint32_t)(kDmapLutExpLo << kDmapLutULog2P) * 4u;
     const float clip = a.clip_dev ? *a.clip_dev : a.clip_host;
     const float omb1 = __fsub_rn(1.0f, a.b1), omb2 = __fsub_rn(1.0f, a.b2);
     const float2 b1x2 = make_float2(a.b1, a.b1), b2x2 = make_float2(a.b2, a.b2);
@@ -497,7 +561,9 @@ __global__ void __launch_bounds__(kAdamDynThreads, 1) b2_adam_dyn_kernel(const _
             const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
             const float2 smx2 = make_float2(sm, sm), svx2 = make_float2(sv, sv);
             float nq[8];
-            uint32_t dmask = fast_dir ? 0u : 0xffu;  // elements whose quotient needs the IEEE path
+            // the approximate quotients' checks, folded per thread (adam_dir_fast_thread_ok)
+            uint32_t tie_min = 0xffffffffu, tiny_min = 0xffffffffu;
+            float vmin = 0.0f;
 #pragma unroll
             for (int k = 0; k < 8; k += 2) {
                 const uint32_t wm = k < 4 ? qm.x : qm.y, wv = k < 4 ? qv.x : qv.y;
@@ -515,17 +581,20 @@ __global__ void __launch_bounds__(kAdamDynThreads, 1) b2_adam_dyn_kernel(const _
                 mo[k + 1] = mo2.y;
                 va[k] = va2.x;
                 va[k + 1] = va2.y;
-                uint32_t f0, f1;
-                nq[k] = adam_dir_q(mo2.x, va2.x, a.eps, f0);
-                nq[k + 1] = adam_dir_q(mo2.y, va2.y, a.eps, f1);
-                dmask |= (f0 | (f1 << 1)) << k;
+                nq[k] = adam_dir_q_raw(mo2.x, va2.x, a.eps, m16, m1, tie_min, tiny_min);
+                nq[k + 1] = adam_dir_q_raw(mo2.y, va2.y, a.eps, m16, m1, tie_min, tiny_min);
                 am = fmax3_nan(am, fabsf(mo2.x), fabsf(mo2.y));
                 av = fmax3_nan(av, fabsf(va2.x), fabsf(va2.y));
+                vmin = fmin3(vmin, va2.x, va2.y);
             }
-            if (dmask) {  // rare (or eps < 1e-10): the flagged quotients the IEEE way
+            if (!fast_dir || !adam_dir_fast_thread_ok(tie_min, tiny_min, am, av, vmin)) {
+                // rare (or eps < 1e-10): each element's own check, the flagged ones the IEEE way
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    if (dmask & (1u << k)) nq[k] = adam_dir_exact_rare(mo[k], va[k], a.eps);
+                for (int k = 0; k < 8; ++k) {
+                    uint32_t f;
+                    adam_dir_q(mo[k], va[k], a.eps, f);
+                    if (f || !fast_dir) nq[k] = adam_dir_exact_rare(mo[k], va[k], a.eps);
+                }
             }
             uint32_t nb[4];
 #pragma unroll
@@ -575,16 +644,19 @@ __global__ void __launch_bounds__(kAdamDynThreads, 1) b2_adam_dyn_kernel(const _
             uint32_t om[2] = {0u, 0u}, ov[2] = {0u, 0u};
             if (finite) {
                 const float2 imx2 = make_float2(im, im), ivx2 = make_float2(iv, iv);
+                uint32_t hm[4], hv[4];  // codes of element pairs in bytes 0 and 1
 #pragma unroll
                 for (int k = 0; k < 8; k += 2) {
                     const float2 m2 = mul2_rn(make_float2(mo[k], mo[k + 1]), imx2);  // dyn_xn, paired
                     const float2 v2 = mul2_rn(make_float2(va[k], va[k + 1]), ivx2);
-                    // byte (k & 3) and (k & 3) + 1 of the words: multiply-adds by 2^(8 j)
-                    const uint32_t lo = (k & 2) ? m16 : one, hi = (k & 2) ? p24 : p8;
-                    om[k >> 2] += dmap_enc_fast_s(lut_s_adj, m2.x, m1, m15) * lo +
-                                  dmap_enc_fast_s(lut_s_adj, m2.y, m1, m15) * hi;
-                    ov[k >> 2] += dmap_enc_fast_u(lut_u_adj, v2.x, m16) * lo + dmap_enc_fast_u(lut_u_adj, v2.y, m16) * hi;
+                    hm[k >> 1] = prmt(dmap_enc4_s(lut_s_adj, m2.x, m1, m8, m15), dmap_enc4_s(lut_s_adj, m2.y, m1, m8, m15),
+                                      0x3340u);
+                    hv[k >> 1] = prmt(dmap_enc4_u(lut_u_adj, v2.x, m8, m16), dmap_enc4_u(lut_u_adj, v2.y, m8, m16), 0x3340u);
                 }
+                om[0] = prmt(hm[0], hm[1], 0x5410u);
+                om[1] = prmt(hm[2], hm[3], 0x5410u);
+                ov[0] = prmt(hv[0], hv[1], 0x5410u);
+                ov[1] = prmt(hv[2], hv[3], 0x5410u);
             } else {
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {

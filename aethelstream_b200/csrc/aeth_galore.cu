@@ -671,7 +671,7 @@ int b2_adam_group(aeth_galore_ctx* c, Param* const* ps, int np, float clip, cons
         }
     }
     const bool dyn = cfg.state_codec == AETH_CODEC_BLOCK_DYNAMIC;
-    // 116 KB of tables per 1024-thread CTA, one CTA (32 warps) per SM
+    // 91 KB of tables per 1024-thread CTA, one CTA (32 warps) per SM
     static_assert(kAdamDynSmem2 + 1024 <= 227 * 1024, "the dynamic-codec Adam tables must fit one CTA");
     static bool attr_set[kMaxDevices] = {};
     int dev = 0;

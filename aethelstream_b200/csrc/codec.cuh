@@ -55,6 +55,8 @@ constexpr int kDmapLutUEntries = kDmapLutUN + 1;
 constexpr uint32_t kDmapSearch = 0x100u;                // in the code word: always search
 __device__ uint2 g_dmap_lut_s[2 * kDmapLutEntries];    // signed map: x >= 0, then x < 0
 __device__ uint2 g_dmap_lut_u[kDmapLutUEntries];       // unsigned map: x >= 0
+__device__ uint32_t g_dmap_lut4_s[2 * kDmapLutEntries];  // the same, packed to 4 bytes (build_dmap_lut4)
+__device__ uint32_t g_dmap_lut4_u[kDmapLutUEntries];
 
 // The binary search on the host (dmap_encode's arithmetic: IEEE single
 // subtraction and comparison).
@@ -105,6 +107,29 @@ inline void build_dmap_lut(const float map[256], int halves, int log2p, uint2* o
     }
 }
 
+// The 4-byte form of a bucket table for the flag-free encode (dmap_enc4_*):
+// entry = t << 8 | code below, t = the threshold key's offset from the
+// bucket's first key (0: every key of the bucket reaches it; 2^(23 - log2p):
+// none does).  A bucket then spans 2^(23 - log2p) keys, bucket 0 included,
+// because the flag-free encode raises magnitudes below 2^-24 to 2^-24; the
+// offset of a key is its low 23 - log2p bits (keys ~bits(|x|) for x < 0
+// count down from the bucket's largest magnitude, so the same holds).
+// Entries only reachable outside that domain (|x| >= 2) are never used.
+inline void build_dmap_lut4(const uint2* lut8, int halves, int log2p, uint32_t* out) {
+    const int nb = (128 - kDmapLutExpLo) << log2p, sh = 23 - log2p;
+    const uint32_t span = 1u << sh;
+    for (int h = 0; h < halves; ++h) {
+        for (int b = 0; b <= nb; ++b) {
+            const uint2 e = lut8[h * (nb + 1) + b];
+            const uint32_t lo_ab = (uint32_t)(b + (kDmapLutExpLo << log2p)) << sh, hi_ab = lo_ab + span - 1u;
+            const uint32_t first = h ? ~hi_ab : lo_ab;
+            uint32_t t = span;
+            if (b < nb && !(e.y & kDmapSearch)) t = e.x <= first ? 0u : (e.x - first >= span ? span : e.x - first);
+            out[h * (nb + 1) + b] = (t << 8) | (e.y & 0xffu);
+        }
+    }
+}
+
 inline bool g_maps_uploaded[kMaxDevices] = {};
 
 inline int codec_maps_ensure() {
@@ -122,6 +147,11 @@ inline int codec_maps_ensure() {
         build_dmap_lut(u, 1, kDmapLutULog2P, lut_u);
         AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut_s, lut_s, sizeof(lut_s)));
         AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut_u, lut_u, sizeof(lut_u)));
+        static uint32_t lut4_s[2 * kDmapLutEntries], lut4_u[kDmapLutUEntries];
+        build_dmap_lut4(lut_s, 2, kDmapLutLog2P, lut4_s);
+        build_dmap_lut4(lut_u, 1, kDmapLutULog2P, lut4_u);
+        AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut4_s, lut4_s, sizeof(lut4_s)));
+        AETH_CUDA(cudaMemcpyToSymbol(g_dmap_lut4_u, lut4_u, sizeof(lut4_u)));
         g_maps_uploaded[dev] = true;
     }
     return AETH_OK;
@@ -197,35 +227,32 @@ __device__ __forceinline__ uint32_t dmap_encode_lut(const uint2* __restrict__ lu
 // Flag-free bucket encodes for a block whose normalised values are all
 // finite, |xn| <= 1 + 2^-22 (x = xn * (1 / absmax) of a finite absmax): no
 // bucket in that range holds two code changes or needs the search, so the
-// entry's code word carries no flag and the index needs no upper clamp.  A
-// magnitude below 2^-24 is raised to 2^-24: every key of bucket 0 has the
-// code of 0.0 in both maps (their smallest non-zero entries are above
-// 1.6e-7), so the raised key encodes the same.  The bucket index is formed by
-// a multiply-high with a power of two known only at run time (m15 = 2^15:
-// bits >> 17, m16 = 2^16: bits >> 16, m1 = 2: the sign bit), which issues on
-// the FMA pipe rather than as a shift on the integer pipe.  lut_adj is the
-// table's shared address minus 8 x the first bucket's (kDmapLutExpLo << log2 P)
-// index.  `code + 1` never carries out of the byte (a bucket's lower code is
-// below 255 wherever the compare can add one).
-__device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
-    uint2 e;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(e.x), "=r"(e.y) : "r"(addr));
-    return e;
-}
-
-__device__ __forceinline__ uint32_t dmap_enc_fast_s(uint32_t lut_adj, float xn, uint32_t m1, uint32_t m15) {
+// entry carries no flag and the index needs no upper clamp.  A magnitude
+// below 2^-24 is raised to 2^-24: every key of bucket 0 has the code of 0.0 in
+// both maps (their smallest non-zero entries are above 1.6e-7), so the raised
+// key encodes the same.  The tables are the 4-byte ones (build_dmap_lut4):
+// code = below + [key offset >= t], in the low byte of the result (the byte
+// never carries: a bucket whose compare can add one has a code above it).
+// The bucket index is a multiply-high by a power of two known only at run
+// time (m15 = 2^15: bits >> 17, m16 = 2^16: bits >> 16, m1 = 2: the sign bit),
+// which issues on the FMA pipe rather than as a shift on the integer pipe.
+// lut_adj is the table's shared address minus 4 x the first bucket's index
+// (kDmapLutExpLo << log2 P).
+// The compare offset >= t is done as 256 offset + 255 >= t << 8 | below (m8 =
+// 256 at run time: a multiply-add instead of a shift of the entry).
+__device__ __forceinline__ uint32_t dmap_enc4_s(uint32_t lut_adj, float xn, uint32_t m1, uint32_t m8, uint32_t m15) {
     const uint32_t xb = __float_as_uint(xn);
     const uint32_t km = __float_as_uint(fmaxf(fabsf(xn), 0x1p-24f));
     const uint32_t neg = (uint32_t)((int32_t)xb >> 31);
     const uint32_t idx = __umulhi(km, m15) + __umulhi(xb, m1) * (uint32_t)kDmapLutEntries;
-    const uint2 e = lds_u2(lut_adj + idx * 8u);
-    return e.y + ((km ^ neg) >= e.x ? 1u : 0u);
+    const uint32_t e = lds_u32(lut_adj + idx * 4u);
+    return e + (((km ^ neg) & 0x1ffffu) * m8 + 255u >= e ? 1u : 0u);
 }
 
-__device__ __forceinline__ uint32_t dmap_enc_fast_u(uint32_t lut_adj, float xn, uint32_t m16) {
+__device__ __forceinline__ uint32_t dmap_enc4_u(uint32_t lut_adj, float xn, uint32_t m8, uint32_t m16) {
     const uint32_t k = __float_as_uint(fmaxf(xn, 0x1p-24f));
-    const uint2 e = lds_u2(lut_adj + __umulhi(k, m16) * 8u);
-    return e.y + (k >= e.x ? 1u : 0u);
+    const uint32_t e = lds_u32(lut_adj + __umulhi(k, m16) * 4u);
+    return e + ((k & 0xffffu) * m8 + 255u >= e ? 1u : 0u);
 }
 
 // Every float bit pattern through dmap_encode_lut and dmap_encode; counts
@@ -235,13 +262,16 @@ __device__ __forceinline__ uint32_t dmap_enc_fast_u(uint32_t lut_adj, float xn, 
 __global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restrict__ mismatches, uint32_t one) {
     __shared__ float map[256];
     __shared__ uint2 lut[2 * kDmapLutEntries];
+    __shared__ uint32_t lut4[2 * kDmapLutEntries];
     for (int i = threadIdx.x; i < 256; i += blockDim.x) map[i] = is_signed ? c_dmap_signed[i] : c_dmap_unsigned[i];
     static_assert(kDmapLutUEntries <= 2 * kDmapLutEntries, "the unsigned table must fit the signed one's space");
-    for (int i = threadIdx.x; i < (is_signed ? 2 * kDmapLutEntries : kDmapLutUEntries); i += blockDim.x)
+    for (int i = threadIdx.x; i < (is_signed ? 2 * kDmapLutEntries : kDmapLutUEntries); i += blockDim.x) {
         lut[i] = is_signed ? g_dmap_lut_s[i] : g_dmap_lut_u[i];
+        lut4[i] = is_signed ? g_dmap_lut4_s[i] : g_dmap_lut4_u[i];
+    }
     __syncthreads();
-    const uint32_t adj = smem_u32_addr(lut) - (uint32_t)(kDmapLutExpLo << (is_signed ? kDmapLutLog2P : kDmapLutULog2P)) * 8u;
-    const uint32_t m1 = one << 1, m15 = one << 15, m16 = one << 16;
+    const uint32_t adj = smem_u32_addr(lut4) - (uint32_t)(kDmapLutExpLo << (is_signed ? kDmapLutLog2P : kDmapLutULog2P)) * 4u;
+    const uint32_t m1 = one << 1, m8 = one << 8, m15 = one << 15, m16 = one << 16;
     const uint32_t top = __float_as_uint(1.0f) + 2u;  // bits of 1 + 2^-22
     unsigned long long bad = 0;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -251,8 +281,9 @@ __global__ void dmap_selfcheck_kernel(int is_signed, unsigned long long* __restr
         const uint32_t got = is_signed ? dmap_encode_lut<true>(lut, map, x) : dmap_encode_lut<false>(lut, map, x);
         bad += got != want;
         const uint32_t ab = (uint32_t)i & 0x7fffffffu;
-        if (is_signed && ab <= top) bad += dmap_enc_fast_s(adj, x, m1, m15) != want;
-        if (!is_signed && ((uint32_t)i <= top || (uint32_t)i == 0x80000000u)) bad += dmap_enc_fast_u(adj, x, m16) != want;
+        if (is_signed && ab <= top) bad += (dmap_enc4_s(adj, x, m1, m8, m15) & 0xffu) != want;
+        if (!is_signed && ((uint32_t)i <= top || (uint32_t)i == 0x80000000u))
+            bad += (dmap_enc4_u(adj, x, m8, m16) & 0xffu) != want;
     }
     bad = warp_sum_u64(bad);
     if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);

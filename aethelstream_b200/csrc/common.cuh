@@ -145,6 +145,19 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 
 __device__ __forceinline__ uint32_t smem_u32_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// Loads from read-only shared tables at a 32-bit shared address (no memory
+// clobber: use only for tables written before a __syncthreads and never after).
+__device__ __forceinline__ uint32_t lds_u32(uint32_t saddr) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));
+    return v;
+}
+__device__ __forceinline__ float2 lds_f2(uint32_t saddr) {
+    float2 v;
+    asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(saddr));
+    return v;
+}
+
 // prmt.b32 in its default mode: a selector nibble with bit 3 set fills the
 // output byte with the sign of the selected byte.
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
