@@ -149,4 +149,13 @@ void b2_lomo_update(const uint16_t* g, int64_t n, float clip, float beta, float 
 #ifdef __cplusplus
 }
 #endif
+
+/* ---- the galore tests' toy transformer (doublepass_toy.c; test infrastructure) ---- */
+int64_t toy_layer_size(int d, int ff);
+void toy_init_layer(int d, int ff, int layer, float* w);
+void toy_lm_head(int vocab, int d, float* out);
+void toy_inputs(int d, int seq, int batch, float* out);
+void toy_labels(int seq, int batch, int vocab, uint32_t* out);
+float toy_step(int d, int h, int ff, int seq, int bsz, int nl, const float* weights, const float* x_in,
+               const float* lm_head, int vocab, int chunk_size, const uint32_t* labels, float* grads);
 #endif

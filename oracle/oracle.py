@@ -23,14 +23,15 @@ _lib = None
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 _i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 _vp = C.c_void_p
 
 
 def build(force: bool = False) -> str:
     """Compile liboracle.so with the committed Makefile (gcc)."""
-    src = os.path.join(_HERE, "galore_ref.c")
-    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, f) for f in ("galore_ref.c", "doublepass_toy.c", "galore_ref.h")]
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", _HERE, "-B"], check=True)
     return _LIB_PATH
 
@@ -72,6 +73,13 @@ def lib():
             "ref_rsvd_jacobi": (None, [_f32p, C.c_int, _f32p]),
             "ref_randomized_svd": (C.c_int, [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, _f32p, _f32p]),
             "ref_randomized_svd_sketch": (C.c_int, [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p]),
+            "toy_layer_size": (C.c_int64, [C.c_int, C.c_int]),
+            "toy_init_layer": (None, [C.c_int, C.c_int, C.c_int, _f32p]),
+            "toy_lm_head": (None, [C.c_int, C.c_int, _f32p]),
+            "toy_inputs": (None, [C.c_int, C.c_int, C.c_int, _f32p]),
+            "toy_labels": (None, [C.c_int, C.c_int, C.c_int, _u32p]),
+            "toy_step": (C.c_float, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p,
+                                     C.c_int, C.c_int, _u32p, _f32p]),
             "ref_full_adam_apply": (None, [_f32p, _f32p, _f32p, _f32p, C.c_int64, C.c_float, C.c_float, C.c_float,
                                            C.c_float, C.c_float, C.c_int]),
             "b2_dynamic_map": (None, [C.c_int, _f32p]),
@@ -494,3 +502,58 @@ def apply_galore_bf16_update(master, delta, state: int):
     st = C.c_uint64(state & (2**64 - 1))
     lib().dp_apply_galore_bf16_update(m, d, m.size, C.byref(st))
     return m, int(st.value)
+
+
+# ---- the galore tests' toy transformer (doublepass_toy.c) ----
+class ToyModel:
+    """The model galore/tests/common/mod.rs trains (doublepass Model::new with
+    BlockWeights::from_formula_layered), its inputs, labels and LM head, and one
+    step's loss and gradients in the reference's f32 arithmetic."""
+
+    NAMES = ("d_rms1_w", "d_wq", "d_wk", "d_wv", "d_wo", "d_rms2_w", "d_wg", "d_wu", "d_wd")
+
+    def __init__(self, d, n_heads, d_ff, seq_len=4, batch=1, n_layers=2, vocab=64, chunk_size=256):
+        self.d, self.h, self.ff, self.s, self.b, self.nl, self.vocab, self.chunk = (d, n_heads, d_ff, seq_len, batch,
+                                                                                 n_layers, vocab, chunk_size)
+        self.lf = int(lib().toy_layer_size(d, d_ff))
+        self.w = np.empty(self.nl * self.lf, np.float32)
+        for li in range(self.nl):
+            blk = np.empty(self.lf, np.float32)
+            lib().toy_init_layer(d, d_ff, li, blk)
+            self.w[li * self.lf:(li + 1) * self.lf] = blk
+        self.lm = np.empty(vocab * d, np.float32)
+        lib().toy_lm_head(vocab, d, self.lm)
+        self.x = np.empty(seq_len * batch * d, np.float32)
+        lib().toy_inputs(d, seq_len, batch, self.x)
+        self.labels = np.empty(seq_len * batch, np.uint32)
+        lib().toy_labels(seq_len, batch, vocab, self.labels)
+        d_, ff = d, d_ff
+        self.shapes = [(1, d_), (d_, d_), (d_, d_), (d_, d_), (d_, d_), (1, d_), (ff, d_), (ff, d_), (d_, ff)]
+
+    def param_specs(self):
+        """(layer, name, m, n) in the order of galore/tests/common/mod.rs:73-89."""
+        return [(li, nm, m, n) for li in range(self.nl) for nm, (m, n) in zip(self.NAMES, self.shapes)]
+
+    def _slot(self, li, name):
+        off = li * self.lf
+        for nm, (m, n) in zip(self.NAMES, self.shapes):
+            if nm == name:
+                return off, m * n
+            off += m * n
+        raise KeyError(name)
+
+    def step(self):
+        """(loss, {(layer, name): gradient m x n})."""
+        g = np.empty_like(self.w)
+        loss = lib().toy_step(self.d, self.h, self.ff, self.s, self.b, self.nl, self.w, self.x, self.lm, self.vocab,
+                              self.chunk, self.labels, g)
+        out = {}
+        for li, nm, m, n in self.param_specs():
+            off, cnt = self._slot(li, nm)
+            out[(li, nm)] = g[off:off + cnt].reshape(m, n)
+        return float(np.float32(loss)), out
+
+    def apply_delta(self, li, name, delta):
+        """apply_weight_delta (common/mod.rs:106-111): w -= delta, f32."""
+        off, cnt = self._slot(li, name)
+        self.w[off:off + cnt] -= np.asarray(delta, np.float32).ravel()
