@@ -23,7 +23,8 @@ One part of the reference's behaviour depends on its process: the refresh
 the rest.  `refresh_order` states which keys a run reached before its first
 failure; the tests name, per recorded run, the set identified from its curve.
 
-The model's losses and gradients come from oracle.ToyModel (doublepass_toy.c).
+RefStandardAdamW restates the full-rank baseline the same run records.  The
+model's losses and gradients come from oracle.ToyModel (doublepass_toy.c).
 """
 from __future__ import annotations
 
@@ -100,6 +101,42 @@ class RefGaLoreOptimizer:
                       sv=np.float32(1.0))
 
 
+class RefStandardAdamW:
+    """StandardAdamW (galore/src/standard_adamw.rs:17-140), the full-rank
+    baseline of the theorem-3.8 run: full-gradient accumulator, global clip,
+    m = b1 m + (1-b1) g, v = b2 v + (1-b2) g g, delta = lr m / (sqrt(v) + eps)
+    with no bias correction (oracle ref_full_adam_apply with step 0)."""
+
+    def __init__(self, specs, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8):
+        self.hp = (beta1, beta2, eps, lr)
+        self.p = {(li, nm): dict(m=np.zeros(m * n, np.float32), v=np.zeros(m * n, np.float32),
+                                 acc=np.zeros(m * n, np.float32)) for (li, nm, m, n) in specs}
+        self.deltas = {}
+
+    def project_and_accumulate(self, grad, key):
+        ps = self.p[key]
+        ps["acc"] = (ps["acc"] + np.asarray(grad, np.float32).ravel()).astype(np.float32)
+
+    def lowrank_grad_sqnorm(self, key):
+        return O.sqnorm_f64(self.p[key]["acc"])
+
+    def apply_update(self, key, clip):
+        ps = self.p[key]
+        b1, b2, eps, lr = self.hp
+        zero = np.zeros_like(ps["acc"])  # param 0 - delta = -delta exactly
+        neg, ps["m"], ps["v"] = O.full_adam_apply(zero, ps["acc"], ps["m"], ps["v"], clip, b1, b2, eps, lr, 0)
+        self.deltas[key] = -neg
+
+    def zero_accum(self, key):
+        self.p[key]["acc"][:] = 0.0
+
+    def take_weight_delta(self, key):
+        return self.deltas.pop(key, None)
+
+    def notify_step(self, step):
+        pass
+
+
 def global_clip(sqnorms, max_norm=1.0):
     """hook.rs:141-186: f64 sum in spec order, clip = min(f32(max / (norm + 1e-6)), 1)."""
     gsq = 0.0
@@ -135,6 +172,7 @@ def train(model, opt, steps, max_norm=1.0):
 # failing job (identified from the curves: the runs whose first job failed
 # refreshed nothing).
 RECORDED_RUNS = {
+    "theorem_38/adamw": dict(kind="adamw", model=(64, 4, 256), lr=2e-4),
     "theorem_38/galore_periodic_200": dict(model=(64, 4, 256), layer_ranks=(32, 40, 32, 8), switch_interval=200,
                                            lr=2e-4, scale_lr_by_rank=False, refresh_order=((0, "d_rms1_w"),)),
     "theorem_38/galore_constant": dict(model=(64, 4, 256), layer_ranks=(32, 40, 32, 8), switch_interval=0, lr=2e-4,
@@ -151,6 +189,9 @@ def run_recorded(name, steps):
     """The oracle's losses for one recorded run of the reference's suite."""
     cfg = RECORDED_RUNS[name]
     model = O.ToyModel(*cfg["model"])
+    if cfg.get("kind") == "adamw":
+        opt = RefStandardAdamW(model.param_specs(), lr=cfg["lr"])
+        return train(model, opt, steps), opt
     opt = RefGaLoreOptimizer(model.param_specs(), layer_ranks=cfg["layer_ranks"],
                              switch_interval=cfg["switch_interval"], lr=cfg["lr"],
                              scale_lr_by_rank=cfg["scale_lr_by_rank"], refresh_order=cfg["refresh_order"])

@@ -14,7 +14,8 @@ The runs here are the three recorded runs whose subspace refresh reached no
 matrix (their first refresh job failed; tests/test_oracle_reference_curves.py),
 so the library's refresh is off.  The losses equal the oracle's restatement of
 the same run bit for bit over all 32 recorded steps, and the recorded losses
-bit for bit over the steps where the oracle does.
+bit for bit over the steps where the oracle does.  The run's full-rank AdamW
+baseline goes through doublepass_galore_apply the same way.
 """
 import json
 import os
@@ -24,13 +25,19 @@ import pytest
 
 from oracle import oracle as O
 from oracle.galore_optimizer import RECORDED_RUNS, global_clip, run_recorded
-from tests._gpu import dev, host
+from tests._gpu import dev, host, ptr
 from tests.test_oracle_reference_curves import AGREEMENT
 
 pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 STEPS = 32
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from aethelstream_b200 import _lib
+    return _lib.load()
 
 
 @pytest.fixture(scope="module")
@@ -72,3 +79,36 @@ def test_ref_mode_reproduces_the_recorded_run(curves, run):
     assert np.array_equal(losses, oracle_losses), np.flatnonzero(losses != oracle_losses)
     exact = AGREEMENT[run][0]
     assert np.array_equal(losses[:exact], curves[run][:exact])
+
+
+def test_full_rank_adam_reproduces_the_recorded_baseline(curves, lib):
+    """The theorem-3.8 run's AdamW baseline with every update by the library's
+    doublepass_galore_apply (step 0: StandardAdamW's update without bias
+    correction) on device-resident weights and moments."""
+    import torch
+    cfg = RECORDED_RUNS["theorem_38/adamw"]
+    model = O.ToyModel(*cfg["model"])
+    specs = model.param_specs()
+    state = {(li, nm): [torch.zeros(m * n, dtype=torch.float32, device="cuda:0") for _ in range(3)]
+             for (li, nm, m, n) in specs}  # m, v, full-gradient accumulator
+    losses = []
+    for s in range(STEPS):
+        loss, grads = model.step()
+        for li in reversed(range(model.nl)):
+            for name in model.NAMES:
+                state[(li, name)][2] += dev(grads[(li, name)].ravel())
+        clip = global_clip([O.sqnorm_f64(host(state[(li, nm)][2])) for (li, nm, _, _) in specs])
+        for (li, nm, m, n) in specs:
+            mm, vv, acc = state[(li, nm)]
+            w = torch.zeros(m * n, dtype=torch.float32, device="cuda:0")  # 0 - delta = -delta exactly
+            lib.doublepass_galore_apply(ptr(w), ptr(acc), ptr(mm), ptr(vv), float(clip), 0.9, 0.999, 1e-8, cfg["lr"],
+                                        m * n, 0)
+            assert lib.aeth_last_error() == 0
+            model.apply_delta(li, nm, -host(w))
+            acc.zero_()
+        losses.append(np.float32(loss))
+    losses = np.array(losses, np.float32)
+    oracle_losses, _ = run_recorded("theorem_38/adamw", STEPS)
+    assert np.array_equal(losses, oracle_losses), np.flatnonzero(losses != oracle_losses)
+    exact = AGREEMENT["theorem_38/adamw"][0]
+    assert np.array_equal(losses[:exact], curves["theorem_38/adamw"][:exact])
