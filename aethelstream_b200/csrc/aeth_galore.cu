@@ -2417,7 +2417,7 @@ int aeth_lomo_update(const void* grad_bf16, int64_t n, const double* sq_dev, flo
     const int grid = (int)std::min<int64_t>((nb + kLomoGroups - 1) / kLomoGroups,
                                             (int64_t)num_sms() * std::max(per_sm, 1));
     kern<<<grid, kLomoThreads, kLomoSmem, to_stream(stream)>>>(gb, n, sq_dev, max_norm, lr, beta, mom8, mom_scales,
-                                                               w_packed, w_absmax, prequant_out);
+                                                               w_packed, w_absmax, prequant_out, 1u);
     AETH_LAUNCH_CHECK();
     return AETH_OK;
 }

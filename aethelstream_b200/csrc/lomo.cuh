@@ -48,15 +48,16 @@ __global__ void __launch_bounds__(256) lomo_sqnorm_kernel(const uint16_t* __rest
 // at 128 + 4 lane -- so one byte permute forms either offset from the packed
 // code word and the lane (nf4_dequant_word_s), and no lookup of a warp meets a
 // bank conflict whatever the codes.  bucket32: the 29-bucket classifier of the
-// fused apply epilogue (requant); dm and dlut: the signed map and its bucket
-// table (dm only for the rare binary search).
+// fused apply epilogue (requant); dm and dlut4: the signed map (for the rare
+// binary search) and its 4-byte bucket table (the flag-free encode of finite
+// blocks, dmap_enc4_s).
 constexpr int kLomoGroups = 5;  // independent 128-thread groups per CTA
 constexpr int kLomoThreads = 128 * kLomoGroups;
 struct LomoTables {
     uint8_t rep[256 * 256];
     uint32_t bucket32[32];
     float dm[256];
-    uint2 dlut[2 * kDmapLutEntries];
+    uint32_t dlut4[2 * kDmapLutEntries];
 };
 constexpr int kLomoSmem = (int)sizeof(LomoTables);
 
@@ -73,10 +74,11 @@ template <int CODEC>
 __global__ void __launch_bounds__(kLomoThreads, 1)
     lomo_update_kernel(const uint16_t* __restrict__ g, int64_t n, const double* __restrict__ sq, float max_norm,
                        float lr, float beta, int8_t* __restrict__ mom8, float* __restrict__ mom_scales,
-                       uint8_t* __restrict__ wp, float* __restrict__ wa, float* __restrict__ prequant) {
+                       uint8_t* __restrict__ wp, float* __restrict__ wa, float* __restrict__ prequant, uint32_t one) {
     extern __shared__ __align__(16) uint8_t lomo_smem[];
     LomoTables& tab = *reinterpret_cast<LomoTables*>(lomo_smem);
-    __shared__ float red[kLomoGroups][2][4];
+    __shared__ uint32_t red[kLomoGroups][2][4];  // NaN-propagating momentum maxima (bits), by block parity
+    __shared__ uint32_t red2[kLomoGroups][4];    // NaN-ignoring maxima of a block holding NaN or inf
     for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
         const int b = i >> 4;
         *reinterpret_cast<float2*>(tab.rep + b * 256 + (i & 15) * 8) =
@@ -86,7 +88,7 @@ __global__ void __launch_bounds__(kLomoThreads, 1)
         for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x)
             *reinterpret_cast<float*>(tab.rep + (i >> 5) * 256 + 128 + (i & 31) * 4) = c_dmap_signed[i >> 5];
         for (int i = threadIdx.x; i < 256; i += blockDim.x) tab.dm[i] = c_dmap_signed[i];
-        for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) tab.dlut[i] = g_dmap_lut_s[i];
+        for (int i = threadIdx.x; i < 2 * kDmapLutEntries; i += blockDim.x) tab.dlut4[i] = g_dmap_lut4_s[i];
     }
     for (int b = threadIdx.x; b < 32; b += blockDim.x) tab.bucket32[b] = nf4_bucket32_entry(b);
     __syncthreads();
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(kLomoThreads, 1)
             mo[k + 1] = mm.y;
             w[k] = ww.x;
             w[k + 1] = ww.y;
-            am = fmax3(am, fabsf(mm.x), fabsf(mm.y));
+            am = fmax3_nan(am, fabsf(mm.x), fabsf(mm.y));
             aw = fmax3_nan(aw, fabsf(ww.x), fabsf(ww.y));
         }
         // NF4 block absmax over the 4 threads of the block (NaN-propagating, as the reference's max)
@@ -185,12 +187,25 @@ __global__ void __launch_bounds__(kLomoThreads, 1)
             for (int k = 0; k < 16; k += 4)
                 *reinterpret_cast<float4*>(prequant + e0 + k) = make_float4(w[k], w[k + 1], w[k + 2], w[k + 3]);
         }
-        // momentum block absmax over the group (double-buffered slots: one barrier per block)
-        am = warp_max_nonneg(am);  // fmax3 from 0 ignores NaN: am >= 0 and not NaN
-        float* rs = red[group][it & 1];
-        if (lane == 0) rs[warp] = am;
+        // momentum block maxima over the group, NaN-propagating (canonical NaN orders
+        // above +inf as unsigned bits; double-buffered slots: one barrier per block)
+        const uint32_t amb = __reduce_max_sync(0xffffffffu, __float_as_uint(am));
+        uint32_t* rs = red[group][it & 1];
+        if (lane == 0) rs[warp] = amb;
         asm volatile("bar.sync %0, 128;" ::"r"(1 + group) : "memory");
-        const float bm = fmax3(fmaxf(rs[0], rs[1]), rs[2], rs[3]);
+        const uint32_t bmb = max(max(rs[0], rs[1]), max(rs[2], rs[3]));
+        float bm = __uint_as_float(bmb);
+        // finite and 0 or normal: every normalised value lies within 1 + 2^-23 (group-uniform)
+        const bool finite = bmb < 0x7f800000u && (bmb == 0u || bmb >= 0x00800000u);
+        if (!finite) {  // rare: the maximum again, ignoring NaN, as the reference's max does
+            float a2 = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 16; k += 2) a2 = fmax3(a2, fabsf(mo[k]), fabsf(mo[k + 1]));
+            a2 = warp_max_nonneg(a2);
+            if (lane == 0) red2[group][warp] = __float_as_uint(a2);
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + group) : "memory");
+            bm = __uint_as_float(max(max(red2[group][0], red2[group][1]), max(red2[group][2], red2[group][3])));
+        }
         uint32_t out[4] = {0u, 0u, 0u, 0u};
         if (CODEC == AETH_CODEC_BLOCK_LINEAR) {
             const float nsm = lin_scale_from_absmax(bm), linv = lin_inv(nsm);
@@ -199,19 +214,22 @@ __global__ void __launch_bounds__(kLomoThreads, 1)
             if (tid == 0) mom_scales[b] = nsm;
         } else {
             const float dinv = dyn_inv(bm);
-            const float2 dinv2 = make_float2(dinv, dinv);
-            uint32_t ef = 0;
+            if (finite) {
+                const float2 dinv2 = make_float2(dinv, dinv);
+                const uint32_t m1 = one << 1, m8 = one << 8, m15 = one << 15;
+                const uint32_t lut_adj = smem_u32_addr(tab.dlut4) - (uint32_t)(kDmapLutExpLo << kDmapLutLog2P) * 4u;
+                uint32_t hp[8];  // codes of element pairs in bytes 0 and 1
 #pragma unroll
-            for (int k = 0; k < 16; k += 2) {
-                const float2 x2 = mul2_rn(make_float2(mo[k], mo[k + 1]), dinv2);
-                out[k >> 2] |= (dmap_encode_lut_flag<true>(tab.dlut, x2.x, ef) |
-                                (dmap_encode_lut_flag<true>(tab.dlut, x2.y, ef) << 8))
-                               << (8 * (k & 3));
-            }
-            if (ef > 0xffu) {  // rare: a bucket that needs the search; redo this thread's 16 codes
-                out[0] = out[1] = out[2] = out[3] = 0u;
+                for (int k = 0; k < 16; k += 2) {
+                    const float2 x2 = mul2_rn(make_float2(mo[k], mo[k + 1]), dinv2);
+                    hp[k >> 1] = prmt(dmap_enc4_s(lut_adj, x2.x, m1, m8, m15), dmap_enc4_s(lut_adj, x2.y, m1, m8, m15),
+                                      0x3340u);
+                }
 #pragma unroll
-                for (int k = 0; k < 16; ++k)  // the same normalised values, formed again
+                for (int w4 = 0; w4 < 4; ++w4) out[w4] = prmt(hp[2 * w4], hp[2 * w4 + 1], 0x5410u);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
                     out[k >> 2] |= dmap_encode_rare(tab.dm, __fmul_rn(mo[k], dinv)) << (8 * (k & 3));
             }
             if (tid == 0) mom_scales[b] = bm;
