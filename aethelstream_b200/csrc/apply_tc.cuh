@@ -101,13 +101,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[N]) {
     for (int i = 0; i < 16; ++i) v[OFF + i] = __uint_as_float(r[i]);
 }
 
-template <int STAGES, bool PAIR>
+// DECAY: some problem of the launch has a decoupled decay (each problem's
+// has_decay still selects it); OUT: some problem writes the fp32 delta or the
+// pre-quantisation weights.  Launches with neither (the usual case) carry no
+// per-element test or predicated-off store for them.
+template <int STAGES, bool PAIR, bool DECAY = false, bool OUT = false>
 __global__ void __launch_bounds__(kApplyThreads, 1)
     apply_grouped_kernel(const __grid_constant__ ApplyArgs args, uint32_t* err) {
     using L = ApplyLayout<STAGES, PAIR>;
     constexpr int kEpiThreads = 32 * kApplyEpiWarps;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // an offset from the shared array (not an integer round trip), so every
+    // pointer below stays known to be shared: ld/st.shared, not generic accesses
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = base;
     uint8_t* sB = base + STAGES * L::kA;
     uint8_t* wslot = base + STAGES * L::kStage;  // kApplyWSlots x (packed tile, scale tile)
@@ -259,8 +265,13 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
                 const float amax_old = *sp;
                 const uint32_t tcol = tcol0 + (uint32_t)(b * kApplyBN);
                 const int64_t grow = (int64_t)(m0 + row);
-                float* dout = (pr.delta_out && grow < pr.m) ? pr.delta_out + grow * pr.n + n0 + cl : nullptr;
-                float* pout = (pr.prequant_out && grow < pr.m) ? pr.prequant_out + grow * pr.n + n0 + cl : nullptr;
+                float* dout = nullptr;
+                float* pout = nullptr;
+                if constexpr (OUT) {
+                    if (pr.delta_out && grow < pr.m) dout = pr.delta_out + grow * pr.n + n0 + cl;
+                    if (pr.prequant_out && grow < pr.m) pout = pr.prequant_out + grow * pr.n + n0 + cl;
+                }
+                const bool decay = DECAY && pr.has_decay;
                 // pass 1: w = CODES * absmax_old - fl(lr * dW) [* decay] -> TMEM; block absmax.
                 // The next chunk's TMEM load is in flight while this chunk is updated.
                 float amax = 0.0f;
@@ -287,20 +298,20 @@ __global__ void __launch_bounds__(kApplyThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 16; i += 2) {
                         float2 ww = fma2_rn(make_float2(v[i], v[i + 1]), nlr2, make_float2(w[i], w[i + 1]));
-                        if (pr.has_decay) ww = mul2_rn(ww, dmul2);
+                        if (DECAY && decay) ww = mul2_rn(ww, dmul2);
                         w[i] = ww.x;
                         w[i + 1] = ww.y;
                         amax = fmax3_nan(amax, fabsf(ww.x), fabsf(ww.y));  // NaN-propagating, as torch's max
                     }
                     tmem_st16(tcol + (uint32_t)(c * 16), w);
-                    if (dout) {  // take_weight_delta: fl(lr * dW)
+                    if (OUT && dout) {  // take_weight_delta: fl(lr * dW)
 #pragma unroll
                         for (int i = 0; i < 16; i += 4)
                             *reinterpret_cast<float4*>(dout + c * 16 + i) =
                                 make_float4(__fmul_rn(v[i], pr.lr), __fmul_rn(v[i + 1], pr.lr),
                                             __fmul_rn(v[i + 2], pr.lr), __fmul_rn(v[i + 3], pr.lr));
                     }
-                    if (pout) {
+                    if (OUT && pout) {
 #pragma unroll
                         for (int i = 0; i < 16; i += 4)
                             *reinterpret_cast<float4*>(pout + c * 16 + i) = make_float4(w[i], w[i + 1], w[i + 2], w[i + 3]);

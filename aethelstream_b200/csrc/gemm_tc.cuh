@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(192, 1)
                    int K, uint32_t idesc, Epi epi, uint32_t* err) {
     using L = TcLayout<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
     uint8_t* sA = base;
     uint8_t* sB = base + STAGES * L::kABytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(base + L::kOperandBytes);

@@ -512,6 +512,43 @@ inline bool apply_use_pair() {
     return on;
 }
 
+// One launch of the specialisation for the group's decay and output flags.
+template <int STAGES, bool PAIR, bool DECAY, bool OUT>
+int apply_kernel_launch(const ApplyArgs& a, int units, uint32_t* err_word, cudaStream_t st) {
+    using L = ApplyLayout<STAGES, PAIR>;
+    const int smem = 1024 + L::kTotal;
+    auto kern = apply_grouped_kernel<STAGES, PAIR, DECAY, OUT>;
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    AETH_TRY(current_device(&dev));
+    if (!attr_set[dev]) {
+        AETH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr_set[dev] = true;
+    }
+    if (PAIR) {
+        // one cluster of two CTAs per pair unit, at most a CTA per SM
+        const int grid = 2 * std::min(num_sms() / 2, units);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kApplyThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        AETH_CUDA(cudaLaunchKernelEx(&cfg, kern, a, err_word));
+    } else {
+        const int grid = std::min(num_sms(), units);
+        kern<<<grid, kApplyThreads, smem, st>>>(a, err_word);
+        AETH_LAUNCH_CHECK();
+    }
+    return AETH_OK;
+}
+
 template <int STAGES, bool PAIR>
 int apply_grouped_launch_t(const ApplyJob* jobs, int nj, int r, cudaStream_t st) {
     using L = ApplyLayout<STAGES, PAIR>;
@@ -554,36 +591,17 @@ int apply_grouped_launch_t(const ApplyJob* jobs, int nj, int r, cudaStream_t st)
             units += ((j.m + rows_per_unit - 1) / rows_per_unit) * p.n_tiles;
         }
         a.total_units = units;
-        const int smem = 1024 + L::kTotal;
-        auto kern = apply_grouped_kernel<STAGES, PAIR>;
-        static bool attr_set[kMaxDevices] = {};
-        int dev = 0;
-        AETH_TRY(current_device(&dev));
-        if (!attr_set[dev]) {
-            AETH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            attr_set[dev] = true;
+        bool decay = false, out = false;
+        for (int i = 0; i < cnt; ++i) {
+            decay = decay || a.p[i].has_decay;
+            out = out || a.p[i].prequant_out || a.p[i].delta_out;
         }
-        if (PAIR) {
-            // one cluster of two CTAs per pair unit, at most a CTA per SM
-            const int grid = 2 * std::min(num_sms() / 2, units);
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(grid);
-            cfg.blockDim = dim3(kApplyThreads);
-            cfg.dynamicSmemBytes = smem;
-            cfg.stream = st;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = 2;
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            AETH_CUDA(cudaLaunchKernelEx(&cfg, kern, a, rt->err_word));
-        } else {
-            const int grid = std::min(num_sms(), units);
-            kern<<<grid, kApplyThreads, smem, st>>>(a, rt->err_word);
-            AETH_LAUNCH_CHECK();
-        }
+        int st_launch;
+        if (decay) st_launch = out ? apply_kernel_launch<STAGES, PAIR, true, true>(a, units, rt->err_word, st)
+                                   : apply_kernel_launch<STAGES, PAIR, true, false>(a, units, rt->err_word, st);
+        else st_launch = out ? apply_kernel_launch<STAGES, PAIR, false, true>(a, units, rt->err_word, st)
+                             : apply_kernel_launch<STAGES, PAIR, false, false>(a, units, rt->err_word, st);
+        AETH_TRY(st_launch);
     }
     return AETH_OK;
 }

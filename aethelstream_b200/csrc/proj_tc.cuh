@@ -65,7 +65,7 @@ template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1) proj_grouped_kernel(const __grid_constant__ ProjArgs args, uint32_t* err) {
     using L = ProjLayout<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
     uint8_t* sA = base;
     uint8_t* sB = base + STAGES * L::kA;
     uint8_t* staging = base + STAGES * L::kStage;
@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(192, 1) proj_pair_kernel(const __grid_constant
     using L = ProjPairLayout<RT, STAGES>;
     constexpr int NB = L::kAccBufs;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
     uint8_t* sA = base;
     uint8_t* sB = base + STAGES * L::kA;
     uint8_t* staging = base + STAGES * L::kStage;

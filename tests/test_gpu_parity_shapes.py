@@ -32,7 +32,7 @@ def _opt(mode, specs, **kw):
 
 
 def _check_b200_param(oracle, opt, li, name, m, n, r, g_exact, acc_gpu, clip, wp0, wa0, pre, W, lr=1e-3,
-                      codec="dynamic"):
+                      codec="dynamic", wd=0.0):
     """One parameter after one step from zero state: projection, INT8 state,
     weight update and requantisation against the oracle."""
     right = m >= n
@@ -49,7 +49,7 @@ def _check_b200_param(oracle, opt, li, name, m, n, r, g_exact, acc_gpu, clip, wp
     gm8, gv8, gms, gvs = opt.get_state(li, name)
     assert np.array_equal(host(gm8), m8) and np.array_equal(host(gv8), v8), name
     assert np.array_equal(host(gms), ms) and np.array_equal(host(gvs), vs), name
-    _, _, pre_ref, _ = oracle.b2_apply_weight(n_ref, proj, m, n, r, wp0, wa0, lr)
+    _, _, pre_ref, _ = oracle.b2_apply_weight(n_ref, proj, m, n, r, wp0, wa0, lr, wd)
     w_old = oracle.nf4_dequant_f32(wp0, wa0, m * n)
     pre_h = host(pre).ravel()
     assert rel_fro(pre_h - w_old, pre_ref - w_old) < 1e-5, (name, rel_fro(pre_h - w_old, pre_ref - w_old))
@@ -115,6 +115,37 @@ def test_large_shapes_against_oracle(oracle, m, n, r):
     opt.apply_update(1, "d_wg", clip, weight=W, prequant_out=pre)
     _check_b200_param(oracle, opt, 1, "d_wg", m, n, r, g, acc, clip, wp0, wa0, pre, W)
     opt.close()
+
+
+@pytest.mark.parametrize("wd", [0.0, 0.1])
+def test_apply_specialisations_and_decay(oracle, wd):
+    """The back-projection kernel is compiled per launch for the decoupled
+    decay (adamw.rs:194-202) and for the optional fp32 outputs.  With
+    prequant_out the update is checked against the oracle (decay included);
+    the launch without it -- the one the streamed step runs -- must write the
+    same NF4 codes and scales from the same state."""
+    from aethelstream_b200 import AdamWConfig, nf4_quantize
+    m, n, r = 1024, 8192, 512
+    rng = np.random.default_rng(int(wd * 10) + 77)
+    w0 = rng.standard_normal((m, n), dtype=np.float32) * np.float32(0.02)
+    g = oracle.bf16_round(rng.standard_normal((m, n), dtype=np.float32) * np.float32(1e-3))
+    out = []
+    for with_pre in (True, False):
+        opt = _opt("b200", [(1, "d_wq", m, n, r)], state_codec="dynamic", adam=AdamWConfig(weight_decay=wd))
+        W = nf4_quantize(dev(w0))
+        wp0, wa0 = host(W.packed), host(W.absmax)
+        opt.project_and_accumulate(dev(g).to(torch.bfloat16), 1, "d_wq")
+        acc = host(opt.get_accum(1, "d_wq"))
+        clip = float(oracle.clip_coeff(opt.lowrank_grad_sqnorm(1, "d_wq"), 1.0))
+        if with_pre:
+            pre = torch.empty(m, n, dtype=torch.float32, device=DEV)
+            opt.apply_update(1, "d_wq", clip, weight=W, prequant_out=pre)
+            _check_b200_param(oracle, opt, 1, "d_wq", m, n, r, g, acc, clip, wp0, wa0, pre, W, wd=wd)
+        else:
+            opt.apply_update(1, "d_wq", clip, weight=W)
+        out.append((host(W.packed), host(W.absmax).view(np.uint32)))
+        opt.close()
+    assert np.array_equal(out[0][0], out[1][0]) and np.array_equal(out[0][1], out[1][1])
 
 
 LAYER = [("d_rms1_w", 1, 256), ("d_wq", 256, 256), ("d_wk", 128, 256), ("d_wv", 128, 256), ("d_wo", 256, 256),
