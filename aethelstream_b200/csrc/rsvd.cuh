@@ -351,6 +351,25 @@ __device__ __forceinline__ void chol_store_panel(double* __restrict__ a, const d
     }
 }
 
+// The panel rows k0 .. l-1, columns k0 .. k0+kw-1 (lower triangle of the
+// diagonal block, zeros elsewhere) into shared memory, as asynchronous 8-byte
+// copies (zero-filled outside the triangle): a thread's copies are all in
+// flight at once instead of one L2 round trip per element, and they hold no
+// registers.  The caller waits with cp_async_wait_all() and a barrier.
+__device__ __forceinline__ void chol_load_panel(double* __restrict__ pan, const double* __restrict__ a, int l, int k0,
+                                                int kw, int prow) {
+    const int n = prow * 32;
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        const int i = t >> 5, c = t & 31;
+        const bool in = c < kw && c <= i;
+        const double* src = a + (int64_t)(k0 + (in ? i : 0)) * l + k0 + (in ? c : 0);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32_addr(pan + i * 33 + c)), "l"(src),
+                     "r"(in ? 8 : 0)
+                     : "memory");
+    }
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __restrict__ a, int l,
                                                                     double* __restrict__ linv, int* __restrict__ fail) {
     extern __shared__ double pan[];  // (l - k0) x 33
@@ -369,10 +388,8 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
             chol_store_panel(a, pan, l, k0 - 32, 32);
             __syncthreads();
         }
-        for (int t = tid; t < prow * 32; t += blockDim.x) {
-            const int i = t >> 5, c = t & 31;
-            pan[i * 33 + c] = (c < kw && c <= i) ? a[(int64_t)(k0 + i) * l + k0 + c] : 0.0;
-        }
+        chol_load_panel(pan, a, l, k0, kw, prow);
+        cp_async_wait_all();
         __syncthreads();
         if (warp == 0) {
             // the diagonal block in registers, lane = row: column c's pivot comes
@@ -474,10 +491,17 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
             const int d0 = db * 32, dw = min(32, l - d0);
             double* ld = pan + warp * (2 * 32 * 33);
             double* xc = ld + 32 * 33;
-            for (int t = lane; t < 32 * 32; t += 32) {
-                const int i = t >> 5, j = t & 31;
-                ld[i * 33 + j] = (i < dw && j <= i) ? a[(int64_t)(d0 + i) * l + d0 + j] : (i == j ? 1.0 : 0.0);
+            // asynchronous copies, zero-filled outside the block's lower
+            // triangle; rows past the matrix get a unit diagonal afterwards
+            for (int i = 0; i < 32; ++i) {
+                const bool in = i < dw && lane <= i;
+                const double* src = a + (int64_t)(d0 + (in ? i : 0)) * l + d0 + (in ? lane : 0);
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32_addr(ld + i * 33 + lane)),
+                             "l"(src), "r"(in ? 8 : 0)
+                             : "memory");
             }
+            cp_async_wait_all();
+            if (lane >= dw) ld[lane * 33 + lane] = 1.0;
             __syncwarp();
             for (int i = 0; i < 32; ++i) {
                 double v = (i == lane) ? 1.0 : 0.0;
@@ -506,14 +530,19 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
     for (int ib = 1; ib < nb; ++ib) {
         const int i0 = ib * 32, iw = min(32, l - i0);
         // columns 0 .. i0 - 1 of the block row (i0 < l < pitch)
-        for (int t = tid; t < 32 * i0; t += blockDim.x) {
-            const int r = t / i0, k = t % i0;
-            pan[r * pitch + k] = r < iw ? a[(int64_t)(i0 + r) * l + k] : 0.0;
+        // (a warp per row; asynchronous copies, zero rows past the matrix)
+        for (int r = warp; r < 32; r += nwarps) {
+            const double* src = a + (int64_t)(i0 + (r < iw ? r : 0)) * l;
+            for (int k = lane; k < i0; k += 32)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32_addr(pan + r * pitch + k)),
+                             "l"(src + k), "r"(r < iw ? 8 : 0)
+                             : "memory");
         }
         for (int t = tid; t < 32 * 32; t += blockDim.x) {
             const int r = t >> 5, c = t & 31;
             dinv_s[r * 33 + c] = (r < iw && c < iw) ? linv[(int64_t)(i0 + r) * l + i0 + c] : 0.0;
         }
+        cp_async_wait_all();
         __syncthreads();
         const double* lrow = pan + lane * pitch;
         for (int piece = gw; piece < ib * 8; piece += gwarps) {
