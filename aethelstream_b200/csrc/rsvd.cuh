@@ -405,9 +405,15 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
                     const double d = __shfl_sync(0xffffffffu, r[c], c);
                     const bool ok = d > 0.0;
                     okall = okall && ok;
-                    const double piv = ok ? sqrt(d) : 1.0;
-                    if (lane == c) r[c] = piv;
-                    else if (lane > c) r[c] = r[c] / piv;
+                    // 1 / pivot from rsqrt (no square root and no division on the
+                    // chain from one pivot to the next); the solve below reuses it
+                    const double ip = ok ? rsqrt(d) : 1.0;
+                    if (lane == c) {
+                        r[c] = ok ? d * ip : 1.0;
+                        rdiag[c] = ip;
+                    } else if (lane > c) {
+                        r[c] = r[c] * ip;
+                    }
 #pragma unroll
                     for (int j = c + 1; j < 32; ++j) {
                         const double ljc = __shfl_sync(0xffffffffu, r[c], j);
@@ -424,9 +430,8 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
         __syncthreads();
         if (bad) break;  // the same step in every CTA
         // the panel below the diagonal block: row i solves x L_kk^T = a_i
-        // (one reciprocal per pivot instead of a division per element)
-        if (tid < 32) rdiag[tid] = tid < kw ? 1.0 / pan[tid * 33 + tid] : 0.0;
-        __syncthreads();
+        // (the pivots' reciprocals from the factorisation above instead of a
+        // division per element)
         for (int i = kw + tid; i < prow; i += blockDim.x) {
             double x[32];
 #pragma unroll
@@ -454,24 +459,25 @@ __global__ void __launch_bounds__(kCholThreads) chol_cluster_kernel(double* __re
             while ((bi + 1) * (bi + 2) / 2 <= p) ++bi;
             while (bi * (bi + 1) / 2 > p) --bi;
             const int bj = p - bi * (bi + 1) / 2;
-            const int gi = (kb + 1 + bi) * 32 + lane, gj0 = (kb + 1 + bj) * 32;
+            // lane = column gj of the block, acc[i] = row gi0 + i: the global
+            // read-modify-write of each row is one coalesced 256-byte access
+            const int gi0 = (kb + 1 + bi) * 32, gj = (kb + 1 + bj) * 32 + lane;
             double acc[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] = 0.0;
-            if (gi < l) {
+            for (int i = 0; i < 32; ++i) acc[i] = 0.0;
+            const int ni = min(32, l - gi0);  // rows of the block inside the matrix (warp-uniform)
+            if (gj < l) {
+                const double* prow = pan + (gi0 - k0) * 33;
                 for (int t = 0; t < kw; ++t) {
-                    const double li = pan[(gi - k0) * 33 + t];
+                    const double lj = pan[(gj - k0) * 33 + t];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int gj = gj0 + j;
-                        acc[j] += li * (gj < l ? pan[(gj - k0) * 33 + t] : 0.0);
-                    }
+                    for (int i = 0; i < 32; ++i)
+                        if (i < ni) acc[i] += prow[i * 33 + t] * lj;
                 }
+                double* arow = a + (int64_t)gi0 * l + gj;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int gj = gj0 + j;
-                    if (gj < l && gj <= gi) a[(int64_t)gi * l + gj] -= acc[j];
-                }
+                for (int i = 0; i < 32; ++i)
+                    if (i < ni && gj <= gi0 + i) arow[i * l] -= acc[i];
             }
         }
         cluster_sync();  // the trailing updates of every CTA before the next panel load
