@@ -1745,7 +1745,7 @@ uint64_t aeth_galore_step_count(const aeth_galore_ctx* ctx) { return ctx ? ctx->
 namespace {
 
 // Concurrent refreshes of aeth_galore_refresh_layer.
-constexpr int kRefreshStreams = 16;
+constexpr int kRefreshStreams = 8;
 
 // Phase ids of aeth_galore_phase_times.
 enum { PH_PROJ = 0, PH_NORM = 1, PH_ADAM = 2, PH_APPLY = 3 };
