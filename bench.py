@@ -268,6 +268,8 @@ def run_reference_sweep(args):
             "warmup": 0, "ms_per_step": 1000.0 * params_step / v, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": sweep_config(args, world),
             "parallelism": "one host thread (rank 0 only)", "extrapolated": True,
+            "note": (f"each step is one bounded CPU sample (about 20 s); {k} of the {args.steps} requested steps "
+                     f"and none of the {args.warmup} warm-up steps are run, so the arm ends within about a minute"),
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
                              "sample": desc + f"; median of {k} samples, {secs:.1f} s"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -308,6 +310,8 @@ def run_reference(args):
             "steps": k, "warmup": 0, "ms_per_step": 1000.0 * sum(m * n for _, m, n in SHAPES) / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": block_config(), "parallelism": "one host thread (rank 0 only)", "extrapolated": True,
+            "note": (f"each step is one bounded CPU sample; {k} of the {args.steps} requested steps and none of the "
+                     f"{args.warmup} warm-up steps are run, so the arm ends within a few minutes"),
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": 1, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
